@@ -1,0 +1,1351 @@
+// TEST INFRASTRUCTURE — the CPU oracle of the FlyHighFG Core hot path (Session::pair / Session::mid).
+//
+// A plain C++17 restatement of the reference's algorithm for this path, used ONLY by tests/, by
+// __graft_entry__.smoke() and by bench.py's cpu_baseline / --impl reference legs, as the checker and as the timed CPU
+// baseline. Nothing in the product (flyhigh_engine_b200/) links, loads or calls it.
+//
+// What it restates (paths relative to the reference project root):
+//   - the graph walk of crates/flyhigh-engine/src/net/build.rs:149-484 (views: slice / scale / neg are free, mul_t is a
+//     unary, conv+add and blend_weights+mul+mul+add peepholes) and build_network_with (:532-798): the static-age pass,
+//     the internal-size downscale, the pair / mid split at model/graph.rs:182-186, GMHS after the pair stage, the
+//     full-resolution render that replaces the graph's render_pix, the keep_static apply;
+//   - every WGSL kernel on that path, one function each, cited at its definition;
+//   - session semantics of net/session_ext.rs:377-468 (tex_in x2 + pair plan; mid plan + tex_out) and the persistent
+//     static-protection state (net/build.rs:576-603).
+// Layout is the reference's: planar f16 [C][H][W] tensors, H and W padded to multiples of 32 by edge replication,
+// BGR channel order. Arithmetic follows the shaders: f16 storage (_Float16, round to nearest even), f32 math.
+//
+// Parity pin: the reference ships no value fixtures for this path (its PyTorch fixtures are not in the repository), so
+// value parity of this restatement is pinned by (1) the reference's known-answer tests run on it with the shipped
+// weights (tests/core.rs:67-123 in-between MAE bounds), (2) per-op cross-checks against torch CPU where the shaders
+// follow torch (conv2d, interpolate antialias, grid_sample), (3) the golden plan dumps
+// (crates/flyhigh-engine/tests/golden/*.txt), which pin every derived size and parameter word the planner computes.
+#include "../flyhigh_engine_b200/csrc/json.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <functional>
+#include <map>
+#include <memory>
+#include <sstream>
+#include <string>
+#include <vector>
+
+typedef _Float16 f16;
+static inline float L(f16 v) { return (float)v; }
+static inline f16 S(float v) { return (f16)v; }  // f32 -> f16, round to nearest even
+
+static thread_local std::string g_err;
+
+// ------------------------------------------------------------------------------------------------ tensors & model ----
+
+struct Buf {
+    std::vector<f16> d;
+    explicit Buf(size_t n) : d(n, (f16)0.0f) {}
+};
+using BufP = std::shared_ptr<Buf>;
+
+// ops/tensor.rs:10-28: [c][h][w] f16, or a view: channels [c0, c0+c) of the buffer, values x scale
+struct T {
+    BufP buf;
+    int c = 0, h = 0, w = 0, c0 = 0;
+    float scale = 1.0f;
+    bool plain() const { return c0 == 0 && scale == 1.0f; }
+    T view(int a, int b) const {
+        T t = *this;
+        t.c = b - a;
+        t.c0 = c0 + a;
+        return t;
+    }
+    T scaled(float f) const {
+        T t = *this;
+        t.scale = scale * f;
+        return t;
+    }
+    size_t n() const { return (size_t)c * h * w; }
+};
+static T alloc(int c, int h, int w) {
+    T t;
+    t.buf = std::make_shared<Buf>((size_t)c * h * w);
+    t.c = c;
+    t.h = h;
+    t.w = w;
+    return t;
+}
+
+struct Model {
+    fhjson::Value graph, man;
+    std::vector<uint8_t> bin;
+    bool render_cubic = false;
+    std::vector<int> shape(const std::string& name) const {
+        std::vector<int> s;
+        const auto& a = man["tensors"][name]["shape"];
+        for (size_t i = 0; i < a.size(); i++) s.push_back((int)a[i].as_num());
+        return s;
+    }
+    // model/blob.rs:32-41: little-endian f16 at the manifest offset (in f16 elements)
+    std::vector<float> weight(const std::string& name) const {
+        const auto* t = man["tensors"].find(name);
+        if (!t) throw std::runtime_error("manifest lacks tensor " + name);
+        size_t off = (size_t)(*t)["offset"].as_num();
+        size_t n = 1;
+        for (int d : shape(name)) n *= (size_t)d;
+        if ((off + n) * 2 > bin.size()) throw std::runtime_error("tensor " + name + " outside the blob");
+        std::vector<float> v(n);
+        for (size_t i = 0; i < n; i++) {
+            uint16_t bits = (uint16_t)(bin[(off + i) * 2] | (bin[(off + i) * 2 + 1] << 8));
+            f16 h;
+            memcpy(&h, &bits, 2);
+            v[i] = (float)h;
+        }
+        return v;
+    }
+};
+
+static std::string slurp(const std::string& p) {
+    std::ifstream f(p, std::ios::binary);
+    if (!f) throw std::runtime_error("cannot read " + p);
+    std::stringstream ss;
+    ss << f.rdbuf();
+    return ss.str();
+}
+
+static std::vector<std::string> names(const fhjson::Value& op, const char* key) {
+    std::vector<std::string> v;
+    const auto& a = op[key];
+    for (size_t i = 0; i < a.size(); i++)
+        if (a[i].is_string()) v.push_back(a[i].str);
+    return v;
+}
+
+// ------------------------------------------------------------------------------------------------------ kernels ----
+// One function per WGSL kernel (shaders/<name>.wgsl). Loops over the dispatch's invocations; OpenMP over rows.
+
+// tex_in.wgsl:10-19 / rgba_in.wgsl:10-19: rgba8 [h][w] -> [3][hp][wp] f16 BGR, replicate pad
+static void k_tex_in(const uint8_t* rgba, int w, int h, T& out) {
+    int wp = out.w, hp = out.h;
+    size_t plane = (size_t)hp * wp;
+    f16* o = out.buf->d.data();
+#pragma omp parallel for
+    for (int y = 0; y < hp; y++)
+        for (int x = 0; x < wp; x++) {
+            const uint8_t* p = rgba + ((size_t)std::min(y, h - 1) * w + std::min(x, w - 1)) * 4;
+            size_t i = (size_t)y * wp + x;
+            o[i] = S((float)p[2] / 255.0f);
+            o[plane + i] = S((float)p[1] / 255.0f);
+            o[2 * plane + i] = S((float)p[0] / 255.0f);
+        }
+}
+
+// rgba_out.wgsl:9-17 (crop, alpha 255, q(v) = u32(clamp(v, 0, 1) * 255 + 0.5)); tex_out.wgsl writes the same bytes
+// through an rgba8unorm storage texture
+static void k_tex_out(const T& in, int w, int h, uint8_t* rgba) {
+    size_t plane = (size_t)in.h * in.w;
+    const f16* s = in.buf->d.data();
+    auto q = [](f16 v) { return (uint8_t)(uint32_t)(std::min(std::max(L(v), 0.0f), 1.0f) * 255.0f + 0.5f); };
+#pragma omp parallel for
+    for (int y = 0; y < h; y++)
+        for (int x = 0; x < w; x++) {
+            size_t o = (size_t)y * in.w + x;
+            uint8_t* p = rgba + ((size_t)y * w + x) * 4;
+            p[0] = q(s[2 * plane + o]);
+            p[1] = q(s[plane + o]);
+            p[2] = q(s[o]);
+            p[3] = 255;
+        }
+}
+
+// interp.wgsl:11-45: aa = 0 bilinear align_corners = False; aa = 1 antialias triangle (torch antialias=True);
+// the input may be a view (c0, scale; scale applied to the result)
+static T k_interp(const T& x, int oh, int ow, bool aa) {
+    T out = alloc(x.c, oh, ow);
+    const f16* in = x.buf->d.data();
+    f16* o = out.buf->d.data();
+    int ih = x.h, iw = x.w;
+    float sh = (float)ih / (float)oh, sw = (float)iw / (float)ow;
+#pragma omp parallel for collapse(2)
+    for (int c = 0; c < x.c; c++)
+        for (int oy = 0; oy < oh; oy++)
+            for (int ox = 0; ox < ow; ox++) {
+                size_t base = (size_t)(c + x.c0) * ih * iw;
+                auto at = [&](int yy, int xx) { return L(in[base + (size_t)yy * iw + xx]); };
+                float val;
+                if (!aa) {
+                    float iy = ((float)oy + 0.5f) * sh - 0.5f, ix = ((float)ox + 0.5f) * sw - 0.5f;
+                    int y0 = (int)floorf(iy), x0 = (int)floorf(ix);
+                    float fy = iy - (float)y0, fx = ix - (float)x0;
+                    int y0c = std::max(0, std::min(y0, ih - 1)), y1c = std::max(0, std::min(y0 + 1, ih - 1));
+                    int x0c = std::max(0, std::min(x0, iw - 1)), x1c = std::max(0, std::min(x0 + 1, iw - 1));
+                    float v00 = at(y0c, x0c), v01 = at(y0c, x1c), v10 = at(y1c, x0c), v11 = at(y1c, x1c);
+                    val = (v00 * (1.0f - fx) + v01 * fx) * (1.0f - fy) + (v10 * (1.0f - fx) + v11 * fx) * fy;
+                } else {
+                    float fsh = std::max(sh, 1.0f), fsw = std::max(sw, 1.0f);
+                    float cy = ((float)oy + 0.5f) * sh, cx = ((float)ox + 0.5f) * sw;
+                    int ymin = std::max(0, (int)floorf(cy - fsh + 0.5f)), ymax = std::min(ih, (int)floorf(cy + fsh + 0.5f));
+                    int xmin = std::max(0, (int)floorf(cx - fsw + 0.5f)), xmax = std::min(iw, (int)floorf(cx + fsw + 0.5f));
+                    float acc = 0.0f, norm = 0.0f;
+                    for (int y = ymin; y < ymax; y++) {
+                        float wy = std::max(0.0f, 1.0f - fabsf(((float)y + 0.5f - cy) / fsh));
+                        for (int xx = xmin; xx < xmax; xx++) {
+                            float wx = std::max(0.0f, 1.0f - fabsf(((float)xx + 0.5f - cx) / fsw));
+                            float wgt = wx * wy;
+                            acc = acc + at(y, xx) * wgt;
+                            norm = norm + wgt;
+                        }
+                    }
+                    val = acc / norm;
+                }
+                o[((size_t)c * oh + oy) * ow + ox] = S(val * x.scale);
+            }
+    return out;
+}
+
+// avgpool.wgsl:8-19 (plain input)
+static T k_avgpool(const T& x, int k) {
+    int oh = x.h / k, ow = x.w / k;
+    T out = alloc(x.c, oh, ow);
+    const f16* in = x.buf->d.data();
+#pragma omp parallel for collapse(2)
+    for (int c = 0; c < x.c; c++)
+        for (int oy = 0; oy < oh; oy++)
+            for (int ox = 0; ox < ow; ox++) {
+                float acc = 0.0f;
+                for (int ky = 0; ky < k; ky++)
+                    for (int kx = 0; kx < k; kx++) acc = acc + L(in[((size_t)c * x.h + oy * k + ky) * x.w + ox * k + kx]);
+                out.buf->d[((size_t)c * oh + oy) * ow + ox] = S(acc / (float)(k * k));
+            }
+    return out;
+}
+
+// chcopy.wgsl:19-38: channel concat of up to 7 views; a view with scale != 1 is rescaled through f32 and rounded
+static void k_chcopy(const std::vector<T>& ins, T& out, int dst0) {
+    size_t hw = (size_t)out.h * out.w;
+    int c = dst0;
+    for (const T& t : ins) {
+        for (int k = 0; k < t.c; k++, c++) {
+            const f16* s = t.buf->d.data() + (size_t)(t.c0 + k) * hw;
+            f16* d = out.buf->d.data() + (size_t)c * hw;
+            if (t.scale == 1.0f)
+                memcpy(d, s, hw * sizeof(f16));
+            else
+                for (size_t i = 0; i < hw; i++) d[i] = S(L(s[i]) * t.scale);
+        }
+    }
+}
+// ops/elementwise.rs:118-126: materialise a view (plain tensors pass through)
+static T mat(const T& x) {
+    if (x.plain()) return x;
+    T out = alloc(x.c, x.h, x.w);
+    k_chcopy({x}, out, 0);
+    return out;
+}
+// ops/elementwise.rs:98-110
+static T k_concat(const std::vector<T>& ts) {
+    int c = 0;
+    for (auto& t : ts) c += t.c;
+    T out = alloc(c, ts[0].h, ts[0].w);
+    k_chcopy(ts, out, 0);
+    return out;
+}
+
+// unary.wgsl:8-20: op 0 scale(*a), 1 clamp(a, b), 2 2*sigmoid-1, 3 neg; input may be a view
+static T k_unary(const T& x, int op, float a, float b) {
+    T out = alloc(x.c, x.h, x.w);
+    size_t hw = (size_t)x.h * x.w;
+    const f16* in = x.buf->d.data();
+#pragma omp parallel for
+    for (int c = 0; c < x.c; c++)
+        for (size_t i = 0; i < hw; i++) {
+            float v = L(in[(size_t)(c + x.c0) * hw + i]) * x.scale;
+            float r;
+            if (op == 0) r = v * a;
+            else if (op == 1) r = std::min(std::max(v, a), b);
+            else if (op == 2) r = 2.0f / (1.0f + expf(-v)) - 1.0f;
+            else r = -v;
+            out.buf->d[(size_t)c * hw + i] = S(r);
+        }
+    return out;
+}
+
+// binary.wgsl:9-17: op 0 add, op 1 mul; b with one channel broadcasts; both may be views
+static T k_binary(const T& a, const T& b, int op) {
+    T out = alloc(a.c, a.h, a.w);
+    size_t hw = (size_t)a.h * a.w;
+#pragma omp parallel for
+    for (int c = 0; c < a.c; c++) {
+        int cb = b.c == 1 ? 0 : c;
+        for (size_t i = 0; i < hw; i++) {
+            float av = L(a.buf->d[(size_t)(c + a.c0) * hw + i]) * a.scale;
+            float bv = L(b.buf->d[(size_t)(cb + b.c0) * hw + i]) * b.scale;
+            out.buf->d[(size_t)c * hw + i] = S(op == 1 ? av * bv : av + bv);
+        }
+    }
+    return out;
+}
+
+// luma.wgsl:8-28: BGR -> luma (view ok); grad = |d/dx| + |d/dy| of luma, forward differences
+static T k_luma(const T& x, bool grad) {
+    T out = alloc(1, x.h, x.w);
+    size_t p = (size_t)x.h * x.w;
+    const f16* in = x.buf->d.data();
+    auto lum = [&](int y, int xx) {
+        size_t i = (size_t)x.c0 * p + (size_t)y * x.w + xx;
+        return (0.299f * L(in[2 * p + i]) + 0.587f * L(in[p + i]) + 0.114f * L(in[i])) * x.scale;
+    };
+#pragma omp parallel for
+    for (int y = 0; y < x.h; y++)
+        for (int xx = 0; xx < x.w; xx++) {
+            float v;
+            if (!grad) {
+                v = lum(y, xx);
+            } else {
+                float c = lum(y, xx);
+                float gx = xx + 1 < x.w ? lum(y, xx + 1) - c : 0.0f;
+                float gy = y + 1 < x.h ? lum(y + 1, xx) - c : 0.0f;
+                v = fabsf(gx) + fabsf(gy);
+            }
+            out.buf->d[(size_t)y * x.w + xx] = S(v);
+        }
+    return out;
+}
+
+// sad.wgsl:10-29: (2r+1)^2 channels; 3x3 zero-padded mean of |la - lb(shifted, edge-clamped)|
+static T k_sad(const T& la, const T& lb, int r) {
+    int span = 2 * r + 1, h = la.h, w = la.w;
+    T out = alloc(span * span, h, w);
+    const f16* a = la.buf->d.data();
+    const f16* b = lb.buf->d.data();
+#pragma omp parallel for collapse(2)
+    for (int c = 0; c < span * span; c++)
+        for (int y = 0; y < h; y++)
+            for (int x = 0; x < w; x++) {
+                int dy = c / span - r, dx = c % span - r;
+                float acc = 0.0f;
+                for (int wy = -1; wy <= 1; wy++)
+                    for (int wx = -1; wx <= 1; wx++) {
+                        int yy = y + wy, xx = x + wx;
+                        if (yy >= 0 && yy < h && xx >= 0 && xx < w) {
+                            float lav = L(a[(size_t)yy * w + xx]);
+                            int syy = std::max(0, std::min(yy + dy, h - 1)), sxx = std::max(0, std::min(xx + dx, w - 1));
+                            acc = acc + fabsf(lav - L(b[(size_t)syy * w + sxx]));
+                        }
+                    }
+                out.buf->d[((size_t)c * h + y) * w + x] = S(acc / 9.0f);
+            }
+    return out;
+}
+
+// warp.wgsl:12-29: backward bilinear warp, border clamp; image and flow may be views
+static T k_warp(const T& img, const T& flow) {
+    T out = alloc(img.c, img.h, img.w);
+    int h = img.h, w = img.w;
+    size_t plane = (size_t)h * w;
+    const f16* im = img.buf->d.data();
+    const f16* fl = flow.buf->d.data();
+#pragma omp parallel for collapse(2)
+    for (int c = 0; c < img.c; c++)
+        for (int y = 0; y < h; y++)
+            for (int x = 0; x < w; x++) {
+                float fx = L(fl[((size_t)flow.c0 * h + y) * w + x]) * flow.scale;
+                float fy = L(fl[((size_t)(flow.c0 + 1) * h + y) * w + x]) * flow.scale;
+                float gx = (float)x + fx, gy = (float)y + fy;
+                int x0 = (int)floorf(gx), y0 = (int)floorf(gy);
+                float ax = gx - (float)x0, ay = gy - (float)y0;
+                int x0c = std::max(0, std::min(x0, w - 1)), x1c = std::max(0, std::min(x0 + 1, w - 1));
+                int y0c = std::max(0, std::min(y0, h - 1)), y1c = std::max(0, std::min(y0 + 1, h - 1));
+                size_t base = (size_t)(c + img.c0) * plane;
+                float v00 = L(im[base + (size_t)y0c * w + x0c]), v01 = L(im[base + (size_t)y0c * w + x1c]);
+                float v10 = L(im[base + (size_t)y1c * w + x0c]), v11 = L(im[base + (size_t)y1c * w + x1c]);
+                float top = v00 * (1.0f - ax) + v01 * ax, bot = v10 * (1.0f - ax) + v11 * ax;
+                out.buf->d[(size_t)c * plane + (size_t)y * w + x] = S((top * (1.0f - ay) + bot * ay) * img.scale);
+            }
+    return out;
+}
+
+// conv_fused.wgsl:20-75 / conv_fused2.wgsl (the tensor-core path every conv takes, net/build.rs:216-219): implicit GEMM
+// over K = cin * 9 (k = ci * 9 + ky * 3 + kx, torch weight layout [cout][cin][3][3], ops/conv/kernels.rs:66-78), f32
+// accumulation, then bias, PReLU (slope 1 = identity for conv2d), f16. Residual (conv_tiled.wgsl:57-61, equal to the
+// unfused `binary` add): f16(f32(f16(r)) + res).
+static T k_conv(const T& x, const std::vector<float>& wt, const std::vector<float>& bias,
+                const std::vector<float>& slope, int cout, int stride, const T* resid) {
+    int cin = x.c, h = x.h, w = x.w;
+    int hout = (h + 2 - 3) / stride + 1, wout = (w + 2 - 3) / stride + 1;
+    T out = alloc(cout, hout, wout);
+    const f16* in = x.buf->d.data();
+    size_t hw = (size_t)h * w;
+#pragma omp parallel for collapse(2) schedule(dynamic, 4)
+    for (int co = 0; co < cout; co++)
+        for (int yo = 0; yo < hout; yo++)
+            for (int xo = 0; xo < wout; xo++) {
+                float acc = 0.0f;
+                for (int ci = 0; ci < cin; ci++) {
+                    const f16* pl = in + (size_t)ci * hw;
+                    const float* wk = wt.data() + ((size_t)co * cin + ci) * 9;
+                    for (int ky = 0; ky < 3; ky++) {
+                        int yi = yo * stride + ky - 1;
+                        if (yi < 0 || yi >= h) continue;
+                        for (int kx = 0; kx < 3; kx++) {
+                            int xi = xo * stride + kx - 1;
+                            if (xi < 0 || xi >= w) continue;
+                            acc = acc + L(pl[(size_t)yi * w + xi]) * wk[ky * 3 + kx];
+                        }
+                    }
+                }
+                float v = acc + bias[co];
+                v = v > 0.0f ? v : slope[co] * v;
+                size_t oi = ((size_t)co * hout + yo) * wout + xo;
+                f16 r = S(v);
+                if (resid) r = S(L(r) + L(resid->buf->d[oi]));
+                out.buf->d[oi] = r;
+            }
+    return out;
+}
+
+// film.wgsl:9-15: h * (1 + g[c]) + g[c + C]
+static T k_film(const T& hh, const T& g) {
+    T out = alloc(hh.c, hh.h, hh.w);
+    size_t hw = (size_t)hh.h * hh.w;
+#pragma omp parallel for
+    for (int c = 0; c < hh.c; c++) {
+        float sc = L(g.buf->d[c]), bi = L(g.buf->d[c + hh.c]);
+        for (size_t i = 0; i < hw; i++)
+            out.buf->d[(size_t)c * hw + i] = S(L(hh.buf->d[(size_t)c * hw + i]) * (1.0f + sc) + bi);
+    }
+    return out;
+}
+
+// convex.wgsl:10-35: 2x convex upsample, softmax over 9 weights (channel k*4 + sy*2 + sx), zero-padded 3x3 neighbourhood
+static T k_convex(const T& wt, const T& x) {
+    int h = x.h, w = x.w, oh = 2 * h, ow = 2 * w;
+    T out = alloc(x.c, oh, ow);
+    size_t plane = (size_t)h * w;
+#pragma omp parallel for collapse(2)
+    for (int co = 0; co < x.c; co++)
+        for (int oy = 0; oy < oh; oy++)
+            for (int ox = 0; ox < ow; ox++) {
+                int ihh = oy / 2, iww = ox / 2, sy = oy % 2, sx = ox % 2;
+                float m = -3.0e38f, ws[9];
+                for (int k = 0; k < 9; k++) {
+                    int ch = k * 4 + sy * 2 + sx;
+                    float v = L(wt.buf->d[((size_t)ch * h + ihh) * w + iww]);
+                    ws[k] = v;
+                    m = std::max(m, v);
+                }
+                float denom = 0.0f;
+                for (int k = 0; k < 9; k++) {
+                    ws[k] = expf(ws[k] - m);
+                    denom = denom + ws[k];
+                }
+                float acc = 0.0f;
+                for (int k = 0; k < 9; k++) {
+                    int ny = ihh - 1 + k / 3, nx = iww - 1 + k % 3;
+                    float xv = 0.0f;
+                    if (ny >= 0 && ny < h && nx >= 0 && nx < w) xv = L(x.buf->d[(size_t)co * plane + (size_t)ny * w + nx]);
+                    acc = acc + (ws[k] / denom) * xv;
+                }
+                out.buf->d[((size_t)co * oh + oy) * ow + ox] = S(acc);
+            }
+    return out;
+}
+
+// blend.wgsl:10-21: softmax of 3 logits -> [p0 + p2/2, p1 + p2/2] (vis may be a view)
+static T k_blend(const T& vis) {
+    T out = alloc(2, vis.h, vis.w);
+    size_t p = (size_t)vis.h * vis.w;
+    for (size_t i = 0; i < p; i++) {
+        size_t vb = (size_t)vis.c0 * p + i;
+        float a = L(vis.buf->d[vb]) * vis.scale, b = L(vis.buf->d[vb + p]) * vis.scale, c = L(vis.buf->d[vb + 2 * p]) * vis.scale;
+        float m = std::max(a, std::max(b, c));
+        float ea = expf(a - m), eb = expf(b - m), ec = expf(c - m), s = ea + eb + ec;
+        float p0 = ea / s, p1 = eb / s, p2 = ec / s;
+        out.buf->d[i] = S(p0 + 0.5f * p2);
+        out.buf->d[p + i] = S(p1 + 0.5f * p2);
+    }
+    return out;
+}
+
+// blendmix.wgsl:12-28: fused blend weights + 2 mul + add, with the unfused path's f16 round trips
+static T k_blendmix(const T& wa, const T& wb, const T& vis) {
+    T out = alloc(3, wa.h, wa.w);
+    size_t p = (size_t)wa.h * wa.w;
+#pragma omp parallel for
+    for (size_t i = 0; i < p; i++) {
+        size_t vb = (size_t)vis.c0 * p + i;
+        float a = L(vis.buf->d[vb]) * vis.scale, b = L(vis.buf->d[vb + p]) * vis.scale, c = L(vis.buf->d[vb + 2 * p]) * vis.scale;
+        float m = std::max(a, std::max(b, c));
+        float ea = expf(a - m), eb = expf(b - m), ec = expf(c - m), s = ea + eb + ec;
+        float pa = L(S((ea + 0.5f * ec) / s)), pb = L(S((eb + 0.5f * ec) / s));
+        for (int ch = 0; ch < 3; ch++) {
+            size_t o = (size_t)ch * p + i;
+            float t1 = L(S(L(wa.buf->d[o]) * pa)), t2 = L(S(L(wb.buf->d[o]) * pb));
+            out.buf->d[o] = S(t1 + t2);
+        }
+    }
+    return out;
+}
+
+struct RenderArgs {
+    float fsx, fsy;
+    bool cubic;
+    uint32_t flags;       // bit 0 decisive, bit 1 still test
+    const T* age;         // static protection (render_static): the age plane, or null
+    float min_age;
+};
+
+// render.wgsl:82-161 (+ the static variant of gpu/pipeline.rs:10-34): full-resolution render from the Q-res maps
+static T k_render(const T& A, const T& B, const T& ftq, const T& vtq, const T& rt, const RenderArgs& ra) {
+    int H = A.h, W = A.w, hq = ftq.h, wq = ftq.w;
+    T out = alloc(3, H, W);
+    const f16* a = A.buf->d.data();
+    const f16* b = B.buf->d.data();
+    const float STILL_RUN = 3.0f;
+    auto bil4 = [](float v00, float v01, float v10, float v11, float fx, float fy) {
+        return (v00 * (1.0f - fx) + v01 * fx) * (1.0f - fy) + (v10 * (1.0f - fx) + v11 * fx) * fy;
+    };
+    auto cub1 = [](float x) { const float aa = -0.75f; return ((aa + 2.0f) * x - (aa + 3.0f)) * x * x + 1.0f; };
+    auto cub2 = [](float x) { const float aa = -0.75f; return ((aa * x - 5.0f * aa) * x + 8.0f * aa) * x - 4.0f * aa; };
+    auto clampx = [&](int v) { return std::max(0, std::min(v, W - 1)); };
+    auto clampy = [&](int v) { return std::max(0, std::min(v, H - 1)); };
+    auto sampq = [&](const T& t, int ch, int y0, int y1, int x0, int x1, float fx, float fy) {
+        size_t bse = (size_t)(ch + t.c0) * hq * wq;
+        const f16* d = t.buf->d.data();
+        return bil4(L(d[bse + (size_t)y0 * wq + x0]), L(d[bse + (size_t)y0 * wq + x1]), L(d[bse + (size_t)y1 * wq + x0]),
+                    L(d[bse + (size_t)y1 * wq + x1]), fx, fy);
+    };
+    auto cub = [&](const f16* src, int ch, float gx, float gy) {
+        size_t base = (size_t)ch * H * W;
+        int px = (int)floorf(gx), py = (int)floorf(gy);
+        float tx = gx - (float)px, ty = gy - (float)py;
+        float cx[4] = {cub2(tx + 1.0f), cub1(tx), cub1(1.0f - tx), cub2(2.0f - tx)};
+        float cy[4] = {cub2(ty + 1.0f), cub1(ty), cub1(1.0f - ty), cub2(2.0f - ty)};
+        float acc = 0.0f;
+        for (int j = 0; j < 4; j++) {
+            size_t yy = base + (size_t)clampy(py - 1 + j) * W;
+            float row = L(src[yy + clampx(px - 1)]) * cx[0] + L(src[yy + clampx(px)]) * cx[1] +
+                        L(src[yy + clampx(px + 1)]) * cx[2] + L(src[yy + clampx(px + 2)]) * cx[3];
+            acc = acc + row * cy[j];
+        }
+        return acc;
+    };
+    auto bil = [&](const f16* src, int ch, float gx, float gy) {
+        int xx0 = (int)floorf(gx), yy0 = (int)floorf(gy);
+        float ax = gx - (float)xx0, ay = gy - (float)yy0;
+        int x0 = clampx(xx0), x1 = clampx(xx0 + 1), y0 = clampy(yy0), y1 = clampy(yy0 + 1);
+        size_t bse = (size_t)ch * H * W;
+        return bil4(L(src[bse + (size_t)y0 * W + x0]), L(src[bse + (size_t)y0 * W + x1]), L(src[bse + (size_t)y1 * W + x0]),
+                    L(src[bse + (size_t)y1 * W + x1]), ax, ay);
+    };
+    auto on_static = [&](float gx, float gy) {
+        int cx = (int)rintf(gx), cy = (int)rintf(gy);  // WGSL round(): half to even
+        for (int dy = -1; dy <= 1; dy++)
+            for (int dx = -1; dx <= 1; dx++)
+                if (L(ra.age->buf->d[(size_t)clampy(cy + dy) * W + clampx(cx + dx)]) >= ra.min_age) return true;
+        return false;
+    };
+    float sh = (float)hq / (float)H, sw = (float)wq / (float)W;
+#pragma omp parallel for
+    for (int y = 0; y < H; y++)
+        for (int x = 0; x < W; x++) {
+            float iy = ((float)y + 0.5f) * sh - 0.5f, ix = ((float)x + 0.5f) * sw - 0.5f;
+            int qy0 = (int)floorf(iy), qx0 = (int)floorf(ix);
+            float qfy = iy - (float)qy0, qfx = ix - (float)qx0;
+            int qy0c = std::max(0, std::min(qy0, hq - 1)), qy1c = std::max(0, std::min(qy0 + 1, hq - 1));
+            int qx0c = std::max(0, std::min(qx0, wq - 1)), qx1c = std::max(0, std::min(qx0 + 1, wq - 1));
+            float f[4], v[3], cr[3], ca[3], cb[3];
+            for (int ch = 0; ch < 4; ch++)
+                f[ch] = sampq(ftq, ch, qy0c, qy1c, qx0c, qx1c, qfx, qfy) * ((ch & 1) == 0 ? ra.fsx : ra.fsy);
+            for (int ch = 0; ch < 3; ch++) v[ch] = sampq(vtq, ch, qy0c, qy1c, qx0c, qx1c, qfx, qfy) * vtq.scale;
+            float m = std::max(v[0], std::max(v[1], v[2]));
+            float e0 = expf(v[0] - m), e1 = expf(v[1] - m), e2 = expf(v[2] - m), s = e0 + e1 + e2;
+            float wa_w = (e0 + 0.5f * e2) / s, wb_w = (e1 + 0.5f * e2) / s;
+            float gxa = (float)x + f[0], gya = (float)y + f[1], gxb = (float)x + f[2], gyb = (float)y + f[3];
+            for (int c = 0; c < 3; c++) {
+                if (ra.cubic) {
+                    ca[c] = cub(a, c, gxa, gya);
+                    cb[c] = cub(b, c, gxb, gyb);
+                } else {
+                    ca[c] = bil(a, c, gxa, gya);
+                    cb[c] = bil(b, c, gxb, gyb);
+                }
+                T rtv = rt;
+                rtv.c0 = 0;
+                cr[c] = sampq(rtv, c, qy0c, qy1c, qx0c, qx1c, qfx, qfy);
+            }
+            float bwa = wa_w, bwb = wb_w, rk = 1.0f, stillw = 0.0f, own[3] = {0, 0, 0};
+            const float third = 1.0f / 3.0f;
+            if (ra.flags & 2u) {
+                float es = 0.0f;
+                for (int dy = -1; dy <= 1; dy++)
+                    for (int dx = -1; dx <= 1; dx++) {
+                        int yy = clampy(y + dy), xx = clampx(x + dx);
+                        for (int c = 0; c < 3; c++) {
+                            size_t i = ((size_t)c * H + yy) * W + xx;
+                            es += fabsf(L(a[i]) - L(b[i]));
+                        }
+                    }
+                es = es / 27.0f;
+                for (int c = 0; c < 3; c++) {
+                    size_t i = ((size_t)c * H + y) * W + x;
+                    own[c] = 0.5f * (L(a[i]) + L(b[i]));
+                }
+                float ef = fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
+                stillw = std::min(std::max((ef - es) / 0.04f, 0.0f), 1.0f) * (es < 0.03f ? 1.0f : 0.0f);
+            }
+            if (ra.flags & 1u) {
+                float d = fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
+                float k = std::min(std::max((d - 0.04f) / 0.08f, 0.0f), 1.0f);
+                float pa = wa_w >= wb_w ? 1.0f : 0.0f;
+                bwa = wa_w * (1.0f - k) + pa * k;
+                bwb = wb_w * (1.0f - k) + (1.0f - pa) * k;
+                rk = 1.0f - k;
+            }
+            float raw = 0.0f;
+            if (ra.age) {
+                bool sa = on_static(gxa, gya), sb = on_static(gxb, gyb);
+                stillw = stillw * (fabsf(L(ra.age->buf->d[(size_t)y * W + x])) >= STILL_RUN ? 1.0f : 0.0f);
+                if (sa && sb) {
+                    rk = 0.0f;
+                    raw = 1.0f;
+                } else if (sa) {
+                    rk = 0.0f;
+                    bwa = 0.0f;
+                    bwb = 1.0f;
+                } else if (sb) {
+                    rk = 0.0f;
+                    bwa = 1.0f;
+                    bwb = 0.0f;
+                }
+            }
+            for (int c = 0; c < 3; c++) {
+                float mixv = ca[c] * bwa + cb[c] * bwb + cr[c] * rk;
+                float o = std::min(std::max(mixv * (1.0f - stillw) + own[c] * stillw, 0.0f), 1.0f);
+                size_t i = ((size_t)c * H + y) * W + x;
+                if (ra.age) {
+                    float src = 0.5f * (L(a[i]) + L(b[i]));
+                    o = std::min(std::max(o * (1.0f - raw) + src * raw, 0.0f), 1.0f);
+                }
+                out.buf->d[i] = S(o);
+            }
+        }
+    return out;
+}
+
+struct StaticP {
+    int w, h, wp, hp;
+    float thr, min_age;
+    int use_mask;
+};
+
+// keep_static_age.wgsl:28-77: per-pixel age / verified-run state machine over the padded plane
+static void k_static_age(const T& A, const T& B, const StaticP& p, const T* mask, T& state, T& age) {
+    size_t plane = (size_t)p.hp * p.wp;
+    const f16* a = A.buf->d.data();
+    const f16* b = B.buf->d.data();
+    f16* st = state.buf->d.data();
+    const int DX[8] = {1, -1, 0, 0, 1, -1, 1, -1}, DY[8] = {0, 0, 1, -1, 1, 1, -1, -1}, FAR[4] = {4, 8, 16, 32};
+    auto diff = [&](size_t o) {
+        float d = 0.0f;
+        for (int c = 0; c < 3; c++) d = std::max(d, fabsf(L(a[c * plane + o]) - L(b[c * plane + o])));
+        return d;
+    };
+    auto cx = [&](int v) { return std::max(0, std::min(v, p.w - 1)); };
+    auto cy = [&](int v) { return std::max(0, std::min(v, p.h - 1)); };
+#pragma omp parallel for
+    for (int y = 0; y < p.h; y++)
+        for (int x = 0; x < p.w; x++) {
+            size_t o = (size_t)y * p.wp + x;
+            bool moved = false;
+            for (int dy = -1; dy <= 1; dy++)
+                for (int dx = -1; dx <= 1; dx++) moved = moved || diff((size_t)cy(y + dy) * p.wp + cx(x + dx)) >= p.thr;
+            for (int i = 0; i < 8; i++)
+                for (int j = 0; j < 4; j++)
+                    moved = moved || diff((size_t)cy(y + DY[i] * FAR[j]) * p.wp + cx(x + DX[i] * FAR[j])) >= p.thr;
+            bool same = diff(o) < p.thr;
+            float m = 0.0f;  // spread (:38-50)
+            for (int dy = -1; dy <= 1; dy++)
+                for (int dx = -1; dx <= 1; dx++) {
+                    size_t q = (size_t)cy(y + dy) * p.wp + cx(x + dx);
+                    for (int c = 0; c < 3; c++) {
+                        m = std::max(m, fabsf(L(a[c * plane + q]) - L(a[c * plane + o])));
+                        m = std::max(m, fabsf(L(b[c * plane + q]) - L(b[c * plane + o])));
+                    }
+                }
+            bool still = same && m >= 0.03f;
+            float raw = still ? std::min(L(st[o]) + 1.0f, 255.0f) : 0.0f;
+            float seen = still ? std::min(L(st[plane + o]) + (moved ? 1.0f : 0.0f), 255.0f) : 0.0f;
+            float run = same ? std::min(L(st[2 * plane + o]) + 1.0f, 255.0f) : 0.0f;
+            st[o] = S(raw);
+            st[plane + o] = S(seen);
+            st[2 * plane + o] = S(run);
+            f16 aged = S(seen >= 2.0f ? raw : -run);
+            if (p.use_mask && mask && L(mask->buf->d[o]) > 0.5f) aged = S(255.0f);
+            age.buf->d[o] = aged;
+        }
+}
+
+// keep_static.wgsl:21-32: in place, protected pixels mix toward the sources' mean with a two-pair ramp
+static void k_static_apply(const T& age, const T& A, const T& B, const StaticP& q, T& render) {
+    size_t plane = (size_t)q.hp * q.wp;
+#pragma omp parallel for
+    for (int y = 0; y < q.h; y++)
+        for (int x = 0; x < q.w; x++) {
+            size_t o = (size_t)y * q.wp + x;
+            float k = std::min(std::max((L(age.buf->d[o]) - q.min_age + 2.0f) / 2.0f, 0.0f), 1.0f);
+            if (k <= 0.0f) continue;
+            for (int c = 0; c < 3; c++) {
+                size_t i = c * plane + o;
+                float r = L(render.buf->d[i]), s = 0.5f * (L(A.buf->d[i]) + L(B.buf->d[i]));
+                render.buf->d[i] = S(r * (1.0f - k) + s * k);
+            }
+        }
+}
+
+// ------------------------------------------------------------------------------------------------------- GMHS ----
+// gmhs.rs:155-219 with gm_fit_reduce / gm_fit_solve / gm_cost / gm_box / gm_select.wgsl
+
+struct GmParams {
+    int r_blk, r_dwin, hc, wc;
+    float dmin, delta, s;
+};
+static GmParams gm_params(int h, int w, int full_w, int level) {
+    const int DS = 2;  // gmhs.rs:122
+    GmParams g;
+    g.hc = (h + DS - 1) / DS;
+    g.wc = (w + DS - 1) / DS;
+    g.s = (float)w / ((float)full_w / 2.0f);
+    g.r_blk = std::max(1, (int)roundf(20.0f * g.s / (float)DS));  // Rust f32::round: half away from zero
+    g.r_dwin = std::max(1, (int)roundf(32.0f * g.s / (float)DS));
+    g.dmin = level >= 2 ? 0.0f : 8.0f * g.s;
+    g.delta = 1.5f * g.s;
+    return g;
+}
+
+static void gm_run(const T& A, const T& B, T& flow, int full_w, int level, std::vector<float>* maps_out) {
+    int h8 = flow.h, w8 = flow.w, h = A.h, w = A.w;
+    GmParams g = gm_params(h, w, full_w, level);
+    const int nwg = 32;
+    float coef[16] = {0};
+    std::vector<float> part((size_t)nwg * 36);
+    f16* fl = flow.buf->d.data();
+    int n8 = h8 * w8;
+    for (int it = 0; it < 4; it++) {
+        // gm_fit_reduce.wgsl:14-45 — 32 workgroups of 256 threads, strided accumulation, tree reduction
+        float sx = 2.0f / (float)std::max(w8 - 1, 1), sy = 2.0f / (float)std::max(h8 - 1, 1);
+        for (int wg = 0; wg < nwg; wg++)
+            for (int c = 0; c < 4; c++) {
+                std::vector<float> sh((size_t)9 * 256, 0.0f);
+                for (int tid = 0; tid < 256; tid++) {
+                    float s[9] = {0};
+                    for (int i = wg * 256 + tid; i < n8; i += 256 * nwg) {
+                        int yy = i / w8, xx = i - yy * w8;
+                        float x = -1.0f + sx * (float)xx, y = -1.0f + sy * (float)yy;
+                        float f = L(fl[(size_t)c * n8 + i]);
+                        float w2 = 1.0f;
+                        if (it > 0) {
+                            float r = fabsf(f - (coef[c * 4] + coef[c * 4 + 1] * x + coef[c * 4 + 2] * y));
+                            w2 = g.delta / std::max(g.delta, r);
+                        }
+                        s[0] += w2; s[1] += w2 * x; s[2] += w2 * y;
+                        s[3] += w2 * x * x; s[4] += w2 * x * y; s[5] += w2 * y * y;
+                        s[6] += w2 * f; s[7] += w2 * x * f; s[8] += w2 * y * f;
+                    }
+                    for (int k = 0; k < 9; k++) sh[(size_t)k * 256 + tid] = s[k];
+                }
+                for (int off = 128; off > 0; off >>= 1)
+                    for (int tid = 0; tid < off; tid++)
+                        for (int k = 0; k < 9; k++) sh[(size_t)k * 256 + tid] += sh[(size_t)k * 256 + tid + off];
+                for (int k = 0; k < 9; k++) part[((size_t)wg * 4 + c) * 9 + k] = sh[(size_t)k * 256];
+            }
+        // gm_fit_solve.wgsl:7-26
+        for (int c = 0; c < 4; c++) {
+            float s[9] = {0};
+            for (int wg = 0; wg < nwg; wg++)
+                for (int k = 0; k < 9; k++) s[k] += part[((size_t)wg * 4 + c) * 9 + k];
+            float m00 = s[0] + 1e-6f, m01 = s[1], m02 = s[2], m11 = s[3] + 1e-6f, m12 = s[4], m22 = s[5] + 1e-6f;
+            float det = m00 * (m11 * m22 - m12 * m12) - m01 * (m01 * m22 - m12 * m02) + m02 * (m01 * m12 - m11 * m02);
+            if (fabsf(det) < 1e-12f) {
+                coef[c * 4] = s[6] / std::max(s[0], 1e-6f);
+                coef[c * 4 + 1] = coef[c * 4 + 2] = coef[c * 4 + 3] = 0.0f;
+                continue;
+            }
+            float i00 = (m11 * m22 - m12 * m12) / det, i01 = (m02 * m12 - m01 * m22) / det, i02 = (m01 * m12 - m02 * m11) / det;
+            float i11 = (m00 * m22 - m02 * m02) / det, i12 = (m01 * m02 - m00 * m12) / det, i22 = (m00 * m11 - m01 * m01) / det;
+            coef[c * 4] = i00 * s[6] + i01 * s[7] + i02 * s[8];
+            coef[c * 4 + 1] = i01 * s[6] + i11 * s[7] + i12 * s[8];
+            coef[c * 4 + 2] = i02 * s[6] + i12 * s[7] + i22 * s[8];
+            coef[c * 4 + 3] = 0.0f;
+        }
+    }
+    // gm_cost.wgsl:55-75
+    int hc = g.hc, wc = g.wc, n = hc * wc;
+    std::vector<float> maps((size_t)6 * n), tmp((size_t)5 * n);
+    const f16* a = A.buf->d.data();
+    const f16* b = B.buf->d.data();
+    size_t p = (size_t)h * w;
+    auto lum = [&](const f16* s, int y, int x) {
+        size_t i = (size_t)y * w + x;
+        return 0.299f * L(s[2 * p + i]) + 0.587f * L(s[p + i]) + 0.114f * L(s[i]);
+    };
+    auto samp = [&](const f16* s, float gx, float gy) {
+        int x0 = (int)floorf(gx), y0 = (int)floorf(gy);
+        float ax = gx - (float)x0, ay = gy - (float)y0;
+        int x0c = std::max(0, std::min(x0, w - 1)), x1c = std::max(0, std::min(x0 + 1, w - 1));
+        int y0c = std::max(0, std::min(y0, h - 1)), y1c = std::max(0, std::min(y0 + 1, h - 1));
+        float top = lum(s, y0c, x0c) * (1.0f - ax) + lum(s, y0c, x1c) * ax;
+        float bot = lum(s, y1c, x0c) * (1.0f - ax) + lum(s, y1c, x1c) * ax;
+        return top * (1.0f - ay) + bot * ay;
+    };
+    auto flow8 = [&](int c, float rx, float ry) {
+        float ix = (rx + 0.5f) * (float)w8 / (float)w - 0.5f, iy = (ry + 0.5f) * (float)h8 / (float)h - 0.5f;
+        int x0 = (int)floorf(ix), y0 = (int)floorf(iy);
+        float fx = ix - (float)x0, fy = iy - (float)y0;
+        int x0c = std::max(0, std::min(x0, w8 - 1)), x1c = std::max(0, std::min(x0 + 1, w8 - 1));
+        int y0c = std::max(0, std::min(y0, h8 - 1)), y1c = std::max(0, std::min(y0 + 1, h8 - 1));
+        size_t bb = (size_t)c * n8;
+        float top = L(fl[bb + (size_t)y0c * w8 + x0c]) * (1.0f - fx) + L(fl[bb + (size_t)y0c * w8 + x1c]) * fx;
+        float bot = L(fl[bb + (size_t)y1c * w8 + x0c]) * (1.0f - fx) + L(fl[bb + (size_t)y1c * w8 + x1c]) * fx;
+        return top * (1.0f - fy) + bot * fy;
+    };
+    auto aff = [&](int c, float rx, float ry) {
+        float ix = (rx + 0.5f) * (float)w8 / (float)w - 0.5f, iy = (ry + 0.5f) * (float)h8 / (float)h - 0.5f;
+        float xn = -1.0f + 2.0f * ix / (float)std::max(w8 - 1, 1), yn = -1.0f + 2.0f * iy / (float)std::max(h8 - 1, 1);
+        return coef[c * 4] + coef[c * 4 + 1] * xn + coef[c * 4 + 2] * yn;
+    };
+    const float ds = 2.0f;
+#pragma omp parallel for
+    for (int y = 0; y < hc; y++)
+        for (int x = 0; x < wc; x++) {
+            size_t i = (size_t)y * wc + x;
+            float rx = ((float)x + 0.5f) * ds - 0.5f, ry = ((float)y + 0.5f) * ds - 0.5f;
+            float f0x = flow8(0, rx, ry), f0y = flow8(1, rx, ry), f1x = flow8(2, rx, ry), f1y = flow8(3, rx, ry);
+            float cm = fabsf(samp(a, rx + f0x, ry + f0y) - samp(b, rx + f1x, ry + f1y));
+            float g0x = aff(0, rx, ry), g0y = aff(1, rx, ry), g1x = aff(2, rx, ry), g1y = aff(3, rx, ry);
+            float wm = (float)w - 1.0f, hm = (float)h - 1.0f;
+            float ax = rx + g0x, ay = ry + g0y, bx = rx + g1x, by = ry + g1y;
+            bool inside = ax >= 0.0f && ax <= wm && ay >= 0.0f && ay <= hm && bx >= 0.0f && bx <= wm && by >= 0.0f && by <= hm;
+            float ca = cm;
+            if (inside) ca = fabsf(samp(a, ax, ay) - samp(b, bx, by));
+            float l = samp(a, rx, ry);
+            float dvx = (g1x - g0x) - (f1x - f0x), dvy = (g1y - g0y) - (f1y - f0y);
+            maps[i] = cm;
+            maps[n + i] = ca;
+            maps[2 * (size_t)n + i] = sqrtf(dvx * dvx + dvy * dvy);
+            maps[3 * (size_t)n + i] = l;
+            maps[4 * (size_t)n + i] = l * l;
+            maps[5 * (size_t)n + i] = fabsf(l - samp(b, rx, ry));
+        }
+    // gm_box.wgsl:7-25, texture window (5 maps) then the decision window (3 maps)
+    int radii[2] = {g.r_blk, g.r_dwin}, chans[2] = {5, 3};
+    for (int pass = 0; pass < 2; pass++) {
+        int r = radii[pass], C = chans[pass];
+        for (int c = 0; c < C; c++)
+            for (int y = 0; y < hc; y++)
+                for (int x = 0; x < wc; x++) {
+                    size_t row = ((size_t)c * hc + y) * wc;
+                    float acc = 0.0f;
+                    for (int d = -r; d <= r; d++) acc = acc + maps[row + std::max(0, std::min(x + d, wc - 1))];
+                    tmp[row + x] = acc / (float)(2 * r + 1);
+                }
+        for (int c = 0; c < C; c++)
+            for (int y = 0; y < hc; y++)
+                for (int x = 0; x < wc; x++) {
+                    size_t plane = (size_t)c * hc * wc;
+                    float acc = 0.0f;
+                    for (int d = -r; d <= r; d++) acc = acc + tmp[plane + (size_t)std::max(0, std::min(y + d, hc - 1)) * wc + x];
+                    maps[plane + (size_t)y * wc + x] = acc / (float)(2 * r + 1);
+                }
+    }
+    // gm_select.wgsl:12-28 (eps 0, tex 0.015)
+    const float eps = 0.0f, tex = 0.015f;
+    for (int i = 0; i < h8; i++)
+        for (int j = 0; j < w8; j++) {
+            int x = std::max(0, std::min((int)floorf(((float)j + 0.5f) * (float)wc / (float)w8), wc - 1));
+            int y = std::max(0, std::min((int)floorf(((float)i + 0.5f) * (float)hc / (float)h8), hc - 1));
+            size_t idx = (size_t)y * wc + x;
+            float cm = maps[idx], ca = maps[n + idx], dv = maps[2 * (size_t)n + idx], lm = maps[3 * (size_t)n + idx],
+                  l2 = maps[4 * (size_t)n + idx];
+            float sd = sqrtf(std::max(l2 - lm * lm, 0.0f));
+            if (ca + eps < cm && dv > g.dmin && sd > tex) {
+                float xn = -1.0f + 2.0f * (float)j / (float)std::max(w8 - 1, 1);
+                float yn = -1.0f + 2.0f * (float)i / (float)std::max(h8 - 1, 1);
+                for (int c = 0; c < 4; c++) fl[(size_t)c * n8 + (size_t)i * w8 + j] = S(coef[c * 4] + coef[c * 4 + 1] * xn + coef[c * 4 + 2] * yn);
+            }
+        }
+    if (maps_out) *maps_out = maps;
+}
+
+// ------------------------------------------------------------------------------------------------- graph walk ----
+
+struct Opts {
+    int w, h, iw, ih, k, repair, cubic, keep_static, static_frames, static_tol, still, decisive, protection_mask;
+};
+
+struct Session {
+    const Model* m;
+    Opts o;
+    int wp, hp, iwp, ihp;
+    bool internal;
+    T a, b;                     // full-resolution padded inputs
+    T age, state, mask;         // static protection
+    bool protects = false;
+    StaticP sp{};
+    float min_age = 0;
+    std::map<std::string, T> env;       // after the pair stage
+    std::map<std::string, T> mid_env;   // after the last mid
+    T render;
+    size_t ms = 0, rend = 0;
+    bool have_pair = false;
+    std::vector<fhjson::Value> body;    // graph ops up to (not incl.) the final render_pix in internal mode
+    bool has_rop = false;
+    fhjson::Value rop;
+    std::vector<float> gm_maps;
+};
+
+static std::map<std::string, int> count_uses(const std::vector<fhjson::Value>& ops) {
+    std::map<std::string, int> u;
+    std::function<void(const fhjson::Value&)> rec = [&](const fhjson::Value& op) {
+        for (auto& n : names(op, "in")) u[n]++;
+        if (op["op"].as_str() == "repeat") {
+            const auto& b = op["body"];
+            for (size_t i = 0; i < b.size(); i++) rec(b[i]);
+        }
+    };
+    for (auto& op : ops) rec(op);
+    return u;
+}
+
+struct Walker {
+    Session& s;
+    std::map<std::string, int> uses;
+    float t;
+    Walker(Session& ss, float tt) : s(ss), t(tt) {}
+
+    std::vector<float> ones(int n) { return std::vector<float>(n, 1.0f); }
+
+    void build(const std::vector<fhjson::Value>& ops, std::map<std::string, T>& env) {
+        const Model& m = *s.m;
+        size_t i = 0;
+        while (i < ops.size()) {
+            const fhjson::Value& op = ops[i];
+            i++;
+            std::string name = op["op"].as_str();
+            auto ins = names(op, "in");
+            auto outs = names(op, "out");
+            if (name != "repeat" && name != "render_pix" && !outs.empty()) {
+                bool dead = true;
+                for (auto& o : outs)
+                    if (uses.count(o) && uses[o] > 0) dead = false;
+                if (dead) continue;  // net/build.rs:171-179
+            }
+            auto in = [&](size_t k) -> T {
+                auto it = env.find(ins.at(k));
+                if (it == env.end()) throw std::runtime_error("graph: " + name + " reads unknown tensor " + ins.at(k));
+                return it->second;
+            };
+            T res;
+            if (name == "repeat") {
+                int times = op["times"].is_u64() ? (int)op["times"].as_num() : s.o.k;
+                std::vector<fhjson::Value> body(op["body"].arr.begin(), op["body"].arr.end());
+                for (int r = 0; r < times; r++) build(body, env);
+                continue;
+            } else if (name == "interpolate") {
+                T x = in(0);
+                int oh, ow;
+                if (op["size"].as_str() == "HW") {
+                    oh = s.ihp;
+                    ow = s.iwp;
+                } else {
+                    float sc = (float)op["scale"].as_num();
+                    oh = (int)floorf((float)x.h * sc);
+                    ow = (int)floorf((float)x.w * sc);
+                }
+                res = k_interp(x, oh, ow, op["antialias"].as_bool(false));
+            } else if (name == "conv" || name == "conv2d") {
+                auto w = names(op, "w");
+                bool act = name == "conv";
+                auto sh = m.shape(w[0]);
+                int cout = sh[0];
+                int stride = op["stride"].is_u64() ? (int)op["stride"].as_num() : 1;
+                auto wt = m.weight(w[0]);
+                auto bias = m.weight(w[1]);
+                auto slope = act ? m.weight(w[2]) : ones(cout);
+                T x = mat(in(0));
+                int hout = (x.h + 2 - 3) / stride + 1, wout = (x.w + 2 - 3) / stride + 1;
+                // conv -> add peephole (net/build.rs:222-252): same rounding as the unfused binary add
+                if (i < ops.size() && ops[i]["op"].as_str() == "add" && uses[outs[0]] == 1) {
+                    auto ai = names(ops[i], "in");
+                    if (ai.size() == 2 && (ai[0] == outs[0] || ai[1] == outs[0])) {
+                        const std::string& other = ai[0] == outs[0] ? ai[1] : ai[0];
+                        auto it = env.find(other);
+                        if (it != env.end() && it->second.plain() && it->second.c == cout && it->second.h == hout &&
+                            it->second.w == wout) {
+                            T r = it->second;
+                            env[names(ops[i], "out")[0]] = k_conv(x, wt, bias, slope, cout, stride, &r);
+                            i++;
+                            continue;
+                        }
+                    }
+                }
+                res = k_conv(x, wt, bias, slope, cout, stride, nullptr);
+            } else if (name == "avgpool") {
+                res = k_avgpool(mat(in(0)), (int)op["k"].as_num());
+            } else if (name == "warp") {
+                res = k_warp(in(0), in(1));
+            } else if (name == "concat") {
+                std::vector<T> ts;
+                for (size_t k = 0; k < ins.size(); k++) ts.push_back(in(k));
+                res = k_concat(ts);
+            } else if (name == "slice") {
+                res = in(0).view((int)op["a"].as_num(), (int)op["b"].as_num());
+            } else if (name == "scale") {
+                res = in(0).scaled((float)op["factor"].as_num());
+            } else if (name == "mul_t") {
+                bool fwd = op["mode"].as_str() == "fwd";
+                float f = fwd ? 2.0f * t : 2.0f * (1.0f - t);
+                res = k_unary(in(0), 0, f, 0.0f);
+            } else if (name == "neg") {
+                res = in(0).scaled(-1.0f);
+            } else if (name == "add") {
+                res = k_binary(in(0), in(1), 0);
+            } else if (name == "mul") {
+                res = k_binary(in(0), in(1), 1);
+            } else if (name == "zeros") {
+                T r = in(0);
+                res = alloc((int)op["ch"].as_num(), r.h, r.w);
+            } else if (name == "zeros_like") {
+                T r = in(0);
+                res = alloc(r.c, r.h, r.w);
+            } else if (name == "copy") {
+                res = in(0);
+            } else if (name == "luma") {
+                res = k_luma(in(0), false);
+            } else if (name == "luma_grad") {
+                res = k_luma(mat(in(0)), true);
+            } else if (name == "sad_volume") {
+                res = k_sad(mat(in(0)), mat(in(1)), (int)op["radius"].as_num());
+            } else if (name == "affine_out") {
+                res = k_unary(in(0), 2, 0.0f, 0.0f);
+            } else if (name == "clamp") {
+                res = k_unary(in(0), 1, (float)op["lo"].as_num(), (float)op["hi"].as_num());
+            } else if (name == "film_mlp") {
+                // net/build.rs:332-359: g = b2 + W2 relu(w1 t + b1) in f32 on the host, stored f16
+                auto w1 = m.weight("film.film.0.weight"), b1 = m.weight("film.film.0.bias");
+                auto w2 = m.weight("film.film.2.weight"), b2 = m.weight("film.film.2.bias");
+                int hid = (int)b1.size(), no = (int)b2.size();
+                std::vector<float> hv(hid);
+                for (int k = 0; k < hid; k++) hv[k] = std::max(w1[k] * t + b1[k], 0.0f);
+                res = alloc(no, 1, 1);
+                for (int oo = 0; oo < no; oo++) {
+                    float acc = 0.0f;
+                    for (int k = 0; k < hid; k++) acc += w2[(size_t)oo * hid + k] * hv[k];
+                    res.buf->d[oo] = S(b2[oo] + acc);
+                }
+            } else if (name == "film_modulate") {
+                res = k_film(mat(in(0)), mat(in(1)));
+            } else if (name == "render_pix") {
+                T A = mat(in(0)), B = mat(in(1)), rt = mat(in(4));
+                T ftq = in(2), vtq = in(3);
+                RenderArgs ra{ftq.scale, ftq.scale, s.o.cubic != 0, render_flags(), s.protects ? &s.age : nullptr, s.min_age};
+                res = k_render(A, B, ftq, vtq, rt, ra);
+            } else if (name == "convex_upsample") {
+                T h = mat(in(0)), x = mat(in(1));
+                auto ub = m.weight("up.w.bias");
+                T wt36 = k_conv(h, m.weight("up.w.weight"), ub, ones(36), 36, 1, nullptr);
+                res = k_convex(wt36, x);
+            } else if (name == "blend_weights") {
+                // blendmix peephole (net/build.rs:417-470)
+                bool fused = false;
+                if (i + 3 <= ops.size()) {
+                    const auto &m1 = ops[i], &m2 = ops[i + 1], &ad = ops[i + 2];
+                    auto i1 = names(m1, "in"), i2 = names(m2, "in"), ia = names(ad, "in");
+                    auto o1 = names(m1, "out"), o2 = names(m2, "out");
+                    auto only = [&](const std::string& nn) { return uses.count(nn) && uses[nn] == 1; };
+                    if (m1["op"].as_str() == "mul" && m2["op"].as_str() == "mul" && ad["op"].as_str() == "add" &&
+                        i1.size() == 2 && i2.size() == 2 && ia.size() == 2 && i1[1] == outs[0] && i2[1] == outs[1] &&
+                        ia[0] == o1[0] && ia[1] == o2[0] && only(outs[0]) && only(outs[1]) && only(o1[0]) && only(o2[0])) {
+                        T wa = mat(env.at(i1[0])), wb = mat(env.at(i2[0]));
+                        env[names(ad, "out")[0]] = k_blendmix(wa, wb, in(0));
+                        i += 3;
+                        fused = true;
+                    }
+                }
+                if (fused) continue;
+                T bw = k_blend(in(0));
+                env[outs[0]] = bw.view(0, 1);
+                env[outs[1]] = bw.view(1, 2);
+                continue;
+            } else {
+                throw std::runtime_error("graph: unhandled op " + name);
+            }
+            env[outs[0]] = res;
+        }
+    }
+    uint32_t render_flags() const { return (s.o.decisive ? 1u : 0u) | (s.o.still ? 2u : 0u); }
+};
+
+static void default_internal(int w, int h, int& iw, int& ih) {
+    // options.rs:348-356
+    if (std::max(w, h) <= 960) {
+        iw = w;
+        ih = h;
+        return;
+    }
+    double s = std::min(480.0 / (double)h, 1.0);
+    int rw = std::max((int)std::round((double)w * s / 8.0) * 8, 64);
+    int rh = std::max((int)std::round((double)h * s / 8.0) * 8, 64);
+    iw = std::min(rw, w);
+    ih = std::min(rh, h);
+}
+
+static size_t mid_start(const std::vector<fhjson::Value>& ops) {
+    for (size_t i = 0; i < ops.size(); i++) {
+        std::string n = ops[i]["op"].as_str();
+        if (n == "mul_t" || n == "film_mlp") return i;
+        for (auto& x : names(ops[i], "in"))
+            if (x == "t") return i;
+    }
+    return ops.size();
+}
+
+static Session* session_new(const Model* m, const Opts& o) {
+    auto* s = new Session();
+    s->m = m;
+    s->o = o;
+    if (s->o.iw == 0 || s->o.ih == 0) default_internal(o.w, o.h, s->o.iw, s->o.ih);
+    s->o.iw = std::min(s->o.iw, o.w);
+    s->o.ih = std::min(s->o.ih, o.h);
+    s->hp = (o.h + 31) / 32 * 32;
+    s->wp = (o.w + 31) / 32 * 32;
+    s->ihp = (s->o.ih + 31) / 32 * 32;
+    s->iwp = (s->o.iw + 31) / 32 * 32;
+    s->internal = !(s->iwp == s->wp && s->ihp == s->hp);
+    s->a = alloc(3, s->hp, s->wp);
+    s->b = alloc(3, s->hp, s->wp);
+    s->protects = o.keep_static || o.protection_mask;
+    int frames = o.keep_static ? std::min(std::max(o.static_frames, 1), 255) : 2;  // options.rs:385-392
+    s->min_age = (float)frames;
+    s->sp = StaticP{s->wp, s->hp, s->wp, s->hp,
+                    o.keep_static ? ((float)std::min(o.static_tol, 255) + 0.5f) / 255.0f : 0.0f, (float)frames,
+                    o.protection_mask};
+    if (s->protects) {
+        s->age = alloc(1, s->hp, s->wp);
+        s->state = alloc(3, s->hp, s->wp);
+        s->mask = alloc(1, s->hp, s->wp);
+    }
+    std::vector<fhjson::Value> ops(m->graph["ops"].arr.begin(), m->graph["ops"].arr.end());
+    size_t rend = ops.size();
+    for (size_t i = ops.size(); i-- > 0;)
+        if (ops[i]["op"].as_str() == "render_pix") {
+            rend = i;
+            break;
+        }
+    if (s->internal && rend < ops.size()) {
+        s->body.assign(ops.begin(), ops.begin() + rend);
+        s->has_rop = true;
+        s->rop = ops[rend];
+    } else {
+        s->body = ops;
+    }
+    s->ms = mid_start(s->body);
+    return s;
+}
+
+// net/session_ext.rs:377-443 + net/build.rs:576-661: tex_in x2, static age, internal downscale, pair ops, GMHS
+static void session_pair(Session* s, const uint8_t* ra, const uint8_t* rb) {
+    k_tex_in(ra, s->o.w, s->o.h, s->a);
+    k_tex_in(rb, s->o.w, s->o.h, s->b);
+    if (s->protects) k_static_age(s->a, s->b, s->sp, &s->mask, s->state, s->age);
+    std::map<std::string, T> env;
+    if (s->internal) {
+        env["A"] = k_interp(s->a, s->ihp, s->iwp, true);
+        env["B"] = k_interp(s->b, s->ihp, s->iwp, true);
+    } else {
+        env["A"] = s->a;
+        env["B"] = s->b;
+    }
+    std::vector<fhjson::Value> pair_ops(s->body.begin(), s->body.begin() + s->ms);
+    Walker wk(*s, 0.5f);
+    wk.uses = count_uses(std::vector<fhjson::Value>(s->m->graph["ops"].arr.begin(), s->m->graph["ops"].arr.end()));
+    wk.build(pair_ops, env);
+    if (s->o.repair > 0) {
+        T f;
+        if (env.count("flow")) f = env["flow"];
+        else if (env.count("flowf")) {
+            f = env["flowf"];
+            f.c = 4;
+            f.c0 = 0;
+            f.scale = 1.0f;
+        }
+        if (f.buf && f.plain()) gm_run(env["A"], env["B"], f, s->wp, s->o.repair, &s->gm_maps);
+    }
+    s->env = env;
+    s->have_pair = true;
+}
+
+// net/session_ext.rs:445-468 + net/build.rs:693-756: mid ops at t, full-resolution render, keep_static, tex_out
+static void session_mid(Session* s, float t, uint8_t* out) {
+    if (!s->have_pair) throw std::runtime_error("pair two input slots first");
+    std::map<std::string, T> env = s->env;
+    std::vector<fhjson::Value> mid_ops(s->body.begin() + s->ms, s->body.end());
+    Walker wk(*s, t);
+    wk.uses = count_uses(std::vector<fhjson::Value>(s->m->graph["ops"].arr.begin(), s->m->graph["ops"].arr.end()));
+    wk.build(mid_ops, env);
+    if (s->has_rop) {
+        auto ins = names(s->rop, "in");
+        T ftq = env.at(ins[2]), vtq = env.at(ins[3]);
+        T rt = mat(env.at(ins[4]));
+        float fsx = ftq.scale * (float)s->wp / (float)s->iwp, fsy = ftq.scale * (float)s->hp / (float)s->ihp;
+        RenderArgs ra{fsx, fsy, s->o.cubic != 0, wk.render_flags(), s->protects ? &s->age : nullptr, s->min_age};
+        env[names(s->rop, "out")[0]] = k_render(s->a, s->b, ftq, vtq, rt, ra);
+    }
+    T r = env.at("render");
+    if (s->protects) {
+        // render tensors are fresh per mid: the in-place apply rewrites this mid's own render
+        k_static_apply(s->age, s->a, s->b, s->sp, r);
+    }
+    s->render = r;
+    s->mid_env = env;
+    if (out) k_tex_out(r, s->o.w, s->o.h, out);
+}
+
+// --------------------------------------------------------------------------------------------------------- C API ----
+
+extern "C" {
+
+const char* or_error() { return g_err.c_str(); }
+
+void* or_model_load(const char* dir) {
+    try {
+        auto* m = new Model();
+        std::string d(dir);
+        m->graph = fhjson::parse(slurp(d + "/graph.json"));
+        m->man = fhjson::parse(slurp(d + "/flyhighfg.json"));
+        std::string b = slurp(d + "/flyhighfg.bin");
+        m->bin.assign(b.begin(), b.end());
+        m->render_cubic = m->man["meta"]["render_sampling"].as_str() == "bicubic";
+        return m;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return nullptr;
+    }
+}
+void or_model_free(void* m) { delete (Model*)m; }
+int or_model_cubic(void* m) { return ((Model*)m)->render_cubic ? 1 : 0; }
+
+// options as an int array: w, h, iw, ih, k, repair, cubic(-1 = the model's), keep_static, static_frames, static_tol,
+// still, decisive, protection_mask
+void* or_session_new(void* model, const int* o) {
+    try {
+        Model* m = (Model*)model;
+        Opts op{o[0], o[1], o[2], o[3], o[4], o[5], o[6] < 0 ? (m->render_cubic ? 1 : 0) : o[6], o[7], o[8], o[9], o[10], o[11], o[12]};
+        return session_new(m, op);
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return nullptr;
+    }
+}
+void or_session_free(void* s) { delete (Session*)s; }
+
+int or_pair(void* s, const uint8_t* a, const uint8_t* b) {
+    try {
+        session_pair((Session*)s, a, b);
+        return 0;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+int or_mid(void* s, float t, uint8_t* out) {
+    try {
+        session_mid((Session*)s, t, out);
+        return 0;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+// protection mask (one byte per frame pixel, replicate-padded like SessionExt::write_mask, net/session_ext.rs:156-178)
+int or_write_mask(void* sp, const uint8_t* mask) {
+    Session* s = (Session*)sp;
+    if (!s->protects) return -1;
+    for (int y = 0; y < s->hp; y++)
+        for (int x = 0; x < s->wp; x++)
+            s->mask.buf->d[(size_t)y * s->wp + x] = S(mask[(size_t)std::min(y, s->o.h - 1) * s->o.w + std::min(x, s->o.w - 1)] ? 1.0f : 0.0f);
+    return 0;
+}
+
+// a tensor of the last pair (stage 0) or mid (stage 1) env, as f32 [c][h][w] with its view applied; "render", "age",
+// "state", "a", "b" name the session's own planes. Returns c*h*w, or -1 (unknown name) / -2 (cap too small).
+long or_tensor(void* sp, int stage, const char* name, float* out, long cap, int* dims) {
+    Session* s = (Session*)sp;
+    std::string n(name);
+    T t;
+    if (n == "age") t = s->age;
+    else if (n == "state") t = s->state;
+    else if (n == "a") t = s->a;
+    else if (n == "b") t = s->b;
+    else if (n == "render" && stage == 1) t = s->render;
+    else {
+        auto& e = stage == 0 ? s->env : s->mid_env;
+        auto it = e.find(n);
+        if (it == e.end()) return -1;
+        t = it->second;
+    }
+    if (!t.buf) return -1;
+    long total = (long)t.c * t.h * t.w;
+    dims[0] = t.c;
+    dims[1] = t.h;
+    dims[2] = t.w;
+    if (!out) return total;
+    if (cap < total) return -2;
+    size_t hw = (size_t)t.h * t.w;
+    for (int c = 0; c < t.c; c++)
+        for (size_t i = 0; i < hw; i++) out[(size_t)c * hw + i] = L(t.buf->d[(size_t)(c + t.c0) * hw + i]) * t.scale;
+    return total;
+}
+
+// derived session sizes: hp, wp, ihp, iwp, internal, gm r_blk, r_dwin, hc, wc (ints) and dmin, delta, fsx, fsy (floats)
+void or_session_dims(void* sp, int* iv, float* fv) {
+    Session* s = (Session*)sp;
+    iv[0] = s->hp;
+    iv[1] = s->wp;
+    iv[2] = s->ihp;
+    iv[3] = s->iwp;
+    iv[4] = s->internal;
+    GmParams g = gm_params(s->ihp, s->iwp, s->wp, std::max(s->o.repair, 1));
+    iv[5] = g.r_blk;
+    iv[6] = g.r_dwin;
+    iv[7] = g.hc;
+    iv[8] = g.wc;
+    fv[0] = g.dmin;
+    fv[1] = g.delta;
+    fv[2] = (float)s->wp / (float)s->iwp;
+    fv[3] = (float)s->hp / (float)s->ihp;
+}
+
+// ---- single kernels on caller planes (f16 bits), for per-kernel parity tests ----
+
+// conv: x [cin][h][w], wt [cout][cin][3][3] f32, bias/slope [cout] f32 (slope NULL = identity), resid [cout][ho][wo]
+// or NULL; out [cout][ho][wo] f16 bits
+int or_conv(const uint16_t* x, int cin, int h, int w, const float* wt, const float* bias, const float* slope, int cout,
+            int stride, const uint16_t* resid, uint16_t* out) {
+    T xt = alloc(cin, h, w);
+    memcpy(xt.buf->d.data(), x, xt.n() * 2);
+    std::vector<float> W(wt, wt + (size_t)cout * cin * 9), B(bias, bias + cout),
+        Sl = slope ? std::vector<float>(slope, slope + cout) : std::vector<float>(cout, 1.0f);
+    int ho = (h - 1) / stride + 1, wo = (w - 1) / stride + 1;
+    T r;
+    if (resid) {
+        r = alloc(cout, ho, wo);
+        memcpy(r.buf->d.data(), resid, r.n() * 2);
+    }
+    T o = k_conv(xt, W, B, Sl, cout, stride, resid ? &r : nullptr);
+    memcpy(out, o.buf->d.data(), o.n() * 2);
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,149 @@
+"""TEST INFRASTRUCTURE — ctypes front of the CPU oracle (oracle/oracle.cpp).
+
+The oracle restates the reference's Session::pair / Session::mid (the FlyHighFG Core graph, its WGSL kernels and the
+net/build.rs planner semantics) on the host cores. Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline
+legs use it, as the checker and as the timed CPU baseline; the product never imports this module.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from ctypes import POINTER, c_char_p, c_float, c_int, c_long, c_uint8, c_uint16, c_void_p
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "liboracle.so")
+
+
+def build() -> str:
+    """Compile liboracle.so with the Makefile beside this file (a few seconds)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB):
+            build()
+        L = ctypes.CDLL(LIB)
+        L.or_error.restype = c_char_p
+        L.or_model_load.restype = c_void_p
+        L.or_model_load.argtypes = [c_char_p]
+        L.or_model_free.argtypes = [c_void_p]
+        L.or_model_cubic.argtypes = [c_void_p]
+        L.or_session_new.restype = c_void_p
+        L.or_session_new.argtypes = [c_void_p, POINTER(c_int)]
+        L.or_session_free.argtypes = [c_void_p]
+        L.or_pair.argtypes = [c_void_p, POINTER(c_uint8), POINTER(c_uint8)]
+        L.or_mid.argtypes = [c_void_p, c_float, POINTER(c_uint8)]
+        L.or_write_mask.argtypes = [c_void_p, POINTER(c_uint8)]
+        L.or_tensor.restype = c_long
+        L.or_tensor.argtypes = [c_void_p, c_int, c_char_p, POINTER(c_float), c_long, POINTER(c_int)]
+        L.or_session_dims.argtypes = [c_void_p, POINTER(c_int), POINTER(c_float)]
+        L.or_conv.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, POINTER(c_float), POINTER(c_float),
+                              POINTER(c_float), c_int, c_int, POINTER(c_uint16), POINTER(c_uint16)]
+        _lib = L
+    return _lib
+
+
+def _u8(a: np.ndarray):
+    return a.ctypes.data_as(POINTER(c_uint8))
+
+
+class OracleModel:
+    """graph.json + flyhighfg.json + flyhighfg.bin from a model directory."""
+
+    def __init__(self, directory: str):
+        self.h = lib().or_model_load(directory.encode())
+        if not self.h:
+            raise RuntimeError(lib().or_error().decode())
+
+    @property
+    def cubic(self) -> bool:
+        return bool(lib().or_model_cubic(self.h))
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().or_model_free(self.h)
+            self.h = None
+
+
+class OracleSession:
+    """The reference session semantics on the CPU: defaults of SessionOptions::new (session.rs:118-135) with the
+    still test on (options.rs:296-298)."""
+
+    def __init__(self, model: OracleModel, width: int, height: int, internal=(0, 0), k: int = 1, repair: int = 1,
+                 cubic: int = -1, keep_static: bool = True, static_frames: int = 8, static_tolerance: int = 4,
+                 still: bool = True, decisive: bool = False, protection_mask: bool = False):
+        self.model = model
+        self.w, self.h = width, height
+        o = (c_int * 13)(width, height, internal[0], internal[1], k, repair, cubic, int(keep_static), static_frames,
+                         static_tolerance, int(still), int(decisive), int(protection_mask))
+        self.s = lib().or_session_new(model.h, o)
+        if not self.s:
+            raise RuntimeError(lib().or_error().decode())
+
+    def pair(self, a: np.ndarray, b: np.ndarray) -> None:
+        a = np.ascontiguousarray(a, dtype=np.uint8)
+        b = np.ascontiguousarray(b, dtype=np.uint8)
+        assert a.size == self.w * self.h * 4 and b.size == a.size
+        if lib().or_pair(self.s, _u8(a), _u8(b)) != 0:
+            raise RuntimeError(lib().or_error().decode())
+
+    def mid(self, t: float) -> np.ndarray:
+        out = np.zeros(self.w * self.h * 4, np.uint8)
+        if lib().or_mid(self.s, c_float(t), _u8(out)) != 0:
+            raise RuntimeError(lib().or_error().decode())
+        return out
+
+    def write_mask(self, mask: np.ndarray) -> None:
+        m = np.ascontiguousarray(mask, dtype=np.uint8)
+        assert m.size == self.w * self.h
+        if lib().or_write_mask(self.s, _u8(m)) != 0:
+            raise RuntimeError("the session was built without protection_mask")
+
+    def tensor(self, name: str, stage: int = 0) -> np.ndarray:
+        """A tensor of the last pair (stage 0) or mid (stage 1), f32 [c][h][w] with its view applied."""
+        dims = (c_int * 3)()
+        n = lib().or_tensor(self.s, stage, name.encode(), None, 0, dims)
+        if n < 0:
+            raise KeyError(name)
+        out = np.zeros(n, np.float32)
+        lib().or_tensor(self.s, stage, name.encode(), out.ctypes.data_as(POINTER(c_float)), n, dims)
+        return out.reshape(dims[0], dims[1], dims[2])
+
+    def dims(self) -> dict:
+        iv = (c_int * 9)()
+        fv = (c_float * 4)()
+        lib().or_session_dims(self.s, iv, fv)
+        return dict(hp=iv[0], wp=iv[1], ihp=iv[2], iwp=iv[3], internal=bool(iv[4]), r_blk=iv[5], r_dwin=iv[6],
+                    hc=iv[7], wc=iv[8], dmin=fv[0], delta=fv[1], fsx=fv[2], fsy=fv[3])
+
+    def __del__(self):
+        if getattr(self, "s", None):
+            lib().or_session_free(self.s)
+            self.s = None
+
+
+def conv(x: np.ndarray, w: np.ndarray, bias: np.ndarray, slope, stride: int, resid=None) -> np.ndarray:
+    """One conv of the tensor-core path on CHW f16 x ([cin][h][w]) with torch-layout weights; f16 output."""
+    x = np.ascontiguousarray(x, dtype=np.float16)
+    cin, h, wd = x.shape
+    cout = w.shape[0]
+    ho, wo = (h - 1) // stride + 1, (wd - 1) // stride + 1
+    W = np.ascontiguousarray(w, dtype=np.float32)
+    B = np.ascontiguousarray(bias, dtype=np.float32)
+    Sl = None if slope is None else np.ascontiguousarray(slope, dtype=np.float32)
+    out = np.zeros((cout, ho, wo), np.float16)
+    R = None if resid is None else np.ascontiguousarray(resid, dtype=np.float16)
+    f = lambda a: a.ctypes.data_as(POINTER(c_float))
+    u = lambda a: a.ctypes.data_as(POINTER(c_uint16))
+    lib().or_conv(u(x), cin, h, wd, f(W), f(B), f(Sl) if Sl is not None else None, cout, stride,
+                  u(R) if R is not None else None, u(out))
+    return out
