@@ -1,0 +1,384 @@
+"""FlyHigh B200: the FlyHighFG Core (Session.pair / Session.mid) on an NVIDIA B200, through the drop-in C ABI.
+
+The classes mirror the reference's Python binding over its C ABI (bindings/python/flyhigh.py: Engine, Model, Session,
+FlyHighError), so a host written against it runs unchanged:
+
+    import flyhigh_engine_b200 as flyhigh
+    engine = flyhigh.Engine()
+    model = flyhigh.Model("models")                    # graph.json, flyhighfg.json, flyhighfg.bin
+    s = flyhigh.Session(engine, model, 1920, 1080)     # options as keyword arguments
+    a, b, out = s.add_input(), s.add_input(), s.add_output()
+    s.write(a, frame0); s.write(b, frame1)
+    s.pair(a, b); s.mid(0.5, out)
+    rgba = s.read(out)                                 # bytes, width * height * 4
+
+The library is libflyhigh.so next to this file (built by `flyhigh_engine_b200.build.build()`), or FLYHIGH_LIB.
+There is no fallback: without the CUDA library every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+from ctypes import (POINTER, Structure, byref, c_char_p, c_double, c_float, c_int, c_long, c_size_t, c_uint8, c_uint32,
+                    c_void_p, create_string_buffer)
+from typing import Optional
+
+__all__ = ["FlyHighError", "Engine", "Model", "Session", "library_path"]
+
+
+class FlyHighError(RuntimeError):
+    """A failed engine call, with the message of fh_last_error()."""
+
+
+class EngineOptions(Structure):  # flyhigh.h FhEngineOptions, field for field
+    _fields_ = [("backend", c_uint32), ("tensor_cores", c_uint32), ("autotune", c_uint32), ("adapter", c_char_p),
+                ("precision", c_uint32), ("tune_cache", c_char_p), ("compact_memory", c_uint32),
+                ("dxc_path", c_char_p)]
+
+
+class SessionOptions(Structure):  # flyhigh.h FhSessionOptions, field for field
+    _fields_ = [("width", c_uint32), ("height", c_uint32), ("internal_w", c_uint32), ("internal_h", c_uint32),
+                ("k", c_uint32), ("repair", c_uint32), ("render", c_uint32), ("keep_static", c_uint32),
+                ("static_frames", c_uint32), ("static_tolerance", c_uint32), ("fast_render", c_uint32),
+                ("linear_t", c_uint32), ("keep_maps", c_uint32), ("protection_mask", c_uint32), ("tune", c_char_p)]
+
+
+def library_path() -> str:
+    env = os.environ.get("FLYHIGH_LIB")
+    if env:
+        return env
+    return os.path.join(os.path.dirname(os.path.abspath(__file__)), "libflyhigh.so")
+
+
+_lib = None
+
+# every export of include/flyhigh.h and include/flyhigh_b200.h: (name, restype, argtypes)
+EXPORTS = [
+    ("fh_last_error", c_char_p, []),
+    ("fh_engine_options_default", EngineOptions, []),
+    ("fh_engine_create", c_void_p, [POINTER(EngineOptions)]),
+    ("fh_engine_destroy", None, [c_void_p]),
+    ("fh_engine_info", c_int, [c_void_p, c_char_p, c_size_t]),
+    ("fh_engine_report_json", c_int, [c_void_p, c_char_p, c_size_t]),
+    ("fh_model_load", c_void_p, [c_char_p]),
+    ("fh_model_from_bytes", c_void_p, [POINTER(c_uint8), c_size_t, POINTER(c_uint8), c_size_t, POINTER(c_uint8),
+                                       c_size_t]),
+    ("fh_model_destroy", None, [c_void_p]),
+    ("fh_model_info", c_int, [c_void_p, c_char_p, c_size_t]),
+    ("fh_session_options_default", SessionOptions, [c_uint32, c_uint32]),
+    ("fh_session_create", c_void_p, [c_void_p, c_void_p, POINTER(SessionOptions)]),
+    ("fh_session_destroy", None, [c_void_p]),
+    ("fh_session_add_input", c_int, [c_void_p]),
+    ("fh_session_add_output", c_int, [c_void_p]),
+    ("fh_session_write_rgba", c_int, [c_void_p, c_uint32, c_void_p, c_size_t]),
+    ("fh_session_write_mask", c_int, [c_void_p, c_void_p, c_size_t]),
+    ("fh_session_read_rgba", c_int, [c_void_p, c_uint32, c_void_p, c_size_t]),
+    ("fh_session_pair", c_int, [c_void_p, c_uint32, c_uint32]),
+    ("fh_session_mid", c_int, [c_void_p, c_float, c_uint32]),
+    ("fh_session_generate", c_int, [c_void_p, c_uint32, c_uint32, c_float, c_uint32]),
+    ("fh_session_pair_timed", c_int, [c_void_p, c_uint32, c_uint32, POINTER(c_double)]),
+    ("fh_session_mid_timed", c_int, [c_void_p, c_float, c_uint32, POINTER(c_double)]),
+    ("fh_session_warm_up", c_int, [c_void_p]),
+    ("fh_session_import_d3d11", c_int, [c_void_p, c_void_p, ctypes.c_ssize_t, c_uint32, c_uint32]),
+    ("fh_session_report_json", c_int, [c_void_p, c_char_p, c_size_t]),
+    ("fh_session_cuda_stream", c_int, [c_void_p, POINTER(c_void_p)]),
+    ("fh_session_slot_device_ptr", c_int, [c_void_p, c_uint32, c_int, POINTER(c_void_p)]),
+    ("fh_session_write_rgba_device", c_int, [c_void_p, c_uint32, c_void_p, c_size_t]),
+    ("fh_session_debug_tensor", c_long, [c_void_p, c_char_p, POINTER(c_float), c_size_t, POINTER(c_int)]),
+    ("fh_model_fingerprint", c_long, [c_void_p]),
+    ("fh_session_plan_params", c_int, [c_void_p, POINTER(SessionOptions), POINTER(c_int), POINTER(c_float)]),
+    ("fh_session_launch_counts", c_int, [c_void_p, POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
+    ("fhk_conv3x3", c_int, [c_void_p, c_int, c_int, c_void_p]),
+    ("fhk_conv_pack_weights", c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
+    ("fhk_conv_packed_elems", c_size_t, [c_int, c_int]),
+]
+
+
+def lib():
+    """The loaded libflyhigh.so (raises FlyHighError when it is missing: there is no CPU fallback)."""
+    global _lib
+    if _lib is None:
+        path = library_path()
+        if not os.path.exists(path):
+            raise FlyHighError(f"{path} is missing: build it with flyhigh_engine_b200.build.build()")
+        L = ctypes.CDLL(path)
+        for name, res, args in EXPORTS:
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _error() -> FlyHighError:
+    msg = lib().fh_last_error()
+    return FlyHighError(msg.decode("utf-8", "replace") if msg else "unknown error")
+
+
+def _check(rc: int) -> int:
+    if rc < 0:
+        raise _error()
+    return rc
+
+
+def _json(fn, handle) -> dict:
+    cap = 1 << 12
+    while True:
+        buf = create_string_buffer(cap)
+        n = fn(handle, buf, cap)
+        if n >= 0:
+            return json.loads(buf.raw[:n].decode("utf-8"))
+        if b"buffer too small" in (lib().fh_last_error() or b"") and cap < (1 << 24):
+            cap *= 4
+            continue
+        raise _error()
+
+
+def _buffer(data):
+    """(pointer, length, keep-alive) of a bytes-like object or numpy array, without a copy where possible."""
+    try:
+        import numpy as np
+        if isinstance(data, np.ndarray):
+            a = np.ascontiguousarray(data)
+            return a.ctypes.data_as(c_void_p), a.nbytes, a
+    except ImportError:
+        pass
+    mv = memoryview(data).cast("B")
+    if mv.readonly:
+        b = ctypes.create_string_buffer(bytes(mv), len(mv))
+        return ctypes.cast(b, c_void_p), len(mv), b
+    arr = (c_uint8 * len(mv)).from_buffer(mv)
+    return ctypes.cast(arr, c_void_p), len(mv), arr
+
+
+_PRECISION = {"auto": 0, "f16": 1, "f32": 2}
+_RENDER = {"model": 0, "bilinear": 1, "bicubic": 2}
+
+
+class Engine:
+    """The device: Engine(adapter=None | "#N" (CUDA device N), precision="auto"|"f16"). The graphics-API options of
+    the reference (backend, dxc_path, ...) are accepted and ignored."""
+
+    def __init__(self, backend: str = "auto", precision: str = "auto", tensor_cores: bool = True, autotune: bool = True,
+                 adapter: Optional[str] = None, tune_cache: Optional[str] = None, compact_memory: bool = True,
+                 dxc_path: Optional[str] = None):
+        L = lib()
+        o = L.fh_engine_options_default()
+        o.precision = _PRECISION[precision]
+        o.tensor_cores = int(tensor_cores)
+        o.autotune = int(autotune)
+        o.compact_memory = int(compact_memory)
+        self._keep = [s.encode() if s else None for s in (adapter, tune_cache, dxc_path)]
+        o.adapter, o.tune_cache, o.dxc_path = self._keep
+        self._h = L.fh_engine_create(byref(o))
+        if not self._h:
+            raise _error()
+
+    def info(self) -> dict:
+        return _json(lib().fh_engine_info, self._h)
+
+    def report(self) -> dict:
+        return _json(lib().fh_engine_report_json, self._h)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().fh_engine_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __del__(self):
+        self.close()
+
+
+class Model:
+    """Model(directory) with graph.json, flyhighfg.json and flyhighfg.bin; or Model.from_bytes(...)."""
+
+    def __init__(self, directory: Optional[str] = None, _handle=None):
+        if _handle is not None:
+            self._h = _handle
+        else:
+            self._h = lib().fh_model_load(str(directory).encode())
+        if not self._h:
+            raise _error()
+
+    @classmethod
+    def from_bytes(cls, graph_json: bytes, manifest_json: bytes, weights: bytes) -> "Model":
+        bufs = [(c_uint8 * len(b)).from_buffer_copy(b) for b in (graph_json, manifest_json, weights)]
+        h = lib().fh_model_from_bytes(bufs[0], len(graph_json), bufs[1], len(manifest_json), bufs[2], len(weights))
+        if not h:
+            raise _error()
+        return cls(_handle=h)
+
+    def info(self) -> dict:
+        return _json(lib().fh_model_info, self._h)
+
+    def fingerprint(self) -> int:
+        return int(lib().fh_model_fingerprint(self._h))
+
+    def plan_params(self, width: int, height: int, **options) -> dict:
+        """The sizes and parameter words a session of these options derives (no device needed)."""
+        o = session_options(width, height, **options)
+        iv = (c_int * 22)()
+        fv = (c_float * 6)()
+        _check(lib().fh_session_plan_params(self._h, byref(o), iv, fv))
+        names = ["hp", "wp", "ihp", "iwp", "internal", "NH", "NW", "qh", "qw", "h8", "w8", "h16", "w16", "hc", "wc",
+                 "r_blk", "r_dwin", "k", "repair", "cubic", "protects", "render_flags"]
+        d = dict(zip(names, list(iv)))
+        d.update(zip(["fsx", "fsy", "dmin", "delta", "min_age", "static_thr"], list(fv)))
+        return d
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().fh_model_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __del__(self):
+        self.close()
+
+
+def session_options(width: int, height: int, internal=None, k: int = 1, repair: int = 1, render: str = "model",
+                    static_protection=None, fast_render: bool = False, linear_t: bool = False,
+                    keep_maps: bool = False, protection_mask: bool = False, tune: Optional[str] = None) -> SessionOptions:
+    o = lib().fh_session_options_default(width, height)
+    if internal == "frame":
+        o.internal_w, o.internal_h = width, height
+    elif internal not in (None, "auto"):
+        o.internal_w, o.internal_h = int(internal[0]), int(internal[1])
+    o.k = k
+    o.repair = repair
+    o.render = _RENDER[render]
+    if static_protection is False:
+        o.keep_static = 0
+    elif static_protection:
+        o.keep_static = 1
+        if isinstance(static_protection, dict):
+            o.static_frames = int(static_protection.get("frames", o.static_frames))
+            o.static_tolerance = int(static_protection.get("tolerance", o.static_tolerance))
+    o.fast_render = int(fast_render)
+    o.linear_t = int(linear_t)
+    o.keep_maps = int(keep_maps)
+    o.protection_mask = int(protection_mask)
+    o.tune = tune.encode() if tune else None
+    return o
+
+
+class Session:
+    """The plans of a model for one frame size: Session(engine, model, width, height, internal="auto"|"frame"|(w, h),
+    k=1, repair=1, render="model"|"bilinear"|"bicubic", static_protection=None|True|False|{"frames", "tolerance"},
+    keep_maps=False, protection_mask=False)."""
+
+    def __init__(self, engine: Engine, model: Model, width: int, height: int, **options):
+        self._o = session_options(width, height, **options)
+        self.width, self.height = width, height
+        self._e, self._m = engine, model
+        self._h = lib().fh_session_create(engine._h, model._h, byref(self._o))
+        if not self._h:
+            raise _error()
+
+    def add_input(self) -> int:
+        return _check(lib().fh_session_add_input(self._h))
+
+    def add_output(self) -> int:
+        return _check(lib().fh_session_add_output(self._h))
+
+    def write(self, slot: int, rgba) -> None:
+        p, n, _keep = _buffer(rgba)
+        _check(lib().fh_session_write_rgba(self._h, slot, p, n))
+
+    def write_device(self, slot: int, device_ptr: int, nbytes: int) -> None:
+        """A frame already in device memory (a CUDA pointer) into an input slot."""
+        _check(lib().fh_session_write_rgba_device(self._h, slot, c_void_p(device_ptr), nbytes))
+
+    def write_mask(self, mask) -> None:
+        p, n, _keep = _buffer(mask)
+        _check(lib().fh_session_write_mask(self._h, p, n))
+
+    def read(self, slot: int) -> bytes:
+        n = self.width * self.height * 4
+        buf = (c_uint8 * n)()
+        _check(lib().fh_session_read_rgba(self._h, slot, ctypes.cast(buf, c_void_p), n))
+        return bytes(buf)
+
+    def read_into(self, slot: int, out) -> None:
+        """Into a caller buffer (e.g. pinned host memory: a numpy array over it, or a torch tensor's data_ptr())."""
+        if isinstance(out, int):
+            p, n = c_void_p(out), self.width * self.height * 4
+        else:
+            p, n, _keep = _buffer(out)
+        _check(lib().fh_session_read_rgba(self._h, slot, p, n))
+
+    def pair(self, a: int, b: int) -> None:
+        _check(lib().fh_session_pair(self._h, a, b))
+
+    def mid(self, t: float, out: int) -> None:
+        _check(lib().fh_session_mid(self._h, t, out))
+
+    def generate(self, a: int, b: int, t: float, out: int) -> None:
+        _check(lib().fh_session_generate(self._h, a, b, t, out))
+
+    def pair_timed(self, a: int, b: int) -> Optional[float]:
+        ms = c_double()
+        return ms.value if _check(lib().fh_session_pair_timed(self._h, a, b, byref(ms))) == 1 else None
+
+    def mid_timed(self, t: float, out: int) -> Optional[float]:
+        ms = c_double()
+        return ms.value if _check(lib().fh_session_mid_timed(self._h, t, out, byref(ms))) == 1 else None
+
+    def warm_up(self) -> None:
+        _check(lib().fh_session_warm_up(self._h))
+
+    def report(self) -> dict:
+        return _json(lib().fh_session_report_json, self._h)
+
+    # ---- additions (include/flyhigh_b200.h) ----
+    def cuda_stream(self) -> int:
+        p = c_void_p()
+        _check(lib().fh_session_cuda_stream(self._h, byref(p)))
+        return p.value or 0
+
+    def slot_ptr(self, slot: int, output: bool = False) -> int:
+        p = c_void_p()
+        _check(lib().fh_session_slot_device_ptr(self._h, slot, int(output), byref(p)))
+        return p.value
+
+    def launch_counts(self) -> dict:
+        a, b, c = c_int(), c_int(), c_int()
+        _check(lib().fh_session_launch_counts(self._h, byref(a), byref(b), byref(c)))
+        return {"pair": a.value, "mid": b.value, "frame": c.value}
+
+    def tensor(self, name: str):
+        """A tensor of the last pair / mid as a float32 numpy array [c][h][w] (the reference's planar order)."""
+        import numpy as np
+        dims = (c_int * 3)()
+        n = lib().fh_session_debug_tensor(self._h, name.encode(), None, 0, dims)
+        if n < 0:
+            raise _error()
+        out = np.zeros(n, np.float32)
+        _check(lib().fh_session_debug_tensor(self._h, name.encode(), out.ctypes.data_as(POINTER(c_float)), n, dims))
+        return out.reshape(dims[0], dims[1], dims[2])
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().fh_session_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __del__(self):
+        self.close()

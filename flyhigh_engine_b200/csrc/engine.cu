@@ -1,0 +1,1307 @@
+// The host runtime behind flyhigh.h: model loading and validation, the session planner for the FlyHighFG Core graph,
+// device buffers, CUDA Graph capture of the frame / pair / mid stages, and the C exports.
+//
+// Reference: crates/flyhigh-engine/src/{model, session.rs, net/build.rs, net/session_ext.rs} and
+// crates/flyhigh-capi/src/{core.rs, lib.rs}. The reference walks graph.json op by op into ~90 WGSL dispatches per
+// interval; this planner recognises the FlyHighFG graph (checked by a structural fingerprint) and schedules it as ~45
+// fused CUDA kernels over NHWC f16 buffers, captured as one CUDA Graph per stage:
+//   frame (per input slot, cached until the slot is rewritten): rgba8 -> network input -> aq / i8 / i16 -> encoders
+//   pair  (per slot pair): static age, coarse cost volume + coarse convs, flow upsample, K fine iterations, GMHS, the
+//         convex-upsample weights (t-independent: moved here from the mid stage)
+//   mid   (per phase t): FiLM, FiLM convs, combine, convex upsample, refine head, fused render + keep_static + rgba8
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <memory>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/flyhigh.h"
+#include "../../include/flyhigh_b200.h"
+#include "fh_kernels.h"
+#include "json.hpp"
+#include "stages.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+struct Error : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+[[noreturn]] void fail(const char* fmt, ...) {
+    char b[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(b, sizeof b, fmt, ap);
+    va_end(ap);
+    throw Error(b);
+}
+
+#define CK(x)                                                                                        \
+    do {                                                                                             \
+        cudaError_t e_ = (x);                                                                        \
+        if (e_ != cudaSuccess) fail("CUDA error %s (%s) in %s", cudaGetErrorName(e_), cudaGetErrorString(e_), #x); \
+    } while (0)
+
+int write_json(const std::string& s, char* buf, size_t cap) {
+    if (!buf) fail("null argument");
+    if (s.size() + 1 > cap) fail("buffer too small (%zu needed)", s.size() + 1);
+    memcpy(buf, s.data(), s.size());
+    buf[s.size()] = 0;
+    return (int)s.size();
+}
+
+std::string slurp(const std::string& p) {
+    std::ifstream f(p, std::ios::binary);
+    if (!f) fail("read %s: cannot open", p.c_str());
+    std::stringstream ss;
+    ss << f.rdbuf();
+    return ss.str();
+}
+
+// --------------------------------------------------------------------------------------------------- the model ----
+
+// canonical form of a JSON value (sorted keys) for the graph fingerprint
+void canon(const fhjson::Value& v, std::string& o) {
+    switch (v.kind) {
+        case fhjson::Value::Null: o += "null"; break;
+        case fhjson::Value::Bool: o += v.b ? "true" : "false"; break;
+        case fhjson::Value::Number: {
+            char b[64];
+            if (v.num == std::floor(v.num) && std::fabs(v.num) < 1e15) snprintf(b, sizeof b, "%lld", (long long)v.num);
+            else snprintf(b, sizeof b, "%.9g", v.num);
+            o += b;
+            break;
+        }
+        case fhjson::Value::String: o += fhjson::quote(v.str); break;
+        case fhjson::Value::Array:
+            o += "[";
+            for (size_t i = 0; i < v.arr.size(); i++) {
+                if (i) o += ",";
+                canon(v.arr[i], o);
+            }
+            o += "]";
+            break;
+        case fhjson::Value::Object: {
+            std::vector<const std::pair<std::string, fhjson::Value>*> kv;
+            for (auto& p : v.obj) kv.push_back(&p);
+            std::sort(kv.begin(), kv.end(), [](auto* a, auto* b) { return a->first < b->first; });
+            o += "{";
+            for (size_t i = 0; i < kv.size(); i++) {
+                if (i) o += ",";
+                o += fhjson::quote(kv[i]->first) + ":";
+                canon(kv[i]->second, o);
+            }
+            o += "}";
+            break;
+        }
+    }
+}
+uint64_t fnv1a(const std::string& s) {
+    uint64_t h = 1469598103934665603ull;
+    for (unsigned char c : s) {
+        h ^= c;
+        h *= 1099511628211ull;
+    }
+    return h;
+}
+
+}  // namespace
+
+// the FlyHighFG v1 op list (models/graph.json) as this planner schedules it
+static const uint64_t kFlyHighFgGraph = 0xdd513ef76cf6ae5aull;
+
+struct FhModel {
+    fhjson::Value graph, man;
+    std::vector<uint8_t> bin;
+    bool cubic = false;
+    std::string name;
+    long long train_step = -1;
+    int format_version = 1;
+    size_t graph_ops = 0, tensors = 0;
+    uint64_t fingerprint = 0;
+
+    std::vector<int> shape(const std::string& n) const {
+        std::vector<int> s;
+        const auto& a = man["tensors"][n]["shape"];
+        for (size_t i = 0; i < a.size(); i++) s.push_back((int)a[i].as_num());
+        return s;
+    }
+    bool has(const std::string& n) const { return man["tensors"].find(n) != nullptr; }
+    std::vector<uint16_t> bits(const std::string& n) const {
+        if (!has(n)) fail("the manifest lacks tensor %s", n.c_str());
+        size_t off = (size_t)man["tensors"][n]["offset"].as_num(), cnt = 1;
+        for (int d : shape(n)) cnt *= (size_t)d;
+        std::vector<uint16_t> v(cnt);
+        for (size_t i = 0; i < cnt; i++) v[i] = (uint16_t)(bin[(off + i) * 2] | (bin[(off + i) * 2 + 1] << 8));
+        return v;
+    }
+    std::vector<float> f32(const std::string& n) const {
+        auto b = bits(n);
+        std::vector<float> v(b.size());
+        for (size_t i = 0; i < b.size(); i++) {
+            __half_raw r;
+            r.x = b[i];
+            v[i] = __half2float(__half(r));
+        }
+        return v;
+    }
+};
+
+namespace {
+
+// model/graph.rs:17-46
+void validate_ops(const fhjson::Value& ops, const fhjson::Value& tensors) {
+    static const char* film_w[4] = {"film.film.0.weight", "film.film.0.bias", "film.film.2.weight", "film.film.2.bias"};
+    for (size_t i = 0; i < ops.size(); i++) {
+        const auto& op = ops[i];
+        if (!op["op"].is_string()) fail("graph.json: op %zu has no name", i);
+        const std::string name = op["op"].str;
+        for (const char* key : {"in", "out", "w"}) {
+            const auto* l = op.find(key);
+            if (!l) continue;
+            if (!l->is_array()) fail("graph.json: %s.%s is not a list", name.c_str(), key);
+            for (auto& v : l->arr)
+                if (!v.is_string()) fail("graph.json: %s.%s has a non-string entry", name.c_str(), key);
+        }
+        for (auto& w : op["w"].arr)
+            if (!tensors.find(w.str)) fail("graph.json: %s reads tensor %s, which the manifest lacks", name.c_str(), w.str.c_str());
+        if (name == "repeat") {
+            if (!op["body"].is_array()) fail("graph.json: repeat without a body");
+            validate_ops(op["body"], tensors);
+        } else if (name == "film_mlp") {
+            for (auto* w : film_w)
+                if (!tensors.find(w)) fail("graph.json: film_mlp needs tensor %s, which the manifest lacks", w);
+        }
+    }
+}
+
+// model/mod.rs:54-107
+FhModel* model_from(const uint8_t* g, size_t gl, const uint8_t* m, size_t ml, const uint8_t* w, size_t wl) {
+    auto mod = std::make_unique<FhModel>();
+    try {
+        mod->man = fhjson::parse(m, ml);
+    } catch (std::exception& e) {
+        fail("parse manifest: %s", e.what());
+    }
+    if (!mod->man["tensors"].is_object()) fail("manifest has no tensors");
+    mod->cubic = mod->man["meta"]["render_sampling"].as_str() == "bicubic";
+    fhjson::Value graph;
+    try {
+        graph = fhjson::parse(g, gl);
+    } catch (std::exception& e) {
+        fail("parse graph.json: %s", e.what());
+    }
+    if (!graph["ops"].is_array()) fail("graph.json: no ops");
+    if (graph["ops"].size() == 0) fail("graph.json: no ops");
+    mod->bin.assign(w, w + wl);
+    const auto& meta = mod->man["meta"];
+    int fv = meta["format_version"].is_u64() ? (int)meta["format_version"].as_num() : 1;
+    if (fv != 1) fail("model format_version %d not supported, this engine reads 1..=1", fv);
+    mod->format_version = fv;
+    for (auto& kv : mod->man["tensors"].obj) {
+        const std::string& name = kv.first;
+        const auto& t = kv.second;
+        if (!t["offset"].is_u64()) fail("tensor %s: offset is not an unsigned integer", name.c_str());
+        if (!t["shape"].is_array()) fail("tensor %s: shape is not an array", name.c_str());
+        unsigned long long count = 1;
+        for (auto& d : t["shape"].arr) {
+            if (!d.is_u64()) fail("tensor %s: shape has a non-integer dimension", name.c_str());
+            if (d.num < 1) fail("tensor %s: shape has a zero dimension", name.c_str());
+            if (count > (1ull << 40) / (unsigned long long)d.num) fail("tensor %s: shape overflows", name.c_str());
+            count *= (unsigned long long)d.num;
+        }
+        unsigned long long end = ((unsigned long long)t["offset"].num + count) * 2;
+        if (end > wl) fail("tensor %s runs past the end of the weight blob", name.c_str());
+    }
+    validate_ops(graph["ops"], mod->man["tensors"]);
+    mod->graph = graph;
+    mod->name = meta["model"].as_str("?");
+    mod->train_step = meta["train_step"].is_number() ? (long long)meta["train_step"].num : -1;
+    mod->graph_ops = graph["ops"].size();
+    mod->tensors = mod->man["tensors"].size();
+    std::string c;
+    canon(graph["ops"], c);
+    mod->fingerprint = fnv1a(c);
+    return mod.release();
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------- the engine ----
+
+struct FhEngine {
+    int device = 0;
+    std::string name;
+    int sm_major = 0, sm_minor = 0, sms = 0;
+    size_t tensor_bytes = 0;
+    int graphs_built = 0;
+};
+
+// --------------------------------------------------------------------------------------------------- session ----
+
+namespace {
+
+inline int up8(int c) { return (c + 7) & ~7; }
+inline int up16(int c) { return (c + 15) & ~15; }
+
+struct ConvLayer {
+    std::string name;
+    int cin = 0, cout = 0, stride = 1, cp = 0;
+    bool act = true;
+    uint16_t* wpack = nullptr;
+    float* bias = nullptr;
+    float* slope = nullptr;
+    std::vector<FhConvSrc> src;  // layout only (p = offset from the view pointer; set per launch)
+};
+
+struct SrcSpec {
+    int cs, nc;
+    float scale;
+    std::vector<int> map;  // model input channel of each of the nc channels, -1 = none
+};
+
+struct InSlot {
+    uint8_t* frame = nullptr;
+    __half *A = nullptr, *aq = nullptr, *i8 = nullptr, *i16 = nullptr, *f8 = nullptr, *f16 = nullptr;
+    uint64_t gen = 1, feat_gen = 0;
+    cudaGraphExec_t graph = nullptr;
+};
+
+struct PairSrc {  // what the mid of the current pair reads from its two frames
+    const uint8_t *fa, *fb;
+    const __half *aq, *bq;
+    int a, b;
+};
+
+}  // namespace
+
+struct FhSession {
+    FhEngine* eng = nullptr;
+    const FhModel* model = nullptr;
+    FhSessionOptions o{};
+    // sizes (net/build.rs:548-550, session_ext.rs:100)
+    int w, h, wp, hp, iw, ih, ihp, iwp, NH, NW, qh, qw, h8, w8, h16, w16, hc, wc;
+    bool internal = false, protects = false, cubic = false, still = true, decisive = false;
+    int k = 1, repair = 1;
+    float min_age = 0, fsx = 1, fsy = 1;
+    int r_blk = 1, r_dwin = 1;
+    float delta = 0, dmin = 0;
+    fhk::StaticArgs sargs{};
+    int c8, c16, cc, cr, cq, cin_c1, cin_r1;
+    int C8P, C16P, CCP, CRP, CQP;
+
+    cudaStream_t st = nullptr;
+    std::vector<void*> allocs;
+    size_t bytes = 0;
+
+    std::map<std::string, ConvLayer> convs;
+    float *film_w1 = nullptr, *film_b1 = nullptr, *film_w2 = nullptr, *film_b2 = nullptr;
+    int film_hidden = 0;
+
+    std::vector<InSlot> ins;
+    std::vector<uint8_t*> outs;
+    // frame-stage scratch, pair and mid buffers
+    __half *e1 = nullptr, *e3 = nullptr;
+    uint8_t *changed = nullptr, *mask = nullptr;
+    uchar4* state = nullptr;
+    int16_t* age = nullptr;
+    __half *cv, *ch1, *ch2, *ch3r, *hcb, *ob, *fv, *wbuf, *fcv, *fr1, *fr2, *fr3, *wt36;
+    float *coef, *maps, *tmp, *tdev;
+    __half *hm, *fh1, *fh2, *dfilm, *ftvt, *up7, *rx, *rq1, *rq2, *rq3, *rt;
+    uint8_t *shadow_fa = nullptr, *shadow_fb = nullptr;
+    __half *shadow_aq = nullptr, *shadow_bq = nullptr;
+
+    bool have_pair = false;
+    PairSrc pair{};
+    std::map<std::pair<int, int>, cudaGraphExec_t> pair_graphs;
+    std::map<std::tuple<const void*, const void*, const void*, const void*, const void*>, cudaGraphExec_t> mid_graphs;
+    int pair_kernels = 0, mid_kernels = 0, frame_kernels = 0;
+    bool mid_ran = false;
+    uint64_t pair_static_gen = 0;  // the static state advances once per pair() call
+
+    void* dalloc(size_t n) {
+        void* p = nullptr;
+        CK(cudaMalloc(&p, std::max<size_t>(n, 256)));
+        CK(cudaMemsetAsync(p, 0, std::max<size_t>(n, 256), st));
+        allocs.push_back(p);
+        bytes += n;
+        return p;
+    }
+    template <class T>
+    T* alloc_n(size_t n) { return (T*)dalloc(n * sizeof(T)); }
+    __half* img(int hh, int ww, int cs) { return alloc_n<__half>((size_t)hh * ww * cs); }
+
+    ~FhSession() {
+        if (st) cudaStreamSynchronize(st);
+        for (auto& s : ins)
+            if (s.graph) cudaGraphExecDestroy(s.graph);
+        for (auto& kv : pair_graphs) cudaGraphExecDestroy(kv.second);
+        for (auto& kv : mid_graphs) cudaGraphExecDestroy(kv.second);
+        for (void* p : allocs) cudaFree(p);
+        if (eng) eng->tensor_bytes -= std::min(eng->tensor_bytes, bytes);
+        if (st) cudaStreamDestroy(st);
+    }
+
+    // ---- planning ----
+    ConvLayer make_conv(const std::string& name, int stride, bool act, const std::vector<SrcSpec>& srcs) {
+        ConvLayer L;
+        L.name = name;
+        L.stride = stride;
+        L.act = act;
+        const std::string wn = act ? name + ".0.weight" : name + ".weight";
+        const std::string bn = act ? name + ".0.bias" : name + ".bias";
+        auto sh = model->shape(wn);
+        if (sh.size() != 4 || sh[2] != 3 || sh[3] != 3) fail("%s: not a 3x3 conv weight", wn.c_str());
+        L.cout = sh[0];
+        L.cin = sh[1];
+        if (L.cout > 96) fail("%s: %d output channels (this engine's conv kernels take up to 96)", wn.c_str(), L.cout);
+        int slot = 0;
+        std::vector<int> map;
+        for (auto& s : srcs) {
+            FhConvSrc fs{};
+            fs.cs = s.cs;
+            fs.nc = s.nc;
+            fs.scale = s.scale;
+            fs.slot = slot;
+            L.src.push_back(fs);
+            for (int c = 0; c < up8(s.nc); c++) {
+                int m = c < s.nc ? s.map[c] : -1;
+                if (m >= L.cin) fail("%s: input channel %d out of range (%d)", name.c_str(), m, L.cin);
+                map.push_back(m);
+            }
+            slot += up8(s.nc);
+        }
+        L.cp = up16(slot);
+        map.resize(L.cp, -1);
+        auto wb = model->bits(wn);
+        std::vector<uint16_t> packed(fhk_conv_packed_elems(L.cout, L.cp));
+        if (fhk_conv_pack_weights(wb.data(), L.cin, L.cout, map.data(), L.cp, packed.data()) != 0) fail("%s: pack", name.c_str());
+        L.wpack = alloc_n<uint16_t>(packed.size());
+        CK(cudaMemcpy(L.wpack, packed.data(), packed.size() * 2, cudaMemcpyHostToDevice));
+        auto b = model->f32(bn);
+        if ((int)b.size() != L.cout) fail("%s: bias size", bn.c_str());
+        L.bias = alloc_n<float>(L.cout);
+        CK(cudaMemcpy(L.bias, b.data(), L.cout * 4, cudaMemcpyHostToDevice));
+        if (act) {
+            auto s = model->f32(name + ".1.weight");
+            if ((int)s.size() != L.cout) fail("%s: slope size", name.c_str());
+            L.slope = alloc_n<float>(L.cout);
+            CK(cudaMemcpy(L.slope, s.data(), L.cout * 4, cudaMemcpyHostToDevice));
+        }
+        return L;
+    }
+    static SrcSpec plain(int cs, int nc, int first) {
+        SrcSpec s{cs, nc, 1.0f, {}};
+        for (int c = 0; c < nc; c++) s.map.push_back(first + c);
+        return s;
+    }
+
+    void conv(const std::string& key, std::vector<const __half*> ptrs, int hh, int ww, __half* out, int out_cs,
+              const __half* res = nullptr, int res_cs = 0, int epi = 0) {
+        const ConvLayer& L = convs.at(key);
+        if (ptrs.size() != L.src.size()) fail("conv %s: %zu sources for %zu", key.c_str(), ptrs.size(), L.src.size());
+        FhConvParams p{};
+        for (size_t i = 0; i < ptrs.size(); i++) {
+            p.src[i] = L.src[i];
+            p.src[i].p = ptrs[i];
+            p.src[i].bs = 0;
+        }
+        p.nsrc = (int)ptrs.size();
+        p.h = hh;
+        p.w = ww;
+        p.ho = (hh - 1) / L.stride + 1;
+        p.wo = (ww - 1) / L.stride + 1;
+        p.cp = L.cp;
+        p.cout = L.cout;
+        p.wpack = L.wpack;
+        p.bias = L.bias;
+        p.slope = L.slope;
+        p.epi = epi;
+        p.out = out;
+        p.out_cs = out_cs;
+        p.res = res;
+        p.res_cs = res_cs;
+        p.n = 1;
+        const int tiles4 = ((p.ho + 7) / 8) * ((p.wo + 15) / 16);
+        const int warps = tiles4 >= 148 ? 4 : 2;
+        int e = fhk_conv3x3(&p, L.stride, warps, st);
+        if (e) fail("conv %s: %s", key.c_str(), cudaGetErrorString((cudaError_t)e));
+    }
+
+    void plan() {
+        // widths from the manifest (flyhighfg.json meta.cfg: c8, c16, cc, cr, cq)
+        c8 = model->shape("enc.e1.0.weight")[0];
+        c16 = model->shape("enc.e3.0.weight")[0];
+        cc = model->shape("coarse.c1.0.weight")[0];
+        cr = model->shape("fine.r1.0.weight")[0];
+        cq = model->shape("refine.q1.0.weight")[0];
+        cin_c1 = model->shape("coarse.c1.0.weight")[1];
+        cin_r1 = model->shape("fine.r1.0.weight")[1];
+        if (c8 > 40) fail("enc.e1: %d channels (the fine-warp buffer holds up to 40)", c8);
+        const int zeros_c1 = cin_c1 - (2 * c16 + 6 + 49);
+        if (zeros_c1 < 0) fail("coarse.c1: %d input channels do not fit the coarse concat", cin_c1);
+        if (cin_r1 != 2 * c8 + 6 + 4 + cr + 25) fail("fine.r1: %d input channels do not fit the fine concat", cin_r1);
+        C8P = up8(c8);
+        C16P = up8(c16);
+        CCP = up8(cc);
+        CRP = up8(cr);
+        CQP = up8(cq);
+        convs["e1"] = make_conv("enc.e1", 2, true, {plain(4, 3, 0)});
+        convs["e2"] = make_conv("enc.e2", 1, true, {plain(C8P, c8, 0)});
+        convs["e3"] = make_conv("enc.e3", 2, true, {plain(C8P, c8, 0)});
+        convs["e4"] = make_conv("enc.e4", 1, true, {plain(C16P, c16, 0)});
+        // coarse.c1 on concat(f16a, f16b, img16, side = 0, state = 0, cv): the zero channels are left out
+        convs["c1"] = make_conv("coarse.c1", 1, true,
+                                {plain(C16P, c16, 0), plain(C16P, c16, c16), plain(4, 3, 2 * c16), plain(4, 3, 2 * c16 + 3),
+                                 plain(56, 49, 2 * c16 + 6 + zeros_c1)});
+        convs["c2"] = make_conv("coarse.c2", 1, true, {plain(CCP, cc, 0)});
+        convs["c3"] = make_conv("coarse.c3", 1, true, {plain(CCP, cc, 0)});
+        convs["c4"] = make_conv("coarse.c4", 1, true, {plain(CCP, cc, 0)});
+        convs["head"] = make_conv("coarse.head", 1, false, {plain(CCP, cc, 0)});
+        // fine.r1 on concat(wa, wb, ia, ib, flow8 = flow / 8, h, fcv); h is zero on the first iteration
+        SrcSpec iaib{88, 7, 1.0f, {2 * c8, 2 * c8 + 1, 2 * c8 + 2, -1, 2 * c8 + 3, 2 * c8 + 4, 2 * c8 + 5}};
+        SrcSpec flow8{8, 4, 0.125f, {2 * c8 + 6, 2 * c8 + 7, 2 * c8 + 8, 2 * c8 + 9}};
+        const int hbase = 2 * c8 + 10, cvbase = hbase + cr;
+        convs["r1_0"] = make_conv("fine.r1", 1, true,
+                                  {plain(88, c8, 0), plain(88, c8, c8), iaib, flow8, plain(32, 25, cvbase)});
+        if (k > 1)
+            convs["r1"] = make_conv("fine.r1", 1, true,
+                                    {plain(88, c8, 0), plain(88, c8, c8), iaib, flow8, plain(CRP, cr, hbase), plain(32, 25, cvbase)});
+        convs["r2"] = make_conv("fine.r2", 1, true, {plain(CRP, cr, 0)});
+        convs["r3"] = make_conv("fine.r3", 1, true, {plain(CRP, cr, 0)});
+        convs["out"] = make_conv("fine.out", 1, false, {plain(CRP, cr, 0)});
+        convs["up"] = make_conv("up.w", 1, false, {plain(CRP, cr, 0)});
+        convs["fh1"] = make_conv("film.h1", 1, true, {plain(CRP, cr, 0)});
+        convs["fh2"] = make_conv("film.h2", 1, true, {plain(CRP, cr, 0)});
+        convs["fout"] = make_conv("film.out", 1, false, {plain(CRP, cr, 0)});
+        convs["q1"] = make_conv("refine.q1", 1, true, {plain(16, 14, 0)});
+        convs["q2"] = make_conv("refine.q2", 1, true, {plain(CQP, cq, 0)});
+        convs["q3"] = make_conv("refine.q3", 1, true, {plain(CQP, cq, 0)});
+        convs["q4"] = make_conv("refine.q4", 1, false, {plain(CQP, cq, 0)});
+        if (convs["head"].cout < 7 || convs["out"].cout != 7 || convs["fout"].cout != 5 || convs["up"].cout != 36 ||
+            convs["q4"].cout != 3 || convs["q1"].cin != 14)
+            fail("the manifest's head shapes do not match the FlyHighFG graph");
+        // FiLM MLP weights (f32, the values the host MLP reads: net/build.rs:333-334)
+        auto w1 = model->f32("film.film.0.weight"), b1 = model->f32("film.film.0.bias");
+        auto w2 = model->f32("film.film.2.weight"), b2 = model->f32("film.film.2.bias");
+        film_hidden = (int)b1.size();
+        if ((int)w1.size() != film_hidden || (int)b2.size() != 2 * cr || (int)w2.size() != 2 * cr * film_hidden)
+            fail("film.film: shapes do not match (hidden %d, 2 x %d outputs)", film_hidden, cr);
+        auto up = [&](const std::vector<float>& v) {
+            float* d = alloc_n<float>(v.size());
+            CK(cudaMemcpy(d, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+            return d;
+        };
+        film_w1 = up(w1);
+        film_b1 = up(b1);
+        film_w2 = up(w2);
+        film_b2 = up(b2);
+
+        // buffers
+        e1 = img(h8, w8, C8P);
+        e3 = img(h16, w16, C16P);
+        if (protects) {
+            changed = alloc_n<uint8_t>((size_t)hp * wp);
+            mask = alloc_n<uint8_t>((size_t)hp * wp);
+            state = alloc_n<uchar4>((size_t)hp * wp);
+            age = alloc_n<int16_t>((size_t)hp * wp);
+        }
+        cv = img(h16, w16, 56);
+        ch1 = img(h16, w16, CCP);
+        ch2 = img(h16, w16, CCP);
+        ch3r = img(h16, w16, CCP);
+        hcb = img(h16, w16, CCP);
+        ob = img(h16, w16, 16);
+        fv = img(h8, w8, 8);
+        wbuf = img(h8, w8, 88);
+        fcv = img(h8, w8, 32);
+        fr1 = img(h8, w8, CRP);
+        fr2 = img(h8, w8, CRP);
+        fr3 = img(h8, w8, CRP);
+        wt36 = img(h8, w8, 40);
+        coef = alloc_n<float>(16);
+        maps = alloc_n<float>((size_t)6 * hc * wc);
+        tmp = alloc_n<float>((size_t)5 * hc * wc);
+        tdev = alloc_n<float>(1);
+        hm = img(h8, w8, CRP);
+        fh1 = img(h8, w8, CRP);
+        fh2 = img(h8, w8, CRP);
+        dfilm = img(h8, w8, 8);
+        ftvt = img(h8, w8, 8);
+        up7 = img(qh, qw, 8);
+        rx = img(qh, qw, 16);
+        rq1 = img(qh, qw, CQP);
+        rq2 = img(qh, qw, CQP);
+        rq3 = img(qh, qw, CQP);
+        rt = img(qh, qw, 4);
+        CK(cudaStreamSynchronize(st));
+    }
+
+    // ---- stages ----
+    void run_frame(InSlot& s) {
+        CK(fhk::frame_to_input(s.frame, 0, w, h, hp, wp, internal, ihp, iwp, {s.A, 0}, 1, st));
+        CK(fhk::input_pyramid({s.A, 0}, NH, NW, {s.aq, 0}, {s.i8, 0}, {s.i16, 0}, 1, st));
+        conv("e1", {s.aq}, qh, qw, e1, C8P);
+        conv("e2", {e1}, h8, w8, s.f8, C8P, e1, C8P);
+        conv("e3", {s.f8}, h8, w8, e3, C16P);
+        conv("e4", {e3}, h16, w16, s.f16, C16P, e3, C16P);
+    }
+
+    void run_pair(const InSlot& A, const InSlot& B) {
+        if (protects) {
+            CK(fhk::static_changed(A.frame, B.frame, sargs, changed, st));
+            CK(fhk::static_age(A.frame, B.frame, changed, mask, sargs, state, age, st));
+        }
+        // coarse: img16 = (i16a, i16b), luma, sad r3 (graph ops 18-25), then c1..head (26-32)
+        CK(fhk::sad_volume(A.i16, 4, B.i16, 4, 0, h16, w16, 3, cv, 56, 0, 1, st));
+        conv("c1", {A.f16, B.f16, A.i16, B.i16, cv}, h16, w16, ch1, CCP);
+        conv("c2", {ch1}, h16, w16, ch2, CCP);
+        conv("c3", {ch2}, h16, w16, ch3r, CCP, ch1, CCP);
+        conv("c4", {ch3r}, h16, w16, hcb, CCP);
+        conv("head", {hcb}, h16, w16, ob, 16);
+        CK(fhk::upsample_flow_vis(ob, 16, 0, h16, w16, fv, 0, h8, w8, 1, st));
+        // fine iterations (graph op 42)
+        for (int it = 0; it < k; it++) {
+            fhk::WarpFineArgs wa{fv, 0, A.f8, B.f8, C8P, c8, 0, {A.i8, 0}, {B.i8, 0}, h8, w8, wbuf, 0};
+            CK(fhk::warp_fine(wa, 1, st));
+            CK(fhk::sad_volume(wbuf + 80, 88, wbuf + 84, 88, 0, h8, w8, 2, fcv, 32, 0, 1, st));
+            if (it == 0) conv("r1_0", {wbuf, wbuf + 40, wbuf + 80, fv, fcv}, h8, w8, fr1, CRP);
+            else conv("r1", {wbuf, wbuf + 40, wbuf + 80, fv, fr3, fcv}, h8, w8, fr1, CRP);
+            conv("r2", {fr1}, h8, w8, fr2, CRP);
+            conv("r3", {fr2}, h8, w8, fr3, CRP);
+            conv("out", {fr3}, h8, w8, fv, 8, fv, 8);
+        }
+        if (repair > 0) {
+            fhk::GmArgs g{fv, 0, h8, w8, A.A, B.A, 0, NH, NW, hc, wc, r_blk, r_dwin, delta, dmin, coef, maps, tmp};
+            CK(fhk::gmhs(g, 1, st));
+        }
+        // the convex-upsample weights depend on h only (graph op 62: conv up.w of h)
+        conv("up", {fr3}, h8, w8, wt36, 40);
+    }
+
+    void run_mid(const PairSrc& p, uint8_t* out) {
+        fhk::FilmArgs fa{tdev, film_w1, film_b1, film_w2, film_b2, film_hidden, cr, fr3, CRP, 0, hm, CRP, 0, h8, w8};
+        CK(fhk::film(fa, 1, st));
+        conv("fh1", {hm}, h8, w8, fh1, CRP);
+        conv("fh2", {fh1}, h8, w8, fh2, CRP);
+        conv("fout", {fh2}, h8, w8, dfilm, 8);
+        CK(fhk::mid_combine(tdev, fv, 0, dfilm, 0, ftvt, 0, h8, w8, 1, st));
+        CK(fhk::convex_up(wt36, 40, 0, ftvt, 0, h8, w8, up7, 0, 1, st));
+        CK(fhk::refine_input(up7, 0, {(__half*)p.aq, 0}, {(__half*)p.bq, 0}, qh, qw, rx, 0, 1, st));
+        conv("q1", {rx}, qh, qw, rq1, CQP);
+        conv("q2", {rq1}, qh, qw, rq2, CQP);
+        conv("q3", {rq2}, qh, qw, rq3, CQP);
+        conv("q4", {rq3}, qh, qw, rt, 4, nullptr, 0, 1);
+        fhk::RenderArgs ra{p.fa, p.fb, 0, w, h, hp, wp, up7, 0, rt, 0, qh, qw, fsx, fsy, cubic ? 1 : 0,
+                           (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, 0, min_age, out, 0};
+        CK(fhk::render(ra, 1, st));
+    }
+
+    template <class F>
+    cudaGraphExec_t capture(F&& body, int* nodes) {
+        cudaGraph_t g = nullptr;
+        CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
+        try {
+            body();
+        } catch (...) {
+            cudaStreamEndCapture(st, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+        }
+        CK(cudaStreamEndCapture(st, &g));
+        size_t n = 0;
+        CK(cudaGraphGetNodes(g, nullptr, &n));
+        if (nodes) *nodes = (int)n;
+        cudaGraphExec_t ex = nullptr;
+        cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        CK(e);
+        eng->graphs_built++;
+        return ex;
+    }
+
+    void ensure_features(int i) {
+        InSlot& s = ins[i];
+        if (s.feat_gen == s.gen) return;
+        if (!s.graph) s.graph = capture([&] { run_frame(s); }, &frame_kernels);
+        CK(cudaGraphLaunch(s.graph, st));
+        s.feat_gen = s.gen;
+    }
+
+    void check_in(uint32_t i) const {
+        if (i >= ins.size()) fail("bad input slot %u (the session has %zu)", i, ins.size());
+    }
+    void check_out(uint32_t i) const {
+        if (i >= outs.size()) fail("bad output slot %u (the session has %zu)", i, outs.size());
+    }
+
+    void do_pair(uint32_t a, uint32_t b) {
+        check_in(a);
+        check_in(b);
+        ensure_features(a);
+        ensure_features(b);
+        auto key = std::make_pair((int)a, (int)b);
+        auto it = pair_graphs.find(key);
+        if (it == pair_graphs.end())
+            it = pair_graphs.emplace(key, capture([&] { run_pair(ins[a], ins[b]); }, &pair_kernels)).first;
+        CK(cudaGraphLaunch(it->second, st));
+        pair = PairSrc{ins[a].frame, ins[b].frame, ins[a].aq, ins[b].aq, (int)a, (int)b};
+        have_pair = true;
+    }
+
+    cudaGraphExec_t mid_graph(uint32_t out) {
+        auto key = std::make_tuple((const void*)pair.fa, (const void*)pair.fb, (const void*)pair.aq, (const void*)pair.bq,
+                                   (const void*)outs[out]);
+        auto it = mid_graphs.find(key);
+        if (it == mid_graphs.end()) {
+            PairSrc p = pair;
+            uint8_t* o = outs[out];
+            it = mid_graphs.emplace(key, capture([&] { run_mid(p, o); }, &mid_kernels)).first;
+        }
+        return it->second;
+    }
+
+    void do_mid(float t, uint32_t out) {
+        check_out(out);
+        if (!have_pair) fail("pair two input slots first");
+        if (!std::isfinite(t)) fail("t is not finite");
+        cudaGraphExec_t g = mid_graph(out);
+        CK(fhk::set_scalar(tdev, t, st));
+        CK(cudaGraphLaunch(g, st));
+        mid_ran = true;
+    }
+
+    // a write into a slot the current pair reads: the pair keeps its frame (the reference's pair owns tex_in copies)
+    void protect_pair_slot(uint32_t slot) {
+        if (!have_pair) return;
+        const size_t fb = (size_t)w * h * 4, qb = (size_t)qh * qw * 4 * sizeof(__half);
+        if ((int)slot == pair.a && pair.fa == ins[slot].frame) {
+            if (!shadow_fa) {
+                shadow_fa = alloc_n<uint8_t>(fb);
+                shadow_aq = img(qh, qw, 4);
+            }
+            CK(cudaMemcpyAsync(shadow_fa, ins[slot].frame, fb, cudaMemcpyDeviceToDevice, st));
+            CK(cudaMemcpyAsync(shadow_aq, ins[slot].aq, qb, cudaMemcpyDeviceToDevice, st));
+            pair.fa = shadow_fa;
+            pair.aq = shadow_aq;
+        }
+        if ((int)slot == pair.b && pair.fb == ins[slot].frame) {
+            if (!shadow_fb) {
+                shadow_fb = alloc_n<uint8_t>(fb);
+                shadow_bq = img(qh, qw, 4);
+            }
+            CK(cudaMemcpyAsync(shadow_fb, ins[slot].frame, fb, cudaMemcpyDeviceToDevice, st));
+            CK(cudaMemcpyAsync(shadow_bq, ins[slot].aq, qb, cudaMemcpyDeviceToDevice, st));
+            pair.fb = shadow_fb;
+            pair.bq = shadow_bq;
+        }
+    }
+
+    int add_input() {
+        InSlot s;
+        s.frame = alloc_n<uint8_t>((size_t)w * h * 4);
+        s.A = img(NH, NW, 4);
+        s.aq = img(qh, qw, 4);
+        s.i8 = img(h8, w8, 4);
+        s.i16 = img(h16, w16, 4);
+        s.f8 = img(h8, w8, C8P);
+        s.f16 = img(h16, w16, C16P);
+        ins.push_back(s);
+        return (int)ins.size() - 1;
+    }
+    int add_output() {
+        outs.push_back(alloc_n<uint8_t>((size_t)w * h * 4));
+        return (int)outs.size() - 1;
+    }
+};
+
+namespace {
+
+// options.rs:348-356
+void default_internal(int w, int h, int& iw, int& ih) {
+    if (std::max(w, h) <= 960) {
+        iw = w;
+        ih = h;
+        return;
+    }
+    double s = std::min(480.0 / (double)h, 1.0);
+    int rw = std::max((int)std::lround(w * s / 8.0) * 8, 64);
+    int rh = std::max((int)std::lround(h * s / 8.0) * 8, 64);
+    iw = std::min(rw, w);
+    ih = std::min(rh, h);
+}
+
+// SessionOptions::validate (session.rs:170-197) on the C options (core.rs:117-149), then every size and parameter
+// the plan derives (net/build.rs:548-581, gmhs.rs:160-170, options.rs:308-392)
+void derive(const FhModel* m, const FhSessionOptions& o, FhSession* s) {
+    if (o.width < 64 || o.height < 64) fail("width: frame size %ux%u is below 64x64", o.width, o.height);
+    if (o.width > 16384 || o.height > 16384) fail("width: frame size %ux%u is above 16384x16384", o.width, o.height);
+    if (o.k < 1 || o.k > 3) fail("k: %u is not 1..=3", o.k);
+    if (o.repair > 2) fail("repair: %u is not 0..=2", o.repair);
+    if (o.render > 2) fail("unknown render %u (0 model, 1 bilinear, 2 bicubic)", o.render);
+    if (o.keep_static && o.static_frames > 255) fail("static_protection: frames %u is not 1..=255", o.static_frames);
+    if (o.keep_static && o.static_tolerance > 255) fail("static_protection: tolerance %u is above 255", o.static_tolerance);
+    if (o.linear_t && !o.fast_render) fail("linear_t: needs fast_render");
+    if (o.fast_render) fail("fast_render: the texture-sampled render is not part of this build");
+    if (m->fingerprint != kFlyHighFgGraph)
+        fail("graph.json: not the FlyHighFG v1 graph this engine plans (fingerprint %016llx)", (unsigned long long)m->fingerprint);
+    s->model = m;
+    s->o = o;
+    s->w = (int)o.width;
+    s->h = (int)o.height;
+    if (o.internal_w == 0 && o.internal_h == 0) default_internal(s->w, s->h, s->iw, s->ih);
+    else {
+        s->iw = std::min((int)o.internal_w, s->w);
+        s->ih = std::min((int)o.internal_h, s->h);
+    }
+    if (s->iw < 32 || s->ih < 32) fail("internal: internal size %dx%d is below 32x32", s->iw, s->ih);
+    s->hp = (s->h + 31) / 32 * 32;
+    s->wp = (s->w + 31) / 32 * 32;
+    s->ihp = (s->ih + 31) / 32 * 32;
+    s->iwp = (s->iw + 31) / 32 * 32;
+    s->internal = !(s->iwp == s->wp && s->ihp == s->hp);
+    s->NH = s->internal ? s->ihp : s->hp;
+    s->NW = s->internal ? s->iwp : s->wp;
+    s->qh = s->NH / 4;
+    s->qw = s->NW / 4;
+    s->h8 = (s->qh - 1) / 2 + 1;
+    s->w8 = (s->qw - 1) / 2 + 1;
+    s->h16 = (s->h8 - 1) / 2 + 1;
+    s->w16 = (s->w8 - 1) / 2 + 1;
+    s->k = (int)o.k;
+    s->repair = o.keep_maps ? std::max(1, (int)o.repair) : (int)o.repair;
+    s->cubic = o.render == 0 ? m->cubic : o.render == 2;
+    s->still = true;     // options.rs:296-298 (FH_STILL default on)
+    s->decisive = false; // options.rs:277-280 (FH_BLEND default off)
+    const bool keep_static = o.keep_static != 0;
+    s->protects = keep_static || o.protection_mask;
+    const int frames = keep_static ? std::clamp((int)(o.static_frames ? o.static_frames : 8), 1, 255) : 2;
+    s->min_age = (float)frames;
+    s->sargs = fhk::StaticArgs{s->w, s->h, s->wp, s->hp,
+                               keep_static ? ((float)std::min((int)o.static_tolerance, 255) + 0.5f) / 255.0f : 0.0f,
+                               (float)frames, (int)o.protection_mask};
+    s->fsx = (float)s->wp / (float)s->NW;
+    s->fsy = (float)s->hp / (float)s->NH;
+    // gmhs.rs:160-170 (DS = 2)
+    s->hc = (s->NH + 1) / 2;
+    s->wc = (s->NW + 1) / 2;
+    const float sc = (float)s->NW / ((float)s->wp / 2.0f);
+    s->r_blk = std::max(1, (int)std::round(20.0f * sc / 2.0f));
+    s->r_dwin = std::max(1, (int)std::round(32.0f * sc / 2.0f));
+    s->dmin = s->repair >= 2 ? 0.0f : 8.0f * sc;
+    s->delta = 1.5f * sc;
+}
+
+FhSession* session_new(FhEngine* e, const FhModel* m, const FhSessionOptions& o) {
+    auto s = std::make_unique<FhSession>();
+    derive(m, o, s.get());
+    s->eng = e;
+    CK(cudaSetDevice(e->device));
+    CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+    s->plan();
+    e->tensor_bytes += s->bytes;
+    return s.release();
+}
+
+template <class R, class F>
+R guard(R fallback, F f) {
+    try {
+        return f();
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return fallback;
+    } catch (...) {
+        g_err = "internal error";
+        return fallback;
+    }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------- C exports ----
+
+extern "C" {
+
+const char* fh_last_error(void) { return g_err.c_str(); }
+
+FhEngineOptions fh_engine_options_default(void) {
+    FhEngineOptions o{};
+    o.backend = 0;
+    o.tensor_cores = 1;
+    o.autotune = 1;
+    o.adapter = nullptr;
+    o.precision = 0;
+    o.tune_cache = nullptr;
+    o.compact_memory = 1;
+    o.dxc_path = nullptr;
+    return o;
+}
+
+FhEngine* fh_engine_create(const FhEngineOptions* opts) {
+    return guard((FhEngine*)nullptr, [&]() -> FhEngine* {
+        FhEngineOptions o = opts ? *opts : fh_engine_options_default();
+        if (o.backend > 4) fail("unknown backend %u (0 auto, 1 vulkan, 2 dx12, 3 metal, 4 gl)", o.backend);
+        if (o.precision == 2) fail("precision: the f32 path is not part of this build (f16 storage, f32 math)");
+        int dev = 0;
+        if (o.adapter && o.adapter[0] == '#') dev = atoi(o.adapter + 1);
+        int count = 0;
+        if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) fail("no CUDA device (adapter): none found");
+        if (dev < 0 || dev >= count) fail("adapter %s: %d CUDA devices", o.adapter, count);
+        cudaDeviceProp p;
+        CK(cudaGetDeviceProperties(&p, dev));
+        if (p.major < 10) fail("device %d (%s) is sm_%d%d; this build runs on sm_100a (B200)", dev, p.name, p.major, p.minor);
+        CK(cudaSetDevice(dev));
+        auto* e = new FhEngine();
+        e->device = dev;
+        e->name = p.name;
+        e->sm_major = p.major;
+        e->sm_minor = p.minor;
+        e->sms = p.multiProcessorCount;
+        return e;
+    });
+}
+
+void fh_engine_destroy(FhEngine* e) { delete e; }
+
+int fh_engine_info(const FhEngine* e, char* buf, size_t cap) {
+    return guard(-1, [&] {
+        if (!e) fail("null argument");
+        char b[512];
+        snprintf(b, sizeof b,
+                 "{\"name\":%s,\"class\":\"tc-f16\",\"tensor_cores\":true,\"timestamps\":true,\"bgra_storage\":false,"
+                 "\"shader_compiler\":null,\"sm\":\"%d.%d\",\"sms\":%d,\"device\":%d}",
+                 fhjson::quote(e->name).c_str(), e->sm_major, e->sm_minor, e->sms, e->device);
+        return write_json(b, buf, cap);
+    });
+}
+
+int fh_engine_report_json(const FhEngine* e, char* buf, size_t cap) {
+    return guard(-1, [&] {
+        if (!e) fail("null argument");
+        char b[512];
+        snprintf(b, sizeof b, "{\"device\":%s,\"kernels_compiled\":%d,\"autotune_entries\":0,\"tensor_bytes\":%zu}",
+                 fhjson::quote(e->name).c_str(), e->graphs_built, e->tensor_bytes);
+        return write_json(b, buf, cap);
+    });
+}
+
+FhModel* fh_model_load(const char* dir) {
+    return guard((FhModel*)nullptr, [&] {
+        if (!dir) fail("dir is null");
+        std::string d(dir);
+        std::string g, m, w;
+        try {
+            g = slurp(d + "/graph.json");
+        } catch (Error&) {
+            fail("read graph.json: cannot open %s/graph.json", dir);
+        }
+        try {
+            m = slurp(d + "/flyhighfg.json");
+        } catch (Error&) {
+            fail("read flyhighfg.json: cannot open %s/flyhighfg.json", dir);
+        }
+        try {
+            w = slurp(d + "/flyhighfg.bin");
+        } catch (Error&) {
+            fail("read .bin: cannot open %s/flyhighfg.bin", dir);
+        }
+        return model_from((const uint8_t*)g.data(), g.size(), (const uint8_t*)m.data(), m.size(),
+                          (const uint8_t*)w.data(), w.size());
+    });
+}
+
+FhModel* fh_model_from_bytes(const uint8_t* g, size_t gl, const uint8_t* m, size_t ml, const uint8_t* w, size_t wl) {
+    return guard((FhModel*)nullptr, [&] {
+        if (!g || !m || !w) fail("null argument");
+        return model_from(g, gl, m, ml, w, wl);
+    });
+}
+
+void fh_model_destroy(FhModel* m) { delete m; }
+
+int fh_model_info(const FhModel* m, char* buf, size_t cap) {
+    return guard(-1, [&] {
+        if (!m) fail("null argument");
+        char b[512];
+        snprintf(b, sizeof b,
+                 "{\"name\":%s,\"train_step\":%lld,\"graph_ops\":%zu,\"tensors\":%zu,\"render_sampling\":\"%s\","
+                 "\"format_version\":%d}",
+                 fhjson::quote(m->name).c_str(), m->train_step, m->graph_ops, m->tensors, m->cubic ? "bicubic" : "bilinear",
+                 m->format_version);
+        return write_json(b, buf, cap);
+    });
+}
+
+FhSessionOptions fh_session_options_default(uint32_t width, uint32_t height) {
+    FhSessionOptions o{};
+    o.width = width;
+    o.height = height;
+    o.k = 1;
+    o.repair = 1;
+    o.render = 0;
+    o.keep_static = 1;
+    o.static_frames = 8;
+    o.static_tolerance = 4;
+    return o;
+}
+
+FhSession* fh_session_create(const FhEngine* e, const FhModel* m, const FhSessionOptions* o) {
+    return guard((FhSession*)nullptr, [&] {
+        if (!e || !m || !o) fail("null argument");
+        return session_new(const_cast<FhEngine*>(e), m, *o);
+    });
+}
+
+void fh_session_destroy(FhSession* s) { delete s; }
+
+int fh_session_add_input(FhSession* s) {
+    return guard(-1, [&] {
+        if (!s) fail("null argument");
+        return s->add_input();
+    });
+}
+
+int fh_session_add_output(FhSession* s) {
+    return guard(-1, [&] {
+        if (!s) fail("null argument");
+        return s->add_output();
+    });
+}
+
+int fh_session_write_rgba(const FhSession* cs, uint32_t slot, const uint8_t* rgba, size_t len) {
+    return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
+        if (!s || !rgba) fail("null argument");
+        s->check_in(slot);
+        const size_t n = (size_t)s->w * s->h * 4;
+        if (len != n) fail("frame is %zu bytes, %dx%dx4 = %zu expected", len, s->w, s->h, n);
+        s->protect_pair_slot(slot);
+        CK(cudaMemcpyAsync(s->ins[slot].frame, rgba, n, cudaMemcpyHostToDevice, s->st));
+        s->ins[slot].gen++;
+        return 0;
+    });
+}
+
+int fh_session_write_mask(const FhSession* cs, const uint8_t* mask, size_t len) {
+    return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
+        if (!s || !mask) fail("null argument");
+        if (!s->o.protection_mask) fail("the session was built without protection_mask");
+        if (len != (size_t)s->w * s->h) fail("mask is %zu bytes, %dx%d = %zu expected", len, s->w, s->h, (size_t)s->w * s->h);
+        // net/session_ext.rs:156-178: replicate-padded to the padded plane, nonzero protects
+        std::vector<uint8_t> plane((size_t)s->wp * s->hp);
+        for (int y = 0; y < s->hp; y++)
+            for (int x = 0; x < s->wp; x++)
+                plane[(size_t)y * s->wp + x] = mask[(size_t)std::min(y, s->h - 1) * s->w + std::min(x, s->w - 1)] ? 1 : 0;
+        CK(cudaMemcpyAsync(s->mask, plane.data(), plane.size(), cudaMemcpyHostToDevice, s->st));
+        CK(cudaStreamSynchronize(s->st));
+        return 0;
+    });
+}
+
+int fh_session_read_rgba(const FhSession* cs, uint32_t slot, uint8_t* buf, size_t cap) {
+    return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
+        if (!s || !buf) fail("null argument");
+        s->check_out(slot);
+        const size_t n = (size_t)s->w * s->h * 4;
+        if (n > cap) fail("output buffer too small (%zu needed)", n);
+        CK(cudaMemcpyAsync(buf, s->outs[slot], n, cudaMemcpyDeviceToHost, s->st));
+        CK(cudaStreamSynchronize(s->st));
+        return (int)n;
+    });
+}
+
+int fh_session_pair(const FhSession* cs, uint32_t a, uint32_t b) {
+    return guard(-1, [&] {
+        if (!cs) fail("null argument");
+        const_cast<FhSession*>(cs)->do_pair(a, b);
+        return 0;
+    });
+}
+
+int fh_session_mid(const FhSession* cs, float t, uint32_t out) {
+    return guard(-1, [&] {
+        if (!cs) fail("null argument");
+        const_cast<FhSession*>(cs)->do_mid(t, out);
+        return 0;
+    });
+}
+
+int fh_session_generate(const FhSession* cs, uint32_t a, uint32_t b, float t, uint32_t out) {
+    return guard(-1, [&] {
+        if (!cs) fail("null argument");
+        FhSession* s = const_cast<FhSession*>(cs);
+        s->do_pair(a, b);
+        s->do_mid(t, out);
+        return 0;
+    });
+}
+
+// session.rs:539-551: the min over runs of the device time of the stage (here: CUDA events around the graph)
+int fh_session_pair_timed(const FhSession* cs, uint32_t a, uint32_t b, double* ms) {
+    return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
+        if (!s || !ms) fail("null argument");
+        s->check_in(a);
+        s->check_in(b);
+        cudaEvent_t e0, e1;
+        CK(cudaEventCreate(&e0));
+        CK(cudaEventCreate(&e1));
+        float best = 1e30f;
+        for (int r = 0; r < 3; r++) {
+            // the reference's pair converts and encodes both frames every time (tex_in x2 + the plan): time the same
+            // work, the two frame stages included, without the credit of the per-slot feature cache
+            s->ins[a].feat_gen = s->ins[b].feat_gen = 0;
+            if (!s->ins[a].graph) s->ensure_features(a);
+            if (!s->ins[b].graph) s->ensure_features(b);
+            s->ins[a].feat_gen = s->ins[b].feat_gen = 0;
+            CK(cudaEventRecord(e0, s->st));
+            s->do_pair(a, b);
+            CK(cudaEventRecord(e1, s->st));
+            CK(cudaEventSynchronize(e1));
+            float t = 0;
+            CK(cudaEventElapsedTime(&t, e0, e1));
+            best = std::min(best, t);
+        }
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        *ms = best;
+        return 1;
+    });
+}
+
+int fh_session_mid_timed(const FhSession* cs, float t, uint32_t out, double* ms) {
+    return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
+        if (!s || !ms) fail("null argument");
+        s->check_out(out);
+        if (!s->have_pair) fail("pair two input slots first");
+        s->do_mid(t, out);
+        cudaEvent_t e0, e1;
+        CK(cudaEventCreate(&e0));
+        CK(cudaEventCreate(&e1));
+        float best = 1e30f;
+        for (int r = 0; r < 5; r++) {
+            CK(cudaEventRecord(e0, s->st));
+            s->do_mid(t, out);
+            CK(cudaEventRecord(e1, s->st));
+            CK(cudaEventSynchronize(e1));
+            float v = 0;
+            CK(cudaEventElapsedTime(&v, e0, e1));
+            best = std::min(best, v);
+        }
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        *ms = best;
+        return 1;
+    });
+}
+
+// session.rs:579-588
+int fh_session_warm_up(FhSession* s) {
+    return guard(-1, [&] {
+        if (!s) fail("null argument");
+        while (s->ins.size() < 2) s->add_input();
+        if (s->outs.empty()) s->add_output();
+        s->do_pair(0, 1);
+        s->do_mid(0.5f, 0);
+        CK(cudaStreamSynchronize(s->st));
+        return 0;
+    });
+}
+
+int fh_session_import_d3d11(FhSession*, const FhEngine*, intptr_t, uint32_t, uint32_t) {
+    g_err = "D3D11 interop: not available on this platform (CUDA device, no graphics API)";
+    return -1;
+}
+
+int fh_session_report_json(const FhSession* s, char* buf, size_t cap) {
+    return guard(-1, [&] {
+        if (!s) fail("null argument");
+        char sp[96];
+        if (s->o.keep_static)
+            snprintf(sp, sizeof sp, "{\"frames\":%d,\"tolerance\":%u}", (int)s->min_age, s->o.static_tolerance);
+        else
+            snprintf(sp, sizeof sp, "null");
+        char b[1024];
+        snprintf(b, sizeof b,
+                 "{\"width\":%d,\"height\":%d,\"internal_width\":%d,\"internal_height\":%d,\"k\":%d,\"repair\":%d,"
+                 "\"render\":\"%s\",\"fast_render\":false,\"linear_t\":false,\"static_protection\":%s,"
+                 "\"protection_mask\":%s,\"inputs\":%zu,\"outputs\":%zu,\"pair_steps\":%d,\"mid_steps\":%d,"
+                 "\"frame_steps\":%d,\"tensor_bytes\":%zu}",
+                 s->w, s->h, s->iw, s->ih, s->k, s->repair, s->cubic ? "bicubic" : "bilinear", sp,
+                 s->o.protection_mask ? "true" : "false", s->ins.size(), s->outs.size(), s->pair_kernels, s->mid_kernels,
+                 s->frame_kernels, s->bytes);
+        return write_json(b, buf, cap);
+    });
+}
+
+// ---- flyhigh_b200.h ----
+
+int fh_session_cuda_stream(const FhSession* s, void** stream) {
+    return guard(-1, [&] {
+        if (!s || !stream) fail("null argument");
+        *stream = (void*)s->st;
+        return 0;
+    });
+}
+
+int fh_session_slot_device_ptr(const FhSession* s, uint32_t slot, int output, void** ptr) {
+    return guard(-1, [&] {
+        if (!s || !ptr) fail("null argument");
+        if (output) {
+            s->check_out(slot);
+            *ptr = s->outs[slot];
+        } else {
+            s->check_in(slot);
+            *ptr = s->ins[slot].frame;
+        }
+        return 0;
+    });
+}
+
+int fh_session_write_rgba_device(const FhSession* cs, uint32_t slot, const void* dev, size_t len) {
+    return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
+        if (!s || !dev) fail("null argument");
+        s->check_in(slot);
+        const size_t n = (size_t)s->w * s->h * 4;
+        if (len != n) fail("frame is %zu bytes, %dx%dx4 = %zu expected", len, s->w, s->h, n);
+        s->protect_pair_slot(slot);
+        CK(cudaMemcpyAsync(s->ins[slot].frame, dev, n, cudaMemcpyDeviceToDevice, s->st));
+        s->ins[slot].gen++;
+        return 0;
+    });
+}
+
+int fh_session_launch_counts(const FhSession* s, int* pk, int* mk, int* fk) {
+    return guard(-1, [&] {
+        if (!s) fail("null argument");
+        if (pk) *pk = s->pair_kernels;
+        if (mk) *mk = s->mid_kernels;
+        if (fk) *fk = s->frame_kernels;
+        return 0;
+    });
+}
+
+long fh_session_debug_tensor(const FhSession* cs, const char* name, float* out, size_t cap, int* dims) {
+    return guard(-1L, [&]() -> long {
+        FhSession* s = const_cast<FhSession*>(cs);
+        if (!s || !name || !dims) fail("null argument");
+        if (!s->have_pair) fail("no pair has run");
+        std::string n(name);
+        const InSlot& A = s->ins[s->pair.a];
+        const InSlot& B = s->ins[s->pair.b];
+        // (pointer, pixel pitch, channel offset, channels, height, width, kind 0 = f16 / 1 = int16 / 2 = rgba8 planes)
+        const void* p = nullptr;
+        int cs_ = 0, c0 = 0, c = 0, hh = 0, ww = 0, kind = 0;
+        auto set = [&](const void* pp, int pcs, int pc0, int pc, int ph, int pw) {
+            p = pp;
+            cs_ = pcs;
+            c0 = pc0;
+            c = pc;
+            hh = ph;
+            ww = pw;
+        };
+        if (n == "A") set(A.A, 4, 0, 3, s->NH, s->NW);
+        else if (n == "B") set(B.A, 4, 0, 3, s->NH, s->NW);
+        else if (n == "aq") set(A.aq, 4, 0, 3, s->qh, s->qw);
+        else if (n == "bq") set(B.aq, 4, 0, 3, s->qh, s->qw);
+        else if (n == "i8a") set(A.i8, 4, 0, 3, s->h8, s->w8);
+        else if (n == "i8b") set(B.i8, 4, 0, 3, s->h8, s->w8);
+        else if (n == "i16a") set(A.i16, 4, 0, 3, s->h16, s->w16);
+        else if (n == "i16b") set(B.i16, 4, 0, 3, s->h16, s->w16);
+        else if (n == "f8a") set(A.f8, s->C8P, 0, s->c8, s->h8, s->w8);
+        else if (n == "f8b") set(B.f8, s->C8P, 0, s->c8, s->h8, s->w8);
+        else if (n == "f16a") set(A.f16, s->C16P, 0, s->c16, s->h16, s->w16);
+        else if (n == "f16b") set(B.f16, s->C16P, 0, s->c16, s->h16, s->w16);
+        else if (n == "cv") set(s->cv, 56, 0, 49, s->h16, s->w16);
+        else if (n == "ch1") set(s->ch1, s->CCP, 0, s->cc, s->h16, s->w16);
+        else if (n == "ch2") set(s->ch2, s->CCP, 0, s->cc, s->h16, s->w16);
+        else if (n == "ch3r") set(s->ch3r, s->CCP, 0, s->cc, s->h16, s->w16);
+        else if (n == "hc") set(s->hcb, s->CCP, 0, s->cc, s->h16, s->w16);
+        else if (n == "o") set(s->ob, 16, 0, s->convs.at("head").cout, s->h16, s->w16);
+        else if (n == "flow") set(s->fv, 8, 0, 4, s->h8, s->w8);
+        else if (n == "vis") set(s->fv, 8, 4, 3, s->h8, s->w8);
+        else if (n == "wa") set(s->wbuf, 88, 0, s->c8, s->h8, s->w8);
+        else if (n == "wb") set(s->wbuf, 88, 40, s->c8, s->h8, s->w8);
+        else if (n == "ia") set(s->wbuf, 88, 80, 3, s->h8, s->w8);
+        else if (n == "ib") set(s->wbuf, 88, 84, 3, s->h8, s->w8);
+        else if (n == "fcv") set(s->fcv, 32, 0, 25, s->h8, s->w8);
+        else if (n == "fr1") set(s->fr1, s->CRP, 0, s->cr, s->h8, s->w8);
+        else if (n == "fr2") set(s->fr2, s->CRP, 0, s->cr, s->h8, s->w8);
+        else if (n == "fr3" || n == "h") set(s->fr3, s->CRP, 0, s->cr, s->h8, s->w8);
+        else if (n == "hm") set(s->hm, s->CRP, 0, s->cr, s->h8, s->w8);
+        else if (n == "fh1") set(s->fh1, s->CRP, 0, s->cr, s->h8, s->w8);
+        else if (n == "fh2") set(s->fh2, s->CRP, 0, s->cr, s->h8, s->w8);
+        else if (n == "dfilm") set(s->dfilm, 8, 0, 5, s->h8, s->w8);
+        else if (n == "ft_vt") set(s->ftvt, 8, 0, 7, s->h8, s->w8);
+        else if (n == "up7") set(s->up7, 8, 0, 7, s->qh, s->qw);
+        else if (n == "rx") set(s->rx, 16, 0, 14, s->qh, s->qw);
+        else if (n == "rq1") set(s->rq1, s->CQP, 0, s->cq, s->qh, s->qw);
+        else if (n == "rq2") set(s->rq2, s->CQP, 0, s->cq, s->qh, s->qw);
+        else if (n == "rq3") set(s->rq3, s->CQP, 0, s->cq, s->qh, s->qw);
+        else if (n == "R_t") set(s->rt, 4, 0, 3, s->qh, s->qw);
+        else if (n == "age" && s->protects) {
+            set(s->age, 1, 0, 1, s->hp, s->wp);
+            kind = 1;
+        } else fail("unknown tensor %s", name);
+        dims[0] = c;
+        dims[1] = hh;
+        dims[2] = ww;
+        const long total = (long)c * hh * ww;
+        if (!out) return total;
+        if (cap < (size_t)total) return -2L;
+        CK(cudaStreamSynchronize(s->st));
+        const size_t esz = kind == 1 ? 2 : 2;
+        std::vector<uint16_t> raw((size_t)hh * ww * cs_);
+        CK(cudaMemcpy(raw.data(), p, raw.size() * esz, cudaMemcpyDeviceToHost));
+        for (int ch = 0; ch < c; ch++)
+            for (long i = 0; i < (long)hh * ww; i++) {
+                const uint16_t v = raw[(size_t)i * cs_ + c0 + ch];
+                float f;
+                if (kind == 1) f = (float)(int16_t)v;
+                else {
+                    __half_raw r;
+                    r.x = v;
+                    f = __half2float(__half(r));
+                }
+                out[(size_t)ch * hh * ww + i] = f;
+            }
+        return total;
+    });
+}
+
+int fh_session_plan_params(const FhModel* m, const FhSessionOptions* o, int* iv, float* fv) {
+    return guard(-1, [&] {
+        if (!m || !o || !iv || !fv) fail("null argument");
+        FhSession s;
+        derive(m, *o, &s);
+        s.model = nullptr;
+        const int ints[] = {s.hp, s.wp, s.ihp, s.iwp, s.internal ? 1 : 0, s.NH, s.NW, s.qh, s.qw, s.h8, s.w8, s.h16, s.w16,
+                            s.hc, s.wc, s.r_blk, s.r_dwin, s.k, s.repair, s.cubic ? 1 : 0, s.protects ? 1 : 0,
+                            (s.decisive ? 1 : 0) | (s.still ? 2 : 0)};
+        const float fls[] = {s.fsx, s.fsy, s.dmin, s.delta, s.min_age, s.sargs.thr};
+        memcpy(iv, ints, sizeof ints);
+        memcpy(fv, fls, sizeof fls);
+        return 0;
+    });
+}
+
+long fh_model_fingerprint(const FhModel* m) { return m ? (long)(m->fingerprint & 0x7fffffffffffffffull) : -1; }
+
+}  // extern "C"

@@ -1,0 +1,943 @@
+// The memory-bound stages of the FlyHighFG Core on NHWC f16 (everything but the convs). Compiled with --fmad=false:
+// every f32 product and sum rounds as the shaders write it, so the integer-like decisions downstream (static ages,
+// GMHS selection, the still test) see the same operands as the reference's arithmetic.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "fh_device.cuh"
+#include "stages.h"
+
+namespace fhk {
+namespace {
+
+
+inline dim3 grid2(int w, int h, int n, int bx = 16, int by = 16) { return dim3((w + bx - 1) / bx, (h + by - 1) / by, n); }
+
+// luma of BGR values (luma.wgsl:8-11): 0.299 R + 0.587 G + 0.114 B, left to right
+FH_DEV float lum3(float b, float g, float r) { return 0.299f * r + 0.587f * g + 0.114f * b; }
+
+FH_DEV void ld4(const __half* p, float& b, float& g, float& r) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __half2 x = *reinterpret_cast<const __half2*>(&u.x);
+    const __half2 y = *reinterpret_cast<const __half2*>(&u.y);
+    b = __low2float(x);
+    g = __high2float(x);
+    r = __low2float(y);
+}
+FH_DEV void st4(__half* p, float b, float g, float r) {
+    __half2 x = __halves2half2(f2h(b), f2h(g));
+    __half2 y = __halves2half2(f2h(r), f2h(0.0f));
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&x);
+    u.y = *reinterpret_cast<uint32_t*>(&y);
+    *reinterpret_cast<uint2*>(p) = u;
+}
+
+// ------------------------------------------------------------------------------------------- frame -> network ----
+
+// tex_in.wgsl:10-19 + interp.wgsl:29-43 (aa): the padded plane is never stored; taps read the rgba8 frame at the
+// clamped position (replicate padding)
+__global__ void k_frame_to_input(const uint8_t* __restrict__ frames, long long frame_bs, int w, int h, int hp, int wp,
+                                 int internal, int oh, int ow, __half* out, long long out_bs) {
+    __shared__ float lut[256];
+    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
+    __syncthreads();
+    const int ox = blockIdx.x * blockDim.x + threadIdx.x, oy = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
+    if (ox >= ow || oy >= oh) return;
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(frames + (long long)n * frame_bs);
+    __half* o = out + (long long)n * out_bs + ((long long)oy * ow + ox) * 4;
+    if (!internal) {
+        const uint32_t v = __ldg(f + (long long)min(oy, h - 1) * w + min(ox, w - 1));
+        st4(o, lut[(v >> 16) & 255], lut[(v >> 8) & 255], lut[v & 255]);
+        return;
+    }
+    const float sh = (float)hp / (float)oh, sw = (float)wp / (float)ow;
+    const float fsh = fmaxf(sh, 1.0f), fsw = fmaxf(sw, 1.0f);
+    const float cy = ((float)oy + 0.5f) * sh, cx = ((float)ox + 0.5f) * sw;
+    const int ymin = max(0, (int)floorf(cy - fsh + 0.5f)), ymax = min(hp, (int)floorf(cy + fsh + 0.5f));
+    const int xmin = max(0, (int)floorf(cx - fsw + 0.5f)), xmax = min(wp, (int)floorf(cx + fsw + 0.5f));
+    float ab = 0.0f, ag = 0.0f, ar = 0.0f, norm = 0.0f;
+    for (int y = ymin; y < ymax; y++) {
+        const float wy = fmaxf(0.0f, 1.0f - fabsf(((float)y + 0.5f - cy) / fsh));
+        const uint32_t* row = f + (long long)min(y, h - 1) * w;
+        for (int x = xmin; x < xmax; x++) {
+            const float wx = fmaxf(0.0f, 1.0f - fabsf(((float)x + 0.5f - cx) / fsw));
+            const float wgt = wx * wy;
+            const uint32_t v = __ldg(row + min(x, w - 1));
+            ab = ab + lut[(v >> 16) & 255] * wgt;
+            ag = ag + lut[(v >> 8) & 255] * wgt;
+            ar = ar + lut[v & 255] * wgt;
+            norm = norm + wgt;
+        }
+    }
+    st4(o, ab / norm, ag / norm, ar / norm);
+}
+
+// interp.wgsl aa (x0.25) into a 16 x 16 tile of aq in shared memory, then avgpool.wgsl twice
+__global__ void k_input_pyramid(const __half* __restrict__ A, long long a_bs, int ih, int iw, __half* aq, long long aq_bs,
+                                int qh, int qw, __half* i8, long long i8_bs, __half* i16, long long i16_bs) {
+    __shared__ float tq[16][16][3];
+    __shared__ float t8[8][8][3];
+    const int lx = threadIdx.x & 15, ly = threadIdx.x >> 4, n = blockIdx.z;
+    const int qx = blockIdx.x * 16 + lx, qy = blockIdx.y * 16 + ly;
+    const __half* a = A + (long long)n * a_bs;
+    if (qx < qw && qy < qh) {
+        const float sh = (float)ih / (float)qh, sw = (float)iw / (float)qw;
+        const float fsh = fmaxf(sh, 1.0f), fsw = fmaxf(sw, 1.0f);
+        const float cy = ((float)qy + 0.5f) * sh, cx = ((float)qx + 0.5f) * sw;
+        const int ymin = max(0, (int)floorf(cy - fsh + 0.5f)), ymax = min(ih, (int)floorf(cy + fsh + 0.5f));
+        const int xmin = max(0, (int)floorf(cx - fsw + 0.5f)), xmax = min(iw, (int)floorf(cx + fsw + 0.5f));
+        float ab = 0.0f, ag = 0.0f, ar = 0.0f, norm = 0.0f;
+        for (int y = ymin; y < ymax; y++) {
+            const float wy = fmaxf(0.0f, 1.0f - fabsf(((float)y + 0.5f - cy) / fsh));
+            for (int x = xmin; x < xmax; x++) {
+                const float wx = fmaxf(0.0f, 1.0f - fabsf(((float)x + 0.5f - cx) / fsw));
+                const float wgt = wx * wy;
+                float b, g, r;
+                ld4(a + ((long long)y * iw + x) * 4, b, g, r);
+                ab = ab + b * wgt;
+                ag = ag + g * wgt;
+                ar = ar + r * wgt;
+                norm = norm + wgt;
+            }
+        }
+        const float vb = rh(ab / norm), vg = rh(ag / norm), vr = rh(ar / norm);
+        tq[ly][lx][0] = vb;
+        tq[ly][lx][1] = vg;
+        tq[ly][lx][2] = vr;
+        st4(aq + (long long)n * aq_bs + ((long long)qy * qw + qx) * 4, vb, vg, vr);
+    }
+    __syncthreads();
+    const int h8 = qh / 2, w8 = qw / 2;
+    if (threadIdx.x < 64) {
+        const int x8l = threadIdx.x & 7, y8l = threadIdx.x >> 3;
+        const int x8 = blockIdx.x * 8 + x8l, y8 = blockIdx.y * 8 + y8l;
+        if (x8 < w8 && y8 < h8) {
+            float v[3];
+            for (int c = 0; c < 3; c++) {
+                float acc = 0.0f;
+                acc = acc + tq[2 * y8l][2 * x8l][c];
+                acc = acc + tq[2 * y8l][2 * x8l + 1][c];
+                acc = acc + tq[2 * y8l + 1][2 * x8l][c];
+                acc = acc + tq[2 * y8l + 1][2 * x8l + 1][c];
+                v[c] = rh(acc / 4.0f);
+                t8[y8l][x8l][c] = v[c];
+            }
+            st4(i8 + (long long)n * i8_bs + ((long long)y8 * w8 + x8) * 4, v[0], v[1], v[2]);
+        }
+    }
+    __syncthreads();
+    const int h16 = h8 / 2, w16 = w8 / 2;
+    if (threadIdx.x < 16) {
+        const int xl = threadIdx.x & 3, yl = threadIdx.x >> 2;
+        const int x = blockIdx.x * 4 + xl, y = blockIdx.y * 4 + yl;
+        if (x < w16 && y < h16) {
+            float v[3];
+            for (int c = 0; c < 3; c++) {
+                float acc = 0.0f;
+                acc = acc + t8[2 * yl][2 * xl][c];
+                acc = acc + t8[2 * yl][2 * xl + 1][c];
+                acc = acc + t8[2 * yl + 1][2 * xl][c];
+                acc = acc + t8[2 * yl + 1][2 * xl + 1][c];
+                v[c] = acc / 4.0f;
+            }
+            st4(i16 + (long long)n * i16_bs + ((long long)y * w16 + x) * 4, v[0], v[1], v[2]);
+        }
+    }
+}
+
+// -------------------------------------------------------------------------------------------- static age pass ----
+
+FH_DEV float diff3(uint32_t a, uint32_t b, const float* lut) {
+    float d = 0.0f;
+    d = fmaxf(d, fabsf(lut[a & 255] - lut[b & 255]));
+    d = fmaxf(d, fabsf(lut[(a >> 8) & 255] - lut[(b >> 8) & 255]));
+    d = fmaxf(d, fabsf(lut[(a >> 16) & 255] - lut[(b >> 16) & 255]));
+    return d;
+}
+
+// keep_static_age.wgsl:52-56 `diff(o) >= thr` for every pixel of the padded plane (a, b read at the clamped position)
+__global__ void k_static_changed(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb, StaticArgs s,
+                                 uint8_t* changed) {
+    __shared__ float lut[256];
+    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
+    __syncthreads();
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
+    if (x >= s.wp || y >= s.hp) return;
+    const long long src = (long long)min(y, s.h - 1) * s.w + min(x, s.w - 1);
+    const uint32_t a = __ldg(reinterpret_cast<const uint32_t*>(fa) + src);
+    const uint32_t b = __ldg(reinterpret_cast<const uint32_t*>(fb) + src);
+    changed[(long long)y * s.wp + x] = diff3(a, b, lut) >= s.thr ? 1 : 0;
+}
+
+// keep_static_age.wgsl:59-77: 9 near + 32 far probes of `changed`, the spread test, the state machine (decide, :28-36)
+__global__ void k_static_age(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb,
+                             const uint8_t* __restrict__ changed, const uint8_t* __restrict__ mask, StaticArgs s,
+                             uchar4* state, int16_t* age) {
+    __shared__ float lut[256];
+    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
+    __syncthreads();
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
+    if (x >= s.wp || y >= s.hp) return;
+    // the padded plane: p.w = wp, p.h = hp in the reference dispatch (StaticParams::new(net, wp, hp, wp, hp))
+    const int W = s.wp, H = s.hp;
+    bool moved = false;
+    for (int dy = -1; dy <= 1; dy++)
+        for (int dx = -1; dx <= 1; dx++) moved |= changed[(long long)clampi(y + dy, 0, H - 1) * W + clampi(x + dx, 0, W - 1)] != 0;
+    const int DX[8] = {1, -1, 0, 0, 1, -1, 1, -1}, DY[8] = {0, 0, 1, -1, 1, 1, -1, -1};
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int far = 4 << j;
+            moved |= changed[(long long)clampi(y + DY[i] * far, 0, H - 1) * W + clampi(x + DX[i] * far, 0, W - 1)] != 0;
+        }
+    const long long o = (long long)y * W + x;
+    const bool same = changed[o] == 0;
+    // spread (:38-50): max over the 3 x 3 neighbourhood and channels of |a(q) - a(o)|, |b(q) - b(o)|
+    const uint32_t* A = reinterpret_cast<const uint32_t*>(fa);
+    const uint32_t* B = reinterpret_cast<const uint32_t*>(fb);
+    auto at = [&](const uint32_t* f, int yy, int xx) { return __ldg(f + (long long)min(yy, s.h - 1) * s.w + min(xx, s.w - 1)); };
+    const uint32_t ao = at(A, y, x), bo = at(B, y, x);
+    float m = 0.0f;
+    for (int dy = -1; dy <= 1; dy++)
+        for (int dx = -1; dx <= 1; dx++) {
+            const int yy = clampi(y + dy, 0, H - 1), xx = clampi(x + dx, 0, W - 1);
+            const uint32_t aq = at(A, yy, xx), bq = at(B, yy, xx);
+            for (int c = 0; c < 3; c++) {
+                const int sh = 16 - 8 * c;  // channel c of the BGR plane = byte 2 - c of the rgba pixel
+                m = fmaxf(m, fabsf(lut[(aq >> sh) & 255] - lut[(ao >> sh) & 255]));
+                m = fmaxf(m, fabsf(lut[(bq >> sh) & 255] - lut[(bo >> sh) & 255]));
+            }
+        }
+    const bool still = same && m >= 0.03f;
+    uchar4 st = state[o];
+    const int raw = still ? min((int)st.x + 1, 255) : 0;
+    const int seen = still ? min((int)st.y + (moved ? 1 : 0), 255) : 0;
+    const int run = same ? min((int)st.z + 1, 255) : 0;
+    state[o] = make_uchar4((unsigned char)raw, (unsigned char)seen, (unsigned char)run, 0);
+    int16_t a = (int16_t)(seen >= 2 ? raw : -run);
+    if (s.use_mask && mask && mask[o]) a = 255;
+    age[o] = a;
+}
+
+// ------------------------------------------------------------------------------------------------ cost volume ----
+
+// luma.wgsl:13-18 (f16 luma) + sad.wgsl:10-29: one thread per pixel computes all (2r+1)^2 channels
+template <int R>
+__global__ void k_sad(const __half* __restrict__ a, int a_cs, const __half* __restrict__ b, int b_cs, long long in_bs,
+                      int h, int w, __half* out, int out_cs, long long out_bs) {
+    constexpr int SP = 2 * R + 1, WIN = SP + 2;
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
+    if (x >= w || y >= h) return;
+    const __half* A = a + (long long)n * in_bs;
+    const __half* B = b + (long long)n * in_bs;
+    auto luma = [&](const __half* p, int cs, int yy, int xx) {
+        const __half* q = p + ((long long)yy * w + xx) * cs;
+        return rh(lum3(h2f(q[0]), h2f(q[1]), h2f(q[2])));
+    };
+    float la[3][3];
+    for (int wy = -1; wy <= 1; wy++)
+        for (int wx = -1; wx <= 1; wx++) {
+            const int yy = y + wy, xx = x + wx;
+            la[wy + 1][wx + 1] = (yy >= 0 && yy < h && xx >= 0 && xx < w) ? luma(A, a_cs, yy, xx) : 0.0f;
+        }
+    float lb[WIN][WIN];  // lb at clamp(y + d), d in [-R-1, R+1]
+    for (int i = 0; i < WIN; i++)
+        for (int j = 0; j < WIN; j++)
+            lb[i][j] = luma(B, b_cs, clampi(y + i - R - 1, 0, h - 1), clampi(x + j - R - 1, 0, w - 1));
+    __half* o = out + (long long)n * out_bs + ((long long)y * w + x) * out_cs;
+    for (int c = 0; c < SP * SP; c++) {
+        const int dy = c / SP - R, dx = c % SP - R;
+        float acc = 0.0f;
+        for (int wy = -1; wy <= 1; wy++)
+            for (int wx = -1; wx <= 1; wx++) {
+                const int yy = y + wy, xx = x + wx;
+                if (yy >= 0 && yy < h && xx >= 0 && xx < w) {
+                    // lb(clamp(yy + dy)) = the clamped window entry when yy is inside the image
+                    const int sy = clampi(yy + dy, 0, h - 1) - y + R + 1, sx = clampi(xx + dx, 0, w - 1) - x + R + 1;
+                    acc = acc + fabsf(la[wy + 1][wx + 1] - lb[sy][sx]);
+                }
+            }
+        o[c] = f2h(acc / 9.0f);
+    }
+    for (int c = SP * SP; c < out_cs; c++) o[c] = f2h(0.0f);
+}
+
+// ------------------------------------------------------------------------------------------- flow upsampling ----
+
+// interp.wgsl:19-28 bilinear (align_corners = False) of o[0:4] x 16 (the `flow16` view) and o[4:7] (`vis16`)
+__global__ void k_upsample_flow_vis(const __half* __restrict__ o, int o_cs, long long o_bs, int ih, int iw, __half* fv,
+                                    long long fv_bs, int oh, int ow) {
+    const int ox = blockIdx.x * blockDim.x + threadIdx.x, oy = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
+    if (ox >= ow || oy >= oh) return;
+    const float sh = (float)ih / (float)oh, sw = (float)iw / (float)ow;
+    const float iy = ((float)oy + 0.5f) * sh - 0.5f, ix = ((float)ox + 0.5f) * sw - 0.5f;
+    const int y0 = (int)floorf(iy), x0 = (int)floorf(ix);
+    const float fy = iy - (float)y0, fx = ix - (float)x0;
+    const int y0c = clampi(y0, 0, ih - 1), y1c = clampi(y0 + 1, 0, ih - 1);
+    const int x0c = clampi(x0, 0, iw - 1), x1c = clampi(x0 + 1, 0, iw - 1);
+    const __half* b = o + (long long)n * o_bs;
+    const __half* p00 = b + ((long long)y0c * iw + x0c) * o_cs;
+    const __half* p01 = b + ((long long)y0c * iw + x1c) * o_cs;
+    const __half* p10 = b + ((long long)y1c * iw + x0c) * o_cs;
+    const __half* p11 = b + ((long long)y1c * iw + x1c) * o_cs;
+    __half r[8];
+    for (int c = 0; c < 7; c++) {
+        const float v00 = h2f(p00[c]), v01 = h2f(p01[c]), v10 = h2f(p10[c]), v11 = h2f(p11[c]);
+        const float val = (v00 * (1.0f - fx) + v01 * fx) * (1.0f - fy) + (v10 * (1.0f - fx) + v11 * fx) * fy;
+        r[c] = f2h(c < 4 ? val * 16.0f : val * 1.0f);
+    }
+    r[7] = f2h(0.0f);
+    *reinterpret_cast<uint4*>(fv + (long long)n * fv_bs + ((long long)oy * ow + ox) * 8) = *reinterpret_cast<uint4*>(r);
+}
+
+// ----------------------------------------------------------------------------------------------- fine warps ----
+
+struct Bil {
+    long long i00, i01, i10, i11;
+    float ax, ay;
+};
+// warp.wgsl:17-23: sample position and clamped corners for flow (fx, fy) at pixel (x, y)
+FH_DEV Bil bil_at(int x, int y, float fx, float fy, int h, int w) {
+    const float gx = (float)x + fx, gy = (float)y + fy;
+    const int x0 = (int)floorf(gx), y0 = (int)floorf(gy);
+    Bil b;
+    b.ax = gx - (float)x0;
+    b.ay = gy - (float)y0;
+    const int x0c = clampi(x0, 0, w - 1), x1c = clampi(x0 + 1, 0, w - 1);
+    const int y0c = clampi(y0, 0, h - 1), y1c = clampi(y0 + 1, 0, h - 1);
+    b.i00 = (long long)y0c * w + x0c;
+    b.i01 = (long long)y0c * w + x1c;
+    b.i10 = (long long)y1c * w + x0c;
+    b.i11 = (long long)y1c * w + x1c;
+    return b;
+}
+FH_DEV float bil_mix(float v00, float v01, float v10, float v11, float ax, float ay) {
+    const float top = v00 * (1.0f - ax) + v01 * ax, bot = v10 * (1.0f - ax) + v11 * ax;
+    return top * (1.0f - ay) + bot * ay;
+}
+
+// warp.wgsl of the fine loop: one thread per e8 pixel writes wa, wb, ia, ib (all channels)
+__global__ void k_warp_fine(WarpFineArgs a) {
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
+    if (x >= a.w8 || y >= a.h8) return;
+    const __half* fv = a.fv + (long long)n * a.fv_bs + ((long long)y * a.w8 + x) * 8;
+    __half* o = a.wbuf + (long long)n * a.wbuf_bs + ((long long)y * a.w8 + x) * 88;
+    for (int side = 0; side < 2; side++) {
+        // flow8f = flow[0:2] * 0.125 (the view scale, applied in f32: warp.wgsl:17-18)
+        const float fx = h2f(fv[2 * side]) * 0.125f, fy = h2f(fv[2 * side + 1]) * 0.125f;
+        const Bil b = bil_at(x, y, fx, fy, a.h8, a.w8);
+        const __half* f8 = (side ? a.f8b : a.f8a) + (long long)n * a.f8_bs;
+        __half* ow = o + side * 40;
+        for (int c = 0; c < a.c8; c++) {
+            const float v = bil_mix(h2f(f8[b.i00 * a.f8_cs + c]), h2f(f8[b.i01 * a.f8_cs + c]), h2f(f8[b.i10 * a.f8_cs + c]),
+                                    h2f(f8[b.i11 * a.f8_cs + c]), b.ax, b.ay);
+            ow[c] = f2h(v * 1.0f);
+        }
+        for (int c = a.c8; c < 40; c++) ow[c] = f2h(0.0f);
+        const __half* im = (side ? a.i8b.p + (long long)n * a.i8b.bs : a.i8a.p + (long long)n * a.i8a.bs);
+        float v[3];
+        for (int c = 0; c < 3; c++)
+            v[c] = bil_mix(h2f(im[b.i00 * 4 + c]), h2f(im[b.i01 * 4 + c]), h2f(im[b.i10 * 4 + c]), h2f(im[b.i11 * 4 + c]),
+                           b.ax, b.ay) * 1.0f;
+        st4(o + 80 + side * 4, v[0], v[1], v[2]);
+    }
+}
+
+// ----------------------------------------------------------------------------------------------------- GMHS ----
+
+// gm_fit_reduce.wgsl + gm_fit_solve.wgsl, 4 IRLS iterations in one CTA of 1024 threads. The reduction reproduces the
+// shader's: 32 workgroups x 256 threads, each thread a strided partial sum, a 256-wide tree per workgroup
+// (off = 128 .. 1), then the solve's sequential sum over workgroups. One warp reduces one (workgroup, channel).
+__global__ void __launch_bounds__(1024) k_gm_fit(GmArgs g) {
+    __shared__ float part[32][4][9];
+    __shared__ float coef[16];
+    const int n = blockIdx.x;
+    const __half* fl = g.fv + (long long)n * g.fv_bs;
+    const int w8 = g.w8, h8 = g.h8, np = h8 * w8;
+    const float sx = 2.0f / (float)max(w8 - 1, 1), sy = 2.0f / (float)max(h8 - 1, 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x < 16) coef[threadIdx.x] = 0.0f;
+    __syncthreads();
+    for (int it = 0; it < 4; it++) {
+        for (int task = warp; task < 32 * 4; task += 32) {
+            const int wg = task >> 2, c = task & 3;
+            // 8 tree inputs per lane: virtual threads t = lane + 32 k, k = 0..7
+            float v[8][9];
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                float s[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+                for (int i = wg * 256 + lane + 32 * k; i < np; i += 256 * 32) {
+                    const int yy = i / w8, xx = i - yy * w8;
+                    const float x = -1.0f + sx * (float)xx, y = -1.0f + sy * (float)yy;
+                    const float f = h2f(fl[(long long)i * 8 + c]);
+                    float w2 = 1.0f;
+                    if (it > 0) {
+                        const float r = fabsf(f - (coef[c * 4] + coef[c * 4 + 1] * x + coef[c * 4 + 2] * y));
+                        w2 = g.delta / fmaxf(g.delta, r);
+                    }
+                    s[0] = s[0] + w2;
+                    s[1] = s[1] + w2 * x;
+                    s[2] = s[2] + w2 * y;
+                    s[3] = s[3] + w2 * x * x;
+                    s[4] = s[4] + w2 * x * y;
+                    s[5] = s[5] + w2 * y * y;
+                    s[6] = s[6] + w2 * f;
+                    s[7] = s[7] + w2 * x * f;
+                    s[8] = s[8] + w2 * y * f;
+                }
+#pragma unroll
+                for (int q = 0; q < 9; q++) v[k][q] = s[q];
+            }
+#pragma unroll
+            for (int q = 0; q < 9; q++) {
+                // off 128: t += t + 128 (k += k + 4); off 64: k += k + 2; off 32: k += k + 1
+                const float a0 = v[0][q] + v[4][q], a1 = v[1][q] + v[5][q], a2 = v[2][q] + v[6][q], a3 = v[3][q] + v[7][q];
+                const float b0 = a0 + a2, b1 = a1 + a3;
+                float s = b0 + b1;
+                for (int off = 16; off > 0; off >>= 1) s = s + __shfl_down_sync(0xffffffffu, s, off);
+                if (lane == 0) part[wg][c][q] = s;
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x < 4) {
+            const int c = threadIdx.x;
+            float s[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+            for (int wg = 0; wg < 32; wg++)
+                for (int k = 0; k < 9; k++) s[k] = s[k] + part[wg][c][k];
+            const float m00 = s[0] + 1e-6f, m01 = s[1], m02 = s[2], m11 = s[3] + 1e-6f, m12 = s[4], m22 = s[5] + 1e-6f;
+            const float det = m00 * (m11 * m22 - m12 * m12) - m01 * (m01 * m22 - m12 * m02) + m02 * (m01 * m12 - m11 * m02);
+            float c0, c1, c2;
+            if (fabsf(det) < 1e-12f) {
+                c0 = s[6] / fmaxf(s[0], 1e-6f);
+                c1 = c2 = 0.0f;
+            } else {
+                const float i00 = (m11 * m22 - m12 * m12) / det, i01 = (m02 * m12 - m01 * m22) / det;
+                const float i02 = (m01 * m12 - m02 * m11) / det, i11 = (m00 * m22 - m02 * m02) / det;
+                const float i12 = (m01 * m02 - m00 * m12) / det, i22 = (m00 * m11 - m01 * m01) / det;
+                c0 = i00 * s[6] + i01 * s[7] + i02 * s[8];
+                c1 = i01 * s[6] + i11 * s[7] + i12 * s[8];
+                c2 = i02 * s[6] + i12 * s[7] + i22 * s[8];
+            }
+            coef[c * 4] = c0;
+            coef[c * 4 + 1] = c1;
+            coef[c * 4 + 2] = c2;
+            coef[c * 4 + 3] = 0.0f;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x < 16) g.coef[n * 16 + threadIdx.x] = coef[threadIdx.x];
+}
+
+// gm_cost.wgsl:15-75
+__global__ void k_gm_cost(GmArgs g) {
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
+    if (x >= g.wc || y >= g.hc) return;
+    const float* coef = g.coef + n * 16;
+    const __half* A = g.A + (long long)n * g.ab_bs;
+    const __half* B = g.B + (long long)n * g.ab_bs;
+    const __half* fl = g.fv + (long long)n * g.fv_bs;
+    const int w = g.w, h = g.h, w8 = g.w8, h8 = g.h8;
+    auto lum = [&](const __half* s, int yy, int xx) {
+        float b, gg, r;
+        ld4(s + ((long long)yy * w + xx) * 4, b, gg, r);
+        return lum3(b, gg, r);
+    };
+    auto samp = [&](const __half* s, float gx, float gy) {
+        const int x0 = (int)floorf(gx), y0 = (int)floorf(gy);
+        const float ax = gx - (float)x0, ay = gy - (float)y0;
+        const int x0c = clampi(x0, 0, w - 1), x1c = clampi(x0 + 1, 0, w - 1);
+        const int y0c = clampi(y0, 0, h - 1), y1c = clampi(y0 + 1, 0, h - 1);
+        const float top = lum(s, y0c, x0c) * (1.0f - ax) + lum(s, y0c, x1c) * ax;
+        const float bot = lum(s, y1c, x0c) * (1.0f - ax) + lum(s, y1c, x1c) * ax;
+        return top * (1.0f - ay) + bot * ay;
+    };
+    auto flow8 = [&](int c, float rx, float ry) {
+        const float ix = (rx + 0.5f) * (float)w8 / (float)w - 0.5f, iy = (ry + 0.5f) * (float)h8 / (float)h - 0.5f;
+        const int x0 = (int)floorf(ix), y0 = (int)floorf(iy);
+        const float fx = ix - (float)x0, fy = iy - (float)y0;
+        const int x0c = clampi(x0, 0, w8 - 1), x1c = clampi(x0 + 1, 0, w8 - 1);
+        const int y0c = clampi(y0, 0, h8 - 1), y1c = clampi(y0 + 1, 0, h8 - 1);
+        const float top = h2f(fl[((long long)y0c * w8 + x0c) * 8 + c]) * (1.0f - fx) + h2f(fl[((long long)y0c * w8 + x1c) * 8 + c]) * fx;
+        const float bot = h2f(fl[((long long)y1c * w8 + x0c) * 8 + c]) * (1.0f - fx) + h2f(fl[((long long)y1c * w8 + x1c) * 8 + c]) * fx;
+        return top * (1.0f - fy) + bot * fy;
+    };
+    auto aff = [&](int c, float rx, float ry) {
+        const float ix = (rx + 0.5f) * (float)w8 / (float)w - 0.5f, iy = (ry + 0.5f) * (float)h8 / (float)h - 0.5f;
+        const float xn = -1.0f + 2.0f * ix / (float)max(w8 - 1, 1), yn = -1.0f + 2.0f * iy / (float)max(h8 - 1, 1);
+        return coef[c * 4] + coef[c * 4 + 1] * xn + coef[c * 4 + 2] * yn;
+    };
+    const float ds = 2.0f;
+    const float rx = ((float)x + 0.5f) * ds - 0.5f, ry = ((float)y + 0.5f) * ds - 0.5f;
+    const float f0x = flow8(0, rx, ry), f0y = flow8(1, rx, ry), f1x = flow8(2, rx, ry), f1y = flow8(3, rx, ry);
+    const float cm = fabsf(samp(A, rx + f0x, ry + f0y) - samp(B, rx + f1x, ry + f1y));
+    const float g0x = aff(0, rx, ry), g0y = aff(1, rx, ry), g1x = aff(2, rx, ry), g1y = aff(3, rx, ry);
+    const float wm = (float)w - 1.0f, hm = (float)h - 1.0f;
+    const float ax = rx + g0x, ay = ry + g0y, bx = rx + g1x, by = ry + g1y;
+    const bool inside = ax >= 0.0f && ax <= wm && ay >= 0.0f && ay <= hm && bx >= 0.0f && bx <= wm && by >= 0.0f && by <= hm;
+    const float ca = inside ? fabsf(samp(A, ax, ay) - samp(B, bx, by)) : cm;
+    const float l = samp(A, rx, ry);
+    const float dvx = (g1x - g0x) - (f1x - f0x), dvy = (g1y - g0y) - (f1y - f0y);
+    const long long nn = (long long)g.hc * g.wc, i = (long long)y * g.wc + x;
+    float* maps = g.maps + (long long)n * 6 * nn;
+    maps[i] = cm;
+    maps[nn + i] = ca;
+    maps[2 * nn + i] = sqrtf(dvx * dvx + dvy * dvy);
+    maps[3 * nn + i] = l;
+    maps[4 * nn + i] = l * l;
+    maps[5 * nn + i] = fabsf(l - samp(B, rx, ry));
+}
+
+// gm_box.wgsl box_h / box_v: radius r, edge replicate, the first c maps
+__global__ void k_box_h(const float* src, float* dst, int c, int h, int w, int r, long long bs) {
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
+    const int n = blockIdx.z / c, ch = blockIdx.z - n * c;
+    if (x >= w || y >= h) return;
+    const long long row = (long long)n * bs + ((long long)ch * h + y) * w;
+    float acc = 0.0f;
+    for (int d = -r; d <= r; d++) acc = acc + src[row + clampi(x + d, 0, w - 1)];
+    dst[row + x] = acc / (float)(2 * r + 1);
+}
+__global__ void k_box_v(const float* src, float* dst, int c, int h, int w, int r, long long bs) {
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
+    const int n = blockIdx.z / c, ch = blockIdx.z - n * c;
+    if (x >= w || y >= h) return;
+    const long long plane = (long long)n * bs + (long long)ch * h * w;
+    float acc = 0.0f;
+    for (int d = -r; d <= r; d++) acc = acc + src[plane + (long long)clampi(y + d, 0, h - 1) * w + x];
+    dst[plane + (long long)y * w + x] = acc / (float)(2 * r + 1);
+}
+
+// gm_select.wgsl:12-28 (eps 0, tex 0.015: gmhs.rs:208)
+__global__ void k_gm_select(GmArgs g) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x, i = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
+    if (j >= g.w8 || i >= g.h8) return;
+    const float* coef = g.coef + n * 16;
+    const int x = clampi((int)floorf(((float)j + 0.5f) * (float)g.wc / (float)g.w8), 0, g.wc - 1);
+    const int y = clampi((int)floorf(((float)i + 0.5f) * (float)g.hc / (float)g.h8), 0, g.hc - 1);
+    const long long nn = (long long)g.hc * g.wc, idx = (long long)y * g.wc + x;
+    const float* maps = g.maps + (long long)n * 6 * nn;
+    const float cm = maps[idx], ca = maps[nn + idx], dv = maps[2 * nn + idx], lm = maps[3 * nn + idx], l2 = maps[4 * nn + idx];
+    const float sd = sqrtf(fmaxf(l2 - lm * lm, 0.0f));
+    const float eps = 0.0f, tex = 0.015f;
+    if (ca + eps < cm && dv > g.dmin && sd > tex) {
+        const float xn = -1.0f + 2.0f * (float)j / (float)max(g.w8 - 1, 1), yn = -1.0f + 2.0f * (float)i / (float)max(g.h8 - 1, 1);
+        __half* f = g.fv + (long long)n * g.fv_bs + ((long long)i * g.w8 + j) * 8;
+        for (int c = 0; c < 4; c++) f[c] = f2h(coef[c * 4] + coef[c * 4 + 1] * xn + coef[c * 4 + 2] * yn);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------- mid stage ----
+
+// net/build.rs:332-359 film_mlp (f32, in the host's order) + film.wgsl:9-15
+__global__ void k_film(FilmArgs a) {
+    extern __shared__ float sm[];
+    float* hv = sm;              // [hidden]
+    float* gv = sm + a.hidden;   // [2 cr], f16-rounded
+    const int n = blockIdx.z;
+    const float t = a.t[n];
+    const int tid = threadIdx.y * blockDim.x + threadIdx.x, nt = blockDim.x * blockDim.y;
+    for (int i = tid; i < a.hidden; i += nt) hv[i] = fmaxf(a.w1[i] * t + a.b1[i], 0.0f);
+    __syncthreads();
+    for (int o = tid; o < 2 * a.cr; o += nt) {
+        float acc = 0.0f;
+        for (int i = 0; i < a.hidden; i++) acc = acc + a.w2[o * a.hidden + i] * hv[i];
+        gv[o] = rh(a.b2[o] + acc);
+    }
+    __syncthreads();
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
+    if (x >= a.w8 || y >= a.h8) return;
+    const __half* h = a.h + (long long)n * a.h_bs + ((long long)y * a.w8 + x) * a.h_cs;
+    __half* o = a.hm + (long long)n * a.hm_bs + ((long long)y * a.w8 + x) * a.hm_cs;
+    for (int c = 0; c < a.cr; c++) o[c] = f2h(h2f(h[c]) * (1.0f + gv[c]) + gv[c + a.cr]);
+}
+
+__global__ void k_mid_combine(const float* tt, const __half* __restrict__ fv, long long fv_bs, const __half* __restrict__ d,
+                              long long d_bs, __half* ft, long long ft_bs, int h8, int w8) {
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
+    if (x >= w8 || y >= h8) return;
+    const float t = tt[n];
+    const float af = 2.0f * t, ab = 2.0f * (1.0f - t);  // mul_t fwd / bwd (net/build.rs:290-308)
+    const long long pix = (long long)y * w8 + x;
+    const __half* f = fv + (long long)n * fv_bs + pix * 8;
+    const __half* dd = d + (long long)n * d_bs + pix * 8;
+    __half r[8];
+    for (int c = 0; c < 4; c++) {
+        const float lin = rh(h2f(f[c]) * (c < 2 ? af : ab));
+        r[c] = f2h(lin + h2f(dd[c]));
+    }
+    const float dm = h2f(dd[4]);
+    const float dvis[3] = {dm, rh(dm * -1.0f), 0.0f};
+    for (int c = 0; c < 3; c++) r[4 + c] = f2h(h2f(f[4 + c]) + dvis[c]);
+    r[7] = f2h(0.0f);
+    *reinterpret_cast<uint4*>(ft + (long long)n * ft_bs + pix * 8) = *reinterpret_cast<uint4*>(r);
+}
+
+// convex.wgsl:10-35, all 7 channels of one output pixel per thread
+__global__ void k_convex(const __half* __restrict__ wt, int wt_cs, long long wt_bs, const __half* __restrict__ x,
+                         long long x_bs, int h, int w, __half* up, long long up_bs) {
+    const int ox = blockIdx.x * blockDim.x + threadIdx.x, oy = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
+    if (ox >= 2 * w || oy >= 2 * h) return;
+    const int ihh = oy / 2, iww = ox / 2, sy = oy % 2, sx = ox % 2;
+    const __half* wp = wt + (long long)n * wt_bs + ((long long)ihh * w + iww) * wt_cs;
+    float ws[9], m = -3.0e38f;
+    for (int k = 0; k < 9; k++) {
+        ws[k] = h2f(wp[k * 4 + sy * 2 + sx]);
+        m = fmaxf(m, ws[k]);
+    }
+    float denom = 0.0f;
+    for (int k = 0; k < 9; k++) {
+        ws[k] = expf(ws[k] - m);
+        denom = denom + ws[k];
+    }
+    float acc[7] = {0, 0, 0, 0, 0, 0, 0};
+    const __half* xb = x + (long long)n * x_bs;
+    for (int k = 0; k < 9; k++) {
+        const int ny = ihh - 1 + k / 3, nx = iww - 1 + k % 3;
+        const float wk = ws[k] / denom;
+        const bool in = ny >= 0 && ny < h && nx >= 0 && nx < w;
+        const __half* xp = xb + ((long long)(in ? ny : 0) * w + (in ? nx : 0)) * 8;
+        for (int c = 0; c < 7; c++) acc[c] = acc[c] + wk * (in ? h2f(xp[c]) : 0.0f);
+    }
+    __half r[8];
+    for (int c = 0; c < 7; c++) r[c] = f2h(acc[c]);
+    r[7] = f2h(0.0f);
+    *reinterpret_cast<uint4*>(up + (long long)n * up_bs + ((long long)oy * 2 * w + ox) * 8) = *reinterpret_cast<uint4*>(r);
+}
+
+// warp.wgsl of aq / bq by flow_tq * 0.25 at one q pixel
+FH_DEV void warp3(const __half* img, const __half* up7, int c0, int x, int y, int h, int w, float* v) {
+    const __half* f = up7 + ((long long)y * w + x) * 8;
+    const float fx = h2f(f[c0]) * 0.25f, fy = h2f(f[c0 + 1]) * 0.25f;
+    const Bil b = bil_at(x, y, fx, fy, h, w);
+    for (int c = 0; c < 3; c++)
+        v[c] = rh(bil_mix(h2f(img[b.i00 * 4 + c]), h2f(img[b.i01 * 4 + c]), h2f(img[b.i10 * 4 + c]), h2f(img[b.i11 * 4 + c]),
+                          b.ax, b.ay) * 1.0f);
+}
+// blendmix.wgsl:12-28 at one q pixel (vis = up7[4:7])
+FH_DEV void blendmix_at(const __half* aq, const __half* bq, const __half* up7, int x, int y, int h, int w, float* out,
+                        float* rwa, float* rwb) {
+    warp3(aq, up7, 0, x, y, h, w, rwa);
+    warp3(bq, up7, 2, x, y, h, w, rwb);
+    const __half* v = up7 + ((long long)y * w + x) * 8 + 4;
+    const float a = h2f(v[0]) * 1.0f, b = h2f(v[1]) * 1.0f, c = h2f(v[2]) * 1.0f;
+    const float m = fmaxf(a, fmaxf(b, c));
+    const float ea = expf(a - m), eb = expf(b - m), ec = expf(c - m);
+    const float s = ea + eb + ec;
+    const float pa = rh((ea + 0.5f * ec) / s), pb = rh((eb + 0.5f * ec) / s);
+    for (int ch = 0; ch < 3; ch++) {
+        const float t1 = rh(rwa[ch] * pa), t2 = rh(rwb[ch] * pb);
+        out[ch] = rh(t1 + t2);
+    }
+}
+
+__global__ void k_refine_input(const __half* __restrict__ up7, long long up_bs, Img4 aq, Img4 bq, int h, int w, __half* rx,
+                               long long rx_bs) {
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
+    if (x >= w || y >= h) return;
+    const __half* u = up7 + (long long)n * up_bs;
+    const __half* A = aq.p + (long long)n * aq.bs;
+    const __half* B = bq.p + (long long)n * bq.bs;
+    float bl[3], rwa[3], rwb[3], t0[3], t1[3];
+    blendmix_at(A, B, u, x, y, h, w, bl, rwa, rwb);
+    // luma.wgsl grad (:20-28): forward differences of the (unrounded) luma of blend
+    const float c = lum3(bl[0], bl[1], bl[2]);
+    float gx = 0.0f, gy = 0.0f;
+    if (x + 1 < w) {
+        float b2[3];
+        blendmix_at(A, B, u, x + 1, y, h, w, b2, t0, t1);
+        gx = lum3(b2[0], b2[1], b2[2]) - c;
+    }
+    if (y + 1 < h) {
+        float b2[3];
+        blendmix_at(A, B, u, x, y + 1, h, w, b2, t0, t1);
+        gy = lum3(b2[0], b2[1], b2[2]) - c;
+    }
+    const __half* up = u + ((long long)y * w + x) * 8;
+    __half r[16];
+    for (int k = 0; k < 3; k++) {
+        r[k] = f2h(rwa[k]);
+        r[3 + k] = f2h(rwb[k]);
+        r[6 + k] = up[4 + k];
+    }
+    for (int k = 0; k < 4; k++) r[9 + k] = f2h(h2f(up[k]) * 0.05f);  // the flow_tq20 view, materialised by chcopy
+    r[13] = f2h(fabsf(gx) + fabsf(gy));
+    r[14] = r[15] = f2h(0.0f);
+    uint4* o = reinterpret_cast<uint4*>(rx + (long long)n * rx_bs + ((long long)y * w + x) * 16);
+    o[0] = reinterpret_cast<uint4*>(r)[0];
+    o[1] = reinterpret_cast<uint4*>(r)[1];
+}
+
+// ---------------------------------------------------------------------------------------------------- render ----
+
+FH_DEV float cub1(float x) {
+    const float a = -0.75f;
+    return ((a + 2.0f) * x - (a + 3.0f)) * x * x + 1.0f;
+}
+FH_DEV float cub2(float x) {
+    const float a = -0.75f;
+    return ((a * x - 5.0f * a) * x + 8.0f * a) * x - 4.0f * a;
+}
+
+struct Frame {
+    const uint32_t* p;
+    int w, h;
+    FH_DEV uint32_t at(int y, int x) const { return __ldg(p + (long long)min(y, h - 1) * w + min(x, w - 1)); }
+};
+
+// render.wgsl:82-161 + gpu/pipeline.rs:10-34 (static rules) + keep_static.wgsl:21-32 + rgba_out.wgsl:9-17
+__global__ void __launch_bounds__(256) k_render(RenderArgs r) {
+    __shared__ float lut[256];
+    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
+    __syncthreads();
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
+    if (x >= r.w || y >= r.h) return;
+    const int H = r.hp, W = r.wp, hq = r.hq, wq = r.wq;
+    const Frame A{reinterpret_cast<const uint32_t*>(r.fa + (long long)n * r.f_bs), r.w, r.h};
+    const Frame B{reinterpret_cast<const uint32_t*>(r.fb + (long long)n * r.f_bs), r.w, r.h};
+    const __half* up = r.up7 + (long long)n * r.up_bs;
+    const __half* rt = r.rt + (long long)n * r.rt_bs;
+    const int16_t* age = r.age ? r.age + (long long)n * r.age_bs : nullptr;
+    // the Q-res sample corners (render.wgsl:87-92)
+    const float sh = (float)hq / (float)H, sw = (float)wq / (float)W;
+    const float iy = ((float)y + 0.5f) * sh - 0.5f, ix = ((float)x + 0.5f) * sw - 0.5f;
+    const int qy0 = (int)floorf(iy), qx0 = (int)floorf(ix);
+    const float qfy = iy - (float)qy0, qfx = ix - (float)qx0;
+    const int qy0c = clampi(qy0, 0, hq - 1), qy1c = clampi(qy0 + 1, 0, hq - 1);
+    const int qx0c = clampi(qx0, 0, wq - 1), qx1c = clampi(qx0 + 1, 0, wq - 1);
+    const __half* u00 = up + ((long long)qy0c * wq + qx0c) * 8;
+    const __half* u01 = up + ((long long)qy0c * wq + qx1c) * 8;
+    const __half* u10 = up + ((long long)qy1c * wq + qx0c) * 8;
+    const __half* u11 = up + ((long long)qy1c * wq + qx1c) * 8;
+    float f[4], v[3];
+    for (int c = 0; c < 4; c++)
+        f[c] = bil_mix(h2f(u00[c]), h2f(u01[c]), h2f(u10[c]), h2f(u11[c]), qfx, qfy) * ((c & 1) == 0 ? r.fsx : r.fsy);
+    for (int c = 0; c < 3; c++) v[c] = bil_mix(h2f(u00[4 + c]), h2f(u01[4 + c]), h2f(u10[4 + c]), h2f(u11[4 + c]), qfx, qfy) * 1.0f;
+    const float m = fmaxf(v[0], fmaxf(v[1], v[2]));
+    const float e0 = expf(v[0] - m), e1 = expf(v[1] - m), e2 = expf(v[2] - m);
+    const float s = e0 + e1 + e2;
+    const float wa_w = (e0 + 0.5f * e2) / s, wb_w = (e1 + 0.5f * e2) / s;
+    const float gxa = (float)x + f[0], gya = (float)y + f[1], gxb = (float)x + f[2], gyb = (float)y + f[3];
+    float ca[3], cb[3], cr[3];
+    auto chan = [&](uint32_t px, int c) { return lut[(px >> (16 - 8 * c)) & 255]; };  // BGR channel c of rgba
+    auto sample = [&](const Frame& F, float gx, float gy, float* out) {
+        if (r.cubic) {
+            const int px = (int)floorf(gx), py = (int)floorf(gy);
+            const float tx = gx - (float)px, ty = gy - (float)py;
+            const float cx[4] = {cub2(tx + 1.0f), cub1(tx), cub1(1.0f - tx), cub2(2.0f - tx)};
+            const float cy[4] = {cub2(ty + 1.0f), cub1(ty), cub1(1.0f - ty), cub2(2.0f - ty)};
+            int xs[4];
+            for (int k = 0; k < 4; k++) xs[k] = clampi(px - 1 + k, 0, W - 1);
+            float acc[3] = {0.0f, 0.0f, 0.0f};
+            for (int j = 0; j < 4; j++) {
+                const int yy = clampi(py - 1 + j, 0, H - 1);
+                const uint32_t p0 = F.at(yy, xs[0]), p1 = F.at(yy, xs[1]), p2 = F.at(yy, xs[2]), p3 = F.at(yy, xs[3]);
+                for (int c = 0; c < 3; c++) {
+                    const float row = chan(p0, c) * cx[0] + chan(p1, c) * cx[1] + chan(p2, c) * cx[2] + chan(p3, c) * cx[3];
+                    acc[c] = j == 0 ? row * cy[0] : acc[c] + row * cy[j];
+                }
+            }
+            for (int c = 0; c < 3; c++) out[c] = acc[c];
+        } else {
+            const int xx0 = (int)floorf(gx), yy0 = (int)floorf(gy);
+            const float ax = gx - (float)xx0, ay = gy - (float)yy0;
+            const int x0 = clampi(xx0, 0, W - 1), x1 = clampi(xx0 + 1, 0, W - 1);
+            const int y0 = clampi(yy0, 0, H - 1), y1 = clampi(yy0 + 1, 0, H - 1);
+            const uint32_t p00 = F.at(y0, x0), p01 = F.at(y0, x1), p10 = F.at(y1, x0), p11 = F.at(y1, x1);
+            for (int c = 0; c < 3; c++) out[c] = bil_mix(chan(p00, c), chan(p01, c), chan(p10, c), chan(p11, c), ax, ay);
+        }
+    };
+    sample(A, gxa, gya, ca);
+    sample(B, gxb, gyb, cb);
+    const __half* r00 = rt + ((long long)qy0c * wq + qx0c) * 4;
+    const __half* r01 = rt + ((long long)qy0c * wq + qx1c) * 4;
+    const __half* r10 = rt + ((long long)qy1c * wq + qx0c) * 4;
+    const __half* r11 = rt + ((long long)qy1c * wq + qx1c) * 4;
+    for (int c = 0; c < 3; c++) cr[c] = bil_mix(h2f(r00[c]), h2f(r01[c]), h2f(r10[c]), h2f(r11[c]), qfx, qfy);
+    float bwa = wa_w, bwb = wb_w, rk = 1.0f, stillw = 0.0f, own[3] = {0.0f, 0.0f, 0.0f};
+    const float third = 1.0f / 3.0f;
+    const uint32_t pa_here = A.at(y, x), pb_here = B.at(y, x);
+    if (r.flags & 2u) {
+        float es = 0.0f;
+        for (int dy = -1; dy <= 1; dy++)
+            for (int dx = -1; dx <= 1; dx++) {
+                const int yy = clampi(y + dy, 0, H - 1), xx = clampi(x + dx, 0, W - 1);
+                const uint32_t pa = A.at(yy, xx), pb = B.at(yy, xx);
+                for (int c = 0; c < 3; c++) es += fabsf(chan(pa, c) - chan(pb, c));
+            }
+        es = es / 27.0f;
+        for (int c = 0; c < 3; c++) own[c] = 0.5f * (chan(pa_here, c) + chan(pb_here, c));
+        const float ef = fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
+        stillw = fminf(fmaxf((ef - es) / 0.04f, 0.0f), 1.0f) * (es < 0.03f ? 1.0f : 0.0f);
+    }
+    if (r.flags & 1u) {
+        const float d = fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
+        const float k = fminf(fmaxf((d - 0.04f) / 0.08f, 0.0f), 1.0f);
+        const float pa = wa_w >= wb_w ? 1.0f : 0.0f;
+        bwa = wa_w * (1.0f - k) + pa * k;
+        bwb = wb_w * (1.0f - k) + (1.0f - pa) * k;
+        rk = 1.0f - k;
+    }
+    float raw = 0.0f;
+    const long long o = (long long)y * W + x;
+    if (age) {
+        auto on_static = [&](float gx, float gy) {
+            const int cx = (int)rintf(gx), cy = (int)rintf(gy);  // WGSL round(): half to even
+            for (int dy = -1; dy <= 1; dy++)
+                for (int dx = -1; dx <= 1; dx++)
+                    if ((float)age[(long long)clampi(cy + dy, 0, H - 1) * W + clampi(cx + dx, 0, W - 1)] >= r.min_age) return true;
+            return false;
+        };
+        const bool sa = on_static(gxa, gya), sb = on_static(gxb, gyb);
+        stillw = stillw * (fabsf((float)age[o]) >= 3.0f ? 1.0f : 0.0f);
+        if (sa && sb) {
+            rk = 0.0f;
+            raw = 1.0f;
+        } else if (sa) {
+            rk = 0.0f;
+            bwa = 0.0f;
+            bwb = 1.0f;
+        } else if (sb) {
+            rk = 0.0f;
+            bwa = 1.0f;
+            bwb = 0.0f;
+        }
+    }
+    // keep_static apply ramp (keep_static.wgsl:25-26)
+    const float kk = age ? fminf(fmaxf(((float)age[o] - r.min_age + 2.0f) / 2.0f, 0.0f), 1.0f) : 0.0f;
+    uint32_t q[3];
+    for (int c = 0; c < 3; c++) {
+        const float mixv = ca[c] * bwa + cb[c] * bwb + cr[c] * rk;
+        float ov = fminf(fmaxf(mixv * (1.0f - stillw) + own[c] * stillw, 0.0f), 1.0f);
+        const float src = 0.5f * (chan(pa_here, c) + chan(pb_here, c));
+        if (age) ov = fminf(fmaxf(ov * (1.0f - raw) + src * raw, 0.0f), 1.0f);
+        float hv = rh(ov);  // the render plane is f16
+        if (kk > 0.0f) hv = rh(hv * (1.0f - kk) + src * kk);
+        q[c] = (uint32_t)(fminf(fmaxf(hv, 0.0f), 1.0f) * 255.0f + 0.5f);
+    }
+    // q[0] = B, q[1] = G, q[2] = R
+    reinterpret_cast<uint32_t*>(r.out + (long long)n * r.out_bs)[(long long)y * r.w + x] =
+        q[2] | (q[1] << 8) | (q[0] << 16) | 0xff000000u;
+}
+
+__global__ void k_set_scalar(float* d, float v) { *d = v; }
+
+__global__ void k_frame_planes(const uint8_t* f, int w, int h, int hp, int wp, float* out) {
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
+    if (x >= wp || y >= hp) return;
+    const uint32_t v = reinterpret_cast<const uint32_t*>(f)[(long long)min(y, h - 1) * w + min(x, w - 1)];
+    const long long plane = (long long)hp * wp, o = (long long)y * wp + x;
+    out[o] = u8v((v >> 16) & 255);
+    out[plane + o] = u8v((v >> 8) & 255);
+    out[2 * plane + o] = u8v(v & 255);
+}
+
+}  // namespace
+
+// --------------------------------------------------------------------------------------------------- launchers ----
+
+cudaError_t frame_to_input(const uint8_t* frames, long long frame_bs, int w, int h, int hp, int wp, bool internal, int ih,
+                           int iw, Img4 out, int n, cudaStream_t st) {
+    const int oh = internal ? ih : hp, ow = internal ? iw : wp;
+    k_frame_to_input<<<grid2(ow, oh, n), dim3(16, 16), 0, st>>>(frames, frame_bs, w, h, hp, wp, internal ? 1 : 0, oh, ow,
+                                                               out.p, out.bs);
+    return cudaGetLastError();
+}
+
+cudaError_t input_pyramid(Img4 A, int ih, int iw, Img4 aq, Img4 i8, Img4 i16, int n, cudaStream_t st) {
+    const int qh = ih / 4, qw = iw / 4;  // floor(h * 0.25) (net/build.rs:204-205)
+    k_input_pyramid<<<grid2(qw, qh, n), 256, 0, st>>>(A.p, A.bs, ih, iw, aq.p, aq.bs, qh, qw, i8.p, i8.bs, i16.p, i16.bs);
+    return cudaGetLastError();
+}
+
+cudaError_t static_changed(const uint8_t* fa, const uint8_t* fb, const StaticArgs& s, uint8_t* changed, cudaStream_t st) {
+    k_static_changed<<<grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st>>>(fa, fb, s, changed);
+    return cudaGetLastError();
+}
+
+cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, const uint8_t* changed, const uint8_t* mask,
+                       const StaticArgs& s, uchar4* state, int16_t* age, cudaStream_t st) {
+    k_static_age<<<grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st>>>(fa, fb, changed, mask, s, state, age);
+    return cudaGetLastError();
+}
+
+cudaError_t sad_volume(const __half* a, int a_cs, const __half* b, int b_cs, long long in_bs, int h, int w, int r,
+                       __half* out, int out_cs, long long out_bs, int n, cudaStream_t st) {
+    dim3 g = grid2(w, h, n, 16, 8), blk(16, 8);
+    if (r == 3) k_sad<3><<<g, blk, 0, st>>>(a, a_cs, b, b_cs, in_bs, h, w, out, out_cs, out_bs);
+    else if (r == 2) k_sad<2><<<g, blk, 0, st>>>(a, a_cs, b, b_cs, in_bs, h, w, out, out_cs, out_bs);
+    else return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+cudaError_t upsample_flow_vis(const __half* o, int o_cs, long long o_bs, int h16, int w16, __half* fv, long long fv_bs,
+                              int h8, int w8, int n, cudaStream_t st) {
+    k_upsample_flow_vis<<<grid2(w8, h8, n, 16, 8), dim3(16, 8), 0, st>>>(o, o_cs, o_bs, h16, w16, fv, fv_bs, h8, w8);
+    return cudaGetLastError();
+}
+
+cudaError_t warp_fine(const WarpFineArgs& a, int n, cudaStream_t st) {
+    if (a.c8 > 40) return cudaErrorInvalidValue;
+    k_warp_fine<<<grid2(a.w8, a.h8, n, 16, 8), dim3(16, 8), 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t gmhs(const GmArgs& g, int n, cudaStream_t st) {
+    k_gm_fit<<<n, 1024, 0, st>>>(g);
+    k_gm_cost<<<grid2(g.wc, g.hc, n, 32, 8), dim3(32, 8), 0, st>>>(g);
+    const long long bs5 = 5LL * g.hc * g.wc, bs6 = 6LL * g.hc * g.wc;
+    // maps and tmp have different batch strides: run the box passes per batch entry when n > 1
+    for (int i = 0; i < n; i++) {
+        float* maps = g.maps + i * bs6;
+        float* tmp = g.tmp + i * bs5;
+        k_box_h<<<grid2(g.wc, g.hc, 5, 32, 8), dim3(32, 8), 0, st>>>(maps, tmp, 5, g.hc, g.wc, g.r_blk, 0);
+        k_box_v<<<grid2(g.wc, g.hc, 5, 32, 8), dim3(32, 8), 0, st>>>(tmp, maps, 5, g.hc, g.wc, g.r_blk, 0);
+        k_box_h<<<grid2(g.wc, g.hc, 3, 32, 8), dim3(32, 8), 0, st>>>(maps, tmp, 3, g.hc, g.wc, g.r_dwin, 0);
+        k_box_v<<<grid2(g.wc, g.hc, 3, 32, 8), dim3(32, 8), 0, st>>>(tmp, maps, 3, g.hc, g.wc, g.r_dwin, 0);
+    }
+    k_gm_select<<<grid2(g.w8, g.h8, n, 16, 8), dim3(16, 8), 0, st>>>(g);
+    return cudaGetLastError();
+}
+
+cudaError_t film(const FilmArgs& a, int n, cudaStream_t st) {
+    const size_t smem = (size_t)(a.hidden + 2 * a.cr) * sizeof(float);
+    k_film<<<grid2(a.w8, a.h8, n, 16, 8), dim3(16, 8), smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t mid_combine(const float* t, const __half* fv, long long fv_bs, const __half* dfilm, long long d_bs,
+                        __half* ftvt, long long ft_bs, int h8, int w8, int n, cudaStream_t st) {
+    k_mid_combine<<<grid2(w8, h8, n, 16, 8), dim3(16, 8), 0, st>>>(t, fv, fv_bs, dfilm, d_bs, ftvt, ft_bs, h8, w8);
+    return cudaGetLastError();
+}
+
+cudaError_t convex_up(const __half* wt, int wt_cs, long long wt_bs, const __half* x, long long x_bs, int h8, int w8,
+                      __half* up, long long up_bs, int n, cudaStream_t st) {
+    k_convex<<<grid2(2 * w8, 2 * h8, n, 16, 8), dim3(16, 8), 0, st>>>(wt, wt_cs, wt_bs, x, x_bs, h8, w8, up, up_bs);
+    return cudaGetLastError();
+}
+
+cudaError_t refine_input(const __half* up7, long long up_bs, Img4 aq, Img4 bq, int hq, int wq, __half* rx, long long rx_bs,
+                         int n, cudaStream_t st) {
+    k_refine_input<<<grid2(wq, hq, n, 16, 8), dim3(16, 8), 0, st>>>(up7, up_bs, aq, bq, hq, wq, rx, rx_bs);
+    return cudaGetLastError();
+}
+
+cudaError_t render(const RenderArgs& r, int n, cudaStream_t st) {
+    k_render<<<grid2(r.w, r.h, n, 32, 8), dim3(32, 8), 0, st>>>(r);
+    return cudaGetLastError();
+}
+
+cudaError_t set_scalar(float* dst, float v, cudaStream_t st) {
+    k_set_scalar<<<1, 1, 0, st>>>(dst, v);
+    return cudaGetLastError();
+}
+
+cudaError_t frame_planes(const uint8_t* f, int w, int h, int hp, int wp, float* out, cudaStream_t st) {
+    k_frame_planes<<<grid2(wp, hp, 1), dim3(16, 16), 0, st>>>(f, w, h, hp, wp, out);
+    return cudaGetLastError();
+}
+
+}  // namespace fhk

@@ -1,0 +1,131 @@
+// Launchers of the non-conv kernels of the FlyHighFG Core (stages.cu). Each cites the reference kernel(s) it replaces.
+// Layout: NHWC f16 with an explicit pixel pitch (cs); 3-channel images use cs = 4 (channel 3 is written as 0).
+// Every launcher takes a batch count n (frames or intervals) and batch strides in elements; it returns cudaError_t.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fhk {
+
+struct Img4 {  // an NHWC cs = 4 f16 image
+    __half* p;
+    long long bs;
+};
+
+// rgba8 frame -> network input A: internal mode = antialias triangle downscale of the replicate-padded frame
+// (tex_in.wgsl + interp.wgsl aa); otherwise the padded frame itself as f16. frames: [n] x (w x h x 4 bytes),
+// frame_bs bytes apart.
+cudaError_t frame_to_input(const uint8_t* frames, long long frame_bs, int w, int h, int hp, int wp, bool internal,
+                           int ih, int iw, Img4 out, int n, cudaStream_t st);
+// A -> aq (antialias x0.25), i8 = avgpool2(aq), i16 = avgpool2(i8) (interp.wgsl aa + avgpool.wgsl)
+cudaError_t input_pyramid(Img4 A, int ih, int iw, Img4 aq, Img4 i8, Img4 i16, int n, cudaStream_t st);
+
+// keep_static_age.wgsl:59-77 in two passes: `changed` = per padded pixel max |A - B| >= thr, then the state machine
+struct StaticArgs {
+    int w, h, wp, hp;
+    float thr, min_age;
+    int use_mask;
+};
+cudaError_t static_changed(const uint8_t* fa, const uint8_t* fb, const StaticArgs& s, uint8_t* changed,
+                           cudaStream_t st);
+cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, const uint8_t* changed, const uint8_t* mask,
+                       const StaticArgs& s, uchar4* state, int16_t* age, cudaStream_t st);
+
+// luma.wgsl + sad.wgsl on two 3-channel images (a view at channel offset 0): (2r+1)^2 cost channels into out (cs)
+cudaError_t sad_volume(const __half* a, int a_cs, const __half* b, int b_cs, long long in_bs, int h, int w, int r,
+                       __half* out, int out_cs, long long out_bs, int n, cudaStream_t st);
+
+// interp.wgsl bilinear x2 of the coarse head's flow (ch 0-3, x16) and visibility (ch 4-6) into fv (cs 8)
+cudaError_t upsample_flow_vis(const __half* o, int o_cs, long long o_bs, int h16, int w16, __half* fv, long long fv_bs,
+                              int h8, int w8, int n, cudaStream_t st);
+
+// warp.wgsl x4 of the fine loop: wa = warp(f8a, flow*1/8 [0:2]), wb = warp(f8b, [2:4]), ia / ib of i8a / i8b.
+// Output wbuf (cs 88): wa at 0, wb at 40, ia at 80, ib at 84, pads zero.
+struct WarpFineArgs {
+    const __half* fv;
+    long long fv_bs;
+    const __half *f8a, *f8b;
+    int f8_cs, c8;
+    long long f8_bs;
+    Img4 i8a, i8b;
+    int h8, w8;
+    __half* wbuf;
+    long long wbuf_bs;
+};
+cudaError_t warp_fine(const WarpFineArgs& a, int n, cudaStream_t st);
+
+// GMHS (gmhs.rs:155-219): IRLS affine fit (gm_fit_reduce + gm_fit_solve x4, one CTA), cost maps, box filters, select
+struct GmArgs {
+    __half* fv;  // flow in channels 0-3, rewritten in place
+    long long fv_bs;
+    int h8, w8;
+    const __half *A, *B;  // network-resolution inputs (cs 4)
+    long long ab_bs;
+    int h, w, hc, wc, r_blk, r_dwin;
+    float delta, dmin;
+    float* coef;  // [n][16]
+    float* maps;  // [n][6][hc][wc]
+    float* tmp;   // [n][5][hc][wc]
+};
+cudaError_t gmhs(const GmArgs& g, int n, cudaStream_t st);
+
+// FiLM (net/build.rs:332-359 film_mlp + film.wgsl): g = b2 + W2 relu(w1 t + b1) from the device scalar t, stored f16;
+// hm = h * (1 + g[c]) + g[c + C]
+struct FilmArgs {
+    const float* t;  // [n]
+    const float *w1, *b1, *w2, *b2;
+    int hidden, cr;
+    const __half* h;
+    int h_cs;
+    long long h_bs;
+    __half* hm;
+    int hm_cs;
+    long long hm_bs;
+    int h8, w8;
+};
+cudaError_t film(const FilmArgs& a, int n, cudaStream_t st);
+
+// the mid combine: lin = mul_t(flow) (unary.wgsl op 0), flow_t = lin + d_flow, vis_t = vis + [d, -d, 0]
+// (binary.wgsl, chcopy.wgsl) -> ft_vt (cs 8)
+cudaError_t mid_combine(const float* t, const __half* fv, long long fv_bs, const __half* dfilm, long long d_bs,
+                        __half* ftvt, long long ft_bs, int h8, int w8, int n, cudaStream_t st);
+
+// convex.wgsl: 2x convex upsample of ft_vt (7 ch, cs 8) by the 36-channel weights -> up7 (cs 8)
+cudaError_t convex_up(const __half* wt, int wt_cs, long long wt_bs, const __half* x, long long x_bs, int h8, int w8,
+                      __half* up, long long up_bs, int n, cudaStream_t st);
+
+// refine head input rx (cs 16): rwa / rwb (warp.wgsl of aq / bq by flow_tq / 4), vis_tq, f16(flow_tq * 0.05),
+// lg = grad(luma(blendmix(rwa, rwb, vis_tq))) (blendmix.wgsl, luma.wgsl grad)
+cudaError_t refine_input(const __half* up7, long long up_bs, Img4 aq, Img4 bq, int hq, int wq, __half* rx,
+                         long long rx_bs, int n, cudaStream_t st);
+
+// render.wgsl (+ the static variant, gpu/pipeline.rs:10-34) fused with keep_static.wgsl apply and tex_out.wgsl:
+// full-resolution render from the Q maps straight to rgba8, cropped to w x h
+struct RenderArgs {
+    const uint8_t *fa, *fb;  // source frames, w x h x 4
+    long long f_bs;
+    int w, h, hp, wp;        // frame and padded plane
+    const __half* up7;       // flow_tq (ch 0-3), vis_tq (ch 4-6), cs 8
+    long long up_bs;
+    const __half* rt;        // R_t, cs 4
+    long long rt_bs;
+    int hq, wq;
+    float fsx, fsy;
+    int cubic;
+    unsigned flags;          // bit 0 decisive, bit 1 still test
+    const int16_t* age;      // static age plane (padded), or null
+    long long age_bs;
+    float min_age;
+    uint8_t* out;            // w x h x 4
+    long long out_bs;
+};
+cudaError_t render(const RenderArgs& r, int n, cudaStream_t st);
+
+// a device scalar (the phase t of the mid stage) written on the stream
+cudaError_t set_scalar(float* dst, float v, cudaStream_t st);
+
+// tex_in.wgsl: rgba8 -> padded f16 planes are never materialised; this reads one for tests: [3][hp][wp] f32 BGR
+cudaError_t frame_planes(const uint8_t* f, int w, int h, int hp, int wp, float* out, cudaStream_t st);
+
+}  // namespace fhk

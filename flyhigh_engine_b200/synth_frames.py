@@ -1,0 +1,115 @@
+"""Seeded synthetic RGBA8 frames with the shapes and statistics of the benchmark configurations.
+
+No public image or video set is used: the reference's quality sets are not distributed with it. These generators stand
+in for them:
+  - texture(): a sum of 8 random 2-D sinusoids with periods 8..128 px, plus uniform noise of +-10, clamped to 0..255;
+  - pair_c0(): config 0, frame b = frame a under an integer global pan in [-12, 12]^2 plus 3 rectangles of 20..80 px
+    that move independently by up to 24 px;
+  - sequence_c2(): config 2, a moving sequence whose pan velocity random-walks by +-2 px per frame, with 5 moving
+    rectangles and a static 300 x 60 high-contrast HUD at the bottom-left.
+Every frame is (h, w, 4) uint8 with alpha 255.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def texture(w: int, h: int, rng: np.random.Generator, margin: int = 0) -> np.ndarray:
+    """An RGB float texture of (h + 2 margin) x (w + 2 margin), values 0..255 before noise."""
+    H, W = h + 2 * margin, w + 2 * margin
+    y = np.arange(H, dtype=np.float32)[:, None]
+    x = np.arange(W, dtype=np.float32)[None, :]
+    img = np.zeros((H, W, 3), np.float32)
+    for _ in range(8):
+        period = rng.uniform(8.0, 128.0)
+        ang = rng.uniform(0.0, np.pi)
+        phase = rng.uniform(0.0, 2 * np.pi)
+        amp = rng.uniform(10.0, 30.0, size=3).astype(np.float32)
+        kx, ky = np.cos(ang) * 2 * np.pi / period, np.sin(ang) * 2 * np.pi / period
+        wave = np.sin(kx * x + ky * y + phase).astype(np.float32)
+        img += wave[..., None] * amp
+    return img + 128.0
+
+
+def _finish(rgb: np.ndarray, rng: np.random.Generator) -> np.ndarray:
+    noisy = rgb + rng.uniform(-10.0, 10.0, size=rgb.shape).astype(np.float32)
+    out = np.empty(rgb.shape[:2] + (4,), np.uint8)
+    out[..., :3] = np.clip(noisy, 0, 255).astype(np.uint8)
+    out[..., 3] = 255
+    return out
+
+
+def _rects(n, w, h, rng):
+    rs = []
+    for _ in range(n):
+        rw, rh = int(rng.integers(20, 81)), int(rng.integers(20, 81))
+        rs.append(dict(x=int(rng.integers(0, max(1, w - rw))), y=int(rng.integers(0, max(1, h - rh))), w=rw, h=rh,
+                       color=rng.integers(0, 256, size=3).astype(np.float32)))
+    return rs
+
+
+def _paint(img, r, dx=0, dy=0):
+    H, W = img.shape[:2]
+    x0, y0 = r["x"] + dx, r["y"] + dy
+    xa, ya, xb, yb = max(0, x0), max(0, y0), min(W, x0 + r["w"]), min(H, y0 + r["h"])
+    if xa < xb and ya < yb:
+        img[ya:yb, xa:xb, :] = r["color"]
+
+
+def pair_c0(w: int = 640, h: int = 360, seed: int = 0):
+    """Config 0: (frame a, frame b, (dx, dy))."""
+    rng = np.random.default_rng(seed)
+    m = 12
+    base = texture(w, h, rng, margin=m)
+    dx, dy = (int(v) for v in rng.integers(-12, 13, size=2))
+    a = base[m:m + h, m:m + w].copy()
+    b = base[m - dy:m - dy + h, m - dx:m - dx + w].copy()
+    for r in _rects(3, w, h, rng):
+        _paint(a, r)
+        _paint(b, r, int(rng.integers(-24, 25)), int(rng.integers(-24, 25)))
+    return _finish(a, rng), _finish(b, rng), (dx, dy)
+
+
+def sequence_c2(n: int = 120, w: int = 1920, h: int = 1080, seed: int = 0, hud: bool = True):
+    """Config 2: n frames. The pan velocity random-walks by +-2 px/frame (clamped to +-24), 5 rectangles move, a
+    300 x 60 HUD stays fixed at the bottom-left."""
+    rng = np.random.default_rng(seed)
+    m = 24 * n // 4 + 64
+    m = min(m, 1024)
+    base = texture(w, h, rng, margin=m)
+    rects = _rects(5, w, h, rng)
+    vel = [rng.integers(-3, 4, size=2).astype(np.int64) for _ in rects]
+    hud_img = np.zeros((60, 300, 3), np.float32)
+    hud_img[:, :] = 16.0
+    hud_img[10:50, 10:290] = 240.0
+    hud_img[20:40, 40:260:20] = 16.0
+    px, py, vx, vy = 0, 0, 0, 0
+    frames = []
+    for i in range(n):
+        vx = int(np.clip(vx + rng.integers(-2, 3), -24, 24))
+        vy = int(np.clip(vy + rng.integers(-2, 3), -24, 24))
+        px = int(np.clip(px + vx, -m, m))
+        py = int(np.clip(py + vy, -m, m))
+        img = base[m + py:m + py + h, m + px:m + px + w].copy()
+        for r, v in zip(rects, vel):
+            r["x"] += int(v[0])
+            r["y"] += int(v[1])
+            _paint(img, r)
+        if hud:
+            img[h - 60 - 20:h - 20, 20:320] = hud_img
+        frames.append(_finish(img, rng))
+    return frames
+
+
+def sinusoid_pair(w: int, h: int, dx: float):
+    """The reference's known-answer pattern (tests/core.rs:67-99): a soft pattern shifted dx px to the right."""
+    v = np.zeros((h, w, 4), np.uint8)
+    y = np.arange(h, dtype=np.float32)[:, None]
+    x = np.arange(w, dtype=np.float32)[None, :]
+    u = (x - np.float32(dx)) * np.float32(0.07)
+    ww = y * np.float32(0.05)
+    v[..., 0] = (128 + 100 * np.sin(u)).astype(np.uint8)
+    v[..., 1] = (128 + 100 * np.cos(u * np.float32(0.7) + ww)).astype(np.uint8)
+    v[..., 2] = (128 + 90 * np.sin(u + ww)).astype(np.uint8)
+    v[..., 3] = 255
+    return v

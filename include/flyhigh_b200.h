@@ -1,0 +1,48 @@
+/* FlyHigh B200: additions to the session ABI of flyhigh.h that the reference does not have.
+ *
+ * They serve hosts that keep frames on the GPU and the parity / benchmark harness of this package. None of them
+ * changes what fh_session_pair / fh_session_mid compute.
+ */
+#ifndef FLYHIGH_B200_H
+#define FLYHIGH_B200_H
+#include <stddef.h>
+#include <stdint.h>
+#include "flyhigh.h"
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The CUDA stream (cudaStream_t) every call of this session is ordered on. 0 on success, -1 on error. */
+int fh_session_cuda_stream(const FhSession* session, void** stream);
+
+/* The device buffer (width * height * 4 bytes, RGBA8) behind an input or output slot, for hosts whose frames already
+ * live in device memory (write it on the session's stream, or synchronise first). 0 on success, -1 on error. */
+int fh_session_slot_device_ptr(const FhSession* session, uint32_t slot, int output, void** ptr);
+
+/* A frame already in device memory into an input slot (a device-to-device copy on the session's stream). */
+int fh_session_write_rgba_device(const FhSession* session, uint32_t slot, const void* device_rgba, size_t len);
+
+/* A named tensor of the last pair / mid, read back as f32 [c][h][w] (the reference's planar order, view applied).
+ * Names follow the graph (models/graph.json): A, B, aq, bq, i8a, i8b, i16a, i16b, f8a, f8b, f16a, f16b, cv, ch1, ch2,
+ * ch3r, hc, o, flow, vis, wa, wb, ia, ib, fcv, fr1, fr2, fr3, hm, fh1, fh2, dfilm, ft_vt, up7, rx, rq1, rq2, rq3, R_t,
+ * and age (the static-protection age plane). Waits for the GPU. Returns c * h * w (dims filled with c, h, w); -1 for
+ * an unknown name or an error, -2 when cap is too small. out may be NULL to query the size. */
+long fh_session_debug_tensor(const FhSession* session, const char* name, float* out, size_t cap, int* dims);
+
+/* The structural fingerprint of a model's graph.json (FNV-1a of its canonical op list). Sessions are built only for
+ * the FlyHighFG v1 graph; this lets a host check a model directory before creating one. -1 on a null model. */
+long fh_model_fingerprint(const FhModel* model);
+
+/* Every size and parameter word a session of these options derives, without a device (validation included):
+ * iv[22] = hp, wp, ihp, iwp, internal, NH, NW, qh, qw, h8, w8, h16, w16, hc, wc, r_blk, r_dwin, k, repair, cubic,
+ *          protects, render flags (bit 0 decisive, bit 1 still test);
+ * fv[6]  = fsx, fsy, gmhs dmin, gmhs delta, protecting age, static threshold. 0, or -1 with fh_last_error. */
+int fh_session_plan_params(const FhModel* model, const FhSessionOptions* options, int* iv, float* fv);
+
+/* Kernel launches of one pair and of one mid (the nodes of their CUDA graphs). 0 on success. */
+int fh_session_launch_counts(const FhSession* session, int* pair_kernels, int* mid_kernels, int* frame_kernels);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,68 @@
+/* FlyHigh B200: the kernel-level C ABI under the session layer.
+ *
+ * The reference's device layer is wgpu + WGSL (crates/flyhigh-engine/src/gpu/, shaders/ directory): every kernel is a
+ * compute pipeline driven by a uniform struct (crates/flyhigh-engine/src/ops/params.rs). This header is its B200
+ * replacement: one launch function per kernel family taking a POD params struct, on a caller-given CUDA stream, plus
+ * the weight packing the conv family needs. A host that keeps its own planner (the reference's Rust
+ * net/build.rs) binds these; this project's own planner (flyhigh.h's session layer) calls them too.
+ *
+ * Tensors are NHWC f16 views: a pointer at the view's first channel, a pixel pitch `cs` in elements and a batch stride
+ * `bs` in elements. Return values are cudaError_t codes (0 = success).
+ */
+#ifndef FLYHIGH_KERNELS_H
+#define FLYHIGH_KERNELS_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+#include <cuda_fp16.h>
+typedef __half fh_half;
+extern "C" {
+#else
+typedef uint16_t fh_half;
+#endif
+
+#define FH_CONV_MAX_SRC 6
+
+/* one input source of a conv: the channels it contributes land at packed channel `slot` (a multiple of 8) */
+typedef struct FhConvSrc {
+    const fh_half* p;   /* first channel of the source view; 16-byte aligned (8 when cs == 4) */
+    long long bs;       /* batch stride, elements */
+    int cs;             /* pixel pitch, elements: a multiple of 8, or 4 for a 3-channel image */
+    int nc;             /* channels read */
+    float scale;        /* 1 = plain; else a scaled view: each value becomes f16(x * scale) (chcopy.wgsl:19-22) */
+    int slot;           /* first packed channel */
+} FhConvSrc;
+
+/* 3x3 conv, pad 1: conv_fused.wgsl:20-75 semantics with the fused epilogue of conv_tiled.wgsl:57-70 */
+typedef struct FhConvParams {
+    FhConvSrc src[FH_CONV_MAX_SRC];
+    int nsrc;
+    int h, w;              /* input size */
+    int ho, wo;            /* output size: (h - 1) / stride + 1 */
+    int cp;                /* packed input channels per pixel, a multiple of 16 */
+    int cout;              /* 1..96 */
+    const uint16_t* wpack; /* fhk_conv_pack_weights output, on the device */
+    const float* bias;     /* [cout] */
+    const float* slope;    /* [cout] PReLU slopes, or NULL (identity: the graph's conv2d) */
+    int epi;               /* 0 = bias + PReLU; 1 = then affine_out (2 * sigmoid - 1, unary.wgsl:17) */
+    fh_half* out;
+    int out_cs;
+    long long out_bs;
+    const fh_half* res;    /* residual view added after the f16 activation, or NULL */
+    int res_cs;
+    long long res_bs;
+    int n;                 /* batch */
+} FhConvParams;
+
+/* Replaces the conv family of the reference (ops/conv/kernels.rs:100-279: conv_tc / conv_direct / conv_tiled*,
+ * conv_fused*.wgsl, splitk_reduce.wgsl). stride 1 or 2; warps 2 or 4 (output tile (2 * warps) x 16 pixels). */
+int fhk_conv3x3(const FhConvParams* p, int stride, int warps, void* stream);
+/* Replaces buildb / buildb_tap (ops/conv/kernels.rs:66-78, :194-207): torch [cout][cin][3][3] f16 bits -> the
+ * kernel's B-fragment order; map[pc] = model input channel of packed channel pc, or -1 (weight 0). */
+int fhk_conv_pack_weights(const uint16_t* w, int cin, int cout, const int* map, int cp, uint16_t* out);
+size_t fhk_conv_packed_elems(int cout, int cp);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,299 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle on the same seeded inputs and weights.
+
+Tolerances (the north star's): every layer within 1e-2 relative L2 of the oracle's tensor; final rgba8 frames with
+max |diff| <= 2 levels and PSNR >= 50 dB.
+"""
+import ctypes
+from ctypes import POINTER, Structure, c_float, c_int, c_longlong, c_void_p
+
+import numpy as np
+import pytest
+
+from tests.parity import FRAME_MAX_ABS, FRAME_PSNR_DB, LAYER_REL_L2, frame_stats, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+class ConvSrc(Structure):
+    _fields_ = [("p", c_void_p), ("bs", c_longlong), ("cs", c_int), ("nc", c_int), ("scale", c_float), ("slot", c_int)]
+
+
+class ConvParams(Structure):
+    _fields_ = [("src", ConvSrc * 6), ("nsrc", c_int), ("h", c_int), ("w", c_int), ("ho", c_int), ("wo", c_int),
+                ("cp", c_int), ("cout", c_int), ("wpack", c_void_p), ("bias", c_void_p), ("slope", c_void_p),
+                ("epi", c_int), ("out", c_void_p), ("out_cs", c_int), ("out_bs", c_longlong), ("res", c_void_p),
+                ("res_cs", c_int), ("res_bs", c_longlong), ("n", c_int)]
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+def _up8(c):
+    return (c + 7) // 8 * 8
+
+
+def run_conv(torch, x_chw, w, bias, slope, stride, resid_chw=None, warps=2):
+    """One conv through fhk_conv3x3 on NHWC device buffers; returns CHW f16."""
+    import flyhigh_engine_b200 as fh
+    L = fh.lib()
+    cin, h, wd = x_chw.shape
+    cout = w.shape[0]
+    cs = 4 if cin <= 4 else _up8(cin)
+    ho, wo = (h - 1) // stride + 1, (wd - 1) // stride + 1
+    x = torch.zeros((h, wd, cs), dtype=torch.float16)
+    x[:, :, :cin] = torch.from_numpy(np.ascontiguousarray(x_chw.transpose(1, 2, 0)))
+    x = x.cuda()
+    cp = (_up8(cin) + 15) // 16 * 16
+    cmap = np.full(cp, -1, np.int32)
+    cmap[:cin] = np.arange(cin)
+    n_pack = L.fhk_conv_packed_elems(cout, cp)
+    packed = np.zeros(n_pack, np.uint16)
+    wbits = np.ascontiguousarray(w.astype(np.float16)).view(np.uint16)
+    assert L.fhk_conv_pack_weights(wbits.ctypes.data, cin, cout, cmap.ctypes.data, cp, packed.ctypes.data) == 0
+    wp = torch.from_numpy(packed.view(np.int16)).cuda()
+    b = torch.from_numpy(bias.astype(np.float32)).cuda()
+    s = torch.from_numpy(slope.astype(np.float32)).cuda() if slope is not None else None
+    ocs = _up8(cout)
+    out = torch.zeros((ho, wo, ocs), dtype=torch.float16, device="cuda")
+    r = None
+    if resid_chw is not None:
+        r = torch.zeros((ho, wo, ocs), dtype=torch.float16)
+        r[:, :, :cout] = torch.from_numpy(np.ascontiguousarray(resid_chw.transpose(1, 2, 0)))
+        r = r.cuda()
+    p = ConvParams()
+    p.src[0] = ConvSrc(x.data_ptr(), 0, cs, cin, 1.0, 0)
+    p.nsrc, p.h, p.w, p.ho, p.wo, p.cp, p.cout = 1, h, wd, ho, wo, cp, cout
+    p.wpack, p.bias, p.slope = wp.data_ptr(), b.data_ptr(), (s.data_ptr() if s is not None else None)
+    p.epi, p.out, p.out_cs, p.out_bs = 0, out.data_ptr(), ocs, 0
+    p.res, p.res_cs, p.res_bs, p.n = (r.data_ptr() if r is not None else None), ocs, 0, 1
+    rc = L.fhk_conv3x3(ctypes.byref(p), stride, warps, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, rc
+    torch.cuda.synchronize()
+    return out[:, :, :cout].permute(2, 0, 1).cpu().numpy()
+
+
+# config 1: fp16 activations ~N(0,1), weights ~N(0, 1/sqrt(9 cin)), bias + leaky ReLU(0.1), with and
+# without a residual; the model's own shapes at their network sizes
+CONV_CASES = [
+    # (h, w, cin, cout, stride, residual)
+    (270, 480, 16, 16, 1, False),
+    (270, 480, 32, 64, 2, False),
+    (270, 480, 64, 64, 1, True),
+    (270, 480, 48, 32, 2, True),
+    (540, 960, 16, 32, 1, False),
+    (120, 216, 3, 36, 2, False),
+    (60, 108, 36, 36, 1, True),
+    (60, 108, 36, 72, 2, False),
+    (30, 54, 72, 72, 1, True),
+    (30, 54, 279, 96, 1, False),
+    (30, 54, 96, 12, 1, False),
+    (60, 108, 155, 48, 1, False),
+    (60, 108, 48, 7, 1, True),
+    (60, 108, 48, 36, 1, False),
+    (120, 216, 14, 24, 1, False),
+    (120, 216, 24, 3, 1, False),
+    (37, 29, 24, 24, 1, True),  # ragged: partial tiles in both directions
+]
+
+
+@pytest.mark.parametrize("h,w,cin,cout,stride,res", CONV_CASES)
+@pytest.mark.parametrize("warps", [2, 4])
+def test_conv_matches_oracle(torch_cuda, h, w, cin, cout, stride, res, warps):
+    from oracle import oracle
+    rng = np.random.default_rng(h * 1000 + cin * 10 + cout + stride)
+    x = rng.standard_normal((cin, h, w)).astype(np.float16)
+    wt = (rng.standard_normal((cout, cin, 3, 3)) / np.sqrt(9 * cin)).astype(np.float16).astype(np.float32)
+    bias = rng.standard_normal(cout).astype(np.float16).astype(np.float32) * 0.1
+    slope = np.full(cout, 0.1, np.float32)
+    ho, wo = (h - 1) // stride + 1, (w - 1) // stride + 1
+    resid = rng.standard_normal((cout, ho, wo)).astype(np.float16) if res else None
+    ref = oracle.conv(x, wt, bias, slope, stride, resid).astype(np.float32)
+    got = run_conv(torch_cuda, x, wt, bias, slope, stride, resid, warps).astype(np.float32)
+    assert got.shape == ref.shape
+    assert rel_l2(got, ref) < 2e-3
+    # f32 accumulation order differs from the oracle's: a few f16 ulps at most
+    assert np.abs(got - ref).max() <= 4e-3 * max(1.0, np.abs(ref).max())
+
+
+def _session_pair(model_dir, w, h, frames, t=0.5, **opts):
+    """(gpu session, oracle session) after the same pairs; frames is a list of (a, b)."""
+    import flyhigh_engine_b200 as fh
+    from oracle.oracle import OracleModel, OracleSession
+    eng = fh.Engine()
+    model = fh.Model(model_dir)
+    s = fh.Session(eng, model, w, h, **opts)
+    a, b, out = s.add_input(), s.add_input(), s.add_output()
+    om = OracleModel(model_dir)
+    okw = dict(k=opts.get("k", 1), repair=opts.get("repair", 1),
+               cubic={"model": -1, "bilinear": 0, "bicubic": 1}[opts.get("render", "model")],
+               keep_static=opts.get("static_protection", True) is not False,
+               protection_mask=opts.get("protection_mask", False))
+    if isinstance(opts.get("internal"), tuple):
+        okw["internal"] = opts["internal"]
+    o = OracleSession(om, w, h, **okw)
+    results = []
+    for fa, fb in frames:
+        s.write(a, fa)
+        s.write(b, fb)
+        s.pair(a, b)
+        s.mid(t, out)
+        got = np.frombuffer(s.read(out), np.uint8)
+        o.pair(fa, fb)
+        ref = o.mid(t)
+        results.append((got, ref))
+    return s, o, results, (eng, model, om)
+
+
+PAIR_LAYERS = ["A", "B", "aq", "bq", "i8a", "i8b", "i16a", "i16b", "f8a", "f8b", "f16a", "f16b", "cv", "ch1", "ch2",
+               "ch3r", "hc", "o", "wa", "wb", "ia", "ib", "fcv", "fr1", "fr2", "fr3", "flow", "vis"]
+MID_LAYERS = ["hm", "fh1", "fh2", "dfilm", "ft_vt", "up7", "rx", "rq1", "rq2", "rq3", "R_t"]
+
+
+def _check_layers(s, o, names, stage, tol=LAYER_REL_L2):
+    worst = {}
+    for n in names:
+        got = s.tensor(n)
+        ref = o.tensor(n, stage)
+        assert got.shape == ref.shape, (n, got.shape, ref.shape)
+        worst[n] = rel_l2(got, ref)
+    bad = {k: v for k, v in worst.items() if v > tol}
+    assert not bad, f"layers above {tol}: {bad} (all: {worst})"
+    return worst
+
+
+def test_session_c0_layers_and_frame(synth_model_dir):
+    """Config 0: 640 x 360 (internal = frame), pair(a, b) + mid(0.5); every layer and the final frame."""
+    from flyhigh_engine_b200 import synth_frames
+    fa, fb, _ = synth_frames.pair_c0(640, 360, seed=0)
+    s, o, res, _keep = _session_pair(synth_model_dir, 640, 360, [(fa, fb)])
+    _check_layers(s, o, PAIR_LAYERS, 0)
+    _check_layers(s, o, MID_LAYERS, 1)
+    got, ref = res[0]
+    mx, p = frame_stats(got, ref)
+    assert mx <= FRAME_MAX_ABS and p >= FRAME_PSNR_DB, (mx, p)
+
+
+def test_session_1080p_frame(synth_model_dir):
+    """Config 2's size: 1920 x 1080 (internal 856 x 480 -> 864 x 480), one interval."""
+    from flyhigh_engine_b200 import synth_frames
+    frames = synth_frames.sequence_c2(3, 1920, 1080, seed=1)
+    s, o, res, _keep = _session_pair(synth_model_dir, 1920, 1080, [(frames[0], frames[1]), (frames[1], frames[2])])
+    _check_layers(s, o, ["A", "aq", "f16a", "ch1", "o", "fr3", "flow", "vis"], 0)
+    _check_layers(s, o, MID_LAYERS, 1)
+    for got, ref in res:
+        mx, p = frame_stats(got, ref)
+        assert mx <= FRAME_MAX_ABS and p >= FRAME_PSNR_DB, (mx, p)
+    # the static-protection age is integer state: exact
+    assert np.array_equal(s.tensor("age"), o.tensor("age"))
+
+
+def test_static_protection_sequence(synth_model_dir):
+    """Static protection over 12 consecutive pairs of a sequence with a fixed HUD: the age state machine matches
+    exactly after every pair, and every generated frame stays within tolerance."""
+    from flyhigh_engine_b200 import synth_frames
+    frames = synth_frames.sequence_c2(13, 640, 360, seed=2)
+    import flyhigh_engine_b200 as fh
+    from oracle.oracle import OracleModel, OracleSession
+    eng = fh.Engine()
+    model = fh.Model(synth_model_dir)
+    s = fh.Session(eng, model, 640, 360)
+    slots = [s.add_input(), s.add_input()]
+    out = s.add_output()
+    o = OracleSession(OracleModel(synth_model_dir), 640, 360)
+    s.write(slots[0], frames[0])
+    protected = 0
+    for i in range(1, len(frames)):
+        a, b = slots[(i - 1) % 2], slots[i % 2]
+        s.write(b, frames[i])
+        s.pair(a, b)
+        s.mid(0.5, out)
+        got = np.frombuffer(s.read(out), np.uint8)
+        o.pair(frames[i - 1], frames[i])
+        ref = o.mid(0.5)
+        age = s.tensor("age")
+        assert np.array_equal(age, o.tensor("age")), f"age differs after pair {i}"
+        protected = int((age >= 8).sum())
+        mx, p = frame_stats(got, ref)
+        assert mx <= FRAME_MAX_ABS and p >= FRAME_PSNR_DB, (i, mx, p)
+    assert protected > 1000, "the HUD should be protected after 8+ pairs"
+
+
+@pytest.mark.parametrize("opts", [
+    dict(k=2), dict(k=3, repair=0), dict(repair=2), dict(render="bilinear"), dict(static_protection=False),
+    dict(internal=(320, 192)),
+])
+def test_session_options(synth_model_dir, opts):
+    from flyhigh_engine_b200 import synth_frames
+    fa, fb, _ = synth_frames.pair_c0(640, 360, seed=3)
+    s, o, res, _keep = _session_pair(synth_model_dir, 640, 360, [(fa, fb)], t=0.25, **opts)
+    _check_layers(s, o, ["flow", "vis", "fr3"], 0)
+    _check_layers(s, o, ["up7", "R_t"], 1)
+    got, ref = res[0]
+    mx, p = frame_stats(got, ref)
+    assert mx <= FRAME_MAX_ABS and p >= FRAME_PSNR_DB, (opts, mx, p)
+
+
+def test_odd_size_and_mask(synth_model_dir):
+    """A frame size that is not a multiple of 32 (replicate padding) and the host's protection mask."""
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200 import synth_frames
+    from oracle.oracle import OracleModel, OracleSession
+    w, h = 333, 197
+    fa, fb, _ = synth_frames.pair_c0(w, h, seed=4)
+    mask = np.zeros((h, w), np.uint8)
+    mask[150:180, 20:120] = 1
+    eng = fh.Engine()
+    model = fh.Model(synth_model_dir)
+    s = fh.Session(eng, model, w, h, protection_mask=True)
+    a, b, out = s.add_input(), s.add_input(), s.add_output()
+    s.write_mask(mask)
+    s.write(a, fa)
+    s.write(b, fb)
+    s.generate(a, b, 0.5, out)
+    got = np.frombuffer(s.read(out), np.uint8)
+    o = OracleSession(OracleModel(synth_model_dir), w, h, protection_mask=True)
+    o.write_mask(mask)
+    o.pair(fa, fb)
+    ref = o.mid(0.5)
+    assert np.array_equal(s.tensor("age"), o.tensor("age"))
+    mx, p = frame_stats(got, ref)
+    assert mx <= FRAME_MAX_ABS and p >= FRAME_PSNR_DB, (mx, p)
+    # masked pixels take the sources' mean (keep_static apply at age 255)
+    g = got.reshape(h, w, 4)[155:175, 30:110, :3].astype(np.int32)
+    src = (fa.astype(np.int32) + fb.astype(np.int32))[155:175, 30:110, :3] / 2.0
+    assert np.abs(g - src).max() <= 1.0
+
+
+def test_errors_and_reports(synth_model_dir):
+    """The C ABI's error behaviour (core.rs): -1 / NULL with fh_last_error, never a crash."""
+    import flyhigh_engine_b200 as fh
+    eng = fh.Engine()
+    info = eng.info()
+    assert info["class"] == "tc-f16" and info["sm"].startswith("10.")
+    model = fh.Model(synth_model_dir)
+    s = fh.Session(eng, model, 256, 192)
+    with pytest.raises(fh.FlyHighError, match="pair two input slots first"):
+        s.add_output()
+        s.mid(0.5, 0)
+    with pytest.raises(fh.FlyHighError, match="bad input slot"):
+        s.pair(0, 1)
+    a, b = s.add_input(), s.add_input()
+    with pytest.raises(fh.FlyHighError, match="bytes"):
+        s.write(a, b"\x00" * 10)
+    with pytest.raises(fh.FlyHighError, match="bad output slot"):
+        s.pair(a, b)
+        s.mid(0.5, 7)
+    s.warm_up()
+    r = s.report()
+    assert r["pair_steps"] > 10 and r["mid_steps"] > 5 and r["inputs"] == 2 and r["outputs"] == 1
+    assert s.pair_timed(a, b) > 0 and s.mid_timed(0.5, 0) > 0
+    with pytest.raises(fh.FlyHighError, match="k"):
+        fh.Session(eng, model, 256, 192, k=4)
+    with pytest.raises(fh.FlyHighError, match="64x64"):
+        fh.Session(eng, model, 32, 32)
+    assert eng.report()["tensor_bytes"] > 0
