@@ -1,0 +1,315 @@
+"""Benchmark of the FlyHighFG Core hot path (Session::pair + Session::mid) on B200: 1080p generated frames/s.
+
+Workload: a seeded 120-frame 1920 x 1080 sequence (pan random walk, 5 moving rectangles, a
+static HUD), one pair() + one mid(0.5) per interval = 119 generated frames per step; default session options
+(k 1, repair 1, bicubic render, static protection on, still test on), weights seeded N(0, 0.05) f16 of the FlyHighFG
+shapes. One step = the whole sequence.
+
+  value : frames/s with the 120 source frames resident in HBM when the timed region starts (each interval copies its
+          new frame device-to-device into a session slot, then pair + mid); CUDA events on the session's stream.
+  e2e   : the same through the reference-facing C ABI with host buffers: fh_session_write_rgba from pinned host memory,
+          fh_session_pair, fh_session_mid, fh_session_read_rgba into pinned host memory, every interval.
+The sequence (1 GB) is larger than L2 (126 MB), so no explicit flush is needed between timed steps.
+
+Multi-GPU (torchrun, one process per GPU): every rank runs its own seeded sequence (weak scaling, no collective on
+the data path); the step time is the max over ranks. --impl reference times the reference algorithm's CPU
+restatement (oracle/; the reference itself cannot be built or run here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "1080p generated frames/s (1 GPU and 1/2/4/8 box); device us per pair()/mid()"
+W, H, NFRAMES = 1920, 1080, 120
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--frames", type=int, default=NFRAMES)
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--cpu-sample", type=int, default=3, help="intervals of the CPU baseline sample")
+    return p.parse_args()
+
+
+class Clocks:
+    """nvidia-smi samples of the SM clock and throttle reasons during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        def run():
+            q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap")
+            while not self._stop.is_set():
+                try:
+                    out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                         timeout=5).stdout.strip()
+                    if out:
+                        self.samples.append([x.strip() for x in out.split(",")])
+                except Exception:
+                    pass
+                self._stop.wait(0.2)
+
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [v for v in (num(s[0]) for s in self.samples) if v is not None]
+        mx = [v for v in (num(s[1]) for s in self.samples) if v is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 3 + i and s[3 + i].strip() == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def cpu_baseline(model_dir, frames, n_intervals):
+    """The oracle (the reference algorithm restated in C++, OpenMP over all host cores) on the first n intervals."""
+    from oracle.oracle import OracleModel, OracleSession
+    om = OracleModel(model_dir)
+    o = OracleSession(om, W, H)
+    o.pair(frames[0], frames[1])  # warm the caches once
+    o.mid(0.5)
+    t0 = time.perf_counter()
+    for i in range(1, n_intervals + 1):
+        o.pair(frames[i - 1], frames[i])
+        o.mid(0.5)
+    dt = time.perf_counter() - t0
+    return n_intervals / dt, dt
+
+
+def run_reference(args):
+    ws, rank, _ = dist()
+    if rank != 0:
+        return 0
+    from flyhigh_engine_b200 import synth_frames, synth_model
+    model_dir = synth_model.default_dir(0)
+    frames = synth_frames.sequence_c2(max(args.cpu_sample + 1, 4), W, H, seed=0)
+    cores = os.cpu_count()
+    times = []
+    for _ in range(args.warmup):
+        cpu_baseline(model_dir, frames, 1)
+    for _ in range(args.steps):
+        _fps, dt = cpu_baseline(model_dir, frames, args.cpu_sample)
+        times.append(dt / args.cpu_sample)
+    ms = float(np.max(times) * 1000.0)
+    fps = 1000.0 / ms
+    line = {"impl": "reference", "metric": METRIC, "value": fps, "unit": "generated frames/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms * args.cpu_sample,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded config-2 frames, seeded N(0,0.05) weights)",
+            "config": {"workload": "FlyHighFG Core 1080p pair + mid(0.5) per interval (config 2)",
+                       "sample": f"{args.cpu_sample} intervals per step"},
+            "cpu_baseline": {"value": fps, "unit": "generated frames/s", "cores": cores, "kind": "port",
+                             "sample": f"{args.cpu_sample} consecutive 1080p intervals (pair + mid) per step; the "
+                                       "reference (Rust + wgpu/WGSL) cannot be built or run here: no Rust toolchain, "
+                                       "no graphics stack"},
+            "e2e": {"value": fps, "unit": "generated frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    ws, rank, local = dist()
+    import torch
+    torch.cuda.set_device(local)
+    pg = None
+    if ws > 1:
+        import datetime
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        pg = tdist
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200 import synth_frames, synth_model
+
+    model_dir = synth_model.default_dir(0)
+    n = args.frames
+    frames = synth_frames.sequence_c2(n, W, H, seed=100 + rank)
+    fbytes = W * H * 4
+    dev_frames = torch.from_numpy(np.stack(frames)).to(f"cuda:{local}")  # [n][h][w][4], resident in HBM
+    engine = fh.Engine(adapter=f"#{local}")
+    model = fh.Model(model_dir)
+    s = fh.Session(engine, model, W, H)
+    slots = [s.add_input(), s.add_input()]
+    out = s.add_output()
+    stream = torch.cuda.ExternalStream(s.cuda_stream(), device=f"cuda:{local}")
+    base = dev_frames.data_ptr()
+
+    def step_device():
+        s.write_device(slots[0], base, fbytes)
+        for i in range(1, n):
+            a, b = slots[(i - 1) % 2], slots[i % 2]
+            s.write_device(b, base + i * fbytes, fbytes)
+            s.pair(a, b)
+            s.mid(0.5, out)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    def timed(fn, k):
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(k):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / k
+        barrier()
+        if pg is not None:
+            t = torch.tensor([ms], device=f"cuda:{local}")
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    warm = max(args.warmup, 3)
+    for _ in range(warm):
+        step_device()
+    counts = s.launch_counts()
+    with Clocks(local) as clk:
+        ms = timed(step_device, args.steps)
+    gen_per_rank = n - 1
+    value = gen_per_rank * ws / (ms / 1000.0)
+
+    # device ms per pair() and per mid() (the reference's pair_timed / mid_timed: min of 3 / 5 runs)
+    pair_ms = s.pair_timed(slots[0], slots[1])
+    mid_ms = s.mid_timed(0.5, out)
+
+    # end to end through the C ABI with host buffers
+    e2e = None
+    if not args.no_e2e:
+        pinned = torch.empty((n, H, W, 4), dtype=torch.uint8).pin_memory()
+        pinned.copy_(torch.from_numpy(np.stack(frames)))
+        pin_np = pinned.numpy()
+        outbuf = torch.empty((H, W, 4), dtype=torch.uint8).pin_memory()
+        out_np = outbuf.numpy()
+
+        def step_host():
+            s.write(slots[0], pin_np[0])
+            for i in range(1, n):
+                a, b = slots[(i - 1) % 2], slots[i % 2]
+                s.write(b, pin_np[i])
+                s.pair(a, b)
+                s.mid(0.5, out)
+                s.read_into(out, out_np)
+
+        step_host()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step_host()
+        torch.cuda.synchronize()
+        e2e_ms = (time.perf_counter() - t0) * 1000.0 / args.steps
+        if pg is not None:
+            t = torch.tensor([e2e_ms], device=f"cuda:{local}")
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e = {"value": gen_per_rank * ws / (e2e_ms / 1000.0), "unit": "generated frames/s",
+               "h2d_bytes_per_step": n * fbytes, "d2h_bytes_per_step": gen_per_rank * fbytes,
+               "ms_per_step": e2e_ms}
+
+    roof = roofline_block(s, ms, gen_per_rank)
+    cpu = None
+    if rank == 0 and ws == 1:
+        fps_cpu, dt = cpu_baseline(model_dir, frames, args.cpu_sample)
+        cpu = {"value": fps_cpu, "unit": "generated frames/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{args.cpu_sample} consecutive intervals of the same 1080p sequence (pair + mid(0.5)), "
+                         f"{dt:.1f} s on the host cores"}
+    if rank == 0:
+        per_interval_launches = counts["frame"] + counts["pair"] + counts["mid"] + 1
+        line = {"metric": METRIC, "value": value, "unit": "generated frames/s", "n_gpus": ws, "steps": args.steps,
+                "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16",
+                "data": "synthetic (seeded config-2 frames, seeded N(0,0.05) f16 weights of the FlyHighFG shapes)",
+                "config": {"workload": "FlyHighFG Core 1920x1080, 120-frame sequence, pair + mid(0.5) per interval "
+                                       "(config 2), internal 856x480, k 1, repair 1, bicubic, static protection on",
+                           "frames_per_step": gen_per_rank, "l2": "inputs (1 GB of frames) larger than L2, no flush",
+                           "pair_ms": pair_ms, "mid_ms": mid_ms},
+                "gpu_launches": per_interval_launches * gen_per_rank + counts["frame"],
+                "clocks": clk.summary(), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e}
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def conv_flops_per_interval(s) -> float:
+    """2 * M * 9 * cin * cout summed over the convs of one pair + one mid at this session's sizes (both frames'
+    encoders included, as the reference computes them every pair)."""
+    p = s._m.plan_params(W, H)
+    q, e8, e16 = p["qh"] * p["qw"], p["h8"] * p["w8"], p["h16"] * p["w16"]
+    convs = [  # (pixels, cin, cout)
+        (e8, 3, 36), (e8, 36, 36), (e16, 36, 72), (e16, 72, 72)] * 2 + [
+        (e16, 279, 96), (e16, 96, 96), (e16, 96, 96), (e16, 96, 96), (e16, 96, 12),
+        (e8, 155, 48), (e8, 48, 48), (e8, 48, 48), (e8, 48, 7),
+        (e8, 48, 48), (e8, 48, 48), (e8, 48, 5), (e8, 48, 36),
+        (q, 14, 24), (q, 24, 24), (q, 24, 24), (q, 24, 3)]
+    return float(sum(2 * m * 9 * ci * co for m, ci, co in convs))
+
+
+def roofline_block(s, step_ms, intervals):
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    flops = conv_flops_per_interval(s) * intervals
+    peak = peaks.get("bf16_tflops_sustained") or 1400.0
+    achieved = flops / (step_ms / 1000.0) / 1e12
+    return {"bound": "tensor", "kernel": "conv family (whole path, per step)", "achieved": achieved, "peak": peak,
+            "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+            "note": "algorithmic conv FLOPs of the step / step time; the path is launch-latency bound at batch 1"}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -89,7 +89,7 @@ EXPORTS = [
     ("fh_model_fingerprint", c_long, [c_void_p]),
     ("fh_session_plan_params", c_int, [c_void_p, POINTER(SessionOptions), POINTER(c_int), POINTER(c_float)]),
     ("fh_session_launch_counts", c_int, [c_void_p, POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
-    ("fhk_conv3x3", c_int, [c_void_p, c_int, c_int, c_void_p]),
+    ("fhk_conv3x3", c_int, [c_void_p, c_int, c_void_p]),
     ("fhk_conv_pack_weights", c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
     ("fhk_conv_packed_elems", c_size_t, [c_int, c_int]),
 ]

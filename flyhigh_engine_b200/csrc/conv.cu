@@ -11,11 +11,13 @@
 //   refine `rx`) is never materialised; each source lands in its own 8-channel-aligned slot of the shared-memory halo
 //   tile, with its view scale applied and rounded to f16 on load (chcopy.wgsl:19-22). Sources the planner knows to be
 //   zero (the graph's `zeros` tensors) are dropped together with their weight rows, which leaves the f32 sum unchanged.
-// - One CTA computes a (2 x WARPS) x 16 tile of output pixels for ALL output channels (cout <= 96), so the halo tile
-//   is read from HBM once. Each warp owns 2 m16 tiles (two output rows of 16 pixels); A fragments come from the halo
-//   tile with ldmatrix (pixel pitch padded to an odd number of 16-byte units: conflict-free rows at stride 1), B
-//   fragments from a weight array pre-packed in mma fragment order (one coalesced 8-byte load per lane and n-tile,
-//   L1/L2 resident: the largest layer is 360 KB).
+// - A CTA (4 warps) computes a (2 wm) x 16 tile of output pixels for a slice of NT x 8 output channels. wm warps
+//   split the rows (two m16 tiles each); the 4 / wm warps of a row pair split K (the taps x channel slices) and their
+//   partial accumulators are summed in shared memory in a fixed order. Small layers (e16: 1,620 pixels at 1080p) use
+//   wm = 1 and several channel groups so that ~150 CTAs run; large ones use wm = 4.
+// - A fragments come from the halo tile with ldmatrix (pixel pitch padded to an odd number of 16-byte units:
+//   conflict-free rows at stride 1); B fragments from a weight array pre-packed in mma fragment order (one coalesced
+//   8-byte load per lane and n-tile, L1/L2 resident).
 // - mma.sync m16n8k16 f16 -> f32. The epilogue writes straight from the accumulator fragments into the output view
 //   (which may be a channel slice of a wider buffer).
 #include <cuda_fp16.h>
@@ -28,14 +30,8 @@
 
 namespace {
 
-constexpr int TW = 16;  // output tile width (pixels); rows per warp: 2
-
-template <int S, int WARPS>
-struct Geo {
-    static constexpr int TH = 2 * WARPS;
-    static constexpr int IH = (TH - 1) * S + 3;
-    static constexpr int IW = (TW - 1) * S + 3;
-};
+constexpr int TW = 16;    // output tile width (pixels)
+constexpr int WARPS = 4;  // per CTA
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
@@ -52,27 +48,25 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ __half epi_value(float acc, int c, const FhConvParams& p) {
-    float v = acc + p.bias[c];
-    if (p.slope) v = v > 0.0f ? v : p.slope[c] * v;
-    return __float2half_rn(v);
-}
+__host__ __device__ inline int halo_h(int wm, int s) { return (2 * wm - 1) * s + 3; }
+__host__ __device__ inline int halo_w(int s) { return (TW - 1) * s + 3; }
 
-template <int NT, int S, int WARPS>
+template <int NT, int S>
 __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) {
-    using G = Geo<S, WARPS>;
     extern __shared__ __align__(16) __half tile[];
+    const int wm = p.wm, ks = WARPS / wm;
+    const int IH = halo_h(wm, S), IW = halo_w(S);
     const int P = p.cp + 8;  // pixel pitch in halves: cp % 16 == 0, so P / 8 is odd
     const int nchunk = p.cp / 8;
-    const int n = blockIdx.z;
-    const int oy0 = blockIdx.y * G::TH, ox0 = blockIdx.x * TW;
+    const int n = blockIdx.z / p.ngroups, ng = blockIdx.z - n * p.ngroups;
+    const int oy0 = blockIdx.y * 2 * wm, ox0 = blockIdx.x * TW;
     const int iy0 = oy0 * S - 1, ix0 = ox0 * S - 1;
     const int tid = threadIdx.x;
 
-    // ---- halo tile: G::IH x G::IW pixels x cp channels, zero outside the image and beyond every source ----
-    for (int idx = tid; idx < G::IH * G::IW * nchunk; idx += WARPS * 32) {
+    // ---- halo tile: IH x IW pixels x cp channels, zero outside the image and beyond every source ----
+    for (int idx = tid; idx < IH * IW * nchunk; idx += WARPS * 32) {
         const int pix = idx / nchunk, ch = idx - pix * nchunk;
-        const int hy = pix / G::IW, hx = pix - hy * G::IW;
+        const int hy = pix / IW, hx = pix - hy * IW;
         const int iy = iy0 + hy, ix = ix0 + hx;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (iy >= 0 && iy < p.h && ix >= 0 && ix < p.w) {
@@ -104,7 +98,8 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
     __syncthreads();
 
     const int warp = tid >> 5, lane = tid & 31;
-    const int r0 = warp * 2;  // this warp's first output row inside the tile
+    const int wrow = warp % wm, wk = warp / wm;
+    const int r0 = wrow * 2;  // this warp's first output row inside the tile
     float acc[2][NT][4];
 #pragma unroll
     for (int mt = 0; mt < 2; mt++)
@@ -114,27 +109,56 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
     const uint32_t tile_base = (uint32_t)__cvta_generic_to_shared(tile);
     const int lrow = lane & 15, koff = (lane >> 4) * 8;
     const int cslices = p.cp / 16;
-    const uint2* wp = reinterpret_cast<const uint2*>(p.wpack) + lane;
-    for (int tap = 0; tap < 9; tap++) {
+    const int ntt = (p.cout + 7) / 8;  // n-tiles of the packed weights
+    const uint2* wp = reinterpret_cast<const uint2*>(p.wpack) + (size_t)ng * NT * 32 + lane;
+    const int nsteps = 9 * cslices;
+    for (int kstep = wk; kstep < nsteps; kstep += ks) {
+        const int tap = kstep / cslices, cs = kstep - tap * cslices;
         const int ky = tap / 3, kx = tap - ky * 3;
-        // smem pixel of (row r0 + mt, col lrow) shifted by the tap
-        const int pix0 = ((r0 * S + ky) * G::IW + (lrow * S + kx));
-        const int pix1 = pix0 + S * G::IW;
-        const uint32_t a_addr0 = tile_base + (uint32_t)(pix0 * P + koff) * 2;
-        const uint32_t a_addr1 = tile_base + (uint32_t)(pix1 * P + koff) * 2;
-#pragma unroll 2
-        for (int cs = 0; cs < cslices; cs++) {
-            uint32_t a[2][4];
-            ldsm_x4(a_addr0 + cs * 32, a[0][0], a[0][1], a[0][2], a[0][3]);
-            ldsm_x4(a_addr1 + cs * 32, a[1][0], a[1][1], a[1][2], a[1][3]);
-            const int kstep = tap * cslices + cs;
-            const uint2* wk = wp + (size_t)kstep * NT * 32;
+        // smem pixel of (row r0, col lrow) shifted by the tap; row r0 + 1 is S halo rows further
+        const int pix0 = ((r0 * S + ky) * IW + (lrow * S + kx));
+        const uint32_t a_addr0 = tile_base + (uint32_t)(pix0 * P + koff + cs * 16) * 2;
+        const uint32_t a_addr1 = a_addr0 + (uint32_t)(S * IW * P) * 2;
+        uint32_t a[2][4];
+        ldsm_x4(a_addr0, a[0][0], a[0][1], a[0][2], a[0][3]);
+        ldsm_x4(a_addr1, a[1][0], a[1][1], a[1][2], a[1][3]);
+        const uint2* wk_p = wp + (size_t)kstep * ntt * 32;
 #pragma unroll
-            for (int j = 0; j < NT; j++) {
-                const uint2 b = __ldg(wk + j * 32);
+        for (int j = 0; j < NT; j++) {
+            if (ng * NT + j < ntt) {
+                const uint2 b = __ldg(wk_p + j * 32);
                 mma16816(acc[0][j], a[0][0], a[0][1], a[0][2], a[0][3], b.x, b.y);
                 mma16816(acc[1][j], a[1][0], a[1][1], a[1][2], a[1][3], b.x, b.y);
             }
+        }
+    }
+
+    // ---- K-split reduction: partials of warps wk > 0 through shared memory, summed in wk order ----
+    if (ks > 1) {
+        __syncthreads();  // every warp is done with the halo tile
+        float4* red = reinterpret_cast<float4*>(tile);
+        if (wk > 0) {
+            float4* dst = red + ((size_t)((wk - 1) * wm + wrow) * 32 + lane) * (2 * NT);
+#pragma unroll
+            for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+                for (int j = 0; j < NT; j++)
+                    dst[mt * NT + j] = make_float4(acc[mt][j][0], acc[mt][j][1], acc[mt][j][2], acc[mt][j][3]);
+        }
+        __syncthreads();
+        if (wk > 0) return;
+        for (int q = 1; q < ks; q++) {
+            const float4* src = red + ((size_t)((q - 1) * wm + wrow) * 32 + lane) * (2 * NT);
+#pragma unroll
+            for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+                for (int j = 0; j < NT; j++) {
+                    const float4 v = src[mt * NT + j];
+                    acc[mt][j][0] += v.x;
+                    acc[mt][j][1] += v.y;
+                    acc[mt][j][2] += v.z;
+                    acc[mt][j][3] += v.w;
+                }
         }
     }
 
@@ -154,9 +178,11 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
             for (int j = 0; j < NT; j++) {
 #pragma unroll
                 for (int e = 0; e < 2; e++) {
-                    const int c = j * 8 + q * 2 + e;
+                    const int c = (ng * NT + j) * 8 + q * 2 + e;
                     if (c >= p.cout) continue;
-                    __half r = epi_value(acc[mt][j][hh * 2 + e], c, p);
+                    float v = acc[mt][j][hh * 2 + e] + p.bias[c];
+                    if (p.slope) v = v > 0.0f ? v : p.slope[c] * v;
+                    __half r = __float2half_rn(v);
                     if (p.res) r = __float2half_rn(__half2float(r) + __half2float(p.res[rpix + c]));
                     if (p.epi == 1) r = __float2half_rn(2.0f / (1.0f + expf(-__half2float(r))) - 1.0f);
                     p.out[opix + c] = r;
@@ -166,58 +192,91 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
     }
 }
 
-template <int NT, int S, int WARPS>
+size_t smem_bytes(const FhConvParams& p, int s, int nt) {
+    const size_t tile = (size_t)halo_h(p.wm, s) * halo_w(s) * (p.cp + 8) * sizeof(__half);
+    const int ks = WARPS / p.wm;
+    const size_t red = ks > 1 ? (size_t)(ks - 1) * p.wm * 32 * 2 * nt * sizeof(float4) : 0;
+    return tile > red ? tile : red;
+}
+
+template <int NT, int S>
 cudaError_t launch_t(const FhConvParams& p, cudaStream_t st) {
-    using G = Geo<S, WARPS>;
-    const size_t smem = (size_t)G::IH * G::IW * (p.cp + 8) * sizeof(__half);
+    const size_t smem = smem_bytes(p, S, NT);
     if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
-    auto k = conv3x3_mma<NT, S, WARPS>;
-    static size_t configured = 0;  // per instantiation: raise the dynamic shared-memory limit once
-    if (smem > 48 * 1024 && smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    auto k = conv3x3_mma<NT, S>;
+    static size_t configured = 48 * 1024;  // per instantiation: raise the dynamic shared-memory limit once
+    if (smem > configured) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) return e;
-        configured = smem;
+        configured = 227 * 1024;
     }
-    dim3 grid((p.wo + TW - 1) / TW, (p.ho + G::TH - 1) / G::TH, p.n);
+    dim3 grid((p.wo + TW - 1) / TW, (p.ho + 2 * p.wm - 1) / (2 * p.wm), p.n * p.ngroups);
     k<<<grid, WARPS * 32, smem, st>>>(p);
     return cudaGetLastError();
 }
 
-template <int S, int WARPS>
+template <int S>
 cudaError_t launch_nt(int nt, const FhConvParams& p, cudaStream_t st) {
     switch (nt) {
-        case 1: return launch_t<1, S, WARPS>(p, st);
-        case 2: return launch_t<2, S, WARPS>(p, st);
-        case 3: return launch_t<3, S, WARPS>(p, st);
-        case 4: return launch_t<4, S, WARPS>(p, st);
-        case 5: return launch_t<5, S, WARPS>(p, st);
-        case 6: return launch_t<6, S, WARPS>(p, st);
-        case 7: return launch_t<7, S, WARPS>(p, st);
-        case 8: return launch_t<8, S, WARPS>(p, st);
-        case 9: return launch_t<9, S, WARPS>(p, st);
-        case 10: return launch_t<10, S, WARPS>(p, st);
-        case 11: return launch_t<11, S, WARPS>(p, st);
-        case 12: return launch_t<12, S, WARPS>(p, st);
+        case 1: return launch_t<1, S>(p, st);
+        case 2: return launch_t<2, S>(p, st);
+        case 3: return launch_t<3, S>(p, st);
+        case 4: return launch_t<4, S>(p, st);
+        case 5: return launch_t<5, S>(p, st);
+        case 6: return launch_t<6, S>(p, st);
+        case 7: return launch_t<7, S>(p, st);
+        case 8: return launch_t<8, S>(p, st);
+        case 9: return launch_t<9, S>(p, st);
+        case 10: return launch_t<10, S>(p, st);
+        case 11: return launch_t<11, S>(p, st);
+        case 12: return launch_t<12, S>(p, st);
         default: return cudaErrorInvalidValue;
+    }
+}
+
+// the split for a layer of this size: enough CTAs to occupy the 148 SMs, as few channel groups as that allows
+void choose_split(FhConvParams& q) {
+    const int ntt = (q.cout + 7) / 8;
+    const long long cols = (q.wo + TW - 1) / TW;
+    if (q.wm <= 0) {
+        q.wm = 1;
+        for (int wm : {4, 2}) {
+            if (cols * ((q.ho + 2 * wm - 1) / (2 * wm)) * q.n >= 2 * 148) {
+                q.wm = wm;
+                break;
+            }
+        }
+    }
+    if (q.ngroups <= 0) {
+        const long long tiles = cols * ((q.ho + 2 * q.wm - 1) / (2 * q.wm)) * q.n;
+        int g = 1;
+        while (tiles * g < 148 && (ntt + 2 * g - 1) / (2 * g) >= 3) g *= 2;
+        q.ngroups = g;
     }
 }
 
 }  // namespace
 
-extern "C" int fhk_conv3x3(const FhConvParams* p, int stride, int warps, void* stream) {
-    if (!p || p->cp <= 0 || p->cp % 16 || p->nsrc < 1 || p->nsrc > FH_CONV_MAX_SRC || p->cout < 1 || p->cout > 96)
+extern "C" int fhk_conv3x3(const FhConvParams* pin, int stride, void* stream) {
+    if (!pin || pin->cp <= 0 || pin->cp % 16 || pin->nsrc < 1 || pin->nsrc > FH_CONV_MAX_SRC || pin->cout < 1 ||
+        pin->cout > 96 || pin->n < 1)
         return (int)cudaErrorInvalidValue;
-    for (int s = 0; s < p->nsrc; s++) {
-        const FhConvSrc& src = p->src[s];
+    FhConvParams p = *pin;
+    for (int s = 0; s < p.nsrc; s++) {
+        const FhConvSrc& src = p.src[s];
         if (src.slot % 8 || (src.cs % 8 && src.cs != 4) || ((uintptr_t)src.p % (src.cs == 4 ? 8 : 16)))
             return (int)cudaErrorMisalignedAddress;
-        if (src.slot + ((src.nc + 7) & ~7) > p->cp) return (int)cudaErrorInvalidValue;
+        if (src.slot + ((src.nc + 7) & ~7) > p.cp) return (int)cudaErrorInvalidValue;
     }
-    const int nt = (p->cout + 7) / 8;
+    choose_split(p);
+    if (p.wm != 1 && p.wm != 2 && p.wm != 4) return (int)cudaErrorInvalidValue;
+    const int ntt = (p.cout + 7) / 8;
+    if (p.ngroups < 1 || p.ngroups > ntt) return (int)cudaErrorInvalidValue;
+    const int nt = (ntt + p.ngroups - 1) / p.ngroups;
     cudaStream_t st = (cudaStream_t)stream;
     cudaError_t e;
-    if (stride == 1) e = warps == 2 ? launch_nt<1, 2>(nt, *p, st) : launch_nt<1, 4>(nt, *p, st);
-    else if (stride == 2) e = warps == 2 ? launch_nt<2, 2>(nt, *p, st) : launch_nt<2, 4>(nt, *p, st);
+    if (stride == 1) e = launch_nt<1>(nt, p, st);
+    else if (stride == 2) e = launch_nt<2>(nt, p, st);
     else e = cudaErrorInvalidValue;
     return (int)e;
 }

@@ -273,17 +273,23 @@ struct SrcSpec {
     std::vector<int> map;  // model input channel of each of the nc channels, -1 = none
 };
 
-struct InSlot {
+// one frame of an input slot and everything the network derives from it alone (cached until the frame changes)
+struct FrameSet {
     uint8_t* frame = nullptr;
     __half *A = nullptr, *aq = nullptr, *i8 = nullptr, *i16 = nullptr, *f8 = nullptr, *f16 = nullptr;
     uint64_t gen = 1, feat_gen = 0;
     cudaGraphExec_t graph = nullptr;
 };
 
-struct PairSrc {  // what the mid of the current pair reads from its two frames
-    const uint8_t *fa, *fb;
-    const __half *aq, *bq;
-    int a, b;
+// An input slot is double-buffered: a write into the frame set the current pair reads goes to the other set, so the
+// pair's mids keep reading the frames the pair saw (the reference's pair owns tex_in copies of them) without a copy.
+struct InSlot {
+    FrameSet* set[2] = {nullptr, nullptr};
+    int cur = 0;
+};
+
+struct PairSrc {  // the two frame sets of the current pair
+    const FrameSet *a, *b;
 };
 
 }  // namespace
@@ -321,12 +327,11 @@ struct FhSession {
     __half *cv, *ch1, *ch2, *ch3r, *hcb, *ob, *fv, *wbuf, *fcv, *fr1, *fr2, *fr3, *wt36;
     float *coef, *maps, *tmp, *tdev;
     __half *hm, *fh1, *fh2, *dfilm, *ftvt, *up7, *rx, *rq1, *rq2, *rq3, *rt;
-    uint8_t *shadow_fa = nullptr, *shadow_fb = nullptr;
-    __half *shadow_aq = nullptr, *shadow_bq = nullptr;
+    std::vector<std::unique_ptr<FrameSet>> sets;
 
     bool have_pair = false;
     PairSrc pair{};
-    std::map<std::pair<int, int>, cudaGraphExec_t> pair_graphs;
+    std::map<std::pair<const FrameSet*, const FrameSet*>, cudaGraphExec_t> pair_graphs;
     std::map<std::tuple<const void*, const void*, const void*, const void*, const void*>, cudaGraphExec_t> mid_graphs;
     int pair_kernels = 0, mid_kernels = 0, frame_kernels = 0;
     bool mid_ran = false;
@@ -346,8 +351,8 @@ struct FhSession {
 
     ~FhSession() {
         if (st) cudaStreamSynchronize(st);
-        for (auto& s : ins)
-            if (s.graph) cudaGraphExecDestroy(s.graph);
+        for (auto& fs : sets)
+            if (fs->graph) cudaGraphExecDestroy(fs->graph);
         for (auto& kv : pair_graphs) cudaGraphExecDestroy(kv.second);
         for (auto& kv : mid_graphs) cudaGraphExecDestroy(kv.second);
         for (void* p : allocs) cudaFree(p);
@@ -435,9 +440,9 @@ struct FhSession {
         p.res = res;
         p.res_cs = res_cs;
         p.n = 1;
-        const int tiles4 = ((p.ho + 7) / 8) * ((p.wo + 15) / 16);
-        const int warps = tiles4 >= 148 ? 4 : 2;
-        int e = fhk_conv3x3(&p, L.stride, warps, st);
+        p.wm = 0;  // split chosen by size
+        p.ngroups = 0;
+        int e = fhk_conv3x3(&p, L.stride, st);
         if (e) fail("conv %s: %s", key.c_str(), cudaGetErrorString((cudaError_t)e));
     }
 
@@ -551,7 +556,7 @@ struct FhSession {
     }
 
     // ---- stages ----
-    void run_frame(InSlot& s) {
+    void run_frame(FrameSet& s) {
         CK(fhk::frame_to_input(s.frame, 0, w, h, hp, wp, internal, ihp, iwp, {s.A, 0}, 1, st));
         CK(fhk::input_pyramid({s.A, 0}, NH, NW, {s.aq, 0}, {s.i8, 0}, {s.i16, 0}, 1, st));
         conv("e1", {s.aq}, qh, qw, e1, C8P);
@@ -560,7 +565,7 @@ struct FhSession {
         conv("e4", {e3}, h16, w16, s.f16, C16P, e3, C16P);
     }
 
-    void run_pair(const InSlot& A, const InSlot& B) {
+    void run_pair(const FrameSet& A, const FrameSet& B) {
         if (protects) {
             CK(fhk::static_changed(A.frame, B.frame, sargs, changed, st));
             CK(fhk::static_age(A.frame, B.frame, changed, mask, sargs, state, age, st));
@@ -600,12 +605,12 @@ struct FhSession {
         conv("fout", {fh2}, h8, w8, dfilm, 8);
         CK(fhk::mid_combine(tdev, fv, 0, dfilm, 0, ftvt, 0, h8, w8, 1, st));
         CK(fhk::convex_up(wt36, 40, 0, ftvt, 0, h8, w8, up7, 0, 1, st));
-        CK(fhk::refine_input(up7, 0, {(__half*)p.aq, 0}, {(__half*)p.bq, 0}, qh, qw, rx, 0, 1, st));
+        CK(fhk::refine_input(up7, 0, {p.a->aq, 0}, {p.b->aq, 0}, qh, qw, rx, 0, 1, st));
         conv("q1", {rx}, qh, qw, rq1, CQP);
         conv("q2", {rq1}, qh, qw, rq2, CQP);
         conv("q3", {rq2}, qh, qw, rq3, CQP);
         conv("q4", {rq3}, qh, qw, rt, 4, nullptr, 0, 1);
-        fhk::RenderArgs ra{p.fa, p.fb, 0, w, h, hp, wp, up7, 0, rt, 0, qh, qw, fsx, fsy, cubic ? 1 : 0,
+        fhk::RenderArgs ra{p.a->frame, p.b->frame, 0, w, h, hp, wp, up7, 0, rt, 0, qh, qw, fsx, fsy, cubic ? 1 : 0,
                            (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, 0, min_age, out, 0};
         CK(fhk::render(ra, 1, st));
     }
@@ -633,12 +638,13 @@ struct FhSession {
         return ex;
     }
 
-    void ensure_features(int i) {
-        InSlot& s = ins[i];
-        if (s.feat_gen == s.gen) return;
-        if (!s.graph) s.graph = capture([&] { run_frame(s); }, &frame_kernels);
-        CK(cudaGraphLaunch(s.graph, st));
-        s.feat_gen = s.gen;
+    FrameSet& cur_set(uint32_t i) const { return *ins[i].set[ins[i].cur]; }
+
+    void ensure_features(FrameSet& fs) {
+        if (fs.feat_gen == fs.gen) return;
+        if (!fs.graph) fs.graph = capture([&] { run_frame(fs); }, &frame_kernels);
+        CK(cudaGraphLaunch(fs.graph, st));
+        fs.feat_gen = fs.gen;
     }
 
     void check_in(uint32_t i) const {
@@ -648,22 +654,27 @@ struct FhSession {
         if (i >= outs.size()) fail("bad output slot %u (the session has %zu)", i, outs.size());
     }
 
+    cudaGraphExec_t pair_graph(const FrameSet& A, const FrameSet& B) {
+        auto key = std::make_pair(&A, &B);
+        auto it = pair_graphs.find(key);
+        if (it == pair_graphs.end()) it = pair_graphs.emplace(key, capture([&] { run_pair(A, B); }, &pair_kernels)).first;
+        return it->second;
+    }
+
     void do_pair(uint32_t a, uint32_t b) {
         check_in(a);
         check_in(b);
-        ensure_features(a);
-        ensure_features(b);
-        auto key = std::make_pair((int)a, (int)b);
-        auto it = pair_graphs.find(key);
-        if (it == pair_graphs.end())
-            it = pair_graphs.emplace(key, capture([&] { run_pair(ins[a], ins[b]); }, &pair_kernels)).first;
-        CK(cudaGraphLaunch(it->second, st));
-        pair = PairSrc{ins[a].frame, ins[b].frame, ins[a].aq, ins[b].aq, (int)a, (int)b};
+        FrameSet& A = cur_set(a);
+        FrameSet& B = cur_set(b);
+        ensure_features(A);
+        ensure_features(B);
+        CK(cudaGraphLaunch(pair_graph(A, B), st));
+        pair = PairSrc{&A, &B};
         have_pair = true;
     }
 
     cudaGraphExec_t mid_graph(uint32_t out) {
-        auto key = std::make_tuple((const void*)pair.fa, (const void*)pair.fb, (const void*)pair.aq, (const void*)pair.bq,
+        auto key = std::make_tuple((const void*)pair.a, (const void*)pair.b, (const void*)nullptr, (const void*)nullptr,
                                    (const void*)outs[out]);
         auto it = mid_graphs.find(key);
         if (it == mid_graphs.end()) {
@@ -684,41 +695,36 @@ struct FhSession {
         mid_ran = true;
     }
 
-    // a write into a slot the current pair reads: the pair keeps its frame (the reference's pair owns tex_in copies)
-    void protect_pair_slot(uint32_t slot) {
-        if (!have_pair) return;
-        const size_t fb = (size_t)w * h * 4, qb = (size_t)qh * qw * 4 * sizeof(__half);
-        if ((int)slot == pair.a && pair.fa == ins[slot].frame) {
-            if (!shadow_fa) {
-                shadow_fa = alloc_n<uint8_t>(fb);
-                shadow_aq = img(qh, qw, 4);
-            }
-            CK(cudaMemcpyAsync(shadow_fa, ins[slot].frame, fb, cudaMemcpyDeviceToDevice, st));
-            CK(cudaMemcpyAsync(shadow_aq, ins[slot].aq, qb, cudaMemcpyDeviceToDevice, st));
-            pair.fa = shadow_fa;
-            pair.aq = shadow_aq;
+    FrameSet* new_set() {
+        auto fs = std::make_unique<FrameSet>();
+        fs->frame = alloc_n<uint8_t>((size_t)w * h * 4);
+        fs->A = img(NH, NW, 4);
+        fs->aq = img(qh, qw, 4);
+        fs->i8 = img(h8, w8, 4);
+        fs->i16 = img(h16, w16, 4);
+        fs->f8 = img(h8, w8, C8P);
+        fs->f16 = img(h16, w16, C16P);
+        sets.push_back(std::move(fs));
+        return sets.back().get();
+    }
+
+    // the frame set a write into slot i goes to (the other one when the current pair reads the current one)
+    FrameSet& write_target(uint32_t i) {
+        check_in(i);
+        InSlot& s = ins[i];
+        FrameSet* c = s.set[s.cur];
+        if (have_pair && (pair.a == c || pair.b == c)) {
+            if (!s.set[s.cur ^ 1]) s.set[s.cur ^ 1] = new_set();
+            s.cur ^= 1;
         }
-        if ((int)slot == pair.b && pair.fb == ins[slot].frame) {
-            if (!shadow_fb) {
-                shadow_fb = alloc_n<uint8_t>(fb);
-                shadow_bq = img(qh, qw, 4);
-            }
-            CK(cudaMemcpyAsync(shadow_fb, ins[slot].frame, fb, cudaMemcpyDeviceToDevice, st));
-            CK(cudaMemcpyAsync(shadow_bq, ins[slot].aq, qb, cudaMemcpyDeviceToDevice, st));
-            pair.fb = shadow_fb;
-            pair.bq = shadow_bq;
-        }
+        FrameSet& fs = *s.set[s.cur];
+        fs.gen++;
+        return fs;
     }
 
     int add_input() {
         InSlot s;
-        s.frame = alloc_n<uint8_t>((size_t)w * h * 4);
-        s.A = img(NH, NW, 4);
-        s.aq = img(qh, qw, 4);
-        s.i8 = img(h8, w8, 4);
-        s.i16 = img(h16, w16, 4);
-        s.f8 = img(h8, w8, C8P);
-        s.f16 = img(h16, w16, C16P);
+        s.set[0] = new_set();
         ins.push_back(s);
         return (int)ins.size() - 1;
     }
@@ -988,9 +994,7 @@ int fh_session_write_rgba(const FhSession* cs, uint32_t slot, const uint8_t* rgb
         s->check_in(slot);
         const size_t n = (size_t)s->w * s->h * 4;
         if (len != n) fail("frame is %zu bytes, %dx%dx4 = %zu expected", len, s->w, s->h, n);
-        s->protect_pair_slot(slot);
-        CK(cudaMemcpyAsync(s->ins[slot].frame, rgba, n, cudaMemcpyHostToDevice, s->st));
-        s->ins[slot].gen++;
+        CK(cudaMemcpyAsync(s->write_target(slot).frame, rgba, n, cudaMemcpyHostToDevice, s->st));
         return 0;
     });
 }
@@ -1062,13 +1066,15 @@ int fh_session_pair_timed(const FhSession* cs, uint32_t a, uint32_t b, double* m
         CK(cudaEventCreate(&e0));
         CK(cudaEventCreate(&e1));
         float best = 1e30f;
+        FrameSet& A = s->cur_set(a);
+        FrameSet& B = s->cur_set(b);
+        s->ensure_features(A);
+        s->ensure_features(B);
+        s->pair_graph(A, B);
         for (int r = 0; r < 3; r++) {
             // the reference's pair converts and encodes both frames every time (tex_in x2 + the plan): time the same
             // work, the two frame stages included, without the credit of the per-slot feature cache
-            s->ins[a].feat_gen = s->ins[b].feat_gen = 0;
-            if (!s->ins[a].graph) s->ensure_features(a);
-            if (!s->ins[b].graph) s->ensure_features(b);
-            s->ins[a].feat_gen = s->ins[b].feat_gen = 0;
+            A.feat_gen = B.feat_gen = 0;
             CK(cudaEventRecord(e0, s->st));
             s->do_pair(a, b);
             CK(cudaEventRecord(e1, s->st));
@@ -1168,7 +1174,7 @@ int fh_session_slot_device_ptr(const FhSession* s, uint32_t slot, int output, vo
             *ptr = s->outs[slot];
         } else {
             s->check_in(slot);
-            *ptr = s->ins[slot].frame;
+            *ptr = s->cur_set(slot).frame;
         }
         return 0;
     });
@@ -1181,9 +1187,7 @@ int fh_session_write_rgba_device(const FhSession* cs, uint32_t slot, const void*
         s->check_in(slot);
         const size_t n = (size_t)s->w * s->h * 4;
         if (len != n) fail("frame is %zu bytes, %dx%dx4 = %zu expected", len, s->w, s->h, n);
-        s->protect_pair_slot(slot);
-        CK(cudaMemcpyAsync(s->ins[slot].frame, dev, n, cudaMemcpyDeviceToDevice, s->st));
-        s->ins[slot].gen++;
+        CK(cudaMemcpyAsync(s->write_target(slot).frame, dev, n, cudaMemcpyDeviceToDevice, s->st));
         return 0;
     });
 }
@@ -1204,8 +1208,8 @@ long fh_session_debug_tensor(const FhSession* cs, const char* name, float* out, 
         if (!s || !name || !dims) fail("null argument");
         if (!s->have_pair) fail("no pair has run");
         std::string n(name);
-        const InSlot& A = s->ins[s->pair.a];
-        const InSlot& B = s->ins[s->pair.b];
+        const FrameSet& A = *s->pair.a;
+        const FrameSet& B = *s->pair.b;
         // (pointer, pixel pitch, channel offset, channels, height, width, kind 0 = f16 / 1 = int16 / 2 = rgba8 planes)
         const void* p = nullptr;
         int cs_ = 0, c0 = 0, c = 0, hh = 0, ww = 0, kind = 0;

@@ -52,11 +52,15 @@ typedef struct FhConvParams {
     int res_cs;
     long long res_bs;
     int n;                 /* batch */
+    int wm;                /* warps along output rows (1, 2, 4; the other 4 / wm split K), 0 = chosen by size */
+    int ngroups;           /* CTAs sharing one output tile, each a slice of the output channels; 0 = chosen */
 } FhConvParams;
 
 /* Replaces the conv family of the reference (ops/conv/kernels.rs:100-279: conv_tc / conv_direct / conv_tiled*,
- * conv_fused*.wgsl, splitk_reduce.wgsl). stride 1 or 2; warps 2 or 4 (output tile (2 * warps) x 16 pixels). */
-int fhk_conv3x3(const FhConvParams* p, int stride, int warps, void* stream);
+ * conv_fused*.wgsl, splitk_reduce.wgsl, and the split-K the autotuner picks per shape, autotune.rs:74-150).
+ * stride 1 or 2. A CTA of 4 warps computes (2 * wm) x 16 output pixels for a slice of the output channels; the K
+ * dimension is split over the other 4 / wm warps and reduced in shared memory in a fixed order. */
+int fhk_conv3x3(const FhConvParams* p, int stride, void* stream);
 /* Replaces buildb / buildb_tap (ops/conv/kernels.rs:66-78, :194-207): torch [cout][cin][3][3] f16 bits -> the
  * kernel's B-fragment order; map[pc] = model input channel of packed channel pc, or -1 (weight 0). */
 int fhk_conv_pack_weights(const uint16_t* w, int cin, int cout, const int* map, int cp, uint16_t* out);

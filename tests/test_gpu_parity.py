@@ -22,7 +22,7 @@ class ConvParams(Structure):
     _fields_ = [("src", ConvSrc * 6), ("nsrc", c_int), ("h", c_int), ("w", c_int), ("ho", c_int), ("wo", c_int),
                 ("cp", c_int), ("cout", c_int), ("wpack", c_void_p), ("bias", c_void_p), ("slope", c_void_p),
                 ("epi", c_int), ("out", c_void_p), ("out_cs", c_int), ("out_bs", c_longlong), ("res", c_void_p),
-                ("res_cs", c_int), ("res_bs", c_longlong), ("n", c_int)]
+                ("res_cs", c_int), ("res_bs", c_longlong), ("n", c_int), ("wm", c_int), ("ngroups", c_int)]
 
 
 @pytest.fixture(scope="module")
@@ -37,7 +37,7 @@ def _up8(c):
     return (c + 7) // 8 * 8
 
 
-def run_conv(torch, x_chw, w, bias, slope, stride, resid_chw=None, warps=2):
+def run_conv(torch, x_chw, w, bias, slope, stride, resid_chw=None, wm=0, ngroups=0):
     """One conv through fhk_conv3x3 on NHWC device buffers; returns CHW f16."""
     import flyhigh_engine_b200 as fh
     L = fh.lib()
@@ -71,7 +71,8 @@ def run_conv(torch, x_chw, w, bias, slope, stride, resid_chw=None, warps=2):
     p.wpack, p.bias, p.slope = wp.data_ptr(), b.data_ptr(), (s.data_ptr() if s is not None else None)
     p.epi, p.out, p.out_cs, p.out_bs = 0, out.data_ptr(), ocs, 0
     p.res, p.res_cs, p.res_bs, p.n = (r.data_ptr() if r is not None else None), ocs, 0, 1
-    rc = L.fhk_conv3x3(ctypes.byref(p), stride, warps, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    p.wm, p.ngroups = wm, ngroups
+    rc = L.fhk_conv3x3(ctypes.byref(p), stride, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == 0, rc
     torch.cuda.synchronize()
     return out[:, :, :cout].permute(2, 0, 1).cpu().numpy()
@@ -102,8 +103,8 @@ CONV_CASES = [
 
 
 @pytest.mark.parametrize("h,w,cin,cout,stride,res", CONV_CASES)
-@pytest.mark.parametrize("warps", [2, 4])
-def test_conv_matches_oracle(torch_cuda, h, w, cin, cout, stride, res, warps):
+@pytest.mark.parametrize("split", [(0, 0), (1, 2), (4, 1), (2, 1)])
+def test_conv_matches_oracle(torch_cuda, h, w, cin, cout, stride, res, split):
     from oracle import oracle
     rng = np.random.default_rng(h * 1000 + cin * 10 + cout + stride)
     x = rng.standard_normal((cin, h, w)).astype(np.float16)
@@ -113,7 +114,9 @@ def test_conv_matches_oracle(torch_cuda, h, w, cin, cout, stride, res, warps):
     ho, wo = (h - 1) // stride + 1, (w - 1) // stride + 1
     resid = rng.standard_normal((cout, ho, wo)).astype(np.float16) if res else None
     ref = oracle.conv(x, wt, bias, slope, stride, resid).astype(np.float32)
-    got = run_conv(torch_cuda, x, wt, bias, slope, stride, resid, warps).astype(np.float32)
+    wm, ng = split
+    ng = min(ng, (cout + 7) // 8)
+    got = run_conv(torch_cuda, x, wt, bias, slope, stride, resid, wm, ng).astype(np.float32)
     assert got.shape == ref.shape
     assert rel_l2(got, ref) < 2e-3
     # f32 accumulation order differs from the oracle's: a few f16 ulps at most
