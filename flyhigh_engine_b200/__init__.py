@@ -92,6 +92,8 @@ EXPORTS = [
     ("fhk_conv3x3", c_int, [c_void_p, c_int, c_void_p]),
     ("fhk_conv_pack_weights", c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
     ("fhk_conv_packed_elems", c_size_t, [c_int, c_int]),
+    ("fhk_gmhs", c_int, [c_void_p, c_void_p]),
+    ("fhk_gmhs_scratch_floats", c_size_t, [c_int, c_int]),
 ]
 
 

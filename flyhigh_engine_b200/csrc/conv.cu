@@ -16,8 +16,10 @@
 //   partial accumulators are summed in shared memory in a fixed order. Small layers (e16: 1,620 pixels at 1080p) use
 //   wm = 1 and several channel groups so that ~150 CTAs run; large ones use wm = 4.
 // - A fragments come from the halo tile with ldmatrix (pixel pitch padded to an odd number of 16-byte units:
-//   conflict-free rows at stride 1); B fragments from a weight array pre-packed in mma fragment order (one coalesced
-//   8-byte load per lane and n-tile, L1/L2 resident).
+//   conflict-free rows at stride 1); B fragments from a weight array pre-packed in mma fragment order (one 8-byte
+//   load per lane and n-tile, 256 contiguous bytes per warp). The CTA's weight slice is staged into shared memory with
+//   cp.async while the halo tile is gathered, so the k loop waits on no global load; slices too large to leave room
+//   for three CTAs per SM are read from L1/L2 instead.
 // - mma.sync m16n8k16 f16 -> f32. The epilogue writes straight from the accumulator fragments into the output view
 //   (which may be a channel slice of a wider buffer).
 #include <cuda_fp16.h>
@@ -50,6 +52,13 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
 
 __host__ __device__ inline int halo_h(int wm, int s) { return (2 * wm - 1) * s + 3; }
 __host__ __device__ inline int halo_w(int s) { return (TW - 1) * s + 3; }
+// the halo tile's bytes, rounded to 16
+__host__ __device__ inline int tile_bytes(int wm, int s, int cp) { return halo_h(wm, s) * halo_w(s) * (cp + 8) * 2; }
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::); }
 
 template <int NT, int S>
 __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) {
@@ -62,42 +71,98 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
     const int oy0 = blockIdx.y * 2 * wm, ox0 = blockIdx.x * TW;
     const int iy0 = oy0 * S - 1, ix0 = ox0 * S - 1;
     const int tid = threadIdx.x;
+    const int cslices = p.cp / 16;
+    const int ntt = (p.cout + 7) / 8;  // n-tiles of the packed weights
+    const int nsteps = 9 * cslices;
+    const int nvalid = min(NT, ntt - ng * NT);  // n-tiles of this channel group
+    const int warp = tid >> 5, lane = tid & 31;
+    // ---- the group's weight slice (nsteps x nvalid x 256 B) into shared memory behind the halo tile, when staged:
+    //      issued first, it lands while the halo tile is gathered. Warps take k-steps, lanes 16-byte pieces ----
+    const int wbase = tile_bytes(wm, S, p.cp);
+    // bias and PReLU slopes of the group (f32) at the end of the dynamic shared memory
+    const int redb = ks > 1 ? (ks - 1) * wm * 32 * 2 * NT * 16 : 0;
+    const int sb_off = max(wbase + (p.wsmem ? nsteps * NT * 256 : 0), redb);
+    float* sbias = reinterpret_cast<float*>(reinterpret_cast<char*>(tile) + sb_off);
+    float* sslope = sbias + NT * 8;
+    const bool prelu = p.slope != nullptr;
+    for (int i = tid; i < NT * 8; i += WARPS * 32) {
+        const int c = ng * NT * 8 + i;
+        sbias[i] = c < p.cout ? p.bias[c] : 0.0f;
+        sslope[i] = (prelu && c < p.cout) ? p.slope[c] : 1.0f;
+    }
+    if (p.wsmem) {
+        const uint32_t dst0 = (uint32_t)__cvta_generic_to_shared(tile) + wbase;
+        const char* src0 = reinterpret_cast<const char*>(p.wpack) + (size_t)ng * NT * 256;
+        const int per = nvalid * 16;  // 16-byte pieces per k-step
+        for (int k = warp; k < nsteps; k += WARPS)
+            for (int r = lane; r < per; r += 32)
+                cp_async16(dst0 + (uint32_t)(k * NT * 256 + r * 16), src0 + (size_t)k * ntt * 256 + (size_t)r * 16);
+    }
 
-    // ---- halo tile: IH x IW pixels x cp channels, zero outside the image and beyond every source ----
-    for (int idx = tid; idx < IH * IW * nchunk; idx += WARPS * 32) {
-        const int pix = idx / nchunk, ch = idx - pix * nchunk;
-        const int hy = pix / IW, hx = pix - hy * IW;
-        const int iy = iy0 + hy, ix = ix0 + hx;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (iy >= 0 && iy < p.h && ix >= 0 && ix < p.w) {
-            const int c8 = ch * 8;
-#pragma unroll 1
-            for (int s = 0; s < p.nsrc; s++) {
-                const FhConvSrc& src = p.src[s];
-                const int rel = c8 - src.slot;
-                if (rel < 0 || rel >= ((src.nc + 7) & ~7)) continue;
-                const __half* g = src.p + (long long)n * src.bs + ((long long)iy * p.w + ix) * src.cs + rel;
-                if (src.cs >= rel + 8) {
-                    v = __ldg(reinterpret_cast<const uint4*>(g));
-                } else {  // a 4-channel pixel (3-channel image): 8 bytes
-                    uint2 u = __ldg(reinterpret_cast<const uint2*>(g));
-                    v = make_uint4(u.x, u.y, 0, 0);
-                }
-                __half* hv = reinterpret_cast<__half*>(&v);
-                const int valid = src.nc - rel;
-#pragma unroll
-                for (int k = 0; k < 8; k++) {
-                    if (k >= valid) hv[k] = __float2half_rn(0.0f);
-                    else if (src.scale != 1.0f) hv[k] = __float2half_rn(__half2float(hv[k]) * src.scale);
-                }
+    // ---- halo tile: IH x IW pixels x cp channels, zero outside the image and beyond every source. A lane owns
+    //      8-channel chunks (its source, offset and view scale resolved once); a warp walks pixels, 4 loads in flight ----
+    for (int ch = lane; ch < nchunk; ch += 32) {
+        const int c8 = ch * 8;
+        int si = -1, rel = 0;
+        for (int s_ = 0; s_ < p.nsrc; s_++) {
+            const int r_ = c8 - p.src[s_].slot;
+            if (r_ >= 0 && r_ < ((p.src[s_].nc + 7) & ~7)) {
+                si = s_;
+                rel = r_;
                 break;
             }
         }
-        *reinterpret_cast<uint4*>(tile + pix * P + ch * 8) = v;
+        const __half* base = nullptr;
+        int cs = 0, valid = 0;
+        float scale = 1.0f;
+        bool narrow = false;
+        if (si >= 0) {
+            const FhConvSrc& src = p.src[si];
+            base = src.p + (long long)n * src.bs + rel;
+            cs = src.cs;
+            valid = src.nc - rel;
+            scale = src.scale;
+            narrow = src.cs < rel + 8;
+        }
+        const bool plain = valid >= 8 && scale == 1.0f && !narrow;
+        const int npix = IH * IW;
+        for (int pix0 = warp; pix0 < npix; pix0 += 4 * WARPS) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int pix = pix0 + u * WARPS;
+                const int hy = pix / IW, hx = pix - hy * IW;
+                const int iy = iy0 + hy, ix = ix0 + hx;
+                v[u] = make_uint4(0, 0, 0, 0);
+                if (pix < npix && si >= 0 && iy >= 0 && iy < p.h && ix >= 0 && ix < p.w) {
+                    const __half* g = base + ((long long)iy * p.w + ix) * cs;
+                    if (!narrow) {
+                        v[u] = __ldg(reinterpret_cast<const uint4*>(g));
+                    } else {  // a 4-channel pixel (3-channel image): 8 bytes
+                        const uint2 w2 = __ldg(reinterpret_cast<const uint2*>(g));
+                        v[u] = make_uint4(w2.x, w2.y, 0, 0);
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int pix = pix0 + u * WARPS;
+                if (pix >= npix) break;
+                if (!plain) {
+                    __half* hv = reinterpret_cast<__half*>(&v[u]);
+#pragma unroll
+                    for (int k = 0; k < 8; k++) {
+                        if (k >= valid) hv[k] = __float2half_rn(0.0f);
+                        else if (scale != 1.0f) hv[k] = __float2half_rn(__half2float(hv[k]) * scale);
+                    }
+                }
+                *reinterpret_cast<uint4*>(tile + pix * P + c8) = v[u];
+            }
+        }
     }
+    if (p.wsmem) cp_async_wait_all();
     __syncthreads();
 
-    const int warp = tid >> 5, lane = tid & 31;
     const int wrow = warp % wm, wk = warp / wm;
     const int r0 = wrow * 2;  // this warp's first output row inside the tile
     float acc[2][NT][4];
@@ -108,12 +173,16 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
 
     const uint32_t tile_base = (uint32_t)__cvta_generic_to_shared(tile);
     const int lrow = lane & 15, koff = (lane >> 4) * 8;
-    const int cslices = p.cp / 16;
-    const int ntt = (p.cout + 7) / 8;  // n-tiles of the packed weights
-    const uint2* wp = reinterpret_cast<const uint2*>(p.wpack) + (size_t)ng * NT * 32 + lane;
-    const int nsteps = 9 * cslices;
+    // B fragments: from the staged slice ([kstep][NT][lane]) or from the packed array ([kstep][ntt][lane])
+    const uint2* wp = p.wsmem ? reinterpret_cast<const uint2*>(reinterpret_cast<const char*>(tile) + wbase) + lane
+                              : reinterpret_cast<const uint2*>(p.wpack) + (size_t)ng * NT * 32 + lane;
+    const int wstride = p.wsmem ? NT * 32 : ntt * 32;
+    int tap = 0, cs = wk;  // kstep = tap * cslices + cs, advanced by ks without a division
+    while (cs >= cslices) {
+        cs -= cslices;
+        tap++;
+    }
     for (int kstep = wk; kstep < nsteps; kstep += ks) {
-        const int tap = kstep / cslices, cs = kstep - tap * cslices;
         const int ky = tap / 3, kx = tap - ky * 3;
         // smem pixel of (row r0, col lrow) shifted by the tap; row r0 + 1 is S halo rows further
         const int pix0 = ((r0 * S + ky) * IW + (lrow * S + kx));
@@ -122,14 +191,19 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
         uint32_t a[2][4];
         ldsm_x4(a_addr0, a[0][0], a[0][1], a[0][2], a[0][3]);
         ldsm_x4(a_addr1, a[1][0], a[1][1], a[1][2], a[1][3]);
-        const uint2* wk_p = wp + (size_t)kstep * ntt * 32;
+        const uint2* wk_p = wp + (size_t)kstep * wstride;
 #pragma unroll
         for (int j = 0; j < NT; j++) {
-            if (ng * NT + j < ntt) {
-                const uint2 b = __ldg(wk_p + j * 32);
+            if (j < nvalid) {
+                const uint2 b = wk_p[j * 32];
                 mma16816(acc[0][j], a[0][0], a[0][1], a[0][2], a[0][3], b.x, b.y);
                 mma16816(acc[1][j], a[1][0], a[1][1], a[1][2], a[1][3], b.x, b.y);
             }
+        }
+        cs += ks;
+        while (cs >= cslices) {
+            cs -= cslices;
+            tap++;
         }
     }
 
@@ -162,7 +236,8 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
         }
     }
 
-    // ---- epilogue: bias, PReLU, f16, residual / affine_out, store ----
+    // ---- epilogue: bias, PReLU, f16, residual / affine_out, store. Bias and slopes come from shared memory and the
+    //      residual pair of a lane is loaded before any store, so no load waits behind a store it might alias ----
     const int g = lane >> 2, q = lane & 3;
 #pragma unroll
     for (int mt = 0; mt < 2; mt++) {
@@ -172,35 +247,55 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
         for (int hh = 0; hh < 2; hh++) {
             const int ox = ox0 + g + hh * 8;
             if (ox >= p.wo) continue;
-            const long long opix = (long long)n * p.out_bs + ((long long)oy * p.wo + ox) * p.out_cs;
-            const long long rpix = (long long)n * p.res_bs + ((long long)oy * p.wo + ox) * p.res_cs;
+            __half* __restrict__ out = p.out + (long long)n * p.out_bs + ((long long)oy * p.wo + ox) * p.out_cs;
+            float2 rv[NT];
+            if (p.res) {
+                const __half* __restrict__ res = p.res + (long long)n * p.res_bs + ((long long)oy * p.wo + ox) * p.res_cs;
+#pragma unroll
+                for (int j = 0; j < NT; j++) {
+                    const int c0 = (ng * NT + j) * 8 + q * 2;
+                    rv[j] = make_float2(0.0f, 0.0f);
+                    if (c0 + 1 < p.cout) rv[j] = __half22float2(*reinterpret_cast<const __half2*>(res + c0));
+                    else if (c0 < p.cout) rv[j].x = __half2float(res[c0]);
+                }
+            }
 #pragma unroll
             for (int j = 0; j < NT; j++) {
+                const int jl = j * 8 + q * 2;  // channel of this lane inside the group
+                const int c0 = ng * NT * 8 + jl;
+                if (c0 >= p.cout) continue;
+                __half r[2];
 #pragma unroll
                 for (int e = 0; e < 2; e++) {
-                    const int c = (ng * NT + j) * 8 + q * 2 + e;
-                    if (c >= p.cout) continue;
-                    float v = acc[mt][j][hh * 2 + e] + p.bias[c];
-                    if (p.slope) v = v > 0.0f ? v : p.slope[c] * v;
-                    __half r = __float2half_rn(v);
-                    if (p.res) r = __float2half_rn(__half2float(r) + __half2float(p.res[rpix + c]));
-                    if (p.epi == 1) r = __float2half_rn(2.0f / (1.0f + expf(-__half2float(r))) - 1.0f);
-                    p.out[opix + c] = r;
+                    float v = acc[mt][j][hh * 2 + e] + sbias[jl + e];
+                    if (prelu) v = v > 0.0f ? v : sslope[jl + e] * v;
+                    r[e] = __float2half_rn(v);
+                    if (p.res) r[e] = __float2half_rn(__half2float(r[e]) + (e ? rv[j].y : rv[j].x));
+                    if (p.epi == 1) r[e] = __float2half_rn(2.0f / (1.0f + expf(-__half2float(r[e]))) - 1.0f);
                 }
+                if (c0 + 1 < p.cout) *reinterpret_cast<__half2*>(out + c0) = __halves2half2(r[0], r[1]);
+                else out[c0] = r[0];
             }
         }
     }
 }
 
+constexpr size_t kSmemMax = 227 * 1024;
+
+size_t weight_bytes(const FhConvParams& p, int nt) { return (size_t)9 * (p.cp / 16) * nt * 256; }
+
 size_t smem_bytes(const FhConvParams& p, int s, int nt) {
-    const size_t tile = (size_t)halo_h(p.wm, s) * halo_w(s) * (p.cp + 8) * sizeof(__half);
+    const size_t tile = (size_t)tile_bytes(p.wm, s, p.cp) + (p.wsmem ? weight_bytes(p, nt) : 0);
     const int ks = WARPS / p.wm;
     const size_t red = ks > 1 ? (size_t)(ks - 1) * p.wm * 32 * 2 * nt * sizeof(float4) : 0;
-    return tile > red ? tile : red;
+    return (tile > red ? tile : red) + 2 * (size_t)nt * 8 * sizeof(float);  // + bias and slopes
 }
 
 template <int NT, int S>
-cudaError_t launch_t(const FhConvParams& p, cudaStream_t st) {
+cudaError_t launch_t(FhConvParams p, cudaStream_t st) {
+    // stage the weight slice when it fits beside the halo tile and leaves room for a second CTA on the SM
+    p.wsmem = 1;
+    if (smem_bytes(p, S, NT) > kSmemMax / 3) p.wsmem = 0;
     const size_t smem = smem_bytes(p, S, NT);
     if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
     auto k = conv3x3_mma<NT, S>;
@@ -262,6 +357,8 @@ extern "C" int fhk_conv3x3(const FhConvParams* pin, int stride, void* stream) {
         pin->cout > 96 || pin->n < 1)
         return (int)cudaErrorInvalidValue;
     FhConvParams p = *pin;
+    if (p.out_cs % 2 || (p.res && p.res_cs % 2) || (uintptr_t)p.out % 4 || (p.res && (uintptr_t)p.res % 4))
+        return (int)cudaErrorMisalignedAddress;
     for (int s = 0; s < p.nsrc; s++) {
         const FhConvSrc& src = p.src[s];
         if (src.slot % 8 || (src.cs % 8 && src.cs != 4) || ((uintptr_t)src.p % (src.cs == 4 ? 8 : 16)))
@@ -273,6 +370,7 @@ extern "C" int fhk_conv3x3(const FhConvParams* pin, int stride, void* stream) {
     const int ntt = (p.cout + 7) / 8;
     if (p.ngroups < 1 || p.ngroups > ntt) return (int)cudaErrorInvalidValue;
     const int nt = (ntt + p.ngroups - 1) / p.ngroups;
+    p.ngroups = (ntt + nt - 1) / nt;  // no group without output channels
     cudaStream_t st = (cudaStream_t)stream;
     cudaError_t e;
     if (stride == 1) e = launch_nt<1>(nt, p, st);

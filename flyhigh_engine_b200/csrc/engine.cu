@@ -276,6 +276,7 @@ struct SrcSpec {
 // one frame of an input slot and everything the network derives from it alone (cached until the frame changes)
 struct FrameSet {
     uint8_t* frame = nullptr;
+    __half* half = nullptr;  // the frame's f16 plane (w x h x 4), what the render samples
     __half *A = nullptr, *aq = nullptr, *i8 = nullptr, *i16 = nullptr, *f8 = nullptr, *f16 = nullptr;
     uint64_t gen = 1, feat_gen = 0;
     cudaGraphExec_t graph = nullptr;
@@ -324,6 +325,8 @@ struct FhSession {
     uint8_t *changed = nullptr, *mask = nullptr;
     uchar4* state = nullptr;
     int16_t* age = nullptr;
+    float* dsum = nullptr;      // per pair: the still test's per-pixel |A - B| sums
+    uint8_t* nearp = nullptr;   // per pair: near a protected pixel
     __half *cv, *ch1, *ch2, *ch3r, *hcb, *ob, *fv, *wbuf, *fcv, *fr1, *fr2, *fr3, *wt36;
     float *coef, *maps, *tmp, *tdev;
     __half *hm, *fh1, *fh2, *dfilm, *ftvt, *up7, *rx, *rq1, *rq2, *rq3, *rt;
@@ -337,6 +340,9 @@ struct FhSession {
     bool mid_ran = false;
     uint64_t pair_static_gen = 0;  // the static state advances once per pair() call
 
+    // device memory of this session, zeroed on its stream. Every upload of initial data goes on the same stream
+    // (cudaMemcpyAsync: pageable sources are staged before the call returns), so a zeroing memset can never land
+    // after the data: the stream is non-blocking and is not ordered against the legacy default stream.
     void* dalloc(size_t n) {
         void* p = nullptr;
         CK(cudaMalloc(&p, std::max<size_t>(n, 256)));
@@ -395,16 +401,16 @@ struct FhSession {
         std::vector<uint16_t> packed(fhk_conv_packed_elems(L.cout, L.cp));
         if (fhk_conv_pack_weights(wb.data(), L.cin, L.cout, map.data(), L.cp, packed.data()) != 0) fail("%s: pack", name.c_str());
         L.wpack = alloc_n<uint16_t>(packed.size());
-        CK(cudaMemcpy(L.wpack, packed.data(), packed.size() * 2, cudaMemcpyHostToDevice));
+        CK(cudaMemcpyAsync(L.wpack, packed.data(), packed.size() * 2, cudaMemcpyHostToDevice, st));
         auto b = model->f32(bn);
         if ((int)b.size() != L.cout) fail("%s: bias size", bn.c_str());
         L.bias = alloc_n<float>(L.cout);
-        CK(cudaMemcpy(L.bias, b.data(), L.cout * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpyAsync(L.bias, b.data(), L.cout * 4, cudaMemcpyHostToDevice, st));
         if (act) {
             auto s = model->f32(name + ".1.weight");
             if ((int)s.size() != L.cout) fail("%s: slope size", name.c_str());
             L.slope = alloc_n<float>(L.cout);
-            CK(cudaMemcpy(L.slope, s.data(), L.cout * 4, cudaMemcpyHostToDevice));
+            CK(cudaMemcpyAsync(L.slope, s.data(), L.cout * 4, cudaMemcpyHostToDevice, st));
         }
         return L;
     }
@@ -507,7 +513,7 @@ struct FhSession {
             fail("film.film: shapes do not match (hidden %d, 2 x %d outputs)", film_hidden, cr);
         auto up = [&](const std::vector<float>& v) {
             float* d = alloc_n<float>(v.size());
-            CK(cudaMemcpy(d, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+            CK(cudaMemcpyAsync(d, v.data(), v.size() * 4, cudaMemcpyHostToDevice, st));
             return d;
         };
         film_w1 = up(w1);
@@ -523,7 +529,9 @@ struct FhSession {
             mask = alloc_n<uint8_t>((size_t)hp * wp);
             state = alloc_n<uchar4>((size_t)hp * wp);
             age = alloc_n<int16_t>((size_t)hp * wp);
+            nearp = alloc_n<uint8_t>((size_t)hp * wp);
         }
+        if (still) dsum = alloc_n<float>((size_t)hp * wp);
         cv = img(h16, w16, 56);
         ch1 = img(h16, w16, CCP);
         ch2 = img(h16, w16, CCP);
@@ -557,6 +565,7 @@ struct FhSession {
 
     // ---- stages ----
     void run_frame(FrameSet& s) {
+        CK(fhk::frame_half(s.frame, 0, w, h, s.half, 0, 1, st));
         CK(fhk::frame_to_input(s.frame, 0, w, h, hp, wp, internal, ihp, iwp, {s.A, 0}, 1, st));
         CK(fhk::input_pyramid({s.A, 0}, NH, NW, {s.aq, 0}, {s.i8, 0}, {s.i16, 0}, 1, st));
         conv("e1", {s.aq}, qh, qw, e1, C8P);
@@ -566,9 +575,10 @@ struct FhSession {
     }
 
     void run_pair(const FrameSet& A, const FrameSet& B) {
+        if (protects || still) CK(fhk::pair_planes(A.frame, B.frame, sargs, protects ? changed : nullptr, still ? dsum : nullptr, st));
         if (protects) {
-            CK(fhk::static_changed(A.frame, B.frame, sargs, changed, st));
             CK(fhk::static_age(A.frame, B.frame, changed, mask, sargs, state, age, st));
+            CK(fhk::static_near(age, wp, hp, min_age, nearp, st));
         }
         // coarse: img16 = (i16a, i16b), luma, sad r3 (graph ops 18-25), then c1..head (26-32)
         CK(fhk::sad_volume(A.i16, 4, B.i16, 4, 0, h16, w16, 3, cv, 56, 0, 1, st));
@@ -610,8 +620,9 @@ struct FhSession {
         conv("q2", {rq1}, qh, qw, rq2, CQP);
         conv("q3", {rq2}, qh, qw, rq3, CQP);
         conv("q4", {rq3}, qh, qw, rt, 4, nullptr, 0, 1);
-        fhk::RenderArgs ra{p.a->frame, p.b->frame, 0, w, h, hp, wp, up7, 0, rt, 0, qh, qw, fsx, fsy, cubic ? 1 : 0,
-                           (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, 0, min_age, out, 0};
+        fhk::RenderArgs ra{p.a->half, p.b->half, 0, w, h, hp, wp, up7, 0, rt, 0, qh, qw, fsx, fsy, cubic ? 1 : 0,
+                           (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, 0, dsum, nearp, 0,
+                           min_age, out, 0};
         CK(fhk::render(ra, 1, st));
     }
 
@@ -698,6 +709,7 @@ struct FhSession {
     FrameSet* new_set() {
         auto fs = std::make_unique<FrameSet>();
         fs->frame = alloc_n<uint8_t>((size_t)w * h * 4);
+        fs->half = alloc_n<__half>((size_t)w * h * 4);
         fs->A = img(NH, NW, 4);
         fs->aq = img(qh, qw, 4);
         fs->i8 = img(h8, w8, 4);
@@ -735,6 +747,15 @@ struct FhSession {
 };
 
 namespace {
+
+// an environment variable equal to `v` after trimming whitespace
+bool env_is(const char* name, const char* v) {
+    const char* e = getenv(name);
+    if (!e) return false;
+    std::string t(e);
+    const size_t a = t.find_first_not_of(" \t\r\n"), b = t.find_last_not_of(" \t\r\n");
+    return a != std::string::npos && t.substr(a, b - a + 1) == v;
+}
 
 // options.rs:348-356
 void default_internal(int w, int h, int& iw, int& ih) {
@@ -790,8 +811,10 @@ void derive(const FhModel* m, const FhSessionOptions& o, FhSession* s) {
     s->k = (int)o.k;
     s->repair = o.keep_maps ? std::max(1, (int)o.repair) : (int)o.repair;
     s->cubic = o.render == 0 ? m->cubic : o.render == 2;
-    s->still = true;     // options.rs:296-298 (FH_STILL default on)
-    s->decisive = false; // options.rs:277-280 (FH_BLEND default off)
+    // options.rs:277-280 and :296-298: the still test is on unless FH_STILL=0, the decisive blend off unless
+    // FH_BLEND=decisive (read when the session is built, as the reference's NetOpts are)
+    s->still = !env_is("FH_STILL", "0");
+    s->decisive = env_is("FH_BLEND", "decisive");
     const bool keep_static = o.keep_static != 0;
     s->protects = keep_static || o.protection_mask;
     const int frames = keep_static ? std::clamp((int)(o.static_frames ? o.static_frames : 8), 1, 255) : 2;

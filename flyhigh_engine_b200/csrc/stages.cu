@@ -5,7 +5,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cooperative_groups.h>
+
 #include "fh_device.cuh"
+#include "fh_kernels.h"
 #include "stages.h"
 
 namespace fhk {
@@ -157,9 +160,13 @@ FH_DEV float diff3(uint32_t a, uint32_t b, const float* lut) {
     return d;
 }
 
-// keep_static_age.wgsl:52-56 `diff(o) >= thr` for every pixel of the padded plane (a, b read at the clamped position)
-__global__ void k_static_changed(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb, StaticArgs s,
-                                 uint8_t* changed) {
+// The per-pair planes over the padded plane (a, b read at the clamped position):
+//  - changed = keep_static_age.wgsl:52-56 `diff(o) >= thr` (the age pass probes it 41 times per pixel);
+//  - dsum = sum over the 3 channels of |A - B|, the still test's per-pixel term (render.wgsl:136-143). Each |A - B| is
+//    a multiple of 2^-18 below 1 (f16 values of b / 255), so these sums and the render's 3 x 3 sum of them are exact
+//    in f32 and equal to the shader's 27-term running sum whatever the order.
+__global__ void k_pair_planes(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb, StaticArgs s,
+                              uint8_t* changed, float* dsum) {
     __shared__ float lut[256];
     for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
     __syncthreads();
@@ -168,7 +175,27 @@ __global__ void k_static_changed(const uint8_t* __restrict__ fa, const uint8_t* 
     const long long src = (long long)min(y, s.h - 1) * s.w + min(x, s.w - 1);
     const uint32_t a = __ldg(reinterpret_cast<const uint32_t*>(fa) + src);
     const uint32_t b = __ldg(reinterpret_cast<const uint32_t*>(fb) + src);
-    changed[(long long)y * s.wp + x] = diff3(a, b, lut) >= s.thr ? 1 : 0;
+    const long long o = (long long)y * s.wp + x;
+    if (changed) changed[o] = diff3(a, b, lut) >= s.thr ? 1 : 0;
+    if (dsum) {
+        float d = 0.0f;
+        for (int c = 0; c < 3; c++) {
+            const int sh = 16 - 8 * c;
+            d = d + fabsf(lut[(a >> sh) & 255] - lut[(b >> sh) & 255]);
+        }
+        dsum[o] = d;
+    }
+}
+
+// render_static's on_static (gpu/pipeline.rs:10-34) per pixel: an age >= min_age in the clamped 3 x 3 neighbourhood
+__global__ void k_static_near(const int16_t* __restrict__ age, int W, int H, float min_age, uint8_t* near) {
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
+    if (x >= W || y >= H) return;
+    bool hit = false;
+    for (int dy = -1; dy <= 1; dy++)
+        for (int dx = -1; dx <= 1; dx++)
+            hit |= (float)age[(long long)clampi(y + dy, 0, H - 1) * W + clampi(x + dx, 0, W - 1)] >= min_age;
+    near[(long long)y * W + x] = hit ? 1 : 0;
 }
 
 // keep_static_age.wgsl:59-77: 9 near + 32 far probes of `changed`, the spread test, the state machine (decide, :28-36)
@@ -319,94 +346,114 @@ FH_DEV float bil_mix(float v00, float v01, float v10, float v11, float ax, float
     return top * (1.0f - ay) + bot * ay;
 }
 
-// warp.wgsl of the fine loop: one thread per e8 pixel writes wa, wb, ia, ib (all channels)
+// warp.wgsl of the fine loop: one thread per e8 pixel writes wa, wb, ia, ib (all channels). The four corners of a
+// side are read as 16-byte vectors before anything is stored.
 __global__ void k_warp_fine(WarpFineArgs a) {
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (x >= a.w8 || y >= a.h8) return;
-    const __half* fv = a.fv + (long long)n * a.fv_bs + ((long long)y * a.w8 + x) * 8;
-    __half* o = a.wbuf + (long long)n * a.wbuf_bs + ((long long)y * a.w8 + x) * 88;
+    const uint4 fvv = __ldg(reinterpret_cast<const uint4*>(a.fv + (long long)n * a.fv_bs + ((long long)y * a.w8 + x) * 8));
+    const __half* fv = reinterpret_cast<const __half*>(&fvv);
+    __half* __restrict__ o = a.wbuf + (long long)n * a.wbuf_bs + ((long long)y * a.w8 + x) * 88;
+    const int nv = (a.c8 + 7) / 8;  // 16-byte vectors per f8 pixel (c8 <= 40)
     for (int side = 0; side < 2; side++) {
         // flow8f = flow[0:2] * 0.125 (the view scale, applied in f32: warp.wgsl:17-18)
         const float fx = h2f(fv[2 * side]) * 0.125f, fy = h2f(fv[2 * side + 1]) * 0.125f;
         const Bil b = bil_at(x, y, fx, fy, a.h8, a.w8);
-        const __half* f8 = (side ? a.f8b : a.f8a) + (long long)n * a.f8_bs;
-        __half* ow = o + side * 40;
-        for (int c = 0; c < a.c8; c++) {
-            const float v = bil_mix(h2f(f8[b.i00 * a.f8_cs + c]), h2f(f8[b.i01 * a.f8_cs + c]), h2f(f8[b.i10 * a.f8_cs + c]),
-                                    h2f(f8[b.i11 * a.f8_cs + c]), b.ax, b.ay);
-            ow[c] = f2h(v * 1.0f);
+        const __half* __restrict__ f8 = (side ? a.f8b : a.f8a) + (long long)n * a.f8_bs;
+        const long long idx[4] = {b.i00, b.i01, b.i10, b.i11};
+        for (int v = 0; v < nv; v++) {
+            uint4 c4[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) c4[k] = __ldg(reinterpret_cast<const uint4*>(f8 + idx[k] * a.f8_cs) + v);
+            __half r[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const int c = v * 8 + e;
+                const float val = bil_mix(h2f(reinterpret_cast<const __half*>(&c4[0])[e]), h2f(reinterpret_cast<const __half*>(&c4[1])[e]),
+                                          h2f(reinterpret_cast<const __half*>(&c4[2])[e]), h2f(reinterpret_cast<const __half*>(&c4[3])[e]),
+                                          b.ax, b.ay);
+                r[e] = c < a.c8 ? f2h(val * 1.0f) : f2h(0.0f);
+            }
+            *reinterpret_cast<uint4*>(o + side * 40 + v * 8) = *reinterpret_cast<uint4*>(r);
         }
-        for (int c = a.c8; c < 40; c++) ow[c] = f2h(0.0f);
-        const __half* im = (side ? a.i8b.p + (long long)n * a.i8b.bs : a.i8a.p + (long long)n * a.i8a.bs);
-        float v[3];
-        for (int c = 0; c < 3; c++)
-            v[c] = bil_mix(h2f(im[b.i00 * 4 + c]), h2f(im[b.i01 * 4 + c]), h2f(im[b.i10 * 4 + c]), h2f(im[b.i11 * 4 + c]),
-                           b.ax, b.ay) * 1.0f;
-        st4(o + 80 + side * 4, v[0], v[1], v[2]);
+        for (int v = nv; v < 5; v++) *reinterpret_cast<uint4*>(o + side * 40 + v * 8) = make_uint4(0, 0, 0, 0);
+        const __half* __restrict__ im = (side ? a.i8b.p + (long long)n * a.i8b.bs : a.i8a.p + (long long)n * a.i8a.bs);
+        float c3[4][3];
+#pragma unroll
+        for (int k = 0; k < 4; k++) ld4(im + idx[k] * 4, c3[k][0], c3[k][1], c3[k][2]);
+        float v3[3];
+        for (int c = 0; c < 3; c++) v3[c] = bil_mix(c3[0][c], c3[1][c], c3[2][c], c3[3][c], b.ax, b.ay) * 1.0f;
+        st4(o + 80 + side * 4, v3[0], v3[1], v3[2]);
     }
 }
 
 // ----------------------------------------------------------------------------------------------------- GMHS ----
 
-// gm_fit_reduce.wgsl + gm_fit_solve.wgsl, 4 IRLS iterations in one CTA of 1024 threads. The reduction reproduces the
-// shader's: 32 workgroups x 256 threads, each thread a strided partial sum, a 256-wide tree per workgroup
-// (off = 128 .. 1), then the solve's sequential sum over workgroups. One warp reduces one (workgroup, channel).
-__global__ void __launch_bounds__(1024) k_gm_fit(GmArgs g) {
+// gm_fit_reduce.wgsl + gm_fit_solve.wgsl, 4 IRLS iterations in one thread-block cluster of 8 CTAs x 16 warps. The
+// reduction reproduces the shader's: 32 workgroups x 256 threads, each thread a strided partial sum, a 256-wide tree
+// per workgroup (off = 128 .. 1), then the solve's sequential sum over workgroups. One warp reduces one
+// (workgroup, channel) pair: lane l holds virtual threads l + 32 k, k = 0..7; the 128 warps of the cluster cover the 32
+// workgroups x 4 channels at once and write their partials into CTA 0's shared memory (distributed shared memory);
+// CTA 0 solves and broadcasts the coefficients to every CTA of the cluster.
+constexpr int GM_CLUSTER = 8;
+__global__ void __cluster_dims__(GM_CLUSTER, 1, 1) __launch_bounds__(512, 1) k_gm_fit(GmArgs g) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
     __shared__ float part[32][4][9];
     __shared__ float coef[16];
-    const int n = blockIdx.x;
+    const unsigned rank = cluster.block_rank();
+    const int n = blockIdx.x / GM_CLUSTER;
     const __half* fl = g.fv + (long long)n * g.fv_bs;
     const int w8 = g.w8, h8 = g.h8, np = h8 * w8;
     const float sx = 2.0f / (float)max(w8 - 1, 1), sy = 2.0f / (float)max(h8 - 1, 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int task = (int)rank * 16 + warp;  // 0..127
+    const int wg = task >> 2, c = task & 3;
+    float* part0 = cluster.map_shared_rank(&part[0][0][0], 0);
     if (threadIdx.x < 16) coef[threadIdx.x] = 0.0f;
-    __syncthreads();
+    cluster.sync();
     for (int it = 0; it < 4; it++) {
-        for (int task = warp; task < 32 * 4; task += 32) {
-            const int wg = task >> 2, c = task & 3;
-            // 8 tree inputs per lane: virtual threads t = lane + 32 k, k = 0..7
-            float v[8][9];
+        float v[8][9];
 #pragma unroll
-            for (int k = 0; k < 8; k++) {
-                float s[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
-                for (int i = wg * 256 + lane + 32 * k; i < np; i += 256 * 32) {
-                    const int yy = i / w8, xx = i - yy * w8;
-                    const float x = -1.0f + sx * (float)xx, y = -1.0f + sy * (float)yy;
-                    const float f = h2f(fl[(long long)i * 8 + c]);
-                    float w2 = 1.0f;
-                    if (it > 0) {
-                        const float r = fabsf(f - (coef[c * 4] + coef[c * 4 + 1] * x + coef[c * 4 + 2] * y));
-                        w2 = g.delta / fmaxf(g.delta, r);
-                    }
-                    s[0] = s[0] + w2;
-                    s[1] = s[1] + w2 * x;
-                    s[2] = s[2] + w2 * y;
-                    s[3] = s[3] + w2 * x * x;
-                    s[4] = s[4] + w2 * x * y;
-                    s[5] = s[5] + w2 * y * y;
-                    s[6] = s[6] + w2 * f;
-                    s[7] = s[7] + w2 * x * f;
-                    s[8] = s[8] + w2 * y * f;
+        for (int k = 0; k < 8; k++) {
+            float s0 = 0, s1 = 0, s2 = 0, s3 = 0, s4 = 0, s5 = 0, s6 = 0, s7 = 0, s8 = 0;
+            for (int i = wg * 256 + lane + 32 * k; i < np; i += 256 * 32) {
+                const int yy = i / w8, xx = i - yy * w8;
+                const float x = -1.0f + sx * (float)xx, y = -1.0f + sy * (float)yy;
+                const float f = h2f(fl[(long long)i * 8 + c]);
+                float w2 = 1.0f;
+                if (it > 0) {
+                    const float r = fabsf(f - (coef[c * 4] + coef[c * 4 + 1] * x + coef[c * 4 + 2] * y));
+                    w2 = g.delta / fmaxf(g.delta, r);
                 }
-#pragma unroll
-                for (int q = 0; q < 9; q++) v[k][q] = s[q];
+                s0 = s0 + w2;
+                s1 = s1 + w2 * x;
+                s2 = s2 + w2 * y;
+                s3 = s3 + w2 * x * x;
+                s4 = s4 + w2 * x * y;
+                s5 = s5 + w2 * y * y;
+                s6 = s6 + w2 * f;
+                s7 = s7 + w2 * x * f;
+                s8 = s8 + w2 * y * f;
             }
-#pragma unroll
-            for (int q = 0; q < 9; q++) {
-                // off 128: t += t + 128 (k += k + 4); off 64: k += k + 2; off 32: k += k + 1
-                const float a0 = v[0][q] + v[4][q], a1 = v[1][q] + v[5][q], a2 = v[2][q] + v[6][q], a3 = v[3][q] + v[7][q];
-                const float b0 = a0 + a2, b1 = a1 + a3;
-                float s = b0 + b1;
-                for (int off = 16; off > 0; off >>= 1) s = s + __shfl_down_sync(0xffffffffu, s, off);
-                if (lane == 0) part[wg][c][q] = s;
-            }
+            v[k][0] = s0; v[k][1] = s1; v[k][2] = s2; v[k][3] = s3; v[k][4] = s4;
+            v[k][5] = s5; v[k][6] = s6; v[k][7] = s7; v[k][8] = s8;
         }
-        __syncthreads();
-        if (threadIdx.x < 4) {
-            const int c = threadIdx.x;
+#pragma unroll
+        for (int q = 0; q < 9; q++) {
+            // off 128: t += t + 128 (k += k + 4); off 64: k += k + 2; off 32: k += k + 1; then 16 .. 1 in the warp
+            const float a0 = v[0][q] + v[4][q], a1 = v[1][q] + v[5][q], a2 = v[2][q] + v[6][q], a3 = v[3][q] + v[7][q];
+            const float b0 = a0 + a2, b1 = a1 + a3;
+            float sum = b0 + b1;
+            for (int off = 16; off > 0; off >>= 1) sum = sum + __shfl_down_sync(0xffffffffu, sum, off);
+            if (lane == 0) part0[(wg * 4 + c) * 9 + q] = sum;
+        }
+        cluster.sync();
+        if (rank == 0 && threadIdx.x < 4) {
+            const int cc = threadIdx.x;
             float s[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
-            for (int wg = 0; wg < 32; wg++)
-                for (int k = 0; k < 9; k++) s[k] = s[k] + part[wg][c][k];
+            for (int w = 0; w < 32; w++)
+                for (int k = 0; k < 9; k++) s[k] = s[k] + part[w][cc][k];
             const float m00 = s[0] + 1e-6f, m01 = s[1], m02 = s[2], m11 = s[3] + 1e-6f, m12 = s[4], m22 = s[5] + 1e-6f;
             const float det = m00 * (m11 * m22 - m12 * m12) - m01 * (m01 * m22 - m12 * m02) + m02 * (m01 * m12 - m11 * m02);
             float c0, c1, c2;
@@ -421,14 +468,17 @@ __global__ void __launch_bounds__(1024) k_gm_fit(GmArgs g) {
                 c1 = i01 * s[6] + i11 * s[7] + i12 * s[8];
                 c2 = i02 * s[6] + i12 * s[7] + i22 * s[8];
             }
-            coef[c * 4] = c0;
-            coef[c * 4 + 1] = c1;
-            coef[c * 4 + 2] = c2;
-            coef[c * 4 + 3] = 0.0f;
+            for (unsigned r = 0; r < GM_CLUSTER; r++) {
+                float* cr = cluster.map_shared_rank(coef, r);
+                cr[cc * 4] = c0;
+                cr[cc * 4 + 1] = c1;
+                cr[cc * 4 + 2] = c2;
+                cr[cc * 4 + 3] = 0.0f;
+            }
         }
-        __syncthreads();
+        cluster.sync();
     }
-    if (threadIdx.x < 16) g.coef[n * 16 + threadIdx.x] = coef[threadIdx.x];
+    if (rank == 0 && threadIdx.x < 16) g.coef[n * 16 + threadIdx.x] = coef[threadIdx.x];
 }
 
 // gm_cost.wgsl:15-75
@@ -549,9 +599,29 @@ __global__ void k_film(FilmArgs a) {
     __syncthreads();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
     if (x >= a.w8 || y >= a.h8) return;
-    const __half* h = a.h + (long long)n * a.h_bs + ((long long)y * a.w8 + x) * a.h_cs;
-    __half* o = a.hm + (long long)n * a.hm_bs + ((long long)y * a.w8 + x) * a.hm_cs;
-    for (int c = 0; c < a.cr; c++) o[c] = f2h(h2f(h[c]) * (1.0f + gv[c]) + gv[c + a.cr]);
+    const __half* __restrict__ h = a.h + (long long)n * a.h_bs + ((long long)y * a.w8 + x) * a.h_cs;
+    __half* __restrict__ o = a.hm + (long long)n * a.hm_bs + ((long long)y * a.w8 + x) * a.hm_cs;
+    // the hidden state in 16-byte vectors (cr is a multiple of 8 in this graph; a tail is done per channel)
+    const int nv = a.cr / 8;
+    for (int v0 = 0; v0 < nv; v0 += 3) {
+        uint4 in[3];
+#pragma unroll
+        for (int u = 0; u < 3; u++)
+            if (v0 + u < nv) in[u] = __ldg(reinterpret_cast<const uint4*>(h) + v0 + u);
+#pragma unroll
+        for (int u = 0; u < 3; u++) {
+            if (v0 + u >= nv) break;
+            const __half* hi = reinterpret_cast<const __half*>(&in[u]);
+            __half r[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const int c = (v0 + u) * 8 + e;
+                r[e] = f2h(h2f(hi[e]) * (1.0f + gv[c]) + gv[c + a.cr]);
+            }
+            *(reinterpret_cast<uint4*>(o) + v0 + u) = *reinterpret_cast<uint4*>(r);
+        }
+    }
+    for (int c = nv * 8; c < a.cr; c++) o[c] = f2h(h2f(h[c]) * (1.0f + gv[c]) + gv[c + a.cr]);
 }
 
 __global__ void k_mid_combine(const float* tt, const __half* __restrict__ fv, long long fv_bs, const __half* __restrict__ d,
@@ -681,22 +751,27 @@ FH_DEV float cub2(float x) {
     return ((a * x - 5.0f * a) * x + 8.0f * a) * x - 4.0f * a;
 }
 
+// a source frame as its f16 plane (w x h x 4 halves: B, G, R, 0 = the values tex_in.wgsl stores), read at the
+// clamped position (the replicate padding of the [3][hp][wp] tensor)
 struct Frame {
-    const uint32_t* p;
+    const uint2* p;
     int w, h;
-    FH_DEV uint32_t at(int y, int x) const { return __ldg(p + (long long)min(y, h - 1) * w + min(x, w - 1)); }
+    FH_DEV float3 at(int y, int x) const {
+        const uint2 u = __ldg(p + (long long)min(y, h - 1) * w + min(x, w - 1));
+        const float2 bg = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+        const float2 r0 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+        return make_float3(bg.x, bg.y, r0.x);
+    }
 };
+FH_DEV float comp(const float3& v, int c) { return c == 0 ? v.x : (c == 1 ? v.y : v.z); }
 
 // render.wgsl:82-161 + gpu/pipeline.rs:10-34 (static rules) + keep_static.wgsl:21-32 + rgba_out.wgsl:9-17
 __global__ void __launch_bounds__(256) k_render(RenderArgs r) {
-    __shared__ float lut[256];
-    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
-    __syncthreads();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (x >= r.w || y >= r.h) return;
     const int H = r.hp, W = r.wp, hq = r.hq, wq = r.wq;
-    const Frame A{reinterpret_cast<const uint32_t*>(r.fa + (long long)n * r.f_bs), r.w, r.h};
-    const Frame B{reinterpret_cast<const uint32_t*>(r.fb + (long long)n * r.f_bs), r.w, r.h};
+    const Frame A{reinterpret_cast<const uint2*>(r.ha + (long long)n * r.h_bs), r.w, r.h};
+    const Frame B{reinterpret_cast<const uint2*>(r.hb + (long long)n * r.h_bs), r.w, r.h};
     const __half* up = r.up7 + (long long)n * r.up_bs;
     const __half* rt = r.rt + (long long)n * r.rt_bs;
     const int16_t* age = r.age ? r.age + (long long)n * r.age_bs : nullptr;
@@ -707,10 +782,15 @@ __global__ void __launch_bounds__(256) k_render(RenderArgs r) {
     const float qfy = iy - (float)qy0, qfx = ix - (float)qx0;
     const int qy0c = clampi(qy0, 0, hq - 1), qy1c = clampi(qy0 + 1, 0, hq - 1);
     const int qx0c = clampi(qx0, 0, wq - 1), qx1c = clampi(qx0 + 1, 0, wq - 1);
-    const __half* u00 = up + ((long long)qy0c * wq + qx0c) * 8;
-    const __half* u01 = up + ((long long)qy0c * wq + qx1c) * 8;
-    const __half* u10 = up + ((long long)qy1c * wq + qx0c) * 8;
-    const __half* u11 = up + ((long long)qy1c * wq + qx1c) * 8;
+    // the four Q corners: flow_tq (0-3) and vis_tq (4-6) in one 16-byte load each, R_t in one 8-byte load each
+    const uint4 U00 = __ldg(reinterpret_cast<const uint4*>(up + ((long long)qy0c * wq + qx0c) * 8));
+    const uint4 U01 = __ldg(reinterpret_cast<const uint4*>(up + ((long long)qy0c * wq + qx1c) * 8));
+    const uint4 U10 = __ldg(reinterpret_cast<const uint4*>(up + ((long long)qy1c * wq + qx0c) * 8));
+    const uint4 U11 = __ldg(reinterpret_cast<const uint4*>(up + ((long long)qy1c * wq + qx1c) * 8));
+    const __half* u00 = reinterpret_cast<const __half*>(&U00);
+    const __half* u01 = reinterpret_cast<const __half*>(&U01);
+    const __half* u10 = reinterpret_cast<const __half*>(&U10);
+    const __half* u11 = reinterpret_cast<const __half*>(&U11);
     float f[4], v[3];
     for (int c = 0; c < 4; c++)
         f[c] = bil_mix(h2f(u00[c]), h2f(u01[c]), h2f(u10[c]), h2f(u11[c]), qfx, qfy) * ((c & 1) == 0 ? r.fsx : r.fsy);
@@ -721,7 +801,7 @@ __global__ void __launch_bounds__(256) k_render(RenderArgs r) {
     const float wa_w = (e0 + 0.5f * e2) / s, wb_w = (e1 + 0.5f * e2) / s;
     const float gxa = (float)x + f[0], gya = (float)y + f[1], gxb = (float)x + f[2], gyb = (float)y + f[3];
     float ca[3], cb[3], cr[3];
-    auto chan = [&](uint32_t px, int c) { return lut[(px >> (16 - 8 * c)) & 255]; };  // BGR channel c of rgba
+    // bicubic (Keys a = -0.75, per-tap clamp) or bilinear sampling of a source frame; continuous sums, fused
     auto sample = [&](const Frame& F, float gx, float gy, float* out) {
         if (r.cubic) {
             const int px = (int)floorf(gx), py = (int)floorf(gy);
@@ -730,45 +810,53 @@ __global__ void __launch_bounds__(256) k_render(RenderArgs r) {
             const float cy[4] = {cub2(ty + 1.0f), cub1(ty), cub1(1.0f - ty), cub2(2.0f - ty)};
             int xs[4];
             for (int k = 0; k < 4; k++) xs[k] = clampi(px - 1 + k, 0, W - 1);
-            float acc[3] = {0.0f, 0.0f, 0.0f};
+            float3 acc = make_float3(0.0f, 0.0f, 0.0f);
             for (int j = 0; j < 4; j++) {
                 const int yy = clampi(py - 1 + j, 0, H - 1);
-                const uint32_t p0 = F.at(yy, xs[0]), p1 = F.at(yy, xs[1]), p2 = F.at(yy, xs[2]), p3 = F.at(yy, xs[3]);
-                for (int c = 0; c < 3; c++) {
-                    const float row = chan(p0, c) * cx[0] + chan(p1, c) * cx[1] + chan(p2, c) * cx[2] + chan(p3, c) * cx[3];
-                    acc[c] = j == 0 ? row * cy[0] : acc[c] + row * cy[j];
-                }
+                const float3 p0 = F.at(yy, xs[0]), p1 = F.at(yy, xs[1]), p2 = F.at(yy, xs[2]), p3 = F.at(yy, xs[3]);
+                float3 row;
+                row.x = fmaf(p3.x, cx[3], fmaf(p2.x, cx[2], fmaf(p1.x, cx[1], p0.x * cx[0])));
+                row.y = fmaf(p3.y, cx[3], fmaf(p2.y, cx[2], fmaf(p1.y, cx[1], p0.y * cx[0])));
+                row.z = fmaf(p3.z, cx[3], fmaf(p2.z, cx[2], fmaf(p1.z, cx[1], p0.z * cx[0])));
+                acc.x = fmaf(row.x, cy[j], acc.x);
+                acc.y = fmaf(row.y, cy[j], acc.y);
+                acc.z = fmaf(row.z, cy[j], acc.z);
             }
-            for (int c = 0; c < 3; c++) out[c] = acc[c];
+            out[0] = acc.x;
+            out[1] = acc.y;
+            out[2] = acc.z;
         } else {
             const int xx0 = (int)floorf(gx), yy0 = (int)floorf(gy);
             const float ax = gx - (float)xx0, ay = gy - (float)yy0;
             const int x0 = clampi(xx0, 0, W - 1), x1 = clampi(xx0 + 1, 0, W - 1);
             const int y0 = clampi(yy0, 0, H - 1), y1 = clampi(yy0 + 1, 0, H - 1);
-            const uint32_t p00 = F.at(y0, x0), p01 = F.at(y0, x1), p10 = F.at(y1, x0), p11 = F.at(y1, x1);
-            for (int c = 0; c < 3; c++) out[c] = bil_mix(chan(p00, c), chan(p01, c), chan(p10, c), chan(p11, c), ax, ay);
+            const float3 p00 = F.at(y0, x0), p01 = F.at(y0, x1), p10 = F.at(y1, x0), p11 = F.at(y1, x1);
+            for (int c = 0; c < 3; c++)
+                out[c] = bil_mix(comp(p00, c), comp(p01, c), comp(p10, c), comp(p11, c), ax, ay);
         }
     };
     sample(A, gxa, gya, ca);
     sample(B, gxb, gyb, cb);
-    const __half* r00 = rt + ((long long)qy0c * wq + qx0c) * 4;
-    const __half* r01 = rt + ((long long)qy0c * wq + qx1c) * 4;
-    const __half* r10 = rt + ((long long)qy1c * wq + qx0c) * 4;
-    const __half* r11 = rt + ((long long)qy1c * wq + qx1c) * 4;
+    const uint2 R00 = __ldg(reinterpret_cast<const uint2*>(rt + ((long long)qy0c * wq + qx0c) * 4));
+    const uint2 R01 = __ldg(reinterpret_cast<const uint2*>(rt + ((long long)qy0c * wq + qx1c) * 4));
+    const uint2 R10 = __ldg(reinterpret_cast<const uint2*>(rt + ((long long)qy1c * wq + qx0c) * 4));
+    const uint2 R11 = __ldg(reinterpret_cast<const uint2*>(rt + ((long long)qy1c * wq + qx1c) * 4));
+    const __half* r00 = reinterpret_cast<const __half*>(&R00);
+    const __half* r01 = reinterpret_cast<const __half*>(&R01);
+    const __half* r10 = reinterpret_cast<const __half*>(&R10);
+    const __half* r11 = reinterpret_cast<const __half*>(&R11);
     for (int c = 0; c < 3; c++) cr[c] = bil_mix(h2f(r00[c]), h2f(r01[c]), h2f(r10[c]), h2f(r11[c]), qfx, qfy);
     float bwa = wa_w, bwb = wb_w, rk = 1.0f, stillw = 0.0f, own[3] = {0.0f, 0.0f, 0.0f};
     const float third = 1.0f / 3.0f;
-    const uint32_t pa_here = A.at(y, x), pb_here = B.at(y, x);
+    const float3 pa_here = A.at(y, x), pb_here = B.at(y, x);
     if (r.flags & 2u) {
+        // the 27-term sum of |A - B| over the clamped 3 x 3 neighbourhood, from the per-pixel channel sums (exact)
+        const float* ds = r.dsum + (long long)n * r.plane_bs;
         float es = 0.0f;
         for (int dy = -1; dy <= 1; dy++)
-            for (int dx = -1; dx <= 1; dx++) {
-                const int yy = clampi(y + dy, 0, H - 1), xx = clampi(x + dx, 0, W - 1);
-                const uint32_t pa = A.at(yy, xx), pb = B.at(yy, xx);
-                for (int c = 0; c < 3; c++) es += fabsf(chan(pa, c) - chan(pb, c));
-            }
+            for (int dx = -1; dx <= 1; dx++) es += __ldg(ds + (long long)clampi(y + dy, 0, H - 1) * W + clampi(x + dx, 0, W - 1));
         es = es / 27.0f;
-        for (int c = 0; c < 3; c++) own[c] = 0.5f * (chan(pa_here, c) + chan(pb_here, c));
+        for (int c = 0; c < 3; c++) own[c] = 0.5f * (comp(pa_here, c) + comp(pb_here, c));
         const float ef = fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
         stillw = fminf(fmaxf((ef - es) / 0.04f, 0.0f), 1.0f) * (es < 0.03f ? 1.0f : 0.0f);
     }
@@ -783,8 +871,10 @@ __global__ void __launch_bounds__(256) k_render(RenderArgs r) {
     float raw = 0.0f;
     const long long o = (long long)y * W + x;
     if (age) {
+        const uint8_t* near = r.near + (long long)n * r.plane_bs;
         auto on_static = [&](float gx, float gy) {
             const int cx = (int)rintf(gx), cy = (int)rintf(gy);  // WGSL round(): half to even
+            if (cx >= 0 && cx < W && cy >= 0 && cy < H) return __ldg(near + (long long)cy * W + cx) != 0;
             for (int dy = -1; dy <= 1; dy++)
                 for (int dx = -1; dx <= 1; dx++)
                     if ((float)age[(long long)clampi(cy + dy, 0, H - 1) * W + clampi(cx + dx, 0, W - 1)] >= r.min_age) return true;
@@ -811,7 +901,7 @@ __global__ void __launch_bounds__(256) k_render(RenderArgs r) {
     for (int c = 0; c < 3; c++) {
         const float mixv = ca[c] * bwa + cb[c] * bwb + cr[c] * rk;
         float ov = fminf(fmaxf(mixv * (1.0f - stillw) + own[c] * stillw, 0.0f), 1.0f);
-        const float src = 0.5f * (chan(pa_here, c) + chan(pb_here, c));
+        const float src = 0.5f * (comp(pa_here, c) + comp(pb_here, c));
         if (age) ov = fminf(fmaxf(ov * (1.0f - raw) + src * raw, 0.0f), 1.0f);
         float hv = rh(ov);  // the render plane is f16
         if (kk > 0.0f) hv = rh(hv * (1.0f - kk) + src * kk);
@@ -823,6 +913,17 @@ __global__ void __launch_bounds__(256) k_render(RenderArgs r) {
 }
 
 __global__ void k_set_scalar(float* d, float v) { *d = v; }
+
+// tex_in.wgsl's values for the whole frame: f16(byte / 255) as B, G, R, 0 halves per pixel (unpadded)
+__global__ void k_frame_half(const uint8_t* __restrict__ f, long long f_bs, int w, int h, __half* out, long long o_bs) {
+    __shared__ float lut[256];
+    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
+    __syncthreads();
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
+    if (x >= w || y >= h) return;
+    const uint32_t v = __ldg(reinterpret_cast<const uint32_t*>(f + (long long)n * f_bs) + (long long)y * w + x);
+    st4(out + (long long)n * o_bs + ((long long)y * w + x) * 4, lut[(v >> 16) & 255], lut[(v >> 8) & 255], lut[v & 255]);
+}
 
 __global__ void k_frame_planes(const uint8_t* f, int w, int h, int hp, int wp, float* out) {
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
@@ -852,8 +953,14 @@ cudaError_t input_pyramid(Img4 A, int ih, int iw, Img4 aq, Img4 i8, Img4 i16, in
     return cudaGetLastError();
 }
 
-cudaError_t static_changed(const uint8_t* fa, const uint8_t* fb, const StaticArgs& s, uint8_t* changed, cudaStream_t st) {
-    k_static_changed<<<grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st>>>(fa, fb, s, changed);
+cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, const StaticArgs& s, uint8_t* changed, float* dsum,
+                        cudaStream_t st) {
+    k_pair_planes<<<grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st>>>(fa, fb, s, changed, dsum);
+    return cudaGetLastError();
+}
+
+cudaError_t static_near(const int16_t* age, int wp, int hp, float min_age, uint8_t* near, cudaStream_t st) {
+    k_static_near<<<grid2(wp, hp, 1, 32, 8), dim3(32, 8), 0, st>>>(age, wp, hp, min_age, near);
     return cudaGetLastError();
 }
 
@@ -885,7 +992,7 @@ cudaError_t warp_fine(const WarpFineArgs& a, int n, cudaStream_t st) {
 }
 
 cudaError_t gmhs(const GmArgs& g, int n, cudaStream_t st) {
-    k_gm_fit<<<n, 1024, 0, st>>>(g);
+    k_gm_fit<<<n * GM_CLUSTER, 512, 0, st>>>(g);
     k_gm_cost<<<grid2(g.wc, g.hc, n, 32, 8), dim3(32, 8), 0, st>>>(g);
     const long long bs5 = 5LL * g.hc * g.wc, bs6 = 6LL * g.hc * g.wc;
     // maps and tmp have different batch strides: run the box passes per batch entry when n > 1
@@ -930,6 +1037,12 @@ cudaError_t render(const RenderArgs& r, int n, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+cudaError_t frame_half(const uint8_t* f, long long f_bs, int w, int h, __half* out, long long o_bs, int n,
+                       cudaStream_t st) {
+    k_frame_half<<<grid2(w, h, n, 32, 8), dim3(32, 8), 0, st>>>(f, f_bs, w, h, out, o_bs);
+    return cudaGetLastError();
+}
+
 cudaError_t set_scalar(float* dst, float v, cudaStream_t st) {
     k_set_scalar<<<1, 1, 0, st>>>(dst, v);
     return cudaGetLastError();
@@ -941,3 +1054,43 @@ cudaError_t frame_planes(const uint8_t* f, int w, int h, int hp, int wp, float* 
 }
 
 }  // namespace fhk
+
+// ---- the kernel-level C ABI of the repair stage (include/flyhigh_kernels.h) ----
+
+extern "C" size_t fhk_gmhs_scratch_floats(int h, int w) {
+    const size_t cells = (size_t)((h + 1) / 2) * ((w + 1) / 2);
+    return 16 + 11 * cells;
+}
+
+// gmhs.rs:160-170 (DS = 2) from the sizes, then the stage on the caller's scratch
+extern "C" int fhk_gmhs(const FhGmhsParams* p, void* stream) {
+    if (!p || !p->flow || !p->a || !p->b || !p->scratch || p->n < 1 || p->h8 < 1 || p->w8 < 1 || p->h < 2 || p->w < 2 ||
+        p->full_w < 2 || (p->level != 1 && p->level != 2))
+        return (int)cudaErrorInvalidValue;
+    if ((uintptr_t)p->a % 8 || (uintptr_t)p->b % 8 || (uintptr_t)p->flow % 16) return (int)cudaErrorMisalignedAddress;
+    fhk::GmArgs g{};
+    g.fv = p->flow;
+    g.fv_bs = p->flow_bs;
+    g.h8 = p->h8;
+    g.w8 = p->w8;
+    g.A = p->a;
+    g.B = p->b;
+    g.ab_bs = p->ab_bs;
+    g.h = p->h;
+    g.w = p->w;
+    g.hc = (p->h + 1) / 2;
+    g.wc = (p->w + 1) / 2;
+    const float sc = (float)p->w / ((float)p->full_w / 2.0f);
+    g.r_blk = (int)roundf(20.0f * sc / 2.0f);
+    g.r_dwin = (int)roundf(32.0f * sc / 2.0f);
+    if (g.r_blk < 1) g.r_blk = 1;
+    if (g.r_dwin < 1) g.r_dwin = 1;
+    g.dmin = p->level >= 2 ? 0.0f : 8.0f * sc;
+    g.delta = 1.5f * sc;
+    const size_t cells = (size_t)g.hc * g.wc;
+    // per batch entry: coef [n][16], maps [n][6][cells], tmp [n][5][cells]
+    g.coef = p->scratch;
+    g.maps = p->scratch + 16 * (size_t)p->n;
+    g.tmp = g.maps + 6 * cells * p->n;
+    return (int)fhk::gmhs(g, p->n, (cudaStream_t)stream);
+}

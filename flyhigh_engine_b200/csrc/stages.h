@@ -27,8 +27,11 @@ struct StaticArgs {
     float thr, min_age;
     int use_mask;
 };
-cudaError_t static_changed(const uint8_t* fa, const uint8_t* fb, const StaticArgs& s, uint8_t* changed,
-                           cudaStream_t st);
+// per pair: changed (diff >= thr, when protecting) and dsum (sum_c |A - B|, when the still test is on), padded plane
+cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, const StaticArgs& s, uint8_t* changed, float* dsum,
+                        cudaStream_t st);
+// per pair after the age pass: near = an age >= min_age in the clamped 3 x 3 neighbourhood (render_static on_static)
+cudaError_t static_near(const int16_t* age, int wp, int hp, float min_age, uint8_t* near, cudaStream_t st);
 cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, const uint8_t* changed, const uint8_t* mask,
                        const StaticArgs& s, uchar4* state, int16_t* age, cudaStream_t st);
 
@@ -103,8 +106,8 @@ cudaError_t refine_input(const __half* up7, long long up_bs, Img4 aq, Img4 bq, i
 // render.wgsl (+ the static variant, gpu/pipeline.rs:10-34) fused with keep_static.wgsl apply and tex_out.wgsl:
 // full-resolution render from the Q maps straight to rgba8, cropped to w x h
 struct RenderArgs {
-    const uint8_t *fa, *fb;  // source frames, w x h x 4
-    long long f_bs;
+    const __half *ha, *hb;   // source frames as f16 planes (frame_half), w x h x 4 halves
+    long long h_bs;
     int w, h, hp, wp;        // frame and padded plane
     const __half* up7;       // flow_tq (ch 0-3), vis_tq (ch 4-6), cs 8
     long long up_bs;
@@ -116,11 +119,18 @@ struct RenderArgs {
     unsigned flags;          // bit 0 decisive, bit 1 still test
     const int16_t* age;      // static age plane (padded), or null
     long long age_bs;
+    const float* dsum;       // pair_planes' dsum (when flags bit 1)
+    const uint8_t* near;     // static_near's plane (when age is set)
+    long long plane_bs;
     float min_age;
     uint8_t* out;            // w x h x 4
     long long out_bs;
 };
 cudaError_t render(const RenderArgs& r, int n, cudaStream_t st);
+
+// tex_in.wgsl's values of a frame as an unpadded f16 plane: w x h x (B, G, R, 0) halves
+cudaError_t frame_half(const uint8_t* f, long long f_bs, int w, int h, __half* out, long long o_bs, int n,
+                       cudaStream_t st);
 
 // a device scalar (the phase t of the mid stage) written on the stream
 cudaError_t set_scalar(float* dst, float v, cudaStream_t st);

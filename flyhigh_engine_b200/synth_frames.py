@@ -6,7 +6,7 @@ in for them:
   - pair_c0(): config 0, frame b = frame a under an integer global pan in [-12, 12]^2 plus 3 rectangles of 20..80 px
     that move independently by up to 24 px;
   - sequence_c2(): config 2, a moving sequence whose pan velocity random-walks by +-2 px per frame, with 5 moving
-    rectangles and a static 300 x 60 high-contrast HUD at the bottom-left.
+    rectangles and a static 300 x 60 high-contrast HUD overlay at the bottom-left (noise-free, like a rendered HUD).
 Every frame is (h, w, 4) uint8 with alpha 255.
 """
 from __future__ import annotations
@@ -95,9 +95,10 @@ def sequence_c2(n: int = 120, w: int = 1920, h: int = 1080, seed: int = 0, hud: 
             r["x"] += int(v[0])
             r["y"] += int(v[1])
             _paint(img, r)
-        if hud:
-            img[h - 60 - 20:h - 20, 20:320] = hud_img
-        frames.append(_finish(img, rng))
+        f = _finish(img, rng)
+        if hud:  # an overlay: composited after the sensor noise, identical in every frame
+            f[h - 60 - 20:h - 20, 20:320, :3] = hud_img.astype(np.uint8)
+        frames.append(f)
     return frames
 
 

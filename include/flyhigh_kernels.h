@@ -54,6 +54,7 @@ typedef struct FhConvParams {
     int n;                 /* batch */
     int wm;                /* warps along output rows (1, 2, 4; the other 4 / wm split K), 0 = chosen by size */
     int ngroups;           /* CTAs sharing one output tile, each a slice of the output channels; 0 = chosen */
+    int wsmem;             /* set by fhk_conv3x3: the weight slice is staged in shared memory */
 } FhConvParams;
 
 /* Replaces the conv family of the reference (ops/conv/kernels.rs:100-279: conv_tc / conv_direct / conv_tiled*,
@@ -65,6 +66,28 @@ int fhk_conv3x3(const FhConvParams* p, int stride, void* stream);
  * kernel's B-fragment order; map[pc] = model input channel of packed channel pc, or -1 (weight 0). */
 int fhk_conv_pack_weights(const uint16_t* w, int cin, int cout, const int* map, int cp, uint16_t* out);
 size_t fhk_conv_packed_elems(int cout, int cp);
+
+/* Periodic-structure repair of a pair's E8 flow (GMHS, crates/flyhigh-engine/src/gmhs.rs:155-219 with
+ * gm_fit_reduce / gm_fit_solve / gm_cost / gm_box / gm_select.wgsl): IRLS affine fit, cost maps on a 2x coarser grid,
+ * two box-filter windows, and the in-place rewrite of the flow where the affine hypothesis wins. */
+typedef struct FhGmhsParams {
+    fh_half* flow;        /* [n][h8][w8][8]: the flow in channels 0-3, rewritten in place */
+    long long flow_bs;
+    int h8, w8;
+    const fh_half* a;     /* [n][h][w][4] f16: the network-resolution inputs A and B (channels B, G, R, 0) */
+    const fh_half* b;
+    long long ab_bs;
+    int h, w;             /* network size */
+    int full_w;           /* padded full-frame width: the window radii scale with w / (full_w / 2) */
+    int level;            /* repair level 1 (safe) or 2 (aggressive) */
+    float* scratch;       /* fhk_gmhs_scratch_floats(h, w) floats per batch entry, on the device */
+    int n;                /* batch */
+} FhGmhsParams;
+
+/* Replaces gmhs::gm_steps and its dispatches (10 + 2 per window in the reference) with 7 launches. */
+int fhk_gmhs(const FhGmhsParams* p, void* stream);
+/* Scratch floats per batch entry: 16 coefficients + 6 + 5 cost maps of ceil(h / 2) x ceil(w / 2). */
+size_t fhk_gmhs_scratch_floats(int h, int w);
 
 #ifdef __cplusplus
 }

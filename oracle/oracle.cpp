@@ -903,6 +903,7 @@ struct Session {
     bool has_rop = false;
     fhjson::Value rop;
     std::vector<float> gm_maps;
+    T flow_pre;  // the E8 flow before the repair stage (GMHS rewrites it in place)
 };
 
 static std::map<std::string, int> count_uses(const std::vector<fhjson::Value>& ops) {
@@ -1180,7 +1181,11 @@ static void session_pair(Session* s, const uint8_t* ra, const uint8_t* rb) {
             f.c0 = 0;
             f.scale = 1.0f;
         }
-        if (f.buf && f.plain()) gm_run(env["A"], env["B"], f, s->wp, s->o.repair, &s->gm_maps);
+        if (f.buf && f.plain()) {
+            s->flow_pre = alloc(4, f.h, f.w);
+            std::copy(f.buf->d.begin(), f.buf->d.begin() + s->flow_pre.n(), s->flow_pre.buf->d.begin());
+            gm_run(env["A"], env["B"], f, s->wp, s->o.repair, &s->gm_maps);
+        }
     }
     s->env = env;
     s->have_pair = true;
@@ -1288,6 +1293,7 @@ long or_tensor(void* sp, int stage, const char* name, float* out, long cap, int*
     else if (n == "state") t = s->state;
     else if (n == "a") t = s->a;
     else if (n == "b") t = s->b;
+    else if (n == "flow_pre") t = s->flow_pre;
     else if (n == "render" && stage == 1) t = s->render;
     else {
         auto& e = stage == 0 ? s->env : s->mid_env;
@@ -1328,6 +1334,39 @@ void or_session_dims(void* sp, int* iv, float* fv) {
 }
 
 // ---- single kernels on caller planes (f16 bits), for per-kernel parity tests ----
+
+// The full-resolution render alone (render.wgsl + static variant, keep_static apply, rgba_out) on caller planes: frames
+// a, b (w x h rgba8), up7 [7][hq][wq] (flow_tq 0-3, vis_tq 4-6) and R_t [3][hq][wq] as f32 values of f16 tensors, age
+// [hp][wp] (or NULL: no static protection). fv: fsx, fsy, min_age, static_thr; iv: cubic, flags.
+int or_render_planes(const uint8_t* fa, const uint8_t* fb, int w, int h, const float* up7, const float* rt, int hq,
+                     int wq, const float* age, const float* fv, const int* iv, uint8_t* out) {
+    try {
+        const int hp = (h + 31) / 32 * 32, wp = (w + 31) / 32 * 32;
+        T A = alloc(3, hp, wp), B = alloc(3, hp, wp);
+        k_tex_in(fa, w, h, A);
+        k_tex_in(fb, w, h, B);
+        T up = alloc(7, hq, wq), r = alloc(3, hq, wq);
+        for (size_t i = 0; i < up.n(); i++) up.buf->d[i] = S(up7[i]);
+        for (size_t i = 0; i < r.n(); i++) r.buf->d[i] = S(rt[i]);
+        T ftq = up.view(0, 4), vtq = up.view(4, 7);
+        T ag;
+        if (age) {
+            ag = alloc(1, hp, wp);
+            for (size_t i = 0; i < ag.n(); i++) ag.buf->d[i] = S(age[i]);
+        }
+        RenderArgs ra{fv[0], fv[1], iv[0] != 0, (uint32_t)iv[1], age ? &ag : nullptr, fv[2]};
+        T o = k_render(A, B, ftq, vtq, r, ra);
+        if (age) {
+            StaticP sp{wp, hp, wp, hp, fv[3], fv[2], 0};
+            k_static_apply(ag, A, B, sp, o);
+        }
+        k_tex_out(o, w, h, out);
+        return 0;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
 
 // conv: x [cin][h][w], wt [cout][cin][3][3] f32, bias/slope [cout] f32 (slope NULL = identity), resid [cout][ho][wo]
 // or NULL; out [cout][ho][wo] f16 bits

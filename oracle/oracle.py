@@ -46,6 +46,9 @@ def lib():
         L.or_tensor.restype = c_long
         L.or_tensor.argtypes = [c_void_p, c_int, c_char_p, POINTER(c_float), c_long, POINTER(c_int)]
         L.or_session_dims.argtypes = [c_void_p, POINTER(c_int), POINTER(c_float)]
+        L.or_render_planes.argtypes = [POINTER(c_uint8), POINTER(c_uint8), c_int, c_int, POINTER(c_float),
+                                       POINTER(c_float), c_int, c_int, POINTER(c_float), POINTER(c_float),
+                                       POINTER(c_int), POINTER(c_uint8)]
         L.or_conv.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, POINTER(c_float), POINTER(c_float),
                               POINTER(c_float), c_int, c_int, POINTER(c_uint16), POINTER(c_uint16)]
         _lib = L
@@ -146,4 +149,23 @@ def conv(x: np.ndarray, w: np.ndarray, bias: np.ndarray, slope, stride: int, res
     u = lambda a: a.ctypes.data_as(POINTER(c_uint16))
     lib().or_conv(u(x), cin, h, wd, f(W), f(B), f(Sl) if Sl is not None else None, cout, stride,
                   u(R) if R is not None else None, u(out))
+    return out
+
+
+def render_planes(fa, fb, w, h, up7, rt, age, fsx, fsy, min_age, static_thr, cubic=True, flags=2):
+    """The render alone on given network outputs (up7 [7][hq][wq], R_t [3][hq][wq], age [hp][wp] or None)."""
+    fa = np.ascontiguousarray(fa, np.uint8)
+    fb = np.ascontiguousarray(fb, np.uint8)
+    up7 = np.ascontiguousarray(up7, np.float32)
+    rt = np.ascontiguousarray(rt, np.float32)
+    hq, wq = up7.shape[1], up7.shape[2]
+    ag = None if age is None else np.ascontiguousarray(age, np.float32)
+    fv = np.array([fsx, fsy, min_age, static_thr], np.float32)
+    iv = np.array([int(cubic), int(flags)], np.int32)
+    out = np.zeros(w * h * 4, np.uint8)
+    f = lambda a: a.ctypes.data_as(POINTER(c_float))
+    rc = lib().or_render_planes(_u8(fa), _u8(fb), w, h, f(up7), f(rt), hq, wq, f(ag) if ag is not None else None,
+                                f(fv), iv.ctypes.data_as(POINTER(c_int)), _u8(out))
+    if rc != 0:
+        raise RuntimeError(lib().or_error().decode())
     return out
