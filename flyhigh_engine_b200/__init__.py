@@ -94,6 +94,8 @@ EXPORTS = [
     ("fhk_conv_packed_elems", c_size_t, [c_int, c_int]),
     ("fhk_gmhs", c_int, [c_void_p, c_void_p]),
     ("fhk_gmhs_scratch_floats", c_size_t, [c_int, c_int]),
+    ("fhk_gmhs_noalloc", c_int, [c_void_p, c_void_p]),
+    ("fhk_gmhs_noalloc_max_floats", c_size_t, []),
 ]
 
 
