@@ -88,6 +88,7 @@ EXPORTS = [
     ("fh_session_debug_tensor", c_long, [c_void_p, c_char_p, POINTER(c_float), c_size_t, POINTER(c_int)]),
     ("fh_model_fingerprint", c_long, [c_void_p]),
     ("fh_session_plan_params", c_int, [c_void_p, POINTER(SessionOptions), POINTER(c_int), POINTER(c_float)]),
+    ("fh_session_advance_static", c_int, [c_void_p, c_uint32, c_uint32]),
     ("fh_session_launch_counts", c_int, [c_void_p, POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
     ("fhk_conv3x3", c_int, [c_void_p, c_int, c_void_p]),
     ("fhk_conv_pack_weights", c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
@@ -356,6 +357,10 @@ class Session:
         p = c_void_p()
         _check(lib().fh_session_slot_device_ptr(self._h, slot, int(output), byref(p)))
         return p.value
+
+    def advance_static(self, a: int, b: int) -> None:
+        """The static-protection state of the pair (a, b) without the network (see multi.py)."""
+        _check(lib().fh_session_advance_static(self._h, a, b))
 
     def launch_counts(self) -> dict:
         a, b, c = c_int(), c_int(), c_int()

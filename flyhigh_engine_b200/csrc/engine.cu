@@ -223,7 +223,9 @@ FhModel* model_from(const uint8_t* g, size_t gl, const uint8_t* m, size_t ml, co
             if (count > (1ull << 40) / (unsigned long long)d.num) fail("tensor %s: shape overflows", name.c_str());
             count *= (unsigned long long)d.num;
         }
-        unsigned long long end = ((unsigned long long)t["offset"].num + count) * 2;
+        const unsigned long long off = (unsigned long long)t["offset"].num;
+        if (off > (1ull << 60)) fail("tensor %s: offset overflows", name.c_str());
+        const unsigned long long end = (off + count) * 2;
         if (end > wl) fail("tensor %s runs past the end of the weight blob", name.c_str());
     }
     validate_ops(graph["ops"], mod->man["tensors"]);
@@ -1211,6 +1213,22 @@ int fh_session_write_rgba_device(const FhSession* cs, uint32_t slot, const void*
         const size_t n = (size_t)s->w * s->h * 4;
         if (len != n) fail("frame is %zu bytes, %dx%dx4 = %zu expected", len, s->w, s->h, n);
         CK(cudaMemcpyAsync(s->write_target(slot).frame, dev, n, cudaMemcpyDeviceToDevice, s->st));
+        return 0;
+    });
+}
+
+int fh_session_advance_static(const FhSession* cs, uint32_t a, uint32_t b) {
+    return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
+        if (!s) fail("null argument");
+        s->check_in(a);
+        s->check_in(b);
+        if (!s->protects) return 0;
+        // keep_static_age.wgsl on the two frames only: the state advances exactly as a pair() would advance it
+        const FrameSet& A = s->cur_set(a);
+        const FrameSet& B = s->cur_set(b);
+        CK(fhk::pair_planes(A.frame, B.frame, s->sargs, s->changed, nullptr, s->st));
+        CK(fhk::static_age(A.frame, B.frame, s->changed, s->mask, s->sargs, s->state, s->age, s->st));
         return 0;
     });
 }

@@ -49,7 +49,7 @@ struct Value {
     double as_num(double dflt = 0.0) const { return kind == Number ? num : dflt; }
     bool as_bool(bool dflt = false) const { return kind == Bool ? b : dflt; }
     // an unsigned integer (serde's as_u64): only non-negative integral numbers qualify
-    bool is_u64() const { return kind == Number && num >= 0 && num == (double)(uint64_t)num; }
+    bool is_u64() const { return kind == Number && num >= 0 && num < 18446744073709551616.0 && num == (double)(uint64_t)num; }
 };
 
 class Parser {

@@ -39,6 +39,12 @@ long fh_model_fingerprint(const FhModel* model);
  * fv[6]  = fsx, fsy, gmhs dmin, gmhs delta, protecting age, static threshold. 0, or -1 with fh_last_error. */
 int fh_session_plan_params(const FhModel* model, const FhSessionOptions* options, int* iv, float* fv);
 
+/* The static-protection state of a pair (a, b) without the network: the age pass alone, advancing the state exactly as
+ * fh_session_pair(a, b) would. A GPU that starts a stream in the middle replays it over the frames before its first
+ * interval, so that its protection matches a single GPU's run of the whole stream (no exchange between GPUs). No-op
+ * for sessions without static protection. 0, or -1 with fh_last_error. */
+int fh_session_advance_static(const FhSession* session, uint32_t a, uint32_t b);
+
 /* Kernel launches of one pair and of one mid (the nodes of their CUDA graphs). 0 on success. */
 int fh_session_launch_counts(const FhSession* session, int* pair_kernels, int* mid_kernels, int* frame_kernels);
 

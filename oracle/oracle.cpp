@@ -1368,6 +1368,26 @@ int or_render_planes(const uint8_t* fa, const uint8_t* fb, int w, int h, const f
     }
 }
 
+// interp.wgsl on a plain [c][h][w] f16 tensor (x scale applied to the result); out [c][oh][ow] f16 bits
+int or_interp(const uint16_t* x, int c, int h, int w, int oh, int ow, int aa, float scale, uint16_t* out) {
+    T t = alloc(c, h, w);
+    memcpy(t.buf->d.data(), x, t.n() * 2);
+    t.scale = scale;
+    T o = k_interp(t, oh, ow, aa != 0);
+    memcpy(out, o.buf->d.data(), o.n() * 2);
+    return 0;
+}
+// warp.wgsl: img [c][h][w], flow [2][h][w] (x flow_scale), out [c][h][w] f16 bits
+int or_warp(const uint16_t* img, int c, int h, int w, const uint16_t* flow, float flow_scale, uint16_t* out) {
+    T t = alloc(c, h, w), f = alloc(2, h, w);
+    memcpy(t.buf->d.data(), img, t.n() * 2);
+    memcpy(f.buf->d.data(), flow, f.n() * 2);
+    f.scale = flow_scale;
+    T o = k_warp(t, f);
+    memcpy(out, o.buf->d.data(), o.n() * 2);
+    return 0;
+}
+
 // conv: x [cin][h][w], wt [cout][cin][3][3] f32, bias/slope [cout] f32 (slope NULL = identity), resid [cout][ho][wo]
 // or NULL; out [cout][ho][wo] f16 bits
 int or_conv(const uint16_t* x, int cin, int h, int w, const float* wt, const float* bias, const float* slope, int cout,

@@ -49,6 +49,8 @@ def lib():
         L.or_render_planes.argtypes = [POINTER(c_uint8), POINTER(c_uint8), c_int, c_int, POINTER(c_float),
                                        POINTER(c_float), c_int, c_int, POINTER(c_float), POINTER(c_float),
                                        POINTER(c_int), POINTER(c_uint8)]
+        L.or_interp.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, c_int, c_int, c_int, c_float, POINTER(c_uint16)]
+        L.or_warp.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, POINTER(c_uint16), c_float, POINTER(c_uint16)]
         L.or_conv.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, POINTER(c_float), POINTER(c_float),
                               POINTER(c_float), c_int, c_int, POINTER(c_uint16), POINTER(c_uint16)]
         _lib = L
@@ -168,4 +170,25 @@ def render_planes(fa, fb, w, h, up7, rt, age, fsx, fsy, min_age, static_thr, cub
                                 f(fv), iv.ctypes.data_as(POINTER(c_int)), _u8(out))
     if rc != 0:
         raise RuntimeError(lib().or_error().decode())
+    return out
+
+
+def interp(x, oh: int, ow: int, aa: bool, scale: float = 1.0):
+    """interp.wgsl on [c][h][w] f16 values (bilinear align_corners=False, or the antialias triangle filter)."""
+    x = np.ascontiguousarray(x, dtype=np.float16)
+    c, h, w = x.shape
+    out = np.zeros((c, oh, ow), np.float16)
+    u = lambda a: a.ctypes.data_as(POINTER(c_uint16))
+    lib().or_interp(u(x), c, h, w, oh, ow, int(aa), c_float(scale), u(out))
+    return out
+
+
+def warp(img, flow, flow_scale: float = 1.0):
+    """warp.wgsl: backward bilinear warp with border clamp of [c][h][w] by flow [2][h][w] (px, x flow_scale)."""
+    img = np.ascontiguousarray(img, dtype=np.float16)
+    flow = np.ascontiguousarray(flow, dtype=np.float16)
+    c, h, w = img.shape
+    out = np.zeros((c, h, w), np.float16)
+    u = lambda a: a.ctypes.data_as(POINTER(c_uint16))
+    lib().or_warp(u(img), c, h, w, u(flow), c_float(flow_scale), u(out))
     return out
