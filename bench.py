@@ -256,7 +256,17 @@ def main():
                "h2d_bytes_per_step": n * fbytes, "d2h_bytes_per_step": gen_per_rank * fbytes,
                "ms_per_step": e2e_ms}
 
-    roof = roofline_block(s, ms, gen_per_rank)
+    # per-kernel device times of one pair + mid on the session's own stream (min over 5 eager runs)
+    prof = {}
+    for _ in range(5):
+        seen_this_run = {}
+        for k in s.profile(slots[0], slots[1], 0.5, out):
+            key = k["kernel"]
+            if key in seen_this_run:  # launched again in the run (the second frame stage, k > 1): its own entry
+                key = f"{key} #{seen_this_run[key] + 1}"
+            seen_this_run[k["kernel"]] = seen_this_run.get(k["kernel"], 0) + 1
+            prof[key] = min(prof.get(key, 1e9), k["ms"])
+    roof, roof_conv = roofline_blocks(s, prof, ms, gen_per_rank)
     cpu = None
     if rank == 0 and ws == 1:
         fps_cpu, dt = cpu_baseline(model_dir, frames, args.cpu_sample)
@@ -274,7 +284,8 @@ def main():
                            "frames_per_step": gen_per_rank, "l2": "inputs (1 GB of frames) larger than L2, no flush",
                            "pair_ms": pair_ms, "mid_ms": mid_ms},
                 "gpu_launches": per_interval_launches * gen_per_rank + counts["frame"],
-                "clocks": clk.summary(), "roofline": roof, "cpu_baseline": cpu, "e2e": e2e}
+                "clocks": clk.summary(), "roofline": roof, "roofline_conv": roof_conv, "cpu_baseline": cpu,
+                "e2e": e2e, "kernel_ms": {k: round(v, 5) for k, v in sorted(prof.items(), key=lambda x: -x[1])[:12]}}
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.barrier()
@@ -296,19 +307,48 @@ def conv_flops_per_interval(s) -> float:
     return float(sum(2 * m * 9 * ci * co for m, ci, co in convs))
 
 
-def roofline_block(s, step_ms, intervals):
+def render_bytes(p) -> float:
+    """Algorithmic bytes of one full-resolution render: the two source frames read once (3 channels of f16 each,
+    12 B/px), the quarter-resolution flow / visibility (7 ch) and residual (3 ch) maps (f16), the rgba8 frame written
+    (4 B/px)."""
+    q = p["qh"] * p["qw"]
+    return float(W * H * (12 + 4) + q * (7 + 3) * 2)
+
+
+# dram__bytes_read.sum + dram__bytes_write.sum of one k_render launch at 1920 x 1080 (profiles/render_1080p.md)
+RENDER_TRAFFIC = None
+
+
+def roofline_blocks(s, prof, step_ms, intervals):
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             peaks = json.load(f)
     except Exception:
         pass
-    flops = conv_flops_per_interval(s) * intervals
-    peak = peaks.get("bf16_tflops_sustained") or 1400.0
-    achieved = flops / (step_ms / 1000.0) / 1e12
-    return {"bound": "tensor", "kernel": "conv family (whole path, per step)", "achieved": achieved, "peak": peak,
-            "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
-            "note": "algorithmic conv FLOPs of the step / step time; the path is launch-latency bound at batch 1"}
+    p = s._m.plan_params(W, H)
+    hbm = peaks.get("hbm_gbs")
+    tensor = peaks.get("bf16_tflops")
+    # the dominant single kernel of the step (the longest of a pair + mid)
+    name, kms = max(((k, v) for k, v in prof.items() if k not in ("start",)), key=lambda kv: kv[1])
+    if name == "render":
+        achieved = render_bytes(p) / (kms / 1000.0) / 1e9
+        roof = {"bound": "hbm", "kernel": "k_render (full-resolution render + keep_static + rgba8 out)",
+                "achieved": achieved, "peak": hbm or 6650.0, "unit": "GB/s",
+                "frac": achieved / (hbm or 6650.0), "traffic": RENDER_TRAFFIC,
+                "algorithmic_bytes": render_bytes(p), "launch_ms": kms,
+                "peak_source": "measured" if hbm else "fallback"}
+    else:
+        roof = {"bound": "unknown", "kernel": name, "launch_ms": kms, "achieved": None, "peak": None, "unit": None,
+                "frac": None, "traffic": None}
+    conv_ms = sum(v for k, v in prof.items() if k.startswith("conv "))
+    flops = conv_flops_per_interval(s)
+    ach = flops / (conv_ms / 1000.0) / 1e12
+    roof_conv = {"bound": "tensor", "kernel": "all conv3x3_mma launches of one pair + mid (frame stages of both "
+                                              "frames included)", "achieved": ach, "peak": tensor or 1590.0,
+                 "unit": "TFLOP/s", "frac": ach / (tensor or 1590.0), "flops": flops, "ms": conv_ms,
+                 "peak_source": "measured" if tensor else "fallback"}
+    return roof, roof_conv
 
 
 if __name__ == "__main__":

@@ -89,6 +89,7 @@ EXPORTS = [
     ("fh_model_fingerprint", c_long, [c_void_p]),
     ("fh_session_plan_params", c_int, [c_void_p, POINTER(SessionOptions), POINTER(c_int), POINTER(c_float)]),
     ("fh_session_advance_static", c_int, [c_void_p, c_uint32, c_uint32]),
+    ("fh_session_profile_json", c_int, [c_void_p, c_uint32, c_uint32, c_float, c_uint32, c_char_p, c_size_t]),
     ("fh_session_launch_counts", c_int, [c_void_p, POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
     ("fhk_conv3x3", c_int, [c_void_p, c_int, c_void_p]),
     ("fhk_conv_pack_weights", c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
@@ -361,6 +362,13 @@ class Session:
     def advance_static(self, a: int, b: int) -> None:
         """The static-protection state of the pair (a, b) without the network (see multi.py)."""
         _check(lib().fh_session_advance_static(self._h, a, b))
+
+    def profile(self, a: int, b: int, t: float, out: int) -> list:
+        """Device ms of every kernel of one pair + mid, run eagerly ([{"kernel", "ms"}])."""
+        cap = 1 << 16
+        buf = create_string_buffer(cap)
+        n = _check(lib().fh_session_profile_json(self._h, a, b, t, out, buf, cap))
+        return json.loads(buf.raw[:n].decode())
 
     def launch_counts(self) -> dict:
         a, b, c = c_int(), c_int(), c_int()

@@ -342,6 +342,16 @@ struct FhSession {
     bool mid_ran = false;
     uint64_t pair_static_gen = 0;  // the static state advances once per pair() call
 
+    // profiling (fh_session_profile_json): an event after every launch of an eager run, labelled with the kernel
+    std::vector<std::pair<std::string, cudaEvent_t>>* prof = nullptr;
+    void mark(const std::string& label) {
+        if (!prof) return;
+        cudaEvent_t ev;
+        CK(cudaEventCreate(&ev));
+        CK(cudaEventRecord(ev, st));
+        prof->emplace_back(label, ev);
+    }
+
     // device memory of this session, zeroed on its stream. Every upload of initial data goes on the same stream
     // (cudaMemcpyAsync: pageable sources are staged before the call returns), so a zeroing memset can never land
     // after the data: the stream is non-blocking and is not ordered against the legacy default stream.
@@ -452,6 +462,7 @@ struct FhSession {
         p.ngroups = 0;
         int e = fhk_conv3x3(&p, L.stride, st);
         if (e) fail("conv %s: %s", key.c_str(), cudaGetErrorString((cudaError_t)e));
+        mark("conv " + L.name);
     }
 
     void plan() {
@@ -568,8 +579,11 @@ struct FhSession {
     // ---- stages ----
     void run_frame(FrameSet& s) {
         CK(fhk::frame_half(s.frame, 0, w, h, s.half, 0, 1, st));
+        mark("frame_half");
         CK(fhk::frame_to_input(s.frame, 0, w, h, hp, wp, internal, ihp, iwp, {s.A, 0}, 1, st));
+        mark("frame_to_input");
         CK(fhk::input_pyramid({s.A, 0}, NH, NW, {s.aq, 0}, {s.i8, 0}, {s.i16, 0}, 1, st));
+        mark("input_pyramid");
         conv("e1", {s.aq}, qh, qw, e1, C8P);
         conv("e2", {e1}, h8, w8, s.f8, C8P, e1, C8P);
         conv("e3", {s.f8}, h8, w8, e3, C16P);
@@ -577,24 +591,33 @@ struct FhSession {
     }
 
     void run_pair(const FrameSet& A, const FrameSet& B) {
-        if (protects || still) CK(fhk::pair_planes(A.frame, B.frame, sargs, protects ? changed : nullptr, still ? dsum : nullptr, st));
+        if (protects || still) {
+            CK(fhk::pair_planes(A.frame, B.frame, sargs, protects ? changed : nullptr, still ? dsum : nullptr, st));
+            mark("pair_planes");
+        }
         if (protects) {
             CK(fhk::static_age(A.frame, B.frame, changed, mask, sargs, state, age, st));
+            mark("static_age");
             CK(fhk::static_near(age, wp, hp, min_age, nearp, st));
+            mark("static_near");
         }
         // coarse: img16 = (i16a, i16b), luma, sad r3 (graph ops 18-25), then c1..head (26-32)
         CK(fhk::sad_volume(A.i16, 4, B.i16, 4, 0, h16, w16, 3, cv, 56, 0, 1, st));
+        mark("sad_volume r3");
         conv("c1", {A.f16, B.f16, A.i16, B.i16, cv}, h16, w16, ch1, CCP);
         conv("c2", {ch1}, h16, w16, ch2, CCP);
         conv("c3", {ch2}, h16, w16, ch3r, CCP, ch1, CCP);
         conv("c4", {ch3r}, h16, w16, hcb, CCP);
         conv("head", {hcb}, h16, w16, ob, 16);
         CK(fhk::upsample_flow_vis(ob, 16, 0, h16, w16, fv, 0, h8, w8, 1, st));
+        mark("upsample_flow_vis");
         // fine iterations (graph op 42)
         for (int it = 0; it < k; it++) {
             fhk::WarpFineArgs wa{fv, 0, A.f8, B.f8, C8P, c8, 0, {A.i8, 0}, {B.i8, 0}, h8, w8, wbuf, 0};
             CK(fhk::warp_fine(wa, 1, st));
+            mark("warp_fine");
             CK(fhk::sad_volume(wbuf + 80, 88, wbuf + 84, 88, 0, h8, w8, 2, fcv, 32, 0, 1, st));
+            mark("sad_volume r2");
             if (it == 0) conv("r1_0", {wbuf, wbuf + 40, wbuf + 80, fv, fcv}, h8, w8, fr1, CRP);
             else conv("r1", {wbuf, wbuf + 40, wbuf + 80, fv, fr3, fcv}, h8, w8, fr1, CRP);
             conv("r2", {fr1}, h8, w8, fr2, CRP);
@@ -604,6 +627,7 @@ struct FhSession {
         if (repair > 0) {
             fhk::GmArgs g{fv, 0, h8, w8, A.A, B.A, 0, NH, NW, hc, wc, r_blk, r_dwin, delta, dmin, coef, maps, tmp};
             CK(fhk::gmhs(g, 1, st));
+            mark("gmhs");
         }
         // the convex-upsample weights depend on h only (graph op 62: conv up.w of h)
         conv("up", {fr3}, h8, w8, wt36, 40);
@@ -612,12 +636,16 @@ struct FhSession {
     void run_mid(const PairSrc& p, uint8_t* out) {
         fhk::FilmArgs fa{tdev, film_w1, film_b1, film_w2, film_b2, film_hidden, cr, fr3, CRP, 0, hm, CRP, 0, h8, w8};
         CK(fhk::film(fa, 1, st));
+        mark("film");
         conv("fh1", {hm}, h8, w8, fh1, CRP);
         conv("fh2", {fh1}, h8, w8, fh2, CRP);
         conv("fout", {fh2}, h8, w8, dfilm, 8);
         CK(fhk::mid_combine(tdev, fv, 0, dfilm, 0, ftvt, 0, h8, w8, 1, st));
+        mark("mid_combine");
         CK(fhk::convex_up(wt36, 40, 0, ftvt, 0, h8, w8, up7, 0, 1, st));
+        mark("convex_up");
         CK(fhk::refine_input(up7, 0, {p.a->aq, 0}, {p.b->aq, 0}, qh, qw, rx, 0, 1, st));
+        mark("refine_input");
         conv("q1", {rx}, qh, qw, rq1, CQP);
         conv("q2", {rq1}, qh, qw, rq2, CQP);
         conv("q3", {rq2}, qh, qw, rq3, CQP);
@@ -626,6 +654,7 @@ struct FhSession {
                            (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, 0, dsum, nearp, 0,
                            min_age, out, 0};
         CK(fhk::render(ra, 1, st));
+        mark("render");
     }
 
     template <class F>
@@ -734,6 +763,52 @@ struct FhSession {
         FrameSet& fs = *s.set[s.cur];
         fs.gen++;
         return fs;
+    }
+
+    // Every kernel of a pair (a, b) + mid (t, out) run eagerly (the frame stages of both frames included, as the
+    // reference's pair recomputes them), each followed by an event; a bounded delay kernel first lets the whole
+    // sequence queue up, so the event deltas are device time. The pair's static state advances as a pair() would.
+    std::string profile_json(uint32_t a, uint32_t b, float t, uint32_t out) {
+        check_in(a);
+        check_in(b);
+        check_out(out);
+        if (!std::isfinite(t)) fail("t is not finite");
+        FrameSet& A = cur_set(a);
+        FrameSet& B = cur_set(b);
+        std::vector<std::pair<std::string, cudaEvent_t>> marks;
+        CK(cudaStreamSynchronize(st));
+        CK(fhk::delay(st, 4000000));
+        prof = &marks;
+        try {
+            mark("start");
+            run_frame(A);
+            run_frame(B);
+            run_pair(A, B);
+            CK(fhk::set_scalar(tdev, t, st));
+            mark("set_t");
+            run_mid(PairSrc{&A, &B}, outs[out]);
+        } catch (...) {
+            prof = nullptr;
+            for (auto& m : marks) cudaEventDestroy(m.second);
+            throw;
+        }
+        prof = nullptr;
+        CK(cudaStreamSynchronize(st));
+        A.feat_gen = A.gen;
+        B.feat_gen = B.gen;
+        pair = PairSrc{&A, &B};
+        have_pair = true;
+        std::string js = "[";
+        for (size_t i = 1; i < marks.size(); i++) {
+            float ms = 0;
+            CK(cudaEventElapsedTime(&ms, marks[i - 1].second, marks[i].second));
+            char b2[64];
+            snprintf(b2, sizeof b2, "%.6f", ms);
+            js += std::string(i > 1 ? "," : "") + "{\"kernel\":" + fhjson::quote(marks[i].first) + ",\"ms\":" + b2 + "}";
+        }
+        js += "]";
+        for (auto& m : marks) cudaEventDestroy(m.second);
+        return js;
     }
 
     int add_input() {
@@ -1230,6 +1305,14 @@ int fh_session_advance_static(const FhSession* cs, uint32_t a, uint32_t b) {
         CK(fhk::pair_planes(A.frame, B.frame, s->sargs, s->changed, nullptr, s->st));
         CK(fhk::static_age(A.frame, B.frame, s->changed, s->mask, s->sargs, s->state, s->age, s->st));
         return 0;
+    });
+}
+
+int fh_session_profile_json(const FhSession* cs, uint32_t a, uint32_t b, float t, uint32_t out, char* buf, size_t cap) {
+    return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
+        if (!s || !buf) fail("null argument");
+        return write_json(s->profile_json(a, b, t, out), buf, cap);
     });
 }
 

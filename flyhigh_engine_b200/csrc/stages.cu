@@ -914,6 +914,13 @@ __global__ void __launch_bounds__(256) k_render(RenderArgs r) {
 
 __global__ void k_set_scalar(float* d, float v) { *d = v; }
 
+// a bounded busy wait: returns after `cycles` clock cycles of its own SM
+__global__ void k_delay(long long cycles) {
+    const long long t0 = clock64();
+    while (clock64() - t0 < cycles) {
+    }
+}
+
 // tex_in.wgsl's values for the whole frame: f16(byte / 255) as B, G, R, 0 halves per pixel (unpadded)
 __global__ void k_frame_half(const uint8_t* __restrict__ f, long long f_bs, int w, int h, __half* out, long long o_bs) {
     __shared__ float lut[256];
@@ -1040,6 +1047,11 @@ cudaError_t render(const RenderArgs& r, int n, cudaStream_t st) {
 cudaError_t frame_half(const uint8_t* f, long long f_bs, int w, int h, __half* out, long long o_bs, int n,
                        cudaStream_t st) {
     k_frame_half<<<grid2(w, h, n, 32, 8), dim3(32, 8), 0, st>>>(f, f_bs, w, h, out, o_bs);
+    return cudaGetLastError();
+}
+
+cudaError_t delay(cudaStream_t st, long long cycles) {
+    k_delay<<<1, 1, 0, st>>>(cycles);
     return cudaGetLastError();
 }
 

@@ -132,6 +132,9 @@ cudaError_t render(const RenderArgs& r, int n, cudaStream_t st);
 cudaError_t frame_half(const uint8_t* f, long long f_bs, int w, int h, __half* out, long long o_bs, int n,
                        cudaStream_t st);
 
+// a kernel that keeps the stream busy for about `cycles` SM clock cycles (profiling: lets launches queue up behind it)
+cudaError_t delay(cudaStream_t st, long long cycles);
+
 // a device scalar (the phase t of the mid stage) written on the stream
 cudaError_t set_scalar(float* dst, float v, cudaStream_t st);
 

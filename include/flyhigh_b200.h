@@ -45,6 +45,13 @@ int fh_session_plan_params(const FhModel* model, const FhSessionOptions* options
  * for sessions without static protection. 0, or -1 with fh_last_error. */
 int fh_session_advance_static(const FhSession* session, uint32_t a, uint32_t b);
 
+/* Device time of every kernel of one pair (a, b) + one mid (t, out) (the reference's per-pipeline profile,
+ * crates/flyhigh-engine/src/gpu/timing.rs:261+): the stages run once eagerly with an event after each launch, the
+ * frame stages of both frames included; the pair's static state advances as fh_session_pair would advance it.
+ * JSON [{"kernel", "ms"}...] written NUL-terminated; bytes or -1. */
+int fh_session_profile_json(const FhSession* session, uint32_t a, uint32_t b, float t, uint32_t out, char* buf,
+                            size_t cap);
+
 /* Kernel launches of one pair and of one mid (the nodes of their CUDA graphs). 0 on success. */
 int fh_session_launch_counts(const FhSession* session, int* pair_kernels, int* mid_kernels, int* frame_kernels);
 
