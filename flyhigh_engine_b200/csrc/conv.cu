@@ -99,19 +99,24 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
                 cp_async16(dst0 + (uint32_t)(k * NT * 256 + r * 16), src0 + (size_t)k * ntt * 256 + (size_t)r * 16);
     }
 
-    // ---- halo tile: IH x IW pixels x cp channels, zero outside the image and beyond every source. A lane owns
-    //      8-channel chunks (its source, offset and view scale resolved once); a warp walks pixels, 4 loads in flight ----
-    for (int ch = lane; ch < nchunk; ch += 32) {
+    // ---- halo tile: IH x IW pixels x cp channels, zero outside the image and beyond every source. The 128 threads
+    //      form groups of LP (a power of two >= the chunk count) lanes per pixel: a thread owns one 8-channel chunk
+    //      (its source, offset and view scale resolved once) and walks every (128 / LP)-th pixel, 4 loads in flight ----
+    {
+        int lp = 1;
+        while (lp < nchunk) lp <<= 1;  // nchunk <= 128 (checked on the host)
+        const int ch = tid & (lp - 1), pstep = (WARPS * 32) / lp;
         const int c8 = ch * 8;
         int si = -1, rel = 0;
-        for (int s_ = 0; s_ < p.nsrc; s_++) {
-            const int r_ = c8 - p.src[s_].slot;
-            if (r_ >= 0 && r_ < ((p.src[s_].nc + 7) & ~7)) {
-                si = s_;
-                rel = r_;
-                break;
+        if (ch < nchunk)
+            for (int s_ = 0; s_ < p.nsrc; s_++) {
+                const int r_ = c8 - p.src[s_].slot;
+                if (r_ >= 0 && r_ < ((p.src[s_].nc + 7) & ~7)) {
+                    si = s_;
+                    rel = r_;
+                    break;
+                }
             }
-        }
         const __half* base = nullptr;
         int cs = 0, valid = 0;
         float scale = 1.0f;
@@ -126,37 +131,39 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
         }
         const bool plain = valid >= 8 && scale == 1.0f && !narrow;
         const int npix = IH * IW;
-        for (int pix0 = warp; pix0 < npix; pix0 += 4 * WARPS) {
-            uint4 v[4];
+        if (ch < nchunk) {
+            for (int pix0 = tid / lp; pix0 < npix; pix0 += 4 * pstep) {
+                uint4 v[4];
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int pix = pix0 + u * WARPS;
-                const int hy = pix / IW, hx = pix - hy * IW;
-                const int iy = iy0 + hy, ix = ix0 + hx;
-                v[u] = make_uint4(0, 0, 0, 0);
-                if (pix < npix && si >= 0 && iy >= 0 && iy < p.h && ix >= 0 && ix < p.w) {
-                    const __half* g = base + ((long long)iy * p.w + ix) * cs;
-                    if (!narrow) {
-                        v[u] = __ldg(reinterpret_cast<const uint4*>(g));
-                    } else {  // a 4-channel pixel (3-channel image): 8 bytes
-                        const uint2 w2 = __ldg(reinterpret_cast<const uint2*>(g));
-                        v[u] = make_uint4(w2.x, w2.y, 0, 0);
+                for (int u = 0; u < 4; u++) {
+                    const int pix = pix0 + u * pstep;
+                    const int hy = pix / IW, hx = pix - hy * IW;
+                    const int iy = iy0 + hy, ix = ix0 + hx;
+                    v[u] = make_uint4(0, 0, 0, 0);
+                    if (pix < npix && si >= 0 && iy >= 0 && iy < p.h && ix >= 0 && ix < p.w) {
+                        const __half* g = base + ((long long)iy * p.w + ix) * cs;
+                        if (!narrow) {
+                            v[u] = __ldg(reinterpret_cast<const uint4*>(g));
+                        } else {  // a 4-channel pixel (3-channel image): 8 bytes
+                            const uint2 w2 = __ldg(reinterpret_cast<const uint2*>(g));
+                            v[u] = make_uint4(w2.x, w2.y, 0, 0);
+                        }
                     }
                 }
-            }
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int pix = pix0 + u * WARPS;
-                if (pix >= npix) break;
-                if (!plain) {
-                    __half* hv = reinterpret_cast<__half*>(&v[u]);
+                for (int u = 0; u < 4; u++) {
+                    const int pix = pix0 + u * pstep;
+                    if (pix >= npix) break;
+                    if (!plain) {
+                        __half* hv = reinterpret_cast<__half*>(&v[u]);
 #pragma unroll
-                    for (int k = 0; k < 8; k++) {
-                        if (k >= valid) hv[k] = __float2half_rn(0.0f);
-                        else if (scale != 1.0f) hv[k] = __float2half_rn(__half2float(hv[k]) * scale);
+                        for (int k = 0; k < 8; k++) {
+                            if (k >= valid) hv[k] = __float2half_rn(0.0f);
+                            else if (scale != 1.0f) hv[k] = __float2half_rn(__half2float(hv[k]) * scale);
+                        }
                     }
+                    *reinterpret_cast<uint4*>(tile + pix * P + c8) = v[u];
                 }
-                *reinterpret_cast<uint4*>(tile + pix * P + c8) = v[u];
             }
         }
     }
@@ -353,7 +360,7 @@ void choose_split(FhConvParams& q) {
 }  // namespace
 
 extern "C" int fhk_conv3x3(const FhConvParams* pin, int stride, void* stream) {
-    if (!pin || pin->cp <= 0 || pin->cp % 16 || pin->nsrc < 1 || pin->nsrc > FH_CONV_MAX_SRC || pin->cout < 1 ||
+    if (!pin || pin->cp <= 0 || pin->cp % 16 || pin->cp > 1024 || pin->nsrc < 1 || pin->nsrc > FH_CONV_MAX_SRC || pin->cout < 1 ||
         pin->cout > 96 || pin->n < 1)
         return (int)cudaErrorInvalidValue;
     FhConvParams p = *pin;

@@ -313,6 +313,12 @@ struct FhSession {
     int C8P, C16P, CCP, CRP, CQP;
 
     cudaStream_t st = nullptr;
+    // Independent branches of a stage (the static age pass beside the network, the repair beside the upsample
+    // weights, the render's frame plane beside the encoder) are issued on a second stream forked from and joined back
+    // into st, so a captured stage graph holds them as parallel branches.
+    cudaStream_t side = nullptr;
+    cudaEvent_t fork_ev[4] = {}, join_ev[4] = {};
+    int branches = 0;  // forks of the stage being issued, all joined by join_branches()
     std::vector<void*> allocs;
     size_t bytes = 0;
 
@@ -324,7 +330,8 @@ struct FhSession {
     std::vector<uint8_t*> outs;
     // frame-stage scratch, pair and mid buffers
     __half *e1 = nullptr, *e3 = nullptr;
-    uint8_t *changed = nullptr, *mask = nullptr;
+    uint32_t* changed = nullptr;
+    uint8_t* mask = nullptr;
     uchar4* state = nullptr;
     int16_t* age = nullptr;
     float* dsum = nullptr;      // per pair: the still test's per-pixel |A - B| sums
@@ -367,14 +374,47 @@ struct FhSession {
     T* alloc_n(size_t n) { return (T*)dalloc(n * sizeof(T)); }
     __half* img(int hh, int ww, int cs) { return alloc_n<__half>((size_t)hh * ww * cs); }
 
+    // issues body's launches on the side stream, after everything issued on st so far (inline while profiling, so
+    // that every launch is timed alone)
+    template <class F>
+    void branch(F&& body) {
+        if (prof || !side) {
+            body();
+            return;
+        }
+        if (branches >= 4) fail("too many parallel branches in one stage");
+        const int i = branches++;
+        CK(cudaEventRecord(fork_ev[i], st));
+        CK(cudaStreamWaitEvent(side, fork_ev[i], 0));
+        std::swap(st, side);
+        try {
+            body();
+        } catch (...) {
+            std::swap(st, side);
+            throw;
+        }
+        std::swap(st, side);
+        CK(cudaEventRecord(join_ev[i], side));
+    }
+    void join_branches() {
+        for (int i = 0; i < branches; i++) CK(cudaStreamWaitEvent(st, join_ev[i], 0));
+        branches = 0;
+    }
+
     ~FhSession() {
         if (st) cudaStreamSynchronize(st);
+        if (side) cudaStreamSynchronize(side);
+        for (int i = 0; i < 4; i++) {
+            if (fork_ev[i]) cudaEventDestroy(fork_ev[i]);
+            if (join_ev[i]) cudaEventDestroy(join_ev[i]);
+        }
         for (auto& fs : sets)
             if (fs->graph) cudaGraphExecDestroy(fs->graph);
         for (auto& kv : pair_graphs) cudaGraphExecDestroy(kv.second);
         for (auto& kv : mid_graphs) cudaGraphExecDestroy(kv.second);
         for (void* p : allocs) cudaFree(p);
         if (eng) eng->tensor_bytes -= std::min(eng->tensor_bytes, bytes);
+        if (side) cudaStreamDestroy(side);
         if (st) cudaStreamDestroy(st);
     }
 
@@ -538,7 +578,7 @@ struct FhSession {
         e1 = img(h8, w8, C8P);
         e3 = img(h16, w16, C16P);
         if (protects) {
-            changed = alloc_n<uint8_t>((size_t)hp * wp);
+            changed = alloc_n<uint32_t>((size_t)hp * fhk::changed_words(wp));
             mask = alloc_n<uint8_t>((size_t)hp * wp);
             state = alloc_n<uchar4>((size_t)hp * wp);
             age = alloc_n<int16_t>((size_t)hp * wp);
@@ -578,8 +618,10 @@ struct FhSession {
 
     // ---- stages ----
     void run_frame(FrameSet& s) {
-        CK(fhk::frame_half(s.frame, 0, w, h, s.half, 0, 1, st));
-        mark("frame_half");
+        branch([&] {
+            CK(fhk::frame_half(s.frame, 0, w, h, s.half, 0, 1, st));
+            mark("frame_half");
+        });
         CK(fhk::frame_to_input(s.frame, 0, w, h, hp, wp, internal, ihp, iwp, {s.A, 0}, 1, st));
         mark("frame_to_input");
         CK(fhk::input_pyramid({s.A, 0}, NH, NW, {s.aq, 0}, {s.i8, 0}, {s.i16, 0}, 1, st));
@@ -588,19 +630,22 @@ struct FhSession {
         conv("e2", {e1}, h8, w8, s.f8, C8P, e1, C8P);
         conv("e3", {s.f8}, h8, w8, e3, C16P);
         conv("e4", {e3}, h16, w16, s.f16, C16P, e3, C16P);
+        join_branches();
     }
 
     void run_pair(const FrameSet& A, const FrameSet& B) {
-        if (protects || still) {
-            CK(fhk::pair_planes(A.frame, B.frame, sargs, protects ? changed : nullptr, still ? dsum : nullptr, st));
-            mark("pair_planes");
-        }
-        if (protects) {
-            CK(fhk::static_age(A.frame, B.frame, changed, mask, sargs, state, age, st));
-            mark("static_age");
-            CK(fhk::static_near(age, wp, hp, min_age, nearp, st));
-            mark("static_near");
-        }
+        // the static age pass and the still test's plane read the two frames only: a branch beside the network
+        if (protects || still)
+            branch([&] {
+                CK(fhk::pair_planes(A.frame, B.frame, sargs, protects ? changed : nullptr, still ? dsum : nullptr, st));
+                mark("pair_planes");
+                if (protects) {
+                    CK(fhk::static_age(A.frame, B.frame, changed, mask, sargs, state, age, st));
+                    mark("static_age");
+                    CK(fhk::static_near(age, wp, hp, min_age, nearp, st));
+                    mark("static_near");
+                }
+            });
         // coarse: img16 = (i16a, i16b), luma, sad r3 (graph ops 18-25), then c1..head (26-32)
         CK(fhk::sad_volume(A.i16, 4, B.i16, 4, 0, h16, w16, 3, cv, 56, 0, 1, st));
         mark("sad_volume r3");
@@ -624,13 +669,20 @@ struct FhSession {
             conv("r3", {fr2}, h8, w8, fr3, CRP);
             conv("out", {fr3}, h8, w8, fv, 8, fv, 8);
         }
-        if (repair > 0) {
-            fhk::GmArgs g{fv, 0, h8, w8, A.A, B.A, 0, NH, NW, hc, wc, r_blk, r_dwin, delta, dmin, coef, maps, tmp};
-            CK(fhk::gmhs(g, 1, st));
-            mark("gmhs");
-        }
-        // the convex-upsample weights depend on h only (graph op 62: conv up.w of h)
+        // the repair rewrites the flow; the convex-upsample weights depend on h only (graph op 62: conv up.w of h),
+        // so the two run side by side
+        if (repair > 0)
+            branch([&] {
+                fhk::GmArgs g{fv, 0, h8, w8, A.A, B.A, 0, NH, NW, hc, wc, r_blk, r_dwin, delta, dmin, coef, maps, tmp};
+                CK(fhk::gmhs_fit(g, 1, st));
+                mark("gmhs fit");
+                CK(fhk::gmhs_maps(g, 1, st));
+                mark("gmhs maps");
+                CK(fhk::gmhs_select(g, 1, st));
+                mark("gmhs select");
+            });
         conv("up", {fr3}, h8, w8, wt36, 40);
+        join_branches();
     }
 
     void run_mid(const PairSrc& p, uint8_t* out) {
@@ -664,6 +716,7 @@ struct FhSession {
         try {
             body();
         } catch (...) {
+            branches = 0;
             cudaStreamEndCapture(st, &g);
             if (g) cudaGraphDestroy(g);
             throw;
@@ -917,6 +970,11 @@ FhSession* session_new(FhEngine* e, const FhModel* m, const FhSessionOptions& o)
     s->eng = e;
     CK(cudaSetDevice(e->device));
     CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&s->side, cudaStreamNonBlocking));
+    for (int i = 0; i < 4; i++) {
+        CK(cudaEventCreateWithFlags(&s->fork_ev[i], cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&s->join_ev[i], cudaEventDisableTiming));
+    }
     s->plan();
     e->tensor_bytes += s->bytes;
     return s.release();

@@ -61,17 +61,45 @@ __global__ void k_frame_to_input(const uint8_t* __restrict__ frames, long long f
     const int ymin = max(0, (int)floorf(cy - fsh + 0.5f)), ymax = min(hp, (int)floorf(cy + fsh + 0.5f));
     const int xmin = max(0, (int)floorf(cx - fsw + 0.5f)), xmax = min(wp, (int)floorf(cx + fsw + 0.5f));
     float ab = 0.0f, ag = 0.0f, ar = 0.0f, norm = 0.0f;
-    for (int y = ymin; y < ymax; y++) {
-        const float wy = fmaxf(0.0f, 1.0f - fabsf(((float)y + 0.5f - cy) / fsh));
-        const uint32_t* row = f + (long long)min(y, h - 1) * w;
-        for (int x = xmin; x < xmax; x++) {
-            const float wx = fmaxf(0.0f, 1.0f - fabsf(((float)x + 0.5f - cx) / fsw));
-            const float wgt = wx * wy;
-            const uint32_t v = __ldg(row + min(x, w - 1));
-            ab = ab + lut[(v >> 16) & 255] * wgt;
-            ag = ag + lut[(v >> 8) & 255] * wgt;
-            ar = ar + lut[v & 255] * wgt;
-            norm = norm + wgt;
+    constexpr int XT = 8;  // the column weights of up to XT taps are formed once (downscales up to about 3.5x)
+    if (xmax - xmin <= XT) {
+        float wx[XT];
+        int xs[XT];
+#pragma unroll
+        for (int j = 0; j < XT; j++) {
+            const int x = xmin + j;
+            wx[j] = fmaxf(0.0f, 1.0f - fabsf(((float)x + 0.5f - cx) / fsw));
+            xs[j] = min(x, w - 1);
+        }
+        const int nx = xmax - xmin;
+        for (int y = ymin; y < ymax; y++) {
+            const float wy = fmaxf(0.0f, 1.0f - fabsf(((float)y + 0.5f - cy) / fsh));
+            const uint32_t* row = f + min(y, h - 1) * w;
+#pragma unroll
+            for (int j = 0; j < XT; j++) {
+                if (j < nx) {
+                    const float wgt = wx[j] * wy;
+                    const uint32_t v = __ldg(row + xs[j]);
+                    ab = ab + lut[(v >> 16) & 255] * wgt;
+                    ag = ag + lut[(v >> 8) & 255] * wgt;
+                    ar = ar + lut[v & 255] * wgt;
+                    norm = norm + wgt;
+                }
+            }
+        }
+    } else {
+        for (int y = ymin; y < ymax; y++) {
+            const float wy = fmaxf(0.0f, 1.0f - fabsf(((float)y + 0.5f - cy) / fsh));
+            const uint32_t* row = f + (long long)min(y, h - 1) * w;
+            for (int x = xmin; x < xmax; x++) {
+                const float wx = fmaxf(0.0f, 1.0f - fabsf(((float)x + 0.5f - cx) / fsw));
+                const float wgt = wx * wy;
+                const uint32_t v = __ldg(row + min(x, w - 1));
+                ab = ab + lut[(v >> 16) & 255] * wgt;
+                ag = ag + lut[(v >> 8) & 255] * wgt;
+                ar = ar + lut[v & 255] * wgt;
+                norm = norm + wgt;
+            }
         }
     }
     st4(o, ab / norm, ag / norm, ar / norm);
@@ -161,29 +189,37 @@ FH_DEV float diff3(uint32_t a, uint32_t b, const float* lut) {
 }
 
 // The per-pair planes over the padded plane (a, b read at the clamped position):
-//  - changed = keep_static_age.wgsl:52-56 `diff(o) >= thr` (the age pass probes it 41 times per pixel);
+//  - changed = keep_static_age.wgsl:52-56 `diff(o) >= thr` (the age pass probes it 41 times per pixel), one bit per
+//    pixel: row y is words [y * ww, (y + 1) * ww), bit j of word k = pixel 32 k + j, zero past the padded width;
 //  - dsum = sum over the 3 channels of |A - B|, the still test's per-pixel term (render.wgsl:136-143). Each |A - B| is
 //    a multiple of 2^-18 below 1 (f16 values of b / 255), so these sums and the render's 3 x 3 sum of them are exact
 //    in f32 and equal to the shader's 27-term running sum whatever the order.
-__global__ void k_pair_planes(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb, StaticArgs s,
-                              uint8_t* changed, float* dsum) {
+// Blocks are 32 x 8: a warp is one 32-pixel segment of a row, so its ballot is one word of the bit plane.
+__global__ void __launch_bounds__(256) k_pair_planes(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb,
+                                                     StaticArgs s, uint32_t* changed, float* dsum) {
     __shared__ float lut[256];
     for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
     __syncthreads();
-    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
-    if (x >= s.wp || y >= s.hp) return;
-    const long long src = (long long)min(y, s.h - 1) * s.w + min(x, s.w - 1);
-    const uint32_t a = __ldg(reinterpret_cast<const uint32_t*>(fa) + src);
-    const uint32_t b = __ldg(reinterpret_cast<const uint32_t*>(fb) + src);
-    const long long o = (long long)y * s.wp + x;
-    if (changed) changed[o] = diff3(a, b, lut) >= s.thr ? 1 : 0;
-    if (dsum) {
+    const int x = blockIdx.x * 32 + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
+    if (y >= s.hp) return;  // warp-uniform
+    const bool in = x < s.wp;
+    uint32_t a = 0, b = 0;
+    if (in) {
+        const long long src = (long long)min(y, s.h - 1) * s.w + min(x, s.w - 1);
+        a = __ldg(reinterpret_cast<const uint32_t*>(fa) + src);
+        b = __ldg(reinterpret_cast<const uint32_t*>(fb) + src);
+    }
+    if (changed) {
+        const uint32_t word = __ballot_sync(0xffffffffu, in && diff3(a, b, lut) >= s.thr);
+        if (threadIdx.x == 0) changed[(long long)y * ((s.wp + 31) >> 5) + blockIdx.x] = word;
+    }
+    if (dsum && in) {
         float d = 0.0f;
         for (int c = 0; c < 3; c++) {
             const int sh = 16 - 8 * c;
             d = d + fabsf(lut[(a >> sh) & 255] - lut[(b >> sh) & 255]);
         }
-        dsum[o] = d;
+        dsum[(long long)y * s.wp + x] = d;
     }
 }
 
@@ -198,47 +234,122 @@ __global__ void k_static_near(const int16_t* __restrict__ age, int W, int H, flo
     near[(long long)y * W + x] = hit ? 1 : 0;
 }
 
-// keep_static_age.wgsl:59-77: 9 near + 32 far probes of `changed`, the spread test, the state machine (decide, :28-36)
-__global__ void k_static_age(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb,
-                             const uint8_t* __restrict__ changed, const uint8_t* __restrict__ mask, StaticArgs s,
-                             uchar4* state, int16_t* age) {
+// 32 bits of row `row` of the changed plane: bit i = changed(clamp(s0 + i, 0, W - 1)), the replicate clamp of the
+// shader's probes
+FH_DEV uint32_t bit_window(const uint32_t* __restrict__ row, int ww, int W, int s0) {
+    const int k = s0 >> 5, r = s0 & 31;  // floor division, also for negative starts
+    const uint32_t w0 = (k >= 0 && k < ww) ? __ldg(row + k) : 0u;
+    const uint32_t w1 = (k + 1 >= 0 && k + 1 < ww) ? __ldg(row + k + 1) : 0u;
+    uint32_t v = __funnelshift_r(w0, w1, r);
+    if (s0 < 0) {  // lanes left of pixel 0 read pixel 0
+        const int lo = -s0;
+        const uint32_t m = lo >= 32 ? 0xffffffffu : ((1u << lo) - 1u);
+        v = (v & ~m) | ((__ldg(row) & 1u) ? m : 0u);
+    }
+    const int hi = W - s0;  // lanes i >= hi read pixel W - 1
+    if (hi < 32) {
+        const uint32_t m = hi <= 0 ? 0xffffffffu : ~((1u << hi) - 1u);
+        v = (v & ~m) | (((__ldg(row + ((W - 1) >> 5)) >> ((W - 1) & 31)) & 1u) ? m : 0u);
+    }
+    return v;
+}
+
+// keep_static_age.wgsl:59-77: 9 near + 32 far probes of `changed`, the spread test, the state machine (decide, :28-36).
+// A warp is one 32-pixel row segment. moved: lane l evaluates probe l (and probe 32 + l) as a 32-bit window of the
+// changed bits for the whole segment, and the warp ORs the windows. spread: max over the clamped 3 x 3 neighbourhood
+// and channels of |a(q) - a(o)|, |b(q) - b(o)|; the byte -> value table is monotone and f32 subtraction is monotone
+// in each operand, so that max is max(v(max_q) - v(o), v(o) - v(min_q)) per channel, exactly.
+__global__ void __launch_bounds__(256) k_static_age(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb,
+                                                    const uint32_t* __restrict__ changed, const uint8_t* __restrict__ mask,
+                                                    StaticArgs s, uchar4* state, int16_t* age) {
     __shared__ float lut[256];
     for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
     __syncthreads();
-    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
-    if (x >= s.wp || y >= s.hp) return;
+    const int lane = threadIdx.x, x0 = blockIdx.x * 32, x = x0 + lane, y = blockIdx.y * blockDim.y + threadIdx.y;
     // the padded plane: p.w = wp, p.h = hp in the reference dispatch (StaticParams::new(net, wp, hp, wp, hp))
-    const int W = s.wp, H = s.hp;
-    bool moved = false;
-    for (int dy = -1; dy <= 1; dy++)
-        for (int dx = -1; dx <= 1; dx++) moved |= changed[(long long)clampi(y + dy, 0, H - 1) * W + clampi(x + dx, 0, W - 1)] != 0;
-    const int DX[8] = {1, -1, 0, 0, 1, -1, 1, -1}, DY[8] = {0, 0, 1, -1, 1, 1, -1, -1};
+    const int W = s.wp, H = s.hp, ww = (W + 31) >> 5;
+    if (y >= H) return;  // warp-uniform
+    // moved: probes 0-31 are the far ring (direction l >> 2, distance 4 << (l & 3)), 32-40 the 3 x 3 neighbourhood
+    uint32_t mv;
+    {
+        const int DX[8] = {1, -1, 0, 0, 1, -1, 1, -1}, DY[8] = {0, 0, 1, -1, 1, 1, -1, -1};
+        const int far = 4 << (lane & 3), dir = lane >> 2;
+        int dx = 0, dy = 0;
 #pragma unroll
-    for (int i = 0; i < 8; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int far = 4 << j;
-            moved |= changed[(long long)clampi(y + DY[i] * far, 0, H - 1) * W + clampi(x + DX[i] * far, 0, W - 1)] != 0;
+        for (int i = 0; i < 8; i++)
+            if (dir == i) {
+                dx = DX[i] * far;
+                dy = DY[i] * far;
+            }
+        mv = bit_window(changed + (long long)clampi(y + dy, 0, H - 1) * ww, ww, W, x0 + dx);
+        if (lane < 9) {
+            const int ndy = lane / 3 - 1, ndx = lane % 3 - 1;
+            mv |= bit_window(changed + (long long)clampi(y + ndy, 0, H - 1) * ww, ww, W, x0 + ndx);
         }
-    const long long o = (long long)y * W + x;
-    const bool same = changed[o] == 0;
-    // spread (:38-50): max over the 3 x 3 neighbourhood and channels of |a(q) - a(o)|, |b(q) - b(o)|
+        mv = __reduce_or_sync(0xffffffffu, mv);
+    }
+    const uint32_t own_word = __ldg(changed + (long long)y * ww + blockIdx.x);
+    // spread: column extremes over rows y - 1 .. y + 1, then across the neighbouring lanes' columns
     const uint32_t* A = reinterpret_cast<const uint32_t*>(fa);
     const uint32_t* B = reinterpret_cast<const uint32_t*>(fb);
-    auto at = [&](const uint32_t* f, int yy, int xx) { return __ldg(f + (long long)min(yy, s.h - 1) * s.w + min(xx, s.w - 1)); };
-    const uint32_t ao = at(A, y, x), bo = at(B, y, x);
-    float m = 0.0f;
-    for (int dy = -1; dy <= 1; dy++)
-        for (int dx = -1; dx <= 1; dx++) {
-            const int yy = clampi(y + dy, 0, H - 1), xx = clampi(x + dx, 0, W - 1);
-            const uint32_t aq = at(A, yy, xx), bq = at(B, yy, xx);
-            for (int c = 0; c < 3; c++) {
-                const int sh = 16 - 8 * c;  // channel c of the BGR plane = byte 2 - c of the rgba pixel
-                m = fmaxf(m, fabsf(lut[(aq >> sh) & 255] - lut[(ao >> sh) & 255]));
-                m = fmaxf(m, fabsf(lut[(bq >> sh) & 255] - lut[(bo >> sh) & 255]));
-            }
+    const int r0 = min(max(y - 1, 0), s.h - 1), r1 = min(y, s.h - 1), r2 = min(y + 1, s.h - 1);
+    const int xc = min(x, s.w - 1);
+    const uint32_t a0 = __ldg(A + (long long)r0 * s.w + xc), a1 = __ldg(A + (long long)r1 * s.w + xc),
+                   a2 = __ldg(A + (long long)r2 * s.w + xc);
+    const uint32_t b0 = __ldg(B + (long long)r0 * s.w + xc), b1 = __ldg(B + (long long)r1 * s.w + xc),
+                   b2 = __ldg(B + (long long)r2 * s.w + xc);
+    uint32_t amax = __vmaxu4(__vmaxu4(a0, a1), a2), amin = __vminu4(__vminu4(a0, a1), a2);
+    uint32_t bmax = __vmaxu4(__vmaxu4(b0, b1), b2), bmin = __vminu4(__vminu4(b0, b1), b2);
+    // the edge lanes' outer column: x0 - 1 for lane 0 (x0 itself at the left border), x0 + 32 for lane 31
+    uint32_t eamax = 0, eamin = 0, ebmax = 0, ebmin = 0;
+    if (lane == 0 || lane == 31) {
+        const int xe = lane == 0 ? min(max(x0 - 1, 0), s.w - 1) : min(x0 + 32, s.w - 1);
+        const uint32_t e0 = __ldg(A + (long long)r0 * s.w + xe), e1 = __ldg(A + (long long)r1 * s.w + xe),
+                       e2 = __ldg(A + (long long)r2 * s.w + xe);
+        const uint32_t f0 = __ldg(B + (long long)r0 * s.w + xe), f1 = __ldg(B + (long long)r1 * s.w + xe),
+                       f2 = __ldg(B + (long long)r2 * s.w + xe);
+        eamax = __vmaxu4(__vmaxu4(e0, e1), e2);
+        eamin = __vminu4(__vminu4(e0, e1), e2);
+        ebmax = __vmaxu4(__vmaxu4(f0, f1), f2);
+        ebmin = __vminu4(__vminu4(f0, f1), f2);
+    }
+    {
+        uint32_t l_amax = __shfl_up_sync(0xffffffffu, amax, 1), r_amax = __shfl_down_sync(0xffffffffu, amax, 1);
+        uint32_t l_amin = __shfl_up_sync(0xffffffffu, amin, 1), r_amin = __shfl_down_sync(0xffffffffu, amin, 1);
+        uint32_t l_bmax = __shfl_up_sync(0xffffffffu, bmax, 1), r_bmax = __shfl_down_sync(0xffffffffu, bmax, 1);
+        uint32_t l_bmin = __shfl_up_sync(0xffffffffu, bmin, 1), r_bmin = __shfl_down_sync(0xffffffffu, bmin, 1);
+        if (lane == 0) {
+            l_amax = eamax;
+            l_amin = eamin;
+            l_bmax = ebmax;
+            l_bmin = ebmin;
         }
+        if (lane == 31) {
+            r_amax = eamax;
+            r_amin = eamin;
+            r_bmax = ebmax;
+            r_bmin = ebmin;
+        }
+        amax = __vmaxu4(amax, __vmaxu4(l_amax, r_amax));
+        amin = __vminu4(amin, __vminu4(l_amin, r_amin));
+        bmax = __vmaxu4(bmax, __vmaxu4(l_bmax, r_bmax));
+        bmin = __vminu4(bmin, __vminu4(l_bmin, r_bmin));
+    }
+    if (x >= W) return;
+    float m = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 3; c++) {
+        const int sh = 16 - 8 * c;  // channel c of the BGR plane = byte 2 - c of the rgba pixel
+        const float va = lut[(a1 >> sh) & 255], vb = lut[(b1 >> sh) & 255];
+        m = fmaxf(m, lut[(amax >> sh) & 255] - va);
+        m = fmaxf(m, va - lut[(amin >> sh) & 255]);
+        m = fmaxf(m, lut[(bmax >> sh) & 255] - vb);
+        m = fmaxf(m, vb - lut[(bmin >> sh) & 255]);
+    }
+    const bool moved = (mv >> lane) & 1u;
+    const bool same = ((own_word >> lane) & 1u) == 0;
     const bool still = same && m >= 0.03f;
+    const long long o = (long long)y * W + x;
     uchar4 st = state[o];
     const int raw = still ? min((int)st.x + 1, 255) : 0;
     const int seen = still ? min((int)st.y + (moved ? 1 : 0), 255) : 0;
@@ -393,13 +504,27 @@ __global__ void k_warp_fine(WarpFineArgs a) {
 // reduction reproduces the shader's: 32 workgroups x 256 threads, each thread a strided partial sum, a 256-wide tree
 // per workgroup (off = 128 .. 1), then the solve's sequential sum over workgroups. One warp reduces one
 // (workgroup, channel) pair: lane l holds virtual threads l + 32 k, k = 0..7; the 128 warps of the cluster cover the 32
-// workgroups x 4 channels at once and write their partials into CTA 0's shared memory (distributed shared memory);
-// CTA 0 solves and broadcasts the coefficients to every CTA of the cluster.
+// workgroups x 4 channels at once and write their partials into every CTA's shared memory (distributed shared
+// memory), so each CTA solves on its own copy and one cluster barrier per iteration suffices. The partial buffers
+// alternate between iterations: a CTA writing iteration i + 1's partials has passed iteration i + 1's barrier only after
+// every CTA finished reading iteration i's. A virtual thread's first point (flow value and coordinates) stays in
+// registers across the iterations; further points (more than 8192 flow cells) are reread.
 constexpr int GM_CLUSTER = 8;
+FH_DEV void gm_acc(float w2, float x, float y, float f, float* s) {
+    s[0] = s[0] + w2;
+    s[1] = s[1] + w2 * x;
+    s[2] = s[2] + w2 * y;
+    s[3] = s[3] + w2 * x * x;
+    s[4] = s[4] + w2 * x * y;
+    s[5] = s[5] + w2 * y * y;
+    s[6] = s[6] + w2 * f;
+    s[7] = s[7] + w2 * x * f;
+    s[8] = s[8] + w2 * y * f;
+}
 __global__ void __cluster_dims__(GM_CLUSTER, 1, 1) __launch_bounds__(512, 1) k_gm_fit(GmArgs g) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
-    __shared__ float part[32][4][9];
+    __shared__ float part[2][32][4][9];
     __shared__ float coef[16];
     const unsigned rank = cluster.block_rank();
     const int n = blockIdx.x / GM_CLUSTER;
@@ -409,74 +534,91 @@ __global__ void __cluster_dims__(GM_CLUSTER, 1, 1) __launch_bounds__(512, 1) k_g
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int task = (int)rank * 16 + warp;  // 0..127
     const int wg = task >> 2, c = task & 3;
-    float* part0 = cluster.map_shared_rank(&part[0][0][0], 0);
     if (threadIdx.x < 16) coef[threadIdx.x] = 0.0f;
-    cluster.sync();
-    for (int it = 0; it < 4; it++) {
-        float v[8][9];
+    float f0[8], x0[8], y0[8];
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
-            float s0 = 0, s1 = 0, s2 = 0, s3 = 0, s4 = 0, s5 = 0, s6 = 0, s7 = 0, s8 = 0;
-            for (int i = wg * 256 + lane + 32 * k; i < np; i += 256 * 32) {
-                const int yy = i / w8, xx = i - yy * w8;
-                const float x = -1.0f + sx * (float)xx, y = -1.0f + sy * (float)yy;
-                const float f = h2f(fl[(long long)i * 8 + c]);
-                float w2 = 1.0f;
-                if (it > 0) {
-                    const float r = fabsf(f - (coef[c * 4] + coef[c * 4 + 1] * x + coef[c * 4 + 2] * y));
-                    w2 = g.delta / fmaxf(g.delta, r);
-                }
-                s0 = s0 + w2;
-                s1 = s1 + w2 * x;
-                s2 = s2 + w2 * y;
-                s3 = s3 + w2 * x * x;
-                s4 = s4 + w2 * x * y;
-                s5 = s5 + w2 * y * y;
-                s6 = s6 + w2 * f;
-                s7 = s7 + w2 * x * f;
-                s8 = s8 + w2 * y * f;
-            }
-            v[k][0] = s0; v[k][1] = s1; v[k][2] = s2; v[k][3] = s3; v[k][4] = s4;
-            v[k][5] = s5; v[k][6] = s6; v[k][7] = s7; v[k][8] = s8;
+    for (int k = 0; k < 8; k++) {
+        const int i = wg * 256 + lane + 32 * k;
+        f0[k] = x0[k] = y0[k] = 0.0f;
+        if (i < np) {
+            const int yy = i / w8, xx = i - yy * w8;
+            x0[k] = -1.0f + sx * (float)xx;
+            y0[k] = -1.0f + sy * (float)yy;
+            f0[k] = h2f(fl[(long long)i * 8 + c]);
         }
+    }
+    cluster.sync();  // every CTA runs before any distributed shared memory store
+    for (int it = 0; it < 4; it++) {
+        const float c0 = coef[c * 4], c1 = coef[c * 4 + 1], c2 = coef[c * 4 + 2];
+        // virtual threads k and k + 4 are summed as soon as both are formed (the tree's off = 128 step)
+        float a[4][9];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            float v[2][9];
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int kk = k + 4 * e;
+#pragma unroll
+                for (int q = 0; q < 9; q++) v[e][q] = 0.0f;
+                const int i0 = wg * 256 + lane + 32 * kk;
+                if (i0 < np) {
+                    float w2 = 1.0f;
+                    if (it > 0) w2 = g.delta / fmaxf(g.delta, fabsf(f0[kk] - (c0 + c1 * x0[kk] + c2 * y0[kk])));
+                    gm_acc(w2, x0[kk], y0[kk], f0[kk], v[e]);
+                }
+                for (int i = i0 + 256 * 32; i < np; i += 256 * 32) {
+                    const int yy = i / w8, xx = i - yy * w8;
+                    const float x = -1.0f + sx * (float)xx, y = -1.0f + sy * (float)yy;
+                    const float f = h2f(fl[(long long)i * 8 + c]);
+                    float w2 = 1.0f;
+                    if (it > 0) w2 = g.delta / fmaxf(g.delta, fabsf(f - (c0 + c1 * x + c2 * y)));
+                    gm_acc(w2, x, y, f, v[e]);
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 9; q++) a[k][q] = v[0][q] + v[1][q];
+        }
+        float mine = 0.0f;  // lane q < 9 keeps partial q
 #pragma unroll
         for (int q = 0; q < 9; q++) {
-            // off 128: t += t + 128 (k += k + 4); off 64: k += k + 2; off 32: k += k + 1; then 16 .. 1 in the warp
-            const float a0 = v[0][q] + v[4][q], a1 = v[1][q] + v[5][q], a2 = v[2][q] + v[6][q], a3 = v[3][q] + v[7][q];
-            const float b0 = a0 + a2, b1 = a1 + a3;
+            // off 64: k += k + 2; off 32: k += k + 1; then 16 .. 1 in the warp
+            const float b0 = a[0][q] + a[2][q], b1 = a[1][q] + a[3][q];
             float sum = b0 + b1;
             for (int off = 16; off > 0; off >>= 1) sum = sum + __shfl_down_sync(0xffffffffu, sum, off);
-            if (lane == 0) part0[(wg * 4 + c) * 9 + q] = sum;
+            sum = __shfl_sync(0xffffffffu, sum, 0);
+            if (lane == q) mine = sum;
         }
+        const int buf = it & 1;
+        if (lane < 9)
+#pragma unroll
+            for (unsigned r = 0; r < GM_CLUSTER; r++) cluster.map_shared_rank(&part[buf][0][0][0], r)[(wg * 4 + c) * 9 + lane] = mine;
         cluster.sync();
-        if (rank == 0 && threadIdx.x < 4) {
+        if (threadIdx.x < 4) {
             const int cc = threadIdx.x;
-            float s[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+            float s_[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
             for (int w = 0; w < 32; w++)
-                for (int k = 0; k < 9; k++) s[k] = s[k] + part[w][cc][k];
-            const float m00 = s[0] + 1e-6f, m01 = s[1], m02 = s[2], m11 = s[3] + 1e-6f, m12 = s[4], m22 = s[5] + 1e-6f;
+#pragma unroll
+                for (int k = 0; k < 9; k++) s_[k] = s_[k] + part[buf][w][cc][k];
+            const float m00 = s_[0] + 1e-6f, m01 = s_[1], m02 = s_[2], m11 = s_[3] + 1e-6f, m12 = s_[4], m22 = s_[5] + 1e-6f;
             const float det = m00 * (m11 * m22 - m12 * m12) - m01 * (m01 * m22 - m12 * m02) + m02 * (m01 * m12 - m11 * m02);
-            float c0, c1, c2;
+            float e0, e1, e2;
             if (fabsf(det) < 1e-12f) {
-                c0 = s[6] / fmaxf(s[0], 1e-6f);
-                c1 = c2 = 0.0f;
+                e0 = s_[6] / fmaxf(s_[0], 1e-6f);
+                e1 = e2 = 0.0f;
             } else {
                 const float i00 = (m11 * m22 - m12 * m12) / det, i01 = (m02 * m12 - m01 * m22) / det;
                 const float i02 = (m01 * m12 - m02 * m11) / det, i11 = (m00 * m22 - m02 * m02) / det;
                 const float i12 = (m01 * m02 - m00 * m12) / det, i22 = (m00 * m11 - m01 * m01) / det;
-                c0 = i00 * s[6] + i01 * s[7] + i02 * s[8];
-                c1 = i01 * s[6] + i11 * s[7] + i12 * s[8];
-                c2 = i02 * s[6] + i12 * s[7] + i22 * s[8];
+                e0 = i00 * s_[6] + i01 * s_[7] + i02 * s_[8];
+                e1 = i01 * s_[6] + i11 * s_[7] + i12 * s_[8];
+                e2 = i02 * s_[6] + i12 * s_[7] + i22 * s_[8];
             }
-            for (unsigned r = 0; r < GM_CLUSTER; r++) {
-                float* cr = cluster.map_shared_rank(coef, r);
-                cr[cc * 4] = c0;
-                cr[cc * 4 + 1] = c1;
-                cr[cc * 4 + 2] = c2;
-                cr[cc * 4 + 3] = 0.0f;
-            }
+            coef[cc * 4] = e0;
+            coef[cc * 4 + 1] = e1;
+            coef[cc * 4 + 2] = e2;
+            coef[cc * 4 + 3] = 0.0f;
         }
-        cluster.sync();
+        __syncthreads();
     }
     if (rank == 0 && threadIdx.x < 16) g.coef[n * 16 + threadIdx.x] = coef[threadIdx.x];
 }
@@ -537,10 +679,12 @@ __global__ void k_gm_cost(GmArgs g) {
     maps[2 * nn + i] = sqrtf(dvx * dvx + dvy * dvy);
     maps[3 * nn + i] = l;
     maps[4 * nn + i] = l * l;
-    maps[5 * nn + i] = fabsf(l - samp(B, rx, ry));
+    // gm_cost.wgsl's sixth map (|l - B|) has no reader in the select and is not formed
 }
 
-// gm_box.wgsl box_h / box_v: radius r, edge replicate, the first c maps
+// gm_box.wgsl box_h / box_v: radius r, edge replicate, the first c maps. The select reads the boxed maps only at its
+// sample cells (row ys(i), column xs(j)), so the passes whose result feeds nothing else run there only: each output is
+// formed exactly as the full pass forms it (the same taps in the same order, then / (2r + 1)).
 __global__ void k_box_h(const float* src, float* dst, int c, int h, int w, int r, long long bs) {
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
     const int n = blockIdx.z / c, ch = blockIdx.z - n * c;
@@ -559,17 +703,39 @@ __global__ void k_box_v(const float* src, float* dst, int c, int h, int w, int r
     for (int d = -r; d <= r; d++) acc = acc + src[plane + (long long)clampi(y + d, 0, h - 1) * w + x];
     dst[plane + (long long)y * w + x] = acc / (float)(2 * r + 1);
 }
+// gm_select.wgsl:12-15: the cost cell that select sample j (of w8) reads, along one axis of hc or wc cells
+FH_DEV int gm_cell(int j, int cells, int n8) { return clampi((int)floorf(((float)j + 0.5f) * (float)cells / (float)n8), 0, cells - 1); }
 
-// gm_select.wgsl:12-28 (eps 0, tex 0.015: gmhs.rs:208)
-__global__ void k_gm_select(GmArgs g) {
+// box_h at the select columns: cols[ch][y][j] = box_h(maps[ch])(y, xs(j)) for every row. Maps 0-2 (already through
+// the texture window) take the decision radius, maps 3-4 the texture radius.
+__global__ void k_box_h_cols(GmArgs g, long long cols_bs) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
+    const int n = blockIdx.z / 5, ch = blockIdx.z - n * 5;
+    if (j >= g.w8 || y >= g.hc) return;
+    const int r = ch < 3 ? g.r_dwin : g.r_blk, x = gm_cell(j, g.wc, g.w8);
+    const float* row = g.maps + (long long)n * 6 * g.hc * g.wc + ((long long)ch * g.hc + y) * g.wc;
+    float acc = 0.0f;
+    for (int d = -r; d <= r; d++) acc = acc + row[clampi(x + d, 0, g.wc - 1)];
+    g.tmp[(long long)n * cols_bs + ((long long)ch * g.hc + y) * g.w8 + j] = acc / (float)(2 * r + 1);
+}
+
+// gm_select.wgsl:12-28 (eps 0, tex 0.015: gmhs.rs:208), with the last vertical box pass of each map at its cell
+__global__ void k_gm_select(GmArgs g, long long cols_bs) {
     const int j = blockIdx.x * blockDim.x + threadIdx.x, i = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (j >= g.w8 || i >= g.h8) return;
     const float* coef = g.coef + n * 16;
-    const int x = clampi((int)floorf(((float)j + 0.5f) * (float)g.wc / (float)g.w8), 0, g.wc - 1);
-    const int y = clampi((int)floorf(((float)i + 0.5f) * (float)g.hc / (float)g.h8), 0, g.hc - 1);
-    const long long nn = (long long)g.hc * g.wc, idx = (long long)y * g.wc + x;
-    const float* maps = g.maps + (long long)n * 6 * nn;
-    const float cm = maps[idx], ca = maps[nn + idx], dv = maps[2 * nn + idx], lm = maps[3 * nn + idx], l2 = maps[4 * nn + idx];
+    const int y = gm_cell(i, g.hc, g.h8);
+    const float* cols = g.tmp + (long long)n * cols_bs;
+    float m[5];
+#pragma unroll
+    for (int ch = 0; ch < 5; ch++) {
+        const int r = ch < 3 ? g.r_dwin : g.r_blk;
+        const float* col = cols + (long long)ch * g.hc * g.w8 + j;
+        float acc = 0.0f;
+        for (int d = -r; d <= r; d++) acc = acc + col[(long long)clampi(y + d, 0, g.hc - 1) * g.w8];
+        m[ch] = acc / (float)(2 * r + 1);
+    }
+    const float cm = m[0], ca = m[1], dv = m[2], lm = m[3], l2 = m[4];
     const float sd = sqrtf(fmaxf(l2 - lm * lm, 0.0f));
     const float eps = 0.0f, tex = 0.015f;
     if (ca + eps < cm && dv > g.dmin && sd > tex) {
@@ -751,110 +917,121 @@ FH_DEV float cub2(float x) {
     return ((a * x - 5.0f * a) * x + 8.0f * a) * x - 4.0f * a;
 }
 
-// a source frame as its f16 plane (w x h x 4 halves: B, G, R, 0 = the values tex_in.wgsl stores), read at the
-// clamped position (the replicate padding of the [3][hp][wp] tensor)
-struct Frame {
-    const uint2* p;
-    int w, h;
-    FH_DEV float3 at(int y, int x) const {
-        const uint2 u = __ldg(p + (long long)min(y, h - 1) * w + min(x, w - 1));
-        const float2 bg = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-        const float2 r0 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-        return make_float3(bg.x, bg.y, r0.x);
-    }
-};
+FH_DEV float3 px3(const uint2* p) {
+    const uint2 u = __ldg(p);
+    const float2 bg = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 r0 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float3(bg.x, bg.y, r0.x);
+}
 FH_DEV float comp(const float3& v, int c) { return c == 0 ? v.x : (c == 1 ? v.y : v.z); }
 
-// render.wgsl:82-161 + gpu/pipeline.rs:10-34 (static rules) + keep_static.wgsl:21-32 + rgba_out.wgsl:9-17
+// Bicubic (Keys a = -0.75, per-tap clamp) or bilinear sampling of a source frame at (gx, gy); continuous sums, fused.
+// The frame is its f16 plane (w x h x 4 halves: B, G, R, 0 = the values tex_in.wgsl stores); a tap of the padded
+// [3][hp][wp] tensor at (clamp(y, 0, hp - 1), clamp(x, 0, wp - 1)) reads the frame at the position clamped once
+// more to w x h (the replicate padding), which is clamp(y, 0, h - 1), clamp(x, 0, w - 1) as w <= wp and h <= hp.
+FH_DEV float3 sample_frame(const uint2* __restrict__ f, int w, int h, float gx, float gy, bool cubic) {
+    if (cubic) {
+        const int px = (int)floorf(gx), py = (int)floorf(gy);
+        const float tx = gx - (float)px, ty = gy - (float)py;
+        const float cx0 = cub2(tx + 1.0f), cx1 = cub1(tx), cx2 = cub1(1.0f - tx), cx3 = cub2(2.0f - tx);
+        const float cy[4] = {cub2(ty + 1.0f), cub1(ty), cub1(1.0f - ty), cub2(2.0f - ty)};
+        const int x0 = clampi(px - 1, 0, w - 1), x1 = clampi(px, 0, w - 1), x2 = clampi(px + 1, 0, w - 1),
+                  x3 = clampi(px + 2, 0, w - 1);
+        float3 acc = make_float3(0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint2* row = f + clampi(py - 1 + j, 0, h - 1) * w;
+            const float3 p0 = px3(row + x0), p1 = px3(row + x1), p2 = px3(row + x2), p3 = px3(row + x3);
+            float3 rw;
+            rw.x = fmaf(p3.x, cx3, fmaf(p2.x, cx2, fmaf(p1.x, cx1, p0.x * cx0)));
+            rw.y = fmaf(p3.y, cx3, fmaf(p2.y, cx2, fmaf(p1.y, cx1, p0.y * cx0)));
+            rw.z = fmaf(p3.z, cx3, fmaf(p2.z, cx2, fmaf(p1.z, cx1, p0.z * cx0)));
+            acc.x = fmaf(rw.x, cy[j], acc.x);
+            acc.y = fmaf(rw.y, cy[j], acc.y);
+            acc.z = fmaf(rw.z, cy[j], acc.z);
+        }
+        return acc;
+    }
+    const int xx0 = (int)floorf(gx), yy0 = (int)floorf(gy);
+    const float ax = gx - (float)xx0, ay = gy - (float)yy0;
+    const int x0 = clampi(xx0, 0, w - 1), x1 = clampi(xx0 + 1, 0, w - 1);
+    const uint2* r0 = f + clampi(yy0, 0, h - 1) * w;
+    const uint2* r1 = f + clampi(yy0 + 1, 0, h - 1) * w;
+    const float3 p00 = px3(r0 + x0), p01 = px3(r0 + x1), p10 = px3(r1 + x0), p11 = px3(r1 + x1);
+    return make_float3(bil_mix(p00.x, p01.x, p10.x, p11.x, ax, ay), bil_mix(p00.y, p01.y, p10.y, p11.y, ax, ay),
+                       bil_mix(p00.z, p01.z, p10.z, p11.z, ax, ay));
+}
+
+// render.wgsl:82-161 + gpu/pipeline.rs:10-34 (static rules) + keep_static.wgsl:21-32 + rgba_out.wgsl:9-17.
+// Plane offsets are 32-bit (a padded plane holds < 2^31 pixels; checked by render()).
 __global__ void __launch_bounds__(256) k_render(RenderArgs r) {
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (x >= r.w || y >= r.h) return;
     const int H = r.hp, W = r.wp, hq = r.hq, wq = r.wq;
-    const Frame A{reinterpret_cast<const uint2*>(r.ha + (long long)n * r.h_bs), r.w, r.h};
-    const Frame B{reinterpret_cast<const uint2*>(r.hb + (long long)n * r.h_bs), r.w, r.h};
+    const uint2* __restrict__ A = reinterpret_cast<const uint2*>(r.ha + (long long)n * r.h_bs);
+    const uint2* __restrict__ B = reinterpret_cast<const uint2*>(r.hb + (long long)n * r.h_bs);
     const __half* up = r.up7 + (long long)n * r.up_bs;
     const __half* rt = r.rt + (long long)n * r.rt_bs;
     const int16_t* age = r.age ? r.age + (long long)n * r.age_bs : nullptr;
     // the Q-res sample corners (render.wgsl:87-92)
-    const float sh = (float)hq / (float)H, sw = (float)wq / (float)W;
-    const float iy = ((float)y + 0.5f) * sh - 0.5f, ix = ((float)x + 0.5f) * sw - 0.5f;
+    const float iy = ((float)y + 0.5f) * r.qsy - 0.5f, ix = ((float)x + 0.5f) * r.qsx - 0.5f;
     const int qy0 = (int)floorf(iy), qx0 = (int)floorf(ix);
     const float qfy = iy - (float)qy0, qfx = ix - (float)qx0;
-    const int qy0c = clampi(qy0, 0, hq - 1), qy1c = clampi(qy0 + 1, 0, hq - 1);
-    const int qx0c = clampi(qx0, 0, wq - 1), qx1c = clampi(qx0 + 1, 0, wq - 1);
+    const int qr0 = clampi(qy0, 0, hq - 1) * wq, qr1 = clampi(qy0 + 1, 0, hq - 1) * wq;
+    const int qc0 = clampi(qx0, 0, wq - 1), qc1 = clampi(qx0 + 1, 0, wq - 1);
     // the four Q corners: flow_tq (0-3) and vis_tq (4-6) in one 16-byte load each, R_t in one 8-byte load each
-    const uint4 U00 = __ldg(reinterpret_cast<const uint4*>(up + ((long long)qy0c * wq + qx0c) * 8));
-    const uint4 U01 = __ldg(reinterpret_cast<const uint4*>(up + ((long long)qy0c * wq + qx1c) * 8));
-    const uint4 U10 = __ldg(reinterpret_cast<const uint4*>(up + ((long long)qy1c * wq + qx0c) * 8));
-    const uint4 U11 = __ldg(reinterpret_cast<const uint4*>(up + ((long long)qy1c * wq + qx1c) * 8));
+    const uint4* U = reinterpret_cast<const uint4*>(up);
+    const uint4 U00 = __ldg(U + qr0 + qc0), U01 = __ldg(U + qr0 + qc1), U10 = __ldg(U + qr1 + qc0),
+                U11 = __ldg(U + qr1 + qc1);
+    const uint2* RT = reinterpret_cast<const uint2*>(rt);
+    const uint2 R00 = __ldg(RT + qr0 + qc0), R01 = __ldg(RT + qr0 + qc1), R10 = __ldg(RT + qr1 + qc0),
+                R11 = __ldg(RT + qr1 + qc1);
     const __half* u00 = reinterpret_cast<const __half*>(&U00);
     const __half* u01 = reinterpret_cast<const __half*>(&U01);
     const __half* u10 = reinterpret_cast<const __half*>(&U10);
     const __half* u11 = reinterpret_cast<const __half*>(&U11);
     float f[4], v[3];
+#pragma unroll
     for (int c = 0; c < 4; c++)
         f[c] = bil_mix(h2f(u00[c]), h2f(u01[c]), h2f(u10[c]), h2f(u11[c]), qfx, qfy) * ((c & 1) == 0 ? r.fsx : r.fsy);
+#pragma unroll
     for (int c = 0; c < 3; c++) v[c] = bil_mix(h2f(u00[4 + c]), h2f(u01[4 + c]), h2f(u10[4 + c]), h2f(u11[4 + c]), qfx, qfy) * 1.0f;
     const float m = fmaxf(v[0], fmaxf(v[1], v[2]));
     const float e0 = expf(v[0] - m), e1 = expf(v[1] - m), e2 = expf(v[2] - m);
     const float s = e0 + e1 + e2;
     const float wa_w = (e0 + 0.5f * e2) / s, wb_w = (e1 + 0.5f * e2) / s;
     const float gxa = (float)x + f[0], gya = (float)y + f[1], gxb = (float)x + f[2], gyb = (float)y + f[3];
-    float ca[3], cb[3], cr[3];
-    // bicubic (Keys a = -0.75, per-tap clamp) or bilinear sampling of a source frame; continuous sums, fused
-    auto sample = [&](const Frame& F, float gx, float gy, float* out) {
-        if (r.cubic) {
-            const int px = (int)floorf(gx), py = (int)floorf(gy);
-            const float tx = gx - (float)px, ty = gy - (float)py;
-            const float cx[4] = {cub2(tx + 1.0f), cub1(tx), cub1(1.0f - tx), cub2(2.0f - tx)};
-            const float cy[4] = {cub2(ty + 1.0f), cub1(ty), cub1(1.0f - ty), cub2(2.0f - ty)};
-            int xs[4];
-            for (int k = 0; k < 4; k++) xs[k] = clampi(px - 1 + k, 0, W - 1);
-            float3 acc = make_float3(0.0f, 0.0f, 0.0f);
-            for (int j = 0; j < 4; j++) {
-                const int yy = clampi(py - 1 + j, 0, H - 1);
-                const float3 p0 = F.at(yy, xs[0]), p1 = F.at(yy, xs[1]), p2 = F.at(yy, xs[2]), p3 = F.at(yy, xs[3]);
-                float3 row;
-                row.x = fmaf(p3.x, cx[3], fmaf(p2.x, cx[2], fmaf(p1.x, cx[1], p0.x * cx[0])));
-                row.y = fmaf(p3.y, cx[3], fmaf(p2.y, cx[2], fmaf(p1.y, cx[1], p0.y * cx[0])));
-                row.z = fmaf(p3.z, cx[3], fmaf(p2.z, cx[2], fmaf(p1.z, cx[1], p0.z * cx[0])));
-                acc.x = fmaf(row.x, cy[j], acc.x);
-                acc.y = fmaf(row.y, cy[j], acc.y);
-                acc.z = fmaf(row.z, cy[j], acc.z);
-            }
-            out[0] = acc.x;
-            out[1] = acc.y;
-            out[2] = acc.z;
-        } else {
-            const int xx0 = (int)floorf(gx), yy0 = (int)floorf(gy);
-            const float ax = gx - (float)xx0, ay = gy - (float)yy0;
-            const int x0 = clampi(xx0, 0, W - 1), x1 = clampi(xx0 + 1, 0, W - 1);
-            const int y0 = clampi(yy0, 0, H - 1), y1 = clampi(yy0 + 1, 0, H - 1);
-            const float3 p00 = F.at(y0, x0), p01 = F.at(y0, x1), p10 = F.at(y1, x0), p11 = F.at(y1, x1);
-            for (int c = 0; c < 3; c++)
-                out[c] = bil_mix(comp(p00, c), comp(p01, c), comp(p10, c), comp(p11, c), ax, ay);
-        }
-    };
-    sample(A, gxa, gya, ca);
-    sample(B, gxb, gyb, cb);
-    const uint2 R00 = __ldg(reinterpret_cast<const uint2*>(rt + ((long long)qy0c * wq + qx0c) * 4));
-    const uint2 R01 = __ldg(reinterpret_cast<const uint2*>(rt + ((long long)qy0c * wq + qx1c) * 4));
-    const uint2 R10 = __ldg(reinterpret_cast<const uint2*>(rt + ((long long)qy1c * wq + qx0c) * 4));
-    const uint2 R11 = __ldg(reinterpret_cast<const uint2*>(rt + ((long long)qy1c * wq + qx1c) * 4));
+    const bool cubic = r.cubic != 0;
+    const float3 sa3 = sample_frame(A, r.w, r.h, gxa, gya, cubic);
+    const float3 sb3 = sample_frame(B, r.w, r.h, gxb, gyb, cubic);
+    const float ca[3] = {sa3.x, sa3.y, sa3.z}, cb[3] = {sb3.x, sb3.y, sb3.z};
     const __half* r00 = reinterpret_cast<const __half*>(&R00);
     const __half* r01 = reinterpret_cast<const __half*>(&R01);
     const __half* r10 = reinterpret_cast<const __half*>(&R10);
     const __half* r11 = reinterpret_cast<const __half*>(&R11);
+    float cr[3];
+#pragma unroll
     for (int c = 0; c < 3; c++) cr[c] = bil_mix(h2f(r00[c]), h2f(r01[c]), h2f(r10[c]), h2f(r11[c]), qfx, qfy);
     float bwa = wa_w, bwb = wb_w, rk = 1.0f, stillw = 0.0f, own[3] = {0.0f, 0.0f, 0.0f};
     const float third = 1.0f / 3.0f;
-    const float3 pa_here = A.at(y, x), pb_here = B.at(y, x);
+    const int here = y * r.w + x;  // x < w, y < h: no clamp
+    const float3 pa_here = px3(A + here), pb_here = px3(B + here);
+    const int o = y * W + x;
     if (r.flags & 2u) {
         // the 27-term sum of |A - B| over the clamped 3 x 3 neighbourhood, from the per-pixel channel sums (exact)
         const float* ds = r.dsum + (long long)n * r.plane_bs;
+        const int ym = max(y - 1, 0) * W, yc = y * W, yp = min(y + 1, H - 1) * W;
+        const int xm = max(x - 1, 0), xp = min(x + 1, W - 1);
         float es = 0.0f;
-        for (int dy = -1; dy <= 1; dy++)
-            for (int dx = -1; dx <= 1; dx++) es += __ldg(ds + (long long)clampi(y + dy, 0, H - 1) * W + clampi(x + dx, 0, W - 1));
+        es += __ldg(ds + ym + xm);
+        es += __ldg(ds + ym + x);
+        es += __ldg(ds + ym + xp);
+        es += __ldg(ds + yc + xm);
+        es += __ldg(ds + yc + x);
+        es += __ldg(ds + yc + xp);
+        es += __ldg(ds + yp + xm);
+        es += __ldg(ds + yp + x);
+        es += __ldg(ds + yp + xp);
         es = es / 27.0f;
         for (int c = 0; c < 3; c++) own[c] = 0.5f * (comp(pa_here, c) + comp(pb_here, c));
         const float ef = fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
@@ -868,20 +1045,20 @@ __global__ void __launch_bounds__(256) k_render(RenderArgs r) {
         bwb = wb_w * (1.0f - k) + (1.0f - pa) * k;
         rk = 1.0f - k;
     }
-    float raw = 0.0f;
-    const long long o = (long long)y * W + x;
+    float raw = 0.0f, kk = 0.0f;
     if (age) {
         const uint8_t* near = r.near + (long long)n * r.plane_bs;
         auto on_static = [&](float gx, float gy) {
             const int cx = (int)rintf(gx), cy = (int)rintf(gy);  // WGSL round(): half to even
-            if (cx >= 0 && cx < W && cy >= 0 && cy < H) return __ldg(near + (long long)cy * W + cx) != 0;
+            if (cx >= 0 && cx < W && cy >= 0 && cy < H) return __ldg(near + cy * W + cx) != 0;
             for (int dy = -1; dy <= 1; dy++)
                 for (int dx = -1; dx <= 1; dx++)
-                    if ((float)age[(long long)clampi(cy + dy, 0, H - 1) * W + clampi(cx + dx, 0, W - 1)] >= r.min_age) return true;
+                    if ((float)age[clampi(cy + dy, 0, H - 1) * W + clampi(cx + dx, 0, W - 1)] >= r.min_age) return true;
             return false;
         };
         const bool sa = on_static(gxa, gya), sb = on_static(gxb, gyb);
-        stillw = stillw * (fabsf((float)age[o]) >= 3.0f ? 1.0f : 0.0f);
+        const float age_o = (float)age[o];
+        stillw = stillw * (fabsf(age_o) >= 3.0f ? 1.0f : 0.0f);
         if (sa && sb) {
             rk = 0.0f;
             raw = 1.0f;
@@ -894,10 +1071,11 @@ __global__ void __launch_bounds__(256) k_render(RenderArgs r) {
             bwa = 1.0f;
             bwb = 0.0f;
         }
+        // keep_static apply ramp (keep_static.wgsl:25-26)
+        kk = fminf(fmaxf((age_o - r.min_age + 2.0f) / 2.0f, 0.0f), 1.0f);
     }
-    // keep_static apply ramp (keep_static.wgsl:25-26)
-    const float kk = age ? fminf(fmaxf(((float)age[o] - r.min_age + 2.0f) / 2.0f, 0.0f), 1.0f) : 0.0f;
     uint32_t q[3];
+#pragma unroll
     for (int c = 0; c < 3; c++) {
         const float mixv = ca[c] * bwa + cb[c] * bwb + cr[c] * rk;
         float ov = fminf(fmaxf(mixv * (1.0f - stillw) + own[c] * stillw, 0.0f), 1.0f);
@@ -908,8 +1086,7 @@ __global__ void __launch_bounds__(256) k_render(RenderArgs r) {
         q[c] = (uint32_t)(fminf(fmaxf(hv, 0.0f), 1.0f) * 255.0f + 0.5f);
     }
     // q[0] = B, q[1] = G, q[2] = R
-    reinterpret_cast<uint32_t*>(r.out + (long long)n * r.out_bs)[(long long)y * r.w + x] =
-        q[2] | (q[1] << 8) | (q[0] << 16) | 0xff000000u;
+    reinterpret_cast<uint32_t*>(r.out + (long long)n * r.out_bs)[here] = q[2] | (q[1] << 8) | (q[0] << 16) | 0xff000000u;
 }
 
 __global__ void k_set_scalar(float* d, float v) { *d = v; }
@@ -960,7 +1137,7 @@ cudaError_t input_pyramid(Img4 A, int ih, int iw, Img4 aq, Img4 i8, Img4 i16, in
     return cudaGetLastError();
 }
 
-cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, const StaticArgs& s, uint8_t* changed, float* dsum,
+cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, const StaticArgs& s, uint32_t* changed, float* dsum,
                         cudaStream_t st) {
     k_pair_planes<<<grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st>>>(fa, fb, s, changed, dsum);
     return cudaGetLastError();
@@ -971,7 +1148,7 @@ cudaError_t static_near(const int16_t* age, int wp, int hp, float min_age, uint8
     return cudaGetLastError();
 }
 
-cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, const uint8_t* changed, const uint8_t* mask,
+cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, const uint32_t* changed, const uint8_t* mask,
                        const StaticArgs& s, uchar4* state, int16_t* age, cudaStream_t st) {
     k_static_age<<<grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st>>>(fa, fb, changed, mask, s, state, age);
     return cudaGetLastError();
@@ -998,21 +1175,35 @@ cudaError_t warp_fine(const WarpFineArgs& a, int n, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-cudaError_t gmhs(const GmArgs& g, int n, cudaStream_t st) {
+// The texture window over maps 0-2 in full (the decision window reads all of it), then both windows' remaining passes
+// at the select cells only: horizontal at the select columns (k_box_h_cols), vertical inside the select.
+cudaError_t gmhs_fit(const GmArgs& g, int n, cudaStream_t st) {
     k_gm_fit<<<n * GM_CLUSTER, 512, 0, st>>>(g);
+    return cudaGetLastError();
+}
+cudaError_t gmhs_maps(const GmArgs& g, int n, cudaStream_t st) {
+    if (g.w8 > g.wc) return cudaErrorInvalidValue;  // the column planes live in tmp's [5][hc][wc] per entry
     k_gm_cost<<<grid2(g.wc, g.hc, n, 32, 8), dim3(32, 8), 0, st>>>(g);
     const long long bs5 = 5LL * g.hc * g.wc, bs6 = 6LL * g.hc * g.wc;
-    // maps and tmp have different batch strides: run the box passes per batch entry when n > 1
+    // maps and tmp have different batch strides: run the full passes per batch entry when n > 1
     for (int i = 0; i < n; i++) {
         float* maps = g.maps + i * bs6;
         float* tmp = g.tmp + i * bs5;
-        k_box_h<<<grid2(g.wc, g.hc, 5, 32, 8), dim3(32, 8), 0, st>>>(maps, tmp, 5, g.hc, g.wc, g.r_blk, 0);
-        k_box_v<<<grid2(g.wc, g.hc, 5, 32, 8), dim3(32, 8), 0, st>>>(tmp, maps, 5, g.hc, g.wc, g.r_blk, 0);
-        k_box_h<<<grid2(g.wc, g.hc, 3, 32, 8), dim3(32, 8), 0, st>>>(maps, tmp, 3, g.hc, g.wc, g.r_dwin, 0);
-        k_box_v<<<grid2(g.wc, g.hc, 3, 32, 8), dim3(32, 8), 0, st>>>(tmp, maps, 3, g.hc, g.wc, g.r_dwin, 0);
+        k_box_h<<<grid2(g.wc, g.hc, 3, 32, 8), dim3(32, 8), 0, st>>>(maps, tmp, 3, g.hc, g.wc, g.r_blk, 0);
+        k_box_v<<<grid2(g.wc, g.hc, 3, 32, 8), dim3(32, 8), 0, st>>>(tmp, maps, 3, g.hc, g.wc, g.r_blk, 0);
     }
-    k_gm_select<<<grid2(g.w8, g.h8, n, 16, 8), dim3(16, 8), 0, st>>>(g);
+    k_box_h_cols<<<grid2(g.w8, g.hc, 5 * n, 32, 8), dim3(32, 8), 0, st>>>(g, bs5);
     return cudaGetLastError();
+}
+cudaError_t gmhs_select(const GmArgs& g, int n, cudaStream_t st) {
+    k_gm_select<<<grid2(g.w8, g.h8, n, 16, 8), dim3(16, 8), 0, st>>>(g, 5LL * g.hc * g.wc);
+    return cudaGetLastError();
+}
+cudaError_t gmhs(const GmArgs& g, int n, cudaStream_t st) {
+    cudaError_t e = gmhs_fit(g, n, st);
+    if (e == cudaSuccess) e = gmhs_maps(g, n, st);
+    if (e == cudaSuccess) e = gmhs_select(g, n, st);
+    return e;
 }
 
 cudaError_t film(const FilmArgs& a, int n, cudaStream_t st) {
@@ -1039,7 +1230,11 @@ cudaError_t refine_input(const __half* up7, long long up_bs, Img4 aq, Img4 bq, i
     return cudaGetLastError();
 }
 
-cudaError_t render(const RenderArgs& r, int n, cudaStream_t st) {
+cudaError_t render(const RenderArgs& r0, int n, cudaStream_t st) {
+    if ((long long)r0.hp * r0.wp >= (1ll << 31) || r0.w > r0.wp || r0.h > r0.hp) return cudaErrorInvalidValue;
+    RenderArgs r = r0;
+    r.qsy = (float)r.hq / (float)r.hp;  // the same IEEE quotients render.wgsl:87-88 forms per pixel
+    r.qsx = (float)r.wq / (float)r.wp;
     k_render<<<grid2(r.w, r.h, n, 32, 8), dim3(32, 8), 0, st>>>(r);
     return cudaGetLastError();
 }

@@ -27,12 +27,14 @@ struct StaticArgs {
     float thr, min_age;
     int use_mask;
 };
-// per pair: changed (diff >= thr, when protecting) and dsum (sum_c |A - B|, when the still test is on), padded plane
-cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, const StaticArgs& s, uint8_t* changed, float* dsum,
+// per pair: changed (diff >= thr, when protecting; one bit per pixel, changed_words(wp) 32-bit words per row) and
+// dsum (sum_c |A - B|, when the still test is on), padded plane
+inline int changed_words(int wp) { return (wp + 31) >> 5; }
+cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, const StaticArgs& s, uint32_t* changed, float* dsum,
                         cudaStream_t st);
 // per pair after the age pass: near = an age >= min_age in the clamped 3 x 3 neighbourhood (render_static on_static)
 cudaError_t static_near(const int16_t* age, int wp, int hp, float min_age, uint8_t* near, cudaStream_t st);
-cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, const uint8_t* changed, const uint8_t* mask,
+cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, const uint32_t* changed, const uint8_t* mask,
                        const StaticArgs& s, uchar4* state, int16_t* age, cudaStream_t st);
 
 // luma.wgsl + sad.wgsl on two 3-channel images (a view at channel offset 0): (2r+1)^2 cost channels into out (cs)
@@ -72,6 +74,10 @@ struct GmArgs {
     float* tmp;   // [n][5][hc][wc]
 };
 cudaError_t gmhs(const GmArgs& g, int n, cudaStream_t st);
+// gmhs in its three steps (for per-step timing): the affine fit, the cost maps and windows, the select
+cudaError_t gmhs_fit(const GmArgs& g, int n, cudaStream_t st);
+cudaError_t gmhs_maps(const GmArgs& g, int n, cudaStream_t st);
+cudaError_t gmhs_select(const GmArgs& g, int n, cudaStream_t st);
 
 // FiLM (net/build.rs:332-359 film_mlp + film.wgsl): g = b2 + W2 relu(w1 t + b1) from the device scalar t, stored f16;
 // hm = h * (1 + g[c]) + g[c + C]
@@ -125,6 +131,7 @@ struct RenderArgs {
     float min_age;
     uint8_t* out;            // w x h x 4
     long long out_bs;
+    float qsy, qsx;          // hq / hp and wq / wp (set by render())
 };
 cudaError_t render(const RenderArgs& r, int n, cudaStream_t st);
 
