@@ -29,6 +29,7 @@
 
 #include "fh_device.cuh"
 #include "fh_kernels.h"
+#include "launch.h"
 
 namespace {
 
@@ -98,6 +99,10 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
             for (int r = lane; r < per; r += 32)
                 cp_async16(dst0 + (uint32_t)(k * NT * 256 + r * 16), src0 + (size_t)k * ntt * 256 + (size_t)r * 16);
     }
+    // the weights, bias and slopes are written only when the session is planned: read above before the wait for the
+    // preceding kernel, which covers every other access
+    pdl_wait();
+    pdl_trigger();
 
     // ---- halo tile: IH x IW pixels x cp channels, zero outside the image and beyond every source. The 128 threads
     //      form groups of LP (a power of two >= the chunk count) lanes per pixel: a thread owns one 8-channel chunk
@@ -313,8 +318,7 @@ cudaError_t launch_t(FhConvParams p, cudaStream_t st) {
         configured = 227 * 1024;
     }
     dim3 grid((p.wo + TW - 1) / TW, (p.ho + 2 * p.wm - 1) / (2 * p.wm), p.n * p.ngroups);
-    k<<<grid, WARPS * 32, smem, st>>>(p);
-    return cudaGetLastError();
+    return fhk::launch(k, grid, dim3(WARPS * 32), smem, st, p);
 }
 
 template <int S>

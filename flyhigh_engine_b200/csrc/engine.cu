@@ -30,6 +30,7 @@
 #include "../../include/flyhigh_b200.h"
 #include "fh_kernels.h"
 #include "json.hpp"
+#include "launch.h"
 #include "stages.h"
 
 namespace {
@@ -319,6 +320,7 @@ struct FhSession {
     cudaStream_t side = nullptr;
     cudaEvent_t fork_ev[4] = {}, join_ev[4] = {};
     int branches = 0;  // forks of the stage being issued, all joined by join_branches()
+    bool pdl_on = true;  // programmatic dependent launch inside the stage graphs (FH_PDL=0 turns it off)
     std::vector<void*> allocs;
     size_t bytes = 0;
 
@@ -714,6 +716,9 @@ struct FhSession {
         cudaGraph_t g = nullptr;
         CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
         try {
+            // consecutive kernels of a stage overlap launch and drain (every kernel here starts with
+            // griddepcontrol.wait)
+            fhk::PdlScope pdl(pdl_on);
             body();
         } catch (...) {
             branches = 0;
@@ -945,6 +950,7 @@ void derive(const FhModel* m, const FhSessionOptions& o, FhSession* s) {
     // FH_BLEND=decisive (read when the session is built, as the reference's NetOpts are)
     s->still = !env_is("FH_STILL", "0");
     s->decisive = env_is("FH_BLEND", "decisive");
+    s->pdl_on = !env_is("FH_PDL", "0");
     const bool keep_static = o.keep_static != 0;
     s->protects = keep_static || o.protection_mask;
     const int frames = keep_static ? std::clamp((int)(o.static_frames ? o.static_frames : 8), 1, 255) : 2;

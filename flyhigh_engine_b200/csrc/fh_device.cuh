@@ -15,6 +15,12 @@ FH_DEV __half f2h(float v) { return __float2half_rn(v); }
 // the f16 rounding of an f32 value, back in f32 (a stored-and-reloaded intermediate)
 FH_DEV float rh(float v) { return __half2float(__float2half_rn(v)); }
 
+// Programmatic dependent launch. Every kernel waits for the grids it depends on before it touches device memory that
+// an earlier kernel may write or read (inputs, outputs, scratch), and then lets the next kernel of the stream launch,
+// whose CTAs take free SM slots and wait in turn. Without the launch attribute both are no-ops.
+FH_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+FH_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" :::); }
+
 FH_DEV int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
 
 // rgba8 byte -> the value the reference's tex_in / rgba_in store: f16(byte / 255) (tex_in.wgsl:14-18)

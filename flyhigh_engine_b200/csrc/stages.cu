@@ -9,6 +9,7 @@
 
 #include "fh_device.cuh"
 #include "fh_kernels.h"
+#include "launch.h"
 #include "stages.h"
 
 namespace fhk {
@@ -46,6 +47,8 @@ __global__ void k_frame_to_input(const uint8_t* __restrict__ frames, long long f
     __shared__ float lut[256];
     for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
     __syncthreads();
+    pdl_wait();
+    pdl_trigger();
     const int ox = blockIdx.x * blockDim.x + threadIdx.x, oy = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (ox >= ow || oy >= oh) return;
     const uint32_t* f = reinterpret_cast<const uint32_t*>(frames + (long long)n * frame_bs);
@@ -108,6 +111,8 @@ __global__ void k_frame_to_input(const uint8_t* __restrict__ frames, long long f
 // interp.wgsl aa (x0.25) into a 16 x 16 tile of aq in shared memory, then avgpool.wgsl twice
 __global__ void k_input_pyramid(const __half* __restrict__ A, long long a_bs, int ih, int iw, __half* aq, long long aq_bs,
                                 int qh, int qw, __half* i8, long long i8_bs, __half* i16, long long i16_bs) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float tq[16][16][3];
     __shared__ float t8[8][8][3];
     const int lx = threadIdx.x & 15, ly = threadIdx.x >> 4, n = blockIdx.z;
@@ -200,6 +205,8 @@ __global__ void __launch_bounds__(256) k_pair_planes(const uint8_t* __restrict__
     __shared__ float lut[256];
     for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
     __syncthreads();
+    pdl_wait();
+    pdl_trigger();
     const int x = blockIdx.x * 32 + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
     if (y >= s.hp) return;  // warp-uniform
     const bool in = x < s.wp;
@@ -225,6 +232,8 @@ __global__ void __launch_bounds__(256) k_pair_planes(const uint8_t* __restrict__
 
 // render_static's on_static (gpu/pipeline.rs:10-34) per pixel: an age >= min_age in the clamped 3 x 3 neighbourhood
 __global__ void k_static_near(const int16_t* __restrict__ age, int W, int H, float min_age, uint8_t* near) {
+    pdl_wait();
+    pdl_trigger();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
     if (x >= W || y >= H) return;
     bool hit = false;
@@ -265,6 +274,8 @@ __global__ void __launch_bounds__(256) k_static_age(const uint8_t* __restrict__ 
     __shared__ float lut[256];
     for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
     __syncthreads();
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x, x0 = blockIdx.x * 32, x = x0 + lane, y = blockIdx.y * blockDim.y + threadIdx.y;
     // the padded plane: p.w = wp, p.h = hp in the reference dispatch (StaticParams::new(net, wp, hp, wp, hp))
     const int W = s.wp, H = s.hp, ww = (W + 31) >> 5;
@@ -366,6 +377,8 @@ __global__ void __launch_bounds__(256) k_static_age(const uint8_t* __restrict__ 
 template <int R>
 __global__ void k_sad(const __half* __restrict__ a, int a_cs, const __half* __restrict__ b, int b_cs, long long in_bs,
                       int h, int w, __half* out, int out_cs, long long out_bs) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int SP = 2 * R + 1, WIN = SP + 2;
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (x >= w || y >= h) return;
@@ -408,6 +421,8 @@ __global__ void k_sad(const __half* __restrict__ a, int a_cs, const __half* __re
 // interp.wgsl:19-28 bilinear (align_corners = False) of o[0:4] x 16 (the `flow16` view) and o[4:7] (`vis16`)
 __global__ void k_upsample_flow_vis(const __half* __restrict__ o, int o_cs, long long o_bs, int ih, int iw, __half* fv,
                                     long long fv_bs, int oh, int ow) {
+    pdl_wait();
+    pdl_trigger();
     const int ox = blockIdx.x * blockDim.x + threadIdx.x, oy = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (ox >= ow || oy >= oh) return;
     const float sh = (float)ih / (float)oh, sw = (float)iw / (float)ow;
@@ -460,6 +475,8 @@ FH_DEV float bil_mix(float v00, float v01, float v10, float v11, float ax, float
 // warp.wgsl of the fine loop: one thread per e8 pixel writes wa, wb, ia, ib (all channels). The four corners of a
 // side are read as 16-byte vectors before anything is stored.
 __global__ void k_warp_fine(WarpFineArgs a) {
+    pdl_wait();
+    pdl_trigger();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (x >= a.w8 || y >= a.h8) return;
     const uint4 fvv = __ldg(reinterpret_cast<const uint4*>(a.fv + (long long)n * a.fv_bs + ((long long)y * a.w8 + x) * 8));
@@ -522,6 +539,8 @@ FH_DEV void gm_acc(float w2, float x, float y, float f, float* s) {
     s[8] = s[8] + w2 * y * f;
 }
 __global__ void __cluster_dims__(GM_CLUSTER, 1, 1) __launch_bounds__(512, 1) k_gm_fit(GmArgs g) {
+    pdl_wait();
+    pdl_trigger();
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     __shared__ float part[2][32][4][9];
@@ -625,6 +644,8 @@ __global__ void __cluster_dims__(GM_CLUSTER, 1, 1) __launch_bounds__(512, 1) k_g
 
 // gm_cost.wgsl:15-75
 __global__ void k_gm_cost(GmArgs g) {
+    pdl_wait();
+    pdl_trigger();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (x >= g.wc || y >= g.hc) return;
     const float* coef = g.coef + n * 16;
@@ -686,6 +707,8 @@ __global__ void k_gm_cost(GmArgs g) {
 // sample cells (row ys(i), column xs(j)), so the passes whose result feeds nothing else run there only: each output is
 // formed exactly as the full pass forms it (the same taps in the same order, then / (2r + 1)).
 __global__ void k_box_h(const float* src, float* dst, int c, int h, int w, int r, long long bs) {
+    pdl_wait();
+    pdl_trigger();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
     const int n = blockIdx.z / c, ch = blockIdx.z - n * c;
     if (x >= w || y >= h) return;
@@ -695,6 +718,8 @@ __global__ void k_box_h(const float* src, float* dst, int c, int h, int w, int r
     dst[row + x] = acc / (float)(2 * r + 1);
 }
 __global__ void k_box_v(const float* src, float* dst, int c, int h, int w, int r, long long bs) {
+    pdl_wait();
+    pdl_trigger();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
     const int n = blockIdx.z / c, ch = blockIdx.z - n * c;
     if (x >= w || y >= h) return;
@@ -709,6 +734,8 @@ FH_DEV int gm_cell(int j, int cells, int n8) { return clampi((int)floorf(((float
 // box_h at the select columns: cols[ch][y][j] = box_h(maps[ch])(y, xs(j)) for every row. Maps 0-2 (already through
 // the texture window) take the decision radius, maps 3-4 the texture radius.
 __global__ void k_box_h_cols(GmArgs g, long long cols_bs) {
+    pdl_wait();
+    pdl_trigger();
     const int j = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
     const int n = blockIdx.z / 5, ch = blockIdx.z - n * 5;
     if (j >= g.w8 || y >= g.hc) return;
@@ -721,6 +748,8 @@ __global__ void k_box_h_cols(GmArgs g, long long cols_bs) {
 
 // gm_select.wgsl:12-28 (eps 0, tex 0.015: gmhs.rs:208), with the last vertical box pass of each map at its cell
 __global__ void k_gm_select(GmArgs g, long long cols_bs) {
+    pdl_wait();
+    pdl_trigger();
     const int j = blockIdx.x * blockDim.x + threadIdx.x, i = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (j >= g.w8 || i >= g.h8) return;
     const float* coef = g.coef + n * 16;
@@ -749,6 +778,8 @@ __global__ void k_gm_select(GmArgs g, long long cols_bs) {
 
 // net/build.rs:332-359 film_mlp (f32, in the host's order) + film.wgsl:9-15
 __global__ void k_film(FilmArgs a) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ float sm[];
     float* hv = sm;              // [hidden]
     float* gv = sm + a.hidden;   // [2 cr], f16-rounded
@@ -792,6 +823,8 @@ __global__ void k_film(FilmArgs a) {
 
 __global__ void k_mid_combine(const float* tt, const __half* __restrict__ fv, long long fv_bs, const __half* __restrict__ d,
                               long long d_bs, __half* ft, long long ft_bs, int h8, int w8) {
+    pdl_wait();
+    pdl_trigger();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (x >= w8 || y >= h8) return;
     const float t = tt[n];
@@ -814,6 +847,8 @@ __global__ void k_mid_combine(const float* tt, const __half* __restrict__ fv, lo
 // convex.wgsl:10-35, all 7 channels of one output pixel per thread
 __global__ void k_convex(const __half* __restrict__ wt, int wt_cs, long long wt_bs, const __half* __restrict__ x,
                          long long x_bs, int h, int w, __half* up, long long up_bs) {
+    pdl_wait();
+    pdl_trigger();
     const int ox = blockIdx.x * blockDim.x + threadIdx.x, oy = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (ox >= 2 * w || oy >= 2 * h) return;
     const int ihh = oy / 2, iww = ox / 2, sy = oy % 2, sx = ox % 2;
@@ -871,6 +906,8 @@ FH_DEV void blendmix_at(const __half* aq, const __half* bq, const __half* up7, i
 
 __global__ void k_refine_input(const __half* __restrict__ up7, long long up_bs, Img4 aq, Img4 bq, int h, int w, __half* rx,
                                long long rx_bs) {
+    pdl_wait();
+    pdl_trigger();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (x >= w || y >= h) return;
     const __half* u = up7 + (long long)n * up_bs;
@@ -965,6 +1002,8 @@ FH_DEV float3 sample_frame(const uint2* __restrict__ f, int w, int h, float gx, 
 // render.wgsl:82-161 + gpu/pipeline.rs:10-34 (static rules) + keep_static.wgsl:21-32 + rgba_out.wgsl:9-17.
 // Plane offsets are 32-bit (a padded plane holds < 2^31 pixels; checked by render()).
 __global__ void __launch_bounds__(256) k_render(RenderArgs r) {
+    pdl_wait();
+    pdl_trigger();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (x >= r.w || y >= r.h) return;
     const int H = r.hp, W = r.wp, hq = r.hq, wq = r.wq;
@@ -1093,6 +1132,8 @@ __global__ void k_set_scalar(float* d, float v) { *d = v; }
 
 // a bounded busy wait: returns after `cycles` clock cycles of its own SM
 __global__ void k_delay(long long cycles) {
+    pdl_wait();
+    pdl_trigger();
     const long long t0 = clock64();
     while (clock64() - t0 < cycles) {
     }
@@ -1103,6 +1144,8 @@ __global__ void k_frame_half(const uint8_t* __restrict__ f, long long f_bs, int 
     __shared__ float lut[256];
     for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
     __syncthreads();
+    pdl_wait();
+    pdl_trigger();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (x >= w || y >= h) return;
     const uint32_t v = __ldg(reinterpret_cast<const uint32_t*>(f + (long long)n * f_bs) + (long long)y * w + x);
@@ -1110,6 +1153,8 @@ __global__ void k_frame_half(const uint8_t* __restrict__ f, long long f_bs, int 
 }
 
 __global__ void k_frame_planes(const uint8_t* f, int w, int h, int hp, int wp, float* out) {
+    pdl_wait();
+    pdl_trigger();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
     if (x >= wp || y >= hp) return;
     const uint32_t v = reinterpret_cast<const uint32_t*>(f)[(long long)min(y, h - 1) * w + min(x, w - 1)];
@@ -1126,77 +1171,77 @@ __global__ void k_frame_planes(const uint8_t* f, int w, int h, int hp, int wp, f
 cudaError_t frame_to_input(const uint8_t* frames, long long frame_bs, int w, int h, int hp, int wp, bool internal, int ih,
                            int iw, Img4 out, int n, cudaStream_t st) {
     const int oh = internal ? ih : hp, ow = internal ? iw : wp;
-    k_frame_to_input<<<grid2(ow, oh, n), dim3(16, 16), 0, st>>>(frames, frame_bs, w, h, hp, wp, internal ? 1 : 0, oh, ow,
-                                                               out.p, out.bs);
+    { const cudaError_t e_ = launch(k_frame_to_input, grid2(ow, oh, n), dim3(16, 16), 0, st, frames, frame_bs, w, h, hp, wp, internal ? 1 : 0, oh, ow,
+                                                               out.p, out.bs); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
 cudaError_t input_pyramid(Img4 A, int ih, int iw, Img4 aq, Img4 i8, Img4 i16, int n, cudaStream_t st) {
     const int qh = ih / 4, qw = iw / 4;  // floor(h * 0.25) (net/build.rs:204-205)
-    k_input_pyramid<<<grid2(qw, qh, n), 256, 0, st>>>(A.p, A.bs, ih, iw, aq.p, aq.bs, qh, qw, i8.p, i8.bs, i16.p, i16.bs);
+    { const cudaError_t e_ = launch(k_input_pyramid, grid2(qw, qh, n), 256, 0, st, A.p, A.bs, ih, iw, aq.p, aq.bs, qh, qw, i8.p, i8.bs, i16.p, i16.bs); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
 cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, const StaticArgs& s, uint32_t* changed, float* dsum,
                         cudaStream_t st) {
-    k_pair_planes<<<grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st>>>(fa, fb, s, changed, dsum);
+    { const cudaError_t e_ = launch(k_pair_planes, grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st, fa, fb, s, changed, dsum); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
 cudaError_t static_near(const int16_t* age, int wp, int hp, float min_age, uint8_t* near, cudaStream_t st) {
-    k_static_near<<<grid2(wp, hp, 1, 32, 8), dim3(32, 8), 0, st>>>(age, wp, hp, min_age, near);
+    { const cudaError_t e_ = launch(k_static_near, grid2(wp, hp, 1, 32, 8), dim3(32, 8), 0, st, age, wp, hp, min_age, near); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
 cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, const uint32_t* changed, const uint8_t* mask,
                        const StaticArgs& s, uchar4* state, int16_t* age, cudaStream_t st) {
-    k_static_age<<<grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st>>>(fa, fb, changed, mask, s, state, age);
+    { const cudaError_t e_ = launch(k_static_age, grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st, fa, fb, changed, mask, s, state, age); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
 cudaError_t sad_volume(const __half* a, int a_cs, const __half* b, int b_cs, long long in_bs, int h, int w, int r,
                        __half* out, int out_cs, long long out_bs, int n, cudaStream_t st) {
     dim3 g = grid2(w, h, n, 16, 8), blk(16, 8);
-    if (r == 3) k_sad<3><<<g, blk, 0, st>>>(a, a_cs, b, b_cs, in_bs, h, w, out, out_cs, out_bs);
-    else if (r == 2) k_sad<2><<<g, blk, 0, st>>>(a, a_cs, b, b_cs, in_bs, h, w, out, out_cs, out_bs);
+    if (r == 3) { const cudaError_t e_ = launch(k_sad<3>, g, blk, 0, st, a, a_cs, b, b_cs, in_bs, h, w, out, out_cs, out_bs); if (e_ != cudaSuccess) return e_; }
+    else if (r == 2) { const cudaError_t e_ = launch(k_sad<2>, g, blk, 0, st, a, a_cs, b, b_cs, in_bs, h, w, out, out_cs, out_bs); if (e_ != cudaSuccess) return e_; }
     else return cudaErrorInvalidValue;
     return cudaGetLastError();
 }
 
 cudaError_t upsample_flow_vis(const __half* o, int o_cs, long long o_bs, int h16, int w16, __half* fv, long long fv_bs,
                               int h8, int w8, int n, cudaStream_t st) {
-    k_upsample_flow_vis<<<grid2(w8, h8, n, 16, 8), dim3(16, 8), 0, st>>>(o, o_cs, o_bs, h16, w16, fv, fv_bs, h8, w8);
+    { const cudaError_t e_ = launch(k_upsample_flow_vis, grid2(w8, h8, n, 16, 8), dim3(16, 8), 0, st, o, o_cs, o_bs, h16, w16, fv, fv_bs, h8, w8); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
 cudaError_t warp_fine(const WarpFineArgs& a, int n, cudaStream_t st) {
     if (a.c8 > 40) return cudaErrorInvalidValue;
-    k_warp_fine<<<grid2(a.w8, a.h8, n, 16, 8), dim3(16, 8), 0, st>>>(a);
+    { const cudaError_t e_ = launch(k_warp_fine, grid2(a.w8, a.h8, n, 16, 8), dim3(16, 8), 0, st, a); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
 // The texture window over maps 0-2 in full (the decision window reads all of it), then both windows' remaining passes
 // at the select cells only: horizontal at the select columns (k_box_h_cols), vertical inside the select.
 cudaError_t gmhs_fit(const GmArgs& g, int n, cudaStream_t st) {
-    k_gm_fit<<<n * GM_CLUSTER, 512, 0, st>>>(g);
+    { const cudaError_t e_ = launch(k_gm_fit, n * GM_CLUSTER, 512, 0, st, g); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 cudaError_t gmhs_maps(const GmArgs& g, int n, cudaStream_t st) {
     if (g.w8 > g.wc) return cudaErrorInvalidValue;  // the column planes live in tmp's [5][hc][wc] per entry
-    k_gm_cost<<<grid2(g.wc, g.hc, n, 32, 8), dim3(32, 8), 0, st>>>(g);
+    { const cudaError_t e_ = launch(k_gm_cost, grid2(g.wc, g.hc, n, 32, 8), dim3(32, 8), 0, st, g); if (e_ != cudaSuccess) return e_; }
     const long long bs5 = 5LL * g.hc * g.wc, bs6 = 6LL * g.hc * g.wc;
     // maps and tmp have different batch strides: run the full passes per batch entry when n > 1
     for (int i = 0; i < n; i++) {
         float* maps = g.maps + i * bs6;
         float* tmp = g.tmp + i * bs5;
-        k_box_h<<<grid2(g.wc, g.hc, 3, 32, 8), dim3(32, 8), 0, st>>>(maps, tmp, 3, g.hc, g.wc, g.r_blk, 0);
-        k_box_v<<<grid2(g.wc, g.hc, 3, 32, 8), dim3(32, 8), 0, st>>>(tmp, maps, 3, g.hc, g.wc, g.r_blk, 0);
+        { const cudaError_t e_ = launch(k_box_h, grid2(g.wc, g.hc, 3, 32, 8), dim3(32, 8), 0, st, maps, tmp, 3, g.hc, g.wc, g.r_blk, 0); if (e_ != cudaSuccess) return e_; }
+        { const cudaError_t e_ = launch(k_box_v, grid2(g.wc, g.hc, 3, 32, 8), dim3(32, 8), 0, st, tmp, maps, 3, g.hc, g.wc, g.r_blk, 0); if (e_ != cudaSuccess) return e_; }
     }
-    k_box_h_cols<<<grid2(g.w8, g.hc, 5 * n, 32, 8), dim3(32, 8), 0, st>>>(g, bs5);
+    { const cudaError_t e_ = launch(k_box_h_cols, grid2(g.w8, g.hc, 5 * n, 32, 8), dim3(32, 8), 0, st, g, bs5); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 cudaError_t gmhs_select(const GmArgs& g, int n, cudaStream_t st) {
-    k_gm_select<<<grid2(g.w8, g.h8, n, 16, 8), dim3(16, 8), 0, st>>>(g, 5LL * g.hc * g.wc);
+    { const cudaError_t e_ = launch(k_gm_select, grid2(g.w8, g.h8, n, 16, 8), dim3(16, 8), 0, st, g, 5LL * g.hc * g.wc); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 cudaError_t gmhs(const GmArgs& g, int n, cudaStream_t st) {
@@ -1208,25 +1253,25 @@ cudaError_t gmhs(const GmArgs& g, int n, cudaStream_t st) {
 
 cudaError_t film(const FilmArgs& a, int n, cudaStream_t st) {
     const size_t smem = (size_t)(a.hidden + 2 * a.cr) * sizeof(float);
-    k_film<<<grid2(a.w8, a.h8, n, 16, 8), dim3(16, 8), smem, st>>>(a);
+    { const cudaError_t e_ = launch(k_film, grid2(a.w8, a.h8, n, 16, 8), dim3(16, 8), smem, st, a); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
 cudaError_t mid_combine(const float* t, const __half* fv, long long fv_bs, const __half* dfilm, long long d_bs,
                         __half* ftvt, long long ft_bs, int h8, int w8, int n, cudaStream_t st) {
-    k_mid_combine<<<grid2(w8, h8, n, 16, 8), dim3(16, 8), 0, st>>>(t, fv, fv_bs, dfilm, d_bs, ftvt, ft_bs, h8, w8);
+    { const cudaError_t e_ = launch(k_mid_combine, grid2(w8, h8, n, 16, 8), dim3(16, 8), 0, st, t, fv, fv_bs, dfilm, d_bs, ftvt, ft_bs, h8, w8); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
 cudaError_t convex_up(const __half* wt, int wt_cs, long long wt_bs, const __half* x, long long x_bs, int h8, int w8,
                       __half* up, long long up_bs, int n, cudaStream_t st) {
-    k_convex<<<grid2(2 * w8, 2 * h8, n, 16, 8), dim3(16, 8), 0, st>>>(wt, wt_cs, wt_bs, x, x_bs, h8, w8, up, up_bs);
+    { const cudaError_t e_ = launch(k_convex, grid2(2 * w8, 2 * h8, n, 16, 8), dim3(16, 8), 0, st, wt, wt_cs, wt_bs, x, x_bs, h8, w8, up, up_bs); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
 cudaError_t refine_input(const __half* up7, long long up_bs, Img4 aq, Img4 bq, int hq, int wq, __half* rx, long long rx_bs,
                          int n, cudaStream_t st) {
-    k_refine_input<<<grid2(wq, hq, n, 16, 8), dim3(16, 8), 0, st>>>(up7, up_bs, aq, bq, hq, wq, rx, rx_bs);
+    { const cudaError_t e_ = launch(k_refine_input, grid2(wq, hq, n, 16, 8), dim3(16, 8), 0, st, up7, up_bs, aq, bq, hq, wq, rx, rx_bs); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
@@ -1235,28 +1280,28 @@ cudaError_t render(const RenderArgs& r0, int n, cudaStream_t st) {
     RenderArgs r = r0;
     r.qsy = (float)r.hq / (float)r.hp;  // the same IEEE quotients render.wgsl:87-88 forms per pixel
     r.qsx = (float)r.wq / (float)r.wp;
-    k_render<<<grid2(r.w, r.h, n, 32, 8), dim3(32, 8), 0, st>>>(r);
+    { const cudaError_t e_ = launch(k_render, grid2(r.w, r.h, n, 32, 8), dim3(32, 8), 0, st, r); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
 cudaError_t frame_half(const uint8_t* f, long long f_bs, int w, int h, __half* out, long long o_bs, int n,
                        cudaStream_t st) {
-    k_frame_half<<<grid2(w, h, n, 32, 8), dim3(32, 8), 0, st>>>(f, f_bs, w, h, out, o_bs);
+    { const cudaError_t e_ = launch(k_frame_half, grid2(w, h, n, 32, 8), dim3(32, 8), 0, st, f, f_bs, w, h, out, o_bs); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
 cudaError_t delay(cudaStream_t st, long long cycles) {
-    k_delay<<<1, 1, 0, st>>>(cycles);
+    { const cudaError_t e_ = launch(k_delay, 1, 1, 0, st, cycles); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
 cudaError_t set_scalar(float* dst, float v, cudaStream_t st) {
-    k_set_scalar<<<1, 1, 0, st>>>(dst, v);
+    { const cudaError_t e_ = launch(k_set_scalar, 1, 1, 0, st, dst, v); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
 cudaError_t frame_planes(const uint8_t* f, int w, int h, int hp, int wp, float* out, cudaStream_t st) {
-    k_frame_planes<<<grid2(wp, hp, 1), dim3(16, 16), 0, st>>>(f, w, h, hp, wp, out);
+    { const cudaError_t e_ = launch(k_frame_planes, grid2(wp, hp, 1), dim3(16, 16), 0, st, f, w, h, hp, wp, out); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
