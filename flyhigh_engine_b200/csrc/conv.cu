@@ -60,6 +60,18 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::); }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+// Weight slices too large to stage whole (wsmem 2) stream through a ring of WS_STAGES chunks of ring_chunk(NT) k-steps:
+// chunk c + WS_STAGES - 1 is issued while chunk c is multiplied.
+constexpr int WS_STAGES = 3;
+__host__ __device__ constexpr int ring_chunk(int nt) { return nt <= 6 ? 16 : 8; }
+// the weight bytes a CTA keeps in shared memory for each mode
+__host__ __device__ inline int staged_weight_bytes(int wsmem, int nsteps, int nt) {
+    return wsmem == 1 ? nsteps * nt * 256 : (wsmem == 2 ? WS_STAGES * ring_chunk(nt) * nt * 256 : 0);
+}
 
 template <int NT, int S>
 __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) {
@@ -77,12 +89,13 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
     const int nsteps = 9 * cslices;
     const int nvalid = min(NT, ntt - ng * NT);  // n-tiles of this channel group
     const int warp = tid >> 5, lane = tid & 31;
-    // ---- the group's weight slice (nsteps x nvalid x 256 B) into shared memory behind the halo tile, when staged:
-    //      issued first, it lands while the halo tile is gathered. Warps take k-steps, lanes 16-byte pieces ----
+    // ---- the group's weight slice (nsteps x nvalid x 256 B) into shared memory behind the halo tile: whole (wsmem 1,
+    //      issued first, it lands while the halo tile is gathered) or as a ring of k-step chunks (wsmem 2, the first
+    //      WS_STAGES - 1 chunks issued here). Warps take k-steps, lanes 16-byte pieces ----
     const int wbase = tile_bytes(wm, S, p.cp);
     // bias and PReLU slopes of the group (f32) at the end of the dynamic shared memory
     const int redb = ks > 1 ? (ks - 1) * wm * 32 * 2 * NT * 16 : 0;
-    const int sb_off = max(wbase + (p.wsmem ? nsteps * NT * 256 : 0), redb);
+    const int sb_off = max(wbase + staged_weight_bytes(p.wsmem, nsteps, NT), redb);
     float* sbias = reinterpret_cast<float*>(reinterpret_cast<char*>(tile) + sb_off);
     float* sslope = sbias + NT * 8;
     const bool prelu = p.slope != nullptr;
@@ -91,14 +104,23 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
         sbias[i] = c < p.cout ? p.bias[c] : 0.0f;
         sslope[i] = (prelu && c < p.cout) ? p.slope[c] : 1.0f;
     }
-    if (p.wsmem) {
-        const uint32_t dst0 = (uint32_t)__cvta_generic_to_shared(tile) + wbase;
-        const char* src0 = reinterpret_cast<const char*>(p.wpack) + (size_t)ng * NT * 256;
-        const int per = nvalid * 16;  // 16-byte pieces per k-step
-        for (int k = warp; k < nsteps; k += WARPS)
-            for (int r = lane; r < per; r += 32)
-                cp_async16(dst0 + (uint32_t)(k * NT * 256 + r * 16), src0 + (size_t)k * ntt * 256 + (size_t)r * 16);
-    }
+    constexpr int KC = ring_chunk(NT);
+    const int nwchunks = (nsteps + KC - 1) / KC;
+    const uint32_t wdst0 = (uint32_t)__cvta_generic_to_shared(tile) + wbase;
+    const char* wsrc0 = reinterpret_cast<const char*>(p.wpack) + (size_t)ng * NT * 256;
+    const int wper = nvalid * 16;  // 16-byte pieces per k-step
+    // k-steps [k0, k1) into shared memory at dst ([kstep - k0][NT][256 B])
+    auto stage_steps = [&](uint32_t dst, int k0, int k1) {
+        for (int k = k0 + warp; k < k1; k += WARPS)
+            for (int r = lane; r < wper; r += 32)
+                cp_async16(dst + (uint32_t)((k - k0) * NT * 256 + r * 16), wsrc0 + (size_t)k * ntt * 256 + (size_t)r * 16);
+    };
+    if (p.wsmem == 1) stage_steps(wdst0, 0, nsteps);
+    if (p.wsmem == 2)
+        for (int c = 0; c < WS_STAGES - 1; c++) {
+            if (c < nwchunks) stage_steps(wdst0 + (uint32_t)(c * KC * NT * 256), c * KC, min(c * KC + KC, nsteps));
+            cp_async_commit();
+        }
     // the weights, bias and slopes are written only when the session is planned: read above before the wait for the
     // preceding kernel, which covers every other access
     pdl_wait();
@@ -172,7 +194,7 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
             }
         }
     }
-    if (p.wsmem) cp_async_wait_all();
+    if (p.wsmem == 1) cp_async_wait_all();
     __syncthreads();
 
     const int wrow = warp % wm, wk = warp / wm;
@@ -185,16 +207,13 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
 
     const uint32_t tile_base = (uint32_t)__cvta_generic_to_shared(tile);
     const int lrow = lane & 15, koff = (lane >> 4) * 8;
-    // B fragments: from the staged slice ([kstep][NT][lane]) or from the packed array ([kstep][ntt][lane])
-    const uint2* wp = p.wsmem ? reinterpret_cast<const uint2*>(reinterpret_cast<const char*>(tile) + wbase) + lane
-                              : reinterpret_cast<const uint2*>(p.wpack) + (size_t)ng * NT * 32 + lane;
-    const int wstride = p.wsmem ? NT * 32 : ntt * 32;
     int tap = 0, cs = wk;  // kstep = tap * cslices + cs, advanced by ks without a division
     while (cs >= cslices) {
         cs -= cslices;
         tap++;
     }
-    for (int kstep = wk; kstep < nsteps; kstep += ks) {
+    // one k-step of this warp: A from the halo tile, B fragments at wk_p ([n-tile][lane] uint2, 32 apart)
+    auto kstep_mma = [&](const uint2* wk_p) {
         const int ky = tap / 3, kx = tap - ky * 3;
         // smem pixel of (row r0, col lrow) shifted by the tap; row r0 + 1 is S halo rows further
         const int pix0 = ((r0 * S + ky) * IW + (lrow * S + kx));
@@ -203,7 +222,6 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
         uint32_t a[2][4];
         ldsm_x4(a_addr0, a[0][0], a[0][1], a[0][2], a[0][3]);
         ldsm_x4(a_addr1, a[1][0], a[1][1], a[1][2], a[1][3]);
-        const uint2* wk_p = wp + (size_t)kstep * wstride;
 #pragma unroll
         for (int j = 0; j < NT; j++) {
             if (j < nvalid) {
@@ -217,6 +235,27 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
             cs -= cslices;
             tap++;
         }
+    };
+    if (p.wsmem == 2) {
+        // KC is a multiple of ks, so every chunk holds the same number of this warp's k-steps
+        const uint2* ring = reinterpret_cast<const uint2*>(reinterpret_cast<const char*>(tile) + wbase) + lane;
+        for (int c = 0; c < nwchunks; c++) {
+            cp_async_wait_group<WS_STAGES - 2>();  // chunk c has landed (this thread's pieces)
+            __syncthreads();                        // ... everyone's; and every warp is done with chunk c - 1
+            const int cn = c + WS_STAGES - 1;       // into chunk c - 1's slot
+            if (cn < nwchunks)
+                stage_steps(wdst0 + (uint32_t)((cn % WS_STAGES) * KC * NT * 256), cn * KC, min(cn * KC + KC, nsteps));
+            cp_async_commit();
+            const uint2* slot = ring + (size_t)(c % WS_STAGES) * KC * NT * 32;
+            const int k1 = min(c * KC + KC, nsteps);
+            for (int kstep = c * KC + wk; kstep < k1; kstep += ks) kstep_mma(slot + (size_t)(kstep - c * KC) * NT * 32);
+        }
+    } else {
+        // B fragments: from the staged slice ([kstep][NT][lane]) or from the packed array ([kstep][ntt][lane])
+        const uint2* wp = p.wsmem ? reinterpret_cast<const uint2*>(reinterpret_cast<const char*>(tile) + wbase) + lane
+                                  : reinterpret_cast<const uint2*>(p.wpack) + (size_t)ng * NT * 32 + lane;
+        const int wstride = p.wsmem ? NT * 32 : ntt * 32;
+        for (int kstep = wk; kstep < nsteps; kstep += ks) kstep_mma(wp + (size_t)kstep * wstride);
     }
 
     // ---- K-split reduction: partials of warps wk > 0 through shared memory, summed in wk order ----
@@ -294,10 +333,9 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
 
 constexpr size_t kSmemMax = 227 * 1024;
 
-size_t weight_bytes(const FhConvParams& p, int nt) { return (size_t)9 * (p.cp / 16) * nt * 256; }
 
 size_t smem_bytes(const FhConvParams& p, int s, int nt) {
-    const size_t tile = (size_t)tile_bytes(p.wm, s, p.cp) + (p.wsmem ? weight_bytes(p, nt) : 0);
+    const size_t tile = (size_t)tile_bytes(p.wm, s, p.cp) + staged_weight_bytes(p.wsmem, 9 * (p.cp / 16), nt);
     const int ks = WARPS / p.wm;
     const size_t red = ks > 1 ? (size_t)(ks - 1) * p.wm * 32 * 2 * nt * sizeof(float4) : 0;
     return (tile > red ? tile : red) + 2 * (size_t)nt * 8 * sizeof(float);  // + bias and slopes
@@ -305,9 +343,10 @@ size_t smem_bytes(const FhConvParams& p, int s, int nt) {
 
 template <int NT, int S>
 cudaError_t launch_t(FhConvParams p, cudaStream_t st) {
-    // stage the weight slice when it fits beside the halo tile and leaves room for a second CTA on the SM
+    // stage the whole weight slice when it fits beside the halo tile and leaves room for two more CTAs on the SM, else
+    // stream it through the ring
     p.wsmem = 1;
-    if (smem_bytes(p, S, NT) > kSmemMax / 3) p.wsmem = 0;
+    if (smem_bytes(p, S, NT) > kSmemMax / 3) p.wsmem = 2;
     const size_t smem = smem_bytes(p, S, NT);
     if (smem > 227 * 1024) return cudaErrorInvalidConfiguration;
     auto k = conv3x3_mma<NT, S>;
@@ -383,11 +422,14 @@ extern "C" int fhk_conv3x3(const FhConvParams* pin, int stride, void* stream) {
     const int nt = (ntt + p.ngroups - 1) / p.ngroups;
     p.ngroups = (ntt + nt - 1) / nt;  // no group without output channels
     cudaStream_t st = (cudaStream_t)stream;
-    cudaError_t e;
-    if (stride == 1) e = launch_nt<1>(nt, p, st);
-    else if (stride == 2) e = launch_nt<2>(nt, p, st);
-    else e = cudaErrorInvalidValue;
-    return (int)e;
+    if (stride != 1 && stride != 2) return (int)cudaErrorInvalidValue;
+    const bool wm_given = pin->wm > 0;
+    for (;;) {
+        const cudaError_t e = stride == 1 ? launch_nt<1>(nt, p, st) : launch_nt<2>(nt, p, st);
+        // a halo tile too tall for shared memory (very wide inputs): fewer rows per CTA, unless the caller fixed them
+        if (e != cudaErrorInvalidConfiguration || wm_given || p.wm == 1) return (int)e;
+        p.wm /= 2;
+    }
 }
 
 // Packs torch-layout weights W[cout][cin][3][3] (f16 bits) into the mma B-fragment order the kernel reads:

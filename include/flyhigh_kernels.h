@@ -54,7 +54,8 @@ typedef struct FhConvParams {
     int n;                 /* batch */
     int wm;                /* warps along output rows (1, 2, 4; the other 4 / wm split K), 0 = chosen by size */
     int ngroups;           /* CTAs sharing one output tile, each a slice of the output channels; 0 = chosen */
-    int wsmem;             /* set by fhk_conv3x3: the weight slice is staged in shared memory */
+    int wsmem;             /* set by fhk_conv3x3: 1 = the weight slice staged whole in shared memory, 2 = streamed
+                              through a ring of k-step chunks */
 } FhConvParams;
 
 /* Replaces the conv family of the reference (ops/conv/kernels.rs:100-279: conv_tc / conv_direct / conv_tiled*,

@@ -112,6 +112,7 @@ CONV_CASES = [
     (120, 216, 14, 24, 1, False),
     (120, 216, 24, 3, 1, False),
     (37, 29, 24, 24, 1, True),  # ragged: partial tiles in both directions
+    (24, 40, 400, 40, 1, True),  # a weight slice streamed through the ring in many chunks
 ]
 
 
