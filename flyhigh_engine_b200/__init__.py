@@ -53,7 +53,7 @@ def library_path() -> str:
 
 _lib = None
 
-# every export of include/flyhigh.h and include/flyhigh_b200.h: (name, restype, argtypes)
+# every export of include/flyhigh.h, include/flyhigh_b200.h and include/flyhigh_kernels.h: (name, restype, argtypes)
 EXPORTS = [
     ("fh_last_error", c_char_p, []),
     ("fh_engine_options_default", EngineOptions, []),
@@ -94,6 +94,7 @@ EXPORTS = [
     ("fhk_conv3x3", c_int, [c_void_p, c_int, c_void_p]),
     ("fhk_conv_pack_weights", c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
     ("fhk_conv_packed_elems", c_size_t, [c_int, c_int]),
+    ("fhk_conv_wait_timeouts", ctypes.c_longlong, [c_int]),
     ("fhk_gmhs", c_int, [c_void_p, c_void_p]),
     ("fhk_gmhs_scratch_floats", c_size_t, [c_int, c_int]),
     ("fhk_gmhs_noalloc", c_int, [c_void_p, c_void_p]),

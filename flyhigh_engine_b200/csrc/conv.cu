@@ -56,13 +56,50 @@ __host__ __device__ inline int halo_w(int s) { return (TW - 1) * s + 3; }
 // the halo tile's bytes, rounded to 16
 __host__ __device__ inline int tile_bytes(int wm, int s, int cp) { return halo_h(wm, s) * halo_w(s) * (cp + 8) * 2; }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
+// ---- bulk copies (TMA, no multicast) completing on an mbarrier ----
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
 }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::); }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ unsigned long long g_wait_timeouts;
+// waits for the phase `parity` of an mbarrier for at most `cycles` SM clock cycles; false (and one more timeout counted
+// for fhk_conv_wait_timeouts) when it ran out
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, long long cycles) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > cycles) {
+            atomicAdd(&g_wait_timeouts, 1ull);
+            return false;
+        }
+    }
+    return true;
+}
+// a bounded pause: after a wait ran out, the copies already issued get this long to land before the CTA moves on
+__device__ __forceinline__ void drain_pause(long long cycles) {
+    const long long t0 = clock64();
+    while (clock64() - t0 < cycles) {
+    }
+}
 
 // Weight slices too large to stage whole (wsmem 2) stream through a ring of WS_STAGES chunks of ring_chunk(NT) k-steps:
 // chunk c + WS_STAGES - 1 is issued while chunk c is multiplied.
@@ -106,21 +143,34 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
     }
     constexpr int KC = ring_chunk(NT);
     const int nwchunks = (nsteps + KC - 1) / KC;
-    const uint32_t wdst0 = (uint32_t)__cvta_generic_to_shared(tile) + wbase;
+    const uint32_t smem0 = (uint32_t)__cvta_generic_to_shared(tile);
+    const uint32_t wdst0 = smem0 + wbase;
     const char* wsrc0 = reinterpret_cast<const char*>(p.wpack) + (size_t)ng * NT * 256;
-    const int wper = nvalid * 16;  // 16-byte pieces per k-step
-    // k-steps [k0, k1) into shared memory at dst ([kstep - k0][NT][256 B])
-    auto stage_steps = [&](uint32_t dst, int k0, int k1) {
-        for (int k = k0 + warp; k < k1; k += WARPS)
-            for (int r = lane; r < wper; r += 32)
-                cp_async16(dst + (uint32_t)((k - k0) * NT * 256 + r * 16), wsrc0 + (size_t)k * ntt * 256 + (size_t)r * 16);
+    // mbarriers after the bias and slopes: one for the whole slice, one per ring slot
+    const uint32_t bar0 = smem0 + (uint32_t)(sb_off + NT * 8 * 2 * 4);
+    const long long wait_cycles = p.wait_cycles > 0 ? p.wait_cycles : 2000000000ll;
+    // after the mbarriers: set when a wait for staged weights ran out. From then on no barrier is re-armed (its phase
+    // may still be open) and no thread waits again; the result is wrong and counted in fhk_conv_wait_timeouts
+    volatile int& s_failed = *reinterpret_cast<int*>(reinterpret_cast<char*>(tile) + sb_off + NT * 8 * 2 * 4 + 8 * WS_STAGES);
+    // k-steps [k0, k1) into shared memory at dst ([kstep - k0][NT][256 B]), completing on bar: one bulk copy when the
+    // group is the whole packed row (contiguous), else one per k-step. Issued by thread 0 only.
+    auto stage_steps = [&](uint32_t bar, uint32_t dst, int k0, int k1) {
+        mbar_expect_tx(bar, (uint32_t)((k1 - k0) * nvalid * 256 + p.test_extra_tx));
+        if (nvalid == ntt)
+            bulk_g2s(dst, wsrc0 + (size_t)k0 * ntt * 256, (uint32_t)((k1 - k0) * ntt * 256), bar);
+        else
+            for (int k = k0; k < k1; k++)
+                bulk_g2s(dst + (uint32_t)((k - k0) * NT * 256), wsrc0 + (size_t)k * ntt * 256, (uint32_t)(nvalid * 256), bar);
     };
-    if (p.wsmem == 1) stage_steps(wdst0, 0, nsteps);
-    if (p.wsmem == 2)
-        for (int c = 0; c < WS_STAGES - 1; c++) {
-            if (c < nwchunks) stage_steps(wdst0 + (uint32_t)(c * KC * NT * 256), c * KC, min(c * KC + KC, nsteps));
-            cp_async_commit();
-        }
+    if (tid == 0) s_failed = 0;
+    if (p.wsmem && tid == 0) {
+        for (int sl = 0; sl < WS_STAGES; sl++) mbar_init(bar0 + 8 * sl, 1);
+        mbar_init_fence();
+        if (p.wsmem == 1) stage_steps(bar0, wdst0, 0, nsteps);
+        else
+            for (int c = 0; c < WS_STAGES - 1 && c < nwchunks; c++)
+                stage_steps(bar0 + 8 * c, wdst0 + (uint32_t)(c * KC * NT * 256), c * KC, min(c * KC + KC, nsteps));
+    }
     // the weights, bias and slopes are written only when the session is planned: read above before the wait for the
     // preceding kernel, which covers every other access
     pdl_wait();
@@ -194,8 +244,8 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
             }
         }
     }
-    if (p.wsmem == 1) cp_async_wait_all();
     __syncthreads();
+    if (p.wsmem == 1 && !mbar_wait_bounded(bar0, 0, wait_cycles)) s_failed = 1;
 
     const int wrow = warp % wm, wk = warp / wm;
     const int r0 = wrow * 2;  // this warp's first output row inside the tile
@@ -240,12 +290,15 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
         // KC is a multiple of ks, so every chunk holds the same number of this warp's k-steps
         const uint2* ring = reinterpret_cast<const uint2*>(reinterpret_cast<const char*>(tile) + wbase) + lane;
         for (int c = 0; c < nwchunks; c++) {
-            cp_async_wait_group<WS_STAGES - 2>();  // chunk c has landed (this thread's pieces)
-            __syncthreads();                        // ... everyone's; and every warp is done with chunk c - 1
-            const int cn = c + WS_STAGES - 1;       // into chunk c - 1's slot
-            if (cn < nwchunks)
-                stage_steps(wdst0 + (uint32_t)((cn % WS_STAGES) * KC * NT * 256), cn * KC, min(cn * KC + KC, nsteps));
-            cp_async_commit();
+            // every warp is done with chunk c - 1, whose slot takes chunk c + 2; s_failed is the same for all threads
+            if (c > 0) __syncthreads();
+            const bool failed = s_failed != 0;
+            const int cn = c + WS_STAGES - 1;
+            if (!failed && tid == 0 && cn < nwchunks)
+                stage_steps(bar0 + 8 * (cn % WS_STAGES), wdst0 + (uint32_t)((cn % WS_STAGES) * KC * NT * 256), cn * KC,
+                            min(cn * KC + KC, nsteps));
+            if (!failed && !mbar_wait_bounded(bar0 + 8 * (c % WS_STAGES), (uint32_t)((c / WS_STAGES) & 1), wait_cycles))
+                s_failed = 1;
             const uint2* slot = ring + (size_t)(c % WS_STAGES) * KC * NT * 32;
             const int k1 = min(c * KC + KC, nsteps);
             for (int kstep = c * KC + wk; kstep < k1; kstep += ks) kstep_mma(slot + (size_t)(kstep - c * KC) * NT * 32);
@@ -258,9 +311,12 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
         for (int kstep = wk; kstep < nsteps; kstep += ks) kstep_mma(wp + (size_t)kstep * wstride);
     }
 
+    // a wait that ran out leaves copies possibly in flight into the staged region: give them time to land before the
+    // shared memory is reused or released
+    __syncthreads();
+    if (s_failed) drain_pause(wait_cycles);
     // ---- K-split reduction: partials of warps wk > 0 through shared memory, summed in wk order ----
     if (ks > 1) {
-        __syncthreads();  // every warp is done with the halo tile
         float4* red = reinterpret_cast<float4*>(tile);
         if (wk > 0) {
             float4* dst = red + ((size_t)((wk - 1) * wm + wrow) * 32 + lane) * (2 * NT);
@@ -338,7 +394,8 @@ size_t smem_bytes(const FhConvParams& p, int s, int nt) {
     const size_t tile = (size_t)tile_bytes(p.wm, s, p.cp) + staged_weight_bytes(p.wsmem, 9 * (p.cp / 16), nt);
     const int ks = WARPS / p.wm;
     const size_t red = ks > 1 ? (size_t)(ks - 1) * p.wm * 32 * 2 * nt * sizeof(float4) : 0;
-    return (tile > red ? tile : red) + 2 * (size_t)nt * 8 * sizeof(float);  // + bias and slopes
+    // + bias, slopes, mbarriers, the failure flag
+    return (tile > red ? tile : red) + 2 * (size_t)nt * 8 * sizeof(float) + 8 * WS_STAGES + 16;
 }
 
 template <int NT, int S>
@@ -407,8 +464,11 @@ extern "C" int fhk_conv3x3(const FhConvParams* pin, int stride, void* stream) {
         pin->cout > 96 || pin->n < 1)
         return (int)cudaErrorInvalidValue;
     FhConvParams p = *pin;
-    if (p.out_cs % 2 || (p.res && p.res_cs % 2) || (uintptr_t)p.out % 4 || (p.res && (uintptr_t)p.res % 4))
+    if (p.out_cs % 2 || (p.res && p.res_cs % 2) || (uintptr_t)p.out % 4 || (p.res && (uintptr_t)p.res % 4) ||
+        (uintptr_t)p.wpack % 16)
         return (int)cudaErrorMisalignedAddress;
+    if (p.test_extra_tx < 0 || p.test_extra_tx % 16 || p.test_extra_tx > 65536 || p.wait_cycles < 0)
+        return (int)cudaErrorInvalidValue;
     for (int s = 0; s < p.nsrc; s++) {
         const FhConvSrc& src = p.src[s];
         if (src.slot % 8 || (src.cs % 8 && src.cs != 4) || ((uintptr_t)src.p % (src.cs == 4 ? 8 : 16)))
@@ -455,6 +515,16 @@ extern "C" int fhk_conv_pack_weights(const uint16_t* w, int cin, int cout, const
                 o[3] = B(k0 + 9, nn);
             }
     return 0;
+}
+
+extern "C" long long fhk_conv_wait_timeouts(int reset) {
+    unsigned long long v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof v) != cudaSuccess) return -1;
+    if (reset) {
+        const unsigned long long z = 0;
+        if (cudaMemcpyToSymbol(g_wait_timeouts, &z, sizeof z) != cudaSuccess) return -1;
+    }
+    return (long long)v;
 }
 
 extern "C" size_t fhk_conv_packed_elems(int cout, int cp) { return (size_t)(9 * cp / 16) * ((cout + 7) / 8) * 32 * 4; }

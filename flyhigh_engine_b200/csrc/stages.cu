@@ -125,17 +125,43 @@ __global__ void k_input_pyramid(const __half* __restrict__ A, long long a_bs, in
         const int ymin = max(0, (int)floorf(cy - fsh + 0.5f)), ymax = min(ih, (int)floorf(cy + fsh + 0.5f));
         const int xmin = max(0, (int)floorf(cx - fsw + 0.5f)), xmax = min(iw, (int)floorf(cx + fsw + 0.5f));
         float ab = 0.0f, ag = 0.0f, ar = 0.0f, norm = 0.0f;
-        for (int y = ymin; y < ymax; y++) {
-            const float wy = fmaxf(0.0f, 1.0f - fabsf(((float)y + 0.5f - cy) / fsh));
-            for (int x = xmin; x < xmax; x++) {
-                const float wx = fmaxf(0.0f, 1.0f - fabsf(((float)x + 0.5f - cx) / fsw));
-                const float wgt = wx * wy;
-                float b, g, r;
-                ld4(a + ((long long)y * iw + x) * 4, b, g, r);
-                ab = ab + b * wgt;
-                ag = ag + g * wgt;
-                ar = ar + r * wgt;
-                norm = norm + wgt;
+        constexpr int XT = 8;  // the column weights of up to XT taps are formed once (downscales up to 4x)
+        if (xmax - xmin <= XT) {
+            float wx[XT];
+#pragma unroll
+            for (int j = 0; j < XT; j++) wx[j] = fmaxf(0.0f, 1.0f - fabsf(((float)(xmin + j) + 0.5f - cx) / fsw));
+            const int nx = xmax - xmin;
+            for (int y = ymin; y < ymax; y++) {
+                const float wy = fmaxf(0.0f, 1.0f - fabsf(((float)y + 0.5f - cy) / fsh));
+                const __half* row = a + ((long long)y * iw + xmin) * 4;
+                float pb[XT], pg[XT], pr[XT];
+#pragma unroll
+                for (int j = 0; j < XT; j++)
+                    if (j < nx) ld4(row + j * 4, pb[j], pg[j], pr[j]);
+#pragma unroll
+                for (int j = 0; j < XT; j++) {
+                    if (j < nx) {
+                        const float wgt = wx[j] * wy;
+                        ab = ab + pb[j] * wgt;
+                        ag = ag + pg[j] * wgt;
+                        ar = ar + pr[j] * wgt;
+                        norm = norm + wgt;
+                    }
+                }
+            }
+        } else {
+            for (int y = ymin; y < ymax; y++) {
+                const float wy = fmaxf(0.0f, 1.0f - fabsf(((float)y + 0.5f - cy) / fsh));
+                for (int x = xmin; x < xmax; x++) {
+                    const float wx = fmaxf(0.0f, 1.0f - fabsf(((float)x + 0.5f - cx) / fsw));
+                    const float wgt = wx * wy;
+                    float b, g, r;
+                    ld4(a + ((long long)y * iw + x) * 4, b, g, r);
+                    ab = ab + b * wgt;
+                    ag = ag + g * wgt;
+                    ar = ar + r * wgt;
+                    norm = norm + wgt;
+                }
             }
         }
         const float vb = rh(ab / norm), vg = rh(ag / norm), vr = rh(ar / norm);
@@ -373,47 +399,67 @@ __global__ void __launch_bounds__(256) k_static_age(const uint8_t* __restrict__ 
 
 // ------------------------------------------------------------------------------------------------ cost volume ----
 
-// luma.wgsl:13-18 (f16 luma) + sad.wgsl:10-29: one thread per pixel computes all (2r+1)^2 channels
+// luma.wgsl:13-18 (f16 luma) + sad.wgsl:10-29. A block covers 8 x 8 pixels: the f16 lumas of a (its 10 x 10 zero-padded
+// neighbourhood) and of b (the (8 + 2R + 2)^2 window at edge-clamped positions) go to shared memory once, then
+// SAD_TPP threads per pixel each form every SAD_TPP-th of the (2r+1)^2 channels, and the block writes its pixels'
+// channel vectors (cs halves each, zero past the last channel) as 16-byte stores.
+constexpr int SAD_TPP = 4;
 template <int R>
-__global__ void k_sad(const __half* __restrict__ a, int a_cs, const __half* __restrict__ b, int b_cs, long long in_bs,
-                      int h, int w, __half* out, int out_cs, long long out_bs) {
+__global__ void __launch_bounds__(64 * SAD_TPP) k_sad(const __half* __restrict__ a, int a_cs, const __half* __restrict__ b,
+                                                      int b_cs, long long in_bs, int h, int w, __half* out, int out_cs,
+                                                      long long out_bs) {
+    constexpr int SP = 2 * R + 1, NC = SP * SP, BW = 8 + 2 * R + 2;
+    __shared__ float la[10][10];
+    __shared__ float lb[BW][BW];
+    extern __shared__ __align__(16) __half so[];  // [64][out_cs]
     pdl_wait();
     pdl_trigger();
-    constexpr int SP = 2 * R + 1, WIN = SP + 2;
-    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
-    if (x >= w || y >= h) return;
+    const int n = blockIdx.z, x0 = blockIdx.x * 8, y0 = blockIdx.y * 8, tid = threadIdx.x;
     const __half* A = a + (long long)n * in_bs;
     const __half* B = b + (long long)n * in_bs;
     auto luma = [&](const __half* p, int cs, int yy, int xx) {
         const __half* q = p + ((long long)yy * w + xx) * cs;
         return rh(lum3(h2f(q[0]), h2f(q[1]), h2f(q[2])));
     };
-    float la[3][3];
-    for (int wy = -1; wy <= 1; wy++)
-        for (int wx = -1; wx <= 1; wx++) {
-            const int yy = y + wy, xx = x + wx;
-            la[wy + 1][wx + 1] = (yy >= 0 && yy < h && xx >= 0 && xx < w) ? luma(A, a_cs, yy, xx) : 0.0f;
-        }
-    float lb[WIN][WIN];  // lb at clamp(y + d), d in [-R-1, R+1]
-    for (int i = 0; i < WIN; i++)
-        for (int j = 0; j < WIN; j++)
-            lb[i][j] = luma(B, b_cs, clampi(y + i - R - 1, 0, h - 1), clampi(x + j - R - 1, 0, w - 1));
-    __half* o = out + (long long)n * out_bs + ((long long)y * w + x) * out_cs;
-    for (int c = 0; c < SP * SP; c++) {
-        const int dy = c / SP - R, dx = c % SP - R;
-        float acc = 0.0f;
-        for (int wy = -1; wy <= 1; wy++)
-            for (int wx = -1; wx <= 1; wx++) {
-                const int yy = y + wy, xx = x + wx;
-                if (yy >= 0 && yy < h && xx >= 0 && xx < w) {
-                    // lb(clamp(yy + dy)) = the clamped window entry when yy is inside the image
-                    const int sy = clampi(yy + dy, 0, h - 1) - y + R + 1, sx = clampi(xx + dx, 0, w - 1) - x + R + 1;
-                    acc = acc + fabsf(la[wy + 1][wx + 1] - lb[sy][sx]);
-                }
-            }
-        o[c] = f2h(acc / 9.0f);
+    for (int i = tid; i < 100; i += 64 * SAD_TPP) {
+        const int yy = y0 - 1 + i / 10, xx = x0 - 1 + i % 10;
+        la[i / 10][i % 10] = (yy >= 0 && yy < h && xx >= 0 && xx < w) ? luma(A, a_cs, yy, xx) : 0.0f;
     }
-    for (int c = SP * SP; c < out_cs; c++) o[c] = f2h(0.0f);
+    for (int i = tid; i < BW * BW; i += 64 * SAD_TPP) {
+        const int r = i / BW, c = i - r * BW;
+        lb[r][c] = luma(B, b_cs, clampi(y0 - 1 - R + r, 0, h - 1), clampi(x0 - 1 - R + c, 0, w - 1));
+    }
+    __syncthreads();
+    const int pix = tid & 63, part = tid >> 6, ly = pix >> 3, lx = pix & 7;
+    const int y = y0 + ly, x = x0 + lx;
+    if (y < h && x < w) {
+        for (int c = part; c < NC; c += SAD_TPP) {
+            const int dy = c / SP - R, dx = c % SP - R;
+            float acc = 0.0f;
+#pragma unroll
+            for (int wy = -1; wy <= 1; wy++)
+#pragma unroll
+                for (int wx = -1; wx <= 1; wx++) {
+                    const int yy = y + wy, xx = x + wx;
+                    if (yy >= 0 && yy < h && xx >= 0 && xx < w) {
+                        // lb at clamp(yy + dy), clamp(xx + dx): its window entry
+                        const int sy = clampi(yy + dy, 0, h - 1) - (y0 - 1 - R), sx = clampi(xx + dx, 0, w - 1) - (x0 - 1 - R);
+                        acc = acc + fabsf(la[ly + 1 + wy][lx + 1 + wx] - lb[sy][sx]);
+                    }
+                }
+            so[pix * out_cs + c] = f2h(acc / 9.0f);
+        }
+        for (int c = NC + part; c < out_cs; c += SAD_TPP) so[pix * out_cs + c] = f2h(0.0f);
+    }
+    __syncthreads();
+    const int vec = out_cs / 8;  // 16-byte pieces per pixel
+    for (int i = tid; i < 64 * vec; i += 64 * SAD_TPP) {
+        const int p = i / vec, v = i - p * vec;
+        const int yy = y0 + (p >> 3), xx = x0 + (p & 7);
+        if (yy < h && xx < w)
+            *reinterpret_cast<uint4*>(out + (long long)n * out_bs + ((long long)yy * w + xx) * out_cs + v * 8) =
+                *reinterpret_cast<const uint4*>(so + p * out_cs + v * 8);
+    }
 }
 
 // ------------------------------------------------------------------------------------------- flow upsampling ----
@@ -489,22 +535,30 @@ __global__ void k_warp_fine(WarpFineArgs a) {
         const Bil b = bil_at(x, y, fx, fy, a.h8, a.w8);
         const __half* __restrict__ f8 = (side ? a.f8b : a.f8a) + (long long)n * a.f8_bs;
         const long long idx[4] = {b.i00, b.i01, b.i10, b.i11};
-        for (int v = 0; v < nv; v++) {
-            uint4 c4[4];
+        // every corner vector of the side in flight at once, then the blends
+        uint4 c4[5][4];
 #pragma unroll
-            for (int k = 0; k < 4; k++) c4[k] = __ldg(reinterpret_cast<const uint4*>(f8 + idx[k] * a.f8_cs) + v);
+        for (int v = 0; v < 5; v++)
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                c4[v][k] = v < nv ? __ldg(reinterpret_cast<const uint4*>(f8 + idx[k] * a.f8_cs) + v) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int v = 0; v < 5; v++) {
+            if (v >= nv) {
+                *reinterpret_cast<uint4*>(o + side * 40 + v * 8) = make_uint4(0, 0, 0, 0);
+                continue;
+            }
             __half r[8];
 #pragma unroll
             for (int e = 0; e < 8; e++) {
                 const int c = v * 8 + e;
-                const float val = bil_mix(h2f(reinterpret_cast<const __half*>(&c4[0])[e]), h2f(reinterpret_cast<const __half*>(&c4[1])[e]),
-                                          h2f(reinterpret_cast<const __half*>(&c4[2])[e]), h2f(reinterpret_cast<const __half*>(&c4[3])[e]),
+                const float val = bil_mix(h2f(reinterpret_cast<const __half*>(&c4[v][0])[e]), h2f(reinterpret_cast<const __half*>(&c4[v][1])[e]),
+                                          h2f(reinterpret_cast<const __half*>(&c4[v][2])[e]), h2f(reinterpret_cast<const __half*>(&c4[v][3])[e]),
                                           b.ax, b.ay);
                 r[e] = c < a.c8 ? f2h(val * 1.0f) : f2h(0.0f);
             }
             *reinterpret_cast<uint4*>(o + side * 40 + v * 8) = *reinterpret_cast<uint4*>(r);
         }
-        for (int v = nv; v < 5; v++) *reinterpret_cast<uint4*>(o + side * 40 + v * 8) = make_uint4(0, 0, 0, 0);
         const __half* __restrict__ im = (side ? a.i8b.p + (long long)n * a.i8b.bs : a.i8a.p + (long long)n * a.i8a.bs);
         float c3[4][3];
 #pragma unroll
@@ -517,15 +571,15 @@ __global__ void k_warp_fine(WarpFineArgs a) {
 
 // ----------------------------------------------------------------------------------------------------- GMHS ----
 
-// gm_fit_reduce.wgsl + gm_fit_solve.wgsl, 4 IRLS iterations in one thread-block cluster of 8 CTAs x 16 warps. The
-// reduction reproduces the shader's: 32 workgroups x 256 threads, each thread a strided partial sum, a 256-wide tree
-// per workgroup (off = 128 .. 1), then the solve's sequential sum over workgroups. One warp reduces one
-// (workgroup, channel) pair: lane l holds virtual threads l + 32 k, k = 0..7; the 128 warps of the cluster cover the 32
-// workgroups x 4 channels at once and write their partials into every CTA's shared memory (distributed shared
-// memory), so each CTA solves on its own copy and one cluster barrier per iteration suffices. The partial buffers
-// alternate between iterations: a CTA writing iteration i + 1's partials has passed iteration i + 1's barrier only after
-// every CTA finished reading iteration i's. A virtual thread's first point (flow value and coordinates) stays in
-// registers across the iterations; further points (more than 8192 flow cells) are reread.
+// gm_fit_reduce.wgsl + gm_fit_solve.wgsl, 4 IRLS iterations. The reduction reproduces the shader's: 32 workgroups x
+// 256 threads, each thread a strided partial sum, a 256-wide tree per workgroup (off = 128 .. 1), then the solve's
+// sequential sum over the workgroups. A channel's fit reads only that channel's partials: one thread-block cluster of
+// GM_CLUSTER CTAs x 4 warps per (entry, channel), a warp per workgroup (lane l holds virtual threads l + 32 k,
+// k = 0..7, whose point, coordinates and flow value stay in registers across the iterations). Each warp writes its
+// nine partials into every CTA of the cluster (distributed shared memory), so after one cluster barrier every CTA
+// forms the sequential sums and the solve on its own copy. The partial buffers alternate between iterations: a CTA
+// writing iteration i + 1's partials has passed iteration i + 1's barrier only after every CTA finished reading
+// iteration i's. Flow grids above 8192 cells reread their further points.
 constexpr int GM_CLUSTER = 8;
 FH_DEV void gm_acc(float w2, float x, float y, float f, float* s) {
     s[0] = s[0] + w2;
@@ -538,22 +592,21 @@ FH_DEV void gm_acc(float w2, float x, float y, float f, float* s) {
     s[7] = s[7] + w2 * x * f;
     s[8] = s[8] + w2 * y * f;
 }
-__global__ void __cluster_dims__(GM_CLUSTER, 1, 1) __launch_bounds__(512, 1) k_gm_fit(GmArgs g) {
-    pdl_wait();
-    pdl_trigger();
+__global__ void __cluster_dims__(GM_CLUSTER, 1, 1) __launch_bounds__(128) k_gm_fit(GmArgs g) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
-    __shared__ float part[2][32][4][9];
-    __shared__ float coef[16];
+    __shared__ float part[2][32][9];
+    __shared__ float sums[9];
+    __shared__ float cf[3];
+    pdl_wait();
+    pdl_trigger();
     const unsigned rank = cluster.block_rank();
-    const int n = blockIdx.x / GM_CLUSTER;
+    const int cl = blockIdx.x / GM_CLUSTER, c = cl & 3, n = cl >> 2;
     const __half* fl = g.fv + (long long)n * g.fv_bs;
     const int w8 = g.w8, h8 = g.h8, np = h8 * w8;
     const float sx = 2.0f / (float)max(w8 - 1, 1), sy = 2.0f / (float)max(h8 - 1, 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int task = (int)rank * 16 + warp;  // 0..127
-    const int wg = task >> 2, c = task & 3;
-    if (threadIdx.x < 16) coef[threadIdx.x] = 0.0f;
+    const int wg = (int)rank * 4 + warp;  // 0..31
     float f0[8], x0[8], y0[8];
 #pragma unroll
     for (int k = 0; k < 8; k++) {
@@ -566,9 +619,10 @@ __global__ void __cluster_dims__(GM_CLUSTER, 1, 1) __launch_bounds__(512, 1) k_g
             f0[k] = h2f(fl[(long long)i * 8 + c]);
         }
     }
+    if (threadIdx.x < 3) cf[threadIdx.x] = 0.0f;
     cluster.sync();  // every CTA runs before any distributed shared memory store
     for (int it = 0; it < 4; it++) {
-        const float c0 = coef[c * 4], c1 = coef[c * 4 + 1], c2 = coef[c * 4 + 2];
+        const float c0 = cf[0], c1 = cf[1], c2 = cf[2];
         // virtual threads k and k + 4 are summed as soon as both are formed (the tree's off = 128 step)
         float a[4][9];
 #pragma unroll
@@ -610,14 +664,18 @@ __global__ void __cluster_dims__(GM_CLUSTER, 1, 1) __launch_bounds__(512, 1) k_g
         const int buf = it & 1;
         if (lane < 9)
 #pragma unroll
-            for (unsigned r = 0; r < GM_CLUSTER; r++) cluster.map_shared_rank(&part[buf][0][0][0], r)[(wg * 4 + c) * 9 + lane] = mine;
+            for (unsigned r = 0; r < GM_CLUSTER; r++) cluster.map_shared_rank(&part[buf][0][0], r)[wg * 9 + lane] = mine;
         cluster.sync();
-        if (threadIdx.x < 4) {
-            const int cc = threadIdx.x;
-            float s_[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
-            for (int w = 0; w < 32; w++)
+        if (threadIdx.x < 9) {
+            float s_ = 0.0f;
+            for (int w = 0; w < 32; w++) s_ = s_ + part[buf][w][threadIdx.x];
+            sums[threadIdx.x] = s_;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float s_[9];
 #pragma unroll
-                for (int k = 0; k < 9; k++) s_[k] = s_[k] + part[buf][w][cc][k];
+            for (int k = 0; k < 9; k++) s_[k] = sums[k];
             const float m00 = s_[0] + 1e-6f, m01 = s_[1], m02 = s_[2], m11 = s_[3] + 1e-6f, m12 = s_[4], m22 = s_[5] + 1e-6f;
             const float det = m00 * (m11 * m22 - m12 * m12) - m01 * (m01 * m22 - m12 * m02) + m02 * (m01 * m12 - m11 * m02);
             float e0, e1, e2;
@@ -632,14 +690,13 @@ __global__ void __cluster_dims__(GM_CLUSTER, 1, 1) __launch_bounds__(512, 1) k_g
                 e1 = i01 * s_[6] + i11 * s_[7] + i12 * s_[8];
                 e2 = i02 * s_[6] + i12 * s_[7] + i22 * s_[8];
             }
-            coef[cc * 4] = e0;
-            coef[cc * 4 + 1] = e1;
-            coef[cc * 4 + 2] = e2;
-            coef[cc * 4 + 3] = 0.0f;
+            cf[0] = e0;
+            cf[1] = e1;
+            cf[2] = e2;
         }
         __syncthreads();
     }
-    if (rank == 0 && threadIdx.x < 16) g.coef[n * 16 + threadIdx.x] = coef[threadIdx.x];
+    if (rank == 0 && threadIdx.x < 4) g.coef[n * 16 + c * 4 + threadIdx.x] = threadIdx.x < 3 ? cf[threadIdx.x] : 0.0f;
 }
 
 // gm_cost.wgsl:15-75
@@ -714,6 +771,7 @@ __global__ void k_box_h(const float* src, float* dst, int c, int h, int w, int r
     if (x >= w || y >= h) return;
     const long long row = (long long)n * bs + ((long long)ch * h + y) * w;
     float acc = 0.0f;
+#pragma unroll 8
     for (int d = -r; d <= r; d++) acc = acc + src[row + clampi(x + d, 0, w - 1)];
     dst[row + x] = acc / (float)(2 * r + 1);
 }
@@ -725,6 +783,7 @@ __global__ void k_box_v(const float* src, float* dst, int c, int h, int w, int r
     if (x >= w || y >= h) return;
     const long long plane = (long long)n * bs + (long long)ch * h * w;
     float acc = 0.0f;
+#pragma unroll 8
     for (int d = -r; d <= r; d++) acc = acc + src[plane + (long long)clampi(y + d, 0, h - 1) * w + x];
     dst[plane + (long long)y * w + x] = acc / (float)(2 * r + 1);
 }
@@ -742,29 +801,32 @@ __global__ void k_box_h_cols(GmArgs g, long long cols_bs) {
     const int r = ch < 3 ? g.r_dwin : g.r_blk, x = gm_cell(j, g.wc, g.w8);
     const float* row = g.maps + (long long)n * 6 * g.hc * g.wc + ((long long)ch * g.hc + y) * g.wc;
     float acc = 0.0f;
+#pragma unroll 8
     for (int d = -r; d <= r; d++) acc = acc + row[clampi(x + d, 0, g.wc - 1)];
     g.tmp[(long long)n * cols_bs + ((long long)ch * g.hc + y) * g.w8 + j] = acc / (float)(2 * r + 1);
 }
 
-// gm_select.wgsl:12-28 (eps 0, tex 0.015: gmhs.rs:208), with the last vertical box pass of each map at its cell
-__global__ void k_gm_select(GmArgs g, long long cols_bs) {
+// gm_select.wgsl:12-28 (eps 0, tex 0.015: gmhs.rs:208), with the last vertical box pass of each map at its cell. A
+// block is 32 select cells of a row x the 5 maps: each thread forms one map's window sum, the map-0 threads decide.
+__global__ void __launch_bounds__(160) k_gm_select(GmArgs g, long long cols_bs) {
+    __shared__ float mv[5][32];
     pdl_wait();
     pdl_trigger();
-    const int j = blockIdx.x * blockDim.x + threadIdx.x, i = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
-    if (j >= g.w8 || i >= g.h8) return;
-    const float* coef = g.coef + n * 16;
+    const int j = blockIdx.x * 32 + threadIdx.x, ch = threadIdx.y, i = blockIdx.y, n = blockIdx.z;
     const int y = gm_cell(i, g.hc, g.h8);
-    const float* cols = g.tmp + (long long)n * cols_bs;
-    float m[5];
-#pragma unroll
-    for (int ch = 0; ch < 5; ch++) {
+    if (j < g.w8) {
         const int r = ch < 3 ? g.r_dwin : g.r_blk;
-        const float* col = cols + (long long)ch * g.hc * g.w8 + j;
+        const float* col = g.tmp + (long long)n * cols_bs + (long long)ch * g.hc * g.w8 + j;
         float acc = 0.0f;
+#pragma unroll 8
         for (int d = -r; d <= r; d++) acc = acc + col[(long long)clampi(y + d, 0, g.hc - 1) * g.w8];
-        m[ch] = acc / (float)(2 * r + 1);
+        mv[ch][threadIdx.x] = acc / (float)(2 * r + 1);
     }
-    const float cm = m[0], ca = m[1], dv = m[2], lm = m[3], l2 = m[4];
+    __syncthreads();
+    if (ch != 0 || j >= g.w8) return;
+    const float* coef = g.coef + n * 16;
+    const float cm = mv[0][threadIdx.x], ca = mv[1][threadIdx.x], dv = mv[2][threadIdx.x], lm = mv[3][threadIdx.x],
+                l2 = mv[4][threadIdx.x];
     const float sd = sqrtf(fmaxf(l2 - lm * lm, 0.0f));
     const float eps = 0.0f, tex = 0.015f;
     if (ca + eps < cm && dv > g.dmin && sd > tex) {
@@ -790,7 +852,8 @@ __global__ void k_film(FilmArgs a) {
     __syncthreads();
     for (int o = tid; o < 2 * a.cr; o += nt) {
         float acc = 0.0f;
-        for (int i = 0; i < a.hidden; i++) acc = acc + a.w2[o * a.hidden + i] * hv[i];
+#pragma unroll 8
+        for (int i = 0; i < a.hidden; i++) acc = acc + __ldg(a.w2 + o * a.hidden + i) * hv[i];
         gv[o] = rh(a.b2[o] + acc);
     }
     __syncthreads();
@@ -1201,9 +1264,11 @@ cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, const uint32_t* cha
 
 cudaError_t sad_volume(const __half* a, int a_cs, const __half* b, int b_cs, long long in_bs, int h, int w, int r,
                        __half* out, int out_cs, long long out_bs, int n, cudaStream_t st) {
-    dim3 g = grid2(w, h, n, 16, 8), blk(16, 8);
-    if (r == 3) { const cudaError_t e_ = launch(k_sad<3>, g, blk, 0, st, a, a_cs, b, b_cs, in_bs, h, w, out, out_cs, out_bs); if (e_ != cudaSuccess) return e_; }
-    else if (r == 2) { const cudaError_t e_ = launch(k_sad<2>, g, blk, 0, st, a, a_cs, b, b_cs, in_bs, h, w, out, out_cs, out_bs); if (e_ != cudaSuccess) return e_; }
+    if (out_cs % 8 || out_cs < (2 * r + 1) * (2 * r + 1) || (uintptr_t)out % 16) return cudaErrorInvalidValue;
+    const dim3 g((w + 7) / 8, (h + 7) / 8, n), blk(64 * SAD_TPP);
+    const size_t smem = (size_t)64 * out_cs * sizeof(__half);
+    if (r == 3) { const cudaError_t e_ = launch(k_sad<3>, g, blk, smem, st, a, a_cs, b, b_cs, in_bs, h, w, out, out_cs, out_bs); if (e_ != cudaSuccess) return e_; }
+    else if (r == 2) { const cudaError_t e_ = launch(k_sad<2>, g, blk, smem, st, a, a_cs, b, b_cs, in_bs, h, w, out, out_cs, out_bs); if (e_ != cudaSuccess) return e_; }
     else return cudaErrorInvalidValue;
     return cudaGetLastError();
 }
@@ -1223,7 +1288,7 @@ cudaError_t warp_fine(const WarpFineArgs& a, int n, cudaStream_t st) {
 // The texture window over maps 0-2 in full (the decision window reads all of it), then both windows' remaining passes
 // at the select cells only: horizontal at the select columns (k_box_h_cols), vertical inside the select.
 cudaError_t gmhs_fit(const GmArgs& g, int n, cudaStream_t st) {
-    { const cudaError_t e_ = launch(k_gm_fit, n * GM_CLUSTER, 512, 0, st, g); if (e_ != cudaSuccess) return e_; }
+    { const cudaError_t e_ = launch(k_gm_fit, 4 * n * GM_CLUSTER, 128, 0, st, g); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 cudaError_t gmhs_maps(const GmArgs& g, int n, cudaStream_t st) {
@@ -1241,7 +1306,7 @@ cudaError_t gmhs_maps(const GmArgs& g, int n, cudaStream_t st) {
     return cudaGetLastError();
 }
 cudaError_t gmhs_select(const GmArgs& g, int n, cudaStream_t st) {
-    { const cudaError_t e_ = launch(k_gm_select, grid2(g.w8, g.h8, n, 16, 8), dim3(16, 8), 0, st, g, 5LL * g.hc * g.wc); if (e_ != cudaSuccess) return e_; }
+    { const cudaError_t e_ = launch(k_gm_select, dim3((g.w8 + 31) / 32, g.h8, n), dim3(32, 5), 0, st, g, 5LL * g.hc * g.wc); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 cudaError_t gmhs(const GmArgs& g, int n, cudaStream_t st) {

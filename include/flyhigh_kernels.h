@@ -55,7 +55,9 @@ typedef struct FhConvParams {
     int wm;                /* warps along output rows (1, 2, 4; the other 4 / wm split K), 0 = chosen by size */
     int ngroups;           /* CTAs sharing one output tile, each a slice of the output channels; 0 = chosen */
     int wsmem;             /* set by fhk_conv3x3: 1 = the weight slice staged whole in shared memory, 2 = streamed
-                              through a ring of k-step chunks */
+                              through a ring of k-step chunks (both by bulk copies completing on an mbarrier) */
+    long long wait_cycles; /* bound of each wait for staged weights, SM clock cycles; 0 = 2e9 (about a second) */
+    int test_extra_tx;     /* 0. Tests only: bytes an mbarrier expects beyond the copies, so its waits run out */
 } FhConvParams;
 
 /* Replaces the conv family of the reference (ops/conv/kernels.rs:100-279: conv_tc / conv_direct / conv_tiled*,
@@ -63,6 +65,9 @@ typedef struct FhConvParams {
  * stride 1 or 2. A CTA of 4 warps computes (2 * wm) x 16 output pixels for a slice of the output channels; the K
  * dimension is split over the other 4 / wm warps and reduced in shared memory in a fixed order. */
 int fhk_conv3x3(const FhConvParams* p, int stride, void* stream);
+/* Waits for staged weights that ran out of time (the kernel then computes on whatever landed and goes on) since the
+ * last reset, on the current device; reset != 0 zeroes the count. Returns -1 when the count cannot be read. */
+long long fhk_conv_wait_timeouts(int reset);
 /* Replaces buildb / buildb_tap (ops/conv/kernels.rs:66-78, :194-207): torch [cout][cin][3][3] f16 bits -> the
  * kernel's B-fragment order; map[pc] = model input channel of packed channel pc, or -1 (weight 0). */
 int fhk_conv_pack_weights(const uint16_t* w, int cin, int cout, const int* map, int cp, uint16_t* out);
@@ -85,7 +90,7 @@ typedef struct FhGmhsParams {
     int n;                /* batch */
 } FhGmhsParams;
 
-/* Replaces gmhs::gm_steps and its dispatches (10 + 2 per window in the reference) with 7 launches. */
+/* Replaces gmhs::gm_steps and its dispatches (10 + 2 per window in the reference) with 6 launches. */
 int fhk_gmhs(const FhGmhsParams* p, void* stream);
 /* Scratch floats per batch entry: 16 coefficients + 6 + 5 cost maps of ceil(h / 2) x ceil(w / 2). */
 size_t fhk_gmhs_scratch_floats(int h, int w);

@@ -35,7 +35,7 @@ class ConvParams(Structure):
                 ("cp", c_int), ("cout", c_int), ("wpack", c_void_p), ("bias", c_void_p), ("slope", c_void_p),
                 ("epi", c_int), ("out", c_void_p), ("out_cs", c_int), ("out_bs", c_longlong), ("res", c_void_p),
                 ("res_cs", c_int), ("res_bs", c_longlong), ("n", c_int), ("wm", c_int), ("ngroups", c_int),
-                ("wsmem", c_int)]
+                ("wsmem", c_int), ("wait_cycles", c_longlong), ("test_extra_tx", c_int)]
 
 
 @pytest.fixture(scope="module")
@@ -50,7 +50,7 @@ def _up8(c):
     return (c + 7) // 8 * 8
 
 
-def run_conv(torch, x_chw, w, bias, slope, stride, resid_chw=None, wm=0, ngroups=0):
+def run_conv(torch, x_chw, w, bias, slope, stride, resid_chw=None, wm=0, ngroups=0, wait_cycles=0, extra_tx=0):
     """One conv through fhk_conv3x3 on NHWC device buffers; returns CHW f16."""
     import flyhigh_engine_b200 as fh
     L = fh.lib()
@@ -84,7 +84,7 @@ def run_conv(torch, x_chw, w, bias, slope, stride, resid_chw=None, wm=0, ngroups
     p.wpack, p.bias, p.slope = wp.data_ptr(), b.data_ptr(), (s.data_ptr() if s is not None else None)
     p.epi, p.out, p.out_cs, p.out_bs = 0, out.data_ptr(), ocs, 0
     p.res, p.res_cs, p.res_bs, p.n = (r.data_ptr() if r is not None else None), ocs, 0, 1
-    p.wm, p.ngroups = wm, ngroups
+    p.wm, p.ngroups, p.wait_cycles, p.test_extra_tx = wm, ngroups, wait_cycles, extra_tx
     rc = L.fhk_conv3x3(ctypes.byref(p), stride, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == 0, rc
     torch.cuda.synchronize()
@@ -135,6 +135,28 @@ def test_conv_matches_oracle(torch_cuda, h, w, cin, cout, stride, res, split):
     assert rel_l2(got, ref) < 2e-3
     # f32 accumulation order differs from the oracle's: a few f16 ulps at most
     assert np.abs(got - ref).max() <= 4e-3 * max(1.0, np.abs(ref).max())
+
+
+@pytest.mark.parametrize("h,w,cin,cout", [(60, 108, 48, 48), (30, 54, 279, 96)])
+def test_conv_weight_wait_runs_out(torch_cuda, h, w, cin, cout):
+    """Failure detection without a fault: the weight staging's mbarrier is made to expect 16 bytes that no copy brings
+    (whole slice: 48 -> 48; streamed ring: 279 -> 96), so every wait runs out after its bound; the kernel counts the
+    timeouts, finishes and leaves the context usable, and the next normal launch is exact again."""
+    import flyhigh_engine_b200 as fh
+    from oracle import oracle
+    L = fh.lib()
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((cin, h, w)).astype(np.float16)
+    wt = (rng.standard_normal((cout, cin, 3, 3)) / np.sqrt(9 * cin)).astype(np.float16).astype(np.float32)
+    bias = np.zeros(cout, np.float32)
+    slope = np.full(cout, 0.1, np.float32)
+    assert L.fhk_conv_wait_timeouts(1) >= 0
+    run_conv(torch_cuda, x, wt, bias, slope, 1, wait_cycles=200000, extra_tx=16)
+    assert L.fhk_conv_wait_timeouts(1) > 0
+    got = run_conv(torch_cuda, x, wt, bias, slope, 1).astype(np.float32)
+    assert L.fhk_conv_wait_timeouts(0) == 0
+    ref = oracle.conv(x, wt, bias, slope, 1).astype(np.float32)
+    assert rel_l2(got, ref) < 2e-3
 
 
 def _session_pair(model_dir, w, h, frames, t=0.5, **opts):
