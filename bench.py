@@ -232,14 +232,22 @@ def main():
         outbuf = torch.empty((H, W, 4), dtype=torch.uint8).pin_memory()
         out_np = outbuf.numpy()
 
+        outs = [out, s.add_output()]
+
         def step_host():
+            # the reference's call sequence per interval (write, pair, mid, read), with two output slots: each
+            # interval's frame is read back while the next interval runs (read_rgba waits for that slot only)
             s.write(slots[0], pin_np[0])
+            prev = None
             for i in range(1, n):
                 a, b = slots[(i - 1) % 2], slots[i % 2]
                 s.write(b, pin_np[i])
                 s.pair(a, b)
-                s.mid(0.5, out)
-                s.read_into(out, out_np)
+                s.mid(0.5, outs[i % 2])
+                if prev is not None:
+                    s.read_into(prev, out_np)
+                prev = outs[i % 2]
+            s.read_into(prev, out_np)
 
         step_host()
         barrier()

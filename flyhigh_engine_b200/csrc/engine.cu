@@ -283,6 +283,10 @@ struct FrameSet {
     __half *A = nullptr, *aq = nullptr, *i8 = nullptr, *i16 = nullptr, *f8 = nullptr, *f16 = nullptr;
     uint64_t gen = 1, feat_gen = 0;
     cudaGraphExec_t graph = nullptr;
+    // host uploads run on the session's upload stream: `uploaded` marks the last one (st waits for it before the
+    // set is read), `released` the last compute launch that reads the set (an upload into it waits for that)
+    cudaEvent_t uploaded = nullptr, released = nullptr;
+    bool upload_pending = false, ever_read = false;
 };
 
 // An input slot is double-buffered: a write into the frame set the current pair reads goes to the other set, so the
@@ -330,6 +334,9 @@ struct FhSession {
 
     std::vector<InSlot> ins;
     std::vector<uint8_t*> outs;
+    std::vector<cudaEvent_t> out_ready;  // per output slot: after the last launch that writes it (read_rgba waits)
+    // host <-> device copies on their own streams, so they overlap the compute of other intervals
+    cudaStream_t h2d = nullptr, d2h = nullptr;
     // frame-stage scratch, pair and mid buffers
     __half *e1 = nullptr, *e3 = nullptr;
     uint32_t* changed = nullptr;
@@ -406,6 +413,14 @@ struct FhSession {
     ~FhSession() {
         if (st) cudaStreamSynchronize(st);
         if (side) cudaStreamSynchronize(side);
+        if (h2d) cudaStreamSynchronize(h2d);
+        if (d2h) cudaStreamSynchronize(d2h);
+        for (auto& fs : sets) {
+            if (fs->uploaded) cudaEventDestroy(fs->uploaded);
+            if (fs->released) cudaEventDestroy(fs->released);
+        }
+        for (cudaEvent_t e : out_ready)
+            if (e) cudaEventDestroy(e);
         for (int i = 0; i < 4; i++) {
             if (fork_ev[i]) cudaEventDestroy(fork_ev[i]);
             if (join_ev[i]) cudaEventDestroy(join_ev[i]);
@@ -417,6 +432,8 @@ struct FhSession {
         for (void* p : allocs) cudaFree(p);
         if (eng) eng->tensor_bytes -= std::min(eng->tensor_bytes, bytes);
         if (side) cudaStreamDestroy(side);
+        if (h2d) cudaStreamDestroy(h2d);
+        if (d2h) cudaStreamDestroy(d2h);
         if (st) cudaStreamDestroy(st);
     }
 
@@ -740,6 +757,31 @@ struct FhSession {
 
     FrameSet& cur_set(uint32_t i) const { return *ins[i].set[ins[i].cur]; }
 
+    // st reads the set next: order it after the set's pending host upload
+    void wait_upload(const FrameSet& fs) {
+        FrameSet& f = const_cast<FrameSet&>(fs);
+        if (!f.upload_pending) return;
+        CK(cudaStreamWaitEvent(st, f.uploaded, 0));
+        f.upload_pending = false;
+    }
+    // the launches issued on st so far are the last to read these sets
+    void mark_read(const FrameSet& a, const FrameSet& b) {
+        for (const FrameSet* c : {&a, &b}) {
+            FrameSet& f = const_cast<FrameSet&>(*c);
+            CK(cudaEventRecord(f.released, st));
+            f.ever_read = true;
+        }
+    }
+    // a host upload into the set: on the upload stream after the last compute that reads the set; returns once the
+    // caller's buffer has been copied
+    void upload(FrameSet& fs, const uint8_t* rgba, size_t n) {
+        if (fs.ever_read) CK(cudaStreamWaitEvent(h2d, fs.released, 0));
+        CK(cudaMemcpyAsync(fs.frame, rgba, n, cudaMemcpyHostToDevice, h2d));
+        CK(cudaEventRecord(fs.uploaded, h2d));
+        fs.upload_pending = true;
+        CK(cudaEventSynchronize(fs.uploaded));
+    }
+
     void ensure_features(FrameSet& fs) {
         if (fs.feat_gen == fs.gen) return;
         if (!fs.graph) fs.graph = capture([&] { run_frame(fs); }, &frame_kernels);
@@ -766,9 +808,12 @@ struct FhSession {
         check_in(b);
         FrameSet& A = cur_set(a);
         FrameSet& B = cur_set(b);
+        wait_upload(A);
+        wait_upload(B);
         ensure_features(A);
         ensure_features(B);
         CK(cudaGraphLaunch(pair_graph(A, B), st));
+        mark_read(A, B);
         pair = PairSrc{&A, &B};
         have_pair = true;
     }
@@ -792,6 +837,8 @@ struct FhSession {
         cudaGraphExec_t g = mid_graph(out);
         CK(fhk::set_scalar(tdev, t, st));
         CK(cudaGraphLaunch(g, st));
+        mark_read(*pair.a, *pair.b);
+        CK(cudaEventRecord(out_ready[out], st));
         mid_ran = true;
     }
 
@@ -805,6 +852,8 @@ struct FhSession {
         fs->i16 = img(h16, w16, 4);
         fs->f8 = img(h8, w8, C8P);
         fs->f16 = img(h16, w16, C16P);
+        CK(cudaEventCreateWithFlags(&fs->uploaded, cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&fs->released, cudaEventDisableTiming));
         sets.push_back(std::move(fs));
         return sets.back().get();
     }
@@ -833,6 +882,8 @@ struct FhSession {
         if (!std::isfinite(t)) fail("t is not finite");
         FrameSet& A = cur_set(a);
         FrameSet& B = cur_set(b);
+        wait_upload(A);
+        wait_upload(B);
         std::vector<std::pair<std::string, cudaEvent_t>> marks;
         CK(cudaStreamSynchronize(st));
         CK(fhk::delay(st, 4000000));
@@ -851,6 +902,8 @@ struct FhSession {
             throw;
         }
         prof = nullptr;
+        mark_read(A, B);
+        CK(cudaEventRecord(out_ready[out], st));
         CK(cudaStreamSynchronize(st));
         A.feat_gen = A.gen;
         B.feat_gen = B.gen;
@@ -877,6 +930,10 @@ struct FhSession {
     }
     int add_output() {
         outs.push_back(alloc_n<uint8_t>((size_t)w * h * 4));
+        cudaEvent_t e = nullptr;
+        CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        CK(cudaEventRecord(e, st));  // the zeroed buffer
+        out_ready.push_back(e);
         return (int)outs.size() - 1;
     }
 };
@@ -977,6 +1034,8 @@ FhSession* session_new(FhEngine* e, const FhModel* m, const FhSessionOptions& o)
     CK(cudaSetDevice(e->device));
     CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&s->side, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&s->h2d, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&s->d2h, cudaStreamNonBlocking));
     for (int i = 0; i < 4; i++) {
         CK(cudaEventCreateWithFlags(&s->fork_ev[i], cudaEventDisableTiming));
         CK(cudaEventCreateWithFlags(&s->join_ev[i], cudaEventDisableTiming));
@@ -1158,7 +1217,7 @@ int fh_session_write_rgba(const FhSession* cs, uint32_t slot, const uint8_t* rgb
         s->check_in(slot);
         const size_t n = (size_t)s->w * s->h * 4;
         if (len != n) fail("frame is %zu bytes, %dx%dx4 = %zu expected", len, s->w, s->h, n);
-        CK(cudaMemcpyAsync(s->write_target(slot).frame, rgba, n, cudaMemcpyHostToDevice, s->st));
+        s->upload(s->write_target(slot), rgba, n);
         return 0;
     });
 }
@@ -1187,8 +1246,10 @@ int fh_session_read_rgba(const FhSession* cs, uint32_t slot, uint8_t* buf, size_
         s->check_out(slot);
         const size_t n = (size_t)s->w * s->h * 4;
         if (n > cap) fail("output buffer too small (%zu needed)", n);
-        CK(cudaMemcpyAsync(buf, s->outs[slot], n, cudaMemcpyDeviceToHost, s->st));
-        CK(cudaStreamSynchronize(s->st));
+        // after the last launch that writes the slot, not after everything queued since
+        CK(cudaStreamWaitEvent(s->d2h, s->out_ready[slot], 0));
+        CK(cudaMemcpyAsync(buf, s->outs[slot], n, cudaMemcpyDeviceToHost, s->d2h));
+        CK(cudaStreamSynchronize(s->d2h));
         return (int)n;
     });
 }
@@ -1351,7 +1412,9 @@ int fh_session_write_rgba_device(const FhSession* cs, uint32_t slot, const void*
         s->check_in(slot);
         const size_t n = (size_t)s->w * s->h * 4;
         if (len != n) fail("frame is %zu bytes, %dx%dx4 = %zu expected", len, s->w, s->h, n);
-        CK(cudaMemcpyAsync(s->write_target(slot).frame, dev, n, cudaMemcpyDeviceToDevice, s->st));
+        FrameSet& fs = s->write_target(slot);
+        s->wait_upload(fs);
+        CK(cudaMemcpyAsync(fs.frame, dev, n, cudaMemcpyDeviceToDevice, s->st));
         return 0;
     });
 }
@@ -1366,8 +1429,11 @@ int fh_session_advance_static(const FhSession* cs, uint32_t a, uint32_t b) {
         // keep_static_age.wgsl on the two frames only: the state advances exactly as a pair() would advance it
         const FrameSet& A = s->cur_set(a);
         const FrameSet& B = s->cur_set(b);
+        s->wait_upload(A);
+        s->wait_upload(B);
         CK(fhk::pair_planes(A.frame, B.frame, s->sargs, s->changed, nullptr, s->st));
         CK(fhk::static_age(A.frame, B.frame, s->changed, s->mask, s->sargs, s->state, s->age, s->st));
+        s->mark_read(A, B);
         return 0;
     });
 }
