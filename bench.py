@@ -320,15 +320,16 @@ def conv_flops_per_interval(s) -> float:
 
 
 def render_bytes(p) -> float:
-    """Algorithmic bytes of one full-resolution render: the two source frames read once (3 channels of f16 each,
-    12 B/px), the quarter-resolution flow / visibility (7 ch) and residual (3 ch) maps (f16), the rgba8 frame written
-    (4 B/px)."""
+    """Algorithmic bytes of one full-resolution render: the two source frames read once (B, G, R as f16, 12 B/px), the
+    static planes of the padded plane (age i16, near u8, the still test's per-pixel sums f32: 7 B/px), the
+    quarter-resolution flow / visibility (7 ch) and residual (3 ch) maps (f16), the rgba8 frame written (4 B/px)."""
     q = p["qh"] * p["qw"]
-    return float(W * H * (12 + 4) + q * (7 + 3) * 2)
+    return float(W * H * (12 + 4) + p["hp"] * p["wp"] * 7 + q * (7 + 3) * 2)
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one k_render launch at 1920 x 1080 (profiles/render_1080p.md)
-RENDER_TRAFFIC = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one k_render launch at 1920 x 1080, from the ncu capture summarised
+# in profiles/k_render_1080p.md (48.33 MB read + 0.90 MB written)
+RENDER_TRAFFIC = 49.24e6
 
 
 def roofline_blocks(s, prof, step_ms, intervals):

@@ -12,7 +12,9 @@
 extern "C" {
 #endif
 
-/* The CUDA stream (cudaStream_t) every call of this session is ordered on. 0 on success, -1 on error. */
+/* The CUDA stream (cudaStream_t) the session's compute is ordered on: pair, mid, the device-side writes below. Host
+ * uploads (fh_session_write_rgba) and readbacks (fh_session_read_rgba) run on two more streams of the session, ordered
+ * against this one by events, so they overlap the compute of other intervals. 0 on success, -1 on error. */
 int fh_session_cuda_stream(const FhSession* session, void** stream);
 
 /* The device buffer (width * height * 4 bytes, RGBA8) behind an input or output slot, for hosts whose frames already
