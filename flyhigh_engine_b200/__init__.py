@@ -68,6 +68,7 @@ EXPORTS = [
     ("fh_model_info", c_int, [c_void_p, c_char_p, c_size_t]),
     ("fh_session_options_default", SessionOptions, [c_uint32, c_uint32]),
     ("fh_session_create", c_void_p, [c_void_p, c_void_p, POINTER(SessionOptions)]),
+    ("fh_session_create_batched", c_void_p, [c_void_p, c_void_p, POINTER(SessionOptions), c_uint32]),
     ("fh_session_destroy", None, [c_void_p]),
     ("fh_session_add_input", c_int, [c_void_p]),
     ("fh_session_add_output", c_int, [c_void_p]),
@@ -284,13 +285,17 @@ def session_options(width: int, height: int, internal=None, k: int = 1, repair: 
 class Session:
     """The plans of a model for one frame size: Session(engine, model, width, height, internal="auto"|"frame"|(w, h),
     k=1, repair=1, render="model"|"bilinear"|"bicubic", static_protection=None|True|False|{"frames", "tolerance"},
-    keep_maps=False, protection_mask=False)."""
+    keep_maps=False, protection_mask=False, batch=None). batch = n > 1 queues pair / mid calls and runs n chained
+    intervals per launch (fh_session_create_batched); None leaves it to FH_BATCH."""
 
-    def __init__(self, engine: Engine, model: Model, width: int, height: int, **options):
+    def __init__(self, engine: Engine, model: Model, width: int, height: int, batch=None, **options):
         self._o = session_options(width, height, **options)
         self.width, self.height = width, height
         self._e, self._m = engine, model
-        self._h = lib().fh_session_create(engine._h, model._h, byref(self._o))
+        if batch is None:
+            self._h = lib().fh_session_create(engine._h, model._h, byref(self._o))
+        else:
+            self._h = lib().fh_session_create_batched(engine._h, model._h, byref(self._o), int(batch))
         if not self._h:
             raise _error()
 

@@ -436,14 +436,17 @@ cudaError_t launch_nt(int nt, const FhConvParams& p, cudaStream_t st) {
     }
 }
 
-// the split for a layer of this size: enough CTAs to occupy the 148 SMs, as few channel groups as that allows
+// the split for a layer of this size: enough CTAs to occupy the 148 SMs, as few channel groups as that allows. The
+// rows per CTA (wm, and with it the K split and the f32 summation order) follow one batch entry's size only, so an
+// entry's result does not depend on how many entries a launch carries; channel groups do not change the arithmetic
+// and count the whole batch.
 void choose_split(FhConvParams& q) {
     const int ntt = (q.cout + 7) / 8;
     const long long cols = (q.wo + TW - 1) / TW;
     if (q.wm <= 0) {
         q.wm = 1;
         for (int wm : {4, 2}) {
-            if (cols * ((q.ho + 2 * wm - 1) / (2 * wm)) * q.n >= 2 * 148) {
+            if (cols * ((q.ho + 2 * wm - 1) / (2 * wm)) >= 2 * 148) {
                 q.wm = wm;
                 break;
             }

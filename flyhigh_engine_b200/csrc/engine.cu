@@ -289,15 +289,48 @@ struct FrameSet {
     bool upload_pending = false, ever_read = false;
 };
 
-// An input slot is double-buffered: a write into the frame set the current pair reads goes to the other set, so the
-// pair's mids keep reading the frames the pair saw (the reference's pair owns tex_in copies of them) without a copy.
+// An input slot owns one or more frame sets: a write into a set that the current pair or a queued interval reads
+// goes to another set (made when none is free), so those keep reading the frames they were given (the reference's pair
+// owns tex_in copies of them) without a copy.
 struct InSlot {
-    FrameSet* set[2] = {nullptr, nullptr};
+    std::vector<FrameSet*> sets;
     int cur = 0;
 };
 
-struct PairSrc {  // the two frame sets of the current pair
-    const FrameSet *a, *b;
+// One side of a pair: a frame set's tensors (one entry), or consecutive entries of the batch arena (strides in
+// elements, bytes for the rgba8 frame). `key` identifies it for the graph caches.
+struct FView {
+    const uint8_t* frame = nullptr;
+    const __half *half = nullptr, *A = nullptr, *aq = nullptr, *i8 = nullptr, *i16 = nullptr, *f8 = nullptr,
+                 *f16 = nullptr;
+    long long frame_bs = 0, half_bs = 0, A_bs = 0, aq_bs = 0, i8_bs = 0, i16_bs = 0, f8_bs = 0, f16_bs = 0;
+    const void* key = nullptr;
+};
+FView view_of(const FrameSet& s) {
+    FView v;
+    v.frame = s.frame;
+    v.half = s.half;
+    v.A = s.A;
+    v.aq = s.aq;
+    v.i8 = s.i8;
+    v.i16 = s.i16;
+    v.f8 = s.f8;
+    v.f16 = s.f16;
+    v.key = &s;
+    return v;
+}
+
+struct PairSrc {  // the two sides of the current pair, and their frame sets when they are sets
+    FView a, b;
+    const FrameSet *sa = nullptr, *sb = nullptr;
+};
+
+// an interval queued for a batched launch: pair(a, b), then mid(t, out) once it has come
+struct Pending {
+    FrameSet *a = nullptr, *b = nullptr;
+    bool mid = false;
+    float t = 0;
+    uint32_t out = 0;
 };
 
 }  // namespace
@@ -352,6 +385,17 @@ struct FhSession {
 
     bool have_pair = false;
     PairSrc pair{};
+    // Batching (nbat > 1): queued intervals launch nbat at a time as one graph over the arena, a FrameSet of
+    // nbat + 1 entries (entry j holds the frame of time nbat - j, so the newest interval is entry 0). The per-interval
+    // buffers hold nbat entries, the frame-stage scratch nbat + 1.
+    int nbat = 1;
+    int single = 0;  // > 0: pair / mid run at once (timed calls, warm-up)
+    std::vector<Pending> pend;
+    FrameSet arena;
+    uint8_t* arena_out = nullptr;  // nbat rendered frames, scattered to the output slots
+    cudaGraphExec_t batch_graph = nullptr;
+    int batch_kernels = 0;
+    long long batches_run = 0;
     std::map<std::pair<const FrameSet*, const FrameSet*>, cudaGraphExec_t> pair_graphs;
     std::map<std::tuple<const void*, const void*, const void*, const void*, const void*>, cudaGraphExec_t> mid_graphs;
     int pair_kernels = 0, mid_kernels = 0, frame_kernels = 0;
@@ -381,7 +425,9 @@ struct FhSession {
     }
     template <class T>
     T* alloc_n(size_t n) { return (T*)dalloc(n * sizeof(T)); }
-    __half* img(int hh, int ww, int cs) { return alloc_n<__half>((size_t)hh * ww * cs); }
+    __half* img(int hh, int ww, int cs, int n = 1) { return alloc_n<__half>((size_t)n * hh * ww * cs); }
+    // elements of one entry of an NHWC buffer
+    static long long E(int hh, int ww, int cs) { return (long long)hh * ww * cs; }
 
     // issues body's launches on the side stream, after everything issued on st so far (inline while profiling, so
     // that every launch is timed alone)
@@ -428,6 +474,7 @@ struct FhSession {
         for (auto& fs : sets)
             if (fs->graph) cudaGraphExecDestroy(fs->graph);
         for (auto& kv : pair_graphs) cudaGraphExecDestroy(kv.second);
+        if (batch_graph) cudaGraphExecDestroy(batch_graph);
         for (auto& kv : mid_graphs) cudaGraphExecDestroy(kv.second);
         for (void* p : allocs) cudaFree(p);
         if (eng) eng->tensor_bytes -= std::min(eng->tensor_bytes, bytes);
@@ -491,17 +538,22 @@ struct FhSession {
         return s;
     }
 
-    void conv(const std::string& key, std::vector<const __half*> ptrs, int hh, int ww, __half* out, int out_cs,
-              const __half* res = nullptr, int res_cs = 0, int epi = 0) {
+    // an NHWC view with its batch stride (elements)
+    struct CV {
+        const __half* p;
+        long long bs;
+    };
+    void conv(const std::string& key, std::vector<CV> srcs, int hh, int ww, CV out, int out_cs, int n, CV res = {nullptr, 0},
+              int res_cs = 0, int epi = 0) {
         const ConvLayer& L = convs.at(key);
-        if (ptrs.size() != L.src.size()) fail("conv %s: %zu sources for %zu", key.c_str(), ptrs.size(), L.src.size());
+        if (srcs.size() != L.src.size()) fail("conv %s: %zu sources for %zu", key.c_str(), srcs.size(), L.src.size());
         FhConvParams p{};
-        for (size_t i = 0; i < ptrs.size(); i++) {
+        for (size_t i = 0; i < srcs.size(); i++) {
             p.src[i] = L.src[i];
-            p.src[i].p = ptrs[i];
-            p.src[i].bs = 0;
+            p.src[i].p = srcs[i].p;
+            p.src[i].bs = srcs[i].bs;
         }
-        p.nsrc = (int)ptrs.size();
+        p.nsrc = (int)srcs.size();
         p.h = hh;
         p.w = ww;
         p.ho = (hh - 1) / L.stride + 1;
@@ -512,11 +564,13 @@ struct FhSession {
         p.bias = L.bias;
         p.slope = L.slope;
         p.epi = epi;
-        p.out = out;
+        p.out = const_cast<__half*>(out.p);
         p.out_cs = out_cs;
-        p.res = res;
+        p.out_bs = out.bs;
+        p.res = res.p;
         p.res_cs = res_cs;
-        p.n = 1;
+        p.res_bs = res.bs;
+        p.n = n;
         p.wm = 0;  // split chosen by size
         p.ngroups = 0;
         int e = fhk_conv3x3(&p, L.stride, st);
@@ -593,138 +647,194 @@ struct FhSession {
         film_w2 = up(w2);
         film_b2 = up(b2);
 
-        // buffers
-        e1 = img(h8, w8, C8P);
-        e3 = img(h16, w16, C16P);
+        // buffers: nbat entries per interval buffer, nbat + 1 for the frame-stage scratch when batching
+        const int nb = nbat, nf = nbat > 1 ? nbat + 1 : 1;
+        e1 = img(h8, w8, C8P, nf);
+        e3 = img(h16, w16, C16P, nf);
         if (protects) {
-            changed = alloc_n<uint32_t>((size_t)hp * fhk::changed_words(wp));
+            changed = alloc_n<uint32_t>((size_t)nb * hp * fhk::changed_words(wp));
             mask = alloc_n<uint8_t>((size_t)hp * wp);
             state = alloc_n<uchar4>((size_t)hp * wp);
-            age = alloc_n<int16_t>((size_t)hp * wp);
-            nearp = alloc_n<uint8_t>((size_t)hp * wp);
+            age = alloc_n<int16_t>((size_t)nb * hp * wp);
+            nearp = alloc_n<uint8_t>((size_t)nb * hp * wp);
         }
-        if (still) dsum = alloc_n<float>((size_t)hp * wp);
-        cv = img(h16, w16, 56);
-        ch1 = img(h16, w16, CCP);
-        ch2 = img(h16, w16, CCP);
-        ch3r = img(h16, w16, CCP);
-        hcb = img(h16, w16, CCP);
-        ob = img(h16, w16, 16);
-        fv = img(h8, w8, 8);
-        wbuf = img(h8, w8, 88);
-        fcv = img(h8, w8, 32);
-        fr1 = img(h8, w8, CRP);
-        fr2 = img(h8, w8, CRP);
-        fr3 = img(h8, w8, CRP);
-        wt36 = img(h8, w8, 40);
-        coef = alloc_n<float>(16);
-        maps = alloc_n<float>((size_t)6 * hc * wc);
-        tmp = alloc_n<float>((size_t)5 * hc * wc);
-        tdev = alloc_n<float>(1);
-        hm = img(h8, w8, CRP);
-        fh1 = img(h8, w8, CRP);
-        fh2 = img(h8, w8, CRP);
-        dfilm = img(h8, w8, 8);
-        ftvt = img(h8, w8, 8);
-        up7 = img(qh, qw, 8);
-        rx = img(qh, qw, 16);
-        rq1 = img(qh, qw, CQP);
-        rq2 = img(qh, qw, CQP);
-        rq3 = img(qh, qw, CQP);
-        rt = img(qh, qw, 4);
+        if (still) dsum = alloc_n<float>((size_t)nb * hp * wp);
+        cv = img(h16, w16, 56, nb);
+        ch1 = img(h16, w16, CCP, nb);
+        ch2 = img(h16, w16, CCP, nb);
+        ch3r = img(h16, w16, CCP, nb);
+        hcb = img(h16, w16, CCP, nb);
+        ob = img(h16, w16, 16, nb);
+        fv = img(h8, w8, 8, nb);
+        wbuf = img(h8, w8, 88, nb);
+        fcv = img(h8, w8, 32, nb);
+        fr1 = img(h8, w8, CRP, nb);
+        fr2 = img(h8, w8, CRP, nb);
+        fr3 = img(h8, w8, CRP, nb);
+        wt36 = img(h8, w8, 40, nb);
+        coef = alloc_n<float>((size_t)16 * nb);
+        maps = alloc_n<float>((size_t)6 * hc * wc * nb);
+        tmp = alloc_n<float>((size_t)5 * hc * wc * nb);
+        tdev = alloc_n<float>(nb);
+        hm = img(h8, w8, CRP, nb);
+        fh1 = img(h8, w8, CRP, nb);
+        fh2 = img(h8, w8, CRP, nb);
+        dfilm = img(h8, w8, 8, nb);
+        ftvt = img(h8, w8, 8, nb);
+        up7 = img(qh, qw, 8, nb);
+        rx = img(qh, qw, 16, nb);
+        rq1 = img(qh, qw, CQP, nb);
+        rq2 = img(qh, qw, CQP, nb);
+        rq3 = img(qh, qw, CQP, nb);
+        rt = img(qh, qw, 4, nb);
+        if (nbat > 1) {
+            arena.frame = alloc_n<uint8_t>((size_t)nf * w * h * 4);
+            arena.half = alloc_n<__half>((size_t)nf * w * h * 4);
+            arena.A = img(NH, NW, 4, nf);
+            arena.aq = img(qh, qw, 4, nf);
+            arena.i8 = img(h8, w8, 4, nf);
+            arena.i16 = img(h16, w16, 4, nf);
+            arena.f8 = img(h8, w8, C8P, nf);
+            arena.f16 = img(h16, w16, C16P, nf);
+            arena_out = alloc_n<uint8_t>((size_t)nb * w * h * 4);
+        }
         CK(cudaStreamSynchronize(st));
     }
 
-    // ---- stages ----
-    void run_frame(FrameSet& s) {
+    // consecutive arena entries from entry j on
+    FView arena_view(int j) const {
+        FView v;
+        v.frame_bs = (long long)w * h * 4;
+        v.half_bs = (long long)w * h * 4;
+        v.A_bs = E(NH, NW, 4);
+        v.aq_bs = E(qh, qw, 4);
+        v.i8_bs = E(h8, w8, 4);
+        v.i16_bs = E(h16, w16, 4);
+        v.f8_bs = E(h8, w8, C8P);
+        v.f16_bs = E(h16, w16, C16P);
+        v.frame = arena.frame + j * v.frame_bs;
+        v.half = arena.half + j * v.half_bs;
+        v.A = arena.A + j * v.A_bs;
+        v.aq = arena.aq + j * v.aq_bs;
+        v.i8 = arena.i8 + j * v.i8_bs;
+        v.i16 = arena.i16 + j * v.i16_bs;
+        v.f8 = arena.f8 + j * v.f8_bs;
+        v.f16 = arena.f16 + j * v.f16_bs;
+        v.key = reinterpret_cast<const char*>(&arena) + j;
+        return v;
+    }
+
+    // ---- stages: n entries (n frames, resp. n pairs with the sides' entries at the views' strides) ----
+    void run_frame(const FView& v, int n) {
+        __half* A = const_cast<__half*>(v.A);
+        __half* half = const_cast<__half*>(v.half);
         branch([&] {
-            CK(fhk::frame_half(s.frame, 0, w, h, s.half, 0, 1, st));
+            CK(fhk::frame_half(v.frame, v.frame_bs, w, h, half, v.half_bs, n, st));
             mark("frame_half");
         });
-        CK(fhk::frame_to_input(s.frame, 0, w, h, hp, wp, internal, ihp, iwp, {s.A, 0}, 1, st));
+        CK(fhk::frame_to_input(v.frame, v.frame_bs, w, h, hp, wp, internal, ihp, iwp, {A, v.A_bs}, n, st));
         mark("frame_to_input");
-        CK(fhk::input_pyramid({s.A, 0}, NH, NW, {s.aq, 0}, {s.i8, 0}, {s.i16, 0}, 1, st));
+        CK(fhk::input_pyramid({A, v.A_bs}, NH, NW, {const_cast<__half*>(v.aq), v.aq_bs},
+                              {const_cast<__half*>(v.i8), v.i8_bs}, {const_cast<__half*>(v.i16), v.i16_bs}, n, st));
         mark("input_pyramid");
-        conv("e1", {s.aq}, qh, qw, e1, C8P);
-        conv("e2", {e1}, h8, w8, s.f8, C8P, e1, C8P);
-        conv("e3", {s.f8}, h8, w8, e3, C16P);
-        conv("e4", {e3}, h16, w16, s.f16, C16P, e3, C16P);
+        const long long e8 = E(h8, w8, C8P), e16 = E(h16, w16, C16P);
+        conv("e1", {{v.aq, v.aq_bs}}, qh, qw, {e1, e8}, C8P, n);
+        conv("e2", {{e1, e8}}, h8, w8, {v.f8, v.f8_bs}, C8P, n, {e1, e8}, C8P);
+        conv("e3", {{v.f8, v.f8_bs}}, h8, w8, {e3, e16}, C16P, n);
+        conv("e4", {{e3, e16}}, h16, w16, {v.f16, v.f16_bs}, C16P, n, {e3, e16}, C16P);
         join_branches();
     }
 
-    void run_pair(const FrameSet& A, const FrameSet& B) {
+    // A and B: the pair's sides, with equal strides. The static age pass walks the n pairs in time order: entry n - 1
+    // first (a batch keeps its newest interval in entry 0), so its strides are negated.
+    void run_pair(const FView& A, const FView& B, int n) {
+        const long long P = (long long)hp * wp, CW = (long long)hp * fhk::changed_words(wp);
         // the static age pass and the still test's plane read the two frames only: a branch beside the network
         if (protects || still)
             branch([&] {
-                CK(fhk::pair_planes(A.frame, B.frame, sargs, protects ? changed : nullptr, still ? dsum : nullptr, st));
+                CK(fhk::pair_planes(A.frame, B.frame, A.frame_bs, sargs, protects ? changed : nullptr, CW,
+                                    still ? dsum : nullptr, P, n, st));
                 mark("pair_planes");
                 if (protects) {
-                    CK(fhk::static_age(A.frame, B.frame, changed, mask, sargs, state, age, st));
+                    const long long l = n - 1;
+                    CK(fhk::static_age(A.frame + l * A.frame_bs, B.frame + l * B.frame_bs, -A.frame_bs, changed + l * CW,
+                                       -CW, mask, sargs, state, age + l * P, -P, n, st));
                     mark("static_age");
-                    CK(fhk::static_near(age, wp, hp, min_age, nearp, st));
+                    CK(fhk::static_near(age, P, wp, hp, min_age, nearp, n, st));
                     mark("static_near");
                 }
             });
+        const long long ecv = E(h16, w16, 56), ecc = E(h16, w16, CCP), eob = E(h16, w16, 16), efv = E(h8, w8, 8),
+                        ewb = E(h8, w8, 88), efc = E(h8, w8, 32), efr = E(h8, w8, CRP), ewt = E(h8, w8, 40);
         // coarse: img16 = (i16a, i16b), luma, sad r3 (graph ops 18-25), then c1..head (26-32)
-        CK(fhk::sad_volume(A.i16, 4, B.i16, 4, 0, h16, w16, 3, cv, 56, 0, 1, st));
+        CK(fhk::sad_volume(A.i16, 4, B.i16, 4, A.i16_bs, h16, w16, 3, cv, 56, ecv, n, st));
         mark("sad_volume r3");
-        conv("c1", {A.f16, B.f16, A.i16, B.i16, cv}, h16, w16, ch1, CCP);
-        conv("c2", {ch1}, h16, w16, ch2, CCP);
-        conv("c3", {ch2}, h16, w16, ch3r, CCP, ch1, CCP);
-        conv("c4", {ch3r}, h16, w16, hcb, CCP);
-        conv("head", {hcb}, h16, w16, ob, 16);
-        CK(fhk::upsample_flow_vis(ob, 16, 0, h16, w16, fv, 0, h8, w8, 1, st));
+        conv("c1", {{A.f16, A.f16_bs}, {B.f16, B.f16_bs}, {A.i16, A.i16_bs}, {B.i16, B.i16_bs}, {cv, ecv}}, h16, w16,
+             {ch1, ecc}, CCP, n);
+        conv("c2", {{ch1, ecc}}, h16, w16, {ch2, ecc}, CCP, n);
+        conv("c3", {{ch2, ecc}}, h16, w16, {ch3r, ecc}, CCP, n, {ch1, ecc}, CCP);
+        conv("c4", {{ch3r, ecc}}, h16, w16, {hcb, ecc}, CCP, n);
+        conv("head", {{hcb, ecc}}, h16, w16, {ob, eob}, 16, n);
+        CK(fhk::upsample_flow_vis(ob, 16, eob, h16, w16, fv, efv, h8, w8, n, st));
         mark("upsample_flow_vis");
         // fine iterations (graph op 42)
         for (int it = 0; it < k; it++) {
-            fhk::WarpFineArgs wa{fv, 0, A.f8, B.f8, C8P, c8, 0, {A.i8, 0}, {B.i8, 0}, h8, w8, wbuf, 0};
-            CK(fhk::warp_fine(wa, 1, st));
+            fhk::WarpFineArgs wa{fv, efv, A.f8, B.f8, C8P, c8, A.f8_bs, {const_cast<__half*>(A.i8), A.i8_bs},
+                                 {const_cast<__half*>(B.i8), B.i8_bs}, h8, w8, wbuf, ewb};
+            CK(fhk::warp_fine(wa, n, st));
             mark("warp_fine");
-            CK(fhk::sad_volume(wbuf + 80, 88, wbuf + 84, 88, 0, h8, w8, 2, fcv, 32, 0, 1, st));
+            CK(fhk::sad_volume(wbuf + 80, 88, wbuf + 84, 88, ewb, h8, w8, 2, fcv, 32, efc, n, st));
             mark("sad_volume r2");
-            if (it == 0) conv("r1_0", {wbuf, wbuf + 40, wbuf + 80, fv, fcv}, h8, w8, fr1, CRP);
-            else conv("r1", {wbuf, wbuf + 40, wbuf + 80, fv, fr3, fcv}, h8, w8, fr1, CRP);
-            conv("r2", {fr1}, h8, w8, fr2, CRP);
-            conv("r3", {fr2}, h8, w8, fr3, CRP);
-            conv("out", {fr3}, h8, w8, fv, 8, fv, 8);
+            if (it == 0)
+                conv("r1_0", {{wbuf, ewb}, {wbuf + 40, ewb}, {wbuf + 80, ewb}, {fv, efv}, {fcv, efc}}, h8, w8, {fr1, efr},
+                     CRP, n);
+            else
+                conv("r1", {{wbuf, ewb}, {wbuf + 40, ewb}, {wbuf + 80, ewb}, {fv, efv}, {fr3, efr}, {fcv, efc}}, h8, w8,
+                     {fr1, efr}, CRP, n);
+            conv("r2", {{fr1, efr}}, h8, w8, {fr2, efr}, CRP, n);
+            conv("r3", {{fr2, efr}}, h8, w8, {fr3, efr}, CRP, n);
+            conv("out", {{fr3, efr}}, h8, w8, {fv, efv}, 8, n, {fv, efv}, 8);
         }
         // the repair rewrites the flow; the convex-upsample weights depend on h only (graph op 62: conv up.w of h),
         // so the two run side by side
         if (repair > 0)
             branch([&] {
-                fhk::GmArgs g{fv, 0, h8, w8, A.A, B.A, 0, NH, NW, hc, wc, r_blk, r_dwin, delta, dmin, coef, maps, tmp};
-                CK(fhk::gmhs_fit(g, 1, st));
+                fhk::GmArgs g{fv, efv, h8, w8, A.A, B.A, A.A_bs, NH, NW, hc, wc, r_blk, r_dwin, delta, dmin, coef, maps, tmp};
+                CK(fhk::gmhs_fit(g, n, st));
                 mark("gmhs fit");
-                CK(fhk::gmhs_maps(g, 1, st));
+                CK(fhk::gmhs_maps(g, n, st));
                 mark("gmhs maps");
-                CK(fhk::gmhs_select(g, 1, st));
+                CK(fhk::gmhs_select(g, n, st));
                 mark("gmhs select");
             });
-        conv("up", {fr3}, h8, w8, wt36, 40);
+        conv("up", {{fr3, efr}}, h8, w8, {wt36, ewt}, 40, n);
         join_branches();
     }
 
-    void run_mid(const PairSrc& p, uint8_t* out) {
-        fhk::FilmArgs fa{tdev, film_w1, film_b1, film_w2, film_b2, film_hidden, cr, fr3, CRP, 0, hm, CRP, 0, h8, w8};
-        CK(fhk::film(fa, 1, st));
+    void run_mid(const PairSrc& p, uint8_t* out, long long out_bs, int n) {
+        const long long P = (long long)hp * wp, efr = E(h8, w8, CRP), e8 = E(h8, w8, 8), ewt = E(h8, w8, 40),
+                        eup = E(qh, qw, 8), erx = E(qh, qw, 16), erq = E(qh, qw, CQP), ert = E(qh, qw, 4);
+        fhk::FilmArgs fa{tdev, film_w1, film_b1, film_w2, film_b2, film_hidden, cr, fr3, CRP, efr, hm, CRP, efr, h8, w8};
+        CK(fhk::film(fa, n, st));
         mark("film");
-        conv("fh1", {hm}, h8, w8, fh1, CRP);
-        conv("fh2", {fh1}, h8, w8, fh2, CRP);
-        conv("fout", {fh2}, h8, w8, dfilm, 8);
-        CK(fhk::mid_combine(tdev, fv, 0, dfilm, 0, ftvt, 0, h8, w8, 1, st));
+        conv("fh1", {{hm, efr}}, h8, w8, {fh1, efr}, CRP, n);
+        conv("fh2", {{fh1, efr}}, h8, w8, {fh2, efr}, CRP, n);
+        conv("fout", {{fh2, efr}}, h8, w8, {dfilm, e8}, 8, n);
+        CK(fhk::mid_combine(tdev, fv, e8, dfilm, e8, ftvt, e8, h8, w8, n, st));
         mark("mid_combine");
-        CK(fhk::convex_up(wt36, 40, 0, ftvt, 0, h8, w8, up7, 0, 1, st));
+        CK(fhk::convex_up(wt36, 40, ewt, ftvt, e8, h8, w8, up7, eup, n, st));
         mark("convex_up");
-        CK(fhk::refine_input(up7, 0, {p.a->aq, 0}, {p.b->aq, 0}, qh, qw, rx, 0, 1, st));
+        CK(fhk::refine_input(up7, eup, {const_cast<__half*>(p.a.aq), p.a.aq_bs}, {const_cast<__half*>(p.b.aq), p.b.aq_bs}, qh,
+                             qw, rx, erx, n, st));
         mark("refine_input");
-        conv("q1", {rx}, qh, qw, rq1, CQP);
-        conv("q2", {rq1}, qh, qw, rq2, CQP);
-        conv("q3", {rq2}, qh, qw, rq3, CQP);
-        conv("q4", {rq3}, qh, qw, rt, 4, nullptr, 0, 1);
-        fhk::RenderArgs ra{p.a->half, p.b->half, 0, w, h, hp, wp, up7, 0, rt, 0, qh, qw, fsx, fsy, cubic ? 1 : 0,
-                           (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, 0, dsum, nearp, 0,
-                           min_age, out, 0};
-        CK(fhk::render(ra, 1, st));
+        conv("q1", {{rx, erx}}, qh, qw, {rq1, erq}, CQP, n);
+        conv("q2", {{rq1, erq}}, qh, qw, {rq2, erq}, CQP, n);
+        conv("q3", {{rq2, erq}}, qh, qw, {rq3, erq}, CQP, n);
+        conv("q4", {{rq3, erq}}, qh, qw, {rt, ert}, 4, n, {nullptr, 0}, 0, 1);
+        fhk::RenderArgs ra{p.a.half, p.b.half, p.a.half_bs, w, h, hp, wp, up7, eup, rt, ert, qh, qw, fsx, fsy,
+                           cubic ? 1 : 0, (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, P, dsum,
+                           nearp, P, min_age, out, out_bs};
+        CK(fhk::render(ra, n, st));
         mark("render");
     }
 
@@ -755,7 +865,7 @@ struct FhSession {
         return ex;
     }
 
-    FrameSet& cur_set(uint32_t i) const { return *ins[i].set[ins[i].cur]; }
+    FrameSet& cur_set(uint32_t i) const { return *ins[i].sets[ins[i].cur]; }
 
     // st reads the set next: order it after the set's pending host upload
     void wait_upload(const FrameSet& fs) {
@@ -784,7 +894,7 @@ struct FhSession {
 
     void ensure_features(FrameSet& fs) {
         if (fs.feat_gen == fs.gen) return;
-        if (!fs.graph) fs.graph = capture([&] { run_frame(fs); }, &frame_kernels);
+        if (!fs.graph) fs.graph = capture([&] { run_frame(view_of(fs), 1); }, &frame_kernels);
         CK(cudaGraphLaunch(fs.graph, st));
         fs.feat_gen = fs.gen;
     }
@@ -799,8 +909,21 @@ struct FhSession {
     cudaGraphExec_t pair_graph(const FrameSet& A, const FrameSet& B) {
         auto key = std::make_pair(&A, &B);
         auto it = pair_graphs.find(key);
-        if (it == pair_graphs.end()) it = pair_graphs.emplace(key, capture([&] { run_pair(A, B); }, &pair_kernels)).first;
+        if (it == pair_graphs.end())
+            it = pair_graphs.emplace(key, capture([&] { run_pair(view_of(A), view_of(B), 1); }, &pair_kernels)).first;
         return it->second;
+    }
+
+    // one pair now, on entry 0 of the per-interval buffers
+    void pair_now(FrameSet& A, FrameSet& B) {
+        wait_upload(A);
+        wait_upload(B);
+        ensure_features(A);
+        ensure_features(B);
+        CK(cudaGraphLaunch(pair_graph(A, B), st));
+        mark_read(A, B);
+        pair = PairSrc{view_of(A), view_of(B), &A, &B};
+        have_pair = true;
     }
 
     void do_pair(uint32_t a, uint32_t b) {
@@ -808,38 +931,135 @@ struct FhSession {
         check_in(b);
         FrameSet& A = cur_set(a);
         FrameSet& B = cur_set(b);
-        wait_upload(A);
-        wait_upload(B);
-        ensure_features(A);
-        ensure_features(B);
-        CK(cudaGraphLaunch(pair_graph(A, B), st));
-        mark_read(A, B);
-        pair = PairSrc{&A, &B};
-        have_pair = true;
+        if (nbat > 1 && single == 0) {
+            // queue it; a queued pair whose mid never came, or a pair that does not continue the queued chain, first
+            // lets the queue run
+            if (!pend.empty() && (!pend.back().mid || pend.back().b != &A)) flush();
+            pend.push_back(Pending{&A, &B});
+            return;
+        }
+        flush();
+        pair_now(A, B);
     }
 
     cudaGraphExec_t mid_graph(uint32_t out) {
-        auto key = std::make_tuple((const void*)pair.a, (const void*)pair.b, (const void*)nullptr, (const void*)nullptr,
+        auto key = std::make_tuple(pair.a.key, pair.b.key, (const void*)nullptr, (const void*)nullptr,
                                    (const void*)outs[out]);
         auto it = mid_graphs.find(key);
         if (it == mid_graphs.end()) {
             PairSrc p = pair;
             uint8_t* o = outs[out];
-            it = mid_graphs.emplace(key, capture([&] { run_mid(p, o); }, &mid_kernels)).first;
+            it = mid_graphs.emplace(key, capture([&] { run_mid(p, o, 0, 1); }, &mid_kernels)).first;
         }
         return it->second;
     }
 
     void do_mid(float t, uint32_t out) {
         check_out(out);
-        if (!have_pair) fail("pair two input slots first");
         if (!std::isfinite(t)) fail("t is not finite");
+        if (nbat > 1 && single == 0 && !pend.empty() && !pend.back().mid) {
+            Pending& q = pend.back();
+            q.mid = true;
+            q.t = t;
+            q.out = out;
+            if ((int)pend.size() == nbat) flush();
+            return;
+        }
+        flush();  // a further mid of the last queued pair: that pair has run by now
+        if (!have_pair) fail("pair two input slots first");
         cudaGraphExec_t g = mid_graph(out);
         CK(fhk::set_scalar(tdev, t, st));
         CK(cudaGraphLaunch(g, st));
-        mark_read(*pair.a, *pair.b);
+        if (pair.sa) mark_read(*pair.sa, *pair.sb);
         CK(cudaEventRecord(out_ready[out], st));
         mid_ran = true;
+    }
+
+    // Runs the queued intervals: a full chain of nbat intervals with mids as one batch, anything else one by one.
+    void flush() {
+        if (pend.empty()) return;
+        std::vector<Pending> q;
+        q.swap(pend);
+        if ((int)q.size() == nbat && q.back().mid) {
+            run_batch(q);
+            return;
+        }
+        ++single;
+        try {
+            for (const Pending& x : q) {
+                pair_now(*x.a, *x.b);
+                if (x.mid) {
+                    cudaGraphExec_t g = mid_graph(x.out);
+                    CK(fhk::set_scalar(tdev, x.t, st));
+                    CK(cudaGraphLaunch(g, st));
+                    mark_read(*x.a, *x.b);
+                    CK(cudaEventRecord(out_ready[x.out], st));
+                    mid_ran = true;
+                }
+            }
+        } catch (...) {
+            --single;
+            throw;
+        }
+        --single;
+    }
+
+    // nbat chained intervals (q[i].b == q[i + 1].a) as one graph: the frames of times 0..nbat gathered into the arena
+    // (time t at entry nbat - t), the frame stage of all nbat + 1, the pairs and mids of all nbat (interval i at entry
+    // nbat - 1 - i), then the rendered frames scattered to their output slots in time order.
+    void run_batch(const std::vector<Pending>& q) {
+        const int n = nbat;
+        const size_t fb = (size_t)w * h * 4;
+        for (int j = 0; j <= n; j++) {
+            FrameSet* f = j == 0 ? q[n - 1].b : q[n - j].a;
+            wait_upload(*f);
+            CK(cudaMemcpyAsync(arena.frame + j * fb, f->frame, fb, cudaMemcpyDeviceToDevice, st));
+        }
+        for (int j = 0; j <= n; j++) {
+            FrameSet* f = j == 0 ? q[n - 1].b : q[n - j].a;
+            CK(cudaEventRecord(f->released, st));
+            f->ever_read = true;
+        }
+        std::vector<float> tv(n);
+        for (int e = 0; e < n; e++) tv[e] = q[n - 1 - e].t;
+        CK(cudaMemcpyAsync(tdev, tv.data(), n * sizeof(float), cudaMemcpyHostToDevice, st));
+        if (!batch_graph) {
+            const FView fa = arena_view(1), fbv = arena_view(0);
+            batch_graph = capture(
+                [&] {
+                    run_frame(arena_view(0), n + 1);
+                    run_pair(fa, fbv, n);
+                    run_mid(PairSrc{fa, fbv}, arena_out, (long long)fb, n);
+                },
+                &batch_kernels);
+        }
+        CK(cudaGraphLaunch(batch_graph, st));
+        for (int i = 0; i < n; i++) {
+            const int e = n - 1 - i;
+            CK(cudaMemcpyAsync(outs[q[i].out], arena_out + e * fb, fb, cudaMemcpyDeviceToDevice, st));
+            CK(cudaEventRecord(out_ready[q[i].out], st));
+        }
+        // the newest interval is entry 0 of every per-interval buffer: a further mid of it runs there
+        FView a0 = arena_view(1), b0 = arena_view(0);
+        for (FView* v : {&a0, &b0}) v->frame_bs = v->half_bs = v->A_bs = v->aq_bs = v->i8_bs = v->i16_bs = v->f8_bs = v->f16_bs = 0;
+        pair = PairSrc{a0, b0, nullptr, nullptr};
+        have_pair = true;
+        mid_ran = true;
+        batches_run++;
+    }
+
+    // a set is in use while the current pair or a queued interval reads it
+    bool in_use(const FrameSet* f) const {
+        if (have_pair && (pair.sa == f || pair.sb == f)) return true;
+        for (const Pending& x : pend)
+            if (x.a == f || x.b == f) return true;
+        return false;
+    }
+    // a queued interval writes the output slot
+    bool out_pending(uint32_t out) const {
+        for (const Pending& x : pend)
+            if (x.mid && x.out == out) return true;
+        return false;
     }
 
     FrameSet* new_set() {
@@ -854,20 +1074,29 @@ struct FhSession {
         fs->f16 = img(h16, w16, C16P);
         CK(cudaEventCreateWithFlags(&fs->uploaded, cudaEventDisableTiming));
         CK(cudaEventCreateWithFlags(&fs->released, cudaEventDisableTiming));
+        // the zeroing memsets of the new buffers run on st: an upload (on its own stream) waits for them
+        CK(cudaEventRecord(fs->released, st));
+        fs->ever_read = true;
         sets.push_back(std::move(fs));
         return sets.back().get();
     }
 
-    // the frame set a write into slot i goes to (the other one when the current pair reads the current one)
+    // the frame set a write into slot i goes to: the current one, unless the current pair or a queued interval reads
+    // it; then a free set of the slot, or a new one
     FrameSet& write_target(uint32_t i) {
         check_in(i);
         InSlot& s = ins[i];
-        FrameSet* c = s.set[s.cur];
-        if (have_pair && (pair.a == c || pair.b == c)) {
-            if (!s.set[s.cur ^ 1]) s.set[s.cur ^ 1] = new_set();
-            s.cur ^= 1;
+        if (in_use(s.sets[s.cur])) {
+            int pick = -1;
+            for (int k = 0; k < (int)s.sets.size() && pick < 0; k++)
+                if (!in_use(s.sets[k])) pick = k;
+            if (pick < 0) {
+                s.sets.push_back(new_set());
+                pick = (int)s.sets.size() - 1;
+            }
+            s.cur = pick;
         }
-        FrameSet& fs = *s.set[s.cur];
+        FrameSet& fs = *s.sets[s.cur];
         fs.gen++;
         return fs;
     }
@@ -880,6 +1109,7 @@ struct FhSession {
         check_in(b);
         check_out(out);
         if (!std::isfinite(t)) fail("t is not finite");
+        flush();
         FrameSet& A = cur_set(a);
         FrameSet& B = cur_set(b);
         wait_upload(A);
@@ -890,12 +1120,12 @@ struct FhSession {
         prof = &marks;
         try {
             mark("start");
-            run_frame(A);
-            run_frame(B);
-            run_pair(A, B);
+            run_frame(view_of(A), 1);
+            run_frame(view_of(B), 1);
+            run_pair(view_of(A), view_of(B), 1);
             CK(fhk::set_scalar(tdev, t, st));
             mark("set_t");
-            run_mid(PairSrc{&A, &B}, outs[out]);
+            run_mid(PairSrc{view_of(A), view_of(B), &A, &B}, outs[out], 0, 1);
         } catch (...) {
             prof = nullptr;
             for (auto& m : marks) cudaEventDestroy(m.second);
@@ -907,7 +1137,7 @@ struct FhSession {
         CK(cudaStreamSynchronize(st));
         A.feat_gen = A.gen;
         B.feat_gen = B.gen;
-        pair = PairSrc{&A, &B};
+        pair = PairSrc{view_of(A), view_of(B), &A, &B};
         have_pair = true;
         std::string js = "[";
         for (size_t i = 1; i < marks.size(); i++) {
@@ -924,7 +1154,7 @@ struct FhSession {
 
     int add_input() {
         InSlot s;
-        s.set[0] = new_set();
+        s.sets.push_back(new_set());
         ins.push_back(s);
         return (int)ins.size() - 1;
     }
@@ -936,6 +1166,16 @@ struct FhSession {
         out_ready.push_back(e);
         return (int)outs.size() - 1;
     }
+};
+
+// Runs what is queued, then keeps pair / mid immediate while it lives (timed calls, warm-up).
+struct SingleScope {
+    FhSession* s;
+    explicit SingleScope(FhSession* ss) : s(ss) {
+        s->flush();
+        s->single++;
+    }
+    ~SingleScope() { s->single--; }
 };
 
 namespace {
@@ -1027,9 +1267,17 @@ void derive(const FhModel* m, const FhSessionOptions& o, FhSession* s) {
     s->delta = 1.5f * sc;
 }
 
-FhSession* session_new(FhEngine* e, const FhModel* m, const FhSessionOptions& o) {
+// batch 0: from FH_BATCH (default 1)
+FhSession* session_new(FhEngine* e, const FhModel* m, const FhSessionOptions& o, int batch = 0) {
     auto s = std::make_unique<FhSession>();
     derive(m, o, s.get());
+    if (batch == 0) {
+        batch = 1;
+        if (const char* v = getenv("FH_BATCH")) batch = atoi(v);
+        if (batch < 1) batch = 1;
+    }
+    if (batch > 16) fail("batch: %d intervals per launch (1..16)", batch);
+    s->nbat = batch;
     s->eng = e;
     CK(cudaSetDevice(e->device));
     CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
@@ -1194,6 +1442,14 @@ FhSession* fh_session_create(const FhEngine* e, const FhModel* m, const FhSessio
     });
 }
 
+FhSession* fh_session_create_batched(const FhEngine* e, const FhModel* m, const FhSessionOptions* o, uint32_t batch) {
+    return guard((FhSession*)nullptr, [&] {
+        if (!e || !m || !o) fail("null argument");
+        if (batch < 1 || batch > 16) fail("batch: %u intervals per launch (1..16)", batch);
+        return session_new(const_cast<FhEngine*>(e), m, *o, (int)batch);
+    });
+}
+
 void fh_session_destroy(FhSession* s) { delete s; }
 
 int fh_session_add_input(FhSession* s) {
@@ -1227,6 +1483,7 @@ int fh_session_write_mask(const FhSession* cs, const uint8_t* mask, size_t len) 
         FhSession* s = const_cast<FhSession*>(cs);
         if (!s || !mask) fail("null argument");
         if (!s->o.protection_mask) fail("the session was built without protection_mask");
+        s->flush();  // queued pairs see the mask they were given
         if (len != (size_t)s->w * s->h) fail("mask is %zu bytes, %dx%d = %zu expected", len, s->w, s->h, (size_t)s->w * s->h);
         // net/session_ext.rs:156-178: replicate-padded to the padded plane, nonzero protects
         std::vector<uint8_t> plane((size_t)s->wp * s->hp);
@@ -1244,6 +1501,7 @@ int fh_session_read_rgba(const FhSession* cs, uint32_t slot, uint8_t* buf, size_
         FhSession* s = const_cast<FhSession*>(cs);
         if (!s || !buf) fail("null argument");
         s->check_out(slot);
+        if (s->out_pending(slot)) s->flush();
         const size_t n = (size_t)s->w * s->h * 4;
         if (n > cap) fail("output buffer too small (%zu needed)", n);
         // after the last launch that writes the slot, not after everything queued since
@@ -1285,6 +1543,7 @@ int fh_session_pair_timed(const FhSession* cs, uint32_t a, uint32_t b, double* m
     return guard(-1, [&] {
         FhSession* s = const_cast<FhSession*>(cs);
         if (!s || !ms) fail("null argument");
+        SingleScope single(s);
         s->check_in(a);
         s->check_in(b);
         cudaEvent_t e0, e1;
@@ -1319,6 +1578,7 @@ int fh_session_mid_timed(const FhSession* cs, float t, uint32_t out, double* ms)
     return guard(-1, [&] {
         FhSession* s = const_cast<FhSession*>(cs);
         if (!s || !ms) fail("null argument");
+        SingleScope single(s);
         s->check_out(out);
         if (!s->have_pair) fail("pair two input slots first");
         s->do_mid(t, out);
@@ -1346,6 +1606,7 @@ int fh_session_mid_timed(const FhSession* cs, float t, uint32_t out, double* ms)
 int fh_session_warm_up(FhSession* s) {
     return guard(-1, [&] {
         if (!s) fail("null argument");
+        SingleScope single(s);
         while (s->ins.size() < 2) s->add_input();
         if (s->outs.empty()) s->add_output();
         s->do_pair(0, 1);
@@ -1391,9 +1652,11 @@ int fh_session_cuda_stream(const FhSession* s, void** stream) {
     });
 }
 
-int fh_session_slot_device_ptr(const FhSession* s, uint32_t slot, int output, void** ptr) {
+int fh_session_slot_device_ptr(const FhSession* cs, uint32_t slot, int output, void** ptr) {
     return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
         if (!s || !ptr) fail("null argument");
+        s->flush();  // the buffer is the caller's to use: nothing queued reads or writes it
         if (output) {
             s->check_out(slot);
             *ptr = s->outs[slot];
@@ -1423,6 +1686,7 @@ int fh_session_advance_static(const FhSession* cs, uint32_t a, uint32_t b) {
     return guard(-1, [&] {
         FhSession* s = const_cast<FhSession*>(cs);
         if (!s) fail("null argument");
+        s->flush();
         s->check_in(a);
         s->check_in(b);
         if (!s->protects) return 0;
@@ -1431,8 +1695,8 @@ int fh_session_advance_static(const FhSession* cs, uint32_t a, uint32_t b) {
         const FrameSet& B = s->cur_set(b);
         s->wait_upload(A);
         s->wait_upload(B);
-        CK(fhk::pair_planes(A.frame, B.frame, s->sargs, s->changed, nullptr, s->st));
-        CK(fhk::static_age(A.frame, B.frame, s->changed, s->mask, s->sargs, s->state, s->age, s->st));
+        CK(fhk::pair_planes(A.frame, B.frame, 0, s->sargs, s->changed, 0, nullptr, 0, 1, s->st));
+        CK(fhk::static_age(A.frame, B.frame, 0, s->changed, 0, s->mask, s->sargs, s->state, s->age, 0, 1, s->st));
         s->mark_read(A, B);
         return 0;
     });
@@ -1460,10 +1724,11 @@ long fh_session_debug_tensor(const FhSession* cs, const char* name, float* out, 
     return guard(-1L, [&]() -> long {
         FhSession* s = const_cast<FhSession*>(cs);
         if (!s || !name || !dims) fail("null argument");
+        s->flush();
         if (!s->have_pair) fail("no pair has run");
         std::string n(name);
-        const FrameSet& A = *s->pair.a;
-        const FrameSet& B = *s->pair.b;
+        const FView& A = s->pair.a;
+        const FView& B = s->pair.b;
         // (pointer, pixel pitch, channel offset, channels, height, width, kind 0 = f16 / 1 = int16 / 2 = rgba8 planes)
         const void* p = nullptr;
         int cs_ = 0, c0 = 0, c = 0, hh = 0, ww = 0, kind = 0;

@@ -227,24 +227,25 @@ FH_DEV float diff3(uint32_t a, uint32_t b, const float* lut) {
 //    in f32 and equal to the shader's 27-term running sum whatever the order.
 // Blocks are 32 x 8: a warp is one 32-pixel segment of a row, so its ballot is one word of the bit plane.
 __global__ void __launch_bounds__(256) k_pair_planes(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb,
-                                                     StaticArgs s, uint32_t* changed, float* dsum) {
+                                                     long long frame_bs, StaticArgs s, uint32_t* changed,
+                                                     long long changed_bs, float* dsum, long long dsum_bs) {
     __shared__ float lut[256];
     for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
     __syncthreads();
     pdl_wait();
     pdl_trigger();
-    const int x = blockIdx.x * 32 + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
+    const int x = blockIdx.x * 32 + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (y >= s.hp) return;  // warp-uniform
     const bool in = x < s.wp;
     uint32_t a = 0, b = 0;
     if (in) {
         const long long src = (long long)min(y, s.h - 1) * s.w + min(x, s.w - 1);
-        a = __ldg(reinterpret_cast<const uint32_t*>(fa) + src);
-        b = __ldg(reinterpret_cast<const uint32_t*>(fb) + src);
+        a = __ldg(reinterpret_cast<const uint32_t*>(fa + n * frame_bs) + src);
+        b = __ldg(reinterpret_cast<const uint32_t*>(fb + n * frame_bs) + src);
     }
     if (changed) {
         const uint32_t word = __ballot_sync(0xffffffffu, in && diff3(a, b, lut) >= s.thr);
-        if (threadIdx.x == 0) changed[(long long)y * ((s.wp + 31) >> 5) + blockIdx.x] = word;
+        if (threadIdx.x == 0) changed[n * changed_bs + (long long)y * ((s.wp + 31) >> 5) + blockIdx.x] = word;
     }
     if (dsum && in) {
         float d = 0.0f;
@@ -252,21 +253,22 @@ __global__ void __launch_bounds__(256) k_pair_planes(const uint8_t* __restrict__
             const int sh = 16 - 8 * c;
             d = d + fabsf(lut[(a >> sh) & 255] - lut[(b >> sh) & 255]);
         }
-        dsum[(long long)y * s.wp + x] = d;
+        dsum[n * dsum_bs + (long long)y * s.wp + x] = d;
     }
 }
 
 // render_static's on_static (gpu/pipeline.rs:10-34) per pixel: an age >= min_age in the clamped 3 x 3 neighbourhood
-__global__ void k_static_near(const int16_t* __restrict__ age, int W, int H, float min_age, uint8_t* near) {
+__global__ void k_static_near(const int16_t* __restrict__ age, long long bs, int W, int H, float min_age, uint8_t* near) {
     pdl_wait();
     pdl_trigger();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
     if (x >= W || y >= H) return;
+    const int16_t* ag = age + blockIdx.z * bs;
     bool hit = false;
     for (int dy = -1; dy <= 1; dy++)
         for (int dx = -1; dx <= 1; dx++)
-            hit |= (float)age[(long long)clampi(y + dy, 0, H - 1) * W + clampi(x + dx, 0, W - 1)] >= min_age;
-    near[(long long)y * W + x] = hit ? 1 : 0;
+            hit |= (float)ag[(long long)clampi(y + dy, 0, H - 1) * W + clampi(x + dx, 0, W - 1)] >= min_age;
+    near[blockIdx.z * bs + (long long)y * W + x] = hit ? 1 : 0;
 }
 
 // 32 bits of row `row` of the changed plane: bit i = changed(clamp(s0 + i, 0, W - 1)), the replicate clamp of the
@@ -289,14 +291,18 @@ FH_DEV uint32_t bit_window(const uint32_t* __restrict__ row, int ww, int W, int 
     return v;
 }
 
-// keep_static_age.wgsl:59-77: 9 near + 32 far probes of `changed`, the spread test, the state machine (decide, :28-36).
+// keep_static_age.wgsl:59-77: 9 near + 32 far probes of `changed`, the spread test, the state machine (decide, :28-36),
+// for np consecutive pairs in time order (pair i: frames fa + i * frame_bs, fb + i * frame_bs, its changed plane and its
+// age plane; strides may be negative). A pixel's state is loaded once, advanced pair by pair and stored once: the
+// pairs' sequential dependence is per pixel only.
 // A warp is one 32-pixel row segment. moved: lane l evaluates probe l (and probe 32 + l) as a 32-bit window of the
 // changed bits for the whole segment, and the warp ORs the windows. spread: max over the clamped 3 x 3 neighbourhood
 // and channels of |a(q) - a(o)|, |b(q) - b(o)|; the byte -> value table is monotone and f32 subtraction is monotone
 // in each operand, so that max is max(v(max_q) - v(o), v(o) - v(min_q)) per channel, exactly.
 __global__ void __launch_bounds__(256) k_static_age(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb,
-                                                    const uint32_t* __restrict__ changed, const uint8_t* __restrict__ mask,
-                                                    StaticArgs s, uchar4* state, int16_t* age) {
+                                                    long long frame_bs, const uint32_t* __restrict__ changed,
+                                                    long long changed_bs, const uint8_t* __restrict__ mask, StaticArgs s,
+                                                    uchar4* state, int16_t* age, long long age_bs, int np) {
     __shared__ float lut[256];
     for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
     __syncthreads();
@@ -306,95 +312,98 @@ __global__ void __launch_bounds__(256) k_static_age(const uint8_t* __restrict__ 
     // the padded plane: p.w = wp, p.h = hp in the reference dispatch (StaticParams::new(net, wp, hp, wp, hp))
     const int W = s.wp, H = s.hp, ww = (W + 31) >> 5;
     if (y >= H) return;  // warp-uniform
-    // moved: probes 0-31 are the far ring (direction l >> 2, distance 4 << (l & 3)), 32-40 the 3 x 3 neighbourhood
-    uint32_t mv;
+    const bool active = x < W;
+    const long long o = (long long)y * W + x;
+    uchar4 st = active ? state[o] : make_uchar4(0, 0, 0, 0);
+    const bool masked = active && s.use_mask && mask && mask[o];
+    // probes 0-31 are the far ring (direction l >> 2, distance 4 << (l & 3)), 32-40 the 3 x 3 neighbourhood
+    int pdx, pdy;
     {
         const int DX[8] = {1, -1, 0, 0, 1, -1, 1, -1}, DY[8] = {0, 0, 1, -1, 1, 1, -1, -1};
         const int far = 4 << (lane & 3), dir = lane >> 2;
-        int dx = 0, dy = 0;
+        pdx = pdy = 0;
 #pragma unroll
         for (int i = 0; i < 8; i++)
             if (dir == i) {
-                dx = DX[i] * far;
-                dy = DY[i] * far;
+                pdx = DX[i] * far;
+                pdy = DY[i] * far;
             }
-        mv = bit_window(changed + (long long)clampi(y + dy, 0, H - 1) * ww, ww, W, x0 + dx);
-        if (lane < 9) {
-            const int ndy = lane / 3 - 1, ndx = lane % 3 - 1;
-            mv |= bit_window(changed + (long long)clampi(y + ndy, 0, H - 1) * ww, ww, W, x0 + ndx);
-        }
-        mv = __reduce_or_sync(0xffffffffu, mv);
     }
-    const uint32_t own_word = __ldg(changed + (long long)y * ww + blockIdx.x);
-    // spread: column extremes over rows y - 1 .. y + 1, then across the neighbouring lanes' columns
-    const uint32_t* A = reinterpret_cast<const uint32_t*>(fa);
-    const uint32_t* B = reinterpret_cast<const uint32_t*>(fb);
     const int r0 = min(max(y - 1, 0), s.h - 1), r1 = min(y, s.h - 1), r2 = min(y + 1, s.h - 1);
     const int xc = min(x, s.w - 1);
-    const uint32_t a0 = __ldg(A + (long long)r0 * s.w + xc), a1 = __ldg(A + (long long)r1 * s.w + xc),
-                   a2 = __ldg(A + (long long)r2 * s.w + xc);
-    const uint32_t b0 = __ldg(B + (long long)r0 * s.w + xc), b1 = __ldg(B + (long long)r1 * s.w + xc),
-                   b2 = __ldg(B + (long long)r2 * s.w + xc);
-    uint32_t amax = __vmaxu4(__vmaxu4(a0, a1), a2), amin = __vminu4(__vminu4(a0, a1), a2);
-    uint32_t bmax = __vmaxu4(__vmaxu4(b0, b1), b2), bmin = __vminu4(__vminu4(b0, b1), b2);
-    // the edge lanes' outer column: x0 - 1 for lane 0 (x0 itself at the left border), x0 + 32 for lane 31
-    uint32_t eamax = 0, eamin = 0, ebmax = 0, ebmin = 0;
-    if (lane == 0 || lane == 31) {
-        const int xe = lane == 0 ? min(max(x0 - 1, 0), s.w - 1) : min(x0 + 32, s.w - 1);
-        const uint32_t e0 = __ldg(A + (long long)r0 * s.w + xe), e1 = __ldg(A + (long long)r1 * s.w + xe),
-                       e2 = __ldg(A + (long long)r2 * s.w + xe);
-        const uint32_t f0 = __ldg(B + (long long)r0 * s.w + xe), f1 = __ldg(B + (long long)r1 * s.w + xe),
-                       f2 = __ldg(B + (long long)r2 * s.w + xe);
-        eamax = __vmaxu4(__vmaxu4(e0, e1), e2);
-        eamin = __vminu4(__vminu4(e0, e1), e2);
-        ebmax = __vmaxu4(__vmaxu4(f0, f1), f2);
-        ebmin = __vminu4(__vminu4(f0, f1), f2);
-    }
-    {
-        uint32_t l_amax = __shfl_up_sync(0xffffffffu, amax, 1), r_amax = __shfl_down_sync(0xffffffffu, amax, 1);
-        uint32_t l_amin = __shfl_up_sync(0xffffffffu, amin, 1), r_amin = __shfl_down_sync(0xffffffffu, amin, 1);
-        uint32_t l_bmax = __shfl_up_sync(0xffffffffu, bmax, 1), r_bmax = __shfl_down_sync(0xffffffffu, bmax, 1);
-        uint32_t l_bmin = __shfl_up_sync(0xffffffffu, bmin, 1), r_bmin = __shfl_down_sync(0xffffffffu, bmin, 1);
-        if (lane == 0) {
-            l_amax = eamax;
-            l_amin = eamin;
-            l_bmax = ebmax;
-            l_bmin = ebmin;
+    const int xe = lane == 0 ? min(max(x0 - 1, 0), s.w - 1) : min(x0 + 32, s.w - 1);
+    for (int pi = 0; pi < np; pi++) {
+        const uint32_t* ch = changed + pi * changed_bs;
+        uint32_t mv = bit_window(ch + (long long)clampi(y + pdy, 0, H - 1) * ww, ww, W, x0 + pdx);
+        if (lane < 9) mv |= bit_window(ch + (long long)clampi(y + lane / 3 - 1, 0, H - 1) * ww, ww, W, x0 + lane % 3 - 1);
+        mv = __reduce_or_sync(0xffffffffu, mv);
+        const uint32_t own_word = __ldg(ch + (long long)y * ww + blockIdx.x);
+        // spread: column extremes over rows y - 1 .. y + 1, then across the neighbouring lanes' columns
+        const uint32_t* A = reinterpret_cast<const uint32_t*>(fa + pi * frame_bs);
+        const uint32_t* B = reinterpret_cast<const uint32_t*>(fb + pi * frame_bs);
+        const uint32_t a0 = __ldg(A + (long long)r0 * s.w + xc), a1 = __ldg(A + (long long)r1 * s.w + xc),
+                       a2 = __ldg(A + (long long)r2 * s.w + xc);
+        const uint32_t b0 = __ldg(B + (long long)r0 * s.w + xc), b1 = __ldg(B + (long long)r1 * s.w + xc),
+                       b2 = __ldg(B + (long long)r2 * s.w + xc);
+        uint32_t amax = __vmaxu4(__vmaxu4(a0, a1), a2), amin = __vminu4(__vminu4(a0, a1), a2);
+        uint32_t bmax = __vmaxu4(__vmaxu4(b0, b1), b2), bmin = __vminu4(__vminu4(b0, b1), b2);
+        // the edge lanes' outer column: x0 - 1 for lane 0 (x0 itself at the left border), x0 + 32 for lane 31
+        uint32_t eamax = 0, eamin = 0, ebmax = 0, ebmin = 0;
+        if (lane == 0 || lane == 31) {
+            const uint32_t e0 = __ldg(A + (long long)r0 * s.w + xe), e1 = __ldg(A + (long long)r1 * s.w + xe),
+                           e2 = __ldg(A + (long long)r2 * s.w + xe);
+            const uint32_t f0 = __ldg(B + (long long)r0 * s.w + xe), f1 = __ldg(B + (long long)r1 * s.w + xe),
+                           f2 = __ldg(B + (long long)r2 * s.w + xe);
+            eamax = __vmaxu4(__vmaxu4(e0, e1), e2);
+            eamin = __vminu4(__vminu4(e0, e1), e2);
+            ebmax = __vmaxu4(__vmaxu4(f0, f1), f2);
+            ebmin = __vminu4(__vminu4(f0, f1), f2);
         }
-        if (lane == 31) {
-            r_amax = eamax;
-            r_amin = eamin;
-            r_bmax = ebmax;
-            r_bmin = ebmin;
+        {
+            uint32_t l_amax = __shfl_up_sync(0xffffffffu, amax, 1), r_amax = __shfl_down_sync(0xffffffffu, amax, 1);
+            uint32_t l_amin = __shfl_up_sync(0xffffffffu, amin, 1), r_amin = __shfl_down_sync(0xffffffffu, amin, 1);
+            uint32_t l_bmax = __shfl_up_sync(0xffffffffu, bmax, 1), r_bmax = __shfl_down_sync(0xffffffffu, bmax, 1);
+            uint32_t l_bmin = __shfl_up_sync(0xffffffffu, bmin, 1), r_bmin = __shfl_down_sync(0xffffffffu, bmin, 1);
+            if (lane == 0) {
+                l_amax = eamax;
+                l_amin = eamin;
+                l_bmax = ebmax;
+                l_bmin = ebmin;
+            }
+            if (lane == 31) {
+                r_amax = eamax;
+                r_amin = eamin;
+                r_bmax = ebmax;
+                r_bmin = ebmin;
+            }
+            amax = __vmaxu4(amax, __vmaxu4(l_amax, r_amax));
+            amin = __vminu4(amin, __vminu4(l_amin, r_amin));
+            bmax = __vmaxu4(bmax, __vmaxu4(l_bmax, r_bmax));
+            bmin = __vminu4(bmin, __vminu4(l_bmin, r_bmin));
         }
-        amax = __vmaxu4(amax, __vmaxu4(l_amax, r_amax));
-        amin = __vminu4(amin, __vminu4(l_amin, r_amin));
-        bmax = __vmaxu4(bmax, __vmaxu4(l_bmax, r_bmax));
-        bmin = __vminu4(bmin, __vminu4(l_bmin, r_bmin));
-    }
-    if (x >= W) return;
-    float m = 0.0f;
+        if (!active) continue;
+        float m = 0.0f;
 #pragma unroll
-    for (int c = 0; c < 3; c++) {
-        const int sh = 16 - 8 * c;  // channel c of the BGR plane = byte 2 - c of the rgba pixel
-        const float va = lut[(a1 >> sh) & 255], vb = lut[(b1 >> sh) & 255];
-        m = fmaxf(m, lut[(amax >> sh) & 255] - va);
-        m = fmaxf(m, va - lut[(amin >> sh) & 255]);
-        m = fmaxf(m, lut[(bmax >> sh) & 255] - vb);
-        m = fmaxf(m, vb - lut[(bmin >> sh) & 255]);
+        for (int c = 0; c < 3; c++) {
+            const int sh = 16 - 8 * c;  // channel c of the BGR plane = byte 2 - c of the rgba pixel
+            const float va = lut[(a1 >> sh) & 255], vb = lut[(b1 >> sh) & 255];
+            m = fmaxf(m, lut[(amax >> sh) & 255] - va);
+            m = fmaxf(m, va - lut[(amin >> sh) & 255]);
+            m = fmaxf(m, lut[(bmax >> sh) & 255] - vb);
+            m = fmaxf(m, vb - lut[(bmin >> sh) & 255]);
+        }
+        const bool moved = (mv >> lane) & 1u;
+        const bool same = ((own_word >> lane) & 1u) == 0;
+        const bool still = same && m >= 0.03f;
+        const int raw = still ? min((int)st.x + 1, 255) : 0;
+        const int seen = still ? min((int)st.y + (moved ? 1 : 0), 255) : 0;
+        const int run = same ? min((int)st.z + 1, 255) : 0;
+        st = make_uchar4((unsigned char)raw, (unsigned char)seen, (unsigned char)run, 0);
+        int16_t a = (int16_t)(seen >= 2 ? raw : -run);
+        if (masked) a = 255;
+        age[pi * age_bs + o] = a;
     }
-    const bool moved = (mv >> lane) & 1u;
-    const bool same = ((own_word >> lane) & 1u) == 0;
-    const bool still = same && m >= 0.03f;
-    const long long o = (long long)y * W + x;
-    uchar4 st = state[o];
-    const int raw = still ? min((int)st.x + 1, 255) : 0;
-    const int seen = still ? min((int)st.y + (moved ? 1 : 0), 255) : 0;
-    const int run = same ? min((int)st.z + 1, 255) : 0;
-    state[o] = make_uchar4((unsigned char)raw, (unsigned char)seen, (unsigned char)run, 0);
-    int16_t a = (int16_t)(seen >= 2 ? raw : -run);
-    if (s.use_mask && mask && mask[o]) a = 255;
-    age[o] = a;
+    if (active) state[o] = st;
 }
 
 // ------------------------------------------------------------------------------------------------ cost volume ----
@@ -1245,20 +1254,23 @@ cudaError_t input_pyramid(Img4 A, int ih, int iw, Img4 aq, Img4 i8, Img4 i16, in
     return cudaGetLastError();
 }
 
-cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, const StaticArgs& s, uint32_t* changed, float* dsum,
+cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, long long frame_bs, const StaticArgs& s, uint32_t* changed,
+                        long long changed_bs, float* dsum, long long dsum_bs, int n, cudaStream_t st) {
+    { const cudaError_t e_ = launch(k_pair_planes, grid2(s.wp, s.hp, n, 32, 8), dim3(32, 8), 0, st, fa, fb, frame_bs, s, changed, changed_bs, dsum, dsum_bs); if (e_ != cudaSuccess) return e_; }
+    return cudaGetLastError();
+}
+
+cudaError_t static_near(const int16_t* age, long long bs, int wp, int hp, float min_age, uint8_t* near, int n,
                         cudaStream_t st) {
-    { const cudaError_t e_ = launch(k_pair_planes, grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st, fa, fb, s, changed, dsum); if (e_ != cudaSuccess) return e_; }
+    { const cudaError_t e_ = launch(k_static_near, grid2(wp, hp, n, 32, 8), dim3(32, 8), 0, st, age, bs, wp, hp, min_age, near); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
-cudaError_t static_near(const int16_t* age, int wp, int hp, float min_age, uint8_t* near, cudaStream_t st) {
-    { const cudaError_t e_ = launch(k_static_near, grid2(wp, hp, 1, 32, 8), dim3(32, 8), 0, st, age, wp, hp, min_age, near); if (e_ != cudaSuccess) return e_; }
-    return cudaGetLastError();
-}
-
-cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, const uint32_t* changed, const uint8_t* mask,
-                       const StaticArgs& s, uchar4* state, int16_t* age, cudaStream_t st) {
-    { const cudaError_t e_ = launch(k_static_age, grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st, fa, fb, changed, mask, s, state, age); if (e_ != cudaSuccess) return e_; }
+cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, long long frame_bs, const uint32_t* changed,
+                       long long changed_bs, const uint8_t* mask, const StaticArgs& s, uchar4* state, int16_t* age,
+                       long long age_bs, int np, cudaStream_t st) {
+    if (np < 1) return cudaErrorInvalidValue;
+    { const cudaError_t e_ = launch(k_static_age, grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st, fa, fb, frame_bs, changed, changed_bs, mask, s, state, age, age_bs, np); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 

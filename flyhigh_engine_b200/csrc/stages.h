@@ -28,14 +28,19 @@ struct StaticArgs {
     int use_mask;
 };
 // per pair: changed (diff >= thr, when protecting; one bit per pixel, changed_words(wp) 32-bit words per row) and
-// dsum (sum_c |A - B|, when the still test is on), padded plane
+// dsum (sum_c |A - B|, when the still test is on), padded plane; n pairs (frames, planes frame_bs / *_bs apart)
 inline int changed_words(int wp) { return (wp + 31) >> 5; }
-cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, const StaticArgs& s, uint32_t* changed, float* dsum,
+cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, long long frame_bs, const StaticArgs& s, uint32_t* changed,
+                        long long changed_bs, float* dsum, long long dsum_bs, int n, cudaStream_t st);
+// per pair after the age pass: near = an age >= min_age in the clamped 3 x 3 neighbourhood (render_static on_static);
+// n planes bs elements apart
+cudaError_t static_near(const int16_t* age, long long bs, int wp, int hp, float min_age, uint8_t* near, int n,
                         cudaStream_t st);
-// per pair after the age pass: near = an age >= min_age in the clamped 3 x 3 neighbourhood (render_static on_static)
-cudaError_t static_near(const int16_t* age, int wp, int hp, float min_age, uint8_t* near, cudaStream_t st);
-cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, const uint32_t* changed, const uint8_t* mask,
-                       const StaticArgs& s, uchar4* state, int16_t* age, cudaStream_t st);
+// the age pass over np consecutive pairs in time order (pair i: frames fa / fb + i * frame_bs, changed + i *
+// changed_bs, age + i * age_bs; strides may be negative), advancing the one state plane pair by pair
+cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, long long frame_bs, const uint32_t* changed,
+                       long long changed_bs, const uint8_t* mask, const StaticArgs& s, uchar4* state, int16_t* age,
+                       long long age_bs, int np, cudaStream_t st);
 
 // luma.wgsl + sad.wgsl on two 3-channel images (a view at channel offset 0): (2r+1)^2 cost channels into out (cs)
 cudaError_t sad_volume(const __half* a, int a_cs, const __half* b, int b_cs, long long in_bs, int h, int w, int r,

@@ -12,13 +12,25 @@
 extern "C" {
 #endif
 
+/* fh_session_create with batched execution. pair / mid calls are queued, and `batch` consecutive intervals run as one
+ * launch of batched kernels: each interval a pair whose first slot holds the previous pair's second frame, then one
+ * mid. The frames, the static-protection state and every output are identical to running the intervals one at a
+ * time. A call that observes or changes what queued intervals would produce first runs the queue, then carries on:
+ * read_rgba of a slot a queued mid writes, the timed calls, warm_up, write_mask, advance_static, slot_device_ptr,
+ * the debug tensors and the profile. So does a pair that does not continue the chain, or a second mid of one pair.
+ * A queue shorter than `batch` runs one interval at a time. batch is 1..16; 1 is fh_session_create. FH_BATCH=<n> in
+ * the environment sets the batch of fh_session_create. */
+FhSession* fh_session_create_batched(const FhEngine* engine, const FhModel* model, const FhSessionOptions* options,
+                                     uint32_t batch);
+
 /* The CUDA stream (cudaStream_t) the session's compute is ordered on: pair, mid, the device-side writes below. Host
  * uploads (fh_session_write_rgba) and readbacks (fh_session_read_rgba) run on two more streams of the session, ordered
  * against this one by events, so they overlap the compute of other intervals. 0 on success, -1 on error. */
 int fh_session_cuda_stream(const FhSession* session, void** stream);
 
 /* The device buffer (width * height * 4 bytes, RGBA8) behind an input or output slot, for hosts whose frames already
- * live in device memory (write it on the session's stream, or synchronise first). 0 on success, -1 on error. */
+ * live in device memory (write it on the session's stream, or synchronise first). Runs what a batched session has
+ * queued first. 0 on success, -1 on error. */
 int fh_session_slot_device_ptr(const FhSession* session, uint32_t slot, int output, void** ptr);
 
 /* A frame already in device memory into an input slot (a device-to-device copy on the session's stream). */

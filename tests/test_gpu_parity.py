@@ -379,6 +379,42 @@ def test_pipelined_host_io_matches_sequential(synth_model_dir):
         assert np.array_equal(x, y), i
 
 
+@pytest.mark.parametrize("batch,size,opts", [(4, (320, 192), {}), (3, (384, 160), dict(repair=2, k=2)),
+                                             (4, (1920, 1080), {})])
+def test_batched_session_matches_single(synth_model_dir, batch, size, opts):
+    """A batched session (pair / mid calls queued, `batch` chained intervals per launch) gives bit-identical frames
+    and static-protection state to one interval at a time: full batches, a partial queue run by a read, and a second
+    mid of the newest interval after a batch."""
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200 import synth_frames
+    w, h = size
+    model = fh.Model(synth_model_dir)
+    frames = synth_frames.sequence_c2(2 * batch + 2, w, h, seed=11)
+
+    def run(b, n):
+        s = fh.Session(fh.Engine(), model, w, h, batch=b, **opts)
+        ins = [s.add_input(), s.add_input()]
+        outs = [s.add_output() for _ in range(n)]
+        s.write(ins[0], frames[0])
+        for i in range(1, n):
+            s.write(ins[i % 2], frames[i])
+            s.pair(ins[(i - 1) % 2], ins[i % 2])
+            s.mid(0.25 + 0.5 * (i % 2), outs[i])
+        got = [np.frombuffer(s.read(outs[i]), np.uint8).copy() for i in range(1, n)]
+        extra = s.add_output()
+        s.mid(0.75, extra)  # a further mid of the newest pair
+        got.append(np.frombuffer(s.read(extra), np.uint8).copy())
+        return got, s.tensor("age")
+
+    # 2 * batch intervals: two full batches, then a mid of the newest one; one more: a partial queue run by a read
+    for n in (2 * batch + 1, 2 * batch + 2):
+        single, age1 = run(1, n)
+        batched, ageb = run(batch, n)
+        for i, (x, y) in enumerate(zip(single, batched)):
+            assert np.array_equal(x, y), (n, i)
+        assert np.array_equal(age1, ageb), n
+
+
 def test_errors_and_reports(synth_model_dir):
     """The C ABI's error behaviour (core.rs): -1 / NULL with fh_last_error, never a crash."""
     import flyhigh_engine_b200 as fh
