@@ -358,6 +358,9 @@ struct FhSession {
     cudaEvent_t fork_ev[4] = {}, join_ev[4] = {};
     int branches = 0;  // forks of the stage being issued, all joined by join_branches()
     bool pdl_on = true;  // programmatic dependent launch inside the stage graphs (FH_PDL=0 turns it off)
+    // launch priorities inside the stage graphs: the critical chain high, the side branches low (FH_PRIO=0: none)
+    bool prio_on = true;
+    int prio_hi = 0, prio_lo = 0;
     std::vector<void*> allocs;
     size_t bytes = 0;
 
@@ -380,6 +383,9 @@ struct FhSession {
     uint8_t* nearp = nullptr;   // per pair: near a protected pixel
     __half *cv, *ch1, *ch2, *ch3r, *hcb, *ob, *fv, *wbuf, *fcv, *fr1, *fr2, *fr3, *wt36;
     float *coef, *maps, *tmp, *tdev;
+    // antialias axis tables: the frame -> internal downscale (when internal), A -> aq (x0.25); null when a size needs
+    // more taps than the tables hold
+    fhk::AaAxis aa_fx{}, aa_fy{}, aa_qx{}, aa_qy{};
     __half *hm, *fh1, *fh2, *dfilm, *ftvt, *up7, *rx, *rq1, *rq2, *rq3, *rt;
     std::vector<std::unique_ptr<FrameSet>> sets;
 
@@ -443,6 +449,7 @@ struct FhSession {
         CK(cudaStreamWaitEvent(side, fork_ev[i], 0));
         std::swap(st, side);
         try {
+            fhk::PrioScope low(prio_on, prio_lo);
             body();
         } catch (...) {
             std::swap(st, side);
@@ -687,6 +694,21 @@ struct FhSession {
         rq2 = img(qh, qw, CQP, nb);
         rq3 = img(qh, qw, CQP, nb);
         rt = img(qh, qw, 4, nb);
+        auto make_axis = [&](int in, int out) {
+            int* first = alloc_n<int>(out);
+            int* count = alloc_n<int>(out);
+            float* wv = alloc_n<float>((size_t)out * fhk::AA_TAPS);
+            CK(fhk::aa_axis(in, out, first, count, wv, st));
+            return fhk::AaAxis{first, count, wv};
+        };
+        if (internal && fhk::aa_axis_fits(wp, NW) && fhk::aa_axis_fits(hp, NH)) {
+            aa_fx = make_axis(wp, NW);
+            aa_fy = make_axis(hp, NH);
+        }
+        if (fhk::aa_axis_fits(NW, qw) && fhk::aa_axis_fits(NH, qh)) {
+            aa_qx = make_axis(NW, qw);
+            aa_qy = make_axis(NH, qh);
+        }
         if (nbat > 1) {
             arena.frame = alloc_n<uint8_t>((size_t)nf * w * h * 4);
             arena.half = alloc_n<__half>((size_t)nf * w * h * 4);
@@ -732,10 +754,11 @@ struct FhSession {
             CK(fhk::frame_half(v.frame, v.frame_bs, w, h, half, v.half_bs, n, st));
             mark("frame_half");
         });
-        CK(fhk::frame_to_input(v.frame, v.frame_bs, w, h, hp, wp, internal, ihp, iwp, {A, v.A_bs}, n, st));
+        CK(fhk::frame_to_input(v.frame, v.frame_bs, w, h, hp, wp, internal, ihp, iwp, {A, v.A_bs}, n, st, aa_fx, aa_fy));
         mark("frame_to_input");
         CK(fhk::input_pyramid({A, v.A_bs}, NH, NW, {const_cast<__half*>(v.aq), v.aq_bs},
-                              {const_cast<__half*>(v.i8), v.i8_bs}, {const_cast<__half*>(v.i16), v.i16_bs}, n, st));
+                              {const_cast<__half*>(v.i8), v.i8_bs}, {const_cast<__half*>(v.i16), v.i16_bs}, n, st,
+                              aa_qx, aa_qy));
         mark("input_pyramid");
         const long long e8 = E(h8, w8, C8P), e16 = E(h16, w16, C16P);
         conv("e1", {{v.aq, v.aq_bs}}, qh, qw, {e1, e8}, C8P, n);
@@ -846,6 +869,7 @@ struct FhSession {
             // consecutive kernels of a stage overlap launch and drain (every kernel here starts with
             // griddepcontrol.wait)
             fhk::PdlScope pdl(pdl_on);
+            fhk::PrioScope high(prio_on, prio_hi);
             body();
         } catch (...) {
             branches = 0;
@@ -858,7 +882,7 @@ struct FhSession {
         CK(cudaGraphGetNodes(g, nullptr, &n));
         if (nodes) *nodes = (int)n;
         cudaGraphExec_t ex = nullptr;
-        cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+        cudaError_t e = cudaGraphInstantiate(&ex, g, prio_on ? cudaGraphInstantiateFlagUseNodePriority : 0);
         cudaGraphDestroy(g);
         CK(e);
         eng->graphs_built++;
@@ -1248,6 +1272,7 @@ void derive(const FhModel* m, const FhSessionOptions& o, FhSession* s) {
     s->still = !env_is("FH_STILL", "0");
     s->decisive = env_is("FH_BLEND", "decisive");
     s->pdl_on = !env_is("FH_PDL", "0");
+    s->prio_on = !env_is("FH_PRIO", "0");
     const bool keep_static = o.keep_static != 0;
     s->protects = keep_static || o.protection_mask;
     const int frames = keep_static ? std::clamp((int)(o.static_frames ? o.static_frames : 8), 1, 255) : 2;
@@ -1280,6 +1305,7 @@ FhSession* session_new(FhEngine* e, const FhModel* m, const FhSessionOptions& o,
     s->nbat = batch;
     s->eng = e;
     CK(cudaSetDevice(e->device));
+    CK(cudaDeviceGetStreamPriorityRange(&s->prio_lo, &s->prio_hi));
     CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&s->side, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&s->h2d, cudaStreamNonBlocking));

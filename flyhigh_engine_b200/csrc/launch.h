@@ -20,6 +20,30 @@ struct PdlScope {
     ~PdlScope() { pdl_flag() = prev; }
 };
 
+// A launch priority for this thread's launches (cudaLaunchAttributePriority; lower numbers run first), or none. The
+// session gives the critical chain of a stage graph the device's highest priority and its side branches the lowest,
+// so branch CTAs fill the SMs the chain leaves free.
+inline bool& prio_set() {
+    static thread_local bool on = false;
+    return on;
+}
+inline int& prio_value() {
+    static thread_local int v = 0;
+    return v;
+}
+struct PrioScope {
+    bool prev_on;
+    int prev_v;
+    PrioScope(bool on, int v) : prev_on(prio_set()), prev_v(prio_value()) {
+        prio_set() = on;
+        prio_value() = v;
+    }
+    ~PrioScope() {
+        prio_set() = prev_on;
+        prio_value() = prev_v;
+    }
+};
+
 template <typename... P, typename... A>
 cudaError_t launch(void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A&&... args) {
     cudaLaunchConfig_t cfg{};
@@ -27,13 +51,20 @@ cudaError_t launch(void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStre
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute at[2];
+    unsigned na = 0;
     if (pdl_flag()) {
-        cfg.attrs = at;
-        cfg.numAttrs = 1;
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
     }
+    if (prio_set()) {
+        at[na].id = cudaLaunchAttributePriority;
+        at[na].val.priority = prio_value();
+        na++;
+    }
+    cfg.attrs = na ? at : nullptr;
+    cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, k, std::forward<A>(args)...);
 }
 

@@ -5,6 +5,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+#include <cmath>
+
 #include <cooperative_groups.h>
 
 #include "fh_device.cuh"
@@ -42,8 +45,28 @@ FH_DEV void st4(__half* p, float b, float g, float r) {
 
 // tex_in.wgsl:10-19 + interp.wgsl:29-43 (aa): the padded plane is never stored; taps read the rgba8 frame at the
 // clamped position (replicate padding)
+// the antialias weights of output index o along an axis (in -> out): interp.wgsl:29-43 as the per-tap loops form them
+FH_DEV int aa_span(int in, int out, int o, float& c, float& f) {
+    const float s_ = (float)in / (float)out;
+    f = fmaxf(s_, 1.0f);
+    c = ((float)o + 0.5f) * s_;
+    return max(0, (int)floorf(c - f + 0.5f));
+}
+__global__ void k_aa_axis(int in, int out, int* first, int* count, float* w) {
+    const int o = blockIdx.x * blockDim.x + threadIdx.x;
+    if (o >= out) return;
+    float c, f;
+    const int lo = aa_span(in, out, o, c, f), hi = min(in, (int)floorf(c + f + 0.5f));
+    first[o] = lo;
+    count[o] = hi - lo;
+    for (int j = 0; j < AA_TAPS; j++)
+        w[o * AA_TAPS + j] = j < hi - lo ? fmaxf(0.0f, 1.0f - fabsf(((float)(lo + j) + 0.5f - c) / f)) : 0.0f;
+}
+
+// tex_in.wgsl:10-19 + interp.wgsl:29-43 (aa): the padded plane is never stored; taps read the rgba8 frame at the
+// clamped position (replicate padding). With axis tables the weights are read, not formed per tap.
 __global__ void k_frame_to_input(const uint8_t* __restrict__ frames, long long frame_bs, int w, int h, int hp, int wp,
-                                 int internal, int oh, int ow, __half* out, long long out_bs) {
+                                 int internal, int oh, int ow, __half* out, long long out_bs, AaAxis ax, AaAxis ay) {
     __shared__ float lut[256];
     for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
     __syncthreads();
@@ -58,28 +81,22 @@ __global__ void k_frame_to_input(const uint8_t* __restrict__ frames, long long f
         st4(o, lut[(v >> 16) & 255], lut[(v >> 8) & 255], lut[v & 255]);
         return;
     }
-    const float sh = (float)hp / (float)oh, sw = (float)wp / (float)ow;
-    const float fsh = fmaxf(sh, 1.0f), fsw = fmaxf(sw, 1.0f);
-    const float cy = ((float)oy + 0.5f) * sh, cx = ((float)ox + 0.5f) * sw;
-    const int ymin = max(0, (int)floorf(cy - fsh + 0.5f)), ymax = min(hp, (int)floorf(cy + fsh + 0.5f));
-    const int xmin = max(0, (int)floorf(cx - fsw + 0.5f)), xmax = min(wp, (int)floorf(cx + fsw + 0.5f));
     float ab = 0.0f, ag = 0.0f, ar = 0.0f, norm = 0.0f;
-    constexpr int XT = 8;  // the column weights of up to XT taps are formed once (downscales up to about 3.5x)
-    if (xmax - xmin <= XT) {
-        float wx[XT];
-        int xs[XT];
+    if (ax.w) {
+        const int x0 = __ldg(ax.first + ox), nx = __ldg(ax.count + ox);
+        const int y0 = __ldg(ay.first + oy), ny = __ldg(ay.count + oy);
+        float wx[AA_TAPS];
+        int xs[AA_TAPS];
 #pragma unroll
-        for (int j = 0; j < XT; j++) {
-            const int x = xmin + j;
-            wx[j] = fmaxf(0.0f, 1.0f - fabsf(((float)x + 0.5f - cx) / fsw));
-            xs[j] = min(x, w - 1);
+        for (int j = 0; j < AA_TAPS; j++) {
+            wx[j] = __ldg(ax.w + ox * AA_TAPS + j);
+            xs[j] = min(x0 + j, w - 1);
         }
-        const int nx = xmax - xmin;
-        for (int y = ymin; y < ymax; y++) {
-            const float wy = fmaxf(0.0f, 1.0f - fabsf(((float)y + 0.5f - cy) / fsh));
-            const uint32_t* row = f + min(y, h - 1) * w;
+        for (int yi = 0; yi < ny; yi++) {
+            const float wy = __ldg(ay.w + oy * AA_TAPS + yi);
+            const uint32_t* row = f + min(y0 + yi, h - 1) * w;
 #pragma unroll
-            for (int j = 0; j < XT; j++) {
+            for (int j = 0; j < AA_TAPS; j++) {
                 if (j < nx) {
                     const float wgt = wx[j] * wy;
                     const uint32_t v = __ldg(row + xs[j]);
@@ -90,19 +107,23 @@ __global__ void k_frame_to_input(const uint8_t* __restrict__ frames, long long f
                 }
             }
         }
-    } else {
-        for (int y = ymin; y < ymax; y++) {
-            const float wy = fmaxf(0.0f, 1.0f - fabsf(((float)y + 0.5f - cy) / fsh));
-            const uint32_t* row = f + (long long)min(y, h - 1) * w;
-            for (int x = xmin; x < xmax; x++) {
-                const float wx = fmaxf(0.0f, 1.0f - fabsf(((float)x + 0.5f - cx) / fsw));
-                const float wgt = wx * wy;
-                const uint32_t v = __ldg(row + min(x, w - 1));
-                ab = ab + lut[(v >> 16) & 255] * wgt;
-                ag = ag + lut[(v >> 8) & 255] * wgt;
-                ar = ar + lut[v & 255] * wgt;
-                norm = norm + wgt;
-            }
+        st4(o, ab / norm, ag / norm, ar / norm);
+        return;
+    }
+    float cy, fsh, cx, fsw;
+    const int ymin = aa_span(hp, oh, oy, cy, fsh), ymax = min(hp, (int)floorf(cy + fsh + 0.5f));
+    const int xmin = aa_span(wp, ow, ox, cx, fsw), xmax = min(wp, (int)floorf(cx + fsw + 0.5f));
+    for (int y = ymin; y < ymax; y++) {
+        const float wy = fmaxf(0.0f, 1.0f - fabsf(((float)y + 0.5f - cy) / fsh));
+        const uint32_t* row = f + (long long)min(y, h - 1) * w;
+        for (int x = xmin; x < xmax; x++) {
+            const float wx = fmaxf(0.0f, 1.0f - fabsf(((float)x + 0.5f - cx) / fsw));
+            const float wgt = wx * wy;
+            const uint32_t v = __ldg(row + min(x, w - 1));
+            ab = ab + lut[(v >> 16) & 255] * wgt;
+            ag = ag + lut[(v >> 8) & 255] * wgt;
+            ar = ar + lut[v & 255] * wgt;
+            norm = norm + wgt;
         }
     }
     st4(o, ab / norm, ag / norm, ar / norm);
@@ -110,7 +131,8 @@ __global__ void k_frame_to_input(const uint8_t* __restrict__ frames, long long f
 
 // interp.wgsl aa (x0.25) into a 16 x 16 tile of aq in shared memory, then avgpool.wgsl twice
 __global__ void k_input_pyramid(const __half* __restrict__ A, long long a_bs, int ih, int iw, __half* aq, long long aq_bs,
-                                int qh, int qw, __half* i8, long long i8_bs, __half* i16, long long i16_bs) {
+                                int qh, int qw, __half* i8, long long i8_bs, __half* i16, long long i16_bs, AaAxis ax,
+                                AaAxis ay) {
     pdl_wait();
     pdl_trigger();
     __shared__ float tq[16][16][3];
@@ -119,27 +141,22 @@ __global__ void k_input_pyramid(const __half* __restrict__ A, long long a_bs, in
     const int qx = blockIdx.x * 16 + lx, qy = blockIdx.y * 16 + ly;
     const __half* a = A + (long long)n * a_bs;
     if (qx < qw && qy < qh) {
-        const float sh = (float)ih / (float)qh, sw = (float)iw / (float)qw;
-        const float fsh = fmaxf(sh, 1.0f), fsw = fmaxf(sw, 1.0f);
-        const float cy = ((float)qy + 0.5f) * sh, cx = ((float)qx + 0.5f) * sw;
-        const int ymin = max(0, (int)floorf(cy - fsh + 0.5f)), ymax = min(ih, (int)floorf(cy + fsh + 0.5f));
-        const int xmin = max(0, (int)floorf(cx - fsw + 0.5f)), xmax = min(iw, (int)floorf(cx + fsw + 0.5f));
         float ab = 0.0f, ag = 0.0f, ar = 0.0f, norm = 0.0f;
-        constexpr int XT = 8;  // the column weights of up to XT taps are formed once (downscales up to 4x)
-        if (xmax - xmin <= XT) {
-            float wx[XT];
+        if (ax.w) {
+            const int x0 = __ldg(ax.first + qx), nx = __ldg(ax.count + qx);
+            const int y0 = __ldg(ay.first + qy), ny = __ldg(ay.count + qy);
+            float wx[AA_TAPS];
 #pragma unroll
-            for (int j = 0; j < XT; j++) wx[j] = fmaxf(0.0f, 1.0f - fabsf(((float)(xmin + j) + 0.5f - cx) / fsw));
-            const int nx = xmax - xmin;
-            for (int y = ymin; y < ymax; y++) {
-                const float wy = fmaxf(0.0f, 1.0f - fabsf(((float)y + 0.5f - cy) / fsh));
-                const __half* row = a + ((long long)y * iw + xmin) * 4;
-                float pb[XT], pg[XT], pr[XT];
+            for (int j = 0; j < AA_TAPS; j++) wx[j] = __ldg(ax.w + qx * AA_TAPS + j);
+            for (int yi = 0; yi < ny; yi++) {
+                const float wy = __ldg(ay.w + qy * AA_TAPS + yi);
+                const __half* row = a + ((long long)(y0 + yi) * iw + x0) * 4;
+                float pb[AA_TAPS], pg[AA_TAPS], pr[AA_TAPS];
 #pragma unroll
-                for (int j = 0; j < XT; j++)
+                for (int j = 0; j < AA_TAPS; j++)
                     if (j < nx) ld4(row + j * 4, pb[j], pg[j], pr[j]);
 #pragma unroll
-                for (int j = 0; j < XT; j++) {
+                for (int j = 0; j < AA_TAPS; j++) {
                     if (j < nx) {
                         const float wgt = wx[j] * wy;
                         ab = ab + pb[j] * wgt;
@@ -150,6 +167,9 @@ __global__ void k_input_pyramid(const __half* __restrict__ A, long long a_bs, in
                 }
             }
         } else {
+            float cy, fsh, cx, fsw;
+            const int ymin = aa_span(ih, qh, qy, cy, fsh), ymax = min(ih, (int)floorf(cy + fsh + 0.5f));
+            const int xmin = aa_span(iw, qw, qx, cx, fsw), xmax = min(iw, (int)floorf(cx + fsw + 0.5f));
             for (int y = ymin; y < ymax; y++) {
                 const float wy = fmaxf(0.0f, 1.0f - fabsf(((float)y + 0.5f - cy) / fsh));
                 for (int x = xmin; x < xmax; x++) {
@@ -1240,17 +1260,35 @@ __global__ void k_frame_planes(const uint8_t* f, int w, int h, int hp, int wp, f
 
 // --------------------------------------------------------------------------------------------------- launchers ----
 
-cudaError_t frame_to_input(const uint8_t* frames, long long frame_bs, int w, int h, int hp, int wp, bool internal, int ih,
-                           int iw, Img4 out, int n, cudaStream_t st) {
-    const int oh = internal ? ih : hp, ow = internal ? iw : wp;
-    { const cudaError_t e_ = launch(k_frame_to_input, grid2(ow, oh, n), dim3(16, 16), 0, st, frames, frame_bs, w, h, hp, wp, internal ? 1 : 0, oh, ow,
-                                                               out.p, out.bs); if (e_ != cudaSuccess) return e_; }
+bool aa_axis_fits(int in, int out) {
+    // the same arithmetic as aa_span on the host (IEEE single precision, no contraction)
+    const float s_ = (float)in / (float)out, f = std::max(s_, 1.0f);
+    for (int o = 0; o < out; o++) {
+        const float c = ((float)o + 0.5f) * s_;
+        const int lo = std::max(0, (int)std::floor(c - f + 0.5f)), hi = std::min(in, (int)std::floor(c + f + 0.5f));
+        if (hi - lo > AA_TAPS) return false;
+    }
+    return true;
+}
+
+cudaError_t aa_axis(int in, int out, int* first, int* count, float* w, cudaStream_t st) {
+    k_aa_axis<<<(out + 127) / 128, 128, 0, st>>>(in, out, first, count, w);
     return cudaGetLastError();
 }
 
-cudaError_t input_pyramid(Img4 A, int ih, int iw, Img4 aq, Img4 i8, Img4 i16, int n, cudaStream_t st) {
+cudaError_t frame_to_input(const uint8_t* frames, long long frame_bs, int w, int h, int hp, int wp, bool internal, int ih,
+                           int iw, Img4 out, int n, cudaStream_t st, AaAxis ax, AaAxis ay) {
+    const int oh = internal ? ih : hp, ow = internal ? iw : wp;
+    if (!ax.w || !ay.w) ax = ay = AaAxis{};
+    { const cudaError_t e_ = launch(k_frame_to_input, grid2(ow, oh, n), dim3(16, 16), 0, st, frames, frame_bs, w, h, hp, wp, internal ? 1 : 0, oh, ow,
+                                                               out.p, out.bs, ax, ay); if (e_ != cudaSuccess) return e_; }
+    return cudaGetLastError();
+}
+
+cudaError_t input_pyramid(Img4 A, int ih, int iw, Img4 aq, Img4 i8, Img4 i16, int n, cudaStream_t st, AaAxis ax, AaAxis ay) {
     const int qh = ih / 4, qw = iw / 4;  // floor(h * 0.25) (net/build.rs:204-205)
-    { const cudaError_t e_ = launch(k_input_pyramid, grid2(qw, qh, n), 256, 0, st, A.p, A.bs, ih, iw, aq.p, aq.bs, qh, qw, i8.p, i8.bs, i16.p, i16.bs); if (e_ != cudaSuccess) return e_; }
+    if (!ax.w || !ay.w) ax = ay = AaAxis{};
+    { const cudaError_t e_ = launch(k_input_pyramid, grid2(qw, qh, n), 256, 0, st, A.p, A.bs, ih, iw, aq.p, aq.bs, qh, qw, i8.p, i8.bs, i16.p, i16.bs, ax, ay); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 

@@ -13,13 +13,28 @@ struct Img4 {  // an NHWC cs = 4 f16 image
     long long bs;
 };
 
+// interp.wgsl:29-43 antialias weights along one axis (in -> out), per output index: the first input index, the tap
+// count and AA_TAPS weights (zero past the count). Formed once per session by aa_axis(), with the arithmetic the
+// per-tap kernels use, so a kernel reading them sums the same products in the same order.
+constexpr int AA_TAPS = 8;
+struct AaAxis {
+    const int* first;
+    const int* count;
+    const float* w;  // [out][AA_TAPS]
+};
+// true when every output index of the axis has at most AA_TAPS taps (the tables exist only then)
+bool aa_axis_fits(int in, int out);
+cudaError_t aa_axis(int in, int out, int* first, int* count, float* w, cudaStream_t st);
+
 // rgba8 frame -> network input A: internal mode = antialias triangle downscale of the replicate-padded frame
 // (tex_in.wgsl + interp.wgsl aa); otherwise the padded frame itself as f16. frames: [n] x (w x h x 4 bytes),
-// frame_bs bytes apart.
+// frame_bs bytes apart. ax / ay: the downscale's axis tables (hp -> ih, wp -> iw), or null pointers (weights per tap).
 cudaError_t frame_to_input(const uint8_t* frames, long long frame_bs, int w, int h, int hp, int wp, bool internal,
-                           int ih, int iw, Img4 out, int n, cudaStream_t st);
-// A -> aq (antialias x0.25), i8 = avgpool2(aq), i16 = avgpool2(i8) (interp.wgsl aa + avgpool.wgsl)
-cudaError_t input_pyramid(Img4 A, int ih, int iw, Img4 aq, Img4 i8, Img4 i16, int n, cudaStream_t st);
+                           int ih, int iw, Img4 out, int n, cudaStream_t st, AaAxis ax = {}, AaAxis ay = {});
+// A -> aq (antialias x0.25), i8 = avgpool2(aq), i16 = avgpool2(i8) (interp.wgsl aa + avgpool.wgsl); ax / ay: the
+// x0.25 axis tables (iw -> qw, ih -> qh), or null pointers
+cudaError_t input_pyramid(Img4 A, int ih, int iw, Img4 aq, Img4 i8, Img4 i16, int n, cudaStream_t st, AaAxis ax = {},
+                          AaAxis ay = {});
 
 // keep_static_age.wgsl:59-77 in two passes: `changed` = per padded pixel max |A - B| >= thr, then the state machine
 struct StaticArgs {
