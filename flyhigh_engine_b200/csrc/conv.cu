@@ -520,6 +520,10 @@ extern "C" int fhk_conv_pack_weights(const uint16_t* w, int cin, int cout, const
     return 0;
 }
 
+namespace fhk {
+long long umma_wait_timeouts(int reset);  // conv_umma.cu
+}
+
 extern "C" long long fhk_conv_wait_timeouts(int reset) {
     unsigned long long v = 0;
     if (cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof v) != cudaSuccess) return -1;
@@ -527,7 +531,8 @@ extern "C" long long fhk_conv_wait_timeouts(int reset) {
         const unsigned long long z = 0;
         if (cudaMemcpyToSymbol(g_wait_timeouts, &z, sizeof z) != cudaSuccess) return -1;
     }
-    return (long long)v;
+    const long long u = fhk::umma_wait_timeouts(reset);
+    return u < 0 ? -1 : (long long)v + u;
 }
 
 extern "C" size_t fhk_conv_packed_elems(int cout, int cp) { return (size_t)(9 * cp / 16) * ((cout + 7) / 8) * 32 * 4; }

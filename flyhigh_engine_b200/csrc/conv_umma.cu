@@ -1,0 +1,406 @@
+// 3x3 convolution (pad 1, stride 1) on the 5th-generation tensor cores: tcgen05.mma with the f32 accumulator in tensor
+// memory. Same contract and fused epilogue as conv3x3_mma in conv.cu (conv_fused.wgsl:20-75 + conv_tiled.wgsl:57-61):
+// acc = sum_k A[m][k] B[k][n], then bias, PReLU, f16, optional residual (f16 round, add, f16 round) and affine_out.
+//
+// Design:
+// - A CTA computes an output tile of 8 columns x 16 rows = M 128 pixels for all (padded) output channels N.
+// - The halo tile (18 x 10 pixels) is gathered into shared memory as one plane per 8 input channels, 16 bytes per
+//   pixel. With that layout a tap's A operand (128 pixels x 16 channels, K-major, no swizzle) is a plain descriptor
+//   over the tile: core-matrix rows are the 8 pixels of one output row (consecutive 16-byte halo pixels), the 16 row
+//   groups are IW * 16 bytes apart (SBO), the two 8-channel halves one plane apart (LBO). The tap shift is the start
+//   address. No im2col copy.
+// - The weights are pre-packed (fhk_conv_pack_weights_umma) in the K-major core-matrix order of the B operand,
+//   [kstep][N / 8][2][8 rows][8 channels], and staged whole by one bulk copy (TMA, no multicast) on an mbarrier.
+// - One thread issues the 9 * cp / 16 MMAs (M 128, N, K 16) into the tensor-memory accumulator and commits them to an
+//   mbarrier; the 4 warps then read their 32 accumulator lanes (one pixel per thread, N columns) with tcgen05.ld and
+//   run the epilogue, storing each pixel's channels contiguously.
+// - Every wait is bounded (FhConvParams::wait_cycles); a timeout is counted (fhk_conv_wait_timeouts), no further MMA
+//   is issued, and the tensor memory is freed only after a bounded pause for work still in flight.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "fh_device.cuh"
+#include "fh_kernels.h"
+#include "launch.h"
+
+namespace {
+
+__device__ unsigned long long g_umma_wait_timeouts;
+
+constexpr int UT_W = 8, UT_H = 16;                    // output tile: M = 128 pixels
+constexpr int UIH = UT_H + 2, UIW = UT_W + 2;         // halo tile at stride 1
+constexpr int UPLANE = (UIH * UIW + 1) * 16;          // bytes per 8-channel plane; the extra pixel staggers the banks
+
+__host__ __device__ inline int npad16(int cout) { return (cout + 15) / 16 * 16; }
+__host__ __device__ inline int tmem_cols(int np) {
+    int c = 32;
+    while (c < np) c <<= 1;
+    return c;
+}
+// The weight slice of a CTA (NG output channels) lands in up to WCHUNKS pieces of k-steps, each on its own mbarrier,
+// so the MMAs of the first piece start while the rest is in flight.
+constexpr int WCHUNKS = 4;
+// shared-memory layout: halo planes | weights (NG channels) | bias, slopes | WCHUNKS + 1 mbarriers | TMEM base, flag
+__host__ __device__ inline int umma_wofs(int cp) { return (cp / 8) * UPLANE; }
+__host__ __device__ inline int umma_wbytes(int cp, int ngw) { return 9 * (cp / 16) * ngw * 32; }
+__host__ __device__ inline int umma_bofs(int cp, int ngw) { return umma_wofs(cp) + umma_wbytes(cp, ngw); }
+__host__ __device__ inline int umma_barofs(int cp, int ngw) { return umma_bofs(cp, ngw) + ngw * 8; }
+__host__ __device__ inline int umma_smem(int cp, int ngw) { return umma_barofs(cp, ngw) + 8 * (WCHUNKS + 1) + 16; }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, long long cycles) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > cycles) {
+            atomicAdd(&g_umma_wait_timeouts, 1ull);
+            return false;
+        }
+    }
+    return true;
+}
+
+// ---- tcgen05 ----
+__device__ __forceinline__ void tmem_alloc(uint32_t slot_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(slot_smem), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+// a shared-memory matrix descriptor: no swizzle, K-major core matrices (8 rows x 16 bytes), LBO between the two
+// 8-element K halves, SBO between 8-row groups, descriptor version 1
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
+}
+// D[tmem] (+)= A[smem] x B[smem], kind::f16 (f16 inputs, f32 accumulate), M 128, N from idesc, K 16
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    const uint32_t z = 0;
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+
+// np: the padded output channels; ngw: the channels of one CTA (np / ngw groups along blockIdx.z, n-major)
+__global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int np, int ngw) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int cslices = p.cp / 16, nchunk = p.cp / 8, nsteps = 9 * cslices;
+    const int ngroups = np / ngw;
+    const int n = blockIdx.z / ngroups, grp = blockIdx.z - n * ngroups, cbase = grp * ngw;
+    const int ox0 = blockIdx.x * UT_W, oy0 = blockIdx.y * UT_H;
+    const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(sm);
+    const int wofs = umma_wofs(p.cp), bofs = umma_bofs(p.cp, ngw);
+    const int barofs = umma_barofs(p.cp, ngw);
+    float* sbias = reinterpret_cast<float*>(sm + bofs);
+    float* sslope = sbias + ngw;
+    const uint32_t wbar0 = s0 + barofs, mbar = s0 + barofs + 8 * WCHUNKS;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + barofs + 8 * (WCHUNKS + 1));
+    volatile int& failed = *reinterpret_cast<int*>(sm + barofs + 8 * (WCHUNKS + 1) + 4);
+    const long long wait_cycles = p.wait_cycles > 0 ? p.wait_cycles : 2000000000ll;
+    const uint32_t ncols = (uint32_t)tmem_cols(ngw);
+    const bool prelu = p.slope != nullptr;
+    const int kc = (nsteps + WCHUNKS - 1) / WCHUNKS;  // k-steps per weight piece
+
+    // the weights, bias and slopes are written only when the session is planned: staged before the wait for the
+    // preceding kernel, which covers every other access
+    for (int i = tid; i < ngw; i += 128) {
+        const int c = cbase + i;
+        sbias[i] = c < p.cout ? p.bias[c] : 0.0f;
+        sslope[i] = (prelu && c < p.cout) ? p.slope[c] : 1.0f;
+    }
+    if (tid == 0) {
+        for (int q = 0; q <= WCHUNKS; q++) mbar_init(wbar0 + 8 * q, 1);
+        mbar_init_fence();
+        failed = 0;
+        // piece q: k-steps [q kc, min((q + 1) kc, nsteps)); the packed rows are [kstep][np / 8 groups][2][64 halves],
+        // so a CTA's NG channels are one contiguous run per k-step (the whole k-step when ngw == np)
+        const char* wsrc = reinterpret_cast<const char*>(p.wpack) + (size_t)cbase * 32;
+        for (int q = 0; q < WCHUNKS; q++) {
+            const int k0 = q * kc, k1 = min(k0 + kc, nsteps);
+            if (k0 >= k1) break;
+            const uint32_t bar = wbar0 + 8 * q;
+            mbar_expect_tx(bar, (uint32_t)((k1 - k0) * ngw * 32 + (q == 0 ? p.test_extra_tx : 0)));
+            if (ngw == np)
+                bulk_g2s(s0 + wofs + k0 * ngw * 32, wsrc + (size_t)k0 * np * 32, (uint32_t)((k1 - k0) * np * 32), bar);
+            else
+                for (int k = k0; k < k1; k++)
+                    bulk_g2s(s0 + wofs + k * ngw * 32, wsrc + (size_t)k * np * 32, (uint32_t)(ngw * 32), bar);
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (warp == 0) {
+        tmem_alloc((uint32_t)__cvta_generic_to_shared(tslot), ncols);
+        tmem_relinquish();
+    }
+
+    // ---- halo tile: planes [chunk][UIH x UIW] of 16-byte pixels, zero outside the image and beyond every source.
+    //      LP lanes (a power of two >= the chunk count) per pixel, each owning one chunk ----
+    {
+        int lp = 1;
+        while (lp < nchunk) lp <<= 1;
+        const int ch = tid & (lp - 1), pstep = 128 / lp;
+        const int c8 = ch * 8;
+        int si = -1, rel = 0;
+        if (ch < nchunk)
+            for (int s_ = 0; s_ < p.nsrc; s_++) {
+                const int r_ = c8 - p.src[s_].slot;
+                if (r_ >= 0 && r_ < ((p.src[s_].nc + 7) & ~7)) {
+                    si = s_;
+                    rel = r_;
+                    break;
+                }
+            }
+        const __half* base = nullptr;
+        int cs = 0, valid = 0;
+        float scale = 1.0f;
+        bool narrow = false;
+        if (si >= 0) {
+            const FhConvSrc& src = p.src[si];
+            base = src.p + (long long)n * src.bs + rel;
+            cs = src.cs;
+            valid = src.nc - rel;
+            scale = src.scale;
+            narrow = src.cs < rel + 8;
+        }
+        const bool plain = valid >= 8 && scale == 1.0f && !narrow;
+        constexpr int npix = UIH * UIW;
+        if (ch < nchunk) {
+            uint8_t* plane = sm + ch * UPLANE;
+            for (int pix0 = tid / lp; pix0 < npix; pix0 += 4 * pstep) {
+                uint4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int pix = pix0 + u * pstep;
+                    const int hy = pix / UIW, hx = pix - hy * UIW;
+                    const int iy = oy0 - 1 + hy, ix = ox0 - 1 + hx;
+                    v[u] = make_uint4(0, 0, 0, 0);
+                    if (pix < npix && si >= 0 && iy >= 0 && iy < p.h && ix >= 0 && ix < p.w) {
+                        const __half* g = base + ((long long)iy * p.w + ix) * cs;
+                        if (!narrow) {
+                            v[u] = __ldg(reinterpret_cast<const uint4*>(g));
+                        } else {  // a 4-channel pixel (3-channel image): 8 bytes
+                            const uint2 w2 = __ldg(reinterpret_cast<const uint2*>(g));
+                            v[u] = make_uint4(w2.x, w2.y, 0, 0);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int pix = pix0 + u * pstep;
+                    if (pix >= npix) break;
+                    if (!plain) {
+                        __half* hv = reinterpret_cast<__half*>(&v[u]);
+#pragma unroll
+                        for (int k = 0; k < 8; k++) {
+                            if (k >= valid) hv[k] = __float2half_rn(0.0f);
+                            else if (scale != 1.0f) hv[k] = __float2half_rn(__half2float(hv[k]) * scale);
+                        }
+                    }
+                    *reinterpret_cast<uint4*>(plane + pix * 16) = v[u];
+                }
+            }
+        }
+    }
+    // the tile was written through the generic proxy; the tensor core reads it through the async proxy
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+
+    // ---- the MMAs: one thread, each weight piece as soon as it has landed ----
+    if (tid == 0) {
+        const uint32_t idesc = (1u << 4) | ((uint32_t)(ngw >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+        for (int q = 0; q < WCHUNKS && !failed; q++) {
+            const int k0 = q * kc, k1 = min(k0 + kc, nsteps);
+            if (k0 >= k1) break;
+            if (!mbar_wait_bounded(wbar0 + 8 * q, 0, wait_cycles)) {
+                failed = 1;
+                break;
+            }
+            for (int ks = k0; ks < k1; ks++) {
+                const int tap = ks / cslices, sl = ks - tap * cslices;
+                const int ky = tap / 3, kx = tap - ky * 3;
+                const uint64_t ad = smem_desc(s0 + (uint32_t)(2 * sl * UPLANE + (ky * UIW + kx) * 16), UPLANE, UIW * 16);
+                const uint64_t bd = smem_desc(s0 + (uint32_t)(wofs + ks * ngw * 32), 128, 256);
+                umma_f16(tbase, ad, bd, idesc, ks > 0 ? 1u : 0u);
+            }
+        }
+        umma_commit(mbar);  // arrives once every MMA above has completed (at once when none was issued)
+    }
+    __syncwarp();
+    const bool mma_done = mbar_wait_bounded(mbar, 0, wait_cycles) && !failed;
+    tc_fence_after();
+
+    // ---- epilogue: warp w holds accumulator lanes 32 w .. 32 w + 31 = tile pixels m (row m / 8, column m % 8) ----
+    const int m = warp * 32 + lane;
+    const int oy = oy0 + (m >> 3), ox = ox0 + (m & 7);
+    const bool inside = oy < p.ho && ox < p.wo;
+    __half* __restrict__ out = p.out + (long long)n * p.out_bs + ((long long)oy * p.wo + ox) * p.out_cs;
+    const __half* __restrict__ res =
+        p.res ? p.res + (long long)n * p.res_bs + ((long long)oy * p.wo + ox) * p.res_cs : nullptr;
+    for (int c0 = 0; c0 < ngw; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(tbase + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+        const int cg = cbase + c0;  // output channel of column c0
+        if (!inside || !mma_done) continue;
+        __half hv[16];
+        float rv[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) rv[j] = (p.res && cg + j < p.cout) ? __half2float(res[cg + j]) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            float v = __uint_as_float(r[j]) + sbias[c0 + j];
+            if (prelu) v = v > 0.0f ? v : sslope[c0 + j] * v;
+            __half h = __float2half_rn(v);
+            if (p.res) h = __float2half_rn(__half2float(h) + rv[j]);
+            if (p.epi == 1) h = __float2half_rn(2.0f / (1.0f + expf(-__half2float(h))) - 1.0f);
+            hv[j] = h;
+        }
+        if (cg + 16 <= p.cout && (p.out_cs & 7) == 0 && ((uintptr_t)(out + cg) & 15) == 0) {
+            reinterpret_cast<uint4*>(out + cg)[0] = reinterpret_cast<const uint4*>(hv)[0];
+            reinterpret_cast<uint4*>(out + cg)[1] = reinterpret_cast<const uint4*>(hv)[1];
+        } else {
+            for (int j = 0; j < 16 && cg + j < p.cout; j++) out[cg + j] = hv[j];
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        if (!mma_done) {  // MMAs may still be in flight: give them the bound before the columns are released
+            const long long t0 = clock64();
+            while (clock64() - t0 < wait_cycles) {
+            }
+        }
+        tmem_dealloc(tbase, ncols);
+    }
+}
+
+}  // namespace
+
+// the timeouts of this kernel's waits (fhk_conv_wait_timeouts adds them to conv3x3_mma's)
+namespace fhk {
+long long umma_wait_timeouts(int reset) {
+    unsigned long long v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_umma_wait_timeouts, sizeof v) != cudaSuccess) return -1;
+    if (reset) {
+        const unsigned long long z = 0;
+        if (cudaMemcpyToSymbol(g_umma_wait_timeouts, &z, sizeof z) != cudaSuccess) return -1;
+    }
+    return (long long)v;
+}
+}  // namespace fhk
+
+// 1 when the tcgen05 kernel takes this layer: stride 1, N <= 256, and its halo tile plus the whole weight slice fit
+// in shared memory
+extern "C" int fhk_conv_umma_fits(int cp, int cout, int stride) {
+    if (stride != 1 || cp <= 0 || cp % 16 || cout < 1 || npad16(cout) > 256) return 0;
+    return umma_smem(cp, npad16(cout)) <= 227 * 1024 ? 1 : 0;
+}
+
+extern "C" size_t fhk_conv_packed_elems_umma(int cout, int cp) { return (size_t)9 * (cp / 16) * npad16(cout) * 16; }
+
+// torch-layout weights W[cout][cin][3][3] (f16 bits) into the tcgen05 B-operand order: per k-step (tap, 16-channel
+// slice) N / 8 groups of two core matrices (channels 0-7, 8-15 of the slice), each 8 output channels x 8 input
+// channels; k = tap * cp + packed channel, map[pc] = model input channel of packed channel pc or -1 (weight 0),
+// output channels beyond cout are 0
+extern "C" int fhk_conv_pack_weights_umma(const uint16_t* w, int cin, int cout, const int* map, int cp, uint16_t* out) {
+    if (cp % 16 || cout < 1 || npad16(cout) > 256) return -1;
+    const int np = npad16(cout), cs = cp / 16, nsteps = 9 * cs;
+    for (int ks = 0; ks < nsteps; ks++) {
+        const int tap = ks / cs, sl = ks - tap * cs;
+        for (int g = 0; g < np / 8; g++)
+            for (int hf = 0; hf < 2; hf++)
+                for (int r = 0; r < 8; r++)
+                    for (int e = 0; e < 8; e++) {
+                        const int nn = g * 8 + r, pc = sl * 16 + hf * 8 + e, ci = map[pc];
+                        uint16_t v = 0;
+                        if (ci >= 0 && nn < cout) v = w[((size_t)nn * cin + ci) * 9 + tap];
+                        out[(((size_t)ks * (np / 8) + g) * 2 + hf) * 64 + r * 8 + e] = v;
+                    }
+    }
+    (void)cin;
+    return 0;
+}
+
+extern "C" int fhk_conv3x3_umma(const FhConvParams* pin, void* stream) {
+    if (!pin || pin->nsrc < 1 || pin->nsrc > FH_CONV_MAX_SRC || pin->n < 1) return (int)cudaErrorInvalidValue;
+    if (!fhk_conv_umma_fits(pin->cp, pin->cout, 1)) return (int)cudaErrorInvalidValue;
+    FhConvParams p = *pin;
+    if (p.out_cs % 2 || (p.res && p.res_cs % 2) || (uintptr_t)p.out % 4 || (p.res && (uintptr_t)p.res % 4) ||
+        (uintptr_t)p.wpack % 16)
+        return (int)cudaErrorMisalignedAddress;
+    if (p.test_extra_tx < 0 || p.test_extra_tx % 16 || p.test_extra_tx > 65536 || p.wait_cycles < 0)
+        return (int)cudaErrorInvalidValue;
+    for (int s = 0; s < p.nsrc; s++) {
+        const FhConvSrc& src = p.src[s];
+        if (src.slot % 8 || (src.cs % 8 && src.cs != 4) || ((uintptr_t)src.p % (src.cs == 4 ? 8 : 16)))
+            return (int)cudaErrorMisalignedAddress;
+        if (src.slot + ((src.nc + 7) & ~7) > p.cp) return (int)cudaErrorInvalidValue;
+    }
+    if (p.ho != p.h || p.wo != p.w) return (int)cudaErrorInvalidValue;  // stride 1
+    const int np = npad16(p.cout);
+    // output channels split over CTAs while the grid is small (each output's sum is unchanged): the widest group (a
+    // multiple of 16 dividing the padded channels) that gives 148 CTAs, else the narrowest
+    const long long tiles = (long long)((p.wo + UT_W - 1) / UT_W) * ((p.ho + UT_H - 1) / UT_H) * p.n;
+    int ngw = np;
+    for (int g = np; g >= 16; g -= 16) {
+        if (np % g) continue;
+        ngw = g;
+        if (tiles * (np / g) >= 148) break;
+    }
+    const size_t smem = (size_t)umma_smem(p.cp, ngw);
+    static size_t configured = 48 * 1024;
+    if (smem > configured) {
+        cudaError_t e = cudaFuncSetAttribute(conv3x3_umma, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return (int)e;
+        configured = 227 * 1024;
+    }
+    p.wsmem = 1;
+    const dim3 grid((p.wo + UT_W - 1) / UT_W, (p.ho + UT_H - 1) / UT_H, p.n * (np / ngw));
+    return (int)fhk::launch(conv3x3_umma, grid, dim3(128), smem, (cudaStream_t)stream, p, np, ngw);
+}

@@ -264,6 +264,7 @@ struct ConvLayer {
     std::string name;
     int cin = 0, cout = 0, stride = 1, cp = 0;
     bool act = true;
+    bool umma = false;  // the tcgen05 kernel (conv_umma.cu) and its weight order, else conv3x3_mma
     uint16_t* wpack = nullptr;
     float* bias = nullptr;
     float* slope = nullptr;
@@ -361,6 +362,10 @@ struct FhSession {
     // launch priorities inside the stage graphs: the critical chain high, the side branches low (FH_PRIO=0: none)
     bool prio_on = true;
     int prio_hi = 0, prio_lo = 0;
+    // Stride-1 convs of batched sessions run on the tcgen05 kernel where they fit; one-interval sessions (small grids)
+    // keep the split-K conv3x3_mma kernel. Fixed per session, so an interval's result does not depend on how many
+    // intervals its launch carries. FH_UMMA=0 / 1 forces either.
+    bool umma_on = false;
     std::vector<void*> allocs;
     size_t bytes = 0;
 
@@ -523,8 +528,11 @@ struct FhSession {
         L.cp = up16(slot);
         map.resize(L.cp, -1);
         auto wb = model->bits(wn);
-        std::vector<uint16_t> packed(fhk_conv_packed_elems(L.cout, L.cp));
-        if (fhk_conv_pack_weights(wb.data(), L.cin, L.cout, map.data(), L.cp, packed.data()) != 0) fail("%s: pack", name.c_str());
+        L.umma = umma_on && fhk_conv_umma_fits(L.cp, L.cout, stride);
+        std::vector<uint16_t> packed(L.umma ? fhk_conv_packed_elems_umma(L.cout, L.cp) : fhk_conv_packed_elems(L.cout, L.cp));
+        const int pk = L.umma ? fhk_conv_pack_weights_umma(wb.data(), L.cin, L.cout, map.data(), L.cp, packed.data())
+                              : fhk_conv_pack_weights(wb.data(), L.cin, L.cout, map.data(), L.cp, packed.data());
+        if (pk != 0) fail("%s: pack", name.c_str());
         L.wpack = alloc_n<uint16_t>(packed.size());
         CK(cudaMemcpyAsync(L.wpack, packed.data(), packed.size() * 2, cudaMemcpyHostToDevice, st));
         auto b = model->f32(bn);
@@ -580,7 +588,7 @@ struct FhSession {
         p.n = n;
         p.wm = 0;  // split chosen by size
         p.ngroups = 0;
-        int e = fhk_conv3x3(&p, L.stride, st);
+        int e = L.umma ? fhk_conv3x3_umma(&p, st) : fhk_conv3x3(&p, L.stride, st);
         if (e) fail("conv %s: %s", key.c_str(), cudaGetErrorString((cudaError_t)e));
         mark("conv " + L.name);
     }
@@ -1273,6 +1281,7 @@ void derive(const FhModel* m, const FhSessionOptions& o, FhSession* s) {
     s->decisive = env_is("FH_BLEND", "decisive");
     s->pdl_on = !env_is("FH_PDL", "0");
     s->prio_on = !env_is("FH_PRIO", "0");
+    s->umma_on = env_is("FH_UMMA", "1");
     const bool keep_static = o.keep_static != 0;
     s->protects = keep_static || o.protection_mask;
     const int frames = keep_static ? std::clamp((int)(o.static_frames ? o.static_frames : 8), 1, 255) : 2;
@@ -1303,6 +1312,7 @@ FhSession* session_new(FhEngine* e, const FhModel* m, const FhSessionOptions& o,
     }
     if (batch > 16) fail("batch: %d intervals per launch (1..16)", batch);
     s->nbat = batch;
+    if (batch > 1 && !env_is("FH_UMMA", "0")) s->umma_on = true;
     s->eng = e;
     CK(cudaSetDevice(e->device));
     CK(cudaDeviceGetStreamPriorityRange(&s->prio_lo, &s->prio_hi));

@@ -68,6 +68,15 @@ int fhk_conv3x3(const FhConvParams* p, int stride, void* stream);
 /* Waits for staged weights that ran out of time (the kernel then computes on whatever landed and goes on) since the
  * last reset, on the current device; reset != 0 zeroes the count. Returns -1 when the count cannot be read. */
 long long fhk_conv_wait_timeouts(int reset);
+/* The same convolution (stride 1) on the 5th-generation tensor cores: tcgen05.mma into a tensor-memory f32
+ * accumulator, a CTA per 8 x 16 output pixels and all output channels, the halo tile gathered into shared memory and
+ * the whole weight slice staged by one bulk copy. Weights in fhk_conv_pack_weights_umma order; p->ho == p->h and
+ * p->wo == p->w; wm / ngroups are ignored. fhk_conv_umma_fits tells whether a layer fits (stride 1, Cout <= 256,
+ * shared memory). The f32 summation order differs from fhk_conv3x3's. */
+int fhk_conv3x3_umma(const FhConvParams* p, void* stream);
+int fhk_conv_umma_fits(int cp, int cout, int stride);
+int fhk_conv_pack_weights_umma(const uint16_t* w, int cin, int cout, const int* map, int cp, uint16_t* out);
+size_t fhk_conv_packed_elems_umma(int cout, int cp);
 /* Replaces buildb / buildb_tap (ops/conv/kernels.rs:66-78, :194-207): torch [cout][cin][3][3] f16 bits -> the
  * kernel's B-fragment order; map[pc] = model input channel of packed channel pc, or -1 (weight 0). */
 int fhk_conv_pack_weights(const uint16_t* w, int cin, int cout, const int* map, int cp, uint16_t* out);
