@@ -56,6 +56,12 @@ __host__ __device__ inline int halo_w(int s) { return (TW - 1) * s + 3; }
 // the halo tile's bytes, rounded to 16
 __host__ __device__ inline int tile_bytes(int wm, int s, int cp) { return halo_h(wm, s) * halo_w(s) * (cp + 8) * 2; }
 
+// 16 bytes global -> shared, asynchronously; src_bytes 0 writes zeros (the source is not read)
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
 // ---- bulk copies (TMA, no multicast) completing on an mbarrier ----
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
@@ -209,6 +215,16 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
         const bool plain = valid >= 8 && scale == 1.0f && !narrow;
         const int npix = IH * IW;
         if (ch < nchunk) {
+            if (plain) {
+                // every pixel a 16-byte copy (zero-filled outside the image), all of them in flight at once
+                for (int pix = tid / lp; pix < npix; pix += pstep) {
+                    const int hy = pix / IW, hx = pix - hy * IW;
+                    const int iy = iy0 + hy, ix = ix0 + hx;
+                    const bool ok = iy >= 0 && iy < p.h && ix >= 0 && ix < p.w;
+                    const __half* g = ok ? base + ((long long)iy * p.w + ix) * cs : base;
+                    cp_async16_zfill((uint32_t)__cvta_generic_to_shared(tile) + (uint32_t)(pix * P + c8) * 2, g, ok ? 16u : 0u);
+                }
+            } else
             for (int pix0 = tid / lp; pix0 < npix; pix0 += 4 * pstep) {
                 uint4 v[4];
 #pragma unroll
@@ -244,6 +260,7 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
             }
         }
     }
+    cp_async_wait_all();
     __syncthreads();
     if (p.wsmem == 1 && !mbar_wait_bounded(bar0, 0, wait_cycles)) s_failed = 1;
 

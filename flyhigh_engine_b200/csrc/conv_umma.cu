@@ -83,6 +83,12 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     return true;
 }
 
+// 16 bytes global -> shared, asynchronously; src_bytes 0 writes zeros (the source is not read)
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
 // ---- tcgen05 ----
 __device__ __forceinline__ void tmem_alloc(uint32_t slot_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(slot_smem), "r"(ncols)
@@ -210,6 +216,16 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
         constexpr int npix = UIH * UIW;
         if (ch < nchunk) {
             uint8_t* plane = sm + ch * UPLANE;
+            if (plain) {
+                // every pixel a 16-byte copy (zero-filled outside the image), all of them in flight at once
+                for (int pix = tid / lp; pix < npix; pix += pstep) {
+                    const int hy = pix / UIW, hx = pix - hy * UIW;
+                    const int iy = oy0 - 1 + hy, ix = ox0 - 1 + hx;
+                    const bool ok = iy >= 0 && iy < p.h && ix >= 0 && ix < p.w;
+                    const __half* g = ok ? base + ((long long)iy * p.w + ix) * cs : base;
+                    cp_async16_zfill(s0 + (uint32_t)(ch * UPLANE + pix * 16), g, ok ? 16u : 0u);
+                }
+            } else
             for (int pix0 = tid / lp; pix0 < npix; pix0 += 4 * pstep) {
                 uint4 v[4];
 #pragma unroll
@@ -245,6 +261,7 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
             }
         }
     }
+    cp_async_wait_all();
     // the tile was written through the generic proxy; the tensor core reads it through the async proxy
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     tc_fence_before();

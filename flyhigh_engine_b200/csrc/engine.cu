@@ -381,6 +381,7 @@ struct FhSession {
     // frame-stage scratch, pair and mid buffers
     __half *e1 = nullptr, *e3 = nullptr;
     uint32_t* changed = nullptr;
+    uint32_t* spread = nullptr;  // the static age pass's byte thresholds
     uint8_t* mask = nullptr;
     uchar4* state = nullptr;
     int16_t* age = nullptr;
@@ -668,6 +669,8 @@ struct FhSession {
         e3 = img(h16, w16, C16P, nf);
         if (protects) {
             changed = alloc_n<uint32_t>((size_t)nb * hp * fhk::changed_words(wp));
+            spread = alloc_n<uint32_t>(256);
+            CK(fhk::spread_table(spread, st));
             mask = alloc_n<uint8_t>((size_t)hp * wp);
             state = alloc_n<uchar4>((size_t)hp * wp);
             age = alloc_n<int16_t>((size_t)nb * hp * wp);
@@ -789,7 +792,7 @@ struct FhSession {
                 if (protects) {
                     const long long l = n - 1;
                     CK(fhk::static_age(A.frame + l * A.frame_bs, B.frame + l * B.frame_bs, -A.frame_bs, changed + l * CW,
-                                       -CW, mask, sargs, state, age + l * P, -P, n, st));
+                                       -CW, mask, sargs, state, age + l * P, -P, n, spread, st));
                     mark("static_age");
                     CK(fhk::static_near(age, P, wp, hp, min_age, nearp, n, st));
                     mark("static_near");
@@ -1732,7 +1735,7 @@ int fh_session_advance_static(const FhSession* cs, uint32_t a, uint32_t b) {
         s->wait_upload(A);
         s->wait_upload(B);
         CK(fhk::pair_planes(A.frame, B.frame, 0, s->sargs, s->changed, 0, nullptr, 0, 1, s->st));
-        CK(fhk::static_age(A.frame, B.frame, 0, s->changed, 0, s->mask, s->sargs, s->state, s->age, 0, 1, s->st));
+        CK(fhk::static_age(A.frame, B.frame, 0, s->changed, 0, s->mask, s->sargs, s->state, s->age, 0, 1, s->spread, s->st));
         s->mark_read(A, B);
         return 0;
     });

@@ -311,6 +311,21 @@ FH_DEV uint32_t bit_window(const uint32_t* __restrict__ row, int ww, int W, int 
     return v;
 }
 
+// The spread test per channel, v(q) - v(o) >= 0.03 or v(o) - v(q) >= 0.03 in f32 (v = the byte -> value table), as
+// byte thresholds per o: the first q above o and the last q below o that pass (both differences are monotone in q).
+// Low half: the upper threshold (256: none), high half: the lower one + 1 (0: none).
+__global__ void k_spread_table(uint32_t* out) {
+    __shared__ float lut[256];
+    const int o = threadIdx.x;
+    lut[o] = u8v(o);
+    __syncthreads();
+    int hi = o;
+    while (hi < 256 && !(lut[hi] - lut[o] >= 0.03f)) hi++;
+    int lo = o;
+    while (lo >= 0 && !(lut[o] - lut[lo] >= 0.03f)) lo--;
+    out[o] = (uint32_t)hi | ((uint32_t)(lo + 1) << 16);
+}
+
 // keep_static_age.wgsl:59-77: 9 near + 32 far probes of `changed`, the spread test, the state machine (decide, :28-36),
 // for np consecutive pairs in time order (pair i: frames fa + i * frame_bs, fb + i * frame_bs, its changed plane and its
 // age plane; strides may be negative). A pixel's state is loaded once, advanced pair by pair and stored once: the
@@ -318,13 +333,16 @@ FH_DEV uint32_t bit_window(const uint32_t* __restrict__ row, int ww, int W, int 
 // A warp is one 32-pixel row segment. moved: lane l evaluates probe l (and probe 32 + l) as a 32-bit window of the
 // changed bits for the whole segment, and the warp ORs the windows. spread: max over the clamped 3 x 3 neighbourhood
 // and channels of |a(q) - a(o)|, |b(q) - b(o)|; the byte -> value table is monotone and f32 subtraction is monotone
-// in each operand, so that max is max(v(max_q) - v(o), v(o) - v(min_q)) per channel, exactly.
+// in each operand, so that max is max(v(max_q) - v(o), v(o) - v(min_q)) per channel, exactly; its test against
+// 0.03 is a byte threshold per o (k_spread_table).
 __global__ void __launch_bounds__(256) k_static_age(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb,
                                                     long long frame_bs, const uint32_t* __restrict__ changed,
                                                     long long changed_bs, const uint8_t* __restrict__ mask, StaticArgs s,
-                                                    uchar4* state, int16_t* age, long long age_bs, int np) {
-    __shared__ float lut[256];
-    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
+                                                    uchar4* state, int16_t* age, long long age_bs, int np,
+                                                    const uint32_t* __restrict__ spread) {
+    __shared__ uint32_t spread_tab[256];
+    const int tid = threadIdx.y * blockDim.x + threadIdx.x;
+    for (int i = tid; i < 256; i += blockDim.x * blockDim.y) spread_tab[i] = __ldg(spread + i);
     __syncthreads();
     pdl_wait();
     pdl_trigger();
@@ -402,19 +420,17 @@ __global__ void __launch_bounds__(256) k_static_age(const uint8_t* __restrict__ 
             bmin = __vminu4(bmin, __vminu4(l_bmin, r_bmin));
         }
         if (!active) continue;
-        float m = 0.0f;
+        bool spread = false;
 #pragma unroll
         for (int c = 0; c < 3; c++) {
             const int sh = 16 - 8 * c;  // channel c of the BGR plane = byte 2 - c of the rgba pixel
-            const float va = lut[(a1 >> sh) & 255], vb = lut[(b1 >> sh) & 255];
-            m = fmaxf(m, lut[(amax >> sh) & 255] - va);
-            m = fmaxf(m, va - lut[(amin >> sh) & 255]);
-            m = fmaxf(m, lut[(bmax >> sh) & 255] - vb);
-            m = fmaxf(m, vb - lut[(bmin >> sh) & 255]);
+            const uint32_t ta = spread_tab[(a1 >> sh) & 255], tb = spread_tab[(b1 >> sh) & 255];
+            spread |= ((amax >> sh) & 255) >= (ta & 0xffff) || ((amin >> sh) & 255) < (ta >> 16) ||
+                      ((bmax >> sh) & 255) >= (tb & 0xffff) || ((bmin >> sh) & 255) < (tb >> 16);
         }
         const bool moved = (mv >> lane) & 1u;
         const bool same = ((own_word >> lane) & 1u) == 0;
-        const bool still = same && m >= 0.03f;
+        const bool still = same && spread;
         const int raw = still ? min((int)st.x + 1, 255) : 0;
         const int seen = still ? min((int)st.y + (moved ? 1 : 0), 255) : 0;
         const int run = same ? min((int)st.z + 1, 255) : 0;
@@ -792,29 +808,29 @@ __global__ void k_gm_cost(GmArgs g) {
 // gm_box.wgsl box_h / box_v: radius r, edge replicate, the first c maps. The select reads the boxed maps only at its
 // sample cells (row ys(i), column xs(j)), so the passes whose result feeds nothing else run there only: each output is
 // formed exactly as the full pass forms it (the same taps in the same order, then / (2r + 1)).
-__global__ void k_box_h(const float* src, float* dst, int c, int h, int w, int r, long long bs) {
+__global__ void k_box_h(const float* src, long long src_bs, float* dst, long long dst_bs, int c, int h, int w, int r) {
     pdl_wait();
     pdl_trigger();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
     const int n = blockIdx.z / c, ch = blockIdx.z - n * c;
     if (x >= w || y >= h) return;
-    const long long row = (long long)n * bs + ((long long)ch * h + y) * w;
+    const float* row = src + n * src_bs + ((long long)ch * h + y) * w;
     float acc = 0.0f;
 #pragma unroll 8
-    for (int d = -r; d <= r; d++) acc = acc + src[row + clampi(x + d, 0, w - 1)];
-    dst[row + x] = acc / (float)(2 * r + 1);
+    for (int d = -r; d <= r; d++) acc = acc + row[clampi(x + d, 0, w - 1)];
+    dst[n * dst_bs + ((long long)ch * h + y) * w + x] = acc / (float)(2 * r + 1);
 }
-__global__ void k_box_v(const float* src, float* dst, int c, int h, int w, int r, long long bs) {
+__global__ void k_box_v(const float* src, long long src_bs, float* dst, long long dst_bs, int c, int h, int w, int r) {
     pdl_wait();
     pdl_trigger();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
     const int n = blockIdx.z / c, ch = blockIdx.z - n * c;
     if (x >= w || y >= h) return;
-    const long long plane = (long long)n * bs + (long long)ch * h * w;
+    const float* plane = src + n * src_bs + (long long)ch * h * w;
     float acc = 0.0f;
 #pragma unroll 8
-    for (int d = -r; d <= r; d++) acc = acc + src[plane + (long long)clampi(y + d, 0, h - 1) * w + x];
-    dst[plane + (long long)y * w + x] = acc / (float)(2 * r + 1);
+    for (int d = -r; d <= r; d++) acc = acc + plane[(long long)clampi(y + d, 0, h - 1) * w + x];
+    dst[n * dst_bs + (long long)ch * h * w + (long long)y * w + x] = acc / (float)(2 * r + 1);
 }
 // gm_select.wgsl:12-15: the cost cell that select sample j (of w8) reads, along one axis of hc or wc cells
 FH_DEV int gm_cell(int j, int cells, int n8) { return clampi((int)floorf(((float)j + 0.5f) * (float)cells / (float)n8), 0, cells - 1); }
@@ -1064,20 +1080,31 @@ FH_DEV float3 sample_frame(const uint2* __restrict__ f, int w, int h, float gx, 
         const float tx = gx - (float)px, ty = gy - (float)py;
         const float cx0 = cub2(tx + 1.0f), cx1 = cub1(tx), cx2 = cub1(1.0f - tx), cx3 = cub2(2.0f - tx);
         const float cy[4] = {cub2(ty + 1.0f), cub1(ty), cub1(1.0f - ty), cub2(2.0f - ty)};
-        const int x0 = clampi(px - 1, 0, w - 1), x1 = clampi(px, 0, w - 1), x2 = clampi(px + 1, 0, w - 1),
-                  x3 = clampi(px + 2, 0, w - 1);
-        float3 acc = make_float3(0.0f, 0.0f, 0.0f);
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const uint2* row = f + clampi(py - 1 + j, 0, h - 1) * w;
-            const float3 p0 = px3(row + x0), p1 = px3(row + x1), p2 = px3(row + x2), p3 = px3(row + x3);
+        // one row of taps: continuous sums, fused
+        auto row_sum = [&](const uint2* r0p, const uint2* r1p, const uint2* r2p, const uint2* r3p, float wy, float3& acc) {
+            const float3 p0 = px3(r0p), p1 = px3(r1p), p2 = px3(r2p), p3 = px3(r3p);
             float3 rw;
             rw.x = fmaf(p3.x, cx3, fmaf(p2.x, cx2, fmaf(p1.x, cx1, p0.x * cx0)));
             rw.y = fmaf(p3.y, cx3, fmaf(p2.y, cx2, fmaf(p1.y, cx1, p0.y * cx0)));
             rw.z = fmaf(p3.z, cx3, fmaf(p2.z, cx2, fmaf(p1.z, cx1, p0.z * cx0)));
-            acc.x = fmaf(rw.x, cy[j], acc.x);
-            acc.y = fmaf(rw.y, cy[j], acc.y);
-            acc.z = fmaf(rw.z, cy[j], acc.z);
+            acc.x = fmaf(rw.x, wy, acc.x);
+            acc.y = fmaf(rw.y, wy, acc.y);
+            acc.z = fmaf(rw.z, wy, acc.z);
+        };
+        float3 acc = make_float3(0.0f, 0.0f, 0.0f);
+        if (px >= 1 && px + 2 <= w - 1 && py >= 1 && py + 2 <= h - 1) {
+            // away from the border no tap is clamped: one base, the taps at fixed offsets
+            const uint2* b0 = f + (py - 1) * w + (px - 1);
+#pragma unroll
+            for (int j = 0; j < 4; j++) row_sum(b0 + j * w, b0 + j * w + 1, b0 + j * w + 2, b0 + j * w + 3, cy[j], acc);
+        } else {
+            const int x0 = clampi(px - 1, 0, w - 1), x1 = clampi(px, 0, w - 1), x2 = clampi(px + 1, 0, w - 1),
+                      x3 = clampi(px + 2, 0, w - 1);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const uint2* row = f + clampi(py - 1 + j, 0, h - 1) * w;
+                row_sum(row + x0, row + x1, row + x2, row + x3, cy[j], acc);
+            }
         }
         return acc;
     }
@@ -1304,11 +1331,16 @@ cudaError_t static_near(const int16_t* age, long long bs, int wp, int hp, float 
     return cudaGetLastError();
 }
 
+cudaError_t spread_table(uint32_t* out, cudaStream_t st) {
+    k_spread_table<<<1, 256, 0, st>>>(out);
+    return cudaGetLastError();
+}
+
 cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, long long frame_bs, const uint32_t* changed,
                        long long changed_bs, const uint8_t* mask, const StaticArgs& s, uchar4* state, int16_t* age,
-                       long long age_bs, int np, cudaStream_t st) {
-    if (np < 1) return cudaErrorInvalidValue;
-    { const cudaError_t e_ = launch(k_static_age, grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st, fa, fb, frame_bs, changed, changed_bs, mask, s, state, age, age_bs, np); if (e_ != cudaSuccess) return e_; }
+                       long long age_bs, int np, const uint32_t* spread, cudaStream_t st) {
+    if (np < 1 || !spread) return cudaErrorInvalidValue;
+    { const cudaError_t e_ = launch(k_static_age, grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st, fa, fb, frame_bs, changed, changed_bs, mask, s, state, age, age_bs, np, spread); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
@@ -1345,13 +1377,8 @@ cudaError_t gmhs_maps(const GmArgs& g, int n, cudaStream_t st) {
     if (g.w8 > g.wc) return cudaErrorInvalidValue;  // the column planes live in tmp's [5][hc][wc] per entry
     { const cudaError_t e_ = launch(k_gm_cost, grid2(g.wc, g.hc, n, 32, 8), dim3(32, 8), 0, st, g); if (e_ != cudaSuccess) return e_; }
     const long long bs5 = 5LL * g.hc * g.wc, bs6 = 6LL * g.hc * g.wc;
-    // maps and tmp have different batch strides: run the full passes per batch entry when n > 1
-    for (int i = 0; i < n; i++) {
-        float* maps = g.maps + i * bs6;
-        float* tmp = g.tmp + i * bs5;
-        { const cudaError_t e_ = launch(k_box_h, grid2(g.wc, g.hc, 3, 32, 8), dim3(32, 8), 0, st, maps, tmp, 3, g.hc, g.wc, g.r_blk, 0); if (e_ != cudaSuccess) return e_; }
-        { const cudaError_t e_ = launch(k_box_v, grid2(g.wc, g.hc, 3, 32, 8), dim3(32, 8), 0, st, tmp, maps, 3, g.hc, g.wc, g.r_blk, 0); if (e_ != cudaSuccess) return e_; }
-    }
+    { const cudaError_t e_ = launch(k_box_h, grid2(g.wc, g.hc, 3 * n, 32, 8), dim3(32, 8), 0, st, (const float*)g.maps, bs6, g.tmp, bs5, 3, g.hc, g.wc, g.r_blk); if (e_ != cudaSuccess) return e_; }
+    { const cudaError_t e_ = launch(k_box_v, grid2(g.wc, g.hc, 3 * n, 32, 8), dim3(32, 8), 0, st, (const float*)g.tmp, bs5, g.maps, bs6, 3, g.hc, g.wc, g.r_blk); if (e_ != cudaSuccess) return e_; }
     { const cudaError_t e_ = launch(k_box_h_cols, grid2(g.w8, g.hc, 5 * n, 32, 8), dim3(32, 8), 0, st, g, bs5); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }

@@ -53,9 +53,11 @@ cudaError_t static_near(const int16_t* age, long long bs, int wp, int hp, float 
                         cudaStream_t st);
 // the age pass over np consecutive pairs in time order (pair i: frames fa / fb + i * frame_bs, changed + i *
 // changed_bs, age + i * age_bs; strides may be negative), advancing the one state plane pair by pair
+// spread: the 256-entry byte-threshold table of the spread test (spread_table(), once per session)
 cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, long long frame_bs, const uint32_t* changed,
                        long long changed_bs, const uint8_t* mask, const StaticArgs& s, uchar4* state, int16_t* age,
-                       long long age_bs, int np, cudaStream_t st);
+                       long long age_bs, int np, const uint32_t* spread, cudaStream_t st);
+cudaError_t spread_table(uint32_t* out, cudaStream_t st);
 
 // luma.wgsl + sad.wgsl on two 3-channel images (a view at channel offset 0): (2r+1)^2 cost channels into out (cs)
 cudaError_t sad_volume(const __half* a, int a_cs, const __half* b, int b_cs, long long in_bs, int h, int w, int r,
