@@ -107,9 +107,26 @@ def dist():
     return ws, rank, local
 
 
+WORKLOAD = ("FlyHighFG Core 1920x1080, 120-frame sequence, pair + mid(0.5) per interval (config 2), internal 856x480, "
+            "k 1, repair 1, bicubic, static protection on")
+
+
+def host_threads() -> int:
+    """All host cores this process may use for the oracle (torchrun sets OMP_NUM_THREADS=1 for its workers); returns
+    the threads in force."""
+    from oracle import oracle
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    return oracle.threads(n)
+
+
 def cpu_baseline(model_dir, frames, n_intervals):
     """The oracle (the reference algorithm restated in C++, OpenMP over all host cores) on the first n intervals."""
+    from oracle import oracle
     from oracle.oracle import OracleModel, OracleSession
+    host_threads()
     om = OracleModel(model_dir)
     o = OracleSession(om, W, H)
     o.pair(frames[0], frames[1])  # warm the caches once
@@ -129,7 +146,7 @@ def run_reference(args):
     from flyhigh_engine_b200 import synth_frames, synth_model
     model_dir = synth_model.default_dir(0)
     frames = synth_frames.sequence_c2(max(args.cpu_sample + 1, 4), W, H, seed=0)
-    cores = os.cpu_count()
+    cores = host_threads()
     times = []
     for _ in range(args.warmup):
         cpu_baseline(model_dir, frames, 1)
@@ -142,8 +159,7 @@ def run_reference(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms * args.cpu_sample,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded config-2 frames, seeded N(0,0.05) weights)",
-            "config": {"workload": "FlyHighFG Core 1080p pair + mid(0.5) per interval (config 2)",
-                       "sample": f"{args.cpu_sample} intervals per step"},
+            "config": {"workload": WORKLOAD, "sample": f"{args.cpu_sample} intervals per step"},
             "cpu_baseline": {"value": fps, "unit": "generated frames/s", "cores": cores, "kind": "port",
                              "sample": f"{args.cpu_sample} consecutive 1080p intervals (pair + mid) per step; the "
                                        "reference (Rust + wgpu/WGSL) cannot be built or run here: no Rust toolchain, "
@@ -285,7 +301,7 @@ def main():
     cpu = None
     if rank == 0 and ws == 1:
         fps_cpu, dt = cpu_baseline(model_dir, frames, args.cpu_sample)
-        cpu = {"value": fps_cpu, "unit": "generated frames/s", "cores": os.cpu_count(), "kind": "port",
+        cpu = {"value": fps_cpu, "unit": "generated frames/s", "cores": host_threads(), "kind": "port",
                "sample": f"{args.cpu_sample} consecutive intervals of the same 1080p sequence (pair + mid(0.5)), "
                          f"{dt:.1f} s on the host cores"}
     if rank == 0:
@@ -294,10 +310,9 @@ def main():
                 "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f16",
                 "data": "synthetic (seeded config-2 frames, seeded N(0,0.05) f16 weights of the FlyHighFG shapes)",
-                "config": {"workload": "FlyHighFG Core 1920x1080, 120-frame sequence, pair + mid(0.5) per interval "
-                                       "(config 2), internal 856x480, k 1, repair 1, bicubic, static protection on; "
-                                       "the reference's per-interval calls on a batched session (intervals queued "
-                                       "and launched `batch` at a time, results identical to one at a time)",
+                "config": {"workload": WORKLOAD + "; the reference's per-interval calls on a batched session "
+                                                  "(intervals queued and launched `batch` at a time, results identical "
+                                                  "to one at a time)",
                            "frames_per_step": gen_per_rank, "l2": "inputs (1 GB of frames) larger than L2, no flush",
                            "batch": args.batch, "pair_ms": pair_ms, "mid_ms": mid_ms},
                 "gpu_launches": per_interval_launches * gen_per_rank + counts["frame"],

@@ -22,6 +22,8 @@
 // (crates/flyhigh-engine/tests/golden/*.txt), which pin every derived size and parameter word the planner computes.
 #include "../flyhigh_engine_b200/csrc/json.hpp"
 
+#include <omp.h>
+
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -1408,3 +1410,9 @@ int or_conv(const uint16_t* x, int cin, int h, int w, const float* wt, const flo
 }
 
 }  // extern "C"
+
+// the OpenMP threads the oracle runs on: n > 0 sets them; returns the count in force
+extern "C" int or_threads(int n) {
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+}

@@ -33,6 +33,8 @@ def lib():
             build()
         L = ctypes.CDLL(LIB)
         L.or_error.restype = c_char_p
+        L.or_threads.restype = c_int
+        L.or_threads.argtypes = [c_int]
         L.or_model_load.restype = c_void_p
         L.or_model_load.argtypes = [c_char_p]
         L.or_model_free.argtypes = [c_void_p]
@@ -134,6 +136,11 @@ class OracleSession:
         if getattr(self, "s", None):
             lib().or_session_free(self.s)
             self.s = None
+
+
+def threads(n: int = 0) -> int:
+    """The host threads the oracle's OpenMP loops use; n > 0 sets them (a launcher may have set OMP_NUM_THREADS=1)."""
+    return int(lib().or_threads(int(n)))
 
 
 def conv(x: np.ndarray, w: np.ndarray, bias: np.ndarray, slope, stride: int, resid=None) -> np.ndarray:
