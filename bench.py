@@ -283,17 +283,20 @@ def main():
                "h2d_bytes_per_step": n * fbytes, "d2h_bytes_per_step": gen_per_rank * fbytes,
                "ms_per_step": e2e_ms}
 
-    # per-kernel device times of one pair + mid on the session's own stream (min over 5 eager runs)
+    # per-kernel device times on the session's own stream (min over 5 eager runs): one batch of `batch` intervals for a
+    # batched session (the frame stage of its batch + 1 frames, its pairs and mids), else one pair + mid
+    nb = max(args.batch, 1)
     prof = {}
     for _ in range(5):
         seen_this_run = {}
-        for k in s.profile(slots[0], slots[1], 0.5, out):
+        run = s.profile_batch() if nb > 1 else s.profile(slots[0], slots[1], 0.5, out)
+        for k in run:
             key = k["kernel"]
             if key in seen_this_run:  # launched again in the run (the second frame stage, k > 1): its own entry
                 key = f"{key} #{seen_this_run[key] + 1}"
             seen_this_run[k["kernel"]] = seen_this_run.get(k["kernel"], 0) + 1
             prof[key] = min(prof.get(key, 1e9), k["ms"])
-    roof, roof_conv = roofline_blocks(s, prof, ms, gen_per_rank)
+    roof, roof_conv = roofline_blocks(s, prof, nb)
     if rank == 0:
         total = sum(prof.values())
         for k, v in sorted(prof.items(), key=lambda x: -x[1]):
@@ -325,18 +328,22 @@ def main():
     return 0
 
 
-def conv_flops_per_interval(s) -> float:
-    """2 * M * 9 * cin * cout summed over the convs of one pair + one mid at this session's sizes (both frames'
-    encoders included, as the reference computes them every pair)."""
+def conv_flops(s, nb: int) -> float:
+    """2 * M * 9 * cin * cout summed over the convs of one profiled run at this session's sizes: the encoders of nb + 1
+    frames (both frames of one pair when nb is 1, as the reference computes them every pair) and the pair + mid convs
+    of nb intervals."""
     p = s._m.plan_params(W, H)
     q, e8, e16 = p["qh"] * p["qw"], p["h8"] * p["w8"], p["h16"] * p["w16"]
-    convs = [  # (pixels, cin, cout)
-        (e8, 3, 36), (e8, 36, 36), (e16, 36, 72), (e16, 72, 72)] * 2 + [
+    encoder = [(e8, 3, 36), (e8, 36, 36), (e16, 36, 72), (e16, 72, 72)]  # (pixels, cin, cout)
+    interval = [
         (e16, 279, 96), (e16, 96, 96), (e16, 96, 96), (e16, 96, 96), (e16, 96, 12),
         (e8, 155, 48), (e8, 48, 48), (e8, 48, 48), (e8, 48, 7),
         (e8, 48, 48), (e8, 48, 48), (e8, 48, 5), (e8, 48, 36),
         (q, 14, 24), (q, 24, 24), (q, 24, 24), (q, 24, 3)]
-    return float(sum(2 * m * 9 * ci * co for m, ci, co in convs))
+
+    def fl(cs):
+        return float(sum(2 * m * 9 * ci * co for m, ci, co in cs))
+    return fl(encoder) * (nb + 1) + fl(interval) * nb
 
 
 def render_bytes(p) -> float:
@@ -347,12 +354,15 @@ def render_bytes(p) -> float:
     return float(W * H * (12 + 4) + p["hp"] * p["wp"] * 7 + q * (7 + 3) * 2)
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one k_render launch at 1920 x 1080, from the ncu capture summarised
-# in profiles/k_render_1080p.md (48.33 MB read + 0.90 MB written)
+# dram__bytes_read.sum + dram__bytes_write.sum per rendered 1920 x 1080 frame, from the ncu capture of one batched
+# k_render launch (4 frames) summarised in profiles/k_render_1080p.md
 RENDER_TRAFFIC = 49.24e6
 
 
-def roofline_blocks(s, prof, step_ms, intervals):
+def roofline_blocks(s, prof, nb):
+    """The roofline of the HBM-bound render (the step's largest memory-bound kernel) and of the convs together, from
+    the profiled run's per-kernel device times: nb frames per render launch, nb + 1 encoders and nb intervals of
+    convs."""
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -362,25 +372,26 @@ def roofline_blocks(s, prof, step_ms, intervals):
     p = s._m.plan_params(W, H)
     hbm = peaks.get("hbm_gbs")
     tensor = peaks.get("bf16_tflops")
-    # the HBM-bound kernel that bounds the step: the full-resolution render
     name, kms = ("render", prof["render"]) if "render" in prof else max(prof.items(), key=lambda kv: kv[1])
     if name == "render":
-        achieved = render_bytes(p) / (kms / 1000.0) / 1e9
-        roof = {"bound": "hbm", "kernel": "k_render (full-resolution render + keep_static + rgba8 out)",
+        alg = render_bytes(p) * nb
+        achieved = alg / (kms / 1000.0) / 1e9
+        roof = {"bound": "hbm", "kernel": f"k_render (full-resolution render + keep_static + rgba8 out), {nb} frame(s) "
+                                          "per launch",
                 "achieved": achieved, "peak": hbm or 6650.0, "unit": "GB/s",
-                "frac": achieved / (hbm or 6650.0), "traffic": RENDER_TRAFFIC,
-                "algorithmic_bytes": render_bytes(p), "launch_ms": kms,
+                "frac": achieved / (hbm or 6650.0), "traffic": RENDER_TRAFFIC * nb,
+                "algorithmic_bytes": alg, "launch_ms": kms, "frames_per_launch": nb,
                 "peak_source": "measured" if hbm else "fallback"}
     else:
         roof = {"bound": "unknown", "kernel": name, "launch_ms": kms, "achieved": None, "peak": None, "unit": None,
                 "frac": None, "traffic": None}
     conv_ms = sum(v for k, v in prof.items() if k.startswith("conv "))
-    flops = conv_flops_per_interval(s)
+    flops = conv_flops(s, nb)
     ach = flops / (conv_ms / 1000.0) / 1e12
-    roof_conv = {"bound": "tensor", "kernel": "all conv3x3_mma launches of one pair + mid (frame stages of both "
-                                              "frames included)", "achieved": ach, "peak": tensor or 1590.0,
-                 "unit": "TFLOP/s", "frac": ach / (tensor or 1590.0), "flops": flops, "ms": conv_ms,
-                 "peak_source": "measured" if tensor else "fallback"}
+    roof_conv = {"bound": "tensor", "kernel": f"every conv launch of one profiled run ({nb + 1} frame encoders, {nb} "
+                                              "interval(s) of pair + mid convs)", "achieved": ach,
+                 "peak": tensor or 1590.0, "unit": "TFLOP/s", "frac": ach / (tensor or 1590.0), "flops": flops,
+                 "ms": conv_ms, "peak_source": "measured" if tensor else "fallback"}
     return roof, roof_conv
 
 

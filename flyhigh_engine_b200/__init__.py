@@ -92,6 +92,7 @@ EXPORTS = [
     ("fh_session_advance_static", c_int, [c_void_p, c_uint32, c_uint32]),
     ("fh_session_profile_json", c_int, [c_void_p, c_uint32, c_uint32, c_float, c_uint32, c_char_p, c_size_t]),
     ("fh_session_launch_counts", c_int, [c_void_p, POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
+    ("fh_session_profile_batch_json", c_int, [c_void_p, c_char_p, c_size_t]),
     ("fhk_conv3x3", c_int, [c_void_p, c_int, c_void_p]),
     ("fhk_conv_pack_weights", c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
     ("fhk_conv_packed_elems", c_size_t, [c_int, c_int]),
@@ -378,6 +379,13 @@ class Session:
         cap = 1 << 16
         buf = create_string_buffer(cap)
         n = _check(lib().fh_session_profile_json(self._h, a, b, t, out, buf, cap))
+        return json.loads(buf.raw[:n].decode())
+
+    def profile_batch(self) -> list:
+        """Device ms of every kernel of one batch of a batched session, run eagerly on its batch arena."""
+        cap = 1 << 16
+        buf = create_string_buffer(cap)
+        n = _check(lib().fh_session_profile_batch_json(self._h, buf, cap))
         return json.loads(buf.raw[:n].decode())
 
     def launch_counts(self) -> dict:

@@ -1187,6 +1187,45 @@ struct FhSession {
         return js;
     }
 
+    // Device time of every kernel of one batch of a batched session, run eagerly on the arena as it stands (the frames
+    // of the last batch, the phases last set), each launch followed by an event. The static state advances as that
+    // batch advanced it.
+    std::string profile_batch_json() {
+        if (nbat < 2) fail("not a batched session");
+        flush();
+        if (batches_run == 0) fail("no batch has run");
+        const int n = nbat;
+        const size_t fb = (size_t)w * h * 4;
+        std::vector<std::pair<std::string, cudaEvent_t>> marks;
+        CK(cudaStreamSynchronize(st));
+        CK(fhk::delay(st, 4000000));
+        prof = &marks;
+        try {
+            mark("start");
+            const FView fa = arena_view(1), fbv = arena_view(0);
+            run_frame(arena_view(0), n + 1);
+            run_pair(fa, fbv, n);
+            run_mid(PairSrc{fa, fbv}, arena_out, (long long)fb, n);
+        } catch (...) {
+            prof = nullptr;
+            for (auto& m : marks) cudaEventDestroy(m.second);
+            throw;
+        }
+        prof = nullptr;
+        CK(cudaStreamSynchronize(st));
+        std::string js = "[";
+        for (size_t i = 1; i < marks.size(); i++) {
+            float ms = 0;
+            CK(cudaEventElapsedTime(&ms, marks[i - 1].second, marks[i].second));
+            char b2[64];
+            snprintf(b2, sizeof b2, "%.6f", ms);
+            js += std::string(i > 1 ? "," : "") + "{\"kernel\":" + fhjson::quote(marks[i].first) + ",\"ms\":" + b2 + "}";
+        }
+        js += "]";
+        for (auto& m : marks) cudaEventDestroy(m.second);
+        return js;
+    }
+
     int add_input() {
         InSlot s;
         s.sets.push_back(new_set());
@@ -1738,6 +1777,14 @@ int fh_session_advance_static(const FhSession* cs, uint32_t a, uint32_t b) {
         CK(fhk::static_age(A.frame, B.frame, 0, s->changed, 0, s->mask, s->sargs, s->state, s->age, 0, 1, s->spread, s->st));
         s->mark_read(A, B);
         return 0;
+    });
+}
+
+int fh_session_profile_batch_json(const FhSession* cs, char* buf, size_t cap) {
+    return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
+        if (!s || !buf) fail("null argument");
+        return write_json(s->profile_batch_json(), buf, cap);
     });
 }
 

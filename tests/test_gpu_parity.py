@@ -453,6 +453,38 @@ def test_batched_session_matches_single(synth_model_dir, batch, size, opts):
         assert np.array_equal(age1, ageb), n
 
 
+def test_batch_profile(synth_model_dir):
+    """fh_session_profile_batch_json: one batch's kernels timed eagerly, each stage once (the frame stage for all
+    batch + 1 frames in one launch per kernel); refused for a one-interval session and before any batch ran."""
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200 import synth_frames
+    w, h, batch = 384, 160, 4
+    model = fh.Model(synth_model_dir)
+    frames = synth_frames.sequence_c2(batch + 1, w, h, seed=5)
+    one = fh.Session(fh.Engine(), model, w, h)
+    with pytest.raises(fh.FlyHighError, match="not a batched session"):
+        one.profile_batch()
+    s = fh.Session(fh.Engine(), model, w, h, batch=batch)
+    ins = [s.add_input(), s.add_input()]
+    outs = [s.add_output() for _ in range(batch)]
+    with pytest.raises(fh.FlyHighError, match="no batch has run"):
+        s.profile_batch()
+    s.write(ins[0], frames[0])
+    for i in range(1, batch + 1):
+        s.write(ins[i % 2], frames[i])
+        s.pair(ins[(i - 1) % 2], ins[i % 2])
+        s.mid(0.5, outs[i - 1])
+    first = np.frombuffer(s.read(outs[0]), np.uint8).copy()
+    prof = s.profile_batch()
+    names = [k["kernel"] for k in prof]
+    for k in ("frame_to_input", "input_pyramid", "pair_planes", "static_age", "render", "mid_combine"):
+        assert names.count(k) == 1, (k, names)
+    assert sum(1 for k in names if k.startswith("conv ")) >= 20
+    assert all(k["ms"] >= 0 for k in prof) and sum(k["ms"] for k in prof) > 0
+    # the profile rewrites the arena, not the output slots the batch already filled
+    assert np.array_equal(first, np.frombuffer(s.read(outs[0]), np.uint8))
+
+
 def test_errors_and_reports(synth_model_dir):
     """The C ABI's error behaviour (core.rs): -1 / NULL with fh_last_error, never a crash."""
     import flyhigh_engine_b200 as fh
