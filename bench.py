@@ -355,8 +355,8 @@ def render_bytes(p) -> float:
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum per rendered 1920 x 1080 frame, from the ncu capture of one batched
-# k_render launch (4 frames) summarised in profiles/k_render_1080p.md
-RENDER_TRAFFIC = 49.24e6
+# k_render launch (4 frames: 144.40 MB read + 25.93 MB written) summarised in profiles/k_render_1080p.md
+RENDER_TRAFFIC = 42.58e6
 
 
 def roofline_blocks(s, prof, nb):
