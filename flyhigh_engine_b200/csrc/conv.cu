@@ -27,6 +27,8 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <type_traits>
+
 #include "fh_device.cuh"
 #include "fh_kernels.h"
 #include "launch.h"
@@ -363,44 +365,56 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
     // ---- epilogue: bias, PReLU, f16, residual / affine_out, store. Bias and slopes come from shared memory and the
     //      residual pair of a lane is loaded before any store, so no load waits behind a store it might alias ----
     const int g = lane >> 2, q = lane & 3;
+    // the residual (RES) and affine_out (AFF) steps as compile-time switches: a runtime test inside the unrolled
+    // loops would be if-converted and every element would pay for the exp and the divide
+    auto epilogue = [&](auto res_c, auto aff_c) {
+        constexpr bool RES = decltype(res_c)::value, AFF = decltype(aff_c)::value;
 #pragma unroll
-    for (int mt = 0; mt < 2; mt++) {
-        const int oy = oy0 + r0 + mt;
-        if (oy >= p.ho) continue;
+        for (int mt = 0; mt < 2; mt++) {
+            const int oy = oy0 + r0 + mt;
+            if (oy >= p.ho) continue;
 #pragma unroll
-        for (int hh = 0; hh < 2; hh++) {
-            const int ox = ox0 + g + hh * 8;
-            if (ox >= p.wo) continue;
-            __half* __restrict__ out = p.out + (long long)n * p.out_bs + ((long long)oy * p.wo + ox) * p.out_cs;
-            float2 rv[NT];
-            if (p.res) {
-                const __half* __restrict__ res = p.res + (long long)n * p.res_bs + ((long long)oy * p.wo + ox) * p.res_cs;
+            for (int hh = 0; hh < 2; hh++) {
+                const int ox = ox0 + g + hh * 8;
+                if (ox >= p.wo) continue;
+                __half* __restrict__ out = p.out + (long long)n * p.out_bs + ((long long)oy * p.wo + ox) * p.out_cs;
+                float2 rv[NT];
+                if (RES) {
+                    const __half* __restrict__ res = p.res + (long long)n * p.res_bs + ((long long)oy * p.wo + ox) * p.res_cs;
+#pragma unroll
+                    for (int j = 0; j < NT; j++) {
+                        const int c0 = (ng * NT + j) * 8 + q * 2;
+                        rv[j] = make_float2(0.0f, 0.0f);
+                        if (c0 + 1 < p.cout) rv[j] = __half22float2(*reinterpret_cast<const __half2*>(res + c0));
+                        else if (c0 < p.cout) rv[j].x = __half2float(res[c0]);
+                    }
+                }
 #pragma unroll
                 for (int j = 0; j < NT; j++) {
-                    const int c0 = (ng * NT + j) * 8 + q * 2;
-                    rv[j] = make_float2(0.0f, 0.0f);
-                    if (c0 + 1 < p.cout) rv[j] = __half22float2(*reinterpret_cast<const __half2*>(res + c0));
-                    else if (c0 < p.cout) rv[j].x = __half2float(res[c0]);
-                }
-            }
+                    const int jl = j * 8 + q * 2;  // channel of this lane inside the group
+                    const int c0 = ng * NT * 8 + jl;
+                    if (c0 >= p.cout) continue;
+                    __half r[2];
 #pragma unroll
-            for (int j = 0; j < NT; j++) {
-                const int jl = j * 8 + q * 2;  // channel of this lane inside the group
-                const int c0 = ng * NT * 8 + jl;
-                if (c0 >= p.cout) continue;
-                __half r[2];
-#pragma unroll
-                for (int e = 0; e < 2; e++) {
-                    float v = acc[mt][j][hh * 2 + e] + sbias[jl + e];
-                    if (prelu) v = v > 0.0f ? v : sslope[jl + e] * v;
-                    r[e] = __float2half_rn(v);
-                    if (p.res) r[e] = __float2half_rn(__half2float(r[e]) + (e ? rv[j].y : rv[j].x));
-                    if (p.epi == 1) r[e] = __float2half_rn(2.0f / (1.0f + expf(-__half2float(r[e]))) - 1.0f);
+                    for (int e = 0; e < 2; e++) {
+                        float v = acc[mt][j][hh * 2 + e] + sbias[jl + e];
+                        if (prelu) v = v > 0.0f ? v : sslope[jl + e] * v;
+                        r[e] = __float2half_rn(v);
+                        if (RES) r[e] = __float2half_rn(__half2float(r[e]) + (e ? rv[j].y : rv[j].x));
+                        if (AFF) r[e] = __float2half_rn(2.0f / (1.0f + expf(-__half2float(r[e]))) - 1.0f);
+                    }
+                    if (c0 + 1 < p.cout) *reinterpret_cast<__half2*>(out + c0) = __halves2half2(r[0], r[1]);
+                    else out[c0] = r[0];
                 }
-                if (c0 + 1 < p.cout) *reinterpret_cast<__half2*>(out + c0) = __halves2half2(r[0], r[1]);
-                else out[c0] = r[0];
             }
         }
+    };
+    if (p.res) {
+        if (p.epi == 1) epilogue(std::true_type{}, std::true_type{});
+        else epilogue(std::true_type{}, std::false_type{});
+    } else {
+        if (p.epi == 1) epilogue(std::false_type{}, std::true_type{});
+        else epilogue(std::false_type{}, std::false_type{});
     }
 }
 

@@ -129,6 +129,57 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
 
+// The fused epilogue of 16 channels: bias, PReLU, f16, then the residual (RES) and affine_out (AFF) steps. The
+// optional steps are template parameters so that the common case carries none of their instructions.
+template <bool RES, bool AFF>
+__device__ __forceinline__ void umma_epilogue16(const float (&v)[16], const float* sbias, const float* sslope, bool prelu,
+                                                const __half* res, bool vec_res, int cg, int cout, __half* out,
+                                                bool vec_out) {
+    const bool full = cg + 16 <= cout;
+    float rv[16];
+    if (RES) {
+        if (full && vec_res) {
+            const uint4 q0 = *reinterpret_cast<const uint4*>(res + cg), q1 = *reinterpret_cast<const uint4*>(res + cg + 8);
+            const __half2* h0 = reinterpret_cast<const __half2*>(&q0);
+            const __half2* h1 = reinterpret_cast<const __half2*>(&q1);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float2 a = __half22float2(h0[j]), b = __half22float2(h1[j]);
+                rv[2 * j] = a.x;
+                rv[2 * j + 1] = a.y;
+                rv[8 + 2 * j] = b.x;
+                rv[8 + 2 * j + 1] = b.y;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; j++) rv[j] = cg + j < cout ? __half2float(res[cg + j]) : 0.0f;
+        }
+    }
+    uint32_t packed[8];
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+        __half hh[2];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            float x = v[j + u] + sbias[j + u];
+            if (prelu) x = x > 0.0f ? x : sslope[j + u] * x;
+            __half h = __float2half_rn(x);
+            if (RES) h = __float2half_rn(__half2float(h) + rv[j + u]);
+            if (AFF) h = __float2half_rn(2.0f / (1.0f + expf(-__half2float(h))) - 1.0f);
+            hh[u] = h;
+        }
+        packed[j / 2] = (uint32_t)__half_as_ushort(hh[0]) | ((uint32_t)__half_as_ushort(hh[1]) << 16);
+    }
+    if (full && vec_out) {
+        reinterpret_cast<uint4*>(out + cg)[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        reinterpret_cast<uint4*>(out + cg)[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; j++)
+            if (cg + j < cout) out[cg + j] = __ushort_as_half((unsigned short)(packed[j / 2] >> (16 * (j & 1))));
+    }
+}
+
 // np: the padded output channels; ngw: the channels of one CTA (np / ngw groups along blockIdx.z, n-major)
 __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int np, int ngw) {
     extern __shared__ __align__(128) uint8_t sm[];
@@ -157,23 +208,32 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
         sbias[i] = c < p.cout ? p.bias[c] : 0.0f;
         sslope[i] = (prelu && c < p.cout) ? p.slope[c] : 1.0f;
     }
-    if (tid == 0) {
-        for (int q = 0; q <= WCHUNKS; q++) mbar_init(wbar0 + 8 * q, 1);
-        mbar_init_fence();
-        failed = 0;
-        // piece q: k-steps [q kc, min((q + 1) kc, nsteps)); the packed rows are [kstep][np / 8 groups][2][64 halves],
-        // so a CTA's NG channels are one contiguous run per k-step (the whole k-step when ngw == np)
+    // piece q: k-steps [q kc, min((q + 1) kc, nsteps)); the packed rows are [kstep][np / 8 groups][2][64 halves],
+    // so a CTA's NG channels are one contiguous run per k-step (the whole k-step when ngw == np). Warp 0 stages
+    // them: lane 0 sets up the barriers and their byte counts, then the lanes issue the copies between them.
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int q = 0; q <= WCHUNKS; q++) mbar_init(wbar0 + 8 * q, 1);
+            mbar_init_fence();
+            failed = 0;
+            for (int q = 0; q < WCHUNKS; q++) {
+                const int k0 = q * kc, k1 = min(k0 + kc, nsteps);
+                if (k0 >= k1) break;
+                mbar_expect_tx(wbar0 + 8 * q, (uint32_t)((k1 - k0) * ngw * 32 + (q == 0 ? p.test_extra_tx : 0)));
+            }
+        }
+        __syncwarp();
         const char* wsrc = reinterpret_cast<const char*>(p.wpack) + (size_t)cbase * 32;
-        for (int q = 0; q < WCHUNKS; q++) {
-            const int k0 = q * kc, k1 = min(k0 + kc, nsteps);
-            if (k0 >= k1) break;
-            const uint32_t bar = wbar0 + 8 * q;
-            mbar_expect_tx(bar, (uint32_t)((k1 - k0) * ngw * 32 + (q == 0 ? p.test_extra_tx : 0)));
-            if (ngw == np)
-                bulk_g2s(s0 + wofs + k0 * ngw * 32, wsrc + (size_t)k0 * np * 32, (uint32_t)((k1 - k0) * np * 32), bar);
-            else
-                for (int k = k0; k < k1; k++)
-                    bulk_g2s(s0 + wofs + k * ngw * 32, wsrc + (size_t)k * np * 32, (uint32_t)(ngw * 32), bar);
+        if (ngw == np) {
+            if (lane < WCHUNKS) {
+                const int k0 = lane * kc, k1 = min(k0 + kc, nsteps);
+                if (k0 < k1)
+                    bulk_g2s(s0 + wofs + k0 * ngw * 32, wsrc + (size_t)k0 * np * 32, (uint32_t)((k1 - k0) * np * 32),
+                             wbar0 + 8 * lane);
+            }
+        } else {
+            for (int k = lane; k < nsteps; k += 32)
+                bulk_g2s(s0 + wofs + k * ngw * 32, wsrc + (size_t)k * np * 32, (uint32_t)(ngw * 32), wbar0 + 8 * (k / kc));
         }
     }
     pdl_wait();
@@ -271,20 +331,35 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
 
     // ---- the MMAs: one thread, each weight piece as soon as it has landed ----
     if (tid == 0) {
+        // k-step ks = tap * cslices + sl: A starts at the tap's shift within the halo planes plus two planes per
+        // slice, B at ks * NG * 32 bytes. Both advance by adding to the descriptors' start-address field (address
+        // >> 4; every address here is 16-byte aligned and below 2^18, so the field never carries), keeping the
+        // single issuing thread's loop short. (Each tcgen05.mma of M 128, K 16 occupies the tensor pipe for about the
+        // same time whatever its N, so the layer's MMA time is 9 * cp / 16 instructions per tile; dealing the k-steps
+        // to several accumulators measured no gain.)
         const uint32_t idesc = (1u << 4) | ((uint32_t)(ngw >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+        const uint64_t a0 = smem_desc(s0, UPLANE, UIW * 16), b0 = smem_desc(s0 + (uint32_t)wofs, 128, 256);
+        int ks = 0, sl = 0, kx = 0;
+        uint32_t tap_ofs = 0;  // (ky * UIW + kx) * 16 of the current tap, in 16-byte units
         for (int q = 0; q < WCHUNKS && !failed; q++) {
-            const int k0 = q * kc, k1 = min(k0 + kc, nsteps);
-            if (k0 >= k1) break;
+            const int k1 = min((q + 1) * kc, nsteps);
+            if (ks >= k1) break;
             if (!mbar_wait_bounded(wbar0 + 8 * q, 0, wait_cycles)) {
                 failed = 1;
                 break;
             }
-            for (int ks = k0; ks < k1; ks++) {
-                const int tap = ks / cslices, sl = ks - tap * cslices;
-                const int ky = tap / 3, kx = tap - ky * 3;
-                const uint64_t ad = smem_desc(s0 + (uint32_t)(2 * sl * UPLANE + (ky * UIW + kx) * 16), UPLANE, UIW * 16);
-                const uint64_t bd = smem_desc(s0 + (uint32_t)(wofs + ks * ngw * 32), 128, 256);
-                umma_f16(tbase, ad, bd, idesc, ks > 0 ? 1u : 0u);
+            for (; ks < k1; ks++) {
+                umma_f16(tbase, a0 + tap_ofs + (uint32_t)(sl * (2 * UPLANE / 16)), b0 + (uint32_t)(ks * (ngw * 2)), idesc,
+                         ks > 0 ? 1u : 0u);
+                if (++sl == cslices) {
+                    sl = 0;
+                    if (++kx == 3) {
+                        kx = 0;
+                        tap_ofs += UIW - 2;  // next halo row, first column
+                    } else {
+                        tap_ofs += 1;
+                    }
+                }
             }
         }
         umma_commit(mbar);  // arrives once every MMA above has completed (at once when none was issued)
@@ -300,29 +375,26 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
     __half* __restrict__ out = p.out + (long long)n * p.out_bs + ((long long)oy * p.wo + ox) * p.out_cs;
     const __half* __restrict__ res =
         p.res ? p.res + (long long)n * p.res_bs + ((long long)oy * p.wo + ox) * p.res_cs : nullptr;
+    // 16-byte stores / loads when every pixel's channel run starts on a 16-byte boundary
+    const bool vec_out = (p.out_cs & 7) == 0 && (p.out_bs & 7) == 0 && ((uintptr_t)p.out & 15) == 0;
+    const bool vec_res = p.res && (p.res_cs & 7) == 0 && (p.res_bs & 7) == 0 && ((uintptr_t)p.res & 15) == 0;
     for (int c0 = 0; c0 < ngw; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(tbase + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+        float v[16];
+        {
+            uint32_t r[16];
+            tmem_ld16(tbase + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[j] = __uint_as_float(r[j]);
+        }
         const int cg = cbase + c0;  // output channel of column c0
         if (!inside || !mma_done) continue;
-        __half hv[16];
-        float rv[16];
-#pragma unroll
-        for (int j = 0; j < 16; j++) rv[j] = (p.res && cg + j < p.cout) ? __half2float(res[cg + j]) : 0.0f;
-#pragma unroll
-        for (int j = 0; j < 16; j++) {
-            float v = __uint_as_float(r[j]) + sbias[c0 + j];
-            if (prelu) v = v > 0.0f ? v : sslope[c0 + j] * v;
-            __half h = __float2half_rn(v);
-            if (p.res) h = __float2half_rn(__half2float(h) + rv[j]);
-            if (p.epi == 1) h = __float2half_rn(2.0f / (1.0f + expf(-__half2float(h))) - 1.0f);
-            hv[j] = h;
-        }
-        if (cg + 16 <= p.cout && (p.out_cs & 7) == 0 && ((uintptr_t)(out + cg) & 15) == 0) {
-            reinterpret_cast<uint4*>(out + cg)[0] = reinterpret_cast<const uint4*>(hv)[0];
-            reinterpret_cast<uint4*>(out + cg)[1] = reinterpret_cast<const uint4*>(hv)[1];
+        // uniform across the CTA: one instantiation runs
+        if (p.res) {
+            if (p.epi == 1) umma_epilogue16<true, true>(v, sbias + c0, sslope + c0, prelu, res, vec_res, cg, p.cout, out, vec_out);
+            else umma_epilogue16<true, false>(v, sbias + c0, sslope + c0, prelu, res, vec_res, cg, p.cout, out, vec_out);
         } else {
-            for (int j = 0; j < 16 && cg + j < p.cout; j++) out[cg + j] = hv[j];
+            if (p.epi == 1) umma_epilogue16<false, true>(v, sbias + c0, sslope + c0, prelu, res, vec_res, cg, p.cout, out, vec_out);
+            else umma_epilogue16<false, false>(v, sbias + c0, sslope + c0, prelu, res, vec_res, cg, p.cout, out, vec_out);
         }
     }
     tc_fence_before();
