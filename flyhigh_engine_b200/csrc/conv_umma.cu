@@ -180,8 +180,9 @@ __device__ __forceinline__ void umma_epilogue16(const float (&v)[16], const floa
     }
 }
 
-// np: the padded output channels; ngw: the channels of one CTA (np / ngw groups along blockIdx.z, n-major)
-__global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int np, int ngw) {
+// np: the padded output channels; ngw: the channels of one CTA (np / ngw groups along blockIdx.z, n-major); nis: the
+// issuing warps (1 or 2), each with its own accumulator, summed in the epilogue in warp order
+__global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int np, int ngw, int nis) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int cslices = p.cp / 16, nchunk = p.cp / 8, nsteps = 9 * cslices;
@@ -197,7 +198,7 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
     uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + barofs + 8 * (WCHUNKS + 1));
     volatile int& failed = *reinterpret_cast<int*>(sm + barofs + 8 * (WCHUNKS + 1) + 4);
     const long long wait_cycles = p.wait_cycles > 0 ? p.wait_cycles : 2000000000ll;
-    const uint32_t ncols = (uint32_t)tmem_cols(ngw);
+    const uint32_t ncols = (uint32_t)tmem_cols(ngw * nis);  // accumulator w: columns [w * ngw, (w + 1) * ngw)
     const bool prelu = p.slope != nullptr;
     const int kc = (nsteps + WCHUNKS - 1) / WCHUNKS;  // k-steps per weight piece
 
@@ -213,7 +214,8 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
     // them: lane 0 sets up the barriers and their byte counts, then the lanes issue the copies between them.
     if (warp == 0) {
         if (lane == 0) {
-            for (int q = 0; q <= WCHUNKS; q++) mbar_init(wbar0 + 8 * q, 1);
+            for (int q = 0; q < WCHUNKS; q++) mbar_init(wbar0 + 8 * q, 1);
+            mbar_init(mbar, (uint32_t)nis);  // one commit per issuing warp
             mbar_init_fence();
             failed = 0;
             for (int q = 0; q < WCHUNKS; q++) {
@@ -329,36 +331,38 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
     tc_fence_after();
     const uint32_t tbase = *tslot;
 
-    // ---- the MMAs: one thread, each weight piece as soon as it has landed ----
-    if (tid == 0) {
+    // ---- the MMAs: lane 0 of each of the first nis warps issues a contiguous half (or all) of the k-steps into its
+    //      own accumulator, each weight piece as soon as it has landed. A single issuing thread spends several times
+    //      a small-N MMA's tensor-pipe time on each issue; two issuers keep the pipe busy. ----
+    if (lane == 0 && warp < nis) {
         // k-step ks = tap * cslices + sl: A starts at the tap's shift within the halo planes plus two planes per
         // slice, B at ks * NG * 32 bytes. Both advance by adding to the descriptors' start-address field (address
-        // >> 4; every address here is 16-byte aligned and below 2^18, so the field never carries), keeping the
-        // single issuing thread's loop short. (Each tcgen05.mma of M 128, K 16 occupies the tensor pipe for about the
-        // same time whatever its N, so the layer's MMA time is 9 * cp / 16 instructions per tile; dealing the k-steps
-        // to several accumulators measured no gain.)
+        // >> 4; every address here is 16-byte aligned and below 2^18, so the field never carries).
         const uint32_t idesc = (1u << 4) | ((uint32_t)(ngw >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-        const uint64_t a0 = smem_desc(s0, UPLANE, UIW * 16), b0 = smem_desc(s0 + (uint32_t)wofs, 128, 256);
-        int ks = 0, sl = 0, kx = 0;
-        uint32_t tap_ofs = 0;  // (ky * UIW + kx) * 16 of the current tap, in 16-byte units
-        for (int q = 0; q < WCHUNKS && !failed; q++) {
-            const int k1 = min((q + 1) * kc, nsteps);
-            if (ks >= k1) break;
+        const int kb = warp * nsteps / nis, ke = (warp + 1) * nsteps / nis;
+        const int tap = kb / cslices;
+        int sl = kb - tap * cslices, kx = tap % 3;
+        uint32_t tap_ofs = (uint32_t)((tap / 3) * UIW + kx);  // (ky * UIW + kx) * 16 bytes, in 16-byte units
+        uint64_t ad = smem_desc(s0, UPLANE, UIW * 16) + tap_ofs + (uint32_t)(sl * (2 * UPLANE / 16));
+        uint64_t bd = smem_desc(s0 + (uint32_t)wofs, 128, 256) + (uint32_t)(kb * (ngw * 2));
+        const uint32_t dt = tbase + (uint32_t)(warp * ngw);
+        int ks = kb;
+        for (int q = kb / kc; q < WCHUNKS && ks < ke && !failed; q++) {
+            const int k1 = min(min((q + 1) * kc, nsteps), ke);
             if (!mbar_wait_bounded(wbar0 + 8 * q, 0, wait_cycles)) {
                 failed = 1;
                 break;
             }
             for (; ks < k1; ks++) {
-                umma_f16(tbase, a0 + tap_ofs + (uint32_t)(sl * (2 * UPLANE / 16)), b0 + (uint32_t)(ks * (ngw * 2)), idesc,
-                         ks > 0 ? 1u : 0u);
+                umma_f16(dt, ad, bd, idesc, ks > kb ? 1u : 0u);
+                bd += (uint32_t)(ngw * 2);
                 if (++sl == cslices) {
                     sl = 0;
-                    if (++kx == 3) {
-                        kx = 0;
-                        tap_ofs += UIW - 2;  // next halo row, first column
-                    } else {
-                        tap_ofs += 1;
-                    }
+                    const uint32_t step = ++kx == 3 ? UIW - 2 : 1;  // next tap: next column, or the next halo row
+                    if (kx == 3) kx = 0;
+                    ad += (uint64_t)((long long)step - (long long)((cslices - 1) * (2 * UPLANE / 16)));
+                } else {
+                    ad += (uint32_t)(2 * UPLANE / 16);
                 }
             }
         }
@@ -382,9 +386,15 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
         float v[16];
         {
             uint32_t r[16];
-            tmem_ld16(tbase + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+            const uint32_t ta = tbase + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
+            tmem_ld16(ta, r);
 #pragma unroll
             for (int j = 0; j < 16; j++) v[j] = __uint_as_float(r[j]);
+            if (nis == 2) {
+                tmem_ld16(ta + (uint32_t)ngw, r);
+#pragma unroll
+                for (int j = 0; j < 16; j++) v[j] += __uint_as_float(r[j]);
+            }
         }
         const int cg = cbase + c0;  // output channel of column c0
         if (!inside || !mma_done) continue;
@@ -482,6 +492,9 @@ extern "C" int fhk_conv3x3_umma(const FhConvParams* pin, void* stream) {
         ngw = g;
         if (tiles * (np / g) >= 148) break;
     }
+    // two issuing warps, each with its own accumulator, where both fit in 256 tensor-memory columns (two CTAs an
+    // SM); a function of the layer's shape only, so no output depends on the batch or the channel split
+    const int nis = np <= 128 ? 2 : 1;
     const size_t smem = (size_t)umma_smem(p.cp, ngw);
     static size_t configured = 48 * 1024;
     if (smem > configured) {
@@ -491,5 +504,5 @@ extern "C" int fhk_conv3x3_umma(const FhConvParams* pin, void* stream) {
     }
     p.wsmem = 1;
     const dim3 grid((p.wo + UT_W - 1) / UT_W, (p.ho + UT_H - 1) / UT_H, p.n * (np / ngw));
-    return (int)fhk::launch(conv3x3_umma, grid, dim3(128), smem, (cudaStream_t)stream, p, np, ngw);
+    return (int)fhk::launch(conv3x3_umma, grid, dim3(128), smem, (cudaStream_t)stream, p, np, ngw, nis);
 }
