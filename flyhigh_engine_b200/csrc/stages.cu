@@ -73,7 +73,8 @@ __global__ void k_frame_to_input(const uint8_t* __restrict__ frames, long long f
     pdl_wait();
     pdl_trigger();
     const int ox = blockIdx.x * blockDim.x + threadIdx.x, oy = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
-    if (ox >= ow || oy >= oh) return;
+    const bool inside = ox < ow && oy < oh;
+    if (!inside) return;
     const uint32_t* f = reinterpret_cast<const uint32_t*>(frames + (long long)n * frame_bs);
     __half* o = out + (long long)n * out_bs + ((long long)oy * ow + ox) * 4;
     if (!internal) {
@@ -231,14 +232,6 @@ __global__ void k_input_pyramid(const __half* __restrict__ A, long long a_bs, in
 
 // -------------------------------------------------------------------------------------------- static age pass ----
 
-FH_DEV float diff3(uint32_t a, uint32_t b, const float* lut) {
-    float d = 0.0f;
-    d = fmaxf(d, fabsf(lut[a & 255] - lut[b & 255]));
-    d = fmaxf(d, fabsf(lut[(a >> 8) & 255] - lut[(b >> 8) & 255]));
-    d = fmaxf(d, fabsf(lut[(a >> 16) & 255] - lut[(b >> 16) & 255]));
-    return d;
-}
-
 // The per-pair planes over the padded plane (a, b read at the clamped position):
 //  - changed = keep_static_age.wgsl:52-56 `diff(o) >= thr` (the age pass probes it 41 times per pixel), one bit per
 //    pixel: row y is words [y * ww, (y + 1) * ww), bit j of word k = pixel 32 k + j, zero past the padded width;
@@ -263,32 +256,44 @@ __global__ void __launch_bounds__(256) k_pair_planes(const uint8_t* __restrict__
         a = __ldg(reinterpret_cast<const uint32_t*>(fa + n * frame_bs) + src);
         b = __ldg(reinterpret_cast<const uint32_t*>(fb + n * frame_bs) + src);
     }
+    // |A - B| per channel, once for both planes
+    float d[3];
+#pragma unroll
+    for (int c = 0; c < 3; c++) {
+        const int sh = 16 - 8 * c;  // B, G, R
+        d[c] = fabsf(lut[(a >> sh) & 255] - lut[(b >> sh) & 255]);
+    }
     if (changed) {
-        const uint32_t word = __ballot_sync(0xffffffffu, in && diff3(a, b, lut) >= s.thr);
+        const float dm = fmaxf(fmaxf(d[0], d[1]), d[2]);  // diff(o): the channel maximum
+        const uint32_t word = __ballot_sync(0xffffffffu, in && dm >= s.thr);
         if (threadIdx.x == 0) changed[n * changed_bs + (long long)y * ((s.wp + 31) >> 5) + blockIdx.x] = word;
     }
-    if (dsum && in) {
-        float d = 0.0f;
-        for (int c = 0; c < 3; c++) {
-            const int sh = 16 - 8 * c;
-            d = d + fabsf(lut[(a >> sh) & 255] - lut[(b >> sh) & 255]);
-        }
-        dsum[n * dsum_bs + (long long)y * s.wp + x] = d;
-    }
+    if (dsum && in) dsum[n * dsum_bs + (long long)y * s.wp + x] = (d[0] + d[1]) + d[2];
 }
 
-// render_static's on_static (gpu/pipeline.rs:10-34) per pixel: an age >= min_age in the clamped 3 x 3 neighbourhood
-__global__ void k_static_near(const int16_t* __restrict__ age, long long bs, int W, int H, float min_age, uint8_t* near) {
+// render_static's on_static (gpu/pipeline.rs:10-34) per pixel: an age >= min_age in the clamped 3 x 3 neighbourhood.
+// A warp is one 32-pixel row segment (blocks of 32 x 8): each lane tests its column over rows y - 1 .. y + 1, the
+// ballot of those tests is shifted one column each way, and lanes 0 and 31 test the columns either side of the segment.
+__global__ void __launch_bounds__(256) k_static_near(const int16_t* __restrict__ age, long long bs, int W, int H,
+                                                     float min_age, uint8_t* near) {
     pdl_wait();
     pdl_trigger();
-    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
-    if (x >= W || y >= H) return;
-    const int16_t* ag = age + blockIdx.z * bs;
-    bool hit = false;
-    for (int dy = -1; dy <= 1; dy++)
-        for (int dx = -1; dx <= 1; dx++)
-            hit |= (float)ag[(long long)clampi(y + dy, 0, H - 1) * W + clampi(x + dx, 0, W - 1)] >= min_age;
-    near[blockIdx.z * bs + (long long)y * W + x] = hit ? 1 : 0;
+    const int lane = threadIdx.x, x0 = blockIdx.x * 32, x = x0 + lane, y = blockIdx.y * blockDim.y + threadIdx.y;
+    if (y >= H) return;  // warp-uniform
+    const int16_t* __restrict__ ag = age + blockIdx.z * bs;
+    const long long r0 = (long long)max(y - 1, 0) * W, r1 = (long long)y * W, r2 = (long long)min(y + 1, H - 1) * W;
+    auto column = [&](int c) {  // the three loads issued together, no short-circuit
+        const int16_t a0 = __ldg(ag + r0 + c), a1 = __ldg(ag + r1 + c), a2 = __ldg(ag + r2 + c);
+        return ((float)a0 >= min_age) | ((float)a1 >= min_age) | ((float)a2 >= min_age);
+    };
+    // lanes past the plane's width test its last column, the clamp of their left neighbour's right column; every
+    // lane also tests an outer column (x0 - 1 for lane 0, else x0 + 32; one address for lanes 1-31), so the loads
+    // issue together without a divergent branch, and lanes 0 and 31 supply the ballot bits used
+    const bool own_hit = column(min(x, W - 1)), edge_hit = column(lane == 0 ? max(x0 - 1, 0) : min(x0 + 32, W - 1));
+    const uint32_t col = __ballot_sync(0xffffffffu, own_hit);
+    const uint32_t eb = __ballot_sync(0xffffffffu, edge_hit);
+    const uint32_t nb = col | (col << 1) | (eb & 1u) | (col >> 1) | (eb & 0x80000000u);
+    if (x < W) near[blockIdx.z * bs + r1 + x] = (uint8_t)((nb >> lane) & 1u);
 }
 
 // 32 bits of row `row` of the changed plane: bit i = changed(clamp(s0 + i, 0, W - 1)), the replicate clamp of the
@@ -313,7 +318,7 @@ FH_DEV uint32_t bit_window(const uint32_t* __restrict__ row, int ww, int W, int 
 
 // The spread test per channel, v(q) - v(o) >= 0.03 or v(o) - v(q) >= 0.03 in f32 (v = the byte -> value table), as
 // byte thresholds per o: the first q above o and the last q below o that pass (both differences are monotone in q).
-// Low half: the upper threshold (256: none), high half: the lower one + 1 (0: none).
+// Low half: the upper threshold - 1 (255: none, as no byte exceeds it), high half: the lower threshold + 1 (0: none).
 __global__ void k_spread_table(uint32_t* out) {
     __shared__ float lut[256];
     const int o = threadIdx.x;
@@ -323,7 +328,74 @@ __global__ void k_spread_table(uint32_t* out) {
     while (hi < 256 && !(lut[hi] - lut[o] >= 0.03f)) hi++;
     int lo = o;
     while (lo >= 0 && !(lut[o] - lut[lo] >= 0.03f)) lo--;
-    out[o] = (uint32_t)hi | ((uint32_t)(lo + 1) << 16);
+    out[o] = (uint32_t)(hi - 1) | ((uint32_t)(lo + 1) << 16);
+}
+
+FH_DEV uint32_t max_u16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+FH_DEV uint32_t min_u16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("min.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// Extremes over the clamped 3 x 3 neighbourhood of this lane's pixel, per channel, of one frame. The channels of an
+// rgba8 pixel are split as R | B << 16 (two 16-bit lanes) and G, so the column and neighbour reductions are max / min
+// over 16-bit pairs and plain integers.
+struct Ext3 {
+    uint32_t rb_max, rb_min, g_max, g_min, own;
+};
+FH_DEV Ext3 frame_ext3(const uint32_t* __restrict__ F, int fw, int r0, int r1, int r2, int xc, int xe, int lane) {
+    const uint32_t u0 = __ldg(F + (long long)r0 * fw + xc), u1 = __ldg(F + (long long)r1 * fw + xc),
+                   u2 = __ldg(F + (long long)r2 * fw + xc);
+    Ext3 e;
+    e.own = u1;
+    e.rb_max = max_u16x2(max_u16x2(u0 & 0x00ff00ffu, u1 & 0x00ff00ffu), u2 & 0x00ff00ffu);
+    e.rb_min = min_u16x2(min_u16x2(u0 & 0x00ff00ffu, u1 & 0x00ff00ffu), u2 & 0x00ff00ffu);
+    const uint32_t g0 = (u0 >> 8) & 255u, g1 = (u1 >> 8) & 255u, g2 = (u2 >> 8) & 255u;
+    e.g_max = max(max(g0, g1), g2);
+    e.g_min = min(min(g0, g1), g2);
+    // the edge lanes' outer column: x0 - 1 for lane 0 (x0 itself at the left border), x0 + 32 for lane 31. Every
+    // lane loads its xe (one shared address for lanes 1-31), so the loads issue with the others, unbranched.
+    const uint32_t v0 = __ldg(F + (long long)r0 * fw + xe), v1 = __ldg(F + (long long)r1 * fw + xe),
+                   v2 = __ldg(F + (long long)r2 * fw + xe);
+    const uint32_t x_rbmax = max_u16x2(max_u16x2(v0 & 0x00ff00ffu, v1 & 0x00ff00ffu), v2 & 0x00ff00ffu);
+    const uint32_t x_rbmin = min_u16x2(min_u16x2(v0 & 0x00ff00ffu, v1 & 0x00ff00ffu), v2 & 0x00ff00ffu);
+    const uint32_t h0 = (v0 >> 8) & 255u, h1 = (v1 >> 8) & 255u, h2 = (v2 >> 8) & 255u;
+    const uint32_t x_gmax = max(max(h0, h1), h2), x_gmin = min(min(h0, h1), h2);
+    uint32_t l_rbmax = __shfl_up_sync(0xffffffffu, e.rb_max, 1), r_rbmax = __shfl_down_sync(0xffffffffu, e.rb_max, 1);
+    uint32_t l_rbmin = __shfl_up_sync(0xffffffffu, e.rb_min, 1), r_rbmin = __shfl_down_sync(0xffffffffu, e.rb_min, 1);
+    uint32_t l_gmax = __shfl_up_sync(0xffffffffu, e.g_max, 1), r_gmax = __shfl_down_sync(0xffffffffu, e.g_max, 1);
+    uint32_t l_gmin = __shfl_up_sync(0xffffffffu, e.g_min, 1), r_gmin = __shfl_down_sync(0xffffffffu, e.g_min, 1);
+    if (lane == 0) {
+        l_rbmax = x_rbmax;
+        l_rbmin = x_rbmin;
+        l_gmax = x_gmax;
+        l_gmin = x_gmin;
+    }
+    if (lane == 31) {
+        r_rbmax = x_rbmax;
+        r_rbmin = x_rbmin;
+        r_gmax = x_gmax;
+        r_gmin = x_gmin;
+    }
+    e.rb_max = max_u16x2(e.rb_max, max_u16x2(l_rbmax, r_rbmax));
+    e.rb_min = min_u16x2(e.rb_min, min_u16x2(l_rbmin, r_rbmin));
+    e.g_max = max(e.g_max, max(l_gmax, r_gmax));
+    e.g_min = min(e.g_min, min(l_gmin, r_gmin));
+    return e;
+}
+
+// the spread test of one frame at this pixel: some channel of some neighbour at or beyond a threshold of the own value
+FH_DEV bool frame_spread(const Ext3& e, const uint32_t* tab) {
+    const uint32_t tr = tab[e.own & 255u], tg = tab[(e.own >> 8) & 255u], tb = tab[(e.own >> 16) & 255u];
+    const uint32_t hi_rb = (tr & 0xffffu) | (tb << 16), lo_rb = (tr >> 16) | (tb & 0xffff0000u);
+    // per 16-bit lane: max > hi - 1 <=> max(max, hi - 1) != hi - 1; min < lo + 1... <=> min(min, lo) != lo
+    return max_u16x2(e.rb_max, hi_rb) != hi_rb || min_u16x2(e.rb_min, lo_rb) != lo_rb || e.g_max > (tg & 0xffffu) ||
+           e.g_min < (tg >> 16);
 }
 
 // keep_static_age.wgsl:59-77: 9 near + 32 far probes of `changed`, the spread test, the state machine (decide, :28-36),
@@ -334,7 +406,8 @@ __global__ void k_spread_table(uint32_t* out) {
 // changed bits for the whole segment, and the warp ORs the windows. spread: max over the clamped 3 x 3 neighbourhood
 // and channels of |a(q) - a(o)|, |b(q) - b(o)|; the byte -> value table is monotone and f32 subtraction is monotone
 // in each operand, so that max is max(v(max_q) - v(o), v(o) - v(min_q)) per channel, exactly; its test against
-// 0.03 is a byte threshold per o (k_spread_table).
+// 0.03 is a byte threshold per o (k_spread_table). When the pairs are chained (pair i's second frame is pair i + 1's
+// first, fa + frame_bs == fb) the extremes of a frame are computed once and serve both of its pairs.
 __global__ void __launch_bounds__(256) k_static_age(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb,
                                                     long long frame_bs, const uint32_t* __restrict__ changed,
                                                     long long changed_bs, const uint8_t* __restrict__ mask, StaticArgs s,
@@ -370,67 +443,23 @@ __global__ void __launch_bounds__(256) k_static_age(const uint8_t* __restrict__ 
     const int r0 = min(max(y - 1, 0), s.h - 1), r1 = min(y, s.h - 1), r2 = min(y + 1, s.h - 1);
     const int xc = min(x, s.w - 1);
     const int xe = lane == 0 ? min(max(x0 - 1, 0), s.w - 1) : min(x0 + 32, s.w - 1);
+    const bool chained = fa + frame_bs == fb;
+    Ext3 ea = frame_ext3(reinterpret_cast<const uint32_t*>(fa), s.w, r0, r1, r2, xc, xe, lane);
     for (int pi = 0; pi < np; pi++) {
         const uint32_t* ch = changed + pi * changed_bs;
         uint32_t mv = bit_window(ch + (long long)clampi(y + pdy, 0, H - 1) * ww, ww, W, x0 + pdx);
         if (lane < 9) mv |= bit_window(ch + (long long)clampi(y + lane / 3 - 1, 0, H - 1) * ww, ww, W, x0 + lane % 3 - 1);
         mv = __reduce_or_sync(0xffffffffu, mv);
         const uint32_t own_word = __ldg(ch + (long long)y * ww + blockIdx.x);
-        // spread: column extremes over rows y - 1 .. y + 1, then across the neighbouring lanes' columns
-        const uint32_t* A = reinterpret_cast<const uint32_t*>(fa + pi * frame_bs);
-        const uint32_t* B = reinterpret_cast<const uint32_t*>(fb + pi * frame_bs);
-        const uint32_t a0 = __ldg(A + (long long)r0 * s.w + xc), a1 = __ldg(A + (long long)r1 * s.w + xc),
-                       a2 = __ldg(A + (long long)r2 * s.w + xc);
-        const uint32_t b0 = __ldg(B + (long long)r0 * s.w + xc), b1 = __ldg(B + (long long)r1 * s.w + xc),
-                       b2 = __ldg(B + (long long)r2 * s.w + xc);
-        uint32_t amax = __vmaxu4(__vmaxu4(a0, a1), a2), amin = __vminu4(__vminu4(a0, a1), a2);
-        uint32_t bmax = __vmaxu4(__vmaxu4(b0, b1), b2), bmin = __vminu4(__vminu4(b0, b1), b2);
-        // the edge lanes' outer column: x0 - 1 for lane 0 (x0 itself at the left border), x0 + 32 for lane 31
-        uint32_t eamax = 0, eamin = 0, ebmax = 0, ebmin = 0;
-        if (lane == 0 || lane == 31) {
-            const uint32_t e0 = __ldg(A + (long long)r0 * s.w + xe), e1 = __ldg(A + (long long)r1 * s.w + xe),
-                           e2 = __ldg(A + (long long)r2 * s.w + xe);
-            const uint32_t f0 = __ldg(B + (long long)r0 * s.w + xe), f1 = __ldg(B + (long long)r1 * s.w + xe),
-                           f2 = __ldg(B + (long long)r2 * s.w + xe);
-            eamax = __vmaxu4(__vmaxu4(e0, e1), e2);
-            eamin = __vminu4(__vminu4(e0, e1), e2);
-            ebmax = __vmaxu4(__vmaxu4(f0, f1), f2);
-            ebmin = __vminu4(__vminu4(f0, f1), f2);
-        }
-        {
-            uint32_t l_amax = __shfl_up_sync(0xffffffffu, amax, 1), r_amax = __shfl_down_sync(0xffffffffu, amax, 1);
-            uint32_t l_amin = __shfl_up_sync(0xffffffffu, amin, 1), r_amin = __shfl_down_sync(0xffffffffu, amin, 1);
-            uint32_t l_bmax = __shfl_up_sync(0xffffffffu, bmax, 1), r_bmax = __shfl_down_sync(0xffffffffu, bmax, 1);
-            uint32_t l_bmin = __shfl_up_sync(0xffffffffu, bmin, 1), r_bmin = __shfl_down_sync(0xffffffffu, bmin, 1);
-            if (lane == 0) {
-                l_amax = eamax;
-                l_amin = eamin;
-                l_bmax = ebmax;
-                l_bmin = ebmin;
-            }
-            if (lane == 31) {
-                r_amax = eamax;
-                r_amin = eamin;
-                r_bmax = ebmax;
-                r_bmin = ebmin;
-            }
-            amax = __vmaxu4(amax, __vmaxu4(l_amax, r_amax));
-            amin = __vminu4(amin, __vminu4(l_amin, r_amin));
-            bmax = __vmaxu4(bmax, __vmaxu4(l_bmax, r_bmax));
-            bmin = __vminu4(bmin, __vminu4(l_bmin, r_bmin));
-        }
+        if (pi > 0 && !chained)
+            ea = frame_ext3(reinterpret_cast<const uint32_t*>(fa + pi * frame_bs), s.w, r0, r1, r2, xc, xe, lane);
+        const Ext3 eb = frame_ext3(reinterpret_cast<const uint32_t*>(fb + pi * frame_bs), s.w, r0, r1, r2, xc, xe, lane);
+        const bool spread_ab = frame_spread(ea, spread_tab) || frame_spread(eb, spread_tab);
+        ea = eb;  // the next pair's first frame when chained
         if (!active) continue;
-        bool spread = false;
-#pragma unroll
-        for (int c = 0; c < 3; c++) {
-            const int sh = 16 - 8 * c;  // channel c of the BGR plane = byte 2 - c of the rgba pixel
-            const uint32_t ta = spread_tab[(a1 >> sh) & 255], tb = spread_tab[(b1 >> sh) & 255];
-            spread |= ((amax >> sh) & 255) >= (ta & 0xffff) || ((amin >> sh) & 255) < (ta >> 16) ||
-                      ((bmax >> sh) & 255) >= (tb & 0xffff) || ((bmin >> sh) & 255) < (tb >> 16);
-        }
         const bool moved = (mv >> lane) & 1u;
         const bool same = ((own_word >> lane) & 1u) == 0;
-        const bool still = same && spread;
+        const bool still = same && spread_ab;
         const int raw = still ? min((int)st.x + 1, 255) : 0;
         const int seen = still ? min((int)st.y + (moved ? 1 : 0), 255) : 0;
         const int run = same ? min((int)st.z + 1, 255) : 0;
@@ -1259,16 +1288,40 @@ __global__ void k_delay(long long cycles) {
 }
 
 // tex_in.wgsl's values for the whole frame: f16(byte / 255) as B, G, R, 0 halves per pixel (unpadded)
-__global__ void k_frame_half(const uint8_t* __restrict__ f, long long f_bs, int w, int h, __half* out, long long o_bs) {
-    __shared__ float lut[256];
-    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
+// rgba8 -> the f16 frame plane (B, G, R, 0 per pixel) the render samples. A thread converts 4 pixels: one 16-byte
+// load, two 16-byte stores, the byte -> f16 values from a shared table of halves.
+__global__ void __launch_bounds__(256) k_frame_half(const uint8_t* __restrict__ f, long long f_bs, int w, int h,
+                                                    __half* out, long long o_bs) {
+    __shared__ uint16_t lut[256];
+    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y)
+        lut[i] = __half_as_ushort(__float2half_rn(u8v(i)));  // exact: u8v is an f16 value
     __syncthreads();
     pdl_wait();
     pdl_trigger();
-    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
+    const int x = (blockIdx.x * blockDim.x + threadIdx.x) * 4, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
     if (x >= w || y >= h) return;
-    const uint32_t v = __ldg(reinterpret_cast<const uint32_t*>(f + (long long)n * f_bs) + (long long)y * w + x);
-    st4(out + (long long)n * o_bs + ((long long)y * w + x) * 4, lut[(v >> 16) & 255], lut[(v >> 8) & 255], lut[v & 255]);
+    const uint8_t* src = f + (long long)n * f_bs + ((long long)y * w + x) * 4;
+    __half* dst = out + (long long)n * o_bs + ((long long)y * w + x) * 4;
+    auto px = [&](uint32_t v, uint32_t& lo, uint32_t& hi) {
+        lo = (uint32_t)lut[(v >> 16) & 255] | ((uint32_t)lut[(v >> 8) & 255] << 16);  // B, G
+        hi = (uint32_t)lut[v & 255];                                                   // R, 0
+    };
+    if (x + 4 <= w && ((uintptr_t)src & 15) == 0 && ((uintptr_t)dst & 15) == 0) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(src));
+        uint4 a, b;
+        px(v.x, a.x, a.y);
+        px(v.y, a.z, a.w);
+        px(v.z, b.x, b.y);
+        px(v.w, b.z, b.w);
+        reinterpret_cast<uint4*>(dst)[0] = a;
+        reinterpret_cast<uint4*>(dst)[1] = b;
+    } else {
+        for (int i = 0; i < 4 && x + i < w; i++) {
+            uint2 o;
+            px(__ldg(reinterpret_cast<const uint32_t*>(src) + i), o.x, o.y);
+            reinterpret_cast<uint2*>(dst)[i] = o;
+        }
+    }
 }
 
 __global__ void k_frame_planes(const uint8_t* f, int w, int h, int hp, int wp, float* out) {
@@ -1428,7 +1481,7 @@ cudaError_t render(const RenderArgs& r0, int n, cudaStream_t st) {
 
 cudaError_t frame_half(const uint8_t* f, long long f_bs, int w, int h, __half* out, long long o_bs, int n,
                        cudaStream_t st) {
-    { const cudaError_t e_ = launch(k_frame_half, grid2(w, h, n, 32, 8), dim3(32, 8), 0, st, f, f_bs, w, h, out, o_bs); if (e_ != cudaSuccess) return e_; }
+    { const cudaError_t e_ = launch(k_frame_half, grid2((w + 3) / 4, h, n, 32, 8), dim3(32, 8), 0, st, f, f_bs, w, h, out, o_bs); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
