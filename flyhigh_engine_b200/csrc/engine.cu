@@ -406,6 +406,11 @@ struct FhSession {
     FrameSet arena;
     uint8_t* arena_out = nullptr;  // nbat rendered frames, scattered to the output slots
     cudaGraphExec_t batch_graph = nullptr;
+    // the batch graph for a batch whose oldest frame is the previous batch's newest: that frame's stage outputs are
+    // already in entry nbat (carried there at the end of every batch), so its frame stage covers entries 0..nbat-1
+    cudaGraphExec_t batch_graph_carry = nullptr;
+    const FrameSet* carried = nullptr;  // the frame whose outputs entry nbat holds, at generation carried_gen
+    uint64_t carried_gen = 0;
     int batch_kernels = 0;
     long long batches_run = 0;
     std::map<std::pair<const FrameSet*, const FrameSet*>, cudaGraphExec_t> pair_graphs;
@@ -488,6 +493,7 @@ struct FhSession {
             if (fs->graph) cudaGraphExecDestroy(fs->graph);
         for (auto& kv : pair_graphs) cudaGraphExecDestroy(kv.second);
         if (batch_graph) cudaGraphExecDestroy(batch_graph);
+        if (batch_graph_carry) cudaGraphExecDestroy(batch_graph_carry);
         for (auto& kv : mid_graphs) cudaGraphExecDestroy(kv.second);
         for (void* p : allocs) cudaFree(p);
         if (eng) eng->tensor_bytes -= std::min(eng->tensor_bytes, bytes);
@@ -1039,6 +1045,21 @@ struct FhSession {
         --single;
     }
 
+    // entry 0's frame-stage outputs (the batch's newest frame) into entry nbat, where the next batch's oldest frame sits
+    void carry_newest() {
+        const FView src = arena_view(0), dst = arena_view(nbat);
+        auto cp = [&](const __half* d, const __half* s_, long long elems) {
+            CK(cudaMemcpyAsync(const_cast<__half*>(d), s_, (size_t)elems * sizeof(__half), cudaMemcpyDeviceToDevice, st));
+        };
+        cp(dst.half, src.half, src.half_bs);
+        cp(dst.A, src.A, src.A_bs);
+        cp(dst.aq, src.aq, src.aq_bs);
+        cp(dst.i8, src.i8, src.i8_bs);
+        cp(dst.i16, src.i16, src.i16_bs);
+        cp(dst.f8, src.f8, src.f8_bs);
+        cp(dst.f16, src.f16, src.f16_bs);
+    }
+
     // nbat chained intervals (q[i].b == q[i + 1].a) as one graph: the frames of times 0..nbat gathered into the arena
     // (time t at entry nbat - t), the frame stage of all nbat + 1, the pairs and mids of all nbat (interval i at entry
     // nbat - 1 - i), then the rendered frames scattered to their output slots in time order.
@@ -1058,17 +1079,24 @@ struct FhSession {
         std::vector<float> tv(n);
         for (int e = 0; e < n; e++) tv[e] = q[n - 1 - e].t;
         CK(cudaMemcpyAsync(tdev, tv.data(), n * sizeof(float), cudaMemcpyHostToDevice, st));
-        if (!batch_graph) {
+        // the oldest frame's stage outputs were carried into entry n by the previous batch when it is that batch's
+        // newest frame, unchanged since
+        const bool carry = carried == q[0].a && q[0].a->gen == carried_gen;
+        cudaGraphExec_t& g = carry ? batch_graph_carry : batch_graph;
+        if (!g) {
             const FView fa = arena_view(1), fbv = arena_view(0);
-            batch_graph = capture(
+            g = capture(
                 [&] {
-                    run_frame(arena_view(0), n + 1);
+                    run_frame(arena_view(0), carry ? n : n + 1);
                     run_pair(fa, fbv, n);
                     run_mid(PairSrc{fa, fbv}, arena_out, (long long)fb, n);
+                    carry_newest();
                 },
                 &batch_kernels);
         }
-        CK(cudaGraphLaunch(batch_graph, st));
+        CK(cudaGraphLaunch(g, st));
+        carried = q[n - 1].b;
+        carried_gen = q[n - 1].b->gen;
         for (int i = 0; i < n; i++) {
             const int e = n - 1 - i;
             CK(cudaMemcpyAsync(outs[q[i].out], arena_out + e * fb, fb, cudaMemcpyDeviceToDevice, st));
@@ -1194,6 +1222,7 @@ struct FhSession {
         if (nbat < 2) fail("not a batched session");
         flush();
         if (batches_run == 0) fail("no batch has run");
+        carried = nullptr;  // the frame stage below recomputes entry nbat from the oldest frame
         const int n = nbat;
         const size_t fb = (size_t)w * h * 4;
         std::vector<std::pair<std::string, cudaEvent_t>> marks;
@@ -1740,7 +1769,9 @@ int fh_session_slot_device_ptr(const FhSession* cs, uint32_t slot, int output, v
             *ptr = s->outs[slot];
         } else {
             s->check_in(slot);
-            *ptr = s->cur_set(slot).frame;
+            FrameSet& fs = s->cur_set(slot);
+            fs.gen++;  // the caller may write the frame: nothing derived from the old contents stays cached
+            *ptr = fs.frame;
         }
         return 0;
     });

@@ -591,6 +591,14 @@ FH_DEV float bil_mix(float v00, float v01, float v10, float v11, float ax, float
     const float top = v00 * (1.0f - ax) + v01 * ax, bot = v10 * (1.0f - ax) + v11 * ax;
     return top * (1.0f - ay) + bot * ay;
 }
+// bil_mix of two channels at once, on float2 lanes, with bil_mix's roundings per lane
+FH_DEV float2 bil_mix2(float2 v00, float2 v01, float2 v10, float2 v11, float ax, float ay) {
+    const float2 bx = make_float2(1.0f - ax, 1.0f - ax), fx = make_float2(ax, ax);
+    const float2 top = __fadd2_rn(__fmul2_rn(v00, bx), __fmul2_rn(v01, fx));
+    const float2 bot = __fadd2_rn(__fmul2_rn(v10, bx), __fmul2_rn(v11, fx));
+    return __fadd2_rn(__fmul2_rn(top, make_float2(1.0f - ay, 1.0f - ay)), __fmul2_rn(bot, make_float2(ay, ay)));
+}
+FH_DEV float2 h2x2(uint32_t u) { return __half22float2(*reinterpret_cast<const __half2*>(&u)); }
 
 // warp.wgsl of the fine loop: one thread per e8 pixel writes wa, wb, ia, ib (all channels). The four corners of a
 // side are read as 16-byte vectors before anything is stored.
@@ -1147,9 +1155,77 @@ FH_DEV float3 sample_frame(const uint2* __restrict__ f, int w, int h, float gx, 
                        bil_mix(p00.z, p01.z, p10.z, p11.z, ax, ay));
 }
 
+// The Keys weights of sample_frame on float2 lanes (lane x: frame A, lane y: frame B), operation for operation, so each
+// lane rounds as cub1 / cub2 do.
+FH_DEV float2 cub1x2(float2 x) {  // ((a + 2) x - (a + 3)) x x + 1, a = -0.75
+    float2 t = __fmul2_rn(make_float2(1.25f, 1.25f), x);
+    t = __fadd2_rn(t, make_float2(-2.25f, -2.25f));
+    t = __fmul2_rn(t, x);
+    t = __fmul2_rn(t, x);
+    return __fadd2_rn(t, make_float2(1.0f, 1.0f));
+}
+FH_DEV float2 cub2x2(float2 x) {  // ((a x - 5 a) x + 8 a) x - 4 a
+    float2 t = __fmul2_rn(make_float2(-0.75f, -0.75f), x);
+    t = __fadd2_rn(t, make_float2(3.75f, 3.75f));
+    t = __fmul2_rn(t, x);
+    t = __fadd2_rn(t, make_float2(-6.0f, -6.0f));
+    t = __fmul2_rn(t, x);
+    return __fadd2_rn(t, make_float2(3.0f, 3.0f));
+}
+
+// Bicubic samples of both frames (A at (gxa, gya), B at (gxb, gyb)) with the two frames on the lanes of float2
+// arithmetic: the weights, the row sums and the column sum each take one packed instruction for both frames, with the
+// roundings of sample_frame per lane. Where either sample's taps reach the border, each frame is sampled alone.
+FH_DEV void sample_pair(const uint2* __restrict__ A, const uint2* __restrict__ B, int w, int h, float gxa, float gya,
+                        float gxb, float gyb, float3& sa, float3& sb) {
+    const int pxa = (int)floorf(gxa), pya = (int)floorf(gya), pxb = (int)floorf(gxb), pyb = (int)floorf(gyb);
+    const bool inner = pxa >= 1 && pxa + 2 <= w - 1 && pya >= 1 && pya + 2 <= h - 1 && pxb >= 1 && pxb + 2 <= w - 1 &&
+                       pyb >= 1 && pyb + 2 <= h - 1;
+    if (!inner) {
+        sa = sample_frame(A, w, h, gxa, gya, true);
+        sb = sample_frame(B, w, h, gxb, gyb, true);
+        return;
+    }
+    const float2 tx = make_float2(gxa - (float)pxa, gxb - (float)pxb), ty = make_float2(gya - (float)pya, gyb - (float)pyb);
+    const float2 one = make_float2(1.0f, 1.0f), two = make_float2(2.0f, 2.0f);
+    const float2 cx0 = cub2x2(__fadd2_rn(tx, one)), cx1 = cub1x2(tx), cx2 = cub1x2(__fadd2_rn(one, make_float2(-tx.x, -tx.y))),
+                 cx3 = cub2x2(__fadd2_rn(two, make_float2(-tx.x, -tx.y)));
+    const float2 cy[4] = {cub2x2(__fadd2_rn(ty, one)), cub1x2(ty), cub1x2(__fadd2_rn(one, make_float2(-ty.x, -ty.y))),
+                          cub2x2(__fadd2_rn(two, make_float2(-ty.x, -ty.y)))};
+    const uint2* a0 = A + (pya - 1) * w + (pxa - 1);
+    const uint2* b0 = B + (pyb - 1) * w + (pxb - 1);
+    float2 acc_b = make_float2(0.0f, 0.0f), acc_g = acc_b, acc_r = acc_b;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        float3 pa[4], pb[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            pa[k] = px3(a0 + j * w + k);
+            pb[k] = px3(b0 + j * w + k);
+        }
+        float2 rb = __fmul2_rn(make_float2(pa[0].x, pb[0].x), cx0);
+        float2 rg = __fmul2_rn(make_float2(pa[0].y, pb[0].y), cx0);
+        float2 rr = __fmul2_rn(make_float2(pa[0].z, pb[0].z), cx0);
+        rb = __ffma2_rn(make_float2(pa[1].x, pb[1].x), cx1, rb);
+        rg = __ffma2_rn(make_float2(pa[1].y, pb[1].y), cx1, rg);
+        rr = __ffma2_rn(make_float2(pa[1].z, pb[1].z), cx1, rr);
+        rb = __ffma2_rn(make_float2(pa[2].x, pb[2].x), cx2, rb);
+        rg = __ffma2_rn(make_float2(pa[2].y, pb[2].y), cx2, rg);
+        rr = __ffma2_rn(make_float2(pa[2].z, pb[2].z), cx2, rr);
+        rb = __ffma2_rn(make_float2(pa[3].x, pb[3].x), cx3, rb);
+        rg = __ffma2_rn(make_float2(pa[3].y, pb[3].y), cx3, rg);
+        rr = __ffma2_rn(make_float2(pa[3].z, pb[3].z), cx3, rr);
+        acc_b = __ffma2_rn(rb, cy[j], acc_b);
+        acc_g = __ffma2_rn(rg, cy[j], acc_g);
+        acc_r = __ffma2_rn(rr, cy[j], acc_r);
+    }
+    sa = make_float3(acc_b.x, acc_g.x, acc_r.x);
+    sb = make_float3(acc_b.y, acc_g.y, acc_r.y);
+}
+
 // render.wgsl:82-161 + gpu/pipeline.rs:10-34 (static rules) + keep_static.wgsl:21-32 + rgba_out.wgsl:9-17.
 // Plane offsets are 32-bit (a padded plane holds < 2^31 pixels; checked by render()).
-__global__ void __launch_bounds__(256) k_render(RenderArgs r) {
+__global__ void __launch_bounds__(256, 5) k_render(RenderArgs r) {
     pdl_wait();
     pdl_trigger();
     const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
@@ -1173,32 +1249,32 @@ __global__ void __launch_bounds__(256) k_render(RenderArgs r) {
     const uint2* RT = reinterpret_cast<const uint2*>(rt);
     const uint2 R00 = __ldg(RT + qr0 + qc0), R01 = __ldg(RT + qr0 + qc1), R10 = __ldg(RT + qr1 + qc0),
                 R11 = __ldg(RT + qr1 + qc1);
-    const __half* u00 = reinterpret_cast<const __half*>(&U00);
-    const __half* u01 = reinterpret_cast<const __half*>(&U01);
-    const __half* u10 = reinterpret_cast<const __half*>(&U10);
-    const __half* u11 = reinterpret_cast<const __half*>(&U11);
-    float f[4], v[3];
-#pragma unroll
-    for (int c = 0; c < 4; c++)
-        f[c] = bil_mix(h2f(u00[c]), h2f(u01[c]), h2f(u10[c]), h2f(u11[c]), qfx, qfy) * ((c & 1) == 0 ? r.fsx : r.fsy);
-#pragma unroll
-    for (int c = 0; c < 3; c++) v[c] = bil_mix(h2f(u00[4 + c]), h2f(u01[4 + c]), h2f(u10[4 + c]), h2f(u11[4 + c]), qfx, qfy) * 1.0f;
+    // channel pairs on float2 lanes: (flow 0, 1), (flow 2, 3), (vis 0, 1), (vis 2, R_t 2), (R_t 0, 1)
+    const float2 fs = make_float2(r.fsx, r.fsy);
+    const float2 f01 = __fmul2_rn(bil_mix2(h2x2(U00.x), h2x2(U01.x), h2x2(U10.x), h2x2(U11.x), qfx, qfy), fs);
+    const float2 f23 = __fmul2_rn(bil_mix2(h2x2(U00.y), h2x2(U01.y), h2x2(U10.y), h2x2(U11.y), qfx, qfy), fs);
+    const float2 v01 = bil_mix2(h2x2(U00.z), h2x2(U01.z), h2x2(U10.z), h2x2(U11.z), qfx, qfy);
+    auto lo2 = [](uint32_t a, uint32_t b) {  // the low halves of two words
+        return make_float2(__half2float(__ushort_as_half((unsigned short)(a & 0xffffu))),
+                           __half2float(__ushort_as_half((unsigned short)(b & 0xffffu))));
+    };
+    const float2 v2r2 = bil_mix2(lo2(U00.w, R00.y), lo2(U01.w, R01.y), lo2(U10.w, R10.y), lo2(U11.w, R11.y), qfx, qfy);
+    const float2 r01 = bil_mix2(h2x2(R00.x), h2x2(R01.x), h2x2(R10.x), h2x2(R11.x), qfx, qfy);
+    const float f[4] = {f01.x, f01.y, f23.x, f23.y}, v[3] = {v01.x, v01.y, v2r2.x};
     const float m = fmaxf(v[0], fmaxf(v[1], v[2]));
     const float e0 = expf(v[0] - m), e1 = expf(v[1] - m), e2 = expf(v[2] - m);
     const float s = e0 + e1 + e2;
     const float wa_w = (e0 + 0.5f * e2) / s, wb_w = (e1 + 0.5f * e2) / s;
     const float gxa = (float)x + f[0], gya = (float)y + f[1], gxb = (float)x + f[2], gyb = (float)y + f[3];
-    const bool cubic = r.cubic != 0;
-    const float3 sa3 = sample_frame(A, r.w, r.h, gxa, gya, cubic);
-    const float3 sb3 = sample_frame(B, r.w, r.h, gxb, gyb, cubic);
+    float3 sa3, sb3;
+    if (r.cubic) {
+        sample_pair(A, B, r.w, r.h, gxa, gya, gxb, gyb, sa3, sb3);
+    } else {
+        sa3 = sample_frame(A, r.w, r.h, gxa, gya, false);
+        sb3 = sample_frame(B, r.w, r.h, gxb, gyb, false);
+    }
     const float ca[3] = {sa3.x, sa3.y, sa3.z}, cb[3] = {sb3.x, sb3.y, sb3.z};
-    const __half* r00 = reinterpret_cast<const __half*>(&R00);
-    const __half* r01 = reinterpret_cast<const __half*>(&R01);
-    const __half* r10 = reinterpret_cast<const __half*>(&R10);
-    const __half* r11 = reinterpret_cast<const __half*>(&R11);
-    float cr[3];
-#pragma unroll
-    for (int c = 0; c < 3; c++) cr[c] = bil_mix(h2f(r00[c]), h2f(r01[c]), h2f(r10[c]), h2f(r11[c]), qfx, qfy);
+    const float cr[3] = {r01.x, r01.y, v2r2.y};
     float bwa = wa_w, bwb = wb_w, rk = 1.0f, stillw = 0.0f, own[3] = {0.0f, 0.0f, 0.0f};
     const float third = 1.0f / 3.0f;
     const int here = y * r.w + x;  // x < w, y < h: no clamp

@@ -30,7 +30,8 @@ int fh_session_cuda_stream(const FhSession* session, void** stream);
 
 /* The device buffer (width * height * 4 bytes, RGBA8) behind an input or output slot, for hosts whose frames already
  * live in device memory (write it on the session's stream, or synchronise first). Runs what a batched session has
- * queued first. 0 on success, -1 on error. */
+ * queued first. For an input slot the frame counts as rewritten: the next pair recomputes everything derived from it.
+ * 0 on success, -1 on error. */
 int fh_session_slot_device_ptr(const FhSession* session, uint32_t slot, int output, void** ptr);
 
 /* A frame already in device memory into an input slot (a device-to-device copy on the session's stream). */
