@@ -409,6 +409,7 @@ struct FhSession {
     // the batch graph for a batch whose oldest frame is the previous batch's newest: that frame's stage outputs are
     // already in entry nbat (carried there at the end of every batch), so its frame stage covers entries 0..nbat-1
     cudaGraphExec_t batch_graph_carry = nullptr;
+    std::map<int, cudaGraphExec_t> short_graphs;  // batches of 2 .. nbat - 1 intervals, by size
     const FrameSet* carried = nullptr;  // the frame whose outputs entry nbat holds, at generation carried_gen
     uint64_t carried_gen = 0;
     int batch_kernels = 0;
@@ -494,6 +495,7 @@ struct FhSession {
         for (auto& kv : pair_graphs) cudaGraphExecDestroy(kv.second);
         if (batch_graph) cudaGraphExecDestroy(batch_graph);
         if (batch_graph_carry) cudaGraphExecDestroy(batch_graph_carry);
+        for (auto& kv : short_graphs) cudaGraphExecDestroy(kv.second);
         for (auto& kv : mid_graphs) cudaGraphExecDestroy(kv.second);
         for (void* p : allocs) cudaFree(p);
         if (eng) eng->tensor_bytes -= std::min(eng->tensor_bytes, bytes);
@@ -1016,12 +1018,15 @@ struct FhSession {
         mid_ran = true;
     }
 
-    // Runs the queued intervals: a full chain of nbat intervals with mids as one batch, anything else one by one.
+    // Runs the queued intervals: a chain of two or more intervals, each with its mid, as one batch (a full one, or a
+    // shorter one when a call needs the results first), anything else one by one.
     void flush() {
         if (pend.empty()) return;
         std::vector<Pending> q;
         q.swap(pend);
-        if ((int)q.size() == nbat && q.back().mid) {
+        bool mids = true;
+        for (const Pending& x : q) mids = mids && x.mid;
+        if (q.size() >= 2 && mids) {
             run_batch(q);
             return;
         }
@@ -1060,45 +1065,46 @@ struct FhSession {
         cp(dst.f16, src.f16, src.f16_bs);
     }
 
-    // nbat chained intervals (q[i].b == q[i + 1].a) as one graph: the frames of times 0..nbat gathered into the arena
-    // (time t at entry nbat - t), the frame stage of all nbat + 1, the pairs and mids of all nbat (interval i at entry
-    // nbat - 1 - i), then the rendered frames scattered to their output slots in time order.
+    // m = 2 .. nbat chained intervals (q[i].b == q[i + 1].a) as one graph: the frames of times 0..m gathered into the
+    // arena (time t at entry m - t), the frame stage of all m + 1 (of m when entry m already holds the oldest frame's
+    // outputs), the pairs and mids of all m (interval i at entry m - 1 - i), then the rendered frames scattered to
+    // their output slots in time order.
     void run_batch(const std::vector<Pending>& q) {
-        const int n = nbat;
+        const int m = (int)q.size();
         const size_t fb = (size_t)w * h * 4;
-        for (int j = 0; j <= n; j++) {
-            FrameSet* f = j == 0 ? q[n - 1].b : q[n - j].a;
+        for (int j = 0; j <= m; j++) {
+            FrameSet* f = j == 0 ? q[m - 1].b : q[m - j].a;
             wait_upload(*f);
             CK(cudaMemcpyAsync(arena.frame + j * fb, f->frame, fb, cudaMemcpyDeviceToDevice, st));
         }
-        for (int j = 0; j <= n; j++) {
-            FrameSet* f = j == 0 ? q[n - 1].b : q[n - j].a;
+        for (int j = 0; j <= m; j++) {
+            FrameSet* f = j == 0 ? q[m - 1].b : q[m - j].a;
             CK(cudaEventRecord(f->released, st));
             f->ever_read = true;
         }
-        std::vector<float> tv(n);
-        for (int e = 0; e < n; e++) tv[e] = q[n - 1 - e].t;
-        CK(cudaMemcpyAsync(tdev, tv.data(), n * sizeof(float), cudaMemcpyHostToDevice, st));
-        // the oldest frame's stage outputs were carried into entry n by the previous batch when it is that batch's
-        // newest frame, unchanged since
-        const bool carry = carried == q[0].a && q[0].a->gen == carried_gen;
-        cudaGraphExec_t& g = carry ? batch_graph_carry : batch_graph;
+        std::vector<float> tv(m);
+        for (int e = 0; e < m; e++) tv[e] = q[m - 1 - e].t;
+        CK(cudaMemcpyAsync(tdev, tv.data(), m * sizeof(float), cudaMemcpyHostToDevice, st));
+        // a full batch's oldest frame's stage outputs were carried into entry nbat by the previous batch when it is
+        // that batch's newest frame, unchanged since
+        const bool carry = m == nbat && carried == q[0].a && q[0].a->gen == carried_gen;
+        cudaGraphExec_t& g = m < nbat ? short_graphs[m] : carry ? batch_graph_carry : batch_graph;
         if (!g) {
             const FView fa = arena_view(1), fbv = arena_view(0);
             g = capture(
                 [&] {
-                    run_frame(arena_view(0), carry ? n : n + 1);
-                    run_pair(fa, fbv, n);
-                    run_mid(PairSrc{fa, fbv}, arena_out, (long long)fb, n);
+                    run_frame(arena_view(0), carry ? m : m + 1);
+                    run_pair(fa, fbv, m);
+                    run_mid(PairSrc{fa, fbv}, arena_out, (long long)fb, m);
                     carry_newest();
                 },
                 &batch_kernels);
         }
         CK(cudaGraphLaunch(g, st));
-        carried = q[n - 1].b;
-        carried_gen = q[n - 1].b->gen;
-        for (int i = 0; i < n; i++) {
-            const int e = n - 1 - i;
+        carried = q[m - 1].b;
+        carried_gen = q[m - 1].b->gen;
+        for (int i = 0; i < m; i++) {
+            const int e = m - 1 - i;
             CK(cudaMemcpyAsync(outs[q[i].out], arena_out + e * fb, fb, cudaMemcpyDeviceToDevice, st));
             CK(cudaEventRecord(out_ready[q[i].out], st));
         }

@@ -18,8 +18,9 @@ extern "C" {
  * time. A call that observes or changes what queued intervals would produce first runs the queue, then carries on:
  * read_rgba of a slot a queued mid writes, the timed calls, warm_up, write_mask, advance_static, slot_device_ptr,
  * the debug tensors and the profile. So does a pair that does not continue the chain, or a second mid of one pair.
- * A queue shorter than `batch` runs one interval at a time. batch is 1..16; 1 is fh_session_create. FH_BATCH=<n> in
- * the environment sets the batch of fh_session_create. */
+ * A queue run before it is full runs as a shorter batch when it holds two or more intervals, each with its mid, else
+ * one interval at a time. batch is 1..16; 1 is fh_session_create. FH_BATCH=<n> in the environment sets the batch of
+ * fh_session_create. */
 FhSession* fh_session_create_batched(const FhEngine* engine, const FhModel* model, const FhSessionOptions* options,
                                      uint32_t batch);
 
