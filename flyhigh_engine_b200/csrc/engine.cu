@@ -355,8 +355,11 @@ struct FhSession {
     // Independent branches of a stage (the static age pass beside the network, the repair beside the upsample
     // weights, the render's frame plane beside the encoder) are issued on a second stream forked from and joined back
     // into st, so a captured stage graph holds them as parallel branches.
-    cudaStream_t side = nullptr;
+    cudaStream_t sides[4] = {};  // branch i runs on sides[i], so branches do not wait for one another
     cudaEvent_t fork_ev[4] = {}, join_ev[4] = {};
+    bool joined[4] = {};
+    // the pair's branches a batch graph joins later, where the mid first needs them (-1: none pending)
+    int pend_static = -1, pend_repair = -1;
     int branches = 0;  // forks of the stage being issued, all joined by join_branches()
     bool pdl_on = true;  // programmatic dependent launch inside the stage graphs (FH_PDL=0 turns it off)
     // launch priorities inside the stage graphs: the critical chain high, the side branches low (FH_PRIO=0: none)
@@ -450,13 +453,14 @@ struct FhSession {
     // issues body's launches on the side stream, after everything issued on st so far (inline while profiling, so
     // that every launch is timed alone)
     template <class F>
-    void branch(F&& body) {
-        if (prof || !side) {
+    int branch(F&& body) {
+        if (prof || !sides[0]) {
             body();
-            return;
+            return -1;
         }
         if (branches >= 4) fail("too many parallel branches in one stage");
         const int i = branches++;
+        cudaStream_t& side = sides[i];
         CK(cudaEventRecord(fork_ev[i], st));
         CK(cudaStreamWaitEvent(side, fork_ev[i], 0));
         std::swap(st, side);
@@ -469,15 +473,25 @@ struct FhSession {
         }
         std::swap(st, side);
         CK(cudaEventRecord(join_ev[i], side));
+        joined[i] = false;
+        return i;
+    }
+    // st waits for branch i (no-op for -1 or a branch already joined)
+    void join_branch(int i) {
+        if (i < 0 || joined[i]) return;
+        CK(cudaStreamWaitEvent(st, join_ev[i], 0));
+        joined[i] = true;
     }
     void join_branches() {
-        for (int i = 0; i < branches; i++) CK(cudaStreamWaitEvent(st, join_ev[i], 0));
+        for (int i = 0; i < branches; i++) join_branch(i);
         branches = 0;
+        pend_static = pend_repair = -1;
     }
 
     ~FhSession() {
         if (st) cudaStreamSynchronize(st);
-        if (side) cudaStreamSynchronize(side);
+        for (cudaStream_t sd : sides)
+            if (sd) cudaStreamSynchronize(sd);
         if (h2d) cudaStreamSynchronize(h2d);
         if (d2h) cudaStreamSynchronize(d2h);
         for (auto& fs : sets) {
@@ -499,7 +513,8 @@ struct FhSession {
         for (auto& kv : mid_graphs) cudaGraphExecDestroy(kv.second);
         for (void* p : allocs) cudaFree(p);
         if (eng) eng->tensor_bytes -= std::min(eng->tensor_bytes, bytes);
-        if (side) cudaStreamDestroy(side);
+        for (cudaStream_t sd : sides)
+            if (sd) cudaStreamDestroy(sd);
         if (h2d) cudaStreamDestroy(h2d);
         if (d2h) cudaStreamDestroy(d2h);
         if (st) cudaStreamDestroy(st);
@@ -789,11 +804,13 @@ struct FhSession {
 
     // A and B: the pair's sides, with equal strides. The static age pass walks the n pairs in time order: entry n - 1
     // first (a batch keeps its newest interval in entry 0), so its strides are negated.
-    void run_pair(const FView& A, const FView& B, int n) {
+    // defer: leave the static-pass and repair branches open for run_mid to join where it first needs them (one graph
+    // holding both stages); else both are joined before run_pair returns
+    void run_pair(const FView& A, const FView& B, int n, bool defer = false) {
         const long long P = (long long)hp * wp, CW = (long long)hp * fhk::changed_words(wp);
         // the static age pass and the still test's plane read the two frames only: a branch beside the network
         if (protects || still)
-            branch([&] {
+            pend_static = branch([&] {
                 CK(fhk::pair_planes(A.frame, B.frame, A.frame_bs, sargs, protects ? changed : nullptr, CW,
                                     still ? dsum : nullptr, P, n, st));
                 mark("pair_planes");
@@ -840,7 +857,7 @@ struct FhSession {
         // the repair rewrites the flow; the convex-upsample weights depend on h only (graph op 62: conv up.w of h),
         // so the two run side by side
         if (repair > 0)
-            branch([&] {
+            pend_repair = branch([&] {
                 fhk::GmArgs g{fv, efv, h8, w8, A.A, B.A, A.A_bs, NH, NW, hc, wc, r_blk, r_dwin, delta, dmin, coef, maps, tmp};
                 CK(fhk::gmhs_fit(g, n, st));
                 mark("gmhs fit");
@@ -850,7 +867,7 @@ struct FhSession {
                 mark("gmhs select");
             });
         conv("up", {{fr3, efr}}, h8, w8, {wt36, ewt}, 40, n);
-        join_branches();
+        if (!defer) join_branches();
     }
 
     void run_mid(const PairSrc& p, uint8_t* out, long long out_bs, int n) {
@@ -862,6 +879,7 @@ struct FhSession {
         conv("fh1", {{hm, efr}}, h8, w8, {fh1, efr}, CRP, n);
         conv("fh2", {{fh1, efr}}, h8, w8, {fh2, efr}, CRP, n);
         conv("fout", {{fh2, efr}}, h8, w8, {dfilm, e8}, 8, n);
+        join_branch(pend_repair);  // the repaired flow
         CK(fhk::mid_combine(tdev, fv, e8, dfilm, e8, ftvt, e8, h8, w8, n, st));
         mark("mid_combine");
         CK(fhk::convex_up(wt36, 40, ewt, ftvt, e8, h8, w8, up7, eup, n, st));
@@ -876,8 +894,10 @@ struct FhSession {
         fhk::RenderArgs ra{p.a.half, p.b.half, p.a.half_bs, w, h, hp, wp, up7, eup, rt, ert, qh, qw, fsx, fsy,
                            cubic ? 1 : 0, (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, P, dsum,
                            nearp, P, min_age, out, out_bs};
+        join_branch(pend_static);  // the static planes
         CK(fhk::render(ra, n, st));
         mark("render");
+        join_branches();
     }
 
     template <class F>
@@ -1094,7 +1114,7 @@ struct FhSession {
             g = capture(
                 [&] {
                     run_frame(arena_view(0), carry ? m : m + 1);
-                    run_pair(fa, fbv, m);
+                    run_pair(fa, fbv, m, true);
                     run_mid(PairSrc{fa, fbv}, arena_out, (long long)fb, m);
                     carry_newest();
                 },
@@ -1394,7 +1414,7 @@ FhSession* session_new(FhEngine* e, const FhModel* m, const FhSessionOptions& o,
     CK(cudaSetDevice(e->device));
     CK(cudaDeviceGetStreamPriorityRange(&s->prio_lo, &s->prio_hi));
     CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
-    CK(cudaStreamCreateWithFlags(&s->side, cudaStreamNonBlocking));
+    for (cudaStream_t& sd : s->sides) CK(cudaStreamCreateWithFlags(&sd, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&s->h2d, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&s->d2h, cudaStreamNonBlocking));
     for (int i = 0; i < 4; i++) {
