@@ -301,6 +301,18 @@ def main():
         total = sum(prof.values())
         for k, v in sorted(prof.items(), key=lambda x: -x[1]):
             print(f"# {v * 1000:8.1f} us {100 * v / total:5.1f}%  {k}", file=sys.stderr)
+    # the fast render + linear_t session (texbench's configuration): device ms of one pair and of one further phase
+    fast = None
+    if not args.no_e2e:
+        sf = fh.Session(engine, model, W, H, fast_render=True, linear_t=True)
+        fs = [sf.add_input(), sf.add_input()]
+        fo = sf.add_output()
+        sf.write(fs[0], frames[0])
+        sf.write(fs[1], frames[1])
+        sf.pair(fs[0], fs[1])
+        sf.mid(0.5, fo)
+        fast = {"pair_ms": sf.pair_timed(fs[0], fs[1]), "mid_ms": sf.mid_timed(0.25, fo)}
+        del sf
     cpu = None
     if rank == 0 and ws == 1:
         fps_cpu, dt = cpu_baseline(model_dir, frames, args.cpu_sample)
@@ -320,7 +332,7 @@ def main():
                            "batch": args.batch, "pair_ms": pair_ms, "mid_ms": mid_ms},
                 "gpu_launches": per_interval_launches * gen_per_rank + counts["frame"],
                 "clocks": clk.summary(), "roofline": roof, "roofline_conv": roof_conv, "cpu_baseline": cpu,
-                "e2e": e2e, "kernel_ms": {k: round(v, 5) for k, v in sorted(prof.items(), key=lambda x: -x[1])[:12]}}
+                "e2e": e2e, "fast_render_linear_t": fast, "kernel_ms": {k: round(v, 5) for k, v in sorted(prof.items(), key=lambda x: -x[1])[:12]}}
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.barrier()

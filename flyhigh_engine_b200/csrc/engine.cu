@@ -343,6 +343,11 @@ struct FhSession {
     // sizes (net/build.rs:548-550, session_ext.rs:100)
     int w, h, wp, hp, iw, ih, ihp, iwp, NH, NW, qh, qw, h8, w8, h16, w16, hc, wc;
     bool internal = false, protects = false, cubic = false, still = true, decisive = false;
+    // fast render (net/session_ext.rs:194-443): the network input by tex_down, the age pass and the render on the
+    // frames' rgba8 texels; linear_t: the mid network once per pair at t = 0.5, each phase a render of those maps
+    bool fast = false, linear = false;
+    bool maps_done = false;  // linear_t: the current pair's maps are computed
+    float* tnet = nullptr;   // linear_t: the network's phase, 0.5 for every entry
     int k = 1, repair = 1;
     float min_age = 0, fsx = 1, fsy = 1;
     int r_blk = 1, r_dwin = 1;
@@ -693,11 +698,11 @@ struct FhSession {
         if (protects) {
             changed = alloc_n<uint32_t>((size_t)nb * hp * fhk::changed_words(wp));
             spread = alloc_n<uint32_t>(256);
-            CK(fhk::spread_table(spread, st));
+            CK(fhk::spread_table(spread, st, fast));
             mask = alloc_n<uint8_t>((size_t)hp * wp);
             state = alloc_n<uchar4>((size_t)hp * wp);
             age = alloc_n<int16_t>((size_t)nb * hp * wp);
-            nearp = alloc_n<uint8_t>((size_t)nb * hp * wp);
+            if (!fast) nearp = alloc_n<uint8_t>((size_t)nb * hp * wp);
         }
         if (still) dsum = alloc_n<float>((size_t)nb * hp * wp);
         cv = img(h16, w16, 56, nb);
@@ -717,6 +722,12 @@ struct FhSession {
         maps = alloc_n<float>((size_t)6 * hc * wc * nb);
         tmp = alloc_n<float>((size_t)5 * hc * wc * nb);
         tdev = alloc_n<float>(nb);
+        if (linear) {
+            tnet = alloc_n<float>(nb);
+            std::vector<float> half_t(nb, 0.5f);
+            CK(cudaMemcpyAsync(tnet, half_t.data(), nb * sizeof(float), cudaMemcpyHostToDevice, st));
+            CK(cudaStreamSynchronize(st));
+        }
         hm = img(h8, w8, CRP, nb);
         fh1 = img(h8, w8, CRP, nb);
         fh2 = img(h8, w8, CRP, nb);
@@ -784,11 +795,13 @@ struct FhSession {
     void run_frame(const FView& v, int n) {
         __half* A = const_cast<__half*>(v.A);
         __half* half = const_cast<__half*>(v.half);
-        branch([&] {
-            CK(fhk::frame_half(v.frame, v.frame_bs, w, h, half, v.half_bs, n, st));
-            mark("frame_half");
-        });
-        CK(fhk::frame_to_input(v.frame, v.frame_bs, w, h, hp, wp, internal, ihp, iwp, {A, v.A_bs}, n, st, aa_fx, aa_fy));
+        if (!fast)  // the fast render samples the rgba8 frames themselves
+            branch([&] {
+                CK(fhk::frame_half(v.frame, v.frame_bs, w, h, half, v.half_bs, n, st));
+                mark("frame_half");
+            });
+        CK(fhk::frame_to_input(v.frame, v.frame_bs, w, h, hp, wp, internal, ihp, iwp, {A, v.A_bs}, n, st, aa_fx, aa_fy,
+                               fast));
         mark("frame_to_input");
         CK(fhk::input_pyramid({A, v.A_bs}, NH, NW, {const_cast<__half*>(v.aq), v.aq_bs},
                               {const_cast<__half*>(v.i8), v.i8_bs}, {const_cast<__half*>(v.i16), v.i16_bs}, n, st,
@@ -819,8 +832,10 @@ struct FhSession {
                     CK(fhk::static_age(A.frame + l * A.frame_bs, B.frame + l * B.frame_bs, -A.frame_bs, changed + l * CW,
                                        -CW, mask, sargs, state, age + l * P, -P, n, spread, st));
                     mark("static_age");
-                    CK(fhk::static_near(age, P, wp, hp, min_age, nearp, n, st));
-                    mark("static_near");
+                    if (!fast) {  // the fast render probes the age plane itself
+                        CK(fhk::static_near(age, P, wp, hp, min_age, nearp, n, st));
+                        mark("static_near");
+                    }
                 }
             });
         const long long ecv = E(h16, w16, 56), ecc = E(h16, w16, CCP), eob = E(h16, w16, 16), efv = E(h8, w8, 8),
@@ -870,17 +885,44 @@ struct FhSession {
         if (!defer) join_branches();
     }
 
-    void run_mid(const PairSrc& p, uint8_t* out, long long out_bs, int n) {
-        const long long P = (long long)hp * wp, efr = E(h8, w8, CRP), e8 = E(h8, w8, 8), ewt = E(h8, w8, 40),
-                        eup = E(qh, qw, 8), erx = E(qh, qw, 16), erq = E(qh, qw, CQP), ert = E(qh, qw, 4);
-        fhk::FilmArgs fa{tdev, film_w1, film_b1, film_w2, film_b2, film_hidden, cr, fr3, CRP, efr, hm, CRP, efr, h8, w8};
+    // parts: bit 0 the mid network (FiLM .. R_t: the maps), bit 1 the render. With linear_t the network runs at t = 0.5
+    // (tnet) and the render scales by the entry's t (tdev).
+    void run_mid(const PairSrc& p, uint8_t* out, long long out_bs, int n, int parts = 3) {
+        const long long P = (long long)hp * wp, eup = E(qh, qw, 8), ert = E(qh, qw, 4);
+        if (parts & 1) run_mid_maps(p, n);
+        if (!(parts & 2)) {
+            join_branches();
+            return;
+        }
+        join_branch(pend_static);  // the static planes
+        if (fast) {
+            fhk::RenderTexArgs ra{p.a.frame, p.b.frame, p.a.frame_bs, w, h, hp, wp, up7, eup, rt, ert, qh, qw, fsx, fsy,
+                                  cubic ? 1 : 0, (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, P,
+                                  min_age, dsum, P, tdev, linear ? 1 : 0, out, out_bs};
+            CK(fhk::render_tex(ra, n, st));
+            mark("render_tex");
+        } else {
+            fhk::RenderArgs ra{p.a.half, p.b.half, p.a.half_bs, w, h, hp, wp, up7, eup, rt, ert, qh, qw, fsx, fsy,
+                               cubic ? 1 : 0, (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, P, dsum,
+                               nearp, P, min_age, out, out_bs};
+            CK(fhk::render(ra, n, st));
+            mark("render");
+        }
+        join_branches();
+    }
+
+    void run_mid_maps(const PairSrc& p, int n) {
+        const long long efr = E(h8, w8, CRP), e8 = E(h8, w8, 8), ewt = E(h8, w8, 40), eup = E(qh, qw, 8),
+                        erx = E(qh, qw, 16), erq = E(qh, qw, CQP), ert = E(qh, qw, 4);
+        const float* tn = linear ? tnet : tdev;  // the network's phase
+        fhk::FilmArgs fa{tn, film_w1, film_b1, film_w2, film_b2, film_hidden, cr, fr3, CRP, efr, hm, CRP, efr, h8, w8};
         CK(fhk::film(fa, n, st));
         mark("film");
         conv("fh1", {{hm, efr}}, h8, w8, {fh1, efr}, CRP, n);
         conv("fh2", {{fh1, efr}}, h8, w8, {fh2, efr}, CRP, n);
         conv("fout", {{fh2, efr}}, h8, w8, {dfilm, e8}, 8, n);
         join_branch(pend_repair);  // the repaired flow
-        CK(fhk::mid_combine(tdev, fv, e8, dfilm, e8, ftvt, e8, h8, w8, n, st));
+        CK(fhk::mid_combine(tn, fv, e8, dfilm, e8, ftvt, e8, h8, w8, n, st));
         mark("mid_combine");
         CK(fhk::convex_up(wt36, 40, ewt, ftvt, e8, h8, w8, up7, eup, n, st));
         mark("convex_up");
@@ -891,13 +933,6 @@ struct FhSession {
         conv("q2", {{rq1, erq}}, qh, qw, {rq2, erq}, CQP, n);
         conv("q3", {{rq2, erq}}, qh, qw, {rq3, erq}, CQP, n);
         conv("q4", {{rq3, erq}}, qh, qw, {rt, ert}, 4, n, {nullptr, 0}, 0, 1);
-        fhk::RenderArgs ra{p.a.half, p.b.half, p.a.half_bs, w, h, hp, wp, up7, eup, rt, ert, qh, qw, fsx, fsy,
-                           cubic ? 1 : 0, (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, P, dsum,
-                           nearp, P, min_age, out, out_bs};
-        join_branch(pend_static);  // the static planes
-        CK(fhk::render(ra, n, st));
-        mark("render");
-        join_branches();
     }
 
     template <class F>
@@ -987,6 +1022,7 @@ struct FhSession {
         mark_read(A, B);
         pair = PairSrc{view_of(A), view_of(B), &A, &B};
         have_pair = true;
+        maps_done = false;
     }
 
     void do_pair(uint32_t a, uint32_t b) {
@@ -1005,16 +1041,29 @@ struct FhSession {
         pair_now(A, B);
     }
 
-    cudaGraphExec_t mid_graph(uint32_t out) {
-        auto key = std::make_tuple(pair.a.key, pair.b.key, (const void*)nullptr, (const void*)nullptr,
-                                   (const void*)outs[out]);
+    // the mid of the current pair into output slot `out`: parts as run_mid's (3 whole, 1 the maps, 2 the render)
+    cudaGraphExec_t mid_graph(uint32_t out, int parts = 3) {
+        uint8_t* o = parts == 1 ? nullptr : outs[out];
+        auto key = std::make_tuple(pair.a.key, pair.b.key, (const void*)(intptr_t)parts, (const void*)nullptr,
+                                   (const void*)o);
         auto it = mid_graphs.find(key);
         if (it == mid_graphs.end()) {
             PairSrc p = pair;
-            uint8_t* o = outs[out];
-            it = mid_graphs.emplace(key, capture([&] { run_mid(p, o, 0, 1); }, &mid_kernels)).first;
+            it = mid_graphs.emplace(key, capture([&] { run_mid(p, o, 0, 1, parts); }, &mid_kernels)).first;
         }
         return it->second;
+    }
+    // one mid of the current pair, t already in tdev[0]: with linear_t the maps once per pair, then the render
+    void launch_mid(uint32_t out) {
+        if (linear) {
+            if (!maps_done) {
+                CK(cudaGraphLaunch(mid_graph(out, 1), st));
+                maps_done = true;
+            }
+            CK(cudaGraphLaunch(mid_graph(out, 2), st));
+        } else {
+            CK(cudaGraphLaunch(mid_graph(out), st));
+        }
     }
 
     void do_mid(float t, uint32_t out) {
@@ -1030,9 +1079,8 @@ struct FhSession {
         }
         flush();  // a further mid of the last queued pair: that pair has run by now
         if (!have_pair) fail("pair two input slots first");
-        cudaGraphExec_t g = mid_graph(out);
         CK(fhk::set_scalar(tdev, t, st));
-        CK(cudaGraphLaunch(g, st));
+        launch_mid(out);
         if (pair.sa) mark_read(*pair.sa, *pair.sb);
         CK(cudaEventRecord(out_ready[out], st));
         mid_ran = true;
@@ -1055,9 +1103,8 @@ struct FhSession {
             for (const Pending& x : q) {
                 pair_now(*x.a, *x.b);
                 if (x.mid) {
-                    cudaGraphExec_t g = mid_graph(x.out);
                     CK(fhk::set_scalar(tdev, x.t, st));
-                    CK(cudaGraphLaunch(g, st));
+                    launch_mid(x.out);
                     mark_read(*x.a, *x.b);
                     CK(cudaEventRecord(out_ready[x.out], st));
                     mid_ran = true;
@@ -1133,6 +1180,7 @@ struct FhSession {
         for (FView* v : {&a0, &b0}) v->frame_bs = v->half_bs = v->A_bs = v->aq_bs = v->i8_bs = v->i16_bs = v->f8_bs = v->f16_bs = 0;
         pair = PairSrc{a0, b0, nullptr, nullptr};
         have_pair = true;
+        maps_done = true;  // with linear_t the batch computed the newest pair's maps at t = 0.5
         mid_ran = true;
         batches_run++;
     }
@@ -1228,6 +1276,7 @@ struct FhSession {
         B.feat_gen = B.gen;
         pair = PairSrc{view_of(A), view_of(B), &A, &B};
         have_pair = true;
+        maps_done = true;
         std::string js = "[";
         for (size_t i = 1; i < marks.size(); i++) {
             float ms = 0;
@@ -1343,7 +1392,6 @@ void derive(const FhModel* m, const FhSessionOptions& o, FhSession* s) {
     if (o.keep_static && o.static_frames > 255) fail("static_protection: frames %u is not 1..=255", o.static_frames);
     if (o.keep_static && o.static_tolerance > 255) fail("static_protection: tolerance %u is above 255", o.static_tolerance);
     if (o.linear_t && !o.fast_render) fail("linear_t: needs fast_render");
-    if (o.fast_render) fail("fast_render: the texture-sampled render is not part of this build");
     if (m->fingerprint != kFlyHighFgGraph)
         fail("graph.json: not the FlyHighFG v1 graph this engine plans (fingerprint %016llx)", (unsigned long long)m->fingerprint);
     s->model = m;
@@ -1383,9 +1431,11 @@ void derive(const FhModel* m, const FhSessionOptions& o, FhSession* s) {
     s->protects = keep_static || o.protection_mask;
     const int frames = keep_static ? std::clamp((int)(o.static_frames ? o.static_frames : 8), 1, 255) : 2;
     s->min_age = (float)frames;
+    s->fast = o.fast_render != 0;
+    s->linear = s->fast && o.linear_t != 0;
     s->sargs = fhk::StaticArgs{s->w, s->h, s->wp, s->hp,
                                keep_static ? ((float)std::min((int)o.static_tolerance, 255) + 0.5f) / 255.0f : 0.0f,
-                               (float)frames, (int)o.protection_mask};
+                               (float)frames, (int)o.protection_mask, s->fast ? 1 : 0};
     s->fsx = (float)s->wp / (float)s->NW;
     s->fsy = (float)s->hp / (float)s->NH;
     // gmhs.rs:160-170 (DS = 2)
@@ -1765,10 +1815,11 @@ int fh_session_report_json(const FhSession* s, char* buf, size_t cap) {
         char b[1024];
         snprintf(b, sizeof b,
                  "{\"width\":%d,\"height\":%d,\"internal_width\":%d,\"internal_height\":%d,\"k\":%d,\"repair\":%d,"
-                 "\"render\":\"%s\",\"fast_render\":false,\"linear_t\":false,\"static_protection\":%s,"
+                 "\"render\":\"%s\",\"fast_render\":%s,\"linear_t\":%s,\"static_protection\":%s,"
                  "\"protection_mask\":%s,\"inputs\":%zu,\"outputs\":%zu,\"pair_steps\":%d,\"mid_steps\":%d,"
                  "\"frame_steps\":%d,\"tensor_bytes\":%zu}",
-                 s->w, s->h, s->iw, s->ih, s->k, s->repair, s->cubic ? "bicubic" : "bilinear", sp,
+                 s->w, s->h, s->iw, s->ih, s->k, s->repair, s->cubic ? "bicubic" : "bilinear", s->fast ? "true" : "false",
+                 s->linear ? "true" : "false", sp,
                  s->o.protection_mask ? "true" : "false", s->ins.size(), s->outs.size(), s->pair_kernels, s->mid_kernels,
                  s->frame_kernels, s->bytes);
         return write_json(b, buf, cap);

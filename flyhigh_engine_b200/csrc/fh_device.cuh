@@ -25,6 +25,8 @@ FH_DEV int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v
 
 // rgba8 byte -> the value the reference's tex_in / rgba_in store: f16(byte / 255) (tex_in.wgsl:14-18)
 FH_DEV float u8v(uint32_t b) { return rh((float)b / 255.0f); }
+// the texel of an rgba8unorm texture, as the fast render path samples its source frames: k / 255 in f32
+FH_DEV float texv(uint32_t b) { return (float)b / 255.0f; }
 
 struct ViewC {  // const NHWC view
     const __half* p;

@@ -66,9 +66,11 @@ __global__ void k_aa_axis(int in, int out, int* first, int* count, float* w) {
 // tex_in.wgsl:10-19 + interp.wgsl:29-43 (aa): the padded plane is never stored; taps read the rgba8 frame at the
 // clamped position (replicate padding). With axis tables the weights are read, not formed per tap.
 __global__ void k_frame_to_input(const uint8_t* __restrict__ frames, long long frame_bs, int w, int h, int hp, int wp,
-                                 int internal, int oh, int ow, __half* out, long long out_bs, AaAxis ax, AaAxis ay) {
+                                 int internal, int oh, int ow, __half* out, long long out_bs, AaAxis ax, AaAxis ay,
+                                 int tex) {
     __shared__ float lut[256];
-    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
+    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y)
+        lut[i] = tex ? texv(i) : u8v(i);
     __syncthreads();
     pdl_wait();
     pdl_trigger();
@@ -243,7 +245,8 @@ __global__ void __launch_bounds__(256) k_pair_planes(const uint8_t* __restrict__
                                                      long long frame_bs, StaticArgs s, uint32_t* changed,
                                                      long long changed_bs, float* dsum, long long dsum_bs) {
     __shared__ float lut[256];
-    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = u8v(i);
+    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y)
+        lut[i] = s.tex ? texv(i) : u8v(i);
     __syncthreads();
     pdl_wait();
     pdl_trigger();
@@ -268,7 +271,12 @@ __global__ void __launch_bounds__(256) k_pair_planes(const uint8_t* __restrict__
         const uint32_t word = __ballot_sync(0xffffffffu, in && dm >= s.thr);
         if (threadIdx.x == 0) changed[n * changed_bs + (long long)y * ((s.wp + 31) >> 5) + blockIdx.x] = word;
     }
-    if (dsum && in) dsum[n * dsum_bs + (long long)y * s.wp + x] = (d[0] + d[1]) + d[2];
+    if (dsum && in) {
+        // the fast render's still-test term instead: dot(|A - B|.rgb, 1 / 3), R first (render_tex.wgsl:93-98)
+        const float third = 1.0f / 3.0f;
+        dsum[n * dsum_bs + (long long)y * s.wp + x] = s.tex ? d[2] * third + d[1] * third + d[0] * third
+                                                             : (d[0] + d[1]) + d[2];
+    }
 }
 
 // render_static's on_static (gpu/pipeline.rs:10-34) per pixel: an age >= min_age in the clamped 3 x 3 neighbourhood.
@@ -319,10 +327,10 @@ FH_DEV uint32_t bit_window(const uint32_t* __restrict__ row, int ww, int W, int 
 // The spread test per channel, v(q) - v(o) >= 0.03 or v(o) - v(q) >= 0.03 in f32 (v = the byte -> value table), as
 // byte thresholds per o: the first q above o and the last q below o that pass (both differences are monotone in q).
 // Low half: the upper threshold - 1 (255: none, as no byte exceeds it), high half: the lower threshold + 1 (0: none).
-__global__ void k_spread_table(uint32_t* out) {
+__global__ void k_spread_table(uint32_t* out, int tex) {
     __shared__ float lut[256];
     const int o = threadIdx.x;
-    lut[o] = u8v(o);
+    lut[o] = tex ? texv(o) : u8v(o);
     __syncthreads();
     int hi = o;
     while (hi < 256 && !(lut[hi] - lut[o] >= 0.03f)) hi++;
@@ -1352,6 +1360,167 @@ __global__ void __launch_bounds__(256, 5) k_render(RenderArgs r) {
     reinterpret_cast<uint32_t*>(r.out + (long long)n * r.out_bs)[here] = q[2] | (q[1] << 8) | (q[0] << 16) | 0xff000000u;
 }
 
+// ---------------------------------------------------------------------------------------------- fast render ----
+
+// one rgba8 texel as (R, G, B) through the k / 255 table
+FH_DEV float3 texel3(const uint32_t* __restrict__ f, int i, const float* lut) {
+    const uint32_t v = __ldg(f + i);
+    return make_float3(lut[v & 255], lut[(v >> 8) & 255], lut[(v >> 16) & 255]);
+}
+
+// render_tex.wgsl:53-64 sample(): Keys bicubic (a = -0.75) with per-tap clamp to the frame, or the bilinear filter
+// between the four neighbours (edges clamped); the row and column sums in the shader's order, unfused
+FH_DEV float3 sample_tex(const uint32_t* __restrict__ f, int w, int h, float gx, float gy, bool cubic, const float* lut) {
+    const int px = (int)floorf(gx), py = (int)floorf(gy);
+    if (cubic) {
+        const float tx = gx - (float)px, ty = gy - (float)py;
+        const float cx0 = cub2(tx + 1.0f), cx1 = cub1(tx), cx2 = cub1(1.0f - tx), cx3 = cub2(2.0f - tx);
+        const float cy[4] = {cub2(ty + 1.0f), cub1(ty), cub1(1.0f - ty), cub2(2.0f - ty)};
+        const bool inner = px >= 1 && px + 2 <= w - 1 && py >= 1 && py + 2 <= h - 1;
+        const int x0 = inner ? px - 1 : clampi(px - 1, 0, w - 1), x1 = inner ? px : clampi(px, 0, w - 1),
+                  x2 = inner ? px + 1 : clampi(px + 1, 0, w - 1), x3 = inner ? px + 2 : clampi(px + 2, 0, w - 1);
+        float3 acc = make_float3(0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int row = (inner ? py - 1 + j : clampi(py - 1 + j, 0, h - 1)) * w;
+            const float3 t0 = texel3(f, row + x0, lut), t1 = texel3(f, row + x1, lut), t2 = texel3(f, row + x2, lut),
+                         t3 = texel3(f, row + x3, lut);
+            const float3 r = make_float3(t0.x * cx0 + t1.x * cx1 + t2.x * cx2 + t3.x * cx3,
+                                         t0.y * cx0 + t1.y * cx1 + t2.y * cx2 + t3.y * cx3,
+                                         t0.z * cx0 + t1.z * cx1 + t2.z * cx2 + t3.z * cx3);
+            if (j == 0) acc = make_float3(r.x * cy[0], r.y * cy[0], r.z * cy[0]);
+            else acc = make_float3(acc.x + r.x * cy[j], acc.y + r.y * cy[j], acc.z + r.z * cy[j]);
+        }
+        return acc;
+    }
+    const float ax = gx - (float)px, ay = gy - (float)py;
+    const int x0 = clampi(px, 0, w - 1), x1 = clampi(px + 1, 0, w - 1);
+    const int r0 = clampi(py, 0, h - 1) * w, r1 = clampi(py + 1, 0, h - 1) * w;
+    const float3 p00 = texel3(f, r0 + x0, lut), p01 = texel3(f, r0 + x1, lut), p10 = texel3(f, r1 + x0, lut),
+                 p11 = texel3(f, r1 + x1, lut);
+    return make_float3(bil_mix(p00.x, p01.x, p10.x, p11.x, ax, ay), bil_mix(p00.y, p01.y, p10.y, p11.y, ax, ay),
+                       bil_mix(p00.z, p01.z, p10.z, p11.z, ax, ay));
+}
+
+// render_tex.wgsl:70-120: the fast render. Flow, visibility and residual from the quarter-resolution maps, both frames
+// sampled as rgba8 textures (texels k / 255), the linear-t scales (sa, sb, sr) of the entry's phase, the still test
+// over the frames' own 3 x 3 texels, the static rules on the age plane (3 x 3 around the rounded sample, clamped to the
+// frame) and the keep ramp; written as rgba8.
+__global__ void __launch_bounds__(256) k_render_tex(RenderTexArgs r) {
+    __shared__ float lut[256];
+    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = texv(i);
+    __syncthreads();
+    pdl_wait();
+    pdl_trigger();
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
+    if (x >= r.w || y >= r.h) return;
+    const int w = r.w, h = r.h, hq = r.hq, wq = r.wq;
+    const uint32_t* __restrict__ A = reinterpret_cast<const uint32_t*>(r.fa + (long long)n * r.f_bs);
+    const uint32_t* __restrict__ B = reinterpret_cast<const uint32_t*>(r.fb + (long long)n * r.f_bs);
+    const int16_t* age = r.age ? r.age + (long long)n * r.age_bs : nullptr;
+    float sa = 1.0f, sb = 1.0f, sr = 1.0f;
+    if (r.linear) {  // net/session_ext.rs:273-276
+        const float t = r.t[n];
+        sa = 2.0f * t;
+        sb = 2.0f * (1.0f - t);
+        sr = 1.0f - fabsf(2.0f * t - 1.0f);
+    }
+    const float iy = ((float)y + 0.5f) * (float)hq / (float)r.hp - 0.5f, ix = ((float)x + 0.5f) * (float)wq / (float)r.wp - 0.5f;
+    const int qy0 = (int)floorf(iy), qx0 = (int)floorf(ix);
+    const float fy = iy - (float)qy0, fx = ix - (float)qx0;
+    const int qr0 = clampi(qy0, 0, hq - 1) * wq, qr1 = clampi(qy0 + 1, 0, hq - 1) * wq;
+    const int qc0 = clampi(qx0, 0, wq - 1), qc1 = clampi(qx0 + 1, 0, wq - 1);
+    const uint4* U = reinterpret_cast<const uint4*>(r.up7 + (long long)n * r.up_bs);
+    const uint4 U00 = __ldg(U + qr0 + qc0), U01 = __ldg(U + qr0 + qc1), U10 = __ldg(U + qr1 + qc0),
+                U11 = __ldg(U + qr1 + qc1);
+    const uint2* RT = reinterpret_cast<const uint2*>(r.rt + (long long)n * r.rt_bs);
+    const uint2 R00 = __ldg(RT + qr0 + qc0), R01 = __ldg(RT + qr0 + qc1), R10 = __ldg(RT + qr1 + qc0),
+                R11 = __ldg(RT + qr1 + qc1);
+    const float2 f01 = bil_mix2(h2x2(U00.x), h2x2(U01.x), h2x2(U10.x), h2x2(U11.x), fx, fy);
+    const float2 f23 = bil_mix2(h2x2(U00.y), h2x2(U01.y), h2x2(U10.y), h2x2(U11.y), fx, fy);
+    const float2 v01 = bil_mix2(h2x2(U00.z), h2x2(U01.z), h2x2(U10.z), h2x2(U11.z), fx, fy);
+    auto lo = [](uint32_t a) { return __half2float(__ushort_as_half((unsigned short)(a & 0xffffu))); };
+    const float v2 = bil_mix(lo(U00.w), lo(U01.w), lo(U10.w), lo(U11.w), fx, fy);
+    const float2 r01 = bil_mix2(h2x2(R00.x), h2x2(R01.x), h2x2(R10.x), h2x2(R11.x), fx, fy);
+    const float r2 = bil_mix(lo(R00.y), lo(R01.y), lo(R10.y), lo(R11.y), fx, fy);
+    const float gxa = (float)x + f01.x * r.fsx * sa, gya = (float)y + f01.y * r.fsy * sa;
+    const float gxb = (float)x + f23.x * r.fsx * sb, gyb = (float)y + f23.y * r.fsy * sb;
+    const float m = fmaxf(v01.x, fmaxf(v01.y, v2));
+    const float e0 = expf(v01.x - m), e1 = expf(v01.y - m), e2 = expf(v2 - m), s = e0 + e1 + e2;
+    float wa = (e0 + 0.5f * e2) / s * (2.0f - sa), wb = (e1 + 0.5f * e2) / s * (2.0f - sb);
+    const float wn = fmaxf(wa + wb, 1e-6f);
+    wa = wa / wn;
+    wb = wb / wn;
+    float r_k = sr, raw = 0.0f;
+    const bool cubic = r.cubic != 0;
+    const float3 ca = sample_tex(A, w, h, gxa, gya, cubic, lut), cb = sample_tex(B, w, h, gxb, gyb, cubic, lut);
+    const float third = 1.0f / 3.0f;
+    auto dot3 = [&](float a0, float a1, float a2) { return a0 * third + a1 * third + a2 * third; };
+    const float dab = dot3(fabsf(ca.x - cb.x), fabsf(ca.y - cb.y), fabsf(ca.z - cb.z));
+    const float3 ph = texel3(A, y * w + x, lut), pbh = texel3(B, y * w + x, lut);
+    const float3 own = make_float3(0.5f * (ph.x + pbh.x), 0.5f * (ph.y + pbh.y), 0.5f * (ph.z + pbh.z));
+    float stillw = 0.0f;
+    if (r.flags & 2u) {
+        // the nine per-texel terms dot(|A - B|, 1 / 3) of pair_planes, summed in the shader's order
+        const float* __restrict__ et = r.es + (long long)n * r.es_bs;
+        float es = 0.0f;
+#pragma unroll
+        for (int dy = -1; dy <= 1; dy++)
+#pragma unroll
+            for (int dx = -1; dx <= 1; dx++) es += __ldg(et + clampi(y + dy, 0, h - 1) * r.wp + clampi(x + dx, 0, w - 1));
+        es = es / 9.0f;
+        stillw = fminf(fmaxf((dab - es) / 0.04f, 0.0f), 1.0f) * (es < 0.03f ? 1.0f : 0.0f);
+    }
+    if (r.flags & 1u) {
+        const float k = fminf(fmaxf((dab - 0.04f) / 0.08f, 0.0f), 1.0f);
+        const float pa = wa >= wb ? 1.0f : 0.0f;
+        wa = wa * (1.0f - k) + pa * k;
+        wb = wb * (1.0f - k) + (1.0f - pa) * k;
+        r_k = r_k * (1.0f - k);
+    }
+    float kk = 0.0f;
+    if (age) {
+        auto on_static = [&](float gx, float gy) {
+            const int cx = (int)rintf(gx), cy = (int)rintf(gy);  // WGSL round(): half to even
+            bool hit = false;
+#pragma unroll
+            for (int dy = -1; dy <= 1; dy++)
+#pragma unroll
+                for (int dx = -1; dx <= 1; dx++)
+                    hit |= (float)__ldg(age + clampi(cy + dy, 0, h - 1) * r.wp + clampi(cx + dx, 0, w - 1)) >= r.min_age;
+            return hit;
+        };
+        const bool sta = on_static(gxa, gya), stb = on_static(gxb, gyb);
+        if (sta && stb) {
+            r_k = 0.0f;
+            raw = 1.0f;
+        } else if (sta) {
+            r_k = 0.0f;
+            wa = 0.0f;
+            wb = 1.0f;
+        } else if (stb) {
+            r_k = 0.0f;
+            wa = 1.0f;
+            wb = 0.0f;
+        }
+        kk = fminf(fmaxf(((float)__ldg(age + y * r.wp + x) - r.min_age + 2.0f) / 2.0f, 0.0f), 1.0f);
+    }
+    // (R, G, B); the residual map is BGR
+    float c[3] = {ca.x * wa + cb.x * wb + r2 * r_k, ca.y * wa + cb.y * wb + r01.y * r_k, ca.z * wa + cb.z * wb + r01.x * r_k};
+    const float ow[3] = {own.x, own.y, own.z};
+    uint32_t q[3];
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        if (stillw > 0.0f) c[k] = c[k] * (1.0f - stillw) + ow[k] * stillw;
+        if (age) {
+            c[k] = c[k] * (1.0f - raw) + ow[k] * raw;
+            c[k] = c[k] * (1.0f - kk) + ow[k] * kk;
+        }
+        q[k] = (uint32_t)(fminf(fmaxf(c[k], 0.0f), 1.0f) * 255.0f + 0.5f);
+    }
+    reinterpret_cast<uint32_t*>(r.out + (long long)n * r.out_bs)[y * w + x] = q[0] | (q[1] << 8) | (q[2] << 16) | 0xff000000u;
+}
+
 __global__ void k_set_scalar(float* d, float v) { *d = v; }
 
 // a bounded busy wait: returns after `cycles` clock cycles of its own SM
@@ -1433,11 +1602,11 @@ cudaError_t aa_axis(int in, int out, int* first, int* count, float* w, cudaStrea
 }
 
 cudaError_t frame_to_input(const uint8_t* frames, long long frame_bs, int w, int h, int hp, int wp, bool internal, int ih,
-                           int iw, Img4 out, int n, cudaStream_t st, AaAxis ax, AaAxis ay) {
+                           int iw, Img4 out, int n, cudaStream_t st, AaAxis ax, AaAxis ay, bool tex) {
     const int oh = internal ? ih : hp, ow = internal ? iw : wp;
     if (!ax.w || !ay.w) ax = ay = AaAxis{};
     { const cudaError_t e_ = launch(k_frame_to_input, grid2(ow, oh, n), dim3(16, 16), 0, st, frames, frame_bs, w, h, hp, wp, internal ? 1 : 0, oh, ow,
-                                                               out.p, out.bs, ax, ay); if (e_ != cudaSuccess) return e_; }
+                                                               out.p, out.bs, ax, ay, tex ? 1 : 0); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
@@ -1460,8 +1629,8 @@ cudaError_t static_near(const int16_t* age, long long bs, int wp, int hp, float 
     return cudaGetLastError();
 }
 
-cudaError_t spread_table(uint32_t* out, cudaStream_t st) {
-    k_spread_table<<<1, 256, 0, st>>>(out);
+cudaError_t spread_table(uint32_t* out, cudaStream_t st, bool tex) {
+    k_spread_table<<<1, 256, 0, st>>>(out, tex ? 1 : 0);
     return cudaGetLastError();
 }
 
@@ -1552,6 +1721,14 @@ cudaError_t render(const RenderArgs& r0, int n, cudaStream_t st) {
     r.qsy = (float)r.hq / (float)r.hp;  // the same IEEE quotients render.wgsl:87-88 forms per pixel
     r.qsx = (float)r.wq / (float)r.wp;
     { const cudaError_t e_ = launch(k_render, grid2(r.w, r.h, n, 32, 8), dim3(32, 8), 0, st, r); if (e_ != cudaSuccess) return e_; }
+    return cudaGetLastError();
+}
+
+cudaError_t render_tex(const RenderTexArgs& r, int n, cudaStream_t st) {
+    if ((long long)r.hp * r.wp >= (1ll << 31) || (long long)r.w * r.h >= (1ll << 31)) return cudaErrorInvalidValue;
+    if ((uintptr_t)r.up7 % 16 || (uintptr_t)r.rt % 8 || (uintptr_t)r.fa % 4 || (uintptr_t)r.fb % 4 || (uintptr_t)r.out % 4)
+        return cudaErrorMisalignedAddress;
+    { const cudaError_t e_ = launch(k_render_tex, grid2(r.w, r.h, n, 32, 8), dim3(32, 8), 0, st, r); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 

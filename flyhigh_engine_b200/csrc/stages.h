@@ -29,8 +29,10 @@ cudaError_t aa_axis(int in, int out, int* first, int* count, float* w, cudaStrea
 // rgba8 frame -> network input A: internal mode = antialias triangle downscale of the replicate-padded frame
 // (tex_in.wgsl + interp.wgsl aa); otherwise the padded frame itself as f16. frames: [n] x (w x h x 4 bytes),
 // frame_bs bytes apart. ax / ay: the downscale's axis tables (hp -> ih, wp -> iw), or null pointers (weights per tap).
+// tex: the fast render path's tex_down.wgsl, whose source texels are k / 255 in f32 (not f16(k / 255))
 cudaError_t frame_to_input(const uint8_t* frames, long long frame_bs, int w, int h, int hp, int wp, bool internal,
-                           int ih, int iw, Img4 out, int n, cudaStream_t st, AaAxis ax = {}, AaAxis ay = {});
+                           int ih, int iw, Img4 out, int n, cudaStream_t st, AaAxis ax = {}, AaAxis ay = {},
+                           bool tex = false);
 // A -> aq (antialias x0.25), i8 = avgpool2(aq), i16 = avgpool2(i8) (interp.wgsl aa + avgpool.wgsl); ax / ay: the
 // x0.25 axis tables (iw -> qw, ih -> qh), or null pointers
 cudaError_t input_pyramid(Img4 A, int ih, int iw, Img4 aq, Img4 i8, Img4 i16, int n, cudaStream_t st, AaAxis ax = {},
@@ -41,9 +43,11 @@ struct StaticArgs {
     int w, h, wp, hp;
     float thr, min_age;
     int use_mask;
+    int tex;  // 1: the fast render path's keep_static_age_tex.wgsl, comparing texels k / 255 in f32
 };
 // per pair: changed (diff >= thr, when protecting; one bit per pixel, changed_words(wp) 32-bit words per row) and
-// dsum (sum_c |A - B|, when the still test is on), padded plane; n pairs (frames, planes frame_bs / *_bs apart)
+// dsum (sum_c |A - B|, when the still test is on; with s.tex the fast render's term dot(|A - B|.rgb, 1 / 3)), padded
+// plane; n pairs (frames, planes frame_bs / *_bs apart)
 inline int changed_words(int wp) { return (wp + 31) >> 5; }
 cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, long long frame_bs, const StaticArgs& s, uint32_t* changed,
                         long long changed_bs, float* dsum, long long dsum_bs, int n, cudaStream_t st);
@@ -57,7 +61,7 @@ cudaError_t static_near(const int16_t* age, long long bs, int wp, int hp, float 
 cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, long long frame_bs, const uint32_t* changed,
                        long long changed_bs, const uint8_t* mask, const StaticArgs& s, uchar4* state, int16_t* age,
                        long long age_bs, int np, const uint32_t* spread, cudaStream_t st);
-cudaError_t spread_table(uint32_t* out, cudaStream_t st);
+cudaError_t spread_table(uint32_t* out, cudaStream_t st, bool tex = false);
 
 // luma.wgsl + sad.wgsl on two 3-channel images (a view at channel offset 0): (2r+1)^2 cost channels into out (cs)
 cudaError_t sad_volume(const __half* a, int a_cs, const __half* b, int b_cs, long long in_bs, int h, int w, int r,
@@ -156,6 +160,31 @@ struct RenderArgs {
     float qsy, qsx;          // hq / hp and wq / wp (set by render())
 };
 cudaError_t render(const RenderArgs& r, int n, cudaStream_t st);
+
+// render_tex.wgsl (the fast render): the in-between straight from the two rgba8 frames into rgba8
+struct RenderTexArgs {
+    const uint8_t *fa, *fb;  // source frames, w x h x 4 bytes
+    long long f_bs;
+    int w, h, hp, wp;
+    const __half* up7;       // flow_tq (ch 0-3), vis_tq (ch 4-6), cs 8
+    long long up_bs;
+    const __half* rt;        // R_t, cs 4
+    long long rt_bs;
+    int hq, wq;
+    float fsx, fsy;
+    int cubic;
+    unsigned flags;          // bit 0 decisive, bit 1 still test
+    const int16_t* age;      // static age plane (padded), or null
+    long long age_bs;
+    float min_age;
+    const float* es;         // pair_planes' still-test terms on the padded plane (when flags bit 1)
+    long long es_bs;
+    const float* t;          // [n] phases, read when linear (sa, sb, sr = 2 t, 2 (1 - t), 1 - |2 t - 1|)
+    int linear;
+    uint8_t* out;            // w x h x 4
+    long long out_bs;
+};
+cudaError_t render_tex(const RenderTexArgs& r, int n, cudaStream_t st);
 
 // tex_in.wgsl's values of a frame as an unpadded f16 plane: w x h x (B, G, R, 0) halves
 cudaError_t frame_half(const uint8_t* f, long long f_bs, int w, int h, __half* out, long long o_bs, int n,

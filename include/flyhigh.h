@@ -65,8 +65,8 @@ typedef struct FhSessionOptions {
     uint32_t keep_static;            /* 1 = static protection (default on) */
     uint32_t static_frames;          /* unchanged source frames before a pixel is protected (default 8; 0 = 8) */
     uint32_t static_tolerance;       /* largest change, 0..255 levels, still counted as unchanged (default 4) */
-    uint32_t fast_render;            /* 1 = render from the source frames (refused by this build) */
-    uint32_t linear_t;               /* 1 = with fast_render, phases scaled linearly (refused by this build) */
+    uint32_t fast_render;            /* 1 = render straight from the source frames' rgba8 texels */
+    uint32_t linear_t;               /* 1 = with fast_render, the mid network once per pair, phases scaled linearly */
     uint32_t keep_maps;              /* 1 = keep the repair maps (raises repair to 1) */
     uint32_t protection_mask;        /* 1 = the host paints pixels never interpolated (fh_session_write_mask) */
     const char* tune;                /* accepted, ignored */

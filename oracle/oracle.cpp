@@ -706,6 +706,254 @@ static void k_static_apply(const T& age, const T& A, const T& B, const StaticP& 
         }
 }
 
+// ----------------------------------------------------------------------------------------- fast render path ----
+// net/session_ext.rs:194-443: the source frames are sampled as rgba8 textures, whose texels read as k / 255 in f32
+// (not the f16 planes of tex_in)
+
+static inline float texel(const uint8_t* f, int w, int x, int y, int c) {  // c: 0 R, 1 G, 2 B
+    return (float)f[((size_t)y * w + x) * 4 + c] / 255.0f;
+}
+
+// tex_down.wgsl:10-33: the antialiased downscale (interp.wgsl's triangle) of the replicate-padded frame (iw x ih, the
+// padded working size) to the network input oh x ow, straight from the texture; planes B, G, R
+static T k_tex_down(const uint8_t* rgba, int w, int h, int iw, int ih, int oh, int ow) {
+    T out = alloc(3, oh, ow);
+    f16* o = out.buf->d.data();
+    const size_t plane = (size_t)oh * ow;
+#pragma omp parallel for
+    for (int oy = 0; oy < oh; oy++)
+        for (int ox = 0; ox < ow; ox++) {
+            const float sh = (float)ih / (float)oh, sw = (float)iw / (float)ow;
+            const float fsh = std::max(sh, 1.0f), fsw = std::max(sw, 1.0f);
+            const float cy = ((float)oy + 0.5f) * sh, cx = ((float)ox + 0.5f) * sw;
+            const int ymin = std::max(0, (int)floorf(cy - fsh + 0.5f)), ymax = std::min(ih, (int)floorf(cy + fsh + 0.5f));
+            const int xmin = std::max(0, (int)floorf(cx - fsw + 0.5f)), xmax = std::min(iw, (int)floorf(cx + fsw + 0.5f));
+            float ar = 0.0f, ag = 0.0f, ab = 0.0f, norm = 0.0f;
+            for (int y = ymin; y < ymax; y++) {
+                const float wy = std::max(0.0f, 1.0f - fabsf(((float)y + 0.5f - cy) / fsh));
+                const int ty = std::min(y, h - 1);
+                for (int x = xmin; x < xmax; x++) {
+                    const float wx = std::max(0.0f, 1.0f - fabsf(((float)x + 0.5f - cx) / fsw));
+                    const float wgt = wx * wy;
+                    const int tx = std::min(x, w - 1);
+                    ar = ar + texel(rgba, w, tx, ty, 0) * wgt;
+                    ag = ag + texel(rgba, w, tx, ty, 1) * wgt;
+                    ab = ab + texel(rgba, w, tx, ty, 2) * wgt;
+                    norm = norm + wgt;
+                }
+            }
+            const size_t i = (size_t)oy * ow + ox;
+            o[i] = S(ab / norm);
+            o[plane + i] = S(ag / norm);
+            o[2 * plane + i] = S(ar / norm);
+        }
+    return out;
+}
+
+// keep_static_age_tex.wgsl:53-74: the age pass of keep_static_age.wgsl on the two textures. Every position of the
+// padded plane evaluates its pixel clamped to the frame, with probes clamped to the frame.
+static void k_static_age_tex(const uint8_t* fa, const uint8_t* fb, const StaticP& p, const T* mask, T& state, T& age) {
+    const size_t plane = (size_t)p.hp * p.wp;
+    f16* st = state.buf->d.data();
+    const int DX[8] = {1, -1, 0, 0, 1, -1, 1, -1}, DY[8] = {0, 0, 1, -1, 1, 1, -1, -1}, FAR[4] = {4, 8, 16, 32};
+    auto cx = [&](int v) { return std::max(0, std::min(v, p.w - 1)); };
+    auto cy = [&](int v) { return std::max(0, std::min(v, p.h - 1)); };
+    auto change = [&](int x, int y) {
+        float d = 0.0f;
+        for (int c = 0; c < 3; c++) d = std::max(d, fabsf(texel(fa, p.w, x, y, c) - texel(fb, p.w, x, y, c)));
+        return d;
+    };
+#pragma omp parallel for
+    for (int y = 0; y < p.hp; y++)
+        for (int x = 0; x < p.wp; x++) {
+            const int tx = std::min(x, p.w - 1), ty = std::min(y, p.h - 1);
+            const size_t o = (size_t)y * p.wp + x;
+            bool moved = false;
+            for (int dy = -1; dy <= 1; dy++)
+                for (int dx = -1; dx <= 1; dx++) moved = moved || change(cx(tx + dx), cy(ty + dy)) >= p.thr;
+            for (int i = 0; i < 8; i++)
+                for (int j = 0; j < 4; j++) moved = moved || change(cx(tx + DX[i] * FAR[j]), cy(ty + DY[i] * FAR[j])) >= p.thr;
+            const bool same = change(tx, ty) < p.thr;
+            float m = 0.0f;  // spread (:41-51)
+            for (int dy = -1; dy <= 1; dy++)
+                for (int dx = -1; dx <= 1; dx++) {
+                    const int qx = cx(tx + dx), qy = cy(ty + dy);
+                    for (int c = 0; c < 3; c++) {
+                        m = std::max(m, fabsf(texel(fa, p.w, qx, qy, c) - texel(fa, p.w, tx, ty, c)));
+                        m = std::max(m, fabsf(texel(fb, p.w, qx, qy, c) - texel(fb, p.w, tx, ty, c)));
+                    }
+                }
+            const bool still = same && m >= 0.03f;
+            const float raw = still ? std::min(L(st[o]) + 1.0f, 255.0f) : 0.0f;
+            const float seen = still ? std::min(L(st[plane + o]) + (moved ? 1.0f : 0.0f), 255.0f) : 0.0f;
+            const float run = same ? std::min(L(st[2 * plane + o]) + 1.0f, 255.0f) : 0.0f;
+            st[o] = S(raw);
+            st[plane + o] = S(seen);
+            st[2 * plane + o] = S(run);
+            f16 aged = S(seen >= 2.0f ? raw : -run);
+            if (p.use_mask && mask && L(mask->buf->d[o]) > 0.5f) aged = S(255.0f);
+            age.buf->d[o] = aged;
+        }
+}
+
+struct RenderTexArgs {
+    int w, h, wp, hp;
+    float fsx, fsy, vs, min_age;
+    bool cubic;
+    uint32_t flags;  // bit 0 decisive, bit 1 still test
+    float sa, sb, sr;  // linear-t scales (1, 1, 1: as computed)
+    const T* age;    // static protection, or null
+};
+
+// render_tex.wgsl:70-120: the in-between straight from the two rgba8 frames into rgba8, from the quarter-resolution
+// maps ftq (4 channels), vtq (3), rt (3, BGR)
+static void k_render_tex(const uint8_t* fa, const uint8_t* fb, const T& ftq, const T& vtq, const T& rt,
+                         const RenderTexArgs& ra, uint8_t* out) {
+    const int w = ra.w, h = ra.h, hq = ftq.h, wq = ftq.w;
+    auto bil4 = [](float v00, float v01, float v10, float v11, float fx, float fy) {
+        return (v00 * (1.0f - fx) + v01 * fx) * (1.0f - fy) + (v10 * (1.0f - fx) + v11 * fx) * fy;
+    };
+    auto cub1 = [](float x) { const float aa = -0.75f; return ((aa + 2.0f) * x - (aa + 3.0f)) * x * x + 1.0f; };
+    auto cub2 = [](float x) { const float aa = -0.75f; return ((aa * x - 5.0f * aa) * x + 8.0f * aa) * x - 4.0f * aa; };
+    auto q = [&](const T& t, int ch, int y0, int y1, int x0, int x1, float fx, float fy) {
+        const size_t b = (size_t)(ch + t.c0) * hq * wq;
+        const f16* d = t.buf->d.data();
+        return bil4(L(d[b + (size_t)y0 * wq + x0]), L(d[b + (size_t)y0 * wq + x1]), L(d[b + (size_t)y1 * wq + x0]),
+                    L(d[b + (size_t)y1 * wq + x1]), fx, fy);
+    };
+    auto tap = [&](const uint8_t* f, int x, int y, float (&v)[3]) {
+        x = std::max(0, std::min(x, w - 1));
+        y = std::max(0, std::min(y, h - 1));
+        for (int c = 0; c < 3; c++) v[c] = texel(f, w, x, y, c);
+    };
+    // sample(): Keys bicubic with per-tap clamp, or bilinear between the four neighbours (the sampler's filter, edges
+    // clamped); RGB
+    auto sample = [&](const uint8_t* f, float gx, float gy, float (&r)[3]) {
+        const int px = (int)floorf(gx), py = (int)floorf(gy);
+        if (ra.cubic) {
+            const float tx = gx - (float)px, ty = gy - (float)py;
+            const float cx[4] = {cub2(tx + 1.0f), cub1(tx), cub1(1.0f - tx), cub2(2.0f - tx)};
+            const float cyw[4] = {cub2(ty + 1.0f), cub1(ty), cub1(1.0f - ty), cub2(2.0f - ty)};
+            float rows[4][3];
+            for (int j = 0; j < 4; j++) {
+                float t0[3], t1[3], t2[3], t3[3];
+                tap(f, px - 1, py - 1 + j, t0);
+                tap(f, px, py - 1 + j, t1);
+                tap(f, px + 1, py - 1 + j, t2);
+                tap(f, px + 2, py - 1 + j, t3);
+                for (int c = 0; c < 3; c++) rows[j][c] = t0[c] * cx[0] + t1[c] * cx[1] + t2[c] * cx[2] + t3[c] * cx[3];
+            }
+            for (int c = 0; c < 3; c++)
+                r[c] = rows[0][c] * cyw[0] + rows[1][c] * cyw[1] + rows[2][c] * cyw[2] + rows[3][c] * cyw[3];
+        } else {
+            const float ax = gx - (float)px, ay = gy - (float)py;
+            float t00[3], t01[3], t10[3], t11[3];
+            tap(f, px, py, t00);
+            tap(f, px + 1, py, t01);
+            tap(f, px, py + 1, t10);
+            tap(f, px + 1, py + 1, t11);
+            for (int c = 0; c < 3; c++) r[c] = bil4(t00[c], t01[c], t10[c], t11[c], ax, ay);
+        }
+    };
+    auto on_static = [&](float gx, float gy) {
+        const int cx = (int)rintf(gx), cy = (int)rintf(gy);  // WGSL round(): half to even
+        for (int dy = -1; dy <= 1; dy++)
+            for (int dx = -1; dx <= 1; dx++) {
+                const int xx = std::max(0, std::min(cx + dx, w - 1)), yy = std::max(0, std::min(cy + dy, h - 1));
+                if (L(ra.age->buf->d[(size_t)yy * ra.wp + xx]) >= ra.min_age) return true;
+            }
+        return false;
+    };
+    const float third = 1.0f / 3.0f;
+    auto dot3 = [&](const float (&v)[3]) { return v[0] * third + v[1] * third + v[2] * third; };
+#pragma omp parallel for
+    for (int y = 0; y < h; y++)
+        for (int x = 0; x < w; x++) {
+            const float iy = ((float)y + 0.5f) * (float)hq / (float)ra.hp - 0.5f;
+            const float ix = ((float)x + 0.5f) * (float)wq / (float)ra.wp - 0.5f;
+            const int qy0 = (int)floorf(iy), qx0 = (int)floorf(ix);
+            const float fy = iy - (float)qy0, fx = ix - (float)qx0;
+            const int y0 = std::max(0, std::min(qy0, hq - 1)), y1 = std::max(0, std::min(qy0 + 1, hq - 1));
+            const int x0 = std::max(0, std::min(qx0, wq - 1)), x1 = std::max(0, std::min(qx0 + 1, wq - 1));
+            const float gxa = (float)x + q(ftq, 0, y0, y1, x0, x1, fx, fy) * ra.fsx * ra.sa;
+            const float gya = (float)y + q(ftq, 1, y0, y1, x0, x1, fx, fy) * ra.fsy * ra.sa;
+            const float gxb = (float)x + q(ftq, 2, y0, y1, x0, x1, fx, fy) * ra.fsx * ra.sb;
+            const float gyb = (float)y + q(ftq, 3, y0, y1, x0, x1, fx, fy) * ra.fsy * ra.sb;
+            const float v0 = q(vtq, 0, y0, y1, x0, x1, fx, fy) * ra.vs, v1 = q(vtq, 1, y0, y1, x0, x1, fx, fy) * ra.vs,
+                        v2 = q(vtq, 2, y0, y1, x0, x1, fx, fy) * ra.vs;
+            const float m = std::max(v0, std::max(v1, v2));
+            const float e0 = expf(v0 - m), e1 = expf(v1 - m), e2 = expf(v2 - m), s = e0 + e1 + e2;
+            float wa = (e0 + 0.5f * e2) / s * (2.0f - ra.sa), wb = (e1 + 0.5f * e2) / s * (2.0f - ra.sb);
+            const float wn = std::max(wa + wb, 1e-6f);
+            wa = wa / wn;
+            wb = wb / wn;
+            float r_k = ra.sr, raw = 0.0f;
+            float ca[3], cb[3];
+            sample(fa, gxa, gya, ca);
+            sample(fb, gxb, gyb, cb);
+            float dab[3];
+            for (int c = 0; c < 3; c++) dab[c] = fabsf(ca[c] - cb[c]);
+            float stillw = 0.0f;
+            if (ra.flags & 2u) {
+                float es = 0.0f;
+                for (int dy = -1; dy <= 1; dy++)
+                    for (int dx = -1; dx <= 1; dx++) {
+                        float pa[3], pb[3], d[3];
+                        tap(fa, x + dx, y + dy, pa);
+                        tap(fb, x + dx, y + dy, pb);
+                        for (int c = 0; c < 3; c++) d[c] = fabsf(pa[c] - pb[c]);
+                        es += dot3(d);
+                    }
+                es = es / 9.0f;
+                const float ef = dot3(dab);
+                stillw = std::min(std::max((ef - es) / 0.04f, 0.0f), 1.0f) * (es < 0.03f ? 1.0f : 0.0f);
+            }
+            if (ra.flags & 1u) {
+                const float k = std::min(std::max((dot3(dab) - 0.04f) / 0.08f, 0.0f), 1.0f);
+                const float pa = wa >= wb ? 1.0f : 0.0f;
+                wa = wa * (1.0f - k) + pa * k;
+                wb = wb * (1.0f - k) + (1.0f - pa) * k;
+                r_k = r_k * (1.0f - k);
+            }
+            if (ra.age) {
+                const bool sa = on_static(gxa, gya), sb = on_static(gxb, gyb);
+                if (sa && sb) {
+                    r_k = 0.0f;
+                    raw = 1.0f;
+                } else if (sa) {
+                    r_k = 0.0f;
+                    wa = 0.0f;
+                    wb = 1.0f;
+                } else if (sb) {
+                    r_k = 0.0f;
+                    wa = 1.0f;
+                    wb = 0.0f;
+                }
+            }
+            const float res[3] = {q(rt, 2, y0, y1, x0, x1, fx, fy), q(rt, 1, y0, y1, x0, x1, fx, fy),
+                                  q(rt, 0, y0, y1, x0, x1, fx, fy)};  // BGR -> RGB
+            float c[3], own[3], pa[3], pb[3];
+            tap(fa, x, y, pa);
+            tap(fb, x, y, pb);
+            for (int k = 0; k < 3; k++) {
+                c[k] = ca[k] * wa + cb[k] * wb + res[k] * r_k;
+                own[k] = 0.5f * (pa[k] + pb[k]);
+            }
+            if (stillw > 0.0f)
+                for (int k = 0; k < 3; k++) c[k] = c[k] * (1.0f - stillw) + own[k] * stillw;
+            if (ra.age) {
+                const float kk = std::min(std::max((L(ra.age->buf->d[(size_t)y * ra.wp + x]) - ra.min_age + 2.0f) / 2.0f, 0.0f), 1.0f);
+                for (int k = 0; k < 3; k++) {
+                    c[k] = c[k] * (1.0f - raw) + own[k] * raw;
+                    c[k] = c[k] * (1.0f - kk) + own[k] * kk;
+                }
+            }
+            uint8_t* o = out + ((size_t)y * w + x) * 4;
+            for (int k = 0; k < 3; k++) o[k] = (uint8_t)(uint32_t)(std::min(std::max(c[k], 0.0f), 1.0f) * 255.0f + 0.5f);
+            o[3] = 255;
+        }
+}
+
 // ------------------------------------------------------------------------------------------------------- GMHS ----
 // gmhs.rs:155-219 with gm_fit_reduce / gm_fit_solve / gm_cost / gm_box / gm_select.wgsl
 
@@ -884,6 +1132,7 @@ static void gm_run(const T& A, const T& B, T& flow, int full_w, int level, std::
 
 struct Opts {
     int w, h, iw, ih, k, repair, cubic, keep_static, static_frames, static_tol, still, decisive, protection_mask;
+    int fast_render = 0, linear_t = 0;
 };
 
 struct Session {
@@ -906,6 +1155,10 @@ struct Session {
     fhjson::Value rop;
     std::vector<float> gm_maps;
     T flow_pre;  // the E8 flow before the repair stage (GMHS rewrites it in place)
+    // fast render (net/session_ext.rs:194-443): the pair's source frames, and with linear_t the maps of the current
+    // pair at t = 0.5, computed by its first mid
+    std::vector<uint8_t> fa, fb;
+    bool half_done = false;
 };
 
 static std::map<std::string, int> count_uses(const std::vector<fhjson::Value>& ops) {
@@ -1146,7 +1399,7 @@ static Session* session_new(const Model* m, const Opts& o) {
             rend = i;
             break;
         }
-    if (s->internal && rend < ops.size()) {
+    if ((s->internal || o.fast_render) && rend < ops.size()) {
         s->body.assign(ops.begin(), ops.begin() + rend);
         s->has_rop = true;
         s->rop = ops[rend];
@@ -1159,16 +1412,39 @@ static Session* session_new(const Model* m, const Opts& o) {
 
 // net/session_ext.rs:377-443 + net/build.rs:576-661: tex_in x2, static age, internal downscale, pair ops, GMHS
 static void session_pair(Session* s, const uint8_t* ra, const uint8_t* rb) {
-    k_tex_in(ra, s->o.w, s->o.h, s->a);
-    k_tex_in(rb, s->o.w, s->o.h, s->b);
-    if (s->protects) k_static_age(s->a, s->b, s->sp, &s->mask, s->state, s->age);
     std::map<std::string, T> env;
-    if (s->internal) {
-        env["A"] = k_interp(s->a, s->ihp, s->iwp, true);
-        env["B"] = k_interp(s->b, s->ihp, s->iwp, true);
+    if (s->o.fast_render) {
+        // net/session_ext.rs:389-437: tex_down (or tex_in at the frame size), then the age pass on the textures
+        const size_t n = (size_t)s->o.w * s->o.h * 4;
+        s->fa.assign(ra, ra + n);
+        s->fb.assign(rb, rb + n);
+        s->half_done = false;
+        if (s->internal) {
+            env["A"] = k_tex_down(ra, s->o.w, s->o.h, s->wp, s->hp, s->ihp, s->iwp);
+            env["B"] = k_tex_down(rb, s->o.w, s->o.h, s->wp, s->hp, s->ihp, s->iwp);
+        } else {
+            k_tex_in(ra, s->o.w, s->o.h, s->a);
+            k_tex_in(rb, s->o.w, s->o.h, s->b);
+            env["A"] = s->a;
+            env["B"] = s->b;
+        }
+        if (s->protects) {
+            StaticP tp = s->sp;
+            tp.w = s->o.w;
+            tp.h = s->o.h;
+            k_static_age_tex(ra, rb, tp, &s->mask, s->state, s->age);
+        }
     } else {
-        env["A"] = s->a;
-        env["B"] = s->b;
+        k_tex_in(ra, s->o.w, s->o.h, s->a);
+        k_tex_in(rb, s->o.w, s->o.h, s->b);
+        if (s->protects) k_static_age(s->a, s->b, s->sp, &s->mask, s->state, s->age);
+        if (s->internal) {
+            env["A"] = k_interp(s->a, s->ihp, s->iwp, true);
+            env["B"] = k_interp(s->b, s->ihp, s->iwp, true);
+        } else {
+            env["A"] = s->a;
+            env["B"] = s->b;
+        }
     }
     std::vector<fhjson::Value> pair_ops(s->body.begin(), s->body.begin() + s->ms);
     Walker wk(*s, 0.5f);
@@ -1196,6 +1472,39 @@ static void session_pair(Session* s, const uint8_t* ra, const uint8_t* rb) {
 // net/session_ext.rs:445-468 + net/build.rs:693-756: mid ops at t, full-resolution render, keep_static, tex_out
 static void session_mid(Session* s, float t, uint8_t* out) {
     if (!s->have_pair) throw std::runtime_error("pair two input slots first");
+    if (s->o.fast_render) {
+        // session.rs:495-507: linear_t runs the mid network once per pair at t = 0.5 and renders every phase from it
+        if (!s->o.linear_t || !s->half_done) {
+            std::map<std::string, T> env = s->env;
+            std::vector<fhjson::Value> mid_ops(s->body.begin() + s->ms, s->body.end());
+            Walker wk(*s, s->o.linear_t ? 0.5f : t);
+            wk.uses = count_uses(std::vector<fhjson::Value>(s->m->graph["ops"].arr.begin(), s->m->graph["ops"].arr.end()));
+            wk.build(mid_ops, env);
+            s->mid_env = env;
+            s->half_done = true;
+        }
+        const auto ins = names(s->rop, "in");
+        const T ftq = s->mid_env.at(ins[2]), vtq = s->mid_env.at(ins[3]);
+        const T rt = mat(s->mid_env.at(ins[4]));
+        float sa = 1.0f, sb = 1.0f, sr = 1.0f;  // net/session_ext.rs:273-276
+        if (s->o.linear_t) {
+            sa = 2.0f * t;
+            sb = 2.0f * (1.0f - t);
+            sr = 1.0f - fabsf(2.0f * t - 1.0f);
+        }
+        RenderTexArgs ra{s->o.w, s->o.h, s->wp, s->hp,
+                         ftq.scale * (float)s->wp / (float)s->iwp, ftq.scale * (float)s->hp / (float)s->ihp, vtq.scale,
+                         s->min_age, s->o.cubic != 0, (s->o.decisive ? 1u : 0u) | (s->o.still ? 2u : 0u), sa, sb, sr,
+                         s->protects ? &s->age : nullptr};
+        std::vector<uint8_t> tmp;
+        if (!out) {
+            tmp.resize((size_t)s->o.w * s->o.h * 4);
+            out = tmp.data();
+        }
+        k_render_tex(s->fa.data(), s->fb.data(), ftq, vtq, rt, ra, out);
+        s->render = T();
+        return;
+    }
     std::map<std::string, T> env = s->env;
     std::vector<fhjson::Value> mid_ops(s->body.begin() + s->ms, s->body.end());
     Walker wk(*s, t);
@@ -1244,11 +1553,14 @@ void or_model_free(void* m) { delete (Model*)m; }
 int or_model_cubic(void* m) { return ((Model*)m)->render_cubic ? 1 : 0; }
 
 // options as an int array: w, h, iw, ih, k, repair, cubic(-1 = the model's), keep_static, static_frames, static_tol,
-// still, decisive, protection_mask
+// still, decisive, protection_mask, fast_render, linear_t
 void* or_session_new(void* model, const int* o) {
     try {
         Model* m = (Model*)model;
         Opts op{o[0], o[1], o[2], o[3], o[4], o[5], o[6] < 0 ? (m->render_cubic ? 1 : 0) : o[6], o[7], o[8], o[9], o[10], o[11], o[12]};
+        op.fast_render = o[13];
+        op.linear_t = o[14];
+        if (op.linear_t && !op.fast_render) throw std::runtime_error("linear_t: needs fast_render");
         return session_new(m, op);
     } catch (std::exception& e) {
         g_err = e.what();
@@ -1371,6 +1683,47 @@ int or_render_planes(const uint8_t* fa, const uint8_t* fb, int w, int h, const f
 }
 
 // interp.wgsl on a plain [c][h][w] f16 tensor (x scale applied to the result); out [c][oh][ow] f16 bits
+// The fast render alone (render_tex.wgsl) on caller maps: frames a, b (w x h rgba8), up7 [7][hq][wq] and R_t [3][hq][wq]
+// as f32 values of f16 tensors, age [hp][wp] or NULL. fv: fsx, fsy, min_age, sa, sb, sr; iv: cubic, flags.
+int or_render_tex_planes(const uint8_t* fa, const uint8_t* fb, int w, int h, const float* up7, const float* rt, int hq,
+                         int wq, const float* age, const float* fv, const int* iv, uint8_t* out) {
+    try {
+        const int hp = (h + 31) / 32 * 32, wp = (w + 31) / 32 * 32;
+        T up = alloc(7, hq, wq), r = alloc(3, hq, wq);
+        for (size_t i = 0; i < up.n(); i++) up.buf->d[i] = S(up7[i]);
+        for (size_t i = 0; i < r.n(); i++) r.buf->d[i] = S(rt[i]);
+        T ftq = up.view(0, 4), vtq = up.view(4, 7);
+        T ag;
+        if (age) {
+            ag = alloc(1, hp, wp);
+            for (size_t i = 0; i < ag.n(); i++) ag.buf->d[i] = S(age[i]);
+        }
+        RenderTexArgs ra{w, h, wp, hp, fv[0], fv[1], 1.0f, fv[2], iv[0] != 0, (uint32_t)iv[1], fv[3], fv[4], fv[5],
+                         age ? &ag : nullptr};
+        k_render_tex(fa, fb, ftq, vtq, r, ra, out);
+        return 0;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
+// tex_down alone: frame (w x h rgba8) -> [3][oh][ow] f16 bits (B, G, R) of the padded frame's antialiased downscale
+int or_tex_down(const uint8_t* f, int w, int h, int oh, int ow, uint16_t* out) {
+    try {
+        const int hp = (h + 31) / 32 * 32, wp = (w + 31) / 32 * 32;
+        T o = k_tex_down(f, w, h, wp, hp, oh, ow);
+        for (size_t i = 0; i < o.n(); i++) {
+            const f16 v = o.buf->d[i];
+            std::memcpy(out + i, &v, 2);
+        }
+        return 0;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
 int or_interp(const uint16_t* x, int c, int h, int w, int oh, int ow, int aa, float scale, uint16_t* out) {
     T t = alloc(c, h, w);
     memcpy(t.buf->d.data(), x, t.n() * 2);

@@ -51,6 +51,8 @@ def lib():
         L.or_render_planes.argtypes = [POINTER(c_uint8), POINTER(c_uint8), c_int, c_int, POINTER(c_float),
                                        POINTER(c_float), c_int, c_int, POINTER(c_float), POINTER(c_float),
                                        POINTER(c_int), POINTER(c_uint8)]
+        L.or_render_tex_planes.argtypes = L.or_render_planes.argtypes
+        L.or_tex_down.argtypes = [POINTER(c_uint8), c_int, c_int, c_int, c_int, POINTER(c_uint16)]
         L.or_interp.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, c_int, c_int, c_int, c_float, POINTER(c_uint16)]
         L.or_warp.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, POINTER(c_uint16), c_float, POINTER(c_uint16)]
         L.or_conv.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, POINTER(c_float), POINTER(c_float),
@@ -87,11 +89,13 @@ class OracleSession:
 
     def __init__(self, model: OracleModel, width: int, height: int, internal=(0, 0), k: int = 1, repair: int = 1,
                  cubic: int = -1, keep_static: bool = True, static_frames: int = 8, static_tolerance: int = 4,
-                 still: bool = True, decisive: bool = False, protection_mask: bool = False):
+                 still: bool = True, decisive: bool = False, protection_mask: bool = False, fast_render: bool = False,
+                 linear_t: bool = False):
         self.model = model
         self.w, self.h = width, height
-        o = (c_int * 13)(width, height, internal[0], internal[1], k, repair, cubic, int(keep_static), static_frames,
-                         static_tolerance, int(still), int(decisive), int(protection_mask))
+        o = (c_int * 15)(width, height, internal[0], internal[1], k, repair, cubic, int(keep_static), static_frames,
+                         static_tolerance, int(still), int(decisive), int(protection_mask), int(fast_render),
+                         int(linear_t))
         self.s = lib().or_session_new(model.h, o)
         if not self.s:
             raise RuntimeError(lib().or_error().decode())
@@ -199,3 +203,32 @@ def warp(img, flow, flow_scale: float = 1.0):
     u = lambda a: a.ctypes.data_as(POINTER(c_uint16))
     lib().or_warp(u(img), c, h, w, u(flow), c_float(flow_scale), u(out))
     return out
+
+
+def render_tex_planes(fa, fb, w, h, up7, rt, age, fsx, fsy, min_age, cubic=True, flags=2, sa=1.0, sb=1.0, sr=1.0):
+    """The fast render (render_tex.wgsl) alone on given network outputs (up7 [7][hq][wq], R_t [3][hq][wq], age
+    [hp][wp] or None); rgba8 out."""
+    fa = np.ascontiguousarray(fa, np.uint8)
+    fb = np.ascontiguousarray(fb, np.uint8)
+    up7 = np.ascontiguousarray(up7, np.float32)
+    rt = np.ascontiguousarray(rt, np.float32)
+    hq, wq = up7.shape[1], up7.shape[2]
+    ag = None if age is None else np.ascontiguousarray(age, np.float32)
+    fv = np.array([fsx, fsy, min_age, sa, sb, sr], np.float32)
+    iv = np.array([int(cubic), int(flags)], np.int32)
+    out = np.zeros(w * h * 4, np.uint8)
+    f = lambda a: a.ctypes.data_as(POINTER(c_float))
+    rc = lib().or_render_tex_planes(_u8(fa), _u8(fb), w, h, f(up7), f(rt), hq, wq, f(ag) if ag is not None else None,
+                                    f(fv), iv.ctypes.data_as(POINTER(c_int)), _u8(out))
+    if rc != 0:
+        raise RuntimeError(lib().or_error().decode())
+    return out
+
+
+def tex_down(frame, w, h, oh, ow):
+    """tex_down.wgsl alone: the padded frame's antialiased downscale to [3][oh][ow] (B, G, R) as f16 bits."""
+    f = np.ascontiguousarray(frame, np.uint8)
+    out = np.zeros(3 * oh * ow, np.uint16)
+    if lib().or_tex_down(_u8(f), w, h, oh, ow, out.ctypes.data_as(POINTER(c_uint16))) != 0:
+        raise RuntimeError(lib().or_error().decode())
+    return out.reshape(3, oh, ow)

@@ -201,7 +201,8 @@ def _session_pair(model_dir, w, h, frames, t=0.5, **opts):
     okw = dict(k=opts.get("k", 1), repair=opts.get("repair", 1), still=still,
                cubic={"model": -1, "bilinear": 0, "bicubic": 1}[opts.get("render", "model")],
                keep_static=opts.get("static_protection", True) is not False,
-               protection_mask=opts.get("protection_mask", False))
+               protection_mask=opts.get("protection_mask", False), fast_render=opts.get("fast_render", False),
+               linear_t=opts.get("linear_t", False))
     if isinstance(opts.get("internal"), tuple):
         okw["internal"] = opts["internal"]
     o = OracleSession(om, w, h, **okw)
@@ -549,6 +550,110 @@ def test_render_on_identical_inputs(synth_model_dir, size, opts):
                                flags=pp["render_flags"])
     d = np.abs(got.astype(np.int32) - ref.astype(np.int32)).reshape(-1, 4)[:, :3]
     assert d.max() <= 1, (int(d.max()), int((d > 1).sum()))
+
+
+@pytest.mark.parametrize("size,opts,t", [((1280, 720), dict(fast_render=True), 0.5),
+                                         ((1280, 720), dict(fast_render=True, linear_t=True), 0.25),
+                                         ((640, 360), dict(fast_render=True, linear_t=True, render="bilinear"), 0.75),
+                                         ((333, 197), dict(fast_render=True, protection_mask=True), 0.5)])
+def test_render_tex_on_identical_inputs(synth_model_dir, size, opts, t):
+    """The fast render (render_tex.wgsl: rgba8 texels, linear-t scales, its own still test and static rules) against
+    the oracle's on the GPU's own maps and age plane: within one level everywhere."""
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200 import synth_frames
+    from oracle import oracle
+    w, h = size
+    frames = synth_frames.sequence_c2(10, w, h, seed=6)
+    eng = fh.Engine()
+    model = fh.Model(synth_model_dir)
+    s = fh.Session(eng, model, w, h, **opts)
+    slots = [s.add_input(), s.add_input()]
+    out = s.add_output()
+    if opts.get("protection_mask"):
+        m = np.zeros((h, w), np.uint8)
+        m[h - 60:h - 20, 20:200] = 1
+        s.write_mask(m)
+    pp = model.plan_params(w, h, **opts)
+    s.write(slots[0], frames[0])
+    for i in range(1, len(frames)):
+        a, b = slots[(i - 1) % 2], slots[i % 2]
+        s.write(b, frames[i])
+        s.pair(a, b)
+        s.mid(t, out)
+    got = np.frombuffer(s.read(out), np.uint8)
+    age = s.tensor("age")[0] if pp["protects"] else None
+    sa, sb, sr = (2 * t, 2 * (1 - t), 1 - abs(2 * t - 1)) if opts.get("linear_t") else (1.0, 1.0, 1.0)
+    ref = oracle.render_tex_planes(frames[-2], frames[-1], w, h, s.tensor("up7"), s.tensor("R_t"), age, pp["fsx"],
+                                   pp["fsy"], pp["min_age"], cubic=bool(pp["cubic"]), flags=pp["render_flags"],
+                                   sa=np.float32(2) * np.float32(t) if opts.get("linear_t") else 1.0,
+                                   sb=np.float32(2) * (np.float32(1) - np.float32(t)) if opts.get("linear_t") else 1.0,
+                                   sr=sr)
+    d = np.abs(got.astype(np.int32) - ref.astype(np.int32)).reshape(-1, 4)[:, :3]
+    assert d.max() <= 1, (int(d.max()), int((d > 1).sum()), (sa, sb, sr))
+
+
+@pytest.mark.parametrize("size,opts", [((640, 360), dict(fast_render=True)),
+                                       ((1280, 720), dict(fast_render=True, linear_t=True))])
+def test_fast_session_matches_oracle(synth_model_dir, size, opts):
+    """The fast render session end to end (tex_down or tex_in, the age pass on texels, the mid maps, render_tex; with
+    linear_t the maps once per pair at t = 0.5) against the oracle's: the network input and the maps per layer, the
+    age state inside the frame exactly, and every phase's frame."""
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200 import synth_frames
+    from oracle.oracle import OracleModel, OracleSession
+    w, h = size
+    frames = synth_frames.sequence_c2(4, w, h, seed=7)
+    s = fh.Session(fh.Engine(), fh.Model(synth_model_dir), w, h, **opts)
+    slots = [s.add_input(), s.add_input()]
+    out = s.add_output()
+    o = OracleSession(OracleModel(synth_model_dir), w, h, **opts)
+    s.write(slots[0], frames[0])
+    for i in range(1, len(frames)):
+        a, b = slots[(i - 1) % 2], slots[i % 2]
+        s.write(b, frames[i])
+        s.pair(a, b)
+        o.pair(frames[i - 1], frames[i])
+        _check_layers(s, o, ["A", "B", "o", "fr3"], 0)
+        assert np.array_equal(s.tensor("age")[:, :h, :w], o.tensor("age")[:, :h, :w]), f"age differs after pair {i}"
+        for t in (0.25, 0.5, 0.75):
+            s.mid(t, out)
+            got = np.frombuffer(s.read(out), np.uint8)
+            ref = o.mid(t)
+            ok, info = _frame_ok(got, ref)
+            assert ok, (i, t, info)
+        _check_layers(s, o, ["up7", "R_t"], 1)
+
+
+def test_batched_fast_matches_single(synth_model_dir):
+    """A batched fast_render + linear_t session gives the same frames whether its intervals run four at a time or one
+    at a time, including further phases of the newest pair after a batch."""
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200 import synth_frames
+    w, h, batch = 384, 160, 4
+    model = fh.Model(synth_model_dir)
+    frames = synth_frames.sequence_c2(batch + 2, w, h, seed=8)
+
+    def run(read_each):
+        s = fh.Session(fh.Engine(), model, w, h, batch=batch, fast_render=True, linear_t=True)
+        ins = [s.add_input(), s.add_input()]
+        outs = [s.add_output() for _ in range(batch + 3)]
+        got = {}
+        s.write(ins[0], frames[0])
+        for i in range(1, batch + 1):
+            s.write(ins[i % 2], frames[i])
+            s.pair(ins[(i - 1) % 2], ins[i % 2])
+            s.mid(0.2 * i, outs[i])
+            if read_each:
+                got[i] = np.frombuffer(s.read(outs[i]), np.uint8).copy()
+        for i in range(1, batch + 1):
+            if i not in got:
+                got[i] = np.frombuffer(s.read(outs[i]), np.uint8).copy()
+        s.mid(0.6, outs[0])  # a further phase of the newest pair: its t = 0.5 maps are reused
+        return [got[i] for i in range(1, batch + 1)] + [np.frombuffer(s.read(outs[0]), np.uint8).copy()]
+
+    single, batched = run(True), run(False)
+    for i, (x, y) in enumerate(zip(single, batched)):
+        assert np.array_equal(x, y), i
 
 
 class GmhsParams(Structure):

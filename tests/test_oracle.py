@@ -60,6 +60,39 @@ def test_oracle_protection_mask(reference_models):
     assert inside < 1.0, inside
 
 
+def _shift_pattern(w, h, dx):
+    """crates/flyhigh-engine/tests/core.rs:233-246: a soft pattern shifted dx px to the right."""
+    x = np.arange(w, dtype=np.float32)[None, :]
+    y = np.arange(h, dtype=np.float32)[:, None]
+    u = (x - np.float32(dx)) * np.float32(0.05)
+    f = np.zeros((h, w, 4), np.uint8)
+    f[..., 0] = np.broadcast_to(128 + 100 * np.sin(u), (h, w)).astype(np.uint8)
+    f[..., 1] = (128 + 90 * np.cos(u * np.float32(0.7) + y * np.float32(0.03))).astype(np.uint8)
+    f[..., 2] = np.broadcast_to(128 + 80 * np.sin(y * np.float32(0.04)), (h, w)).astype(np.uint8)
+    f[..., 3] = 255
+    return f
+
+
+def test_oracle_fast_render_known_answer(reference_models):
+    """tests/core.rs:222-262 and tests/gpu_smoke.rs:286-325 at 1280 x 720: the fast render reproduces the exact one
+    (MAE < 0.5), and fast_render + linear_t stays within MAE < 4 of the true frame at t = 0.25, 0.5, 0.75 on linear
+    motion, close to the exact render's own error."""
+    W, H = 1280, 720
+    m = oracle.OracleModel(reference_models)
+    f0, f1 = _shift_pattern(W, H, 0.0), _shift_pattern(W, H, 16.0)
+    runs = {}
+    for name, kw in (("exact", {}), ("fast", dict(fast_render=True)), ("linear", dict(fast_render=True, linear_t=True))):
+        o = oracle.OracleSession(m, W, H, **kw)
+        o.pair(f0, f1)
+        runs[name] = [o.mid(t).reshape(H, W, 4) for t in (0.25, 0.5, 0.75)]
+    for i, dx in enumerate((4.0, 8.0, 12.0)):
+        truth = _shift_pattern(W, H, dx)
+        mae = lambda a, b: _mae(a[..., :3], b[..., :3])
+        assert mae(runs["fast"][i], runs["exact"][i]) < 0.5
+        assert mae(runs["linear"][i], truth) < 4.0
+        assert mae(runs["linear"][i], truth) < mae(runs["exact"][i], truth) + 1.0
+
+
 def _f16(a):
     return a.astype(np.float16)
 
