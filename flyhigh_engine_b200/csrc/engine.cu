@@ -702,7 +702,7 @@ struct FhSession {
             mask = alloc_n<uint8_t>((size_t)hp * wp);
             state = alloc_n<uchar4>((size_t)hp * wp);
             age = alloc_n<int16_t>((size_t)nb * hp * wp);
-            if (!fast) nearp = alloc_n<uint8_t>((size_t)nb * hp * wp);
+            nearp = alloc_n<uint8_t>((size_t)nb * hp * wp);
         }
         if (still) dsum = alloc_n<float>((size_t)nb * hp * wp);
         cv = img(h16, w16, 56, nb);
@@ -832,10 +832,9 @@ struct FhSession {
                     CK(fhk::static_age(A.frame + l * A.frame_bs, B.frame + l * B.frame_bs, -A.frame_bs, changed + l * CW,
                                        -CW, mask, sargs, state, age + l * P, -P, n, spread, st));
                     mark("static_age");
-                    if (!fast) {  // the fast render probes the age plane itself
-                        CK(fhk::static_near(age, P, wp, hp, min_age, nearp, n, st));
-                        mark("static_near");
-                    }
+                    // the fast render's probes clamp to the frame, the exact render's to the padded plane
+                    CK(fhk::static_near(age, P, wp, hp, min_age, nearp, n, st, fast ? w : 0, fast ? h : 0));
+                    mark("static_near");
                 }
             });
         const long long ecv = E(h16, w16, 56), ecc = E(h16, w16, CCP), eob = E(h16, w16, 16), efv = E(h8, w8, 8),
@@ -898,7 +897,7 @@ struct FhSession {
         if (fast) {
             fhk::RenderTexArgs ra{p.a.frame, p.b.frame, p.a.frame_bs, w, h, hp, wp, up7, eup, rt, ert, qh, qw, fsx, fsy,
                                   cubic ? 1 : 0, (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, P,
-                                  min_age, dsum, P, tdev, linear ? 1 : 0, out, out_bs};
+                                  nearp, min_age, dsum, P, tdev, linear ? 1 : 0, out, out_bs};
             CK(fhk::render_tex(ra, n, st));
             mark("render_tex");
         } else {

@@ -282,14 +282,17 @@ __global__ void __launch_bounds__(256) k_pair_planes(const uint8_t* __restrict__
 // render_static's on_static (gpu/pipeline.rs:10-34) per pixel: an age >= min_age in the clamped 3 x 3 neighbourhood.
 // A warp is one 32-pixel row segment (blocks of 32 x 8): each lane tests its column over rows y - 1 .. y + 1, the
 // ballot of those tests is shifted one column each way, and lanes 0 and 31 test the columns either side of the segment.
-__global__ void __launch_bounds__(256) k_static_near(const int16_t* __restrict__ age, long long bs, int W, int H,
-                                                     float min_age, uint8_t* near) {
+// W x H: the region covered and clamped to (the padded plane, or the frame for the fast render); pitch: the planes' row
+// pitch in elements
+__global__ void __launch_bounds__(256) k_static_near(const int16_t* __restrict__ age, long long bs, int pitch, int W,
+                                                     int H, float min_age, uint8_t* near) {
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x, x0 = blockIdx.x * 32, x = x0 + lane, y = blockIdx.y * blockDim.y + threadIdx.y;
     if (y >= H) return;  // warp-uniform
     const int16_t* __restrict__ ag = age + blockIdx.z * bs;
-    const long long r0 = (long long)max(y - 1, 0) * W, r1 = (long long)y * W, r2 = (long long)min(y + 1, H - 1) * W;
+    const long long r0 = (long long)max(y - 1, 0) * pitch, r1 = (long long)y * pitch,
+                    r2 = (long long)min(y + 1, H - 1) * pitch;
     auto column = [&](int c) {  // the three loads issued together, no short-circuit
         const int16_t a0 = __ldg(ag + r0 + c), a1 = __ldg(ag + r1 + c), a2 = __ldg(ag + r2 + c);
         return ((float)a0 >= min_age) | ((float)a1 >= min_age) | ((float)a2 >= min_age);
@@ -1402,12 +1405,77 @@ FH_DEV float3 sample_tex(const uint32_t* __restrict__ f, int w, int h, float gx,
                        bil_mix(p00.z, p01.z, p10.z, p11.z, ax, ay));
 }
 
+// byte c of two rgba8 texels as integer-valued floats on float2 lanes, without an integer-to-float conversion: the
+// byte goes into the mantissa of 2^23 (one byte permute), then 2^23 is subtracted (exact)
+template <int C>
+FH_DEV float2 bytes2(uint32_t va, uint32_t vb) {
+    constexpr uint32_t sel = 0x7440u | (uint32_t)C;  // bytes: C of the texel, 0, 0, 0x4b
+    const float2 f = make_float2(__uint_as_float(__byte_perm(va, 0x4b000000u, sel)),
+                                 __uint_as_float(__byte_perm(vb, 0x4b000000u, sel)));
+    return __fadd2_rn(f, make_float2(-8388608.0f, -8388608.0f));
+}
+
+// Bicubic samples of both frames on float2 lanes (lane x: A at (gxa, gya), lane y: B at (gxb, gyb)): the taps as their
+// byte values, the row and column sums by packed fused multiply-adds, the 1 / 255 texel scale applied once to each
+// sum. The result differs from render_tex.wgsl's per-tap k / 255 and unfused sums by f32 rounding only (relative 1e-7),
+// below one level of the rgba8 output. Where either sample's taps reach the frame's border, each frame is sampled alone.
+FH_DEV void sample_tex_pair(const uint32_t* __restrict__ A, const uint32_t* __restrict__ B, int w, int h, float gxa,
+                            float gya, float gxb, float gyb, const float* lut, float3& sa, float3& sb) {
+    const int pxa = (int)floorf(gxa), pya = (int)floorf(gya), pxb = (int)floorf(gxb), pyb = (int)floorf(gyb);
+    const bool inner = pxa >= 1 && pxa + 2 <= w - 1 && pya >= 1 && pya + 2 <= h - 1 && pxb >= 1 && pxb + 2 <= w - 1 &&
+                       pyb >= 1 && pyb + 2 <= h - 1;
+    if (!inner) {
+        sa = sample_tex(A, w, h, gxa, gya, true, lut);
+        sb = sample_tex(B, w, h, gxb, gyb, true, lut);
+        return;
+    }
+    const float2 tx = make_float2(gxa - (float)pxa, gxb - (float)pxb), ty = make_float2(gya - (float)pya, gyb - (float)pyb);
+    const float2 one = make_float2(1.0f, 1.0f), two = make_float2(2.0f, 2.0f);
+    const float2 ntx = make_float2(-tx.x, -tx.y), nty = make_float2(-ty.x, -ty.y);
+    const float2 cx0 = cub2x2(__fadd2_rn(tx, one)), cx1 = cub1x2(tx), cx2 = cub1x2(__fadd2_rn(one, ntx)),
+                 cx3 = cub2x2(__fadd2_rn(two, ntx));
+    const float2 cy[4] = {cub2x2(__fadd2_rn(ty, one)), cub1x2(ty), cub1x2(__fadd2_rn(one, nty)), cub2x2(__fadd2_rn(two, nty))};
+    const uint32_t* a0 = A + (pya - 1) * w + (pxa - 1);
+    const uint32_t* b0 = B + (pyb - 1) * w + (pxb - 1);
+    float2 ar = make_float2(0.0f, 0.0f), ag = ar, ab = ar;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        uint32_t ta[4], tb[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            ta[k] = __ldg(a0 + j * w + k);
+            tb[k] = __ldg(b0 + j * w + k);
+        }
+        float2 rr = __fmul2_rn(bytes2<0>(ta[0], tb[0]), cx0);
+        float2 rg = __fmul2_rn(bytes2<1>(ta[0], tb[0]), cx0);
+        float2 rb = __fmul2_rn(bytes2<2>(ta[0], tb[0]), cx0);
+        rr = __ffma2_rn(bytes2<0>(ta[1], tb[1]), cx1, rr);
+        rg = __ffma2_rn(bytes2<1>(ta[1], tb[1]), cx1, rg);
+        rb = __ffma2_rn(bytes2<2>(ta[1], tb[1]), cx1, rb);
+        rr = __ffma2_rn(bytes2<0>(ta[2], tb[2]), cx2, rr);
+        rg = __ffma2_rn(bytes2<1>(ta[2], tb[2]), cx2, rg);
+        rb = __ffma2_rn(bytes2<2>(ta[2], tb[2]), cx2, rb);
+        rr = __ffma2_rn(bytes2<0>(ta[3], tb[3]), cx3, rr);
+        rg = __ffma2_rn(bytes2<1>(ta[3], tb[3]), cx3, rg);
+        rb = __ffma2_rn(bytes2<2>(ta[3], tb[3]), cx3, rb);
+        ar = __ffma2_rn(rr, cy[j], ar);
+        ag = __ffma2_rn(rg, cy[j], ag);
+        ab = __ffma2_rn(rb, cy[j], ab);
+    }
+    const float2 s255 = make_float2(1.0f / 255.0f, 1.0f / 255.0f);
+    ar = __fmul2_rn(ar, s255);
+    ag = __fmul2_rn(ag, s255);
+    ab = __fmul2_rn(ab, s255);
+    sa = make_float3(ar.x, ag.x, ab.x);
+    sb = make_float3(ar.y, ag.y, ab.y);
+}
+
 // render_tex.wgsl:70-120: the fast render. Flow, visibility and residual from the quarter-resolution maps, both frames
 // sampled as rgba8 textures (texels k / 255), the linear-t scales (sa, sb, sr) of the entry's phase, the still test
 // over the frames' own 3 x 3 texels, the static rules on the age plane (3 x 3 around the rounded sample, clamped to the
 // frame) and the keep ramp; written as rgba8.
 __global__ void __launch_bounds__(256) k_render_tex(RenderTexArgs r) {
-    __shared__ float lut[256];
+    __shared__ float lut[256];  // k / 255 (the border taps, the pixel's own texels)
     for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y) lut[i] = texv(i);
     __syncthreads();
     pdl_wait();
@@ -1452,8 +1520,13 @@ __global__ void __launch_bounds__(256) k_render_tex(RenderTexArgs r) {
     wa = wa / wn;
     wb = wb / wn;
     float r_k = sr, raw = 0.0f;
-    const bool cubic = r.cubic != 0;
-    const float3 ca = sample_tex(A, w, h, gxa, gya, cubic, lut), cb = sample_tex(B, w, h, gxb, gyb, cubic, lut);
+    float3 ca, cb;
+    if (r.cubic) {
+        sample_tex_pair(A, B, w, h, gxa, gya, gxb, gyb, lut, ca, cb);
+    } else {
+        ca = sample_tex(A, w, h, gxa, gya, false, lut);
+        cb = sample_tex(B, w, h, gxb, gyb, false, lut);
+    }
     const float third = 1.0f / 3.0f;
     auto dot3 = [&](float a0, float a1, float a2) { return a0 * third + a1 * third + a2 * third; };
     const float dab = dot3(fabsf(ca.x - cb.x), fabsf(ca.y - cb.y), fabsf(ca.z - cb.z));
@@ -1480,12 +1553,12 @@ __global__ void __launch_bounds__(256) k_render_tex(RenderTexArgs r) {
     }
     float kk = 0.0f;
     if (age) {
+        const uint8_t* near = r.near + (long long)n * r.age_bs;
         auto on_static = [&](float gx, float gy) {
             const int cx = (int)rintf(gx), cy = (int)rintf(gy);  // WGSL round(): half to even
-            bool hit = false;
-#pragma unroll
+            if (cx >= 0 && cx < w && cy >= 0 && cy < h) return __ldg(near + cy * r.wp + cx) != 0;
+            bool hit = false;  // a position off the frame: its own clamped probes
             for (int dy = -1; dy <= 1; dy++)
-#pragma unroll
                 for (int dx = -1; dx <= 1; dx++)
                     hit |= (float)__ldg(age + clampi(cy + dy, 0, h - 1) * r.wp + clampi(cx + dx, 0, w - 1)) >= r.min_age;
             return hit;
@@ -1624,8 +1697,9 @@ cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, long long frame_bs
 }
 
 cudaError_t static_near(const int16_t* age, long long bs, int wp, int hp, float min_age, uint8_t* near, int n,
-                        cudaStream_t st) {
-    { const cudaError_t e_ = launch(k_static_near, grid2(wp, hp, n, 32, 8), dim3(32, 8), 0, st, age, bs, wp, hp, min_age, near); if (e_ != cudaSuccess) return e_; }
+                        cudaStream_t st, int cw_, int ch_) {
+    const int cw = cw_ > 0 ? cw_ : wp, ch = ch_ > 0 ? ch_ : hp;
+    { const cudaError_t e_ = launch(k_static_near, grid2(cw, ch, n, 32, 8), dim3(32, 8), 0, st, age, bs, wp, cw, ch, min_age, near); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 

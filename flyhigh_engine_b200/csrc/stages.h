@@ -53,8 +53,9 @@ cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, long long frame_bs
                         long long changed_bs, float* dsum, long long dsum_bs, int n, cudaStream_t st);
 // per pair after the age pass: near = an age >= min_age in the clamped 3 x 3 neighbourhood (render_static on_static);
 // n planes bs elements apart
+// (cw, ch: the region, clamped to itself; 0 = the padded plane. The fast render's on_static clamps to the frame.)
 cudaError_t static_near(const int16_t* age, long long bs, int wp, int hp, float min_age, uint8_t* near, int n,
-                        cudaStream_t st);
+                        cudaStream_t st, int cw = 0, int ch = 0);
 // the age pass over np consecutive pairs in time order (pair i: frames fa / fb + i * frame_bs, changed + i *
 // changed_bs, age + i * age_bs; strides may be negative), advancing the one state plane pair by pair
 // spread: the 256-entry byte-threshold table of the spread test (spread_table(), once per session)
@@ -176,6 +177,7 @@ struct RenderTexArgs {
     unsigned flags;          // bit 0 decisive, bit 1 still test
     const int16_t* age;      // static age plane (padded), or null
     long long age_bs;
+    const uint8_t* near;     // static_near over the frame (when age is set), age_bs apart
     float min_age;
     const float* es;         // pair_planes' still-test terms on the padded plane (when flags bit 1)
     long long es_bs;
