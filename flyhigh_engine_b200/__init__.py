@@ -206,7 +206,10 @@ class Engine:
         self.close()
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except TypeError:  # interpreter shutdown: the module's globals are already gone, the process frees everything
+            pass
 
 
 class Model:
@@ -258,7 +261,10 @@ class Model:
         self.close()
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except TypeError:  # interpreter shutdown: the module's globals are already gone, the process frees everything
+            pass
 
 
 def session_options(width: int, height: int, internal=None, k: int = 1, repair: int = 1, render: str = "model",
@@ -416,4 +422,7 @@ class Session:
         self.close()
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except TypeError:  # interpreter shutdown: the module's globals are already gone, the process frees everything
+            pass
