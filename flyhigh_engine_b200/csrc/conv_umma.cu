@@ -120,14 +120,15 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar) : "memory");
 }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+// 16 columns of this warp's 32 lanes; the registers are valid after tmem_wait_ld
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
           "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 
 // The fused epilogue of 16 channels: bias, PReLU, f16, then the residual (RES) and affine_out (AFF) steps. The
 // optional steps are template parameters so that the common case carries none of their instructions.
@@ -156,19 +157,39 @@ __device__ __forceinline__ void umma_epilogue16(const float (&v)[16], const floa
         }
     }
     uint32_t packed[8];
+    if (!RES && !AFF) {
+        // bias and PReLU on channel pairs (packed f32x2, the same roundings), both halves converted by one instruction
+        float bs[16], sl[16];
 #pragma unroll
-    for (int j = 0; j < 16; j += 2) {
-        __half hh[2];
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            float x = v[j + u] + sbias[j + u];
-            if (prelu) x = x > 0.0f ? x : sslope[j + u] * x;
-            __half h = __float2half_rn(x);
-            if (RES) h = __float2half_rn(__half2float(h) + rv[j + u]);
-            if (AFF) h = __float2half_rn(2.0f / (1.0f + expf(-__half2float(h))) - 1.0f);
-            hh[u] = h;
+        for (int j = 0; j < 16; j += 4) {
+            *reinterpret_cast<float4*>(bs + j) = *reinterpret_cast<const float4*>(sbias + j);
+            *reinterpret_cast<float4*>(sl + j) = *reinterpret_cast<const float4*>(sslope + j);
         }
-        packed[j / 2] = (uint32_t)__half_as_ushort(hh[0]) | ((uint32_t)__half_as_ushort(hh[1]) << 16);
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+            float2 x = __fadd2_rn(make_float2(v[j], v[j + 1]), make_float2(bs[j], bs[j + 1]));
+            if (prelu) {
+                const float2 t = __fmul2_rn(make_float2(sl[j], sl[j + 1]), x);
+                x = make_float2(x.x > 0.0f ? x.x : t.x, x.y > 0.0f ? x.y : t.y);
+            }
+            const __half2 h = __floats2half2_rn(x.x, x.y);
+            packed[j / 2] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+            __half hh[2];
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                float x = v[j + u] + sbias[j + u];
+                if (prelu) x = x > 0.0f ? x : sslope[j + u] * x;
+                __half h = __float2half_rn(x);
+                if (RES) h = __float2half_rn(__half2float(h) + rv[j + u]);
+                if (AFF) h = __float2half_rn(2.0f / (1.0f + expf(-__half2float(h))) - 1.0f);
+                hh[u] = h;
+            }
+            packed[j / 2] = (uint32_t)__half_as_ushort(hh[0]) | ((uint32_t)__half_as_ushort(hh[1]) << 16);
+        }
     }
     if (full && vec_out) {
         reinterpret_cast<uint4*>(out + cg)[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
@@ -385,15 +406,17 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
     for (int c0 = 0; c0 < ngw; c0 += 16) {
         float v[16];
         {
-            uint32_t r[16];
+            // both accumulators' columns in flight together, one wait
+            uint32_t r[16], r2[16];
             const uint32_t ta = tbase + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
-            tmem_ld16(ta, r);
+            tmem_ld16_async(ta, r);
+            if (nis == 2) tmem_ld16_async(ta + (uint32_t)ngw, r2);
+            tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < 16; j++) v[j] = __uint_as_float(r[j]);
             if (nis == 2) {
-                tmem_ld16(ta + (uint32_t)ngw, r);
 #pragma unroll
-                for (int j = 0; j < 16; j++) v[j] += __uint_as_float(r[j]);
+                for (int j = 0; j < 16; j++) v[j] += __uint_as_float(r2[j]);
             }
         }
         const int cg = cbase + c0;  // output channel of column c0
