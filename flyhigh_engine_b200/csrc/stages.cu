@@ -65,9 +65,12 @@ __global__ void k_aa_axis(int in, int out, int* first, int* count, float* w) {
 
 // tex_in.wgsl:10-19 + interp.wgsl:29-43 (aa): the padded plane is never stored; taps read the rgba8 frame at the
 // clamped position (replicate padding). With axis tables the weights are read, not formed per tap.
+// NX: the most taps of any output along x (the tables' weights are zero past an output's own count, and a zero-weight
+// tap adds exactly zero, so every output runs NX taps per row and ny_max rows, in the reference's order, unpredicated)
+template <int NX>
 __global__ void k_frame_to_input(const uint8_t* __restrict__ frames, long long frame_bs, int w, int h, int hp, int wp,
                                  int internal, int oh, int ow, __half* out, long long out_bs, AaAxis ax, AaAxis ay,
-                                 int tex) {
+                                 int tex, int ny_max) {
     __shared__ float lut[256];
     for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y)
         lut[i] = tex ? texv(i) : u8v(i);
@@ -86,28 +89,27 @@ __global__ void k_frame_to_input(const uint8_t* __restrict__ frames, long long f
     }
     float ab = 0.0f, ag = 0.0f, ar = 0.0f, norm = 0.0f;
     if (ax.w) {
-        const int x0 = __ldg(ax.first + ox), nx = __ldg(ax.count + ox);
-        const int y0 = __ldg(ay.first + oy), ny = __ldg(ay.count + oy);
-        float wx[AA_TAPS];
-        int xs[AA_TAPS];
+        const int x0 = __ldg(ax.first + ox), y0 = __ldg(ay.first + oy);
+        float wx[NX];
+        int xs[NX];
 #pragma unroll
-        for (int j = 0; j < AA_TAPS; j++) {
+        for (int j = 0; j < NX; j++) {
             wx[j] = __ldg(ax.w + ox * AA_TAPS + j);
             xs[j] = min(x0 + j, w - 1);
         }
-        for (int yi = 0; yi < ny; yi++) {
+        for (int yi = 0; yi < ny_max; yi++) {
             const float wy = __ldg(ay.w + oy * AA_TAPS + yi);
             const uint32_t* row = f + min(y0 + yi, h - 1) * w;
+            uint32_t v[NX];
 #pragma unroll
-            for (int j = 0; j < AA_TAPS; j++) {
-                if (j < nx) {
-                    const float wgt = wx[j] * wy;
-                    const uint32_t v = __ldg(row + xs[j]);
-                    ab = ab + lut[(v >> 16) & 255] * wgt;
-                    ag = ag + lut[(v >> 8) & 255] * wgt;
-                    ar = ar + lut[v & 255] * wgt;
-                    norm = norm + wgt;
-                }
+            for (int j = 0; j < NX; j++) v[j] = __ldg(row + xs[j]);
+#pragma unroll
+            for (int j = 0; j < NX; j++) {
+                const float wgt = wx[j] * wy;
+                ab = ab + lut[(v[j] >> 16) & 255] * wgt;
+                ag = ag + lut[(v[j] >> 8) & 255] * wgt;
+                ar = ar + lut[v[j] & 255] * wgt;
+                norm = norm + wgt;
             }
         }
         st4(o, ab / norm, ag / norm, ar / norm);
@@ -1658,16 +1660,18 @@ __global__ void k_frame_planes(const uint8_t* f, int w, int h, int hp, int wp, f
 
 // --------------------------------------------------------------------------------------------------- launchers ----
 
-bool aa_axis_fits(int in, int out) {
-    // the same arithmetic as aa_span on the host (IEEE single precision, no contraction)
+// the most taps of any output index along an axis (the same arithmetic as aa_span, IEEE single precision, no contraction)
+int aa_axis_max(int in, int out) {
     const float s_ = (float)in / (float)out, f = std::max(s_, 1.0f);
+    int m = 0;
     for (int o = 0; o < out; o++) {
         const float c = ((float)o + 0.5f) * s_;
         const int lo = std::max(0, (int)std::floor(c - f + 0.5f)), hi = std::min(in, (int)std::floor(c + f + 0.5f));
-        if (hi - lo > AA_TAPS) return false;
+        m = std::max(m, hi - lo);
     }
-    return true;
+    return m;
 }
+bool aa_axis_fits(int in, int out) { return aa_axis_max(in, out) <= AA_TAPS; }
 
 cudaError_t aa_axis(int in, int out, int* first, int* count, float* w, cudaStream_t st) {
     k_aa_axis<<<(out + 127) / 128, 128, 0, st>>>(in, out, first, count, w);
@@ -1677,9 +1681,25 @@ cudaError_t aa_axis(int in, int out, int* first, int* count, float* w, cudaStrea
 cudaError_t frame_to_input(const uint8_t* frames, long long frame_bs, int w, int h, int hp, int wp, bool internal, int ih,
                            int iw, Img4 out, int n, cudaStream_t st, AaAxis ax, AaAxis ay, bool tex) {
     const int oh = internal ? ih : hp, ow = internal ? iw : wp;
-    if (!ax.w || !ay.w) ax = ay = AaAxis{};
-    { const cudaError_t e_ = launch(k_frame_to_input, grid2(ow, oh, n), dim3(16, 16), 0, st, frames, frame_bs, w, h, hp, wp, internal ? 1 : 0, oh, ow,
-                                                               out.p, out.bs, ax, ay, tex ? 1 : 0); if (e_ != cudaSuccess) return e_; }
+    if (!ax.w || !ay.w || !internal) ax = ay = AaAxis{};
+    // the tables' tap counts (the kernel runs the widest on every output; 8 when there are no tables)
+    const int nx = ax.w ? aa_axis_max(wp, ow) : AA_TAPS, ny = ay.w ? aa_axis_max(hp, oh) : AA_TAPS;
+    auto go = [&](auto kern) {
+        return launch(kern, grid2(ow, oh, n), dim3(16, 16), 0, st, frames, frame_bs, w, h, hp, wp, internal ? 1 : 0, oh, ow,
+                      out.p, out.bs, ax, ay, tex ? 1 : 0, ny);
+    };
+    cudaError_t e_;
+    switch (nx) {
+        case 1: e_ = go(k_frame_to_input<1>); break;
+        case 2: e_ = go(k_frame_to_input<2>); break;
+        case 3: e_ = go(k_frame_to_input<3>); break;
+        case 4: e_ = go(k_frame_to_input<4>); break;
+        case 5: e_ = go(k_frame_to_input<5>); break;
+        case 6: e_ = go(k_frame_to_input<6>); break;
+        case 7: e_ = go(k_frame_to_input<7>); break;
+        default: e_ = go(k_frame_to_input<8>); break;
+    }
+    if (e_ != cudaSuccess) return e_;
     return cudaGetLastError();
 }
 
