@@ -866,8 +866,14 @@ __global__ void k_box_h(const float* src, long long src_bs, float* dst, long lon
     if (x >= w || y >= h) return;
     const float* row = src + n * src_bs + ((long long)ch * h + y) * w;
     float acc = 0.0f;
+    if (x - r >= 0 && x + r <= w - 1) {  // no tap clamped: one base, fixed offsets
+        const float* p = row + x - r;
 #pragma unroll 8
-    for (int d = -r; d <= r; d++) acc = acc + row[clampi(x + d, 0, w - 1)];
+        for (int d = 0; d <= 2 * r; d++) acc = acc + __ldg(p + d);
+    } else {
+#pragma unroll 8
+        for (int d = -r; d <= r; d++) acc = acc + __ldg(row + clampi(x + d, 0, w - 1));
+    }
     dst[n * dst_bs + ((long long)ch * h + y) * w + x] = acc / (float)(2 * r + 1);
 }
 __global__ void k_box_v(const float* src, long long src_bs, float* dst, long long dst_bs, int c, int h, int w, int r) {
@@ -878,8 +884,14 @@ __global__ void k_box_v(const float* src, long long src_bs, float* dst, long lon
     if (x >= w || y >= h) return;
     const float* plane = src + n * src_bs + (long long)ch * h * w;
     float acc = 0.0f;
+    if (y - r >= 0 && y + r <= h - 1) {  // no tap clamped: one base, a fixed stride
+        const float* p = plane + (long long)(y - r) * w + x;
 #pragma unroll 8
-    for (int d = -r; d <= r; d++) acc = acc + plane[(long long)clampi(y + d, 0, h - 1) * w + x];
+        for (int d = 0; d <= 2 * r; d++) acc = acc + __ldg(p + (long long)d * w);
+    } else {
+#pragma unroll 8
+        for (int d = -r; d <= r; d++) acc = acc + __ldg(plane + (long long)clampi(y + d, 0, h - 1) * w + x);
+    }
     dst[n * dst_bs + (long long)ch * h * w + (long long)y * w + x] = acc / (float)(2 * r + 1);
 }
 // gm_select.wgsl:12-15: the cost cell that select sample j (of w8) reads, along one axis of hc or wc cells
@@ -896,8 +908,14 @@ __global__ void k_box_h_cols(GmArgs g, long long cols_bs) {
     const int r = ch < 3 ? g.r_dwin : g.r_blk, x = gm_cell(j, g.wc, g.w8);
     const float* row = g.maps + (long long)n * 6 * g.hc * g.wc + ((long long)ch * g.hc + y) * g.wc;
     float acc = 0.0f;
+    if (x - r >= 0 && x + r <= g.wc - 1) {
+        const float* p = row + x - r;
 #pragma unroll 8
-    for (int d = -r; d <= r; d++) acc = acc + row[clampi(x + d, 0, g.wc - 1)];
+        for (int d = 0; d <= 2 * r; d++) acc = acc + __ldg(p + d);
+    } else {
+#pragma unroll 8
+        for (int d = -r; d <= r; d++) acc = acc + __ldg(row + clampi(x + d, 0, g.wc - 1));
+    }
     g.tmp[(long long)n * cols_bs + ((long long)ch * g.hc + y) * g.w8 + j] = acc / (float)(2 * r + 1);
 }
 
