@@ -236,6 +236,7 @@ __global__ void k_input_pyramid(const __half* __restrict__ A, long long a_bs, in
 
 // -------------------------------------------------------------------------------------------- static age pass ----
 
+constexpr int PP_ROWS = 4;  // rows per thread of k_pair_planes
 // The per-pair planes over the padded plane (a, b read at the clamped position):
 //  - changed = keep_static_age.wgsl:52-56 `diff(o) >= thr` (the age pass probes it 41 times per pixel), one bit per
 //    pixel: row y is words [y * ww, (y + 1) * ww), bit j of word k = pixel 32 k + j, zero past the padded width;
@@ -252,61 +253,83 @@ __global__ void __launch_bounds__(256) k_pair_planes(const uint8_t* __restrict__
     __syncthreads();
     pdl_wait();
     pdl_trigger();
-    const int x = blockIdx.x * 32 + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
-    if (y >= s.hp) return;  // warp-uniform
+    // a block covers 32 columns x PP_ROWS * 8 rows: warp row ty takes rows ty, ty + 8, ..., every load issued first
+    const int x = blockIdx.x * 32 + threadIdx.x, n = blockIdx.z;
     const bool in = x < s.wp;
-    uint32_t a = 0, b = 0;
-    if (in) {
-        const long long src = (long long)min(y, s.h - 1) * s.w + min(x, s.w - 1);
-        a = __ldg(reinterpret_cast<const uint32_t*>(fa + n * frame_bs) + src);
-        b = __ldg(reinterpret_cast<const uint32_t*>(fb + n * frame_bs) + src);
-    }
-    // |A - B| per channel, once for both planes
-    float d[3];
+    const uint32_t* A = reinterpret_cast<const uint32_t*>(fa + n * frame_bs);
+    const uint32_t* B = reinterpret_cast<const uint32_t*>(fb + n * frame_bs);
+    uint32_t a[PP_ROWS], b[PP_ROWS];
 #pragma unroll
-    for (int c = 0; c < 3; c++) {
-        const int sh = 16 - 8 * c;  // B, G, R
-        d[c] = fabsf(lut[(a >> sh) & 255] - lut[(b >> sh) & 255]);
+    for (int r = 0; r < PP_ROWS; r++) {
+        const int y = blockIdx.y * (PP_ROWS * 8) + threadIdx.y + 8 * r;
+        a[r] = b[r] = 0;
+        if (in && y < s.hp) {
+            const long long src = (long long)min(y, s.h - 1) * s.w + min(x, s.w - 1);
+            a[r] = __ldg(A + src);
+            b[r] = __ldg(B + src);
+        }
     }
-    if (changed) {
-        const float dm = fmaxf(fmaxf(d[0], d[1]), d[2]);  // diff(o): the channel maximum
-        const uint32_t word = __ballot_sync(0xffffffffu, in && dm >= s.thr);
-        if (threadIdx.x == 0) changed[n * changed_bs + (long long)y * ((s.wp + 31) >> 5) + blockIdx.x] = word;
-    }
-    if (dsum && in) {
-        // the fast render's still-test term instead: dot(|A - B|.rgb, 1 / 3), R first (render_tex.wgsl:93-98)
-        const float third = 1.0f / 3.0f;
-        dsum[n * dsum_bs + (long long)y * s.wp + x] = s.tex ? d[2] * third + d[1] * third + d[0] * third
-                                                             : (d[0] + d[1]) + d[2];
+#pragma unroll
+    for (int r = 0; r < PP_ROWS; r++) {
+        const int y = blockIdx.y * (PP_ROWS * 8) + threadIdx.y + 8 * r;
+        if (y >= s.hp) break;  // warp-uniform
+        // |A - B| per channel, once for both planes
+        float d[3];
+#pragma unroll
+        for (int c = 0; c < 3; c++) {
+            const int sh = 16 - 8 * c;  // B, G, R
+            d[c] = fabsf(lut[(a[r] >> sh) & 255] - lut[(b[r] >> sh) & 255]);
+        }
+        if (changed) {
+            const float dm = fmaxf(fmaxf(d[0], d[1]), d[2]);  // diff(o): the channel maximum
+            const uint32_t word = __ballot_sync(0xffffffffu, in && dm >= s.thr);
+            if (threadIdx.x == 0) changed[n * changed_bs + (long long)y * ((s.wp + 31) >> 5) + blockIdx.x] = word;
+        }
+        if (dsum && in) {
+            // the fast render's still-test term instead: dot(|A - B|.rgb, 1 / 3), R first (render_tex.wgsl:93-98)
+            const float third = 1.0f / 3.0f;
+            dsum[n * dsum_bs + (long long)y * s.wp + x] = s.tex ? d[2] * third + d[1] * third + d[0] * third
+                                                                 : (d[0] + d[1]) + d[2];
+        }
     }
 }
 
 // render_static's on_static (gpu/pipeline.rs:10-34) per pixel: an age >= min_age in the clamped 3 x 3 neighbourhood.
 // A warp is one 32-pixel row segment (blocks of 32 x 8): each lane tests its column over rows y - 1 .. y + 1, the
 // ballot of those tests is shifted one column each way, and lanes 0 and 31 test the columns either side of the segment.
+constexpr int NEAR_ROWS = 4;
 // W x H: the region covered and clamped to (the padded plane, or the frame for the fast render); pitch: the planes' row
 // pitch in elements
 __global__ void __launch_bounds__(256) k_static_near(const int16_t* __restrict__ age, long long bs, int pitch, int W,
                                                      int H, float min_age, uint8_t* near) {
     pdl_wait();
     pdl_trigger();
-    const int lane = threadIdx.x, x0 = blockIdx.x * 32, x = x0 + lane, y = blockIdx.y * blockDim.y + threadIdx.y;
-    if (y >= H) return;  // warp-uniform
+    // a thread takes NEAR_ROWS consecutive rows: rows y0 - 1 .. y0 + NEAR_ROWS of its column (and of its outer column)
+    // are loaded once and tested once, each output row ORs three of them
+    const int lane = threadIdx.x, x0 = blockIdx.x * 32, x = x0 + lane;
+    const int y0 = (blockIdx.y * blockDim.y + threadIdx.y) * NEAR_ROWS;
+    if (y0 >= H) return;  // warp-uniform
     const int16_t* __restrict__ ag = age + blockIdx.z * bs;
-    const long long r0 = (long long)max(y - 1, 0) * pitch, r1 = (long long)y * pitch,
-                    r2 = (long long)min(y + 1, H - 1) * pitch;
-    auto column = [&](int c) {  // the three loads issued together, no short-circuit
-        const int16_t a0 = __ldg(ag + r0 + c), a1 = __ldg(ag + r1 + c), a2 = __ldg(ag + r2 + c);
-        return ((float)a0 >= min_age) | ((float)a1 >= min_age) | ((float)a2 >= min_age);
-    };
     // lanes past the plane's width test its last column, the clamp of their left neighbour's right column; every
     // lane also tests an outer column (x0 - 1 for lane 0, else x0 + 32; one address for lanes 1-31), so the loads
     // issue together without a divergent branch, and lanes 0 and 31 supply the ballot bits used
-    const bool own_hit = column(min(x, W - 1)), edge_hit = column(lane == 0 ? max(x0 - 1, 0) : min(x0 + 32, W - 1));
-    const uint32_t col = __ballot_sync(0xffffffffu, own_hit);
-    const uint32_t eb = __ballot_sync(0xffffffffu, edge_hit);
-    const uint32_t nb = col | (col << 1) | (eb & 1u) | (col >> 1) | (eb & 0x80000000u);
-    if (x < W) near[blockIdx.z * bs + r1 + x] = (uint8_t)((nb >> lane) & 1u);
+    const int xc = min(x, W - 1), xe = lane == 0 ? max(x0 - 1, 0) : min(x0 + 32, W - 1);
+    bool own[NEAR_ROWS + 2], edge[NEAR_ROWS + 2];
+#pragma unroll
+    for (int k = 0; k < NEAR_ROWS + 2; k++) {
+        const long long row = (long long)clampi(y0 - 1 + k, 0, H - 1) * pitch;
+        own[k] = (float)__ldg(ag + row + xc) >= min_age;
+        edge[k] = (float)__ldg(ag + row + xe) >= min_age;
+    }
+#pragma unroll
+    for (int k = 0; k < NEAR_ROWS; k++) {
+        const int y = y0 + k;
+        if (y >= H) break;  // warp-uniform
+        const uint32_t col = __ballot_sync(0xffffffffu, own[k] | own[k + 1] | own[k + 2]);
+        const uint32_t eb = __ballot_sync(0xffffffffu, edge[k] | edge[k + 1] | edge[k + 2]);
+        const uint32_t nb = col | (col << 1) | (eb & 1u) | (col >> 1) | (eb & 0x80000000u);
+        if (x < W) near[blockIdx.z * bs + (long long)y * pitch + x] = (uint8_t)((nb >> lane) & 1u);
+    }
 }
 
 // 32 bits of row `row` of the changed plane: bit i = changed(clamp(s0 + i, 0, W - 1)), the replicate clamp of the
@@ -1730,14 +1753,14 @@ cudaError_t input_pyramid(Img4 A, int ih, int iw, Img4 aq, Img4 i8, Img4 i16, in
 
 cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, long long frame_bs, const StaticArgs& s, uint32_t* changed,
                         long long changed_bs, float* dsum, long long dsum_bs, int n, cudaStream_t st) {
-    { const cudaError_t e_ = launch(k_pair_planes, grid2(s.wp, s.hp, n, 32, 8), dim3(32, 8), 0, st, fa, fb, frame_bs, s, changed, changed_bs, dsum, dsum_bs); if (e_ != cudaSuccess) return e_; }
+    { const cudaError_t e_ = launch(k_pair_planes, grid2(s.wp, s.hp, n, 32, 8 * PP_ROWS), dim3(32, 8), 0, st, fa, fb, frame_bs, s, changed, changed_bs, dsum, dsum_bs); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
 cudaError_t static_near(const int16_t* age, long long bs, int wp, int hp, float min_age, uint8_t* near, int n,
                         cudaStream_t st, int cw_, int ch_) {
     const int cw = cw_ > 0 ? cw_ : wp, ch = ch_ > 0 ? ch_ : hp;
-    { const cudaError_t e_ = launch(k_static_near, grid2(cw, ch, n, 32, 8), dim3(32, 8), 0, st, age, bs, wp, cw, ch, min_age, near); if (e_ != cudaSuccess) return e_; }
+    { const cudaError_t e_ = launch(k_static_near, grid2(cw, ch, n, 32, 8 * NEAR_ROWS), dim3(32, 8), 0, st, age, bs, wp, cw, ch, min_age, near); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 
