@@ -389,6 +389,7 @@ struct FhSession {
     // frame-stage scratch, pair and mid buffers
     __half *e1 = nullptr, *e3 = nullptr;
     uint32_t* changed = nullptr;
+    uint32_t* moved = nullptr;
     uint32_t* spread = nullptr;  // the static age pass's byte thresholds
     uint8_t* mask = nullptr;
     uchar4* state = nullptr;
@@ -697,6 +698,7 @@ struct FhSession {
         e3 = img(h16, w16, C16P, nf);
         if (protects) {
             changed = alloc_n<uint32_t>((size_t)nb * hp * fhk::changed_words(wp));
+            moved = alloc_n<uint32_t>((size_t)nb * hp * fhk::changed_words(wp));
             spread = alloc_n<uint32_t>(256);
             CK(fhk::spread_table(spread, st, fast));
             mask = alloc_n<uint8_t>((size_t)hp * wp);
@@ -828,9 +830,11 @@ struct FhSession {
                                     still ? dsum : nullptr, P, n, st));
                 mark("pair_planes");
                 if (protects) {
+                    CK(fhk::moved_plane(changed, CW, wp, hp, moved, n, st));
+                    mark("moved_plane");
                     const long long l = n - 1;
                     CK(fhk::static_age(A.frame + l * A.frame_bs, B.frame + l * B.frame_bs, -A.frame_bs, changed + l * CW,
-                                       -CW, mask, sargs, state, age + l * P, -P, n, spread, st));
+                                       moved + l * CW, -CW, mask, sargs, state, age + l * P, -P, n, spread, st));
                     mark("static_age");
                     // the fast render's probes clamp to the frame, the exact render's to the padded plane
                     CK(fhk::static_near(age, P, wp, hp, min_age, nearp, n, st, fast ? w : 0, fast ? h : 0));
@@ -1881,7 +1885,9 @@ int fh_session_advance_static(const FhSession* cs, uint32_t a, uint32_t b) {
         s->wait_upload(A);
         s->wait_upload(B);
         CK(fhk::pair_planes(A.frame, B.frame, 0, s->sargs, s->changed, 0, nullptr, 0, 1, s->st));
-        CK(fhk::static_age(A.frame, B.frame, 0, s->changed, 0, s->mask, s->sargs, s->state, s->age, 0, 1, s->spread, s->st));
+        CK(fhk::moved_plane(s->changed, 0, s->wp, s->hp, s->moved, 1, s->st));
+        CK(fhk::static_age(A.frame, B.frame, 0, s->changed, s->moved, 0, s->mask, s->sargs, s->state, s->age, 0, 1,
+                           s->spread, s->st));
         s->mark_read(A, B);
         return 0;
     });

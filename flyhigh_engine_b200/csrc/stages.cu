@@ -332,24 +332,75 @@ __global__ void __launch_bounds__(256) k_static_near(const int16_t* __restrict__
     }
 }
 
-// 32 bits of row `row` of the changed plane: bit i = changed(clamp(s0 + i, 0, W - 1)), the replicate clamp of the
-// shader's probes
-FH_DEV uint32_t bit_window(const uint32_t* __restrict__ row, int ww, int W, int s0) {
-    const int k = s0 >> 5, r = s0 & 31;  // floor division, also for negative starts
-    const uint32_t w0 = (k >= 0 && k < ww) ? __ldg(row + k) : 0u;
-    const uint32_t w1 = (k + 1 >= 0 && k + 1 < ww) ? __ldg(row + k + 1) : 0u;
-    uint32_t v = __funnelshift_r(w0, w1, r);
-    if (s0 < 0) {  // lanes left of pixel 0 read pixel 0
-        const int lo = -s0;
-        const uint32_t m = lo >= 32 ? 0xffffffffu : ((1u << lo) - 1u);
-        v = (v & ~m) | ((__ldg(row) & 1u) ? m : 0u);
+// Pixels kw * 32 - 32 .. kw * 32 + 63 of one row of the changed plane (W bits) as three words m, c, p, each bit the
+// pixel's clamp to 0 .. W - 1 (the replicate clamp of the shader's probes): left of pixel 0 pixel 0, right of pixel
+// W - 1 pixel W - 1. Then every probe window of |dx| <= 32 is one funnel shift.
+struct RowWords {
+    uint32_t m, c, p;
+};
+FH_DEV RowWords row_words(const uint32_t* __restrict__ row, int ww, int W, int kw) {
+    RowWords r;
+    r.c = __ldg(row + kw);
+    const uint32_t pr = kw + 1 < ww ? __ldg(row + kw + 1) : 0u;
+    r.m = kw > 0 ? __ldg(row + kw - 1) : 0u - (r.c & 1u);
+    // the word of pixel W - 1 is c or p for the last two words of the row; pixels past it read it
+    const int lb = (W - 1) & 31;
+    const uint32_t keep = lb == 31 ? 0xffffffffu : ((2u << lb) - 1u);
+    const uint32_t fill = 0u - (((kw == ww - 1 ? r.c : pr) >> lb) & 1u);
+    r.p = pr;
+    if (kw == ww - 1) {
+        r.c = (r.c & keep) | (fill & ~keep);
+        r.p = fill;
+    } else if (kw == ww - 2) {
+        r.p = (pr & keep) | (fill & ~keep);
     }
-    const int hi = W - s0;  // lanes i >= hi read pixel W - 1
-    if (hi < 32) {
-        const uint32_t m = hi <= 0 ? 0xffffffffu : ~((1u << hi) - 1u);
-        v = (v & ~m) | (((__ldg(row + ((W - 1) >> 5)) >> ((W - 1) & 31)) & 1u) ? m : 0u);
+    return r;
+}
+// 32 bits of the row: bit i = changed(clamp(32 kw + DX + i, 0, W - 1))
+template <int DX>
+FH_DEV uint32_t row_window(const RowWords& r) {
+    static_assert(DX >= -32 && DX <= 32, "one word either side");
+    return DX < 0 ? __funnelshift_r(r.m, r.c, DX + 32) : (DX < 32 ? __funnelshift_r(r.c, r.p, DX) : r.p);
+}
+// keep_static_age.wgsl:59-70's `moved` for the 32 pixels of word kw of row y: the OR over the 41 probes (the clamped
+// 3 x 3 neighbourhood and the far ring: 8 directions at distances 4, 8, 16, 32) of the changed plane (W x H, ww
+// words per row). Eleven rows, three words of each, all loaded before the windows are formed.
+FH_DEV uint32_t moved_word(const uint32_t* __restrict__ ch, int ww, int W, int H, int kw, int y) {
+    constexpr int D[5] = {1, 4, 8, 16, 32};
+    RowWords dn[5], up[5];
+    const RowWords r0 = row_words(ch + (long long)y * ww, ww, W, kw);
+#pragma unroll
+    for (int i = 0; i < 5; i++) {
+        dn[i] = row_words(ch + (long long)min(y + D[i], H - 1) * ww, ww, W, kw);
+        up[i] = row_words(ch + (long long)max(y - D[i], 0) * ww, ww, W, kw);
     }
-    return v;
+    // row y: dx 0, +-1 (the 3 x 3 neighbourhood) and +-4 .. +-32 (directions 0, 1); rows y +- d: dx -d, 0, +d
+    // (the 3 x 3 neighbourhood for d = 1; directions 2, 4, 5 and 3, 6, 7 of the far ring)
+    uint32_t mv = row_window<0>(r0) | row_window<-1>(r0) | row_window<1>(r0) | row_window<-4>(r0) |
+                  row_window<4>(r0) | row_window<-8>(r0) | row_window<8>(r0) | row_window<-16>(r0) |
+                  row_window<16>(r0) | row_window<-32>(r0) | row_window<32>(r0);
+    mv |= row_window<-1>(dn[0]) | row_window<0>(dn[0]) | row_window<1>(dn[0]) | row_window<-1>(up[0]) |
+          row_window<0>(up[0]) | row_window<1>(up[0]);
+    mv |= row_window<-4>(dn[1]) | row_window<0>(dn[1]) | row_window<4>(dn[1]) | row_window<-4>(up[1]) |
+          row_window<0>(up[1]) | row_window<4>(up[1]);
+    mv |= row_window<-8>(dn[2]) | row_window<0>(dn[2]) | row_window<8>(dn[2]) | row_window<-8>(up[2]) |
+          row_window<0>(up[2]) | row_window<8>(up[2]);
+    mv |= row_window<-16>(dn[3]) | row_window<0>(dn[3]) | row_window<16>(dn[3]) | row_window<-16>(up[3]) |
+          row_window<0>(up[3]) | row_window<16>(up[3]);
+    mv |= row_window<-32>(dn[4]) | row_window<0>(dn[4]) | row_window<32>(dn[4]) | row_window<-32>(up[4]) |
+          row_window<0>(up[4]) | row_window<32>(up[4]);
+    return mv;
+}
+
+// The moved plane: moved_word for every word of n changed planes (W x H bits, bs words apart), one thread per word
+__global__ void __launch_bounds__(256) k_moved_plane(const uint32_t* __restrict__ changed, long long bs, int W, int H,
+                                                     uint32_t* moved) {
+    pdl_wait();
+    pdl_trigger();
+    const int ww = (W + 31) >> 5, kw = blockIdx.x * 32 + threadIdx.x, y = blockIdx.y * 8 + threadIdx.y;
+    if (kw >= ww || y >= H) return;
+    const long long n = blockIdx.z;
+    moved[n * bs + (long long)y * ww + kw] = moved_word(changed + n * bs, ww, W, H, kw, y);
 }
 
 // The spread test per channel, v(q) - v(o) >= 0.03 or v(o) - v(q) >= 0.03 in f32 (v = the byte -> value table), as
@@ -438,15 +489,16 @@ FH_DEV bool frame_spread(const Ext3& e, const uint32_t* tab) {
 // for np consecutive pairs in time order (pair i: frames fa + i * frame_bs, fb + i * frame_bs, its changed plane and its
 // age plane; strides may be negative). A pixel's state is loaded once, advanced pair by pair and stored once: the
 // pairs' sequential dependence is per pixel only.
-// A warp is one 32-pixel row segment. moved: lane l evaluates probe l (and probe 32 + l) as a 32-bit window of the
-// changed bits for the whole segment, and the warp ORs the windows. spread: max over the clamped 3 x 3 neighbourhood
-// and channels of |a(q) - a(o)|, |b(q) - b(o)|; the byte -> value table is monotone and f32 subtraction is monotone
-// in each operand, so that max is max(v(max_q) - v(o), v(o) - v(min_q)) per channel, exactly; its test against
-// 0.03 is a byte threshold per o (k_spread_table). When the pairs are chained (pair i's second frame is pair i + 1's
-// first, fa + frame_bs == fb) the extremes of a frame are computed once and serve both of its pairs.
+// A warp is one 32-pixel row segment: moved and same are bits of the moved plane (k_moved_plane) and of the changed
+// plane, one word each per pair. spread: max over the clamped 3 x 3 neighbourhood and channels of |a(q) - a(o)|,
+// |b(q) - b(o)|; the byte -> value table is monotone and f32 subtraction is monotone in each operand, so that max is
+// max(v(max_q) - v(o), v(o) - v(min_q)) per channel, exactly; its test against 0.03 is a byte threshold per o
+// (k_spread_table). When the pairs are chained (pair i's second frame is pair i + 1's first, fa + frame_bs == fb) a
+// frame's spread test is formed once and serves both of its pairs.
 __global__ void __launch_bounds__(256) k_static_age(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb,
                                                     long long frame_bs, const uint32_t* __restrict__ changed,
-                                                    long long changed_bs, const uint8_t* __restrict__ mask, StaticArgs s,
+                                                    const uint32_t* __restrict__ moved_plane, long long changed_bs,
+                                                    const uint8_t* __restrict__ mask, StaticArgs s,
                                                     uchar4* state, int16_t* age, long long age_bs, int np,
                                                     const uint32_t* __restrict__ spread) {
     __shared__ uint32_t spread_tab[256];
@@ -463,35 +515,23 @@ __global__ void __launch_bounds__(256) k_static_age(const uint8_t* __restrict__ 
     const long long o = (long long)y * W + x;
     uchar4 st = active ? state[o] : make_uchar4(0, 0, 0, 0);
     const bool masked = active && s.use_mask && mask && mask[o];
-    // probes 0-31 are the far ring (direction l >> 2, distance 4 << (l & 3)), 32-40 the 3 x 3 neighbourhood
-    int pdx, pdy;
-    {
-        const int DX[8] = {1, -1, 0, 0, 1, -1, 1, -1}, DY[8] = {0, 0, 1, -1, 1, 1, -1, -1};
-        const int far = 4 << (lane & 3), dir = lane >> 2;
-        pdx = pdy = 0;
-#pragma unroll
-        for (int i = 0; i < 8; i++)
-            if (dir == i) {
-                pdx = DX[i] * far;
-                pdy = DY[i] * far;
-            }
-    }
     const int r0 = min(max(y - 1, 0), s.h - 1), r1 = min(y, s.h - 1), r2 = min(y + 1, s.h - 1);
     const int xc = min(x, s.w - 1);
     const int xe = lane == 0 ? min(max(x0 - 1, 0), s.w - 1) : min(x0 + 32, s.w - 1);
     const bool chained = fa + frame_bs == fb;
-    Ext3 ea = frame_ext3(reinterpret_cast<const uint32_t*>(fa), s.w, r0, r1, r2, xc, xe, lane);
+    bool spread_a =
+        frame_spread(frame_ext3(reinterpret_cast<const uint32_t*>(fa), s.w, r0, r1, r2, xc, xe, lane), spread_tab);
     for (int pi = 0; pi < np; pi++) {
-        const uint32_t* ch = changed + pi * changed_bs;
-        uint32_t mv = bit_window(ch + (long long)clampi(y + pdy, 0, H - 1) * ww, ww, W, x0 + pdx);
-        if (lane < 9) mv |= bit_window(ch + (long long)clampi(y + lane / 3 - 1, 0, H - 1) * ww, ww, W, x0 + lane % 3 - 1);
-        mv = __reduce_or_sync(0xffffffffu, mv);
-        const uint32_t own_word = __ldg(ch + (long long)y * ww + blockIdx.x);
+        const long long wo = pi * changed_bs + (long long)y * ww + blockIdx.x;
+        const uint32_t mv = __ldg(moved_plane + wo), own_word = __ldg(changed + wo);
         if (pi > 0 && !chained)
-            ea = frame_ext3(reinterpret_cast<const uint32_t*>(fa + pi * frame_bs), s.w, r0, r1, r2, xc, xe, lane);
-        const Ext3 eb = frame_ext3(reinterpret_cast<const uint32_t*>(fb + pi * frame_bs), s.w, r0, r1, r2, xc, xe, lane);
-        const bool spread_ab = frame_spread(ea, spread_tab) || frame_spread(eb, spread_tab);
-        ea = eb;  // the next pair's first frame when chained
+            spread_a = frame_spread(
+                frame_ext3(reinterpret_cast<const uint32_t*>(fa + pi * frame_bs), s.w, r0, r1, r2, xc, xe, lane),
+                spread_tab);
+        const bool spread_b = frame_spread(
+            frame_ext3(reinterpret_cast<const uint32_t*>(fb + pi * frame_bs), s.w, r0, r1, r2, xc, xe, lane), spread_tab);
+        const bool spread_ab = spread_a || spread_b;
+        spread_a = spread_b;  // the next pair's first frame when chained
         if (!active) continue;
         const bool moved = (mv >> lane) & 1u;
         const bool same = ((own_word >> lane) & 1u) == 0;
@@ -1769,11 +1809,16 @@ cudaError_t spread_table(uint32_t* out, cudaStream_t st, bool tex) {
     return cudaGetLastError();
 }
 
+cudaError_t moved_plane(const uint32_t* changed, long long bs, int wp, int hp, uint32_t* moved, int n, cudaStream_t st) {
+    { const cudaError_t e_ = launch(k_moved_plane, grid2(changed_words(wp), hp, n, 32, 8), dim3(32, 8), 0, st, changed, bs, wp, hp, moved); if (e_ != cudaSuccess) return e_; }
+    return cudaGetLastError();
+}
+
 cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, long long frame_bs, const uint32_t* changed,
-                       long long changed_bs, const uint8_t* mask, const StaticArgs& s, uchar4* state, int16_t* age,
-                       long long age_bs, int np, const uint32_t* spread, cudaStream_t st) {
+                       const uint32_t* moved, long long changed_bs, const uint8_t* mask, const StaticArgs& s,
+                       uchar4* state, int16_t* age, long long age_bs, int np, const uint32_t* spread, cudaStream_t st) {
     if (np < 1 || !spread) return cudaErrorInvalidValue;
-    { const cudaError_t e_ = launch(k_static_age, grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st, fa, fb, frame_bs, changed, changed_bs, mask, s, state, age, age_bs, np, spread); if (e_ != cudaSuccess) return e_; }
+    { const cudaError_t e_ = launch(k_static_age, grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st, fa, fb, frame_bs, changed, moved, changed_bs, mask, s, state, age, age_bs, np, spread); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 

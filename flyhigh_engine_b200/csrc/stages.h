@@ -56,12 +56,15 @@ cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, long long frame_bs
 // (cw, ch: the region, clamped to itself; 0 = the padded plane. The fast render's on_static clamps to the frame.)
 cudaError_t static_near(const int16_t* age, long long bs, int wp, int hp, float min_age, uint8_t* near, int n,
                         cudaStream_t st, int cw = 0, int ch = 0);
-// the age pass over np consecutive pairs in time order (pair i: frames fa / fb + i * frame_bs, changed + i *
+// per pair after pair_planes: moved = the changed plane dilated by the 41 probes of keep_static_age.wgsl:59-70 (the
+// clamped 3 x 3 neighbourhood and the far ring), same layout; n planes bs words apart
+cudaError_t moved_plane(const uint32_t* changed, long long bs, int wp, int hp, uint32_t* moved, int n, cudaStream_t st);
+// the age pass over np consecutive pairs in time order (pair i: frames fa / fb + i * frame_bs, changed / moved + i *
 // changed_bs, age + i * age_bs; strides may be negative), advancing the one state plane pair by pair
 // spread: the 256-entry byte-threshold table of the spread test (spread_table(), once per session)
 cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, long long frame_bs, const uint32_t* changed,
-                       long long changed_bs, const uint8_t* mask, const StaticArgs& s, uchar4* state, int16_t* age,
-                       long long age_bs, int np, const uint32_t* spread, cudaStream_t st);
+                       const uint32_t* moved, long long changed_bs, const uint8_t* mask, const StaticArgs& s,
+                       uchar4* state, int16_t* age, long long age_bs, int np, const uint32_t* spread, cudaStream_t st);
 cudaError_t spread_table(uint32_t* out, cudaStream_t st, bool tex = false);
 
 // luma.wgsl + sad.wgsl on two 3-channel images (a view at channel offset 0): (2r+1)^2 cost channels into out (cs)
