@@ -395,6 +395,7 @@ struct FhSession {
     uchar4* state = nullptr;
     int16_t* age = nullptr;
     float* dsum = nullptr;      // per pair: the still test's per-pixel |A - B| sums
+    float2* ownp = nullptr;     // per pair: the exact render's own-pixel (es, kk) plane (static_planes)
     uint8_t* nearp = nullptr;   // per pair: near a protected pixel
     __half *cv, *ch1, *ch2, *ch3r, *hcb, *ob, *fv, *wbuf, *fcv, *fr1, *fr2, *fr3, *wt36;
     float *coef, *maps, *tmp, *tdev;
@@ -707,6 +708,7 @@ struct FhSession {
             nearp = alloc_n<uint8_t>((size_t)nb * hp * wp);
         }
         if (still) dsum = alloc_n<float>((size_t)nb * hp * wp);
+        if (!fast && (still || protects)) ownp = alloc_n<float2>((size_t)nb * hp * wp);
         cv = img(h16, w16, 56, nb);
         ch1 = img(h16, w16, CCP, nb);
         ch2 = img(h16, w16, CCP, nb);
@@ -836,9 +838,16 @@ struct FhSession {
                     CK(fhk::static_age(A.frame + l * A.frame_bs, B.frame + l * B.frame_bs, -A.frame_bs, changed + l * CW,
                                        moved + l * CW, -CW, mask, sargs, state, age + l * P, -P, n, spread, st));
                     mark("static_age");
-                    // the fast render's probes clamp to the frame, the exact render's to the padded plane
-                    CK(fhk::static_near(age, P, wp, hp, min_age, nearp, n, st, fast ? w : 0, fast ? h : 0));
-                    mark("static_near");
+                }
+                // the fast render's probes clamp to the frame, the exact render's to the padded plane; the exact
+                // render also takes its own-pixel (es, kk) plane
+                if (fast && protects) {
+                    CK(fhk::static_planes(age, nullptr, P, wp, hp, min_age, nearp, nullptr, n, st, w, h));
+                    mark("static_planes");
+                } else if (!fast) {
+                    CK(fhk::static_planes(protects ? age : nullptr, still ? dsum : nullptr, P, wp, hp, min_age,
+                                          protects ? nearp : nullptr, ownp, n, st));
+                    mark("static_planes");
                 }
             });
         const long long ecv = E(h16, w16, 56), ecc = E(h16, w16, CCP), eob = E(h16, w16, 16), efv = E(h8, w8, 8),
@@ -906,7 +915,7 @@ struct FhSession {
             mark("render_tex");
         } else {
             fhk::RenderArgs ra{p.a.half, p.b.half, p.a.half_bs, w, h, hp, wp, up7, eup, rt, ert, qh, qw, fsx, fsy,
-                               cubic ? 1 : 0, (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, P, dsum,
+                               cubic ? 1 : 0, (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, P, ownp,
                                nearp, P, min_age, out, out_bs};
             CK(fhk::render(ra, n, st));
             mark("render");

@@ -294,41 +294,80 @@ __global__ void __launch_bounds__(256) k_pair_planes(const uint8_t* __restrict__
     }
 }
 
-// render_static's on_static (gpu/pipeline.rs:10-34) per pixel: an age >= min_age in the clamped 3 x 3 neighbourhood.
-// A warp is one 32-pixel row segment (blocks of 32 x 8): each lane tests its column over rows y - 1 .. y + 1, the
-// ballot of those tests is shifted one column each way, and lanes 0 and 31 test the columns either side of the segment.
+// The static planes the render reads, per pixel of the region, in one pass:
+//  - near (AGE): render_static's on_static (gpu/pipeline.rs:10-34), an age >= min_age in the clamped 3 x 3
+//    neighbourhood;
+//  - own (OWN): the render's terms at its own pixel, (es, kk). es = the still test's 27-term mean of |A - B| over the
+//    clamped 3 x 3 neighbourhood (render.wgsl:136-143): the sum of the 9 per-pixel channel sums (ES, from
+//    pair_planes; every partial sum is exact in f32, so the order does not matter) / 27; where the pixel's age is
+//    below 3 in magnitude (AGE: the static rules zero the still weight there) es is 1, which the still test's
+//    es < 0.03 turns into the same zero weight. kk = the keep_static apply ramp of the pixel's age
+//    (keep_static.wgsl:25-26), 0 without static protection. The render reads both in one 8-byte load.
+// A warp is one 32-pixel row segment (blocks of 32 x 8): each lane reduces its column over rows y - 1 .. y + 1, and the
+// columns either side come from the neighbouring lanes (a ballot shifted one column each way for near, shuffles for
+// es) or, for lanes 0 and 31, from the columns either side of the segment.
 constexpr int NEAR_ROWS = 4;
 // W x H: the region covered and clamped to (the padded plane, or the frame for the fast render); pitch: the planes' row
 // pitch in elements
-__global__ void __launch_bounds__(256) k_static_near(const int16_t* __restrict__ age, long long bs, int pitch, int W,
-                                                     int H, float min_age, uint8_t* near) {
+template <bool AGE, bool ES, bool OWN>
+__global__ void __launch_bounds__(256) k_static_planes(const int16_t* __restrict__ age, const float* __restrict__ dsum,
+                                                       long long bs, int pitch, int W, int H, float min_age,
+                                                       uint8_t* near, float2* own_plane) {
     pdl_wait();
     pdl_trigger();
     // a thread takes NEAR_ROWS consecutive rows: rows y0 - 1 .. y0 + NEAR_ROWS of its column (and of its outer column)
-    // are loaded once and tested once, each output row ORs three of them
+    // are loaded once, each output row combines three of them
     const int lane = threadIdx.x, x0 = blockIdx.x * 32, x = x0 + lane;
     const int y0 = (blockIdx.y * blockDim.y + threadIdx.y) * NEAR_ROWS;
     if (y0 >= H) return;  // warp-uniform
-    const int16_t* __restrict__ ag = age + blockIdx.z * bs;
-    // lanes past the plane's width test its last column, the clamp of their left neighbour's right column; every
-    // lane also tests an outer column (x0 - 1 for lane 0, else x0 + 32; one address for lanes 1-31), so the loads
-    // issue together without a divergent branch, and lanes 0 and 31 supply the ballot bits used
+    const int16_t* __restrict__ ag = AGE ? age + blockIdx.z * bs : nullptr;
+    const float* __restrict__ ds = ES ? dsum + blockIdx.z * bs : nullptr;
+    // lanes past the region's width read its last column, the clamp of their left neighbour's right column; every
+    // lane also reads an outer column (x0 - 1 for lane 0, else x0 + 32; one address for lanes 1-31), so the loads
+    // issue together without a divergent branch, and lanes 0 and 31 supply the outer terms used
     const int xc = min(x, W - 1), xe = lane == 0 ? max(x0 - 1, 0) : min(x0 + 32, W - 1);
-    bool own[NEAR_ROWS + 2], edge[NEAR_ROWS + 2];
+    int16_t ac[NEAR_ROWS + 2], ae[NEAR_ROWS + 2];
+    float dc[NEAR_ROWS + 2], de[NEAR_ROWS + 2];
 #pragma unroll
     for (int k = 0; k < NEAR_ROWS + 2; k++) {
         const long long row = (long long)clampi(y0 - 1 + k, 0, H - 1) * pitch;
-        own[k] = (float)__ldg(ag + row + xc) >= min_age;
-        edge[k] = (float)__ldg(ag + row + xe) >= min_age;
+        if (AGE) {
+            ac[k] = __ldg(ag + row + xc);
+            ae[k] = __ldg(ag + row + xe);
+        }
+        if (ES) {
+            dc[k] = __ldg(ds + row + xc);
+            de[k] = __ldg(ds + row + xe);
+        }
     }
 #pragma unroll
     for (int k = 0; k < NEAR_ROWS; k++) {
         const int y = y0 + k;
         if (y >= H) break;  // warp-uniform
-        const uint32_t col = __ballot_sync(0xffffffffu, own[k] | own[k + 1] | own[k + 2]);
-        const uint32_t eb = __ballot_sync(0xffffffffu, edge[k] | edge[k + 1] | edge[k + 2]);
-        const uint32_t nb = col | (col << 1) | (eb & 1u) | (col >> 1) | (eb & 0x80000000u);
-        if (x < W) near[blockIdx.z * bs + (long long)y * pitch + x] = (uint8_t)((nb >> lane) & 1u);
+        const long long o = blockIdx.z * bs + (long long)y * pitch + x;
+        if (AGE) {
+            auto on = [&](int16_t v) { return (float)v >= min_age; };
+            const uint32_t col = __ballot_sync(0xffffffffu, on(ac[k]) | on(ac[k + 1]) | on(ac[k + 2]));
+            const uint32_t eb = __ballot_sync(0xffffffffu, on(ae[k]) | on(ae[k + 1]) | on(ae[k + 2]));
+            const uint32_t nb = col | (col << 1) | (eb & 1u) | (col >> 1) | (eb & 0x80000000u);
+            if (x < W) near[o] = (uint8_t)((nb >> lane) & 1u);
+        }
+        if (OWN) {
+            float es = 0.0f, kk = 0.0f;
+            if (ES) {
+                const float col = dc[k] + dc[k + 1] + dc[k + 2], ecol = de[k] + de[k + 1] + de[k + 2];
+                float l = __shfl_up_sync(0xffffffffu, col, 1), r = __shfl_down_sync(0xffffffffu, col, 1);
+                if (lane == 0) l = ecol;
+                if (lane == 31) r = ecol;
+                es = ((l + col) + r) / 27.0f;
+            }
+            if (AGE) {
+                const float age_o = (float)ac[k + 1];
+                if (!(fabsf(age_o) >= 3.0f)) es = 1.0f;
+                kk = fminf(fmaxf((age_o - min_age + 2.0f) / 2.0f, 0.0f), 1.0f);
+            }
+            if (x < W) own_plane[o] = make_float2(es, kk);
+        }
     }
 }
 
@@ -1374,22 +1413,11 @@ __global__ void __launch_bounds__(256, 5) k_render(RenderArgs r) {
     const int here = y * r.w + x;  // x < w, y < h: no clamp
     const float3 pa_here = px3(A + here), pb_here = px3(B + here);
     const int o = y * W + x;
+    // the pixel's (es, kk) (static_planes): the still test's 27-term mean (1 where the static rules zero the still
+    // weight) and the keep_static ramp
+    const float2 ok = r.own ? __ldg(r.own + (long long)n * r.plane_bs + o) : make_float2(0.0f, 0.0f);
     if (r.flags & 2u) {
-        // the 27-term sum of |A - B| over the clamped 3 x 3 neighbourhood, from the per-pixel channel sums (exact)
-        const float* ds = r.dsum + (long long)n * r.plane_bs;
-        const int ym = max(y - 1, 0) * W, yc = y * W, yp = min(y + 1, H - 1) * W;
-        const int xm = max(x - 1, 0), xp = min(x + 1, W - 1);
-        float es = 0.0f;
-        es += __ldg(ds + ym + xm);
-        es += __ldg(ds + ym + x);
-        es += __ldg(ds + ym + xp);
-        es += __ldg(ds + yc + xm);
-        es += __ldg(ds + yc + x);
-        es += __ldg(ds + yc + xp);
-        es += __ldg(ds + yp + xm);
-        es += __ldg(ds + yp + x);
-        es += __ldg(ds + yp + xp);
-        es = es / 27.0f;
+        const float es = ok.x;
         for (int c = 0; c < 3; c++) own[c] = 0.5f * (comp(pa_here, c) + comp(pb_here, c));
         const float ef = fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
         stillw = fminf(fmaxf((ef - es) / 0.04f, 0.0f), 1.0f) * (es < 0.03f ? 1.0f : 0.0f);
@@ -1414,8 +1442,6 @@ __global__ void __launch_bounds__(256, 5) k_render(RenderArgs r) {
             return false;
         };
         const bool sa = on_static(gxa, gya), sb = on_static(gxb, gyb);
-        const float age_o = (float)age[o];
-        stillw = stillw * (fabsf(age_o) >= 3.0f ? 1.0f : 0.0f);
         if (sa && sb) {
             rk = 0.0f;
             raw = 1.0f;
@@ -1428,8 +1454,7 @@ __global__ void __launch_bounds__(256, 5) k_render(RenderArgs r) {
             bwa = 1.0f;
             bwb = 0.0f;
         }
-        // keep_static apply ramp (keep_static.wgsl:25-26)
-        kk = fminf(fmaxf((age_o - r.min_age + 2.0f) / 2.0f, 0.0f), 1.0f);
+        kk = ok.y;  // keep_static apply ramp (keep_static.wgsl:25-26)
     }
     uint32_t q[3];
 #pragma unroll
@@ -1797,10 +1822,17 @@ cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, long long frame_bs
     return cudaGetLastError();
 }
 
-cudaError_t static_near(const int16_t* age, long long bs, int wp, int hp, float min_age, uint8_t* near, int n,
-                        cudaStream_t st, int cw_, int ch_) {
+cudaError_t static_planes(const int16_t* age, const float* dsum, long long bs, int wp, int hp, float min_age,
+                          uint8_t* near, float2* own, int n, cudaStream_t st, int cw_, int ch_) {
     const int cw = cw_ > 0 ? cw_ : wp, ch = ch_ > 0 ? ch_ : hp;
-    { const cudaError_t e_ = launch(k_static_near, grid2(cw, ch, n, 32, 8 * NEAR_ROWS), dim3(32, 8), 0, st, age, bs, wp, cw, ch, min_age, near); if (e_ != cudaSuccess) return e_; }
+    if (!age != !near || (dsum && !own) || (!age && !own) || (!age && !dsum)) return cudaErrorInvalidValue;
+    const dim3 g = grid2(cw, ch, n, 32, 8 * NEAR_ROWS), b(32, 8);
+    const cudaError_t e =
+        !own    ? launch(k_static_planes<true, false, false>, g, b, 0, st, age, dsum, bs, wp, cw, ch, min_age, near, own)
+        : !dsum ? launch(k_static_planes<true, false, true>, g, b, 0, st, age, dsum, bs, wp, cw, ch, min_age, near, own)
+        : !age  ? launch(k_static_planes<false, true, true>, g, b, 0, st, age, dsum, bs, wp, cw, ch, min_age, near, own)
+                : launch(k_static_planes<true, true, true>, g, b, 0, st, age, dsum, bs, wp, cw, ch, min_age, near, own);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
@@ -1897,6 +1929,8 @@ cudaError_t refine_input(const __half* up7, long long up_bs, Img4 aq, Img4 bq, i
 
 cudaError_t render(const RenderArgs& r0, int n, cudaStream_t st) {
     if ((long long)r0.hp * r0.wp >= (1ll << 31) || r0.w > r0.wp || r0.h > r0.hp) return cudaErrorInvalidValue;
+    if (((r0.flags & 2u) || r0.age) && !r0.own) return cudaErrorInvalidValue;
+    if (r0.age && !r0.near) return cudaErrorInvalidValue;
     RenderArgs r = r0;
     r.qsy = (float)r.hq / (float)r.hp;  // the same IEEE quotients render.wgsl:87-88 forms per pixel
     r.qsx = (float)r.wq / (float)r.wp;

@@ -51,11 +51,14 @@ struct StaticArgs {
 inline int changed_words(int wp) { return (wp + 31) >> 5; }
 cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, long long frame_bs, const StaticArgs& s, uint32_t* changed,
                         long long changed_bs, float* dsum, long long dsum_bs, int n, cudaStream_t st);
-// per pair after the age pass: near = an age >= min_age in the clamped 3 x 3 neighbourhood (render_static on_static);
-// n planes bs elements apart
+// per pair after the age pass, the planes the render reads (n planes bs elements apart, row pitch wp):
+//  - near (with age): an age >= min_age in the clamped 3 x 3 neighbourhood (render_static on_static);
+//  - own (the exact render): per pixel (es, kk): es the still test's 3 x 3 mean of dsum (dsum may be null when the
+//    still test is off), set to 1 where the age is below 3 in magnitude, and kk the keep_static ramp of the age (0
+//    without age).
 // (cw, ch: the region, clamped to itself; 0 = the padded plane. The fast render's on_static clamps to the frame.)
-cudaError_t static_near(const int16_t* age, long long bs, int wp, int hp, float min_age, uint8_t* near, int n,
-                        cudaStream_t st, int cw = 0, int ch = 0);
+cudaError_t static_planes(const int16_t* age, const float* dsum, long long bs, int wp, int hp, float min_age,
+                          uint8_t* near, float2* own, int n, cudaStream_t st, int cw = 0, int ch = 0);
 // per pair after pair_planes: moved = the changed plane dilated by the 41 probes of keep_static_age.wgsl:59-70 (the
 // clamped 3 x 3 neighbourhood and the far ring), same layout; n planes bs words apart
 cudaError_t moved_plane(const uint32_t* changed, long long bs, int wp, int hp, uint32_t* moved, int n, cudaStream_t st);
@@ -155,8 +158,8 @@ struct RenderArgs {
     unsigned flags;          // bit 0 decisive, bit 1 still test
     const int16_t* age;      // static age plane (padded), or null
     long long age_bs;
-    const float* dsum;       // pair_planes' dsum (when flags bit 1)
-    const uint8_t* near;     // static_near's plane (when age is set)
+    const float2* own;       // static_planes' (es, kk) plane (when flags bit 1 or age is set)
+    const uint8_t* near;     // static_planes' near plane (when age is set)
     long long plane_bs;
     float min_age;
     uint8_t* out;            // w x h x 4
@@ -180,7 +183,7 @@ struct RenderTexArgs {
     unsigned flags;          // bit 0 decisive, bit 1 still test
     const int16_t* age;      // static age plane (padded), or null
     long long age_bs;
-    const uint8_t* near;     // static_near over the frame (when age is set), age_bs apart
+    const uint8_t* near;     // static_planes' near over the frame (when age is set), age_bs apart
     float min_age;
     const float* es;         // pair_planes' still-test terms on the padded plane (when flags bit 1)
     long long es_bs;
