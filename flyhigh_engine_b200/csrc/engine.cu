@@ -799,13 +799,14 @@ struct FhSession {
     void run_frame(const FView& v, int n) {
         __half* A = const_cast<__half*>(v.A);
         __half* half = const_cast<__half*>(v.half);
-        if (!fast)  // the fast render samples the rgba8 frames themselves
-            branch([&] {
-                CK(fhk::frame_half(v.frame, v.frame_bs, w, h, half, v.half_bs, n, st));
-                mark("frame_half");
-            });
+        // the f16 frame planes (not in the fast render, which samples the rgba8 frames themselves): the render's
+        // source, and the downscale's taps
+        if (!fast) {
+            CK(fhk::frame_half(v.frame, v.frame_bs, w, h, half, v.half_bs, n, st));
+            mark("frame_half");
+        }
         CK(fhk::frame_to_input(v.frame, v.frame_bs, w, h, hp, wp, internal, ihp, iwp, {A, v.A_bs}, n, st, aa_fx, aa_fy,
-                               fast));
+                               fast, fast ? nullptr : half, v.half_bs));
         mark("frame_to_input");
         CK(fhk::input_pyramid({A, v.A_bs}, NH, NW, {const_cast<__half*>(v.aq), v.aq_bs},
                               {const_cast<__half*>(v.i8), v.i8_bs}, {const_cast<__half*>(v.i16), v.i16_bs}, n, st,

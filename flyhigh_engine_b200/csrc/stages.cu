@@ -66,15 +66,20 @@ __global__ void k_aa_axis(int in, int out, int* first, int* count, float* w) {
 // tex_in.wgsl:10-19 + interp.wgsl:29-43 (aa): the padded plane is never stored; taps read the rgba8 frame at the
 // clamped position (replicate padding). With axis tables the weights are read, not formed per tap.
 // NX: the most taps of any output along x (the tables' weights are zero past an output's own count, and a zero-weight
-// tap adds exactly zero, so every output runs NX taps per row and ny_max rows, in the reference's order, unpredicated)
-template <int NX>
+// tap adds exactly zero, so every output runs NX taps per row and ny_max rows, in the reference's order, unpredicated).
+// HALF: with the tables, the taps read the frames' f16 planes (B, G, R, 0: the byte table's values, converted once
+// per source pixel by frame_half) instead of rgba8 through the table, whose random lookups conflict on the shared
+// memory banks.
+template <int NX, bool HALF>
 __global__ void k_frame_to_input(const uint8_t* __restrict__ frames, long long frame_bs, int w, int h, int hp, int wp,
                                  int internal, int oh, int ow, __half* out, long long out_bs, AaAxis ax, AaAxis ay,
-                                 int tex, int ny_max) {
+                                 int tex, int ny_max, const __half* __restrict__ half, long long half_bs) {
     __shared__ float lut[256];
-    for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y)
-        lut[i] = tex ? texv(i) : u8v(i);
-    __syncthreads();
+    if (!HALF) {
+        for (int i = threadIdx.y * blockDim.x + threadIdx.x; i < 256; i += blockDim.x * blockDim.y)
+            lut[i] = tex ? texv(i) : u8v(i);
+        __syncthreads();
+    }
     pdl_wait();
     pdl_trigger();
     const int ox = blockIdx.x * blockDim.x + threadIdx.x, oy = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
@@ -88,6 +93,36 @@ __global__ void k_frame_to_input(const uint8_t* __restrict__ frames, long long f
         return;
     }
     float ab = 0.0f, ag = 0.0f, ar = 0.0f, norm = 0.0f;
+    if (HALF) {
+        const uint2* hf = reinterpret_cast<const uint2*>(half + (long long)n * half_bs);
+        const int x0 = __ldg(ax.first + ox), y0 = __ldg(ay.first + oy);
+        float wx[NX];
+        int xs[NX];
+#pragma unroll
+        for (int j = 0; j < NX; j++) {
+            wx[j] = __ldg(ax.w + ox * AA_TAPS + j);
+            xs[j] = min(x0 + j, w - 1);
+        }
+        for (int yi = 0; yi < ny_max; yi++) {
+            const float wy = __ldg(ay.w + oy * AA_TAPS + yi);
+            const uint2* row = hf + min(y0 + yi, h - 1) * w;
+            uint2 v[NX];
+#pragma unroll
+            for (int j = 0; j < NX; j++) v[j] = __ldg(row + xs[j]);
+#pragma unroll
+            for (int j = 0; j < NX; j++) {
+                const float wgt = wx[j] * wy;
+                const float2 bg = __half22float2(*reinterpret_cast<const __half2*>(&v[j].x));
+                const float r_ = __low2float(*reinterpret_cast<const __half2*>(&v[j].y));
+                ab = ab + bg.x * wgt;
+                ag = ag + bg.y * wgt;
+                ar = ar + r_ * wgt;
+                norm = norm + wgt;
+            }
+        }
+        st4(o, ab / norm, ag / norm, ar / norm);
+        return;
+    }
     if (ax.w) {
         const int x0 = __ldg(ax.first + ox), y0 = __ldg(ay.first + oy);
         float wx[NX];
@@ -1785,25 +1820,30 @@ cudaError_t aa_axis(int in, int out, int* first, int* count, float* w, cudaStrea
 }
 
 cudaError_t frame_to_input(const uint8_t* frames, long long frame_bs, int w, int h, int hp, int wp, bool internal, int ih,
-                           int iw, Img4 out, int n, cudaStream_t st, AaAxis ax, AaAxis ay, bool tex) {
+                           int iw, Img4 out, int n, cudaStream_t st, AaAxis ax, AaAxis ay, bool tex, const __half* half,
+                           long long half_bs) {
     const int oh = internal ? ih : hp, ow = internal ? iw : wp;
     if (!ax.w || !ay.w || !internal) ax = ay = AaAxis{};
+    if (tex && half) return cudaErrorInvalidValue;  // the fast path's texels are not the f16 planes' values
+    const bool hv = half && ax.w;
+    if (hv && (uintptr_t)half % 8) return cudaErrorMisalignedAddress;
     // the tables' tap counts (the kernel runs the widest on every output; 8 when there are no tables)
     const int nx = ax.w ? aa_axis_max(wp, ow) : AA_TAPS, ny = ay.w ? aa_axis_max(hp, oh) : AA_TAPS;
     auto go = [&](auto kern) {
         return launch(kern, grid2(ow, oh, n), dim3(16, 16), 0, st, frames, frame_bs, w, h, hp, wp, internal ? 1 : 0, oh, ow,
-                      out.p, out.bs, ax, ay, tex ? 1 : 0, ny);
+                      out.p, out.bs, ax, ay, tex ? 1 : 0, ny, half, half_bs);
     };
+    auto pick = [&](auto kf, auto kh) { return hv ? go(kh) : go(kf); };
     cudaError_t e_;
     switch (nx) {
-        case 1: e_ = go(k_frame_to_input<1>); break;
-        case 2: e_ = go(k_frame_to_input<2>); break;
-        case 3: e_ = go(k_frame_to_input<3>); break;
-        case 4: e_ = go(k_frame_to_input<4>); break;
-        case 5: e_ = go(k_frame_to_input<5>); break;
-        case 6: e_ = go(k_frame_to_input<6>); break;
-        case 7: e_ = go(k_frame_to_input<7>); break;
-        default: e_ = go(k_frame_to_input<8>); break;
+        case 1: e_ = pick(k_frame_to_input<1, false>, k_frame_to_input<1, true>); break;
+        case 2: e_ = pick(k_frame_to_input<2, false>, k_frame_to_input<2, true>); break;
+        case 3: e_ = pick(k_frame_to_input<3, false>, k_frame_to_input<3, true>); break;
+        case 4: e_ = pick(k_frame_to_input<4, false>, k_frame_to_input<4, true>); break;
+        case 5: e_ = pick(k_frame_to_input<5, false>, k_frame_to_input<5, true>); break;
+        case 6: e_ = pick(k_frame_to_input<6, false>, k_frame_to_input<6, true>); break;
+        case 7: e_ = pick(k_frame_to_input<7, false>, k_frame_to_input<7, true>); break;
+        default: e_ = pick(k_frame_to_input<8, false>, k_frame_to_input<8, true>); break;
     }
     if (e_ != cudaSuccess) return e_;
     return cudaGetLastError();

@@ -29,10 +29,12 @@ cudaError_t aa_axis(int in, int out, int* first, int* count, float* w, cudaStrea
 // rgba8 frame -> network input A: internal mode = antialias triangle downscale of the replicate-padded frame
 // (tex_in.wgsl + interp.wgsl aa); otherwise the padded frame itself as f16. frames: [n] x (w x h x 4 bytes),
 // frame_bs bytes apart. ax / ay: the downscale's axis tables (hp -> ih, wp -> iw), or null pointers (weights per tap).
-// tex: the fast render path's tex_down.wgsl, whose source texels are k / 255 in f32 (not f16(k / 255))
+// tex: the fast render path's tex_down.wgsl, whose source texels are k / 255 in f32 (not f16(k / 255)).
+// half (not with tex): the frames' f16 planes (frame_half, half_bs halves apart), which the antialias taps read
+// instead of converting every rgba8 tap through a byte table
 cudaError_t frame_to_input(const uint8_t* frames, long long frame_bs, int w, int h, int hp, int wp, bool internal,
                            int ih, int iw, Img4 out, int n, cudaStream_t st, AaAxis ax = {}, AaAxis ay = {},
-                           bool tex = false);
+                           bool tex = false, const __half* half = nullptr, long long half_bs = 0);
 // A -> aq (antialias x0.25), i8 = avgpool2(aq), i16 = avgpool2(i8) (interp.wgsl aa + avgpool.wgsl); ax / ay: the
 // x0.25 axis tables (iw -> qw, ih -> qh), or null pointers
 cudaError_t input_pyramid(Img4 A, int ih, int iw, Img4 aq, Img4 i8, Img4 i16, int n, cudaStream_t st, AaAxis ax = {},
