@@ -62,6 +62,9 @@ __host__ __device__ inline int tile_bytes(int wm, int s, int cp) { return halo_h
 __device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
+__device__ __forceinline__ void cp_async8_zfill(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
 // ---- bulk copies (TMA, no multicast) completing on an mbarrier ----
@@ -186,7 +189,7 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
 
     // ---- halo tile: IH x IW pixels x cp channels, zero outside the image and beyond every source. The 128 threads
     //      form groups of LP (a power of two >= the chunk count) lanes per pixel: a thread owns one 8-channel chunk
-    //      (its source, offset and view scale resolved once) and walks every (128 / LP)-th pixel, 4 loads in flight ----
+    //      (its source, offset and view scale resolved once) and walks every (128 / LP)-th pixel ----
     {
         int lp = 1;
         while (lp < nchunk) lp <<= 1;  // nchunk <= 128 (checked on the host)
@@ -216,49 +219,41 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
         }
         const bool plain = valid >= 8 && scale == 1.0f && !narrow;
         const int npix = IH * IW;
+        // every pixel of every chunk an asynchronous copy, all of them in flight at once: 16 bytes (8 for a 4-channel
+        // pixel of a 3-channel image, the other 8 zero-filled), zero-filled outside the image. A chunk past every
+        // source is zeroed by plain stores.
+        const uint32_t t0 = (uint32_t)__cvta_generic_to_shared(tile);
         if (ch < nchunk) {
-            if (plain) {
-                // every pixel a 16-byte copy (zero-filled outside the image), all of them in flight at once
-                for (int pix = tid / lp; pix < npix; pix += pstep) {
-                    const int hy = pix / IW, hx = pix - hy * IW;
-                    const int iy = iy0 + hy, ix = ix0 + hx;
-                    const bool ok = iy >= 0 && iy < p.h && ix >= 0 && ix < p.w;
-                    const __half* g = ok ? base + ((long long)iy * p.w + ix) * cs : base;
-                    cp_async16_zfill((uint32_t)__cvta_generic_to_shared(tile) + (uint32_t)(pix * P + c8) * 2, g, ok ? 16u : 0u);
+            for (int pix = tid / lp; pix < npix; pix += pstep) {
+                const int hy = pix / IW, hx = pix - hy * IW;
+                const int iy = iy0 + hy, ix = ix0 + hx;
+                if (si < 0) {
+                    *reinterpret_cast<uint4*>(tile + pix * P + c8) = make_uint4(0, 0, 0, 0);
+                    continue;
                 }
-            } else
-            for (int pix0 = tid / lp; pix0 < npix; pix0 += 4 * pstep) {
-                uint4 v[4];
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const int pix = pix0 + u * pstep;
-                    const int hy = pix / IW, hx = pix - hy * IW;
-                    const int iy = iy0 + hy, ix = ix0 + hx;
-                    v[u] = make_uint4(0, 0, 0, 0);
-                    if (pix < npix && si >= 0 && iy >= 0 && iy < p.h && ix >= 0 && ix < p.w) {
-                        const __half* g = base + ((long long)iy * p.w + ix) * cs;
-                        if (!narrow) {
-                            v[u] = __ldg(reinterpret_cast<const uint4*>(g));
-                        } else {  // a 4-channel pixel (3-channel image): 8 bytes
-                            const uint2 w2 = __ldg(reinterpret_cast<const uint2*>(g));
-                            v[u] = make_uint4(w2.x, w2.y, 0, 0);
-                        }
-                    }
+                const bool ok = iy >= 0 && iy < p.h && ix >= 0 && ix < p.w;
+                const __half* g = ok ? base + ((long long)iy * p.w + ix) * cs : base;
+                const uint32_t d = t0 + (uint32_t)(pix * P + c8) * 2;
+                if (!narrow) {
+                    cp_async16_zfill(d, g, ok ? 16u : 0u);
+                } else {
+                    cp_async8_zfill(d, g, ok ? 8u : 0u);
+                    cp_async8_zfill(d + 8, base, 0u);
                 }
+            }
+        }
+        cp_async_wait_all();
+        // partial chunks (channels past the source's count) and scaled sources: each thread fixes the pixels it copied
+        if (ch < nchunk && si >= 0 && !plain) {
+            for (int pix = tid / lp; pix < npix; pix += pstep) {
+                uint4 v = *reinterpret_cast<const uint4*>(tile + pix * P + c8);
+                __half* hv = reinterpret_cast<__half*>(&v);
 #pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const int pix = pix0 + u * pstep;
-                    if (pix >= npix) break;
-                    if (!plain) {
-                        __half* hv = reinterpret_cast<__half*>(&v[u]);
-#pragma unroll
-                        for (int k = 0; k < 8; k++) {
-                            if (k >= valid) hv[k] = __float2half_rn(0.0f);
-                            else if (scale != 1.0f) hv[k] = __float2half_rn(__half2float(hv[k]) * scale);
-                        }
-                    }
-                    *reinterpret_cast<uint4*>(tile + pix * P + c8) = v[u];
+                for (int k = 0; k < 8; k++) {
+                    if (k >= valid) hv[k] = __float2half_rn(0.0f);
+                    else if (scale != 1.0f) hv[k] = __float2half_rn(__half2float(hv[k]) * scale);
                 }
+                *reinterpret_cast<uint4*>(tile + pix * P + c8) = v;
             }
         }
     }

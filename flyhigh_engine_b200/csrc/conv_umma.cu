@@ -87,6 +87,9 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
 __device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
+__device__ __forceinline__ void cp_async8_zfill(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
 // ---- tcgen05 ----
@@ -297,50 +300,42 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
         }
         const bool plain = valid >= 8 && scale == 1.0f && !narrow;
         constexpr int npix = UIH * UIW;
+        // every pixel of every chunk an asynchronous copy, all of them in flight at once: 16 bytes (8 for a 4-channel
+        // pixel of a 3-channel image, the other 8 zero-filled), zero-filled outside the image. A chunk past every
+        // source is zeroed by plain stores.
         if (ch < nchunk) {
             uint8_t* plane = sm + ch * UPLANE;
-            if (plain) {
-                // every pixel a 16-byte copy (zero-filled outside the image), all of them in flight at once
-                for (int pix = tid / lp; pix < npix; pix += pstep) {
-                    const int hy = pix / UIW, hx = pix - hy * UIW;
-                    const int iy = oy0 - 1 + hy, ix = ox0 - 1 + hx;
-                    const bool ok = iy >= 0 && iy < p.h && ix >= 0 && ix < p.w;
-                    const __half* g = ok ? base + ((long long)iy * p.w + ix) * cs : base;
-                    cp_async16_zfill(s0 + (uint32_t)(ch * UPLANE + pix * 16), g, ok ? 16u : 0u);
+            for (int pix = tid / lp; pix < npix; pix += pstep) {
+                const int hy = pix / UIW, hx = pix - hy * UIW;
+                const int iy = oy0 - 1 + hy, ix = ox0 - 1 + hx;
+                const uint32_t d = s0 + (uint32_t)(ch * UPLANE + pix * 16);
+                if (si < 0) {
+                    *reinterpret_cast<uint4*>(plane + pix * 16) = make_uint4(0, 0, 0, 0);
+                    continue;
                 }
-            } else
-            for (int pix0 = tid / lp; pix0 < npix; pix0 += 4 * pstep) {
-                uint4 v[4];
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const int pix = pix0 + u * pstep;
-                    const int hy = pix / UIW, hx = pix - hy * UIW;
-                    const int iy = oy0 - 1 + hy, ix = ox0 - 1 + hx;
-                    v[u] = make_uint4(0, 0, 0, 0);
-                    if (pix < npix && si >= 0 && iy >= 0 && iy < p.h && ix >= 0 && ix < p.w) {
-                        const __half* g = base + ((long long)iy * p.w + ix) * cs;
-                        if (!narrow) {
-                            v[u] = __ldg(reinterpret_cast<const uint4*>(g));
-                        } else {  // a 4-channel pixel (3-channel image): 8 bytes
-                            const uint2 w2 = __ldg(reinterpret_cast<const uint2*>(g));
-                            v[u] = make_uint4(w2.x, w2.y, 0, 0);
-                        }
-                    }
+                const bool ok = iy >= 0 && iy < p.h && ix >= 0 && ix < p.w;
+                const __half* g = ok ? base + ((long long)iy * p.w + ix) * cs : base;
+                if (!narrow) {
+                    cp_async16_zfill(d, g, ok ? 16u : 0u);
+                } else {
+                    cp_async8_zfill(d, g, ok ? 8u : 0u);
+                    cp_async8_zfill(d + 8, base, 0u);
                 }
+            }
+        }
+        cp_async_wait_all();
+        // partial chunks (channels past the source's count) and scaled sources: each thread fixes the pixels it copied
+        if (ch < nchunk && si >= 0 && !plain) {
+            uint8_t* plane = sm + ch * UPLANE;
+            for (int pix = tid / lp; pix < npix; pix += pstep) {
+                uint4 v = *reinterpret_cast<const uint4*>(plane + pix * 16);
+                __half* hv = reinterpret_cast<__half*>(&v);
 #pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const int pix = pix0 + u * pstep;
-                    if (pix >= npix) break;
-                    if (!plain) {
-                        __half* hv = reinterpret_cast<__half*>(&v[u]);
-#pragma unroll
-                        for (int k = 0; k < 8; k++) {
-                            if (k >= valid) hv[k] = __float2half_rn(0.0f);
-                            else if (scale != 1.0f) hv[k] = __float2half_rn(__half2float(hv[k]) * scale);
-                        }
-                    }
-                    *reinterpret_cast<uint4*>(plane + pix * 16) = v[u];
+                for (int k = 0; k < 8; k++) {
+                    if (k >= valid) hv[k] = __float2half_rn(0.0f);
+                    else if (scale != 1.0f) hv[k] = __float2half_rn(__half2float(hv[k]) * scale);
                 }
+                *reinterpret_cast<uint4*>(plane + pix * 16) = v;
             }
         }
     }
@@ -457,11 +452,13 @@ long long umma_wait_timeouts(int reset) {
 }
 }  // namespace fhk
 
+constexpr int UMMA_SMEM_MAX = 227 * 1024;
 // 1 when the tcgen05 kernel takes this layer: stride 1, N <= 256, and its halo tile plus the whole weight slice fit
-// in shared memory
+// in shared memory. (A layer whose weights fit only split over channel groups, such as coarse.c1's 279 -> 96, runs
+// longer here than on conv3x3_mma: every CTA then issues 126 small-N MMAs, and the MMA issue rate bounds it.)
 extern "C" int fhk_conv_umma_fits(int cp, int cout, int stride) {
     if (stride != 1 || cp <= 0 || cp % 16 || cout < 1 || npad16(cout) > 256) return 0;
-    return umma_smem(cp, npad16(cout)) <= 227 * 1024 ? 1 : 0;
+    return umma_smem(cp, npad16(cout)) <= UMMA_SMEM_MAX ? 1 : 0;
 }
 
 extern "C" size_t fhk_conv_packed_elems_umma(int cout, int cp) { return (size_t)9 * (cp / 16) * npad16(cout) * 16; }
@@ -509,9 +506,9 @@ extern "C" int fhk_conv3x3_umma(const FhConvParams* pin, void* stream) {
     // output channels split over CTAs while the grid is small (each output's sum is unchanged): the widest group (a
     // multiple of 16 dividing the padded channels) that gives 148 CTAs, else the narrowest
     const long long tiles = (long long)((p.wo + UT_W - 1) / UT_W) * ((p.ho + UT_H - 1) / UT_H) * p.n;
-    int ngw = np;
+    int ngw = 16;
     for (int g = np; g >= 16; g -= 16) {
-        if (np % g) continue;
+        if (np % g || umma_smem(p.cp, g) > UMMA_SMEM_MAX) continue;
         ngw = g;
         if (tiles * (np / g) >= 148) break;
     }
@@ -521,9 +518,9 @@ extern "C" int fhk_conv3x3_umma(const FhConvParams* pin, void* stream) {
     const size_t smem = (size_t)umma_smem(p.cp, ngw);
     static size_t configured = 48 * 1024;
     if (smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(conv3x3_umma, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(conv3x3_umma, cudaFuncAttributeMaxDynamicSharedMemorySize, UMMA_SMEM_MAX);
         if (e != cudaSuccess) return (int)e;
-        configured = 227 * 1024;
+        configured = UMMA_SMEM_MAX;
     }
     p.wsmem = 1;
     const dim3 grid((p.wo + UT_W - 1) / UT_W, (p.ho + UT_H - 1) / UT_H, p.n * (np / ngw));

@@ -94,33 +94,36 @@ __global__ void k_frame_to_input(const uint8_t* __restrict__ frames, long long f
     }
     float ab = 0.0f, ag = 0.0f, ar = 0.0f, norm = 0.0f;
     if (HALF) {
+        // the sums on packed f32x2 lanes, each lane rounding as the scalar code: (ab, ag) += (b, g) * wgt and
+        // (ar, norm) += (r, 1) * wgt, wgt = wx * wy formed on both lanes at once
         const uint2* hf = reinterpret_cast<const uint2*>(half + (long long)n * half_bs);
         const int x0 = __ldg(ax.first + ox), y0 = __ldg(ay.first + oy);
-        float wx[NX];
+        float2 wx[NX];
         int xs[NX];
 #pragma unroll
         for (int j = 0; j < NX; j++) {
-            wx[j] = __ldg(ax.w + ox * AA_TAPS + j);
+            const float v_ = __ldg(ax.w + ox * AA_TAPS + j);
+            wx[j] = make_float2(v_, v_);
             xs[j] = min(x0 + j, w - 1);
         }
+        float2 bg_acc = make_float2(0.0f, 0.0f), rn_acc = make_float2(0.0f, 0.0f);
         for (int yi = 0; yi < ny_max; yi++) {
-            const float wy = __ldg(ay.w + oy * AA_TAPS + yi);
+            const float wy_ = __ldg(ay.w + oy * AA_TAPS + yi);
+            const float2 wy = make_float2(wy_, wy_);
             const uint2* row = hf + min(y0 + yi, h - 1) * w;
             uint2 v[NX];
 #pragma unroll
             for (int j = 0; j < NX; j++) v[j] = __ldg(row + xs[j]);
 #pragma unroll
             for (int j = 0; j < NX; j++) {
-                const float wgt = wx[j] * wy;
+                const float2 wgt = __fmul2_rn(wx[j], wy);
                 const float2 bg = __half22float2(*reinterpret_cast<const __half2*>(&v[j].x));
-                const float r_ = __low2float(*reinterpret_cast<const __half2*>(&v[j].y));
-                ab = ab + bg.x * wgt;
-                ag = ag + bg.y * wgt;
-                ar = ar + r_ * wgt;
-                norm = norm + wgt;
+                const float2 r1 = make_float2(__low2float(*reinterpret_cast<const __half2*>(&v[j].y)), 1.0f);
+                bg_acc = __fadd2_rn(bg_acc, __fmul2_rn(bg, wgt));
+                rn_acc = __fadd2_rn(rn_acc, __fmul2_rn(r1, wgt));
             }
         }
-        st4(o, ab / norm, ag / norm, ar / norm);
+        st4(o, bg_acc.x / rn_acc.y, bg_acc.y / rn_acc.y, rn_acc.x / rn_acc.y);
         return;
     }
     if (ax.w) {
