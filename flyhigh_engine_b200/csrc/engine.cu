@@ -390,6 +390,12 @@ struct FhSession {
     __half *e1 = nullptr, *e3 = nullptr;
     uint32_t* changed = nullptr;
     uint32_t* moved = nullptr;
+    // batched sessions: the spread tests of the last batch's newest frame (a bit plane), which a batch whose oldest
+    // frame that is (the carried frame) reads instead of forming them again; sp_in / sp_out: what the batch being
+    // captured reads and writes (null outside a batch capture)
+    uint32_t* spread_bits = nullptr;
+    const uint32_t* sp_in = nullptr;
+    uint32_t* sp_out = nullptr;
     uint32_t* spread = nullptr;  // the static age pass's byte thresholds
     uint8_t* mask = nullptr;
     uchar4* state = nullptr;
@@ -700,6 +706,7 @@ struct FhSession {
         if (protects) {
             changed = alloc_n<uint32_t>((size_t)nb * hp * fhk::changed_words(wp));
             moved = alloc_n<uint32_t>((size_t)nb * hp * fhk::changed_words(wp));
+            if (nbat > 1) spread_bits = alloc_n<uint32_t>((size_t)hp * fhk::changed_words(wp));
             spread = alloc_n<uint32_t>(256);
             CK(fhk::spread_table(spread, st, fast));
             mask = alloc_n<uint8_t>((size_t)hp * wp);
@@ -837,7 +844,8 @@ struct FhSession {
                     mark("moved_plane");
                     const long long l = n - 1;
                     CK(fhk::static_age(A.frame + l * A.frame_bs, B.frame + l * B.frame_bs, -A.frame_bs, changed + l * CW,
-                                       moved + l * CW, -CW, mask, sargs, state, age + l * P, -P, n, spread, st));
+                                       moved + l * CW, -CW, mask, sargs, state, age + l * P, -P, n, spread, st, sp_in,
+                                       sp_out));
                     mark("static_age");
                 }
                 // the fast render's probes clamp to the frame, the exact render's to the padded plane; the exact
@@ -1171,14 +1179,23 @@ struct FhSession {
         cudaGraphExec_t& g = m < nbat ? short_graphs[m] : carry ? batch_graph_carry : batch_graph;
         if (!g) {
             const FView fa = arena_view(1), fbv = arena_view(0);
-            g = capture(
-                [&] {
-                    run_frame(arena_view(0), carry ? m : m + 1);
-                    run_pair(fa, fbv, m, true);
-                    run_mid(PairSrc{fa, fbv}, arena_out, (long long)fb, m);
-                    carry_newest();
-                },
-                &batch_kernels);
+            // the oldest frame's spread tests from the previous batch when its frame stage is carried too
+            sp_in = carry ? spread_bits : nullptr;
+            sp_out = spread_bits;
+            try {
+                g = capture(
+                    [&] {
+                        run_frame(arena_view(0), carry ? m : m + 1);
+                        run_pair(fa, fbv, m, true);
+                        run_mid(PairSrc{fa, fbv}, arena_out, (long long)fb, m);
+                        carry_newest();
+                    },
+                    &batch_kernels);
+            } catch (...) {
+                sp_in = sp_out = nullptr;
+                throw;
+            }
+            sp_in = sp_out = nullptr;
         }
         CK(cudaGraphLaunch(g, st));
         carried = q[m - 1].b;

@@ -571,13 +571,16 @@ FH_DEV bool frame_spread(const Ext3& e, const uint32_t* tab) {
 // |b(q) - b(o)|; the byte -> value table is monotone and f32 subtraction is monotone in each operand, so that max is
 // max(v(max_q) - v(o), v(o) - v(min_q)) per channel, exactly; its test against 0.03 is a byte threshold per o
 // (k_spread_table). When the pairs are chained (pair i's second frame is pair i + 1's first, fa + frame_bs == fb) a
-// frame's spread test is formed once and serves both of its pairs.
+// frame's spread test is formed once and serves both of its pairs. spread_in: the first frame's spread tests as a bit
+// plane (the changed plane's layout), read instead of formed; spread_out: the last frame's, written (either may be
+// null; both may be the same plane, each word read and written by the one warp that owns it).
 __global__ void __launch_bounds__(256) k_static_age(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb,
                                                     long long frame_bs, const uint32_t* __restrict__ changed,
                                                     const uint32_t* __restrict__ moved_plane, long long changed_bs,
                                                     const uint8_t* __restrict__ mask, StaticArgs s,
                                                     uchar4* state, int16_t* age, long long age_bs, int np,
-                                                    const uint32_t* __restrict__ spread) {
+                                                    const uint32_t* __restrict__ spread, const uint32_t* spread_in,
+                                                    uint32_t* spread_out) {
     __shared__ uint32_t spread_tab[256];
     const int tid = threadIdx.y * blockDim.x + threadIdx.x;
     for (int i = tid; i < 256; i += blockDim.x * blockDim.y) spread_tab[i] = __ldg(spread + i);
@@ -596,8 +599,10 @@ __global__ void __launch_bounds__(256) k_static_age(const uint8_t* __restrict__ 
     const int xc = min(x, s.w - 1);
     const int xe = lane == 0 ? min(max(x0 - 1, 0), s.w - 1) : min(x0 + 32, s.w - 1);
     const bool chained = fa + frame_bs == fb;
+    const long long sw = (long long)y * ww + blockIdx.x;  // this warp's word of a bit plane
     bool spread_a =
-        frame_spread(frame_ext3(reinterpret_cast<const uint32_t*>(fa), s.w, r0, r1, r2, xc, xe, lane), spread_tab);
+        spread_in ? ((spread_in[sw] >> lane) & 1u) != 0
+                  : frame_spread(frame_ext3(reinterpret_cast<const uint32_t*>(fa), s.w, r0, r1, r2, xc, xe, lane), spread_tab);
     for (int pi = 0; pi < np; pi++) {
         const long long wo = pi * changed_bs + (long long)y * ww + blockIdx.x;
         const uint32_t mv = __ldg(moved_plane + wo), own_word = __ldg(changed + wo);
@@ -622,6 +627,10 @@ __global__ void __launch_bounds__(256) k_static_age(const uint8_t* __restrict__ 
         age[pi * age_bs + o] = a;
     }
     if (active) state[o] = st;
+    if (spread_out) {
+        const uint32_t bits = __ballot_sync(0xffffffffu, spread_a);  // the last frame's (spread_a = its spread_b)
+        if (lane == 0) spread_out[sw] = bits;
+    }
 }
 
 // ------------------------------------------------------------------------------------------------ cost volume ----
@@ -1891,9 +1900,10 @@ cudaError_t moved_plane(const uint32_t* changed, long long bs, int wp, int hp, u
 
 cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, long long frame_bs, const uint32_t* changed,
                        const uint32_t* moved, long long changed_bs, const uint8_t* mask, const StaticArgs& s,
-                       uchar4* state, int16_t* age, long long age_bs, int np, const uint32_t* spread, cudaStream_t st) {
+                       uchar4* state, int16_t* age, long long age_bs, int np, const uint32_t* spread, cudaStream_t st,
+                       const uint32_t* spread_in, uint32_t* spread_out) {
     if (np < 1 || !spread) return cudaErrorInvalidValue;
-    { const cudaError_t e_ = launch(k_static_age, grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st, fa, fb, frame_bs, changed, moved, changed_bs, mask, s, state, age, age_bs, np, spread); if (e_ != cudaSuccess) return e_; }
+    { const cudaError_t e_ = launch(k_static_age, grid2(s.wp, s.hp, 1, 32, 8), dim3(32, 8), 0, st, fa, fb, frame_bs, changed, moved, changed_bs, mask, s, state, age, age_bs, np, spread, spread_in, spread_out); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 

@@ -66,10 +66,13 @@ cudaError_t static_planes(const int16_t* age, const float* dsum, long long bs, i
 cudaError_t moved_plane(const uint32_t* changed, long long bs, int wp, int hp, uint32_t* moved, int n, cudaStream_t st);
 // the age pass over np consecutive pairs in time order (pair i: frames fa / fb + i * frame_bs, changed / moved + i *
 // changed_bs, age + i * age_bs; strides may be negative), advancing the one state plane pair by pair
-// spread: the 256-entry byte-threshold table of the spread test (spread_table(), once per session)
+// spread: the 256-entry byte-threshold table of the spread test (spread_table(), once per session). spread_in: the first
+// frame's spread tests as a bit plane (the changed plane's layout; null: formed from the frame); spread_out: where the
+// last frame's are written (or null); the same plane may be both.
 cudaError_t static_age(const uint8_t* fa, const uint8_t* fb, long long frame_bs, const uint32_t* changed,
                        const uint32_t* moved, long long changed_bs, const uint8_t* mask, const StaticArgs& s,
-                       uchar4* state, int16_t* age, long long age_bs, int np, const uint32_t* spread, cudaStream_t st);
+                       uchar4* state, int16_t* age, long long age_bs, int np, const uint32_t* spread, cudaStream_t st,
+                       const uint32_t* spread_in = nullptr, uint32_t* spread_out = nullptr);
 cudaError_t spread_table(uint32_t* out, cudaStream_t st, bool tex = false);
 
 // luma.wgsl + sad.wgsl on two 3-channel images (a view at channel offset 0): (2r+1)^2 cost channels into out (cs)
