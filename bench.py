@@ -205,6 +205,9 @@ def main():
             s.write_device(b, base + i * fbytes, fbytes)
             s.pair(a, b)
             s.mid(0.5, out)
+        # a batched session renders on a stream of its own: the step's end event on the session stream comes after
+        # every render issued in the step
+        s.join()
 
     def barrier():
         torch.cuda.synchronize()

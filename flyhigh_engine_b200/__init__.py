@@ -84,6 +84,7 @@ EXPORTS = [
     ("fh_session_import_d3d11", c_int, [c_void_p, c_void_p, ctypes.c_ssize_t, c_uint32, c_uint32]),
     ("fh_session_report_json", c_int, [c_void_p, c_char_p, c_size_t]),
     ("fh_session_cuda_stream", c_int, [c_void_p, POINTER(c_void_p)]),
+    ("fh_session_join", c_int, [c_void_p]),
     ("fh_session_slot_device_ptr", c_int, [c_void_p, c_uint32, c_int, POINTER(c_void_p)]),
     ("fh_session_write_rgba_device", c_int, [c_void_p, c_uint32, c_void_p, c_size_t]),
     ("fh_session_debug_tensor", c_long, [c_void_p, c_char_p, POINTER(c_float), c_size_t, POINTER(c_int)]),
@@ -370,6 +371,10 @@ class Session:
         p = c_void_p()
         _check(lib().fh_session_cuda_stream(self._h, byref(p)))
         return p.value or 0
+
+    def join(self) -> None:
+        """Orders every batch render issued so far before the work later issued on cuda_stream()."""
+        _check(lib().fh_session_join(self._h))
 
     def slot_ptr(self, slot: int, output: bool = False) -> int:
         p = c_void_p()

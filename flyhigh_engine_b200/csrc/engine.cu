@@ -419,13 +419,56 @@ struct FhSession {
     int nbat = 1;
     int single = 0;  // > 0: pair / mid run at once (timed calls, warm-up)
     std::vector<Pending> pend;
-    FrameSet arena;
-    uint8_t* arena_out = nullptr;  // nbat rendered frames, scattered to the output slots
-    cudaGraphExec_t batch_graph = nullptr;
-    // the batch graph for a batch whose oldest frame is the previous batch's newest: that frame's stage outputs are
-    // already in entry nbat (carried there at the end of every batch), so its frame stage covers entries 0..nbat-1
-    cudaGraphExec_t batch_graph_carry = nullptr;
-    std::map<int, cudaGraphExec_t> short_graphs;  // batches of 2 .. nbat - 1 intervals, by size
+    // A batch runs as two graphs: the network (frame stage, pairs, the mids' maps) on st, then the render on the
+    // render stream rs, so the next batch's network overlaps this batch's render. What the render reads and writes
+    // (the arena's frames and frame planes, the maps, the static planes, the phases, the rendered frames) is held
+    // twice, and consecutive batches alternate between the two render sets; the members below point into the set
+    // the last batch used. Work on st outside a batch first waits for the renders still running (join_render).
+    struct RenderSet {
+        FrameSet arena;
+        uint8_t* out = nullptr;  // nbat rendered frames, scattered to the output slots
+        __half *up7 = nullptr, *rt = nullptr;
+        int16_t* age = nullptr;
+        uint8_t* nearp = nullptr;
+        float2* ownp = nullptr;
+        float *dsum = nullptr, *tdev = nullptr;
+        // graphs over this set: the network of a full batch (by whether its oldest frame's stage is carried) and of
+        // shorter ones (by size), the render by size
+        cudaGraphExec_t net_full[2] = {};
+        std::map<int, cudaGraphExec_t> net_short, render;
+        cudaEvent_t net_done = nullptr, render_done = nullptr;
+        bool render_pending = false;
+    };
+    RenderSet rsets[2];
+    bool overlap_on = true;
+    int rpar = 0;         // the set the members point to
+    // the set holding the current pair's per-interval buffers: 0 for a pair run on its own (its graphs are captured
+    // on set 0), the batch's set for the newest interval of a batch
+    int pair_set = 0;
+    int last_batch = 1;   // the set of the last batch (the first batch takes set 0)
+    cudaStream_t rs = nullptr;
+    FrameSet& arena() { return rsets[rpar].arena; }
+    const FrameSet& arena() const { return rsets[rpar].arena; }
+    uint8_t* arena_out() const { return rsets[rpar].out; }
+    void use_set(int p) {
+        rpar = p;
+        const RenderSet& r = rsets[p];
+        up7 = r.up7;
+        rt = r.rt;
+        age = r.age;
+        nearp = r.nearp;
+        ownp = r.ownp;
+        dsum = r.dsum;
+        tdev = r.tdev;
+    }
+    // st waits for every batch render still running
+    void join_render() {
+        for (RenderSet& r : rsets)
+            if (r.render_pending) {
+                CK(cudaStreamWaitEvent(st, r.render_done, 0));
+                r.render_pending = false;
+            }
+    }
     const FrameSet* carried = nullptr;  // the frame whose outputs entry nbat holds, at generation carried_gen
     uint64_t carried_gen = 0;
     int batch_kernels = 0;
@@ -503,6 +546,7 @@ struct FhSession {
 
     ~FhSession() {
         if (st) cudaStreamSynchronize(st);
+        if (rs) cudaStreamSynchronize(rs);
         for (cudaStream_t sd : sides)
             if (sd) cudaStreamSynchronize(sd);
         if (h2d) cudaStreamSynchronize(h2d);
@@ -520,9 +564,14 @@ struct FhSession {
         for (auto& fs : sets)
             if (fs->graph) cudaGraphExecDestroy(fs->graph);
         for (auto& kv : pair_graphs) cudaGraphExecDestroy(kv.second);
-        if (batch_graph) cudaGraphExecDestroy(batch_graph);
-        if (batch_graph_carry) cudaGraphExecDestroy(batch_graph_carry);
-        for (auto& kv : short_graphs) cudaGraphExecDestroy(kv.second);
+        for (RenderSet& r : rsets) {
+            for (cudaGraphExec_t g : r.net_full)
+                if (g) cudaGraphExecDestroy(g);
+            for (auto& kv : r.net_short) cudaGraphExecDestroy(kv.second);
+            for (auto& kv : r.render) cudaGraphExecDestroy(kv.second);
+            if (r.net_done) cudaEventDestroy(r.net_done);
+            if (r.render_done) cudaEventDestroy(r.render_done);
+        }
         for (auto& kv : mid_graphs) cudaGraphExecDestroy(kv.second);
         for (void* p : allocs) cudaFree(p);
         if (eng) eng->tensor_bytes -= std::min(eng->tensor_bytes, bytes);
@@ -530,6 +579,7 @@ struct FhSession {
             if (sd) cudaStreamDestroy(sd);
         if (h2d) cudaStreamDestroy(h2d);
         if (d2h) cudaStreamDestroy(d2h);
+        if (rs) cudaStreamDestroy(rs);
         if (st) cudaStreamDestroy(st);
     }
 
@@ -765,16 +815,39 @@ struct FhSession {
             aa_qx = make_axis(NW, qw);
             aa_qy = make_axis(NH, qh);
         }
+        // render set 0 holds the buffers above; a batched session has a second set and the arenas
+        rsets[0].up7 = up7;
+        rsets[0].rt = rt;
+        rsets[0].age = age;
+        rsets[0].nearp = nearp;
+        rsets[0].ownp = ownp;
+        rsets[0].dsum = dsum;
+        rsets[0].tdev = tdev;
         if (nbat > 1) {
-            arena.frame = alloc_n<uint8_t>((size_t)nf * w * h * 4);
-            arena.half = alloc_n<__half>((size_t)nf * w * h * 4);
-            arena.A = img(NH, NW, 4, nf);
-            arena.aq = img(qh, qw, 4, nf);
-            arena.i8 = img(h8, w8, 4, nf);
-            arena.i16 = img(h16, w16, 4, nf);
-            arena.f8 = img(h8, w8, C8P, nf);
-            arena.f16 = img(h16, w16, C16P, nf);
-            arena_out = alloc_n<uint8_t>((size_t)nb * w * h * 4);
+            RenderSet& r1 = rsets[1];
+            r1.up7 = img(qh, qw, 8, nb);
+            r1.rt = img(qh, qw, 4, nb);
+            if (protects) {
+                r1.age = alloc_n<int16_t>((size_t)nb * hp * wp);
+                r1.nearp = alloc_n<uint8_t>((size_t)nb * hp * wp);
+            }
+            if (dsum) r1.dsum = alloc_n<float>((size_t)nb * hp * wp);
+            if (ownp) r1.ownp = alloc_n<float2>((size_t)nb * hp * wp);
+            r1.tdev = alloc_n<float>(nb);
+            for (RenderSet& r : rsets) {
+                FrameSet& ar = r.arena;
+                ar.frame = alloc_n<uint8_t>((size_t)nf * w * h * 4);
+                ar.half = alloc_n<__half>((size_t)nf * w * h * 4);
+                ar.A = img(NH, NW, 4, nf);
+                ar.aq = img(qh, qw, 4, nf);
+                ar.i8 = img(h8, w8, 4, nf);
+                ar.i16 = img(h16, w16, 4, nf);
+                ar.f8 = img(h8, w8, C8P, nf);
+                ar.f16 = img(h16, w16, C16P, nf);
+                r.out = alloc_n<uint8_t>((size_t)nb * w * h * 4);
+                CK(cudaEventCreateWithFlags(&r.net_done, cudaEventDisableTiming));
+                CK(cudaEventCreateWithFlags(&r.render_done, cudaEventDisableTiming));
+            }
         }
         CK(cudaStreamSynchronize(st));
     }
@@ -790,15 +863,16 @@ struct FhSession {
         v.i16_bs = E(h16, w16, 4);
         v.f8_bs = E(h8, w8, C8P);
         v.f16_bs = E(h16, w16, C16P);
-        v.frame = arena.frame + j * v.frame_bs;
-        v.half = arena.half + j * v.half_bs;
-        v.A = arena.A + j * v.A_bs;
-        v.aq = arena.aq + j * v.aq_bs;
-        v.i8 = arena.i8 + j * v.i8_bs;
-        v.i16 = arena.i16 + j * v.i16_bs;
-        v.f8 = arena.f8 + j * v.f8_bs;
-        v.f16 = arena.f16 + j * v.f16_bs;
-        v.key = reinterpret_cast<const char*>(&arena) + j;
+        const FrameSet& ar = arena();
+        v.frame = ar.frame + j * v.frame_bs;
+        v.half = ar.half + j * v.half_bs;
+        v.A = ar.A + j * v.A_bs;
+        v.aq = ar.aq + j * v.aq_bs;
+        v.i8 = ar.i8 + j * v.i8_bs;
+        v.i16 = ar.i16 + j * v.i16_bs;
+        v.f8 = ar.f8 + j * v.f8_bs;
+        v.f16 = ar.f16 + j * v.f16_bs;
+        v.key = reinterpret_cast<const char*>(&ar) + j;
         return v;
     }
 
@@ -1026,6 +1100,7 @@ struct FhSession {
     }
 
     cudaGraphExec_t pair_graph(const FrameSet& A, const FrameSet& B) {
+        use_set(0);
         auto key = std::make_pair(&A, &B);
         auto it = pair_graphs.find(key);
         if (it == pair_graphs.end())
@@ -1035,6 +1110,8 @@ struct FhSession {
 
     // one pair now, on entry 0 of the per-interval buffers
     void pair_now(FrameSet& A, FrameSet& B) {
+        use_set(0);
+        pair_set = 0;
         wait_upload(A);
         wait_upload(B);
         ensure_features(A);
@@ -1058,12 +1135,13 @@ struct FhSession {
             pend.push_back(Pending{&A, &B});
             return;
         }
-        flush();
+        sync_all();
         pair_now(A, B);
     }
 
     // the mid of the current pair into output slot `out`: parts as run_mid's (3 whole, 1 the maps, 2 the render)
     cudaGraphExec_t mid_graph(uint32_t out, int parts = 3) {
+        use_set(pair_set);
         uint8_t* o = parts == 1 ? nullptr : outs[out];
         auto key = std::make_tuple(pair.a.key, pair.b.key, (const void*)(intptr_t)parts, (const void*)nullptr,
                                    (const void*)o);
@@ -1098,8 +1176,9 @@ struct FhSession {
             if ((int)pend.size() == nbat) flush();
             return;
         }
-        flush();  // a further mid of the last queued pair: that pair has run by now
+        sync_all();  // a further mid of the last queued pair: that pair (and its batch's render) has run by now
         if (!have_pair) fail("pair two input slots first");
+        use_set(pair_set);
         CK(fhk::set_scalar(tdev, t, st));
         launch_mid(out);
         if (pair.sa) mark_read(*pair.sa, *pair.sb);
@@ -1119,6 +1198,7 @@ struct FhSession {
             run_batch(q);
             return;
         }
+        join_render();  // one at a time on st, after the batch renders
         ++single;
         try {
             for (const Pending& x : q) {
@@ -1138,32 +1218,51 @@ struct FhSession {
         --single;
     }
 
-    // entry 0's frame-stage outputs (the batch's newest frame) into entry nbat, where the next batch's oldest frame sits
-    void carry_newest() {
-        const FView src = arena_view(0), dst = arena_view(nbat);
+    // runs what is queued and orders every render before later work on st
+    void sync_all() {
+        flush();
+        join_render();
+    }
+
+    // the frame-stage outputs of render set src's entry 0 (the last batch's newest frame) into entry nbat of the current
+    // set, where this batch's oldest frame sits
+    void carry_from(int src) {
+        const int keep = rpar;
+        rpar = src;
+        const FView from = arena_view(0);
+        rpar = keep;
+        const FView to = arena_view(nbat);
         auto cp = [&](const __half* d, const __half* s_, long long elems) {
             CK(cudaMemcpyAsync(const_cast<__half*>(d), s_, (size_t)elems * sizeof(__half), cudaMemcpyDeviceToDevice, st));
         };
-        cp(dst.half, src.half, src.half_bs);
-        cp(dst.A, src.A, src.A_bs);
-        cp(dst.aq, src.aq, src.aq_bs);
-        cp(dst.i8, src.i8, src.i8_bs);
-        cp(dst.i16, src.i16, src.i16_bs);
-        cp(dst.f8, src.f8, src.f8_bs);
-        cp(dst.f16, src.f16, src.f16_bs);
+        cp(to.half, from.half, from.half_bs);
+        cp(to.A, from.A, from.A_bs);
+        cp(to.aq, from.aq, from.aq_bs);
+        cp(to.i8, from.i8, from.i8_bs);
+        cp(to.i16, from.i16, from.i16_bs);
+        cp(to.f8, from.f8, from.f8_bs);
+        cp(to.f16, from.f16, from.f16_bs);
     }
 
-    // m = 2 .. nbat chained intervals (q[i].b == q[i + 1].a) as one graph: the frames of times 0..m gathered into the
-    // arena (time t at entry m - t), the frame stage of all m + 1 (of m when entry m already holds the oldest frame's
-    // outputs), the pairs and mids of all m (interval i at entry m - 1 - i), then the rendered frames scattered to
-    // their output slots in time order.
+    // m = 2 .. nbat chained intervals (q[i].b == q[i + 1].a) on the other render set than the last batch's: the frames
+    // of times 0..m gathered into its arena (time t at entry m - t), then on st the network graph (the oldest frame's
+    // stage outputs carried from the last batch when that is its newest frame, unchanged since, else its frame stage
+    // too; the frame stage of the others; the pairs and the mids' maps of all m, interval i at entry m - 1 - i), then
+    // on rs the render graph and the rendered frames scattered to their output slots in time order.
     void run_batch(const std::vector<Pending>& q) {
         const int m = (int)q.size();
         const size_t fb = (size_t)w * h * 4;
+        const int p = 1 - last_batch;
+        RenderSet& R = rsets[p];
+        if (R.render_pending) {  // the render of the batch before the last reads this set
+            CK(cudaStreamWaitEvent(st, R.render_done, 0));
+            R.render_pending = false;
+        }
+        use_set(p);
         for (int j = 0; j <= m; j++) {
             FrameSet* f = j == 0 ? q[m - 1].b : q[m - j].a;
             wait_upload(*f);
-            CK(cudaMemcpyAsync(arena.frame + j * fb, f->frame, fb, cudaMemcpyDeviceToDevice, st));
+            CK(cudaMemcpyAsync(arena().frame + j * fb, f->frame, fb, cudaMemcpyDeviceToDevice, st));
         }
         for (int j = 0; j <= m; j++) {
             FrameSet* f = j == 0 ? q[m - 1].b : q[m - j].a;
@@ -1173,38 +1272,57 @@ struct FhSession {
         std::vector<float> tv(m);
         for (int e = 0; e < m; e++) tv[e] = q[m - 1 - e].t;
         CK(cudaMemcpyAsync(tdev, tv.data(), m * sizeof(float), cudaMemcpyHostToDevice, st));
-        // a full batch's oldest frame's stage outputs were carried into entry nbat by the previous batch when it is
-        // that batch's newest frame, unchanged since
-        const bool carry = m == nbat && carried == q[0].a && q[0].a->gen == carried_gen;
-        cudaGraphExec_t& g = m < nbat ? short_graphs[m] : carry ? batch_graph_carry : batch_graph;
-        if (!g) {
-            const FView fa = arena_view(1), fbv = arena_view(0);
+        const bool carry = m == nbat && carried == q[0].a && q[0].a->gen == carried_gen && batches_run > 0;
+        cudaGraphExec_t& net = m < nbat ? R.net_short[m] : R.net_full[carry ? 1 : 0];
+        const FView fa = arena_view(1), fbv = arena_view(0);
+        if (!net) {
             // the oldest frame's spread tests from the previous batch when its frame stage is carried too
             sp_in = carry ? spread_bits : nullptr;
             sp_out = spread_bits;
+            int nodes = 0;
             try {
-                g = capture(
+                net = capture(
                     [&] {
+                        if (carry) carry_from(1 - p);
                         run_frame(arena_view(0), carry ? m : m + 1);
                         run_pair(fa, fbv, m, true);
-                        run_mid(PairSrc{fa, fbv}, arena_out, (long long)fb, m);
-                        carry_newest();
+                        run_mid(PairSrc{fa, fbv}, nullptr, 0, m, 1);
                     },
-                    &batch_kernels);
+                    &nodes);
             } catch (...) {
                 sp_in = sp_out = nullptr;
                 throw;
             }
             sp_in = sp_out = nullptr;
+            batch_kernels = nodes;
         }
-        CK(cudaGraphLaunch(g, st));
+        cudaGraphExec_t& ren = R.render[m];
+        if (!ren) {
+            int nodes = 0;
+            ren = capture(
+                [&] {
+                    fhk::PrioScope low(prio_on, prio_lo);
+                    run_mid(PairSrc{fa, fbv}, arena_out(), (long long)fb, m, 2);
+                },
+                &nodes);
+            batch_kernels += nodes;
+        }
+        cudaStream_t rst = overlap_on ? rs : st;
+        CK(cudaGraphLaunch(net, st));
+        CK(cudaEventRecord(R.net_done, st));
+        CK(cudaStreamWaitEvent(rst, R.net_done, 0));
+        CK(cudaGraphLaunch(ren, rst));
         carried = q[m - 1].b;
         carried_gen = q[m - 1].b->gen;
         for (int i = 0; i < m; i++) {
             const int e = m - 1 - i;
-            CK(cudaMemcpyAsync(outs[q[i].out], arena_out + e * fb, fb, cudaMemcpyDeviceToDevice, st));
-            CK(cudaEventRecord(out_ready[q[i].out], st));
+            CK(cudaMemcpyAsync(outs[q[i].out], arena_out() + e * fb, fb, cudaMemcpyDeviceToDevice, rst));
+            CK(cudaEventRecord(out_ready[q[i].out], rst));
         }
+        CK(cudaEventRecord(R.render_done, rst));
+        R.render_pending = true;
+        last_batch = p;
+        pair_set = p;
         // the newest interval is entry 0 of every per-interval buffer: a further mid of it runs there
         FView a0 = arena_view(1), b0 = arena_view(0);
         for (FView* v : {&a0, &b0}) v->frame_bs = v->half_bs = v->A_bs = v->aq_bs = v->i8_bs = v->i16_bs = v->f8_bs = v->f16_bs = 0;
@@ -1276,7 +1394,8 @@ struct FhSession {
         check_in(b);
         check_out(out);
         if (!std::isfinite(t)) fail("t is not finite");
-        flush();
+        sync_all();
+        use_set(0);
         FrameSet& A = cur_set(a);
         FrameSet& B = cur_set(b);
         wait_upload(A);
@@ -1304,6 +1423,7 @@ struct FhSession {
         CK(cudaStreamSynchronize(st));
         A.feat_gen = A.gen;
         B.feat_gen = B.gen;
+        pair_set = 0;
         pair = PairSrc{view_of(A), view_of(B), &A, &B};
         have_pair = true;
         maps_done = true;
@@ -1325,7 +1445,8 @@ struct FhSession {
     // batch advanced it.
     std::string profile_batch_json() {
         if (nbat < 2) fail("not a batched session");
-        flush();
+        sync_all();
+        use_set(last_batch);
         if (batches_run == 0) fail("no batch has run");
         carried = nullptr;  // the frame stage below recomputes entry nbat from the oldest frame
         const int n = nbat;
@@ -1339,7 +1460,7 @@ struct FhSession {
             const FView fa = arena_view(1), fbv = arena_view(0);
             run_frame(arena_view(0), n + 1);
             run_pair(fa, fbv, n);
-            run_mid(PairSrc{fa, fbv}, arena_out, (long long)fb, n);
+            run_mid(PairSrc{fa, fbv}, arena_out(), (long long)fb, n);
         } catch (...) {
             prof = nullptr;
             for (auto& m : marks) cudaEventDestroy(m.second);
@@ -1380,7 +1501,7 @@ struct FhSession {
 struct SingleScope {
     FhSession* s;
     explicit SingleScope(FhSession* ss) : s(ss) {
-        s->flush();
+        s->sync_all();
         s->single++;
     }
     ~SingleScope() { s->single--; }
@@ -1494,6 +1615,9 @@ FhSession* session_new(FhEngine* e, const FhModel* m, const FhSessionOptions& o,
     CK(cudaSetDevice(e->device));
     CK(cudaDeviceGetStreamPriorityRange(&s->prio_lo, &s->prio_hi));
     CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+    // batch renders at the lowest priority, beside the next batch's network (FH_OVERLAP=0: on st after it)
+    s->overlap_on = !env_is("FH_OVERLAP", "0");
+    if (batch > 1) CK(cudaStreamCreateWithPriority(&s->rs, cudaStreamNonBlocking, s->prio_lo));
     for (cudaStream_t& sd : s->sides) CK(cudaStreamCreateWithFlags(&sd, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&s->h2d, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&s->d2h, cudaStreamNonBlocking));
@@ -1696,7 +1820,7 @@ int fh_session_write_mask(const FhSession* cs, const uint8_t* mask, size_t len) 
         FhSession* s = const_cast<FhSession*>(cs);
         if (!s || !mask) fail("null argument");
         if (!s->o.protection_mask) fail("the session was built without protection_mask");
-        s->flush();  // queued pairs see the mask they were given
+        s->sync_all();  // queued pairs see the mask they were given
         if (len != (size_t)s->w * s->h) fail("mask is %zu bytes, %dx%d = %zu expected", len, s->w, s->h, (size_t)s->w * s->h);
         // net/session_ext.rs:156-178: replicate-padded to the padded plane, nonzero protects
         std::vector<uint8_t> plane((size_t)s->wp * s->hp);
@@ -1858,10 +1982,21 @@ int fh_session_report_json(const FhSession* s, char* buf, size_t cap) {
 
 // ---- flyhigh_b200.h ----
 
-int fh_session_cuda_stream(const FhSession* s, void** stream) {
+int fh_session_cuda_stream(const FhSession* cs, void** stream) {
     return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
         if (!s || !stream) fail("null argument");
+        s->join_render();
         *stream = (void*)s->st;
+        return 0;
+    });
+}
+
+int fh_session_join(const FhSession* cs) {
+    return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
+        if (!s) fail("null argument");
+        s->join_render();
         return 0;
     });
 }
@@ -1870,7 +2005,7 @@ int fh_session_slot_device_ptr(const FhSession* cs, uint32_t slot, int output, v
     return guard(-1, [&] {
         FhSession* s = const_cast<FhSession*>(cs);
         if (!s || !ptr) fail("null argument");
-        s->flush();  // the buffer is the caller's to use: nothing queued reads or writes it
+        s->sync_all();  // the buffer is the caller's to use: nothing queued or rendering reads or writes it
         if (output) {
             s->check_out(slot);
             *ptr = s->outs[slot];
@@ -1902,7 +2037,7 @@ int fh_session_advance_static(const FhSession* cs, uint32_t a, uint32_t b) {
     return guard(-1, [&] {
         FhSession* s = const_cast<FhSession*>(cs);
         if (!s) fail("null argument");
-        s->flush();
+        s->sync_all();
         s->check_in(a);
         s->check_in(b);
         if (!s->protects) return 0;
@@ -1950,8 +2085,9 @@ long fh_session_debug_tensor(const FhSession* cs, const char* name, float* out, 
     return guard(-1L, [&]() -> long {
         FhSession* s = const_cast<FhSession*>(cs);
         if (!s || !name || !dims) fail("null argument");
-        s->flush();
+        s->sync_all();
         if (!s->have_pair) fail("no pair has run");
+        s->use_set(s->pair_set);
         std::string n(name);
         const FView& A = s->pair.a;
         const FView& B = s->pair.b;

@@ -26,8 +26,14 @@ FhSession* fh_session_create_batched(const FhEngine* engine, const FhModel* mode
 
 /* The CUDA stream (cudaStream_t) the session's compute is ordered on: pair, mid, the device-side writes below. Host
  * uploads (fh_session_write_rgba) and readbacks (fh_session_read_rgba) run on two more streams of the session, ordered
- * against this one by events, so they overlap the compute of other intervals. 0 on success, -1 on error. */
+ * against this one by events, so they overlap the compute of other intervals. A batched session renders each batch on
+ * a render stream of its own, beside the next batch's network; this call (and fh_session_join) orders every render
+ * issued so far before the work later issued on the returned stream. 0 on success, -1 on error. */
 int fh_session_cuda_stream(const FhSession* session, void** stream);
+
+/* Orders everything the session has issued so far, the batch renders included, before the work later issued on its
+ * stream (fh_session_cuda_stream). What is queued stays queued. 0 on success, -1 on error. */
+int fh_session_join(const FhSession* session);
 
 /* The device buffer (width * height * 4 bytes, RGBA8) behind an input or output slot, for hosts whose frames already
  * live in device memory (write it on the session's stream, or synchronise first). Runs what a batched session has
