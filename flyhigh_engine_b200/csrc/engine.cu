@@ -336,6 +336,14 @@ struct Pending {
 
 }  // namespace
 
+// The per-interval buffers of a session (nbat entries each), held once per render set (FhSession::RenderSet)
+#define FH_SET_BUFFERS(X)                                                                                          \
+    X(int16_t*, age) X(uint8_t*, nearp) X(float*, dsum) X(float2*, ownp) X(__half*, cv) X(__half*, ch1)            \
+    X(__half*, ch2) X(__half*, ch3r) X(__half*, hcb) X(__half*, ob) X(__half*, fv) X(__half*, wbuf) X(__half*, fcv) \
+    X(__half*, fr1) X(__half*, fr2) X(__half*, fr3) X(__half*, wt36) X(float*, coef) X(float*, maps) X(float*, tmp) \
+    X(float*, tdev) X(__half*, hm) X(__half*, fh1) X(__half*, fh2) X(__half*, dfilm) X(__half*, ftvt)              \
+    X(__half*, up7) X(__half*, rx) X(__half*, rq1) X(__half*, rq2) X(__half*, rq3) X(__half*, rt)
+
 struct FhSession {
     FhEngine* eng = nullptr;
     const FhModel* model = nullptr;
@@ -399,16 +407,15 @@ struct FhSession {
     uint32_t* spread = nullptr;  // the static age pass's byte thresholds
     uint8_t* mask = nullptr;
     uchar4* state = nullptr;
-    int16_t* age = nullptr;
-    float* dsum = nullptr;      // per pair: the still test's per-pixel |A - B| sums
-    float2* ownp = nullptr;     // per pair: the exact render's own-pixel (es, kk) plane (static_planes)
-    uint8_t* nearp = nullptr;   // per pair: near a protected pixel
-    __half *cv, *ch1, *ch2, *ch3r, *hcb, *ob, *fv, *wbuf, *fcv, *fr1, *fr2, *fr3, *wt36;
-    float *coef, *maps, *tmp, *tdev;
+    // the per-interval buffers of the render set in use: age (static age), nearp (near a protected pixel), dsum (the
+    // still test's per-pixel |A - B| sums), ownp (the exact render's own-pixel (es, kk) plane), the network's
+    // activations and maps, tdev (the entries' phases)
+#define FH_DECL(T, n) T n = nullptr;
+    FH_SET_BUFFERS(FH_DECL)
+#undef FH_DECL
     // antialias axis tables: the frame -> internal downscale (when internal), A -> aq (x0.25); null when a size needs
     // more taps than the tables hold
     fhk::AaAxis aa_fx{}, aa_fy{}, aa_qx{}, aa_qy{};
-    __half *hm, *fh1, *fh2, *dfilm, *ftvt, *up7, *rx, *rq1, *rq2, *rq3, *rt;
     std::vector<std::unique_ptr<FrameSet>> sets;
 
     bool have_pair = false;
@@ -419,55 +426,61 @@ struct FhSession {
     int nbat = 1;
     int single = 0;  // > 0: pair / mid run at once (timed calls, warm-up)
     std::vector<Pending> pend;
-    // A batch runs as two graphs: the network (frame stage, pairs, the mids' maps) on st, then the render on the
-    // render stream rs, so the next batch's network overlaps this batch's render. What the render reads and writes
-    // (the arena's frames and frame planes, the maps, the static planes, the phases, the rendered frames) is held
-    // twice, and consecutive batches alternate between the two render sets; the members below point into the set
-    // the last batch used. Work on st outside a batch first waits for the renders still running (join_render).
+    // A batch runs as four graphs on streams of their own: the frame stage (fst), the static age pass and the still
+    // test's planes (sst), the pairs' network and the mids' maps (nst of its set), the render (rst), so that
+    // consecutive batches overlap. The frame stages of consecutive batches run in order (a batch may carry its oldest
+    // frame's outputs from the last one), and so do the static passes (one state plane, advanced pair by pair) and
+    // the renders. Every per-interval buffer and the arena are held twice; consecutive batches alternate between the
+    // two render sets, and a batch waits for the render of the batch before the last (which used its set) before it
+    // writes it. The members point into the set in use. Work on st outside a batch first waits for every batch
+    // stream (join_render).
     struct RenderSet {
         FrameSet arena;
         uint8_t* out = nullptr;  // nbat rendered frames, scattered to the output slots
-        __half *up7 = nullptr, *rt = nullptr;
-        int16_t* age = nullptr;
-        uint8_t* nearp = nullptr;
-        float2* ownp = nullptr;
-        float *dsum = nullptr, *tdev = nullptr;
-        // graphs over this set: the network of a full batch (by whether its oldest frame's stage is carried) and of
-        // shorter ones (by size), the render by size
-        cudaGraphExec_t net_full[2] = {};
-        std::map<int, cudaGraphExec_t> net_short, render;
-        cudaEvent_t net_done = nullptr, render_done = nullptr;
+#define FH_DECL(T, n) T n = nullptr;
+        FH_SET_BUFFERS(FH_DECL)
+#undef FH_DECL
+        // graphs over this set, by batch size: the frame stage and the static pass also by whether the oldest
+        // frame is carried from the last batch
+        std::map<int, cudaGraphExec_t> frame_g[2], static_g[2], net_g, render_g;
+        cudaEvent_t frame_done = nullptr, static_done = nullptr, net_done = nullptr, render_done = nullptr;
         bool render_pending = false;
     };
     RenderSet rsets[2];
     bool overlap_on = true;
-    int rpar = 0;         // the set the members point to
+    bool static_apart = false;  // run_pair leaves the static branch out (a batch runs it as its own graph)
+    int rpar = 0;               // the set the members point to
     // the set holding the current pair's per-interval buffers: 0 for a pair run on its own (its graphs are captured
     // on set 0), the batch's set for the newest interval of a batch
     int pair_set = 0;
-    int last_batch = 1;   // the set of the last batch (the first batch takes set 0)
-    cudaStream_t rs = nullptr;
+    int last_batch = 1;  // the set of the last batch (the first batch takes set 0)
+    cudaStream_t fst = nullptr, sst = nullptr, rst = nullptr, nst[2] = {};
+    cudaEvent_t st_ev = nullptr, join_evs[5] = {};
     FrameSet& arena() { return rsets[rpar].arena; }
     const FrameSet& arena() const { return rsets[rpar].arena; }
     uint8_t* arena_out() const { return rsets[rpar].out; }
     void use_set(int p) {
         rpar = p;
         const RenderSet& r = rsets[p];
-        up7 = r.up7;
-        rt = r.rt;
-        age = r.age;
-        nearp = r.nearp;
-        ownp = r.ownp;
-        dsum = r.dsum;
-        tdev = r.tdev;
+#define FH_LOAD(T, n) n = r.n;
+        FH_SET_BUFFERS(FH_LOAD)
+#undef FH_LOAD
     }
-    // st waits for every batch render still running
+    void save_set(int p) {
+        RenderSet& r = rsets[p];
+#define FH_STORE(T, n) r.n = n;
+        FH_SET_BUFFERS(FH_STORE)
+#undef FH_STORE
+    }
+    // st waits for everything issued on the batch streams
     void join_render() {
-        for (RenderSet& r : rsets)
-            if (r.render_pending) {
-                CK(cudaStreamWaitEvent(st, r.render_done, 0));
-                r.render_pending = false;
-            }
+        if (!fst) return;
+        cudaStream_t ss[5] = {fst, sst, nst[0], nst[1], rst};
+        for (int i = 0; i < 5; i++) {
+            CK(cudaEventRecord(join_evs[i], ss[i]));
+            CK(cudaStreamWaitEvent(st, join_evs[i], 0));
+        }
+        for (RenderSet& r : rsets) r.render_pending = false;
     }
     const FrameSet* carried = nullptr;  // the frame whose outputs entry nbat holds, at generation carried_gen
     uint64_t carried_gen = 0;
@@ -546,7 +559,8 @@ struct FhSession {
 
     ~FhSession() {
         if (st) cudaStreamSynchronize(st);
-        if (rs) cudaStreamSynchronize(rs);
+        for (cudaStream_t b : {fst, sst, rst, nst[0], nst[1]})
+            if (b) cudaStreamSynchronize(b);
         for (cudaStream_t sd : sides)
             if (sd) cudaStreamSynchronize(sd);
         if (h2d) cudaStreamSynchronize(h2d);
@@ -565,13 +579,14 @@ struct FhSession {
             if (fs->graph) cudaGraphExecDestroy(fs->graph);
         for (auto& kv : pair_graphs) cudaGraphExecDestroy(kv.second);
         for (RenderSet& r : rsets) {
-            for (cudaGraphExec_t g : r.net_full)
-                if (g) cudaGraphExecDestroy(g);
-            for (auto& kv : r.net_short) cudaGraphExecDestroy(kv.second);
-            for (auto& kv : r.render) cudaGraphExecDestroy(kv.second);
-            if (r.net_done) cudaEventDestroy(r.net_done);
-            if (r.render_done) cudaEventDestroy(r.render_done);
+            for (auto* gm : {&r.frame_g[0], &r.frame_g[1], &r.static_g[0], &r.static_g[1], &r.net_g, &r.render_g})
+                for (auto& kv : *gm) cudaGraphExecDestroy(kv.second);
+            for (cudaEvent_t e : {r.frame_done, r.static_done, r.net_done, r.render_done})
+                if (e) cudaEventDestroy(e);
         }
+        if (st_ev) cudaEventDestroy(st_ev);
+        for (cudaEvent_t e : join_evs)
+            if (e) cudaEventDestroy(e);
         for (auto& kv : mid_graphs) cudaGraphExecDestroy(kv.second);
         for (void* p : allocs) cudaFree(p);
         if (eng) eng->tensor_bytes -= std::min(eng->tensor_bytes, bytes);
@@ -579,7 +594,8 @@ struct FhSession {
             if (sd) cudaStreamDestroy(sd);
         if (h2d) cudaStreamDestroy(h2d);
         if (d2h) cudaStreamDestroy(d2h);
-        if (rs) cudaStreamDestroy(rs);
+        for (cudaStream_t b : {fst, sst, rst, nst[0], nst[1]})
+            if (b) cudaStreamDestroy(b);
         if (st) cudaStreamDestroy(st);
     }
 
@@ -761,45 +777,52 @@ struct FhSession {
             CK(fhk::spread_table(spread, st, fast));
             mask = alloc_n<uint8_t>((size_t)hp * wp);
             state = alloc_n<uchar4>((size_t)hp * wp);
-            age = alloc_n<int16_t>((size_t)nb * hp * wp);
-            nearp = alloc_n<uint8_t>((size_t)nb * hp * wp);
         }
-        if (still) dsum = alloc_n<float>((size_t)nb * hp * wp);
-        if (!fast && (still || protects)) ownp = alloc_n<float2>((size_t)nb * hp * wp);
-        cv = img(h16, w16, 56, nb);
-        ch1 = img(h16, w16, CCP, nb);
-        ch2 = img(h16, w16, CCP, nb);
-        ch3r = img(h16, w16, CCP, nb);
-        hcb = img(h16, w16, CCP, nb);
-        ob = img(h16, w16, 16, nb);
-        fv = img(h8, w8, 8, nb);
-        wbuf = img(h8, w8, 88, nb);
-        fcv = img(h8, w8, 32, nb);
-        fr1 = img(h8, w8, CRP, nb);
-        fr2 = img(h8, w8, CRP, nb);
-        fr3 = img(h8, w8, CRP, nb);
-        wt36 = img(h8, w8, 40, nb);
-        coef = alloc_n<float>((size_t)16 * nb);
-        maps = alloc_n<float>((size_t)6 * hc * wc * nb);
-        tmp = alloc_n<float>((size_t)5 * hc * wc * nb);
-        tdev = alloc_n<float>(nb);
         if (linear) {
             tnet = alloc_n<float>(nb);
             std::vector<float> half_t(nb, 0.5f);
             CK(cudaMemcpyAsync(tnet, half_t.data(), nb * sizeof(float), cudaMemcpyHostToDevice, st));
             CK(cudaStreamSynchronize(st));
         }
-        hm = img(h8, w8, CRP, nb);
-        fh1 = img(h8, w8, CRP, nb);
-        fh2 = img(h8, w8, CRP, nb);
-        dfilm = img(h8, w8, 8, nb);
-        ftvt = img(h8, w8, 8, nb);
-        up7 = img(qh, qw, 8, nb);
-        rx = img(qh, qw, 16, nb);
-        rq1 = img(qh, qw, CQP, nb);
-        rq2 = img(qh, qw, CQP, nb);
-        rq3 = img(qh, qw, CQP, nb);
-        rt = img(qh, qw, 4, nb);
+        // the per-interval buffers of a render set (two sets when batching)
+        for (int p = 0; p < (nbat > 1 ? 2 : 1); p++) {
+            if (protects) {
+                age = alloc_n<int16_t>((size_t)nb * hp * wp);
+                nearp = alloc_n<uint8_t>((size_t)nb * hp * wp);
+            }
+            if (still) dsum = alloc_n<float>((size_t)nb * hp * wp);
+            if (!fast && (still || protects)) ownp = alloc_n<float2>((size_t)nb * hp * wp);
+            cv = img(h16, w16, 56, nb);
+            ch1 = img(h16, w16, CCP, nb);
+            ch2 = img(h16, w16, CCP, nb);
+            ch3r = img(h16, w16, CCP, nb);
+            hcb = img(h16, w16, CCP, nb);
+            ob = img(h16, w16, 16, nb);
+            fv = img(h8, w8, 8, nb);
+            wbuf = img(h8, w8, 88, nb);
+            fcv = img(h8, w8, 32, nb);
+            fr1 = img(h8, w8, CRP, nb);
+            fr2 = img(h8, w8, CRP, nb);
+            fr3 = img(h8, w8, CRP, nb);
+            wt36 = img(h8, w8, 40, nb);
+            coef = alloc_n<float>((size_t)16 * nb);
+            maps = alloc_n<float>((size_t)6 * hc * wc * nb);
+            tmp = alloc_n<float>((size_t)5 * hc * wc * nb);
+            tdev = alloc_n<float>(nb);
+            hm = img(h8, w8, CRP, nb);
+            fh1 = img(h8, w8, CRP, nb);
+            fh2 = img(h8, w8, CRP, nb);
+            dfilm = img(h8, w8, 8, nb);
+            ftvt = img(h8, w8, 8, nb);
+            up7 = img(qh, qw, 8, nb);
+            rx = img(qh, qw, 16, nb);
+            rq1 = img(qh, qw, CQP, nb);
+            rq2 = img(qh, qw, CQP, nb);
+            rq3 = img(qh, qw, CQP, nb);
+            rt = img(qh, qw, 4, nb);
+            save_set(p);
+        }
+        use_set(0);
         auto make_axis = [&](int in, int out) {
             int* first = alloc_n<int>(out);
             int* count = alloc_n<int>(out);
@@ -815,25 +838,8 @@ struct FhSession {
             aa_qx = make_axis(NW, qw);
             aa_qy = make_axis(NH, qh);
         }
-        // render set 0 holds the buffers above; a batched session has a second set and the arenas
-        rsets[0].up7 = up7;
-        rsets[0].rt = rt;
-        rsets[0].age = age;
-        rsets[0].nearp = nearp;
-        rsets[0].ownp = ownp;
-        rsets[0].dsum = dsum;
-        rsets[0].tdev = tdev;
+        // a batched session's arenas and its batch streams and events
         if (nbat > 1) {
-            RenderSet& r1 = rsets[1];
-            r1.up7 = img(qh, qw, 8, nb);
-            r1.rt = img(qh, qw, 4, nb);
-            if (protects) {
-                r1.age = alloc_n<int16_t>((size_t)nb * hp * wp);
-                r1.nearp = alloc_n<uint8_t>((size_t)nb * hp * wp);
-            }
-            if (dsum) r1.dsum = alloc_n<float>((size_t)nb * hp * wp);
-            if (ownp) r1.ownp = alloc_n<float2>((size_t)nb * hp * wp);
-            r1.tdev = alloc_n<float>(nb);
             for (RenderSet& r : rsets) {
                 FrameSet& ar = r.arena;
                 ar.frame = alloc_n<uint8_t>((size_t)nf * w * h * 4);
@@ -845,9 +851,18 @@ struct FhSession {
                 ar.f8 = img(h8, w8, C8P, nf);
                 ar.f16 = img(h16, w16, C16P, nf);
                 r.out = alloc_n<uint8_t>((size_t)nb * w * h * 4);
-                CK(cudaEventCreateWithFlags(&r.net_done, cudaEventDisableTiming));
-                CK(cudaEventCreateWithFlags(&r.render_done, cudaEventDisableTiming));
+                for (cudaEvent_t* e : {&r.frame_done, &r.static_done, &r.net_done, &r.render_done})
+                    CK(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
             }
+            // the frame stages and the networks at the critical chain's priority, the static passes and the renders
+            // at the side branches'
+            CK(cudaStreamCreateWithPriority(&fst, cudaStreamNonBlocking, prio_hi));
+            CK(cudaStreamCreateWithPriority(&nst[0], cudaStreamNonBlocking, prio_hi));
+            CK(cudaStreamCreateWithPriority(&nst[1], cudaStreamNonBlocking, prio_hi));
+            CK(cudaStreamCreateWithPriority(&sst, cudaStreamNonBlocking, prio_lo));
+            CK(cudaStreamCreateWithPriority(&rst, cudaStreamNonBlocking, prio_lo));
+            CK(cudaEventCreateWithFlags(&st_ev, cudaEventDisableTiming));
+            for (cudaEvent_t& e : join_evs) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         }
         CK(cudaStreamSynchronize(st));
     }
@@ -901,38 +916,41 @@ struct FhSession {
         join_branches();
     }
 
+    // the static age pass over n pairs and the still test's planes (the pairs' sides A and B, as run_pair's)
+    void run_static(const FView& A, const FView& B, int n) {
+        const long long P = (long long)hp * wp, CW = (long long)hp * fhk::changed_words(wp);
+        CK(fhk::pair_planes(A.frame, B.frame, A.frame_bs, sargs, protects ? changed : nullptr, CW,
+                            still ? dsum : nullptr, P, n, st));
+        mark("pair_planes");
+        if (protects) {
+            CK(fhk::moved_plane(changed, CW, wp, hp, moved, n, st));
+            mark("moved_plane");
+            const long long l = n - 1;
+            CK(fhk::static_age(A.frame + l * A.frame_bs, B.frame + l * B.frame_bs, -A.frame_bs, changed + l * CW,
+                               moved + l * CW, -CW, mask, sargs, state, age + l * P, -P, n, spread, st, sp_in,
+                               sp_out));
+            mark("static_age");
+        }
+        // the fast render's probes clamp to the frame, the exact render's to the padded plane; the exact
+        // render also takes its own-pixel (es, kk) plane
+        if (fast && protects) {
+            CK(fhk::static_planes(age, nullptr, P, wp, hp, min_age, nearp, nullptr, n, st, w, h));
+            mark("static_planes");
+        } else if (!fast) {
+            CK(fhk::static_planes(protects ? age : nullptr, still ? dsum : nullptr, P, wp, hp, min_age,
+                                  protects ? nearp : nullptr, ownp, n, st));
+            mark("static_planes");
+        }
+    }
+
     // A and B: the pair's sides, with equal strides. The static age pass walks the n pairs in time order: entry n - 1
     // first (a batch keeps its newest interval in entry 0), so its strides are negated.
     // defer: leave the static-pass and repair branches open for run_mid to join where it first needs them (one graph
     // holding both stages); else both are joined before run_pair returns
     void run_pair(const FView& A, const FView& B, int n, bool defer = false) {
-        const long long P = (long long)hp * wp, CW = (long long)hp * fhk::changed_words(wp);
-        // the static age pass and the still test's plane read the two frames only: a branch beside the network
-        if (protects || still)
-            pend_static = branch([&] {
-                CK(fhk::pair_planes(A.frame, B.frame, A.frame_bs, sargs, protects ? changed : nullptr, CW,
-                                    still ? dsum : nullptr, P, n, st));
-                mark("pair_planes");
-                if (protects) {
-                    CK(fhk::moved_plane(changed, CW, wp, hp, moved, n, st));
-                    mark("moved_plane");
-                    const long long l = n - 1;
-                    CK(fhk::static_age(A.frame + l * A.frame_bs, B.frame + l * B.frame_bs, -A.frame_bs, changed + l * CW,
-                                       moved + l * CW, -CW, mask, sargs, state, age + l * P, -P, n, spread, st, sp_in,
-                                       sp_out));
-                    mark("static_age");
-                }
-                // the fast render's probes clamp to the frame, the exact render's to the padded plane; the exact
-                // render also takes its own-pixel (es, kk) plane
-                if (fast && protects) {
-                    CK(fhk::static_planes(age, nullptr, P, wp, hp, min_age, nearp, nullptr, n, st, w, h));
-                    mark("static_planes");
-                } else if (!fast) {
-                    CK(fhk::static_planes(protects ? age : nullptr, still ? dsum : nullptr, P, wp, hp, min_age,
-                                          protects ? nearp : nullptr, ownp, n, st));
-                    mark("static_planes");
-                }
-            });
+        // the static age pass and the still test's plane read the two frames only: a branch beside the network (a
+        // graph of its own in a batch)
+        if ((protects || still) && !static_apart) pend_static = branch([&] { run_static(A, B, n); });
         const long long ecv = E(h16, w16, 56), ecc = E(h16, w16, CCP), eob = E(h16, w16, 16), efv = E(h8, w8, 8),
                         ewb = E(h8, w8, 88), efc = E(h8, w8, 32), efr = E(h8, w8, CRP), ewt = E(h8, w8, 40);
         // coarse: img16 = (i16a, i16b), luma, sad r3 (graph ops 18-25), then c1..head (26-32)
@@ -1060,11 +1078,11 @@ struct FhSession {
 
     FrameSet& cur_set(uint32_t i) const { return *ins[i].sets[ins[i].cur]; }
 
-    // st reads the set next: order it after the set's pending host upload
-    void wait_upload(const FrameSet& fs) {
+    // `on` (st by default) reads the set next: order it after the set's pending host upload
+    void wait_upload(const FrameSet& fs, cudaStream_t on = nullptr) {
         FrameSet& f = const_cast<FrameSet&>(fs);
         if (!f.upload_pending) return;
-        CK(cudaStreamWaitEvent(st, f.uploaded, 0));
+        CK(cudaStreamWaitEvent(on ? on : st, f.uploaded, 0));
         f.upload_pending = false;
     }
     // the launches issued on st so far are the last to read these sets
@@ -1244,83 +1262,112 @@ struct FhSession {
         cp(to.f16, from.f16, from.f16_bs);
     }
 
-    // m = 2 .. nbat chained intervals (q[i].b == q[i + 1].a) on the other render set than the last batch's: the frames
-    // of times 0..m gathered into its arena (time t at entry m - t), then on st the network graph (the oldest frame's
-    // stage outputs carried from the last batch when that is its newest frame, unchanged since, else its frame stage
-    // too; the frame stage of the others; the pairs and the mids' maps of all m, interval i at entry m - 1 - i), then
-    // on rs the render graph and the rendered frames scattered to their output slots in time order.
+    // m = 2 .. nbat chained intervals (q[i].b == q[i + 1].a) on the other render set than the last batch's, as four
+    // graphs: on fst the frames of times 0..m gathered into the set's arena (time t at entry m - t) and the frame stage
+    // (the oldest frame's stage outputs carried from the last batch when that is its newest frame, unchanged since,
+    // else its frame stage too); on sst the static pass of the m pairs in time order; on the set's nst the pairs'
+    // network and the mids' maps (interval i at entry m - 1 - i); on rst, after both, the render and the rendered
+    // frames scattered to their output slots in time order. Host-ordered work on st (device-side frame writes, work
+    // done one interval at a time) precedes the batch.
     void run_batch(const std::vector<Pending>& q) {
         const int m = (int)q.size();
         const size_t fb = (size_t)w * h * 4;
         const int p = 1 - last_batch;
         RenderSet& R = rsets[p];
-        if (R.render_pending) {  // the render of the batch before the last reads this set
-            CK(cudaStreamWaitEvent(st, R.render_done, 0));
-            R.render_pending = false;
+        // the streams this batch uses: its own, or st for every one of them
+        cudaStream_t f_s = overlap_on ? fst : st, s_s = overlap_on ? sst : st, n_s = overlap_on ? nst[p] : st,
+                     r_s = overlap_on ? rst : st;
+        if (overlap_on) {
+            CK(cudaEventRecord(st_ev, st));
+            for (cudaStream_t b : {f_s, s_s, n_s}) CK(cudaStreamWaitEvent(b, st_ev, 0));
+            if (R.render_pending)  // the batch before the last used this set: its render is the last to read it
+                for (cudaStream_t b : {f_s, s_s, n_s}) CK(cudaStreamWaitEvent(b, R.render_done, 0));
         }
+        R.render_pending = false;
         use_set(p);
         for (int j = 0; j <= m; j++) {
             FrameSet* f = j == 0 ? q[m - 1].b : q[m - j].a;
-            wait_upload(*f);
-            CK(cudaMemcpyAsync(arena().frame + j * fb, f->frame, fb, cudaMemcpyDeviceToDevice, st));
+            wait_upload(*f, f_s);
+            CK(cudaMemcpyAsync(arena().frame + j * fb, f->frame, fb, cudaMemcpyDeviceToDevice, f_s));
         }
         for (int j = 0; j <= m; j++) {
             FrameSet* f = j == 0 ? q[m - 1].b : q[m - j].a;
-            CK(cudaEventRecord(f->released, st));
+            CK(cudaEventRecord(f->released, f_s));
             f->ever_read = true;
         }
         std::vector<float> tv(m);
         for (int e = 0; e < m; e++) tv[e] = q[m - 1 - e].t;
-        CK(cudaMemcpyAsync(tdev, tv.data(), m * sizeof(float), cudaMemcpyHostToDevice, st));
+        CK(cudaMemcpyAsync(tdev, tv.data(), m * sizeof(float), cudaMemcpyHostToDevice, f_s));
         const bool carry = m == nbat && carried == q[0].a && q[0].a->gen == carried_gen && batches_run > 0;
-        cudaGraphExec_t& net = m < nbat ? R.net_short[m] : R.net_full[carry ? 1 : 0];
         const FView fa = arena_view(1), fbv = arena_view(0);
-        if (!net) {
+        // graphs captured on first use (a key per set, size and carry)
+        auto graph = [&](std::map<int, cudaGraphExec_t>& gm, auto&& body) -> cudaGraphExec_t {
+            cudaGraphExec_t& g = gm[m];
+            if (!g) {
+                int nodes = 0;
+                g = capture(body, &nodes);
+                batch_kernels += nodes;
+            }
+            return g;
+        };
+        cudaGraphExec_t fg = graph(R.frame_g[carry ? 1 : 0], [&] {
+            if (carry) carry_from(1 - p);
+            run_frame(arena_view(0), carry ? m : m + 1);
+        });
+        cudaGraphExec_t sg = nullptr;
+        if (protects || still) {
             // the oldest frame's spread tests from the previous batch when its frame stage is carried too
             sp_in = carry ? spread_bits : nullptr;
             sp_out = spread_bits;
-            int nodes = 0;
             try {
-                net = capture(
-                    [&] {
-                        if (carry) carry_from(1 - p);
-                        run_frame(arena_view(0), carry ? m : m + 1);
-                        run_pair(fa, fbv, m, true);
-                        run_mid(PairSrc{fa, fbv}, nullptr, 0, m, 1);
-                    },
-                    &nodes);
+                sg = graph(R.static_g[carry ? 1 : 0], [&] {
+                    fhk::PrioScope low(prio_on, prio_lo);
+                    run_static(fa, fbv, m);
+                });
             } catch (...) {
                 sp_in = sp_out = nullptr;
                 throw;
             }
             sp_in = sp_out = nullptr;
-            batch_kernels = nodes;
         }
-        cudaGraphExec_t& ren = R.render[m];
-        if (!ren) {
-            int nodes = 0;
-            ren = capture(
-                [&] {
-                    fhk::PrioScope low(prio_on, prio_lo);
-                    run_mid(PairSrc{fa, fbv}, arena_out(), (long long)fb, m, 2);
-                },
-                &nodes);
-            batch_kernels += nodes;
+        static_apart = true;
+        cudaGraphExec_t ng = nullptr;
+        try {
+            ng = graph(R.net_g, [&] {
+                run_pair(fa, fbv, m, true);
+                run_mid(PairSrc{fa, fbv}, nullptr, 0, m, 1);
+            });
+        } catch (...) {
+            static_apart = false;
+            throw;
         }
-        cudaStream_t rst = overlap_on ? rs : st;
-        CK(cudaGraphLaunch(net, st));
-        CK(cudaEventRecord(R.net_done, st));
-        CK(cudaStreamWaitEvent(rst, R.net_done, 0));
-        CK(cudaGraphLaunch(ren, rst));
+        static_apart = false;
+        cudaGraphExec_t rg = graph(R.render_g, [&] {
+            fhk::PrioScope low(prio_on, prio_lo);
+            run_mid(PairSrc{fa, fbv}, arena_out(), (long long)fb, m, 2);
+        });
+        CK(cudaGraphLaunch(fg, f_s));
+        CK(cudaEventRecord(R.frame_done, f_s));
+        if (sg) {
+            CK(cudaStreamWaitEvent(s_s, R.frame_done, 0));
+            CK(cudaGraphLaunch(sg, s_s));
+            CK(cudaEventRecord(R.static_done, s_s));
+        }
+        CK(cudaStreamWaitEvent(n_s, R.frame_done, 0));
+        CK(cudaGraphLaunch(ng, n_s));
+        CK(cudaEventRecord(R.net_done, n_s));
+        CK(cudaStreamWaitEvent(r_s, R.net_done, 0));
+        if (sg) CK(cudaStreamWaitEvent(r_s, R.static_done, 0));
+        CK(cudaGraphLaunch(rg, r_s));
         carried = q[m - 1].b;
         carried_gen = q[m - 1].b->gen;
         for (int i = 0; i < m; i++) {
             const int e = m - 1 - i;
-            CK(cudaMemcpyAsync(outs[q[i].out], arena_out() + e * fb, fb, cudaMemcpyDeviceToDevice, rst));
-            CK(cudaEventRecord(out_ready[q[i].out], rst));
+            CK(cudaMemcpyAsync(outs[q[i].out], arena_out() + e * fb, fb, cudaMemcpyDeviceToDevice, r_s));
+            CK(cudaEventRecord(out_ready[q[i].out], r_s));
         }
-        CK(cudaEventRecord(R.render_done, rst));
-        R.render_pending = true;
+        CK(cudaEventRecord(R.render_done, r_s));
+        R.render_pending = overlap_on;
         last_batch = p;
         pair_set = p;
         // the newest interval is entry 0 of every per-interval buffer: a further mid of it runs there
@@ -1615,9 +1662,8 @@ FhSession* session_new(FhEngine* e, const FhModel* m, const FhSessionOptions& o,
     CK(cudaSetDevice(e->device));
     CK(cudaDeviceGetStreamPriorityRange(&s->prio_lo, &s->prio_hi));
     CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
-    // batch renders at the lowest priority, beside the next batch's network (FH_OVERLAP=0: on st after it)
+    // batches on streams of their own, overlapping one another (FH_OVERLAP=0: every batch on st, one after another)
     s->overlap_on = !env_is("FH_OVERLAP", "0");
-    if (batch > 1) CK(cudaStreamCreateWithPriority(&s->rs, cudaStreamNonBlocking, s->prio_lo));
     for (cudaStream_t& sd : s->sides) CK(cudaStreamCreateWithFlags(&sd, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&s->h2d, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&s->d2h, cudaStreamNonBlocking));
