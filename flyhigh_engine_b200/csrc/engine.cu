@@ -375,7 +375,8 @@ struct FhSession {
     int pend_static = -1, pend_repair = -1;
     int branches = 0;  // forks of the stage being issued, all joined by join_branches()
     bool pdl_on = true;  // programmatic dependent launch inside the stage graphs (FH_PDL=0 turns it off)
-    // launch priorities inside the stage graphs: the critical chain high, the side branches low (FH_PRIO=0: none)
+    // launch priorities inside the stage graphs: the critical chain high, the side branches low (FH_PRIO=0: none; off
+    // by default in batched sessions)
     bool prio_on = true;
     int prio_hi = 0, prio_lo = 0;
     // Stride-1 convs of batched sessions run on the tcgen05 kernel where they fit; one-interval sessions (small grids)
@@ -1658,6 +1659,10 @@ FhSession* session_new(FhEngine* e, const FhModel* m, const FhSessionOptions& o,
     if (batch > 16) fail("batch: %d intervals per launch (1..16)", batch);
     s->nbat = batch;
     if (batch > 1 && !env_is("FH_UMMA", "0")) s->umma_on = true;
+    // a batched session's graphs take the priority of their streams (frame stages and networks high, static passes
+    // and renders low) rather than per-launch priorities, which measured 1.2 % slower with batches overlapping
+    // (FH_PRIO=1 keeps them)
+    if (batch > 1 && !env_is("FH_PRIO", "1")) s->prio_on = false;
     s->eng = e;
     CK(cudaSetDevice(e->device));
     CK(cudaDeviceGetStreamPriorityRange(&s->prio_lo, &s->prio_hi));
