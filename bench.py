@@ -107,7 +107,7 @@ def dist():
     return ws, rank, local
 
 
-WORKLOAD = ("FlyHighFG Core 1920x1080, 120-frame sequence, pair + mid(0.5) per interval (config 2), internal 856x480, "
+WORKLOAD = ("FlyHighFG Core 1920x1080, 120-frame sequence, pair + mid(0.5) per interval (config 2), internal 864x480, "
             "k 1, repair 1, bicubic, static protection on")
 
 
@@ -234,9 +234,10 @@ def main():
     warm = max(args.warmup, 3)
     for _ in range(warm):
         step_device()
-    counts = s.launch_counts()
+    k0 = s.kernel_launches()
     with Clocks(local) as clk:
         ms = timed(step_device, args.steps)
+    launches = s.kernel_launches() - k0  # this rank's kernels in the timed steps
     gen_per_rank = n - 1
     value = gen_per_rank * ws / (ms / 1000.0)
 
@@ -323,7 +324,6 @@ def main():
                "sample": f"{args.cpu_sample} consecutive intervals of the same 1080p sequence (pair + mid(0.5)), "
                          f"{dt:.1f} s on the host cores"}
     if rank == 0:
-        per_interval_launches = counts["frame"] + counts["pair"] + counts["mid"] + 1
         line = {"metric": METRIC, "value": value, "unit": "generated frames/s", "n_gpus": ws, "steps": args.steps,
                 "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f16",
@@ -333,7 +333,7 @@ def main():
                                                   "to one at a time)",
                            "frames_per_step": gen_per_rank, "l2": "inputs (1 GB of frames) larger than L2, no flush",
                            "batch": args.batch, "pair_ms": pair_ms, "mid_ms": mid_ms},
-                "gpu_launches": per_interval_launches * gen_per_rank + counts["frame"],
+                "gpu_launches": launches * ws,
                 "clocks": clk.summary(), "roofline": roof, "roofline_conv": roof_conv, "cpu_baseline": cpu,
                 "e2e": e2e, "fast_render_linear_t": fast, "kernel_ms": {k: round(v, 5) for k, v in sorted(prof.items(), key=lambda x: -x[1])[:12]}}
         print(json.dumps(line), flush=True)
@@ -363,15 +363,15 @@ def conv_flops(s, nb: int) -> float:
 
 def render_bytes(p) -> float:
     """Algorithmic bytes of one full-resolution render: the two source frames read once (B, G, R as f16, 12 B/px), the
-    static planes of the padded plane (age i16, near u8, the still test's per-pixel sums f32: 7 B/px), the
-    quarter-resolution flow / visibility (7 ch) and residual (3 ch) maps (f16), the rgba8 frame written (4 B/px)."""
+    static planes of the padded plane (the own-pixel (es, kk) pair f32 and near u8: 9 B/px), the quarter-resolution
+    flow / visibility (7 ch) and residual (3 ch) maps (f16), the rgba8 frame written (4 B/px)."""
     q = p["qh"] * p["qw"]
-    return float(W * H * (12 + 4) + p["hp"] * p["wp"] * 7 + q * (7 + 3) * 2)
+    return float(W * H * (12 + 4) + p["hp"] * p["wp"] * 9 + q * (7 + 3) * 2)
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum per rendered 1920 x 1080 frame, from the ncu capture of one batched
-# k_render launch (4 frames: 144.40 MB read + 25.93 MB written) summarised in profiles/k_render_1080p.md
-RENDER_TRAFFIC = 42.58e6
+# k_render launch (4 frames: 164.33 MB read + 26.68 MB written) summarised in profiles/k_render_1080p.md
+RENDER_TRAFFIC = 47.75e6
 
 
 def roofline_blocks(s, prof, nb):

@@ -85,6 +85,7 @@ EXPORTS = [
     ("fh_session_report_json", c_int, [c_void_p, c_char_p, c_size_t]),
     ("fh_session_cuda_stream", c_int, [c_void_p, POINTER(c_void_p)]),
     ("fh_session_join", c_int, [c_void_p]),
+    ("fh_session_kernel_launches", ctypes.c_longlong, [c_void_p]),
     ("fh_session_slot_device_ptr", c_int, [c_void_p, c_uint32, c_int, POINTER(c_void_p)]),
     ("fh_session_write_rgba_device", c_int, [c_void_p, c_uint32, c_void_p, c_size_t]),
     ("fh_session_debug_tensor", c_long, [c_void_p, c_char_p, POINTER(c_float), c_size_t, POINTER(c_int)]),
@@ -371,6 +372,10 @@ class Session:
         p = c_void_p()
         _check(lib().fh_session_cuda_stream(self._h, byref(p)))
         return p.value or 0
+
+    def kernel_launches(self) -> int:
+        """Kernels this session has launched so far (graph kernel nodes and eager launches; profiling excepted)."""
+        return _check(lib().fh_session_kernel_launches(self._h))
 
     def join(self) -> None:
         """Orders every batch render issued so far before the work later issued on cuda_stream()."""

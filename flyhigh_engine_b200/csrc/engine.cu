@@ -486,6 +486,15 @@ struct FhSession {
     const FrameSet* carried = nullptr;  // the frame whose outputs entry nbat holds, at generation carried_gen
     uint64_t carried_gen = 0;
     int batch_kernels = 0;
+    // kernels launched so far by this session's graphs and eager steps outside the profiling calls
+    // (fh_session_kernel_launches); graph_kernel_nodes: the kernel nodes of each instantiated graph
+    long long kernels_launched = 0;
+    std::map<cudaGraphExec_t, int> graph_kernel_nodes;
+    void launch_graph(cudaGraphExec_t g, cudaStream_t on) {
+        CK(cudaGraphLaunch(g, on));
+        auto it = graph_kernel_nodes.find(g);
+        if (it != graph_kernel_nodes.end()) kernels_launched += it->second;
+    }
     long long batches_run = 0;
     std::map<std::pair<const FrameSet*, const FrameSet*>, cudaGraphExec_t> pair_graphs;
     std::map<std::tuple<const void*, const void*, const void*, const void*, const void*>, cudaGraphExec_t> mid_graphs;
@@ -1069,10 +1078,19 @@ struct FhSession {
         size_t n = 0;
         CK(cudaGraphGetNodes(g, nullptr, &n));
         if (nodes) *nodes = (int)n;
+        std::vector<cudaGraphNode_t> nv(n);
+        int kn = 0;
+        if (n) CK(cudaGraphGetNodes(g, nv.data(), &n));
+        for (cudaGraphNode_t nd : nv) {
+            cudaGraphNodeType ty;
+            CK(cudaGraphNodeGetType(nd, &ty));
+            if (ty == cudaGraphNodeTypeKernel) kn++;
+        }
         cudaGraphExec_t ex = nullptr;
         cudaError_t e = cudaGraphInstantiate(&ex, g, prio_on ? cudaGraphInstantiateFlagUseNodePriority : 0);
         cudaGraphDestroy(g);
         CK(e);
+        graph_kernel_nodes[ex] = kn;
         eng->graphs_built++;
         return ex;
     }
@@ -1107,7 +1125,7 @@ struct FhSession {
     void ensure_features(FrameSet& fs) {
         if (fs.feat_gen == fs.gen) return;
         if (!fs.graph) fs.graph = capture([&] { run_frame(view_of(fs), 1); }, &frame_kernels);
-        CK(cudaGraphLaunch(fs.graph, st));
+        launch_graph(fs.graph, st);
         fs.feat_gen = fs.gen;
     }
 
@@ -1135,7 +1153,7 @@ struct FhSession {
         wait_upload(B);
         ensure_features(A);
         ensure_features(B);
-        CK(cudaGraphLaunch(pair_graph(A, B), st));
+        launch_graph(pair_graph(A, B), st);
         mark_read(A, B);
         pair = PairSrc{view_of(A), view_of(B), &A, &B};
         have_pair = true;
@@ -1175,12 +1193,12 @@ struct FhSession {
     void launch_mid(uint32_t out) {
         if (linear) {
             if (!maps_done) {
-                CK(cudaGraphLaunch(mid_graph(out, 1), st));
+                launch_graph(mid_graph(out, 1), st);
                 maps_done = true;
             }
-            CK(cudaGraphLaunch(mid_graph(out, 2), st));
+            launch_graph(mid_graph(out, 2), st);
         } else {
-            CK(cudaGraphLaunch(mid_graph(out), st));
+            launch_graph(mid_graph(out), st);
         }
     }
 
@@ -1199,6 +1217,7 @@ struct FhSession {
         if (!have_pair) fail("pair two input slots first");
         use_set(pair_set);
         CK(fhk::set_scalar(tdev, t, st));
+        kernels_launched++;
         launch_mid(out);
         if (pair.sa) mark_read(*pair.sa, *pair.sb);
         CK(cudaEventRecord(out_ready[out], st));
@@ -1224,6 +1243,7 @@ struct FhSession {
                 pair_now(*x.a, *x.b);
                 if (x.mid) {
                     CK(fhk::set_scalar(tdev, x.t, st));
+                    kernels_launched++;
                     launch_mid(x.out);
                     mark_read(*x.a, *x.b);
                     CK(cudaEventRecord(out_ready[x.out], st));
@@ -1347,19 +1367,19 @@ struct FhSession {
             fhk::PrioScope low(prio_on, prio_lo);
             run_mid(PairSrc{fa, fbv}, arena_out(), (long long)fb, m, 2);
         });
-        CK(cudaGraphLaunch(fg, f_s));
+        launch_graph(fg, f_s);
         CK(cudaEventRecord(R.frame_done, f_s));
         if (sg) {
             CK(cudaStreamWaitEvent(s_s, R.frame_done, 0));
-            CK(cudaGraphLaunch(sg, s_s));
+            launch_graph(sg, s_s);
             CK(cudaEventRecord(R.static_done, s_s));
         }
         CK(cudaStreamWaitEvent(n_s, R.frame_done, 0));
-        CK(cudaGraphLaunch(ng, n_s));
+        launch_graph(ng, n_s);
         CK(cudaEventRecord(R.net_done, n_s));
         CK(cudaStreamWaitEvent(r_s, R.net_done, 0));
         if (sg) CK(cudaStreamWaitEvent(r_s, R.static_done, 0));
-        CK(cudaGraphLaunch(rg, r_s));
+        launch_graph(rg, r_s);
         carried = q[m - 1].b;
         carried_gen = q[m - 1].b->gen;
         for (int i = 0; i < m; i++) {
@@ -1458,6 +1478,8 @@ struct FhSession {
             run_frame(view_of(B), 1);
             run_pair(view_of(A), view_of(B), 1);
             CK(fhk::set_scalar(tdev, t, st));
+            kernels_launched++;
+        kernels_launched++;
             mark("set_t");
             run_mid(PairSrc{view_of(A), view_of(B), &A, &B}, outs[out], 0, 1);
         } catch (...) {
@@ -2043,6 +2065,13 @@ int fh_session_cuda_stream(const FhSession* cs, void** stream) {
     });
 }
 
+long long fh_session_kernel_launches(const FhSession* cs) {
+    return guard(-1LL, [&]() -> long long {
+        if (!cs) fail("null argument");
+        return cs->kernels_launched;
+    });
+}
+
 int fh_session_join(const FhSession* cs) {
     return guard(-1, [&] {
         FhSession* s = const_cast<FhSession*>(cs);
@@ -2101,6 +2130,7 @@ int fh_session_advance_static(const FhSession* cs, uint32_t a, uint32_t b) {
         CK(fhk::moved_plane(s->changed, 0, s->wp, s->hp, s->moved, 1, s->st));
         CK(fhk::static_age(A.frame, B.frame, 0, s->changed, s->moved, 0, s->mask, s->sargs, s->state, s->age, 0, 1,
                            s->spread, s->st));
+        s->kernels_launched += 3;
         s->mark_read(A, B);
         return 0;
     });

@@ -79,6 +79,11 @@ int fh_session_profile_json(const FhSession* session, uint32_t a, uint32_t b, fl
  * last batch left it; the static state advances as that batch advanced it. Needs a batch to have run. */
 int fh_session_profile_batch_json(const FhSession* session, char* buf, size_t cap);
 
+/* Kernels this session has launched so far (the kernel nodes of every graph launch, and the few kernels it launches
+ * outside graphs), the profiling calls excepted: the difference over a stretch of calls counts its launches. -1 on a
+ * null session. */
+long long fh_session_kernel_launches(const FhSession* session);
+
 /* Kernel launches of one pair and of one mid (the nodes of their CUDA graphs). 0 on success. */
 int fh_session_launch_counts(const FhSession* session, int* pair_kernels, int* mid_kernels, int* frame_kernels);
 
