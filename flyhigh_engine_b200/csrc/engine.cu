@@ -447,16 +447,18 @@ struct FhSession {
         cudaEvent_t frame_done = nullptr, static_done = nullptr, net_done = nullptr, render_done = nullptr;
         bool render_pending = false;
     };
-    RenderSet rsets[2];
+    static constexpr int MAX_SETS = 3;
+    RenderSet rsets[MAX_SETS];
+    int nsets = 2;  // render sets of a batched session (FH_SETS=3: three, one more batch in flight)
     bool overlap_on = true;
     bool static_apart = false;  // run_pair leaves the static branch out (a batch runs it as its own graph)
     int rpar = 0;               // the set the members point to
     // the set holding the current pair's per-interval buffers: 0 for a pair run on its own (its graphs are captured
     // on set 0), the batch's set for the newest interval of a batch
     int pair_set = 0;
-    int last_batch = 1;  // the set of the last batch (the first batch takes set 0)
-    cudaStream_t fst = nullptr, sst = nullptr, rst = nullptr, nst[2] = {};
-    cudaEvent_t st_ev = nullptr, join_evs[5] = {};
+    int last_batch = -1;  // the set of the last batch (-1: none yet; the first batch takes set 0)
+    cudaStream_t fst = nullptr, sst = nullptr, rst = nullptr, nst[MAX_SETS] = {};
+    cudaEvent_t st_ev = nullptr, join_evs[3 + MAX_SETS] = {};
     FrameSet& arena() { return rsets[rpar].arena; }
     const FrameSet& arena() const { return rsets[rpar].arena; }
     uint8_t* arena_out() const { return rsets[rpar].out; }
@@ -476,8 +478,10 @@ struct FhSession {
     // st waits for everything issued on the batch streams
     void join_render() {
         if (!fst) return;
-        cudaStream_t ss[5] = {fst, sst, nst[0], nst[1], rst};
-        for (int i = 0; i < 5; i++) {
+        cudaStream_t ss[3 + MAX_SETS] = {fst, sst, rst};
+        for (int i = 0; i < MAX_SETS; i++) ss[3 + i] = nst[i];
+        for (int i = 0; i < 3 + MAX_SETS; i++) {
+            if (!ss[i]) continue;
             CK(cudaEventRecord(join_evs[i], ss[i]));
             CK(cudaStreamWaitEvent(st, join_evs[i], 0));
         }
@@ -569,7 +573,7 @@ struct FhSession {
 
     ~FhSession() {
         if (st) cudaStreamSynchronize(st);
-        for (cudaStream_t b : {fst, sst, rst, nst[0], nst[1]})
+        for (cudaStream_t b : {fst, sst, rst, nst[0], nst[1], nst[2]})
             if (b) cudaStreamSynchronize(b);
         for (cudaStream_t sd : sides)
             if (sd) cudaStreamSynchronize(sd);
@@ -604,7 +608,7 @@ struct FhSession {
             if (sd) cudaStreamDestroy(sd);
         if (h2d) cudaStreamDestroy(h2d);
         if (d2h) cudaStreamDestroy(d2h);
-        for (cudaStream_t b : {fst, sst, rst, nst[0], nst[1]})
+        for (cudaStream_t b : {fst, sst, rst, nst[0], nst[1], nst[2]})
             if (b) cudaStreamDestroy(b);
         if (st) cudaStreamDestroy(st);
     }
@@ -795,7 +799,7 @@ struct FhSession {
             CK(cudaStreamSynchronize(st));
         }
         // the per-interval buffers of a render set (two sets when batching)
-        for (int p = 0; p < (nbat > 1 ? 2 : 1); p++) {
+        for (int p = 0; p < (nbat > 1 ? nsets : 1); p++) {
             if (protects) {
                 age = alloc_n<int16_t>((size_t)nb * hp * wp);
                 nearp = alloc_n<uint8_t>((size_t)nb * hp * wp);
@@ -850,7 +854,8 @@ struct FhSession {
         }
         // a batched session's arenas and its batch streams and events
         if (nbat > 1) {
-            for (RenderSet& r : rsets) {
+            for (int p = 0; p < nsets; p++) {
+                RenderSet& r = rsets[p];
                 FrameSet& ar = r.arena;
                 ar.frame = alloc_n<uint8_t>((size_t)nf * w * h * 4);
                 ar.half = alloc_n<__half>((size_t)nf * w * h * 4);
@@ -867,8 +872,7 @@ struct FhSession {
             // the frame stages and the networks at the critical chain's priority, the static passes and the renders
             // at the side branches'
             CK(cudaStreamCreateWithPriority(&fst, cudaStreamNonBlocking, prio_hi));
-            CK(cudaStreamCreateWithPriority(&nst[0], cudaStreamNonBlocking, prio_hi));
-            CK(cudaStreamCreateWithPriority(&nst[1], cudaStreamNonBlocking, prio_hi));
+            for (int p = 0; p < nsets; p++) CK(cudaStreamCreateWithPriority(&nst[p], cudaStreamNonBlocking, prio_hi));
             CK(cudaStreamCreateWithPriority(&sst, cudaStreamNonBlocking, prio_lo));
             CK(cudaStreamCreateWithPriority(&rst, cudaStreamNonBlocking, prio_lo));
             CK(cudaEventCreateWithFlags(&st_ev, cudaEventDisableTiming));
@@ -1293,7 +1297,7 @@ struct FhSession {
     void run_batch(const std::vector<Pending>& q) {
         const int m = (int)q.size();
         const size_t fb = (size_t)w * h * 4;
-        const int p = 1 - last_batch;
+        const int p = (last_batch + 1) % nsets;
         RenderSet& R = rsets[p];
         // the streams this batch uses: its own, or st for every one of them
         cudaStream_t f_s = overlap_on ? fst : st, s_s = overlap_on ? sst : st, n_s = overlap_on ? nst[p] : st,
@@ -1332,7 +1336,7 @@ struct FhSession {
             return g;
         };
         cudaGraphExec_t fg = graph(R.frame_g[carry ? 1 : 0], [&] {
-            if (carry) carry_from(1 - p);
+            if (carry) carry_from(last_batch);
             run_frame(arena_view(0), carry ? m : m + 1);
         });
         cudaGraphExec_t sg = nullptr;
@@ -1685,6 +1689,7 @@ FhSession* session_new(FhEngine* e, const FhModel* m, const FhSessionOptions& o,
     // and renders low) rather than per-launch priorities, which measured 1.2 % slower with batches overlapping
     // (FH_PRIO=1 keeps them)
     if (batch > 1 && !env_is("FH_PRIO", "1")) s->prio_on = false;
+    if (batch > 1 && env_is("FH_SETS", "3")) s->nsets = 3;
     s->eng = e;
     CK(cudaSetDevice(e->device));
     CK(cudaDeviceGetStreamPriorityRange(&s->prio_lo, &s->prio_hi));
