@@ -1503,16 +1503,42 @@ __global__ void __launch_bounds__(256, 5) k_render(RenderArgs r) {
         }
         kk = ok.y;  // keep_static apply ramp (keep_static.wgsl:25-26)
     }
+    // per channel: the blend, the still mix, the static mix, the f16 render plane, the keep_static ramp, rgba8. B and G
+    // on the lanes of packed f32x2 arithmetic (each lane rounding as the scalar code of R), R alone.
+    auto clamp01 = [](float v) { return fminf(fmaxf(v, 0.0f), 1.0f); };
+    auto dup = [](float v) { return make_float2(v, v); };
+    const float2 sw = dup(stillw), sw1 = dup(1.0f - stillw), rw = dup(raw), rw1 = dup(1.0f - raw), k2 = dup(kk),
+                 k1 = dup(1.0f - kk);
     uint32_t q[3];
-#pragma unroll
-    for (int c = 0; c < 3; c++) {
-        const float mixv = ca[c] * bwa + cb[c] * bwb + cr[c] * rk;
-        float ov = fminf(fmaxf(mixv * (1.0f - stillw) + own[c] * stillw, 0.0f), 1.0f);
-        const float src = 0.5f * (comp(pa_here, c) + comp(pb_here, c));
-        if (age) ov = fminf(fmaxf(ov * (1.0f - raw) + src * raw, 0.0f), 1.0f);
-        float hv = rh(ov);  // the render plane is f16
+    {
+        const float2 mixv = __fadd2_rn(__fadd2_rn(__fmul2_rn(make_float2(ca[0], ca[1]), dup(bwa)),
+                                                  __fmul2_rn(make_float2(cb[0], cb[1]), dup(bwb))),
+                                       __fmul2_rn(make_float2(cr[0], cr[1]), dup(rk)));
+        float2 ov = __fadd2_rn(__fmul2_rn(mixv, sw1), __fmul2_rn(make_float2(own[0], own[1]), sw));
+        ov = make_float2(clamp01(ov.x), clamp01(ov.y));
+        const float2 src = __fmul2_rn(dup(0.5f), __fadd2_rn(make_float2(pa_here.x, pa_here.y),
+                                                             make_float2(pb_here.x, pb_here.y)));
+        if (age) {
+            ov = __fadd2_rn(__fmul2_rn(ov, rw1), __fmul2_rn(src, rw));
+            ov = make_float2(clamp01(ov.x), clamp01(ov.y));
+        }
+        float2 hv = __half22float2(__floats2half2_rn(ov.x, ov.y));  // the render plane is f16
+        if (kk > 0.0f) {
+            const float2 m = __fadd2_rn(__fmul2_rn(hv, k1), __fmul2_rn(src, k2));
+            hv = __half22float2(__floats2half2_rn(m.x, m.y));
+        }
+        const float2 qv = __fadd2_rn(__fmul2_rn(make_float2(clamp01(hv.x), clamp01(hv.y)), dup(255.0f)), dup(0.5f));
+        q[0] = (uint32_t)qv.x;
+        q[1] = (uint32_t)qv.y;
+    }
+    {
+        const float mixv = ca[2] * bwa + cb[2] * bwb + cr[2] * rk;
+        float ov = clamp01(mixv * (1.0f - stillw) + own[2] * stillw);
+        const float src = 0.5f * (pa_here.z + pb_here.z);
+        if (age) ov = clamp01(ov * (1.0f - raw) + src * raw);
+        float hv = rh(ov);
         if (kk > 0.0f) hv = rh(hv * (1.0f - kk) + src * kk);
-        q[c] = (uint32_t)(fminf(fmaxf(hv, 0.0f), 1.0f) * 255.0f + 0.5f);
+        q[2] = (uint32_t)(clamp01(hv) * 255.0f + 0.5f);
     }
     // q[0] = B, q[1] = G, q[2] = R
     reinterpret_cast<uint32_t*>(r.out + (long long)n * r.out_bs)[here] = q[2] | (q[1] << 8) | (q[0] << 16) | 0xff000000u;
