@@ -454,6 +454,41 @@ def test_batched_session_matches_single(synth_model_dir, batch, size, opts):
         assert np.array_equal(age1, ageb), n
 
 
+def test_batch_streams_match_one_stream_and_count_launches(synth_model_dir, monkeypatch):
+    """A batched session runs each batch as four graphs on streams of their own, so that consecutive batches overlap
+    (the frame stage, the static pass, the network, the render). The frames and the static state must not depend on
+    that: the same intervals with every batch serialised on the session stream (FH_OVERLAP=0, read when the session is
+    built) give the same bytes. fh_session_kernel_launches counts the session's kernels: the same calls launch the
+    same number, the same on both schedules."""
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200 import synth_frames
+    w, h, batch, n = 384, 160, 4, 11
+    model = fh.Model(synth_model_dir)
+    frames = synth_frames.sequence_c2(n, w, h, seed=23)
+
+    def run(overlap):
+        monkeypatch.setenv("FH_OVERLAP", "1" if overlap else "0")
+        s = fh.Session(fh.Engine(), model, w, h, batch=batch)
+        ins = [s.add_input(), s.add_input()]
+        outs = [s.add_output() for _ in range(n - 1)]
+        k0 = s.kernel_launches()
+        s.write(ins[0], frames[0])
+        for i in range(1, n):
+            s.write(ins[i % 2], frames[i])
+            s.pair(ins[(i - 1) % 2], ins[i % 2])
+            s.mid(0.5, outs[i - 1])
+        got = [np.frombuffer(s.read(o), np.uint8).copy() for o in outs]
+        s.join()
+        return got, s.tensor("age"), s.kernel_launches() - k0
+
+    a, age_a, ka = run(True)
+    b, age_b, kb = run(False)
+    for i, (x, y) in enumerate(zip(a, b)):
+        assert np.array_equal(x, y), i
+    assert np.array_equal(age_a, age_b)
+    assert ka == kb and ka > 2 * 40, (ka, kb)
+
+
 def test_batch_profile(synth_model_dir):
     """fh_session_profile_batch_json: one batch's kernels timed eagerly, each stage once (the frame stage for all
     batch + 1 frames in one launch per kernel); refused for a one-interval session and before any batch ran."""
