@@ -371,7 +371,7 @@ struct FhSession {
     cudaStream_t sides[4] = {};  // branch i runs on sides[i], so branches do not wait for one another
     cudaEvent_t fork_ev[4] = {}, join_ev[4] = {};
     bool joined[4] = {};
-    // the pair's branches a batch graph joins later, where the mid first needs them (-1: none pending)
+    // the pair's branches a stage graph joins later, where the mid first needs them (-1: none pending)
     int pend_static = -1, pend_repair = -1;
     int branches = 0;  // forks of the stage being issued, all joined by join_branches()
     bool pdl_on = true;  // programmatic dependent launch inside the stage graphs (FH_PDL=0 turns it off)

@@ -74,7 +74,7 @@ int fh_session_advance_static(const FhSession* session, uint32_t a, uint32_t b);
 int fh_session_profile_json(const FhSession* session, uint32_t a, uint32_t b, float t, uint32_t out, char* buf,
                             size_t cap);
 
-/* The same for one batch of a batched session (fh_session_create_batched): every kernel of the batch graph (the frame
+/* The same for one batch of a batched session (fh_session_create_batched): every kernel of a batch's graphs (the frame
  * stage of its B + 1 frames, the pairs and mids of its B intervals) run once eagerly on the session's batch arena as the
  * last batch left it; the static state advances as that batch advanced it. Needs a batch to have run. */
 int fh_session_profile_batch_json(const FhSession* session, char* buf, size_t cap);
