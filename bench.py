@@ -362,16 +362,37 @@ def conv_flops(s, nb: int) -> float:
 
 
 def render_bytes(p) -> float:
-    """Algorithmic bytes of one full-resolution render: the two source frames read once (B, G, R as f16, 12 B/px), the
-    static planes of the padded plane (the own-pixel (es, kk) pair f32 and near u8: 9 B/px), the quarter-resolution
-    flow / visibility (7 ch) and residual (3 ch) maps (f16), the rgba8 frame written (4 B/px)."""
+    """Algorithmic bytes of one full-resolution render as the hot-path measurement defines them: the two source frames
+    read once (B, G, R as f16, 12 B/px), the quarter-resolution flow / visibility (7 ch) and residual (3 ch) maps (f16)
+    read once, the rgba8 frame written (4 B/px)."""
     q = p["qh"] * p["qw"]
-    return float(W * H * (12 + 4) + p["hp"] * p["wp"] * 9 + q * (7 + 3) * 2)
+    return float(W * H * (12 + 4) + q * (7 + 3) * 2)
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum per rendered 1920 x 1080 frame, from the ncu capture of one batched
-# k_render launch (4 frames: 164.33 MB read + 26.68 MB written) summarised in profiles/k_render_1080p.md
-RENDER_TRAFFIC = 47.75e6
+def render_design_bytes(p) -> float:
+    """Bytes this design adds to one render beyond the algorithmic ones: the static planes of the padded plane that
+    k_static_planes writes and k_render reads (the own-pixel (es, kk) pair as two f32 and near as u8, 9 B/px)."""
+    return float(p["hp"] * p["wp"] * 9)
+
+
+RENDER_PROFILE = os.path.join(ROOT, "profiles", "k_render_1080p.md")
+
+
+def render_traffic():
+    """DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per rendered 1920 x 1080 frame of the current k_render,
+    from the ncu capture that profiles/k_render_1080p.md summarises (its 'traffic per frame' line), with the capture's
+    description; (None, reason) when the summary is missing."""
+    import re
+    try:
+        with open(RENDER_PROFILE) as f:
+            text = f.read()
+    except OSError:
+        return None, "no ncu summary"
+    m = re.search(r"traffic per frame \(read \+ write\): ([0-9.]+) MB", text)
+    c = re.search(r"capture: (.+)", text)
+    if not m:
+        return None, "no traffic line in the ncu summary"
+    return float(m.group(1)) * 1e6, (c.group(1).strip() if c else "profiles/k_render_1080p.md")
 
 
 def roofline_blocks(s, prof, nb):
@@ -391,12 +412,13 @@ def roofline_blocks(s, prof, nb):
     if name == "render":
         alg = render_bytes(p) * nb
         achieved = alg / (kms / 1000.0) / 1e9
+        traffic, tsrc = render_traffic()
         roof = {"bound": "hbm", "kernel": f"k_render (full-resolution render + keep_static + rgba8 out), {nb} frame(s) "
                                           "per launch",
                 "achieved": achieved, "peak": hbm or 6650.0, "unit": "GB/s",
-                "frac": achieved / (hbm or 6650.0), "traffic": RENDER_TRAFFIC * nb,
-                "algorithmic_bytes": alg, "launch_ms": kms, "frames_per_launch": nb,
-                "peak_source": "measured" if hbm else "fallback"}
+                "frac": achieved / (hbm or 6650.0), "traffic": traffic * nb if traffic else None,
+                "traffic_source": tsrc, "algorithmic_bytes": alg, "design_bytes": render_design_bytes(p) * nb,
+                "launch_ms": kms, "frames_per_launch": nb, "peak_source": "measured" if hbm else "fallback"}
     else:
         roof = {"bound": "unknown", "kernel": name, "launch_ms": kms, "achieved": None, "peak": None, "unit": None,
                 "frac": None, "traffic": None}

@@ -1,16 +1,18 @@
 """FlyHigh B200: the FlyHighFG Core (Session.pair / Session.mid) on an NVIDIA B200, through the drop-in C ABI.
 
-The classes mirror the reference's Python binding over its C ABI (bindings/python/flyhigh.py: Engine, Model, Session,
-FlyHighError), so a host written against it runs unchanged:
+The classes keep the names, arguments and errors of the reference's ctypes binding (Engine, Model, Session,
+FlyHighError), so code written against that binding keeps working. A typical 2x interpolation loop over a list of
+rgba8 frames (numpy arrays of shape (h, w, 4) or bytes) looks like this:
 
-    import flyhigh_engine_b200 as flyhigh
-    engine = flyhigh.Engine()
-    model = flyhigh.Model("models")                    # graph.json, flyhighfg.json, flyhighfg.bin
-    s = flyhigh.Session(engine, model, 1920, 1080)     # options as keyword arguments
-    a, b, out = s.add_input(), s.add_input(), s.add_output()
-    s.write(a, frame0); s.write(b, frame1)
-    s.pair(a, b); s.mid(0.5, out)
-    rgba = s.read(out)                                 # bytes, width * height * 4
+    import flyhigh_engine_b200 as fh
+    sess = fh.Session(fh.Engine(), fh.Model(model_dir), width, height)
+    slots, dst = (sess.add_input(), sess.add_input()), sess.add_output()
+    sess.write(slots[0], frames[0])
+    for i in range(1, len(frames)):
+        sess.write(slots[i % 2], frames[i])
+        sess.pair(slots[(i - 1) % 2], slots[i % 2])   # the motion between the two frames
+        sess.mid(0.5, dst)                            # the frame halfway between them
+        between = sess.read(dst)                      # width * height * 4 bytes
 
 The library is libflyhigh.so next to this file (built by `flyhigh_engine_b200.build.build()`), or FLYHIGH_LIB.
 There is no fallback: without the CUDA library every call raises.
@@ -28,7 +30,7 @@ __all__ = ["FlyHighError", "Engine", "Model", "Session", "library_path"]
 
 
 class FlyHighError(RuntimeError):
-    """A failed engine call, with the message of fh_last_error()."""
+    """Raised when a library call reports failure (NULL or a negative status); the text is fh_last_error()'s."""
 
 
 class EngineOptions(Structure):  # flyhigh.h FhEngineOptions, field for field
@@ -89,6 +91,7 @@ EXPORTS = [
     ("fh_session_slot_device_ptr", c_int, [c_void_p, c_uint32, c_int, POINTER(c_void_p)]),
     ("fh_session_write_rgba_device", c_int, [c_void_p, c_uint32, c_void_p, c_size_t]),
     ("fh_session_debug_tensor", c_long, [c_void_p, c_char_p, POINTER(c_float), c_size_t, POINTER(c_int)]),
+    ("fh_session_debug_tensor_at", c_long, [c_void_p, c_char_p, c_int, POINTER(c_float), c_size_t, POINTER(c_int)]),
     ("fh_model_fingerprint", c_long, [c_void_p]),
     ("fh_session_plan_params", c_int, [c_void_p, POINTER(SessionOptions), POINTER(c_int), POINTER(c_float)]),
     ("fh_session_advance_static", c_int, [c_void_p, c_uint32, c_uint32]),
@@ -296,10 +299,13 @@ def session_options(width: int, height: int, internal=None, k: int = 1, repair: 
 
 
 class Session:
-    """The plans of a model for one frame size: Session(engine, model, width, height, internal="auto"|"frame"|(w, h),
-    k=1, repair=1, render="model"|"bilinear"|"bicubic", static_protection=None|True|False|{"frames", "tolerance"},
-    keep_maps=False, protection_mask=False, batch=None). batch = n > 1 queues pair / mid calls and runs n chained
-    intervals per launch (fh_session_create_batched); None leaves it to FH_BATCH."""
+    """A model planned for one frame size, with its input and output slots.
+
+    Keyword options map onto FhSessionOptions: internal ("auto", "frame" or a (w, h) network size), k (fine-loop
+    passes), repair (0-2), render ("model", "bilinear", "bicubic"), static_protection (None for the default, a bool,
+    or a dict with "frames" / "tolerance"), fast_render, linear_t, keep_maps, protection_mask and tune. batch = n > 1
+    builds a batched session (fh_session_create_batched): pair / mid calls queue up and n chained intervals run per
+    launch; None leaves the choice to the FH_BATCH environment variable."""
 
     def __init__(self, engine: Engine, model: Model, width: int, height: int, batch=None, **options):
         self._o = session_options(width, height, **options)
@@ -409,15 +415,17 @@ class Session:
         _check(lib().fh_session_launch_counts(self._h, byref(a), byref(b), byref(c)))
         return {"pair": a.value, "mid": b.value, "frame": c.value}
 
-    def tensor(self, name: str):
-        """A tensor of the last pair / mid as a float32 numpy array [c][h][w] (the reference's planar order)."""
+    def tensor(self, name: str, interval: int = -1):
+        """A tensor of the last pair / mid as a float32 numpy array [c][h][w] (the reference's planar order); with
+        interval >= 0, that interval of the last batch (0 = its oldest) of a batched session."""
         import numpy as np
         dims = (c_int * 3)()
-        n = lib().fh_session_debug_tensor(self._h, name.encode(), None, 0, dims)
+        n = lib().fh_session_debug_tensor_at(self._h, name.encode(), interval, None, 0, dims)
         if n < 0:
             raise _error()
         out = np.zeros(n, np.float32)
-        _check(lib().fh_session_debug_tensor(self._h, name.encode(), out.ctypes.data_as(POINTER(c_float)), n, dims))
+        _check(lib().fh_session_debug_tensor_at(self._h, name.encode(), interval,
+                                                out.ctypes.data_as(POINTER(c_float)), n, dims))
         return out.reshape(dims[0], dims[1], dims[2])
 
     def close(self):

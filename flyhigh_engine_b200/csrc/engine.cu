@@ -457,6 +457,7 @@ struct FhSession {
     // on set 0), the batch's set for the newest interval of a batch
     int pair_set = 0;
     int last_batch = -1;  // the set of the last batch (-1: none yet; the first batch takes set 0)
+    int last_m = 0;       // the intervals of the last batch
     cudaStream_t fst = nullptr, sst = nullptr, rst = nullptr, nst[MAX_SETS] = {};
     cudaEvent_t st_ev = nullptr, join_evs[3 + MAX_SETS] = {};
     FrameSet& arena() { return rsets[rpar].arena; }
@@ -1153,6 +1154,7 @@ struct FhSession {
     void pair_now(FrameSet& A, FrameSet& B) {
         use_set(0);
         pair_set = 0;
+        last_m = 0;
         wait_upload(A);
         wait_upload(B);
         ensure_features(A);
@@ -1394,6 +1396,7 @@ struct FhSession {
         CK(cudaEventRecord(R.render_done, r_s));
         R.render_pending = overlap_on;
         last_batch = p;
+        last_m = m;
         pair_set = p;
         // the newest interval is entry 0 of every per-interval buffer: a further mid of it runs there
         FView a0 = arena_view(1), b0 = arena_view(0);
@@ -1498,6 +1501,7 @@ struct FhSession {
         A.feat_gen = A.gen;
         B.feat_gen = B.gen;
         pair_set = 0;
+        last_m = 0;
         pair = PairSrc{view_of(A), view_of(B), &A, &B};
         have_pair = true;
         maps_done = true;
@@ -2168,6 +2172,10 @@ int fh_session_launch_counts(const FhSession* s, int* pk, int* mk, int* fk) {
 }
 
 long fh_session_debug_tensor(const FhSession* cs, const char* name, float* out, size_t cap, int* dims) {
+    return fh_session_debug_tensor_at(cs, name, -1, out, cap, dims);
+}
+
+long fh_session_debug_tensor_at(const FhSession* cs, const char* name, int interval, float* out, size_t cap, int* dims) {
     return guard(-1L, [&]() -> long {
         FhSession* s = const_cast<FhSession*>(cs);
         if (!s || !name || !dims) fail("null argument");
@@ -2175,11 +2183,21 @@ long fh_session_debug_tensor(const FhSession* cs, const char* name, float* out, 
         if (!s->have_pair) fail("no pair has run");
         s->use_set(s->pair_set);
         std::string n(name);
-        const FView& A = s->pair.a;
-        const FView& B = s->pair.b;
+        // interval i of the last batch (time order) sits at entry m - 1 - i of every per-interval buffer, its frames
+        // at arena entries m - i (A) and m - 1 - i (B); -1: the current pair (entry 0)
+        int entry = 0;
+        FView A = s->pair.a, B = s->pair.b;
+        if (interval >= 0) {
+            if (s->last_m < 1) fail("no batch ran last");
+            if (interval >= s->last_m) fail("interval %d: the last batch held %d", interval, s->last_m);
+            entry = s->last_m - 1 - interval;
+            A = s->arena_view(entry + 1);
+            B = s->arena_view(entry);
+        }
         // (pointer, pixel pitch, channel offset, channels, height, width, kind 0 = f16 / 1 = int16 / 2 = rgba8 planes)
         const void* p = nullptr;
         int cs_ = 0, c0 = 0, c = 0, hh = 0, ww = 0, kind = 0;
+        bool per_interval = true;  // a per-interval buffer (entry stride hh * ww * cs_), not a frame view
         auto set = [&](const void* pp, int pcs, int pc0, int pc, int ph, int pw) {
             p = pp;
             cs_ = pcs;
@@ -2188,6 +2206,10 @@ long fh_session_debug_tensor(const FhSession* cs, const char* name, float* out, 
             hh = ph;
             ww = pw;
         };
+        static const char* frame_names[] = {"A", "B", "aq", "bq", "i8a", "i8b", "i16a", "i16b", "f8a", "f8b", "f16a",
+                                            "f16b"};
+        for (const char* f : frame_names)
+            if (n == f) per_interval = false;
         if (n == "A") set(A.A, 4, 0, 3, s->NH, s->NW);
         else if (n == "B") set(B.A, 4, 0, 3, s->NH, s->NW);
         else if (n == "aq") set(A.aq, 4, 0, 3, s->qh, s->qw);
@@ -2231,6 +2253,7 @@ long fh_session_debug_tensor(const FhSession* cs, const char* name, float* out, 
             set(s->age, 1, 0, 1, s->hp, s->wp);
             kind = 1;
         } else fail("unknown tensor %s", name);
+        if (per_interval) p = static_cast<const uint16_t*>(p) + (size_t)entry * hh * ww * cs_;
         dims[0] = c;
         dims[1] = hh;
         dims[2] = ww;

@@ -51,6 +51,13 @@ int fh_session_write_rgba_device(const FhSession* session, uint32_t slot, const 
  * an unknown name or an error, -2 when cap is too small. out may be NULL to query the size. */
 long fh_session_debug_tensor(const FhSession* session, const char* name, float* out, size_t cap, int* dims);
 
+/* The same for one interval of the last batch of a batched session: interval i (0 = the oldest of that batch, in the
+ * order its pairs were called) reads that interval's own entry of every per-interval buffer and its two frames' arena
+ * entries, so each interval a batch computed can be compared layer by layer. interval -1 is the current pair, as
+ * fh_session_debug_tensor. -1 when no batch ran last (a pair run on its own since) or i is beyond its size. */
+long fh_session_debug_tensor_at(const FhSession* session, const char* name, int interval, float* out, size_t cap,
+                                int* dims);
+
 /* The structural fingerprint of a model's graph.json (FNV-1a of its canonical op list). Sessions are built only for
  * the FlyHighFG v1 graph; this lets a host check a model directory before creating one. -1 on a null model. */
 long fh_model_fingerprint(const FhModel* model);

@@ -498,10 +498,20 @@ struct RenderArgs {
     float min_age;
 };
 
-// render.wgsl:82-161 (+ the static variant of gpu/pipeline.rs:10-34): full-resolution render from the Q-res maps
-static T k_render(const T& A, const T& B, const T& ftq, const T& vtq, const T& rt, const RenderArgs& ra) {
+// Per-pixel decision record of k_render (test diagnostics: which discrete choices a pixel took, and the continuous
+// values around them), RENDER_DIAG floats per probed pixel:
+//   0-3 the bicubic source positions gxa, gya, gxb, gyb (full-resolution px); 4-5 the static rules' hits sa, sb (0/1);
+//   6 the still weight (after its age gate); 7 the still ramp's input ef - es; 8 es; 9-12 bwa, bwb, rk, raw;
+//   13-14 the value range (max - min) of the 4 x 4 taps of A resp. B over the three channels; 15-17 ca; 18-20 cb;
+//   21-23 cr; 24-26 own; 27 the age at the pixel (0 without static protection)
+enum { RENDER_DIAG = 28 };
+
+// render.wgsl:82-161 (+ the static variant of gpu/pipeline.rs:10-34): full-resolution render from the Q-res maps.
+// With probe (x, y pairs) only those pixels are evaluated, each writing its RENDER_DIAG record into diag.
+static T k_render(const T& A, const T& B, const T& ftq, const T& vtq, const T& rt, const RenderArgs& ra,
+                  const std::vector<int>* probe = nullptr, float* diag = nullptr) {
     int H = A.h, W = A.w, hq = ftq.h, wq = ftq.w;
-    T out = alloc(3, H, W);
+    T out = alloc(3, probe ? 1 : H, probe ? 1 : W);
     const f16* a = A.buf->d.data();
     const f16* b = B.buf->d.data();
     const float STILL_RUN = 3.0f;
@@ -548,10 +558,21 @@ static T k_render(const T& A, const T& B, const T& ftq, const T& vtq, const T& r
                 if (L(ra.age->buf->d[(size_t)clampy(cy + dy) * W + clampx(cx + dx)]) >= ra.min_age) return true;
         return false;
     };
+    auto range16 = [&](const f16* src, float gx, float gy) {
+        int px = (int)floorf(gx), py = (int)floorf(gy);
+        float lo = 1e30f, hi = -1e30f;
+        for (int c = 0; c < 3; c++)
+            for (int j = 0; j < 4; j++)
+                for (int i = 0; i < 4; i++) {
+                    float v = L(src[((size_t)c * H + clampy(py - 1 + j)) * W + clampx(px - 1 + i)]);
+                    lo = std::min(lo, v);
+                    hi = std::max(hi, v);
+                }
+        return hi - lo;
+    };
     float sh = (float)hq / (float)H, sw = (float)wq / (float)W;
-#pragma omp parallel for
-    for (int y = 0; y < H; y++)
-        for (int x = 0; x < W; x++) {
+    auto pix = [&](int x, int y, float* dg) {
+        {
             float iy = ((float)y + 0.5f) * sh - 0.5f, ix = ((float)x + 0.5f) * sw - 0.5f;
             int qy0 = (int)floorf(iy), qx0 = (int)floorf(ix);
             float qfy = iy - (float)qy0, qfx = ix - (float)qx0;
@@ -596,6 +617,10 @@ static T k_render(const T& A, const T& B, const T& ftq, const T& vtq, const T& r
                 }
                 float ef = fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
                 stillw = std::min(std::max((ef - es) / 0.04f, 0.0f), 1.0f) * (es < 0.03f ? 1.0f : 0.0f);
+                if (dg) {
+                    dg[7] = ef - es;
+                    dg[8] = es;
+                }
             }
             if (ra.flags & 1u) {
                 float d = fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
@@ -606,8 +631,21 @@ static T k_render(const T& A, const T& B, const T& ftq, const T& vtq, const T& r
                 rk = 1.0f - k;
             }
             float raw = 0.0f;
+            if (dg) {
+                dg[0] = gxa;
+                dg[1] = gya;
+                dg[2] = gxb;
+                dg[3] = gyb;
+                dg[4] = dg[5] = 0.0f;
+                dg[27] = ra.age ? L(ra.age->buf->d[(size_t)y * W + x]) : 0.0f;
+                if (!(ra.flags & 2u)) dg[7] = dg[8] = 0.0f;
+            }
             if (ra.age) {
                 bool sa = on_static(gxa, gya), sb = on_static(gxb, gyb);
+                if (dg) {
+                    dg[4] = sa ? 1.0f : 0.0f;
+                    dg[5] = sb ? 1.0f : 0.0f;
+                }
                 stillw = stillw * (fabsf(L(ra.age->buf->d[(size_t)y * W + x])) >= STILL_RUN ? 1.0f : 0.0f);
                 if (sa && sb) {
                     rk = 0.0f;
@@ -622,6 +660,22 @@ static T k_render(const T& A, const T& B, const T& ftq, const T& vtq, const T& r
                     bwb = 0.0f;
                 }
             }
+            if (dg) {
+                dg[6] = stillw;
+                dg[9] = bwa;
+                dg[10] = bwb;
+                dg[11] = rk;
+                dg[12] = raw;
+                dg[13] = range16(a, gxa, gya);
+                dg[14] = range16(b, gxb, gyb);
+                for (int c = 0; c < 3; c++) {
+                    dg[15 + c] = ca[c];
+                    dg[18 + c] = cb[c];
+                    dg[21 + c] = cr[c];
+                    dg[24 + c] = own[c];
+                }
+                return;
+            }
             for (int c = 0; c < 3; c++) {
                 float mixv = ca[c] * bwa + cb[c] * bwb + cr[c] * rk;
                 float o = std::min(std::max(mixv * (1.0f - stillw) + own[c] * stillw, 0.0f), 1.0f);
@@ -633,6 +687,16 @@ static T k_render(const T& A, const T& B, const T& ftq, const T& vtq, const T& r
                 out.buf->d[i] = S(o);
             }
         }
+    };
+    if (probe) {
+        const long np = (long)probe->size() / 2;
+#pragma omp parallel for
+        for (long i = 0; i < np; i++) pix((*probe)[2 * i], (*probe)[2 * i + 1], diag + i * RENDER_DIAG);
+        return out;
+    }
+#pragma omp parallel for
+    for (int y = 0; y < H; y++)
+        for (int x = 0; x < W; x++) pix(x, y, nullptr);
     return out;
 }
 
@@ -1681,6 +1745,40 @@ int or_render_planes(const uint8_t* fa, const uint8_t* fb, int w, int h, const f
         return -1;
     }
 }
+
+// The render's decision record (RENDER_DIAG floats per pixel, k_render) at the n pixels xy[2 i], xy[2 i + 1], on the
+// same caller planes and parameters as or_render_planes. Test diagnostics: a parity test uses it to say which
+// discrete choice (a static rule, the still ramp) separates two renders of slightly different network outputs.
+int or_render_diag(const uint8_t* fa, const uint8_t* fb, int w, int h, const float* up7, const float* rt, int hq,
+                   int wq, const float* age, const float* fv, const int* iv, int n, const int* xy, float* diag) {
+    try {
+        const int hp = (h + 31) / 32 * 32, wp = (w + 31) / 32 * 32;
+        T A = alloc(3, hp, wp), B = alloc(3, hp, wp);
+        k_tex_in(fa, w, h, A);
+        k_tex_in(fb, w, h, B);
+        T up = alloc(7, hq, wq), r = alloc(3, hq, wq);
+        for (size_t i = 0; i < up.n(); i++) up.buf->d[i] = S(up7[i]);
+        for (size_t i = 0; i < r.n(); i++) r.buf->d[i] = S(rt[i]);
+        T ftq = up.view(0, 4), vtq = up.view(4, 7);
+        T ag;
+        if (age) {
+            ag = alloc(1, hp, wp);
+            for (size_t i = 0; i < ag.n(); i++) ag.buf->d[i] = S(age[i]);
+        }
+        for (int i = 0; i < n; i++)
+            if (xy[2 * i] < 0 || xy[2 * i] >= w || xy[2 * i + 1] < 0 || xy[2 * i + 1] >= h)
+                throw std::runtime_error("probe pixel outside the frame");
+        RenderArgs ra{fv[0], fv[1], iv[0] != 0, (uint32_t)iv[1], age ? &ag : nullptr, fv[2]};
+        std::vector<int> probe(xy, xy + 2 * (size_t)n);
+        k_render(A, B, ftq, vtq, r, ra, &probe, diag);
+        return 0;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
+int or_render_diag_size() { return RENDER_DIAG; }
 
 // interp.wgsl on a plain [c][h][w] f16 tensor (x scale applied to the result); out [c][oh][ow] f16 bits
 // The fast render alone (render_tex.wgsl) on caller maps: frames a, b (w x h rgba8), up7 [7][hq][wq] and R_t [3][hq][wq]

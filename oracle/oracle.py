@@ -52,6 +52,8 @@ def lib():
                                        POINTER(c_float), c_int, c_int, POINTER(c_float), POINTER(c_float),
                                        POINTER(c_int), POINTER(c_uint8)]
         L.or_render_tex_planes.argtypes = L.or_render_planes.argtypes
+        L.or_render_diag.argtypes = L.or_render_planes.argtypes[:-1] + [c_int, POINTER(c_int), POINTER(c_float)]
+        L.or_render_diag_size.restype = c_int
         L.or_tex_down.argtypes = [POINTER(c_uint8), c_int, c_int, c_int, c_int, POINTER(c_uint16)]
         L.or_interp.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, c_int, c_int, c_int, c_float, POINTER(c_uint16)]
         L.or_warp.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, POINTER(c_uint16), c_float, POINTER(c_uint16)]
@@ -182,6 +184,36 @@ def render_planes(fa, fb, w, h, up7, rt, age, fsx, fsy, min_age, static_thr, cub
     if rc != 0:
         raise RuntimeError(lib().or_error().decode())
     return out
+
+
+DIAG_FIELDS = ["gxa", "gya", "gxb", "gyb", "sa", "sb", "stillw", "ramp", "es", "bwa", "bwb", "rk", "raw", "range_a",
+               "range_b", "ca0", "ca1", "ca2", "cb0", "cb1", "cb2", "cr0", "cr1", "cr2", "own0", "own1", "own2", "age"]
+
+
+def render_diag(fa, fb, w, h, up7, rt, age, fsx, fsy, min_age, xs, ys, cubic=True, flags=2):
+    """The render's decision record at pixels (xs[i], ys[i]) on given network outputs, as render_planes evaluates them:
+    a dict of DIAG_FIELDS -> float32 arrays (source positions, static-rule hits, still weight and its ramp input, blend
+    weights, tap value ranges, the blended terms, the age)."""
+    fa = np.ascontiguousarray(fa, np.uint8)
+    fb = np.ascontiguousarray(fb, np.uint8)
+    up7 = np.ascontiguousarray(up7, np.float32)
+    rt = np.ascontiguousarray(rt, np.float32)
+    hq, wq = up7.shape[1], up7.shape[2]
+    ag = None if age is None else np.ascontiguousarray(age, np.float32)
+    fv = np.array([fsx, fsy, min_age, 0.0], np.float32)
+    iv = np.array([int(cubic), int(flags)], np.int32)
+    xy = np.ascontiguousarray(np.stack([np.asarray(xs, np.int32), np.asarray(ys, np.int32)], 1).reshape(-1))
+    n = xy.size // 2
+    k = lib().or_render_diag_size()
+    assert k == len(DIAG_FIELDS)
+    out = np.zeros(max(n, 1) * k, np.float32)
+    f = lambda a: a.ctypes.data_as(POINTER(c_float))
+    rc = lib().or_render_diag(_u8(fa), _u8(fb), w, h, f(up7), f(rt), hq, wq, f(ag) if ag is not None else None,
+                              f(fv), iv.ctypes.data_as(POINTER(c_int)), n, xy.ctypes.data_as(POINTER(c_int)), f(out))
+    if rc != 0:
+        raise RuntimeError(lib().or_error().decode())
+    out = out[:n * k].reshape(n, k)
+    return {name: out[:, i] for i, name in enumerate(DIAG_FIELDS)}
 
 
 def interp(x, oh: int, ow: int, aa: bool, scale: float = 1.0):

@@ -4,8 +4,8 @@ The reference pins its planner with text dumps of every dispatch (crates/flyhigh
 written by tests/golden_plans.rs: pipeline, workgroups, binding sizes, uniform words). This script keeps, for the
 configurations the exact-render Session builds (fast render is not part of this build), the words that fix sizes and
 parameters: every conv's (cin, h, w, hout, wout, stride, cout), every interp, sad, warp, the GMHS windows and
-thresholds, and the render's scales, sampler and protecting age. Run it where the reference is present:
-    python tests/golden/make_plan_params.py /root/reference
+thresholds, and the render's scales, sampler and protecting age. Run it with a checkout of the reference repository:
+    python tests/golden/make_plan_params.py <reference checkout>    (or FLYHIGH_REFERENCE=<checkout>)
 """
 import json
 import os
@@ -85,7 +85,9 @@ def extract(path):
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FLYHIGH_REFERENCE", "")
+    if not ref:
+        sys.exit("usage: make_plan_params.py <reference checkout>")
     gdir = os.path.join(ref, "crates", "flyhigh-engine", "tests", "golden")
     out = [extract(os.path.join(gdir, f"{c}.tc-f16.txt")) for c in CONFIGS]
     dst = os.path.join(os.path.dirname(os.path.abspath(__file__)), "plan_params.json")
