@@ -13,7 +13,8 @@
 // library holds it until the process exits. Larger sizes are rejected with cudaErrorInvalidValue.
 //
 // The first call on a device looks up the array's device address with cudaGetSymbolAddress (on that device, which must
-// be current); make that first call before any stream capture. All calls share the one array and it keeps the last
+// be current). Under CUDA's lazy module loading that first call may also load the library's device code, the array
+// included, so a host should make it once per device at start-up, before frames flow and before any stream capture. All calls share the one array and it keeps the last
 // call's contents. Nothing in it needs to start at zero: each kernel of the stage writes every scratch element before
 // any kernel reads it. Calls whose executions overlap on the GPU (two streams, or two host threads) race on the array;
 // order them on one stream.

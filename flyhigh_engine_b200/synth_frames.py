@@ -6,7 +6,9 @@ in for them:
   - pair_c0(): config 0, frame b = frame a under an integer global pan in [-12, 12]^2 plus 3 rectangles of 20..80 px
     that move independently by up to 24 px;
   - sequence_c2(): config 2, a moving sequence whose pan velocity random-walks by +-2 px per frame, with 5 moving
-    rectangles and a static 300 x 60 high-contrast HUD overlay at the bottom-left (noise-free, like a rendered HUD).
+    rectangles and a static 300 x 60 high-contrast HUD overlay at the bottom-left (noise-free, like a rendered HUD);
+  - sequence_c3(): config 3, a camera pan of up to +-40 px per frame over a texture and a fence (a 32-px-period grid of
+    bars) covering 30 % of the frame, the periodic structure the repair stage exists for.
 Every frame is (h, w, 4) uint8 with alpha 255.
 """
 from __future__ import annotations
@@ -99,6 +101,31 @@ def sequence_c2(n: int = 120, w: int = 1920, h: int = 1080, seed: int = 0, hud: 
         if hud:  # an overlay: composited after the sensor noise, identical in every frame
             f[h - 60 - 20:h - 20, 20:320, :3] = hud_img.astype(np.uint8)
         frames.append(f)
+    return frames
+
+
+def sequence_c3(n: int = 60, w: int = 3840, h: int = 2160, seed: int = 0):
+    """Config 3: n frames of a pan whose velocity is drawn once per frame within +-40 px (x) and +-12 px (y); a region
+    of 30 % of the frame shows a fence (dark 6-px bars every 32 px in both directions over a lit backdrop) that moves
+    with the pan, as a camera panning past it would see it."""
+    rng = np.random.default_rng(seed)
+    m = min(40 * n + 64, 2048)
+    base = texture(w, h, rng, margin=m)
+    # the fence: a band of the frame's full width and 30 % of its height, centred vertically
+    fh = int(round(0.3 * h))
+    f0 = (h - fh) // 2
+    yy = np.arange(h + 2 * m)[:, None]
+    xx = np.arange(w + 2 * m)[None, :]
+    bars = ((yy % 32) < 6) | ((xx % 32) < 6)
+    fence = np.where(bars[..., None], 24.0, 200.0 + 0.2 * (base - 128.0)).astype(np.float32)
+    px, py = 0, 0
+    frames = []
+    for _ in range(n):
+        px = int(np.clip(px + rng.integers(-40, 41), -m, m))
+        py = int(np.clip(py + rng.integers(-12, 13), -m, m))
+        img = base[m + py:m + py + h, m + px:m + px + w].copy()
+        img[f0:f0 + fh] = fence[m + py + f0:m + py + f0 + fh, m + px:m + px + w]
+        frames.append(_finish(img, rng))
     return frames
 
 

@@ -108,9 +108,10 @@ size_t fhk_gmhs_scratch_floats(int h, int w);
  * that reserve all GPU memory up front, plugins whose memory belongs to the host's allocator): the scratch lives in a
  * file-scope device array of fhk_gmhs_noalloc_max_floats() floats (4.87 MB, held by every GPU that loads the library),
  * so the call allocates nothing. p->scratch must be NULL and p->n 1; sizes needing more than the array are rejected
- * (cudaErrorInvalidValue). The first call on a device looks the array up on the current device: make it before any
- * stream capture. All calls share the array (it keeps the last call's contents; nothing in it must start at zero);
- * calls that overlap on the GPU race. */
+ * (cudaErrorInvalidValue). The first call on a device looks the array up on the current device, and under CUDA's
+ * lazy module loading it may also load the library's device code (the array included) then: make one warm-up call on
+ * each device at start-up, before frames flow and before any stream capture. All calls share the array (it keeps
+ * the last call's contents; nothing in it must start at zero); calls that overlap on the GPU race. */
 int fhk_gmhs_noalloc(const FhGmhsParams* p, void* stream);
 size_t fhk_gmhs_noalloc_max_floats(void);
 

@@ -502,7 +502,8 @@ struct RenderArgs {
 // values around them), RENDER_DIAG floats per probed pixel:
 //   0-3 the bicubic source positions gxa, gya, gxb, gyb (full-resolution px); 4-5 the static rules' hits sa, sb (0/1);
 //   6 the still weight (after its age gate); 7 the still ramp's input ef - es; 8 es; 9-12 bwa, bwb, rk, raw;
-//   13-14 the value range (max - min) of the 4 x 4 taps of A resp. B over the three channels; 15-17 ca; 18-20 cb;
+//   13-14 the value range (max - min) over the three channels of A's resp. B's 4 x 4 taps widened by one row and
+//   column (so that it covers the taps of any source position less than a pixel further right or down); 15-17 ca; 18-20 cb;
 //   21-23 cr; 24-26 own; 27 the age at the pixel (0 without static protection)
 enum { RENDER_DIAG = 28 };
 
@@ -558,12 +559,12 @@ static T k_render(const T& A, const T& B, const T& ftq, const T& vtq, const T& r
                 if (L(ra.age->buf->d[(size_t)clampy(cy + dy) * W + clampx(cx + dx)]) >= ra.min_age) return true;
         return false;
     };
-    auto range16 = [&](const f16* src, float gx, float gy) {
+    auto range16 = [&](const f16* src, float gx, float gy) {  // the 4 x 4 taps and one more row and column
         int px = (int)floorf(gx), py = (int)floorf(gy);
         float lo = 1e30f, hi = -1e30f;
         for (int c = 0; c < 3; c++)
-            for (int j = 0; j < 4; j++)
-                for (int i = 0; i < 4; i++) {
+            for (int j = 0; j < 5; j++)
+                for (int i = 0; i < 5; i++) {
                     float v = L(src[((size_t)c * H + clampy(py - 1 + j)) * W + clampx(px - 1 + i)]);
                     lo = std::min(lo, v);
                     hi = std::max(hi, v);
@@ -1038,7 +1039,11 @@ static GmParams gm_params(int h, int w, int full_w, int level) {
     return g;
 }
 
-static void gm_run(const T& A, const T& B, T& flow, int full_w, int level, std::vector<float>* maps_out) {
+// sel_out (test diagnostics, optional): per E8 pixel (i, j) four floats at [4 * (i * w8 + j)]: the select decision
+// (1 = the affine flow replaced the network's), and the margins of its three conditions, ca + eps < cm (cm - ca - eps),
+// dv > dmin (dv - dmin) and sd > tex (sd - tex): the decision is 1 exactly when all three are positive.
+static void gm_run(const T& A, const T& B, T& flow, int full_w, int level, std::vector<float>* maps_out,
+                   std::vector<float>* sel_out = nullptr) {
     int h8 = flow.h, w8 = flow.w, h = A.h, w = A.w;
     GmParams g = gm_params(h, w, full_w, level);
     const int nwg = 32;
@@ -1183,6 +1188,13 @@ static void gm_run(const T& A, const T& B, T& flow, int full_w, int level, std::
             float cm = maps[idx], ca = maps[n + idx], dv = maps[2 * (size_t)n + idx], lm = maps[3 * (size_t)n + idx],
                   l2 = maps[4 * (size_t)n + idx];
             float sd = sqrtf(std::max(l2 - lm * lm, 0.0f));
+            if (sel_out) {
+                float* r = sel_out->data() + 4 * ((size_t)i * w8 + j);
+                r[0] = (ca + eps < cm && dv > g.dmin && sd > tex) ? 1.0f : 0.0f;
+                r[1] = cm - (ca + eps);
+                r[2] = dv - g.dmin;
+                r[3] = sd - tex;
+            }
             if (ca + eps < cm && dv > g.dmin && sd > tex) {
                 float xn = -1.0f + 2.0f * (float)j / (float)std::max(w8 - 1, 1);
                 float yn = -1.0f + 2.0f * (float)i / (float)std::max(h8 - 1, 1);
@@ -1779,6 +1791,27 @@ int or_render_diag(const uint8_t* fa, const uint8_t* fb, int w, int h, const flo
 }
 
 int or_render_diag_size() { return RENDER_DIAG; }
+
+// The repair stage's select decisions and margins (gm_run's sel_out: 4 floats per E8 pixel) for a given pre-repair
+// flow flow_pre [4][h8][w8] (f32 values of f16) on the session's last pair (its internal-size frames A and B). Test
+// diagnostics: with another implementation's pre-repair flow it tells which cells that implementation's repair
+// selected, and how far each condition was from its threshold. 0, or -1 (no pair, no repair stage, size mismatch).
+int or_gmhs_select(void* sp, const float* flow_pre, int h8, int w8, float* sel) {
+    try {
+        Session* s = (Session*)sp;
+        if (!s->have_pair || s->o.repair <= 0 || !s->flow_pre.buf) throw std::runtime_error("no repair stage has run");
+        if (s->flow_pre.h != h8 || s->flow_pre.w != w8) throw std::runtime_error("flow size mismatch");
+        T f = alloc(4, h8, w8);
+        for (size_t i = 0; i < f.n(); i++) f.buf->d[i] = S(flow_pre[i]);
+        std::vector<float> maps, rec((size_t)4 * h8 * w8, 0.0f);
+        gm_run(s->env.at("A"), s->env.at("B"), f, s->wp, s->o.repair, &maps, &rec);
+        std::copy(rec.begin(), rec.end(), sel);
+        return 0;
+    } catch (std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
 
 // interp.wgsl on a plain [c][h][w] f16 tensor (x scale applied to the result); out [c][oh][ow] f16 bits
 // The fast render alone (render_tex.wgsl) on caller maps: frames a, b (w x h rgba8), up7 [7][hq][wq] and R_t [3][hq][wq]

@@ -54,6 +54,7 @@ def lib():
         L.or_render_tex_planes.argtypes = L.or_render_planes.argtypes
         L.or_render_diag.argtypes = L.or_render_planes.argtypes[:-1] + [c_int, POINTER(c_int), POINTER(c_float)]
         L.or_render_diag_size.restype = c_int
+        L.or_gmhs_select.argtypes = [c_void_p, POINTER(c_float), c_int, c_int, POINTER(c_float)]
         L.or_tex_down.argtypes = [POINTER(c_uint8), c_int, c_int, c_int, c_int, POINTER(c_uint16)]
         L.or_interp.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, c_int, c_int, c_int, c_float, POINTER(c_uint16)]
         L.or_warp.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, POINTER(c_uint16), c_float, POINTER(c_uint16)]
@@ -130,6 +131,19 @@ class OracleSession:
         out = np.zeros(n, np.float32)
         lib().or_tensor(self.s, stage, name.encode(), out.ctypes.data_as(POINTER(c_float)), n, dims)
         return out.reshape(dims[0], dims[1], dims[2])
+
+    def gmhs_select(self, flow_pre: np.ndarray) -> dict:
+        """The repair stage's decisions on the last pair's frames for a given pre-repair flow [4][h8][w8]: "sel" (1 where
+        the affine flow replaces the network's) and the margins of its three conditions "m_cost" (cm - ca), "m_dv"
+        (dv - dmin), "m_sd" (sd - tex), each [h8][w8]; a cell is selected exactly when all three are positive."""
+        f = np.ascontiguousarray(flow_pre, np.float32)
+        _, h8, w8 = f.shape
+        out = np.zeros(4 * h8 * w8, np.float32)
+        P = lambda a: a.ctypes.data_as(POINTER(c_float))
+        if lib().or_gmhs_select(self.s, P(f), h8, w8, P(out)) != 0:
+            raise RuntimeError(lib().or_error().decode())
+        r = out.reshape(h8, w8, 4)
+        return {"sel": r[..., 0], "m_cost": r[..., 1], "m_dv": r[..., 2], "m_sd": r[..., 3]}
 
     def dims(self) -> dict:
         iv = (c_int * 9)()

@@ -1,0 +1,168 @@
+"""End-to-end parity of the configurations that bench.py times, against the oracle, frame by frame.
+
+- Config 2 as bench.py runs it: a batched session (4 intervals per launch; its stride-1 convs on the tcgen05 kernel)
+  at 1920 x 1080 with the Session defaults (k 1, repair 1, bicubic, static protection and the still test on), over 12
+  consecutive intervals of a seeded config-2 sequence, so that the HUD becomes protected.
+- Config 3: 3840 x 2160 with three phases (0.25, 0.5, 0.75) per interval over a fence pattern, on a session run one
+  interval at a time (the reference's per-call path).
+
+Per interval: every network layer of the first and the last batch within 1e-2 relative L2 (all layers are compared on
+each interval of those batches, through fh_session_debug_tensor_at), the static age plane exactly after every pair,
+flow_tq within 0.05 px L1 (the reference's backend check, crates/flyhigh-cli/src/cli/selftest.rs:132-151), and every
+generated frame through tests/frame_parity.check_frame: PSNR >= 50 dB, the render within 1 level of the oracle's render
+of the GPU's own network outputs, and every pixel beyond 2 levels explained by a threshold or a steep edge of the render
+in the oracle's run (gmhs / static / still / edge) -- none unexplained. The repair stage's decisions of the GPU run come
+from its pre-repair flow, which a second session without the repair stage yields (its flow equals the first session's
+wherever the repair selected nothing, which the test checks).
+
+FH_PARITY_REPORT=<path> writes the per-frame reports as JSON.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from tests.frame_parity import check_frame
+from tests.parity import LAYER_REL_L2, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+PAIR_LAYERS = ["A", "B", "aq", "bq", "i8a", "i8b", "i16a", "i16b", "f8a", "f8b", "f16a", "f16b", "cv", "ch1", "ch2",
+               "ch3r", "hc", "o", "wa", "wb", "ia", "ib", "fcv", "fr1", "fr2", "fr3", "flow", "vis"]
+MID_LAYERS = ["hm", "fh1", "fh2", "dfilm", "ft_vt", "up7", "rx", "rq1", "rq2", "rq3", "R_t"]
+
+
+@pytest.fixture(scope="module")
+def cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def _report(name, rows):
+    path = os.environ.get("FH_PARITY_REPORT")
+    if not path:
+        return
+    data = {}
+    if os.path.exists(path):
+        with open(path) as f:
+            data = json.load(f)
+    data[name] = rows
+    with open(path, "w") as f:
+        json.dump(data, f, indent=1)
+
+
+def _gmhs_records(o, gpu_pre_flow):
+    """The repair stage's decision records of the oracle's own pre-repair flow and of the GPU's, on the oracle's
+    current pair."""
+    return o.gmhs_select(o.tensor("flow_pre")), o.gmhs_select(gpu_pre_flow)
+
+
+def _check_pre_flow(flow_rep, flow_pre, sel):
+    """The no-repair session's flow equals the repair session's flow wherever the repair selected nothing."""
+    keep = sel == 0
+    assert np.array_equal(flow_rep[:, keep], flow_pre[:, keep])
+
+
+def test_batched_1080p_defaults_match_oracle(synth_model_dir, cuda):
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200 import synth_frames
+    from oracle.oracle import OracleModel, OracleSession
+    W, H, B, N = 1920, 1080, 4, 12
+    frames = synth_frames.sequence_c2(N + 1, W, H, seed=7)
+    model = fh.Model(synth_model_dir)
+    pp = model.plan_params(W, H)
+
+    def session(**kw):
+        s = fh.Session(fh.Engine(), model, W, H, batch=B, **kw)
+        ins = [s.add_input(), s.add_input()]
+        outs = [s.add_output() for _ in range(N + 1)]
+        s.write(ins[0], frames[0])
+        return s, ins, outs
+
+    s, ins, outs = session()
+    s0, ins0, outs0 = session(repair=0)  # the same network without the repair stage: the GPU's pre-repair flow
+    o = OracleSession(OracleModel(synth_model_dir), W, H)
+    rows, protected = [], 0
+    for b0 in range(1, N + 1, B):
+        idx = list(range(b0, b0 + B))
+        for ss, ii, oo in ((s, ins, outs), (s0, ins0, outs0)):
+            for i in idx:
+                ss.write(ii[i % 2], frames[i])
+                ss.pair(ii[(i - 1) % 2], ii[i % 2])
+                ss.mid(0.5, oo[i])
+        gots = {i: np.frombuffer(s.read(outs[i]), np.uint8).copy() for i in idx}  # runs the full batch
+        s0.read(outs0[idx[-1]])
+        for k, i in enumerate(idx):
+            o.pair(frames[i - 1], frames[i])
+            ref = o.mid(0.5)
+            if b0 == 1 or b0 + B > N:
+                worst = {n: rel_l2(s.tensor(n, k), o.tensor(n, 0)) for n in PAIR_LAYERS}
+                worst.update({n: rel_l2(s.tensor(n, k), o.tensor(n, 1)) for n in MID_LAYERS})
+                bad = {n: v for n, v in worst.items() if v > LAYER_REL_L2}
+                assert not bad, (i, bad)
+            age = s.tensor("age", k)
+            assert np.array_equal(age, o.tensor("age")), f"age differs after pair {i}"
+            protected = int((age >= 8).sum())
+            up7g, rtg = s.tensor("up7", k), s.tensor("R_t", k)
+            up7o, rto = o.tensor("up7", 1), o.tensor("R_t", 1)
+            flow_l1 = float(np.abs(up7g[:4] - up7o[:4]).mean())
+            assert flow_l1 <= 0.05, (i, flow_l1)
+            pre = s0.tensor("flow", k)
+            gm = _gmhs_records(o, pre)
+            _check_pre_flow(s.tensor("flow", k), pre, gm[1]["sel"])
+            rep = check_frame(gots[i], ref, frames[i - 1], frames[i], W, H, pp, (up7g, rtg), (up7o, rto), age, gm)
+            rep.update(i=i, flow_l1=flow_l1, protected=protected)
+            rows.append(rep)
+            _report("batched_1080p", rows)
+            assert rep["ok"], rep
+    assert protected > 2000, "the HUD should be protected after 8+ pairs"
+
+
+def test_4k_three_phases_match_oracle(synth_model_dir, cuda):
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200 import synth_frames
+    from oracle.oracle import OracleModel, OracleSession
+    W, H, N = 3840, 2160, 3
+    phases = (0.25, 0.5, 0.75)
+    frames = synth_frames.sequence_c3(N + 1, W, H, seed=3)
+    model = fh.Model(synth_model_dir)
+    pp = model.plan_params(W, H)
+    s = fh.Session(fh.Engine(), model, W, H)
+    s0 = fh.Session(fh.Engine(), model, W, H, repair=0)
+    ins, ins0 = [s.add_input(), s.add_input()], [s0.add_input(), s0.add_input()]
+    out = s.add_output()
+    o = OracleSession(OracleModel(synth_model_dir), W, H)
+    s.write(ins[0], frames[0])
+    s0.write(ins0[0], frames[0])
+    rows = []
+    for i in range(1, N + 1):
+        for ss, ii in ((s, ins), (s0, ins0)):
+            ss.write(ii[i % 2], frames[i])
+            ss.pair(ii[(i - 1) % 2], ii[i % 2])
+        o.pair(frames[i - 1], frames[i])
+        pre = s0.tensor("flow")
+        gm = _gmhs_records(o, pre)
+        _check_pre_flow(s.tensor("flow"), pre, gm[1]["sel"])
+        if i == N:
+            worst = {n: rel_l2(s.tensor(n), o.tensor(n, 0)) for n in PAIR_LAYERS}
+            assert max(worst.values()) <= LAYER_REL_L2, worst
+        age = s.tensor("age")
+        assert np.array_equal(age, o.tensor("age")), f"age differs after pair {i}"
+        for t in phases:
+            s.mid(t, out)
+            got = np.frombuffer(s.read(out), np.uint8)
+            ref = o.mid(t)
+            if i == N:
+                worst = {n: rel_l2(s.tensor(n), o.tensor(n, 1)) for n in MID_LAYERS}
+                assert max(worst.values()) <= LAYER_REL_L2, (t, worst)
+            up7g, rtg = s.tensor("up7"), s.tensor("R_t")
+            up7o, rto = o.tensor("up7", 1), o.tensor("R_t", 1)
+            flow_l1 = float(np.abs(up7g[:4] - up7o[:4]).mean())
+            assert flow_l1 <= 0.05, (i, t, flow_l1)
+            rep = check_frame(got, ref, frames[i - 1], frames[i], W, H, pp, (up7g, rtg), (up7o, rto), age, gm)
+            rep.update(i=i, t=t, flow_l1=flow_l1)
+            rows.append(rep)
+            _report("4k_three_phases", rows)
+            assert rep["ok"], rep

@@ -85,3 +85,31 @@ def test_gmhs_without_allocation_rejects_too_large():
     p = GmhsParams(dummy.data_ptr(), 0, 60, 108, dummy.data_ptr(), dummy.data_ptr(), 0, 480, 864, 1920, 1,
                    dummy.data_ptr(), 1)
     assert lib.fhk_gmhs_noalloc(ctypes.byref(p), stream) == 1  # a caller scratch is refused: it allocates nothing
+
+
+def test_gmhs_without_allocation_holds_device_memory_steady(synth_model_dir):
+    """After a warm-up call, a further call changes neither the device's free memory (cudaMemGetInfo) nor torch's
+    allocations: inputs and outputs are allocated before, nothing during the call."""
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200 import synth_frames
+    from oracle.oracle import OracleModel, OracleSession
+    lib = fh.lib()
+    fa, fb, _ = synth_frames.pair_c0(1920, 1080, seed=7)
+    o = OracleSession(OracleModel(synth_model_dir), 1920, 1080)
+    o.pair(fa, fb)
+    a, b, pre = o.tensor("A"), o.tensor("B"), o.tensor("flow_pre")
+    _, h, w = a.shape
+    _, h8, w8 = pre.shape
+    A, B, F = _device(torch, a, 4), _device(torch, b, 4), _device(torch, pre, 8)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = GmhsParams(F.data_ptr(), 0, h8, w8, A.data_ptr(), B.data_ptr(), 0, h, w, o.dims()["wp"], 1, None, 1)
+    assert lib.fhk_gmhs_noalloc(ctypes.byref(p), stream) == 0  # the warm-up call
+    torch.cuda.synchronize()
+    free0, alloc0 = torch.cuda.mem_get_info()[0], torch.cuda.memory_allocated()
+    assert lib.fhk_gmhs_noalloc(ctypes.byref(p), stream) == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert torch.cuda.memory_allocated() == alloc0
