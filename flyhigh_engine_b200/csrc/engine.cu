@@ -32,6 +32,7 @@
 #include "json.hpp"
 #include "launch.h"
 #include "stages.h"
+#include "tune.hpp"
 
 namespace {
 
@@ -251,6 +252,8 @@ struct FhEngine {
     int sm_major = 0, sm_minor = 0, sms = 0;
     size_t tensor_bytes = 0;
     int graphs_built = 0;
+    bool autotune = true;   // FhEngineOptions.autotune: time the conv kernels of each new shape when a session is built
+    std::string tune_file;  // FhEngineOptions.tune_cache: where this device's choices persist ("" = in memory only)
 };
 
 // --------------------------------------------------------------------------------------------------- session ----
@@ -265,6 +268,12 @@ struct ConvLayer {
     int cin = 0, cout = 0, stride = 1, cp = 0;
     bool act = true;
     bool umma = false;  // the tcgen05 kernel (conv_umma.cu) and its weight order, else conv3x3_mma
+    int wm = 0;         // conv3x3_mma: output rows per CTA pair (its K split), 0 = by size
+    uint8_t cand = 0;   // the autotune candidate in force (tune.hpp)
+    const char* how = "fixed";  // where the choice came from: "fixed", "tuned", "table", "session"
+    int hh = 0, ww = 0, n = 1;  // input size and entries per launch, for timing the candidates
+    std::vector<uint16_t> wbits;  // torch-layout weights (f16 bits) and the packed channel map, until packed
+    std::vector<int> map;
     uint16_t* wpack = nullptr;
     float* bias = nullptr;
     float* slope = nullptr;
@@ -645,14 +654,8 @@ struct FhSession {
         }
         L.cp = up16(slot);
         map.resize(L.cp, -1);
-        auto wb = model->bits(wn);
-        L.umma = umma_on && fhk_conv_umma_fits(L.cp, L.cout, stride);
-        std::vector<uint16_t> packed(L.umma ? fhk_conv_packed_elems_umma(L.cout, L.cp) : fhk_conv_packed_elems(L.cout, L.cp));
-        const int pk = L.umma ? fhk_conv_pack_weights_umma(wb.data(), L.cin, L.cout, map.data(), L.cp, packed.data())
-                              : fhk_conv_pack_weights(wb.data(), L.cin, L.cout, map.data(), L.cp, packed.data());
-        if (pk != 0) fail("%s: pack", name.c_str());
-        L.wpack = alloc_n<uint16_t>(packed.size());
-        CK(cudaMemcpyAsync(L.wpack, packed.data(), packed.size() * 2, cudaMemcpyHostToDevice, st));
+        L.wbits = model->bits(wn);
+        L.map = map;
         auto b = model->f32(bn);
         if ((int)b.size() != L.cout) fail("%s: bias size", bn.c_str());
         L.bias = alloc_n<float>(L.cout);
@@ -704,11 +707,209 @@ struct FhSession {
         p.res_cs = res_cs;
         p.res_bs = res.bs;
         p.n = n;
-        p.wm = 0;  // split chosen by size
+        p.wm = L.wm;  // the layer's K split (0: by size); channel groups by the launch's size
         p.ngroups = 0;
         int e = L.umma ? fhk_conv3x3_umma(&p, st) : fhk_conv3x3(&p, L.stride, st);
         if (e) fail("conv %s: %s", key.c_str(), cudaGetErrorString((cudaError_t)e));
         mark("conv " + L.name);
+    }
+
+    // ---- conv kernel choice (ops/conv/autotune.rs:74-150, conv_pick) ----
+    // Each conv layer runs one kernel, fixed when the session is built: from the session's tune text
+    // (FhSessionOptions.tune) when it names the layer's shape, else from the choices made on this device so far (and
+    // read from the engine's tune_cache), else, with FhEngineOptions.autotune on, by timing every candidate on the
+    // layer's own sizes (min over repeated runs, CUDA events) and keeping the fastest; with autotune off (or FH_UMMA
+    // set) the fixed rule: tcgen05 for batched sessions' stride-1 layers where it fits, mma.sync with rows by size
+    // otherwise. A choice holds for every launch of the layer whatever the launch's entry count, so an interval's
+    // result does not depend on how many intervals its launch carries.
+    std::string session_tune;  // FhSessionOptions.tune, copied at creation
+    bool tune_forced = false;  // FH_UMMA=0 / 1: the fixed rule with that kernel policy, no tuning
+    int tuned_now = 0;         // shapes timed while building this session
+
+    uint8_t fixed_choice(const ConvLayer& L) const {
+        return umma_on && fhk_conv_umma_fits(L.cp, L.cout, L.stride) ? (uint8_t)fhtune::KERNEL_UMMA : fhtune::mma(0);
+    }
+    // the input size and entries per launch of each layer: the encoders run per frame (nbat + 1 frames in a batch's
+    // frame stage), the rest per interval
+    void conv_geometry() {
+        const int nf = nbat > 1 ? nbat + 1 : 1;
+        auto geo = [&](const char* key, int hh, int ww, int n) {
+            auto it = convs.find(key);
+            if (it == convs.end()) return;
+            it->second.hh = hh;
+            it->second.ww = ww;
+            it->second.n = n;
+        };
+        geo("e1", qh, qw, nf);
+        geo("e2", h8, w8, nf);
+        geo("e3", h8, w8, nf);
+        geo("e4", h16, w16, nf);
+        for (const char* k : {"c1", "c2", "c3", "c4", "head"}) geo(k, h16, w16, nbat);
+        for (const char* k : {"r1_0", "r1", "r2", "r3", "out", "up", "fh1", "fh2", "fout"}) geo(k, h8, w8, nbat);
+        for (const char* k : {"q1", "q2", "q3", "q4"}) geo(k, qh, qw, nbat);
+    }
+    // device weights of a layer in a kernel's order (a fresh allocation the caller owns)
+    std::vector<uint16_t> packed_for(const ConvLayer& L, bool umma) const {
+        std::vector<uint16_t> packed(umma ? fhk_conv_packed_elems_umma(L.cout, L.cp) : fhk_conv_packed_elems(L.cout, L.cp));
+        const int pk = umma ? fhk_conv_pack_weights_umma(L.wbits.data(), L.cin, L.cout, L.map.data(), L.cp, packed.data())
+                            : fhk_conv_pack_weights(L.wbits.data(), L.cin, L.cout, L.map.data(), L.cp, packed.data());
+        if (pk != 0) fail("%s: pack", L.name.c_str());
+        return packed;
+    }
+    // Times every candidate kernel of a layer on scratch buffers of its sizes (its own source layout, n entries) and
+    // returns the fastest: conv3x3_mma at 1, 2 and 4 rows per CTA pair (a configuration that does not fit is skipped)
+    // and, for stride 1 where it fits, conv3x3_umma. The scratch is freed before returning.
+    uint8_t time_candidates(const ConvLayer& L) {
+        const int ho = (L.hh - 1) / L.stride + 1, wo = (L.ww - 1) / L.stride + 1, ocs = up8(L.cout);
+        int max_cs = 4;
+        for (const FhConvSrc& f : L.src) max_cs = std::max(max_cs, f.cs);
+        std::vector<void*> tmp;
+        auto dev = [&](size_t bytes) {
+            void* p = nullptr;
+            CK(cudaMalloc(&p, std::max<size_t>(bytes, 256)));
+            tmp.push_back(p);
+            CK(cudaMemsetAsync(p, 0, std::max<size_t>(bytes, 256), st));
+            return p;
+        };
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        uint8_t best = fixed_choice(L);
+        try {
+            const long long in_bs = (long long)L.hh * L.ww * max_cs, out_bs = (long long)ho * wo * ocs;
+            __half* in = (__half*)dev((size_t)in_bs * L.n * 2);
+            __half* out = (__half*)dev((size_t)out_bs * L.n * 2);
+            auto upload = [&](const std::vector<uint16_t>& v) {
+                void* d = dev(v.size() * 2);
+                CK(cudaMemcpyAsync(d, v.data(), v.size() * 2, cudaMemcpyHostToDevice, st));
+                return (uint16_t*)d;
+            };
+            uint16_t* w_mma = upload(packed_for(L, false));
+            const bool umma_ok = L.stride == 1 && fhk_conv_umma_fits(L.cp, L.cout, 1);
+            uint16_t* w_umma = umma_ok ? upload(packed_for(L, true)) : nullptr;
+            CK(cudaEventCreate(&e0));
+            CK(cudaEventCreate(&e1));
+            std::vector<uint8_t> cands = {fhtune::mma(1), fhtune::mma(2), fhtune::mma(4)};
+            if (umma_ok) cands.push_back(fhtune::KERNEL_UMMA);
+            float best_ms = 1e30f;
+            for (uint8_t c : cands) {
+                const bool um = fhtune::kernel_of(c) == fhtune::KERNEL_UMMA;
+                FhConvParams p{};
+                for (size_t i = 0; i < L.src.size(); i++) {
+                    p.src[i] = L.src[i];
+                    p.src[i].p = in;
+                    p.src[i].bs = in_bs;
+                    p.src[i].cs = L.src[i].cs;
+                }
+                p.nsrc = (int)L.src.size();
+                p.h = L.hh;
+                p.w = L.ww;
+                p.ho = ho;
+                p.wo = wo;
+                p.cp = L.cp;
+                p.cout = L.cout;
+                p.wpack = um ? w_umma : w_mma;
+                p.bias = L.bias;
+                p.slope = L.slope;
+                p.out = out;
+                p.out_cs = ocs;
+                p.out_bs = out_bs;
+                p.n = L.n;
+                p.wm = um ? 0 : fhtune::wm_of(c);
+                auto launch = [&]() { return um ? fhk_conv3x3_umma(&p, st) : fhk_conv3x3(&p, L.stride, st); };
+                if (launch() != 0) {  // this configuration does not fit the layer: not a candidate
+                    cudaGetLastError();
+                    continue;
+                }
+                const int reps = 8;
+                float ms = 1e30f;
+                for (int trial = 0; trial < 3; trial++) {
+                    CK(cudaEventRecord(e0, st));
+                    for (int r = 0; r < reps; r++)
+                        if (launch() != 0) fail("conv %s: candidate %s failed", L.name.c_str(), fhtune::name(c).c_str());
+                    CK(cudaEventRecord(e1, st));
+                    CK(cudaEventSynchronize(e1));
+                    float t = 0;
+                    CK(cudaEventElapsedTime(&t, e0, e1));
+                    ms = std::min(ms, t / reps);
+                }
+                if (ms < best_ms) {
+                    best_ms = ms;
+                    best = c;
+                }
+            }
+        } catch (...) {
+            cudaStreamSynchronize(st);
+            for (void* q : tmp) cudaFree(q);
+            if (e0) cudaEventDestroy(e0);
+            if (e1) cudaEventDestroy(e1);
+            throw;
+        }
+        CK(cudaStreamSynchronize(st));
+        for (void* q : tmp) CK(cudaFree(q));
+        CK(cudaEventDestroy(e0));
+        CK(cudaEventDestroy(e1));
+        return best;
+    }
+    void choose_conv_kernels() {
+        conv_geometry();
+        const fhtune::Table mine = fhtune::parse(session_tune);
+        fhtune::Store& store = fhtune::Store::get();
+        for (auto& kv : convs) {
+            ConvLayer& L = kv.second;
+            const fhtune::Key key{(uint32_t)L.cin, (uint32_t)L.cout, (uint32_t)L.hh, (uint32_t)L.ww, (uint32_t)L.stride};
+            uint8_t c = 0;
+            auto it = mine.find(key);
+            if (it != mine.end()) {
+                c = it->second;
+                L.how = "session";
+            } else if (tune_forced || !eng->autotune) {
+                c = fixed_choice(L);
+                L.how = "fixed";
+            } else {
+                bool have = false;
+                {
+                    std::lock_guard<std::mutex> lock(store.m);
+                    auto& t = store.tables[eng->device];
+                    auto f = t.find(key);
+                    if (f != t.end()) {
+                        c = f->second;
+                        have = true;
+                    }
+                }
+                if (have) {
+                    L.how = "table";
+                } else {
+                    c = time_candidates(L);
+                    L.how = "tuned";
+                    tuned_now++;
+                    std::lock_guard<std::mutex> lock(store.m);
+                    store.tables[eng->device].emplace(key, c);
+                }
+            }
+            // a choice the layer cannot run (a byte of another kernel set, a table from other sizes or options) falls
+            // back to the fixed rule
+            if (!fhtune::valid(c) ||
+                (fhtune::kernel_of(c) == fhtune::KERNEL_UMMA && !(L.stride == 1 && fhk_conv_umma_fits(L.cp, L.cout, 1)))) {
+                c = fixed_choice(L);
+                L.how = "fixed";
+            }
+            L.cand = c;
+            L.umma = fhtune::kernel_of(c) == fhtune::KERNEL_UMMA;
+            L.wm = L.umma ? 0 : fhtune::wm_of(c);
+            std::vector<uint16_t> packed = packed_for(L, L.umma);
+            L.wpack = alloc_n<uint16_t>(packed.size());
+            CK(cudaMemcpyAsync(L.wpack, packed.data(), packed.size() * 2, cudaMemcpyHostToDevice, st));
+            CK(cudaStreamSynchronize(st));  // packed lives on the host stack
+            std::vector<uint16_t>().swap(L.wbits);
+        }
+        if (tuned_now && !eng->tune_file.empty()) {  // tune_cache.rs:24-35: persist when something new was timed
+            std::string text;
+            {
+                std::lock_guard<std::mutex> lock(store.m);
+                text = fhtune::format(store.tables[eng->device]);
+            }
+            std::ofstream f(eng->tune_file, std::ios::binary | std::ios::trunc);
+            if (f) f << text;
+        }
     }
 
     void plan() {
@@ -764,6 +965,7 @@ struct FhSession {
         if (convs["head"].cout < 7 || convs["out"].cout != 7 || convs["fout"].cout != 5 || convs["up"].cout != 36 ||
             convs["q4"].cout != 3 || convs["q1"].cin != 14)
             fail("the manifest's head shapes do not match the FlyHighFG graph");
+        choose_conv_kernels();
         // FiLM MLP weights (f32, the values the host MLP reads: net/build.rs:333-334)
         auto w1 = model->f32("film.film.0.weight"), b1 = model->f32("film.film.0.bias");
         auto w2 = model->f32("film.film.2.weight"), b2 = model->f32("film.film.2.bias");
@@ -1689,6 +1891,8 @@ FhSession* session_new(FhEngine* e, const FhModel* m, const FhSessionOptions& o,
     if (batch > 16) fail("batch: %d intervals per launch (1..16)", batch);
     s->nbat = batch;
     if (batch > 1 && !env_is("FH_UMMA", "0")) s->umma_on = true;
+    s->tune_forced = env_is("FH_UMMA", "0") || env_is("FH_UMMA", "1");
+    if (o.tune) s->session_tune = o.tune;
     // a batched session's graphs take the priority of their streams (frame stages and networks high, static passes
     // and renders low) rather than per-launch priorities, which measured 1.2 % slower with batches overlapping
     // (FH_PRIO=1 keeps them)
@@ -1766,6 +1970,23 @@ FhEngine* fh_engine_create(const FhEngineOptions* opts) {
         e->sm_major = p.major;
         e->sm_minor = p.minor;
         e->sms = p.multiProcessorCount;
+        e->autotune = o.autotune != 0;
+        if (o.tune_cache && o.tune_cache[0]) {
+            // the device's persisted choices (gpu/device.rs:241-259): merged into this process's table for the device,
+            // choices already made in this process win
+            int driver = 0;
+            cudaDriverGetVersion(&driver);
+            e->tune_file = fhtune::file_name(o.tune_cache, e->name, driver);
+            std::ifstream f(e->tune_file, std::ios::binary);
+            if (f) {
+                std::stringstream ss;
+                ss << f.rdbuf();
+                const fhtune::Table t = fhtune::parse(ss.str());
+                fhtune::Store& store = fhtune::Store::get();
+                std::lock_guard<std::mutex> lock(store.m);
+                for (const auto& kv : t) store.tables[dev].emplace(kv.first, kv.second);
+            }
+        }
         return e;
     });
 }
@@ -1787,10 +2008,24 @@ int fh_engine_info(const FhEngine* e, char* buf, size_t cap) {
 int fh_engine_report_json(const FhEngine* e, char* buf, size_t cap) {
     return guard(-1, [&] {
         if (!e) fail("null argument");
-        char b[512];
-        snprintf(b, sizeof b, "{\"device\":%s,\"kernels_compiled\":%d,\"autotune_entries\":0,\"tensor_bytes\":%zu}",
-                 fhjson::quote(e->name).c_str(), e->graphs_built, e->tensor_bytes);
-        return write_json(b, buf, cap);
+        size_t entries = 0;
+        std::string table;
+        {
+            fhtune::Store& store = fhtune::Store::get();
+            std::lock_guard<std::mutex> lock(store.m);
+            auto it = store.tables.find(e->device);
+            if (it != store.tables.end()) {
+                entries = it->second.size();
+                table = fhtune::format(it->second);
+            }
+        }
+        std::string js = "{\"device\":" + fhjson::quote(e->name) + ",\"kernels_compiled\":" +
+                         std::to_string(e->graphs_built) + ",\"autotune_entries\":" + std::to_string(entries) +
+                         ",\"autotune\":" + (e->autotune ? "true" : "false") + ",\"tune_table\":" +
+                         fhjson::quote(table) + ",\"tune_cache\":" +
+                         (e->tune_file.empty() ? std::string("null") : fhjson::quote(e->tune_file)) +
+                         ",\"tensor_bytes\":" + std::to_string(e->tensor_bytes) + "}";
+        return write_json(js.c_str(), buf, cap);
     });
 }
 
@@ -2058,7 +2293,20 @@ int fh_session_report_json(const FhSession* s, char* buf, size_t cap) {
                  s->linear ? "true" : "false", sp,
                  s->o.protection_mask ? "true" : "false", s->ins.size(), s->outs.size(), s->pair_kernels, s->mid_kernels,
                  s->frame_kernels, s->bytes);
-        return write_json(b, buf, cap);
+        // the conv kernel of every layer and where its choice came from (fixed rule, timed, this device's table, the
+        // session's tune text)
+        std::string js(b);
+        js.pop_back();
+        js += ",\"autotuned\":" + std::to_string(s->tuned_now) + ",\"convs\":{";
+        bool first = true;
+        for (const auto& kv : s->convs) {
+            js += std::string(first ? "" : ",") + fhjson::quote(kv.second.name + (kv.first == "r1_0" ? "#0" : "")) +
+                  ":{\"kernel\":" + fhjson::quote(fhtune::name(kv.second.cand)) + ",\"choice\":" +
+                  fhjson::quote(kv.second.how) + "}";
+            first = false;
+        }
+        js += "}}";
+        return write_json(js.c_str(), buf, cap);
     });
 }
 

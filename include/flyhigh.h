@@ -31,10 +31,10 @@ const char* fh_last_error(void);
 typedef struct FhEngineOptions {
     uint32_t backend;        /* accepted, ignored (CUDA) */
     uint32_t tensor_cores;   /* accepted; the conv kernels always use the tensor cores */
-    uint32_t autotune;       /* accepted; kernel choices are fixed per shape */
+    uint32_t autotune;       /* 1 (default) = time each conv shape's kernels when a session is built, 0 = fixed */
     const char* adapter;     /* NULL = device 0, "#N" = CUDA device N */
     uint32_t precision;      /* 0 auto / 1 f16 (f16 storage, f32 math); 2 (f32) is refused */
-    const char* tune_cache;  /* accepted, ignored */
+    const char* tune_cache;  /* NULL or a directory: the device's conv choices persist there, one file per GPU / driver */
     uint32_t compact_memory; /* accepted, ignored */
     const char* dxc_path;    /* accepted, ignored */
 } FhEngineOptions;
@@ -44,7 +44,7 @@ FhEngine* fh_engine_create(const FhEngineOptions* options); /* NULL options = th
 void fh_engine_destroy(FhEngine* engine);
 /* {"name","class":"tc-f16","tensor_cores","timestamps","bgra_storage","shader_compiler":null,"sm","device"} */
 int fh_engine_info(const FhEngine* engine, char* buf, size_t cap);
-/* {"device","kernels_compiled","autotune_entries","tensor_bytes"} */
+/* {"device","kernels_compiled","autotune_entries","autotune","tune_table","tune_cache","tensor_bytes"} */
 int fh_engine_report_json(const FhEngine* engine, char* buf, size_t cap);
 
 /* ---- Model: weights and graph (flyhigh.h:57-62) ---- */
@@ -69,7 +69,7 @@ typedef struct FhSessionOptions {
     uint32_t linear_t;               /* 1 = with fast_render, the mid network once per pair, phases scaled linearly */
     uint32_t keep_maps;              /* 1 = keep the repair maps (raises repair to 1) */
     uint32_t protection_mask;        /* 1 = the host paints pixels never interpolated (fh_session_write_mask) */
-    const char* tune;                /* accepted, ignored */
+    const char* tune;                /* NULL or autotune table text ("cin,cout,h,w,stride=candidate" lines) */
 } FhSessionOptions;
 
 FhSessionOptions fh_session_options_default(uint32_t width, uint32_t height);

@@ -58,3 +58,15 @@ def test_reference_c_host_runs(reference_models):
     assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
     assert r.stdout.strip().splitlines()[-1] == "ok", r.stdout
     assert "in-between: MAE to the true middle" in r.stdout
+
+
+def test_tune_table_format(tmp_path):
+    """The conv autotune table's text format (csrc/tune.hpp) on the host: the reference's own round-trip case
+    (crates/flyhigh-engine/tests/defaults.rs:55-63), malformed lines skipped, sorted output, this library's candidate
+    bytes and the per-GPU / driver file name."""
+    exe = str(tmp_path / "tune_roundtrip")
+    subprocess.run(["g++", "-std=c++17", "-Wall", "-I", os.path.join(ROOT, "flyhigh_engine_b200", "csrc"), "-o", exe,
+                    os.path.join(ROOT, "tests", "c_abi", "tune_roundtrip.cpp")], check=True)
+    r = subprocess.run([exe], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout
+    assert r.stdout.count("ok ") == 11
