@@ -317,6 +317,23 @@ def main():
         sf.mid(0.5, fo)
         fast = {"pair_ms": sf.pair_timed(fs[0], fs[1]), "mid_ms": sf.mid_timed(0.25, fo)}
         del sf
+    # config 3's latency and config 1's per-conv sweep (rank 0 of a 1-GPU run; the scaling runs skip them)
+    c3 = sweep = None
+    if rank == 0 and ws == 1 and not args.no_e2e:
+        peaks = {}
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                peaks = json.load(f)
+        except Exception:
+            pass
+        try:  # side measurements: a failure is reported in the line, not as a failed run
+            c3 = config3_latency(engine, model)
+        except Exception as e:
+            c3 = {"error": str(e)}
+        try:
+            sweep = conv_sweep(f"cuda:{local}", peaks.get("bf16_tflops"))
+        except Exception as e:
+            sweep = {"error": str(e)}
     cpu = None
     if rank == 0 and ws == 1:
         fps_cpu, dt = cpu_baseline(model_dir, frames, args.cpu_sample)
@@ -335,12 +352,85 @@ def main():
                            "batch": args.batch, "pair_ms": pair_ms, "mid_ms": mid_ms},
                 "gpu_launches": launches * ws,
                 "clocks": clk.summary(), "roofline": roof, "roofline_conv": roof_conv, "cpu_baseline": cpu,
-                "e2e": e2e, "fast_render_linear_t": fast, "kernel_ms": {k: round(v, 5) for k, v in sorted(prof.items(), key=lambda x: -x[1])[:12]}}
+                "e2e": e2e, "fast_render_linear_t": fast, "config3_4k": c3, "conv_sweep": sweep,
+                "conv_kernels": {k: v["kernel"] for k, v in s.report()["convs"].items()},
+                "kernel_ms": {k: round(v, 5) for k, v in sorted(prof.items(), key=lambda x: -x[1])[:12]}}
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()
     return 0
+
+
+def conv_sweep(device: str, peak_tflops):
+    """Config 1: every implicit-GEMM 3x3 conv of the isolated sweep (480x270 and 960x540, Cin / Cout in {16, 32, 48,
+    64}, stride 1 and 2, bias + PReLU(0.1), with and without an f16 residual) on both conv kernels where they apply
+    (mma.sync at the rows-per-CTA rule; tcgen05 for stride 1), batch 1. Each timed as the mean of 20 back-to-back
+    launches (CUDA events on the launching stream, min over 3 trials, after 3 warm-up launches). Returns the per-shape
+    records [h, w, cin, cout, stride, residual, best kernel, us, TFLOP/s] and a summary against the tensor peak."""
+    import torch
+    from flyhigh_engine_b200.kernels import Conv3x3
+    rng = np.random.default_rng(1)
+    stream = torch.cuda.current_stream()
+    rows = []
+    for (h, w) in ((270, 480), (540, 960)):
+        for cin in (16, 32, 48, 64):
+            x = torch.from_numpy(rng.standard_normal((1, h, w, cin)).astype(np.float16)).to(device)
+            for cout in (16, 32, 48, 64):
+                wt = (rng.standard_normal((cout, cin, 3, 3)) / np.sqrt(9 * cin)).astype(np.float32)
+                bias = (0.1 * rng.standard_normal(cout)).astype(np.float32)
+                slope = np.full(cout, 0.1, np.float32)
+                for stride in (1, 2):
+                    for res in (False, True):
+                        best = None
+                        for kernel in ("mma", "umma") if stride == 1 else ("mma",):
+                            conv = Conv3x3(wt, bias, slope, stride=stride, kernel=kernel, device=device)
+                            out = torch.zeros(conv.out_shape(1, h, w), dtype=torch.float16, device=device)
+                            r = torch.zeros_like(out) if res else None
+                            prm = conv.params(x, out, r)
+                            for _ in range(3):
+                                conv.launch(prm, stream.cuda_stream)
+                            ms = 1e9
+                            for _ in range(3):
+                                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                                e0.record(stream)
+                                for _ in range(20):
+                                    conv.launch(prm, stream.cuda_stream)
+                                e1.record(stream)
+                                e1.synchronize()
+                                ms = min(ms, e0.elapsed_time(e1) / 20)
+                            if best is None or ms < best[1]:
+                                best = (kernel, ms)
+                        ho, wo = (h - 1) // stride + 1, (w - 1) // stride + 1
+                        tflops = 2.0 * ho * wo * 9 * cin * cout / (best[1] / 1000.0) / 1e12
+                        rows.append([h, w, cin, cout, stride, int(res), best[0], round(best[1] * 1000, 2),
+                                     round(tflops, 2)])
+    top = max(rows, key=lambda r: r[8])
+    return {"fields": ["h", "w", "cin", "cout", "stride", "residual", "kernel", "us", "tflops"], "rows": rows,
+            "best": {"shape": top[:6], "kernel": top[6], "us": top[7], "tflops": top[8],
+                     "frac": top[8] / peak_tflops if peak_tflops else None},
+            "note": "batch 1, inputs L2-resident (<= 66 MB), mean of 20 back-to-back launches"}
+
+
+def config3_latency(engine, model):
+    """Config 3 (3840 x 2160, 4x: a pair and phases 0.25 / 0.5 / 0.75) on a session run one interval at a time: device
+    ms of pair() and of each mid() (the reference's pair_timed / mid_timed: min of 3 / 5 runs) on seeded fence-pan
+    frames, and ms per generated frame = (pair + three mids) / 3."""
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200 import synth_frames
+    w4, h4 = 3840, 2160
+    fr = synth_frames.sequence_c3(2, w4, h4, seed=3)
+    s = fh.Session(engine, model, w4, h4)
+    a, b, out = s.add_input(), s.add_input(), s.add_output()
+    s.write(a, fr[0])
+    s.write(b, fr[1])
+    s.pair(a, b)
+    s.mid(0.5, out)
+    pair_ms = s.pair_timed(a, b)
+    mids = [s.mid_timed(t, out) for t in (0.25, 0.5, 0.75)]
+    del s
+    return {"workload": "3840x2160, pair + mid(0.25 / 0.5 / 0.75), one interval per launch, fence pan frames",
+            "pair_ms": pair_ms, "mid_ms": mids, "ms_per_generated_frame": (pair_ms + sum(mids)) / 3.0}
 
 
 def conv_flops(s, nb: int) -> float:
