@@ -11,6 +11,13 @@ shapes. One step = the whole sequence.
           fh_session_pair, fh_session_mid, fh_session_read_rgba into pinned host memory, every interval.
 The sequence (1 GB) is larger than L2 (126 MB), so no explicit flush is needed between timed steps.
 
+Further keys of the line: `strong` (one 120-frame stream split by interval over the ranks, each replaying the
+static-age pass over its prefix: strong scaling), `e2e.copy_ceiling` (the e2e loop's bytes with no compute, serial and
+overlapped, and e2e as a fraction of the serial ceiling), `roofline` (k_render against HBM: algorithmic bytes, design
+bytes, DRAM traffic from its ncu summary), `roofline_conv` (every conv of a batch against the tensor peak),
+`conv_sweep` (config 1: each isolated conv shape on both conv kernels), `config3_4k` (3840 x 2160 latency of a pair
+and three phases), `fast_render_linear_t`, `conv_kernels` (the autotuned kernel of each layer), `kernel_ms`.
+
 Multi-GPU (torchrun, one process per GPU): every rank runs its own seeded sequence (weak scaling, no collective on
 the data path); the step time is the max over ranks. --impl reference times the reference algorithm's CPU
 restatement (oracle/; the reference itself cannot be built or run here) on the host cores.
@@ -42,6 +49,7 @@ def parse():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--frames", type=int, default=NFRAMES)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-strong", action="store_true", help="skip the strong-scaling arm")
     p.add_argument("--cpu-sample", type=int, default=3, help="intervals of the CPU baseline sample")
     p.add_argument("--batch", type=int, default=4,
                    help="intervals per launch (fh_session_create_batched); 1 = one interval per launch")
@@ -241,6 +249,61 @@ def main():
     gen_per_rank = n - 1
     value = gen_per_rank * ws / (ms / 1000.0)
 
+    # strong scaling: ONE 120-frame stream (the same seeded sequence on every rank) split into contiguous interval
+    # shards; a rank whose shard starts at interval s first replays the static-age pass over intervals 1..s
+    # (fh_session_advance_static), so its protection state equals a single GPU's; the replay is inside the timed region
+    strong = None
+    if not args.no_strong:
+        from flyhigh_engine_b200.multi import shard
+        one = synth_frames.sequence_c2(n, W, H, seed=100) if ws > 1 else frames
+        one_dev = torch.from_numpy(np.stack(one)).to(f"cuda:{local}") if ws > 1 else dev_frames
+        s0, e0 = shard(n - 1, ws, rank)
+        ss = fh.Session(engine, model, W, H, batch=args.batch)
+        sslots = [ss.add_input(), ss.add_input()]
+        sout = ss.add_output()
+        sbase = one_dev.data_ptr()
+
+        def step_strong():
+            ss.write_device(sslots[0], sbase, fbytes)
+            for i in range(1, s0 + 1):
+                ss.write_device(sslots[i % 2], sbase + i * fbytes, fbytes)
+                ss.advance_static(sslots[(i - 1) % 2], sslots[i % 2])
+            for i in range(s0 + 1, e0 + 1):
+                ss.write_device(sslots[i % 2], sbase + i * fbytes, fbytes)
+                ss.pair(sslots[(i - 1) % 2], sslots[i % 2])
+                ss.mid(0.5, sout)
+            ss.join()
+
+        sstream = torch.cuda.ExternalStream(ss.cuda_stream(), device=f"cuda:{local}")
+
+        def timed_on(fn, k, strm):
+            barrier()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(strm)
+            for _ in range(k):
+                fn()
+            ev1.record(strm)
+            ev1.synchronize()
+            t_ms = ev0.elapsed_time(ev1) / k
+            barrier()
+            if pg is not None:
+                t = torch.tensor([t_ms], device=f"cuda:{local}")
+                pg.all_reduce(t, op=pg.ReduceOp.MAX)
+                t_ms = float(t.item())
+            return t_ms
+
+        for _ in range(warm):
+            step_strong()
+        strong_ms = timed_on(step_strong, args.steps, sstream)
+        strong = {"value": (n - 1) / (strong_ms / 1000.0), "unit": "generated frames/s", "scaling": "strong",
+                  "ms_per_step": strong_ms, "intervals": n - 1, "this_rank": [s0, e0],
+                  "replayed_intervals_max": (ws - 1) * (n - 1) // ws,
+                  "workload": "one 120-frame config-2 stream split by interval over the ranks, each replaying the "
+                              "static-age pass over its prefix (device-resident frames)"}
+        del ss
+        if ws > 1:
+            del one_dev
+
     # device ms per pair() and per mid() (the reference's pair_timed / mid_timed: min of 3 / 5 runs)
     pair_ms = s.pair_timed(slots[0], slots[1])
     mid_ms = s.mid_timed(0.5, out)
@@ -286,6 +349,45 @@ def main():
         e2e = {"value": gen_per_rank * ws / (e2e_ms / 1000.0), "unit": "generated frames/s",
                "h2d_bytes_per_step": n * fbytes, "d2h_bytes_per_step": gen_per_rank * fbytes,
                "ms_per_step": e2e_ms}
+
+        # The copy ceiling of this call pattern: the same bytes between the same pinned buffers and the device with no
+        # compute, one host thread per rank. "serial": each copy waited for before the next call, as write_rgba and
+        # read_rgba wait for theirs; "overlapped": uploads and readbacks on two streams at once, what the link and host
+        # memory allow. Max over ranks, wall clock as e2e.
+        cin_dev = torch.empty((H, W, 4), dtype=torch.uint8, device=f"cuda:{local}")
+        cout_dev = torch.empty_like(cin_dev)
+        up_s, dn_s = torch.cuda.Stream(device=f"cuda:{local}"), torch.cuda.Stream(device=f"cuda:{local}")
+
+        def step_copy(overlapped):
+            for i in range(n):
+                with torch.cuda.stream(up_s):
+                    cin_dev.copy_(pinned[i], non_blocking=True)
+                if not overlapped:
+                    up_s.synchronize()
+                if i > 0:
+                    with torch.cuda.stream(dn_s):
+                        outbuf.copy_(cout_dev, non_blocking=True)
+                    if not overlapped:
+                        dn_s.synchronize()
+            up_s.synchronize()
+            dn_s.synchronize()
+
+        copy = {}
+        for mode in ("serial", "overlapped"):
+            step_copy(mode == "overlapped")
+            barrier()
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                step_copy(mode == "overlapped")
+            c_ms = (time.perf_counter() - t0) * 1000.0 / args.steps
+            if pg is not None:
+                t = torch.tensor([c_ms], device=f"cuda:{local}")
+                pg.all_reduce(t, op=pg.ReduceOp.MAX)
+                c_ms = float(t.item())
+            copy[mode] = {"value": gen_per_rank * ws / (c_ms / 1000.0), "ms_per_step": c_ms,
+                          "gb_per_s_per_rank": (n + gen_per_rank) * fbytes / (c_ms / 1000.0) / 1e9}
+        e2e["copy_ceiling"] = copy
+        e2e["frac_of_serial_copy_ceiling"] = e2e["value"] / copy["serial"]["value"]
 
     # per-kernel device times on the session's own stream (min over 5 eager runs): one batch of `batch` intervals for a
     # batched session (the frame stage of its batch + 1 frames, its pairs and mids), else one pair + mid
@@ -352,7 +454,7 @@ def main():
                            "batch": args.batch, "pair_ms": pair_ms, "mid_ms": mid_ms},
                 "gpu_launches": launches * ws,
                 "clocks": clk.summary(), "roofline": roof, "roofline_conv": roof_conv, "cpu_baseline": cpu,
-                "e2e": e2e, "fast_render_linear_t": fast, "config3_4k": c3, "conv_sweep": sweep,
+                "e2e": e2e, "strong": strong, "fast_render_linear_t": fast, "config3_4k": c3, "conv_sweep": sweep,
                 "conv_kernels": {k: v["kernel"] for k, v in s.report()["convs"].items()},
                 "kernel_ms": {k: round(v, 5) for k, v in sorted(prof.items(), key=lambda x: -x[1])[:12]}}
         print(json.dumps(line), flush=True)
