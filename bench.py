@@ -12,7 +12,8 @@ shapes. One step = the whole sequence.
 The sequence (1 GB) is larger than L2 (126 MB), so no explicit flush is needed between timed steps.
 
 Further keys of the line: `strong` (one 120-frame stream split by interval over the ranks, each replaying the
-static-age pass over its prefix: strong scaling), `e2e.copy_ceiling` (the e2e loop's bytes with no compute, serial and
+static-age pass over its prefix: strong scaling), `config4_streams` (config 4: 64 streams through the Stream layer,
+sharded by stream), `e2e.copy_ceiling` (the e2e loop's bytes with no compute, serial and
 overlapped, and e2e as a fraction of the serial ceiling), `roofline` (k_render against HBM: algorithmic bytes, design
 bytes, DRAM traffic from its ncu summary), `roofline_conv` (every conv of a batch against the tensor peak),
 `conv_sweep` (config 1: each isolated conv shape on both conv kernels), `config3_4k` (3840 x 2160 latency of a pair
@@ -50,6 +51,7 @@ def parse():
     p.add_argument("--frames", type=int, default=NFRAMES)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-strong", action="store_true", help="skip the strong-scaling arm")
+    p.add_argument("--no-c4", action="store_true", help="skip config 4 (the multi-stream Stream-layer run)")
     p.add_argument("--cpu-sample", type=int, default=3, help="intervals of the CPU baseline sample")
     p.add_argument("--batch", type=int, default=4,
                    help="intervals per launch (fh_session_create_batched); 1 = one interval per launch")
@@ -419,6 +421,15 @@ def main():
         sf.mid(0.5, fo)
         fast = {"pair_ms": sf.pair_timed(fs[0], fs[1]), "mid_ms": sf.mid_timed(0.25, fo)}
         del sf
+    # config 4 through the Stream layer, sharded by stream (every rank, every N)
+    c4 = None
+    if not args.no_c4:
+        try:
+            c4 = config4(engine, model, ws, rank, local, barrier, pg)
+        except Exception as e:  # a side measurement: reported in the line, not a failed run
+            c4 = {"error": str(e)}
+            if pg is not None:
+                raise
     # config 3's latency and config 1's per-conv sweep (rank 0 of a 1-GPU run; the scaling runs skip them)
     c3 = sweep = None
     if rank == 0 and ws == 1 and not args.no_e2e:
@@ -454,7 +465,8 @@ def main():
                            "batch": args.batch, "pair_ms": pair_ms, "mid_ms": mid_ms},
                 "gpu_launches": launches * ws,
                 "clocks": clk.summary(), "roofline": roof, "roofline_conv": roof_conv, "cpu_baseline": cpu,
-                "e2e": e2e, "strong": strong, "fast_render_linear_t": fast, "config3_4k": c3, "conv_sweep": sweep,
+                "e2e": e2e, "strong": strong, "config4_streams": c4, "fast_render_linear_t": fast, "config3_4k": c3,
+                "conv_sweep": sweep,
                 "conv_kernels": {k: v["kernel"] for k, v in s.report()["convs"].items()},
                 "kernel_ms": {k: round(v, 5) for k, v in sorted(prof.items(), key=lambda x: -x[1])[:12]}}
         print(json.dumps(line), flush=True)
@@ -535,6 +547,118 @@ def config3_latency(engine, model):
             "pair_ms": pair_ms, "mid_ms": mids, "ms_per_generated_frame": (pair_ms + sum(mids)) / 3.0}
 
 
+def c4_pool(device, scenes=5, per_scene=48, seed=400):
+    """Config 4's source frames, made on the GPU: `scenes` seeded scenes of `per_scene` 1080p frames each, with the
+    statistics of the config-2 generator (a texture of 8 random sinusoids, periods 8-128 px, uniform noise of +-10; a pan
+    whose velocity random-walks by +-2 px per frame; 5 rectangles of 20-80 px moving independently). [scenes *
+    per_scene][H][W][4] uint8 on `device`."""
+    import torch
+    out = torch.empty((scenes * per_scene, H, W, 4), dtype=torch.uint8, device=device)
+    m = 24 * per_scene // 4 + 64
+    yy = torch.arange(H + 2 * m, device=device, dtype=torch.float32)[:, None]
+    xx = torch.arange(W + 2 * m, device=device, dtype=torch.float32)[None, :]
+    for k in range(scenes):
+        rng = np.random.default_rng(seed + k)
+        tex = torch.full((H + 2 * m, W + 2 * m, 3), 128.0, device=device)
+        for _ in range(8):
+            period, ang, phase = rng.uniform(8.0, 128.0), rng.uniform(0.0, np.pi), rng.uniform(0.0, 2 * np.pi)
+            amp = torch.tensor(rng.uniform(10.0, 30.0, size=3), dtype=torch.float32, device=device)
+            kx, ky = float(np.cos(ang) * 2 * np.pi / period), float(np.sin(ang) * 2 * np.pi / period)
+            tex += torch.sin(kx * xx + ky * yy + phase)[..., None] * amp
+        rects = [dict(x=int(rng.integers(0, W - 80)), y=int(rng.integers(0, H - 80)), w=int(rng.integers(20, 81)),
+                      h=int(rng.integers(20, 81)), v=rng.integers(-3, 4, size=2),
+                      c=torch.tensor(rng.integers(0, 256, size=3), dtype=torch.float32, device=device))
+                 for _ in range(5)]
+        gen = torch.Generator(device=device).manual_seed(seed + k)
+        px = py = vx = vy = 0
+        for i in range(per_scene):
+            vx = int(np.clip(vx + rng.integers(-2, 3), -24, 24))
+            vy = int(np.clip(vy + rng.integers(-2, 3), -24, 24))
+            px, py = int(np.clip(px + vx, -m, m)), int(np.clip(py + vy, -m, m))
+            img = tex[m + py:m + py + H, m + px:m + px + W].clone()
+            for r in rects:
+                r["x"] += int(r["v"][0])
+                r["y"] += int(r["v"][1])
+                x0, y0 = max(0, r["x"]), max(0, r["y"])
+                x1, y1 = min(W, r["x"] + r["w"]), min(H, r["y"] + r["h"])
+                if x0 < x1 and y0 < y1:
+                    img[y0:y1, x0:x1] = r["c"]
+            img += torch.rand(img.shape, generator=gen, device=device) * 20.0 - 10.0
+            out[k * per_scene + i, ..., :3] = img.clamp_(0, 255).to(torch.uint8)
+            out[k * per_scene + i, ..., 3] = 255
+    return out
+
+
+def config4(engine, model, ws, rank, local, barrier, pg, streams_total=64, frames=240, phases=(0.2, 0.4, 0.6, 0.8)):
+    """Config 4: 64 independent 1080p streams of 240 source frames each (24 -> 120 fps: four mids per interval), a scene
+    cut every 48 frames, 2-frame held runs every 30 frames, through the Stream layer (realtime, scene cuts at the
+    default threshold, held frames on), sharded by stream over the ranks with no collective. Per frame and stream: the
+    next input slot, the frame (device-resident pool), classify, push, and the four mids when the pair is motion (cuts
+    and holds show source frames). One pass, wall clock from a barrier to the synchronize after the last call, max over
+    ranks."""
+    import torch
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200 import synth_frames
+    from flyhigh_engine_b200.multi import shard
+    dev = f"cuda:{local}"
+    pool = c4_pool(dev)
+    fbytes = W * H * 4
+    base = pool.data_ptr()
+    s0, s1 = shard(streams_total, ws, rank)
+    sts = [fh.Stream(engine, model, W, H, held_frames=True) for _ in range(s0, s1)]
+    orders = [synth_frames.stream_c4(frames, 48, 30, scenes=5, offset=k) for k in range(s0, s1)]
+    for st in sts:  # every graph built before the timed pass: the ring's four pairs, each into the four outputs
+        prev_w = None
+        for i in range(5):
+            slot = st.next_input([] if prev_w is None else [prev_w])
+            st.write_device(slot, base + i * fbytes, fbytes)
+            if st.push(slot, float(i)).ready:
+                for j, t in enumerate(phases):
+                    st.generate(t, j)
+            prev_w = slot
+        st.reset()
+    torch.cuda.synchronize()
+    counts = {"motion": 0, "cut": 0, "hold": 0}
+    mids = 0
+    prev = [None] * len(sts)
+    barrier()
+    t0 = time.perf_counter()
+    for f in range(frames):
+        for k, st in enumerate(sts):
+            sc, j = orders[k][f]
+            slot = st.next_input([] if prev[k] is None else [prev[k]])
+            st.write_device(slot, base + (sc * 48 + j) * fbytes, fbytes)
+            kind = None
+            if prev[k] is not None:
+                c = st.classify(prev[k], slot)
+                kind = c.kind if c is not None else "motion"
+                counts[kind] += 1
+            p = st.push(slot, f * 1000.0 / 24.0)
+            if p.ready and kind == "motion":
+                for j2, t in enumerate(phases):
+                    st.generate(t, j2)
+                mids += len(phases)
+            prev[k] = slot
+    torch.cuda.synchronize()
+    ms = (time.perf_counter() - t0) * 1000.0
+    tot = torch.tensor([ms, float(mids), float(frames * len(sts))], device=dev, dtype=torch.float64)
+    if pg is not None:
+        t = tot[:1].clone()
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        s = tot[1:].clone()
+        pg.all_reduce(s, op=pg.ReduceOp.SUM)
+        tot = torch.cat([t, s])
+    ms, mids_all, src_all = float(tot[0]), float(tot[1]), float(tot[2])
+    del sts, pool
+    torch.cuda.empty_cache()
+    return {"workload": "64 streams x 240 frames at 1920x1080, 24 -> 120 fps (mids at 0.2 / 0.4 / 0.6 / 0.8), scene cut "
+                        "every 48 frames, 2-frame holds every 30, realtime Stream with held-frame detection, sharded by "
+                        "stream", "streams": streams_total, "streams_this_rank": s1 - s0,
+            "generated_frames_per_s": mids_all / (ms / 1000.0), "source_frames_per_s": src_all / (ms / 1000.0),
+            "ms": ms, "generated": int(mids_all), "pairs_by_kind_this_rank": counts, "scaling": "strong",
+            "timing": "wall clock from a barrier to the device synchronize after the last call, max over ranks"}
+
+
 def conv_flops(s, nb: int) -> float:
     """2 * M * 9 * cin * cout summed over the convs of one profiled run at this session's sizes: the encoders of nb + 1
     frames (both frames of one pair when nb is 1, as the reference computes them every pair) and the pair + mid convs
@@ -562,8 +686,8 @@ def render_bytes(p) -> float:
 
 
 def render_design_bytes(p) -> float:
-    """Bytes this design adds to one render beyond the algorithmic ones: the static planes of the padded plane that
-    k_static_planes writes and k_render reads (the own-pixel (es, kk) pair as two f32 and near as u8, 9 B/px)."""
+    """Bytes this design's render reads beyond the algorithmic ones: the static planes of the padded plane that
+    k_static_planes writes (the own-pixel (es, kk) pair as two f32 and near as u8, 9 B/px)."""
     return float(p["hp"] * p["wp"] * 9)
 
 

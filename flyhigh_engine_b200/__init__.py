@@ -26,7 +26,7 @@ from ctypes import (POINTER, Structure, byref, c_char_p, c_double, c_float, c_in
                     c_void_p, create_string_buffer)
 from typing import Optional
 
-__all__ = ["FlyHighError", "Engine", "Model", "Session", "library_path"]
+__all__ = ["FlyHighError", "Engine", "Model", "Session", "Stream", "Classification", "Push", "library_path"]
 
 
 class FlyHighError(RuntimeError):
@@ -44,6 +44,20 @@ class SessionOptions(Structure):  # flyhigh.h FhSessionOptions, field for field
                 ("k", c_uint32), ("repair", c_uint32), ("render", c_uint32), ("keep_static", c_uint32),
                 ("static_frames", c_uint32), ("static_tolerance", c_uint32), ("fast_render", c_uint32),
                 ("linear_t", c_uint32), ("keep_maps", c_uint32), ("protection_mask", c_uint32), ("tune", c_char_p)]
+
+
+class StreamOptions(Structure):  # flyhigh.h FhStreamOptions, field for field
+    _fields_ = [("mode", c_uint32), ("cadence", c_uint32), ("scene_cut", c_double), ("held_frames", c_uint32),
+                ("held_mean", c_double), ("held_max", c_double), ("inputs", c_uint32), ("outputs", c_uint32)]
+
+
+class _Classification(Structure):  # flyhigh.h FhClassification
+    _fields_ = [("kind", c_uint32), ("mean", c_float), ("max", c_float), ("black", c_uint32), ("motion", c_double)]
+
+
+class _Push(Structure):  # flyhigh.h FhPush
+    _fields_ = [("ready", c_uint32), ("base_slot", ctypes.c_int32), ("stats_pending", c_uint32),
+                ("start_pts", c_double), ("end_pts", c_double)]
 
 
 def library_path() -> str:
@@ -98,6 +112,28 @@ EXPORTS = [
     ("fh_session_profile_json", c_int, [c_void_p, c_uint32, c_uint32, c_float, c_uint32, c_char_p, c_size_t]),
     ("fh_session_launch_counts", c_int, [c_void_p, POINTER(c_int), POINTER(c_int), POINTER(c_int)]),
     ("fh_session_profile_batch_json", c_int, [c_void_p, c_char_p, c_size_t]),
+    ("fh_stream_options_default", StreamOptions, []),
+    ("fh_stream_create", c_void_p, [c_void_p, c_void_p, POINTER(SessionOptions), POINTER(StreamOptions)]),
+    ("fh_stream_destroy", None, [c_void_p]),
+    ("fh_stream_add_input", c_int, [c_void_p, c_void_p]),
+    ("fh_stream_add_output", c_int, [c_void_p, c_void_p]),
+    ("fh_stream_next_input", c_int, [c_void_p, POINTER(c_uint32), c_size_t]),
+    ("fh_stream_write_rgba", c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_size_t]),
+    ("fh_stream_write_rgba_device", c_int, [c_void_p, c_uint32, c_void_p, c_size_t]),
+    ("fh_stream_write_mask", c_int, [c_void_p, c_void_p, c_void_p, c_size_t]),
+    ("fh_stream_classify", c_int, [c_void_p, c_void_p, c_uint32, c_uint32, POINTER(_Classification)]),
+    ("fh_stream_push", c_int, [c_void_p, c_void_p, c_uint32, c_double, POINTER(_Push)]),
+    ("fh_stream_resolve_stats", c_int, [c_void_p, c_void_p]),
+    ("fh_stream_real_replaced", c_int, [c_void_p]),
+    ("fh_stream_generate", c_int, [c_void_p, c_void_p, c_float, c_uint32]),
+    ("fh_stream_read_rgba", c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_size_t]),
+    ("fh_stream_warm_up", c_int, [c_void_p, c_void_p]),
+    ("fh_stream_import_d3d11", c_int, [c_void_p, c_void_p, ctypes.c_ssize_t, c_uint32, c_uint32]),
+    ("fh_stream_reset", c_int, [c_void_p]),
+    ("fh_stream_mouse", c_int, [c_void_p, c_void_p, c_double, c_double, c_double]),
+    ("fh_stream_set_mouse_captured", c_int, [c_void_p, c_uint32]),
+    ("fh_stream_warp", c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_uint32, c_double]),
+    ("fh_stream_report_json", c_int, [c_void_p, c_char_p, c_size_t]),
     ("fhk_conv3x3", c_int, [c_void_p, c_int, c_void_p]),
     ("fhk_conv_pack_weights", c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
     ("fhk_conv_packed_elems", c_size_t, [c_int, c_int]),
@@ -431,6 +467,150 @@ class Session:
     def close(self):
         if getattr(self, "_h", None):
             lib().fh_session_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except TypeError:  # interpreter shutdown: the module's globals are already gone, the process frees everything
+            pass
+
+
+_KIND = {0: "motion", 1: "cut", 2: "hold"}
+_MODE = {"realtime": 0, "video": 1}
+
+
+class Classification:
+    """A pair's kind as Stream.classify found it: kind ("motion", "cut" or "hold"), mean and max cell difference (0..1),
+    black (the frames are identical) and motion (the mean in the Pacer's 0..765 units)."""
+
+    def __init__(self, c: _Classification):
+        self.kind = _KIND.get(c.kind, "motion")
+        self.mean, self.max, self.black, self.motion = c.mean, c.max, bool(c.black), c.motion
+
+    def __repr__(self):
+        return f"Classification({self.kind}, mean={self.mean:.4f}, max={self.max:.4f})"
+
+
+class Push:
+    """The interval a Stream.push made ready: ready, base_slot (its real first frame), stats_pending, start_pts,
+    end_pts."""
+
+    def __init__(self, p: _Push):
+        self.ready, self.base_slot, self.stats_pending = bool(p.ready), p.base_slot, bool(p.stats_pending)
+        self.start_pts, self.end_pts = p.start_pts, p.end_pts
+
+    def __repr__(self):
+        return f"Push(ready={self.ready}, base_slot={self.base_slot}, {self.start_pts}..{self.end_pts})"
+
+
+class Stream:
+    """Source frames with timestamps in, generatable intervals out (fh_stream_*).
+
+    Stream(engine, model, width, height, mode="realtime" | "video", cadence=False, scene_cut=0.08 (0: never),
+    held_frames=False | True | {"mean", "max"}, inputs=4, outputs=4, **session options). Realtime runs the pair of the
+    previous and the newest frame at each push; video keeps one frame of lookahead. Re-timing of elements animated on
+    twos (cadence) is not part of this build and is refused."""
+
+    def __init__(self, engine: Engine, model: Model, width: int, height: int, mode: str = "realtime",
+                 cadence: bool = False, scene_cut: float = 0.08, held_frames=False, inputs: int = 4, outputs: int = 4,
+                 **session_opts):
+        L = lib()
+        self._so = session_options(width, height, **session_opts)
+        o = L.fh_stream_options_default()
+        o.mode = _MODE[mode]
+        o.cadence = int(cadence)
+        o.scene_cut = float(scene_cut)
+        o.held_frames = int(bool(held_frames))
+        if isinstance(held_frames, dict):
+            o.held_mean = float(held_frames.get("mean", 0.0))
+            o.held_max = float(held_frames.get("max", 0.0))
+        o.inputs, o.outputs = inputs, outputs
+        self.width, self.height = width, height
+        self._e, self._m = engine, model
+        self._h = L.fh_stream_create(engine._h, model._h, byref(self._so), byref(o))
+        if not self._h:
+            raise _error()
+
+    def add_input(self) -> int:
+        return _check(lib().fh_stream_add_input(self._h, self._e._h))
+
+    def add_output(self) -> int:
+        return _check(lib().fh_stream_add_output(self._h, self._e._h))
+
+    def next_input(self, in_use=()) -> Optional[int]:
+        """The slot to write the next frame into (never one the stream or the host still needs), or None."""
+        arr = (c_uint32 * max(1, len(in_use)))(*in_use)
+        slot = lib().fh_stream_next_input(self._h, arr, len(in_use))  # -1: the ring is exhausted (not an error)
+        return None if slot < 0 else slot
+
+    def write(self, slot: int, rgba) -> None:
+        p, n, _keep = _buffer(rgba)
+        _check(lib().fh_stream_write_rgba(self._h, self._e._h, slot, p, n))
+
+    def write_device(self, slot: int, device_ptr: int, nbytes: int) -> None:
+        """A frame already in device memory (a CUDA pointer) into an input slot."""
+        _check(lib().fh_stream_write_rgba_device(self._h, slot, c_void_p(device_ptr), nbytes))
+
+    def write_mask(self, mask) -> None:
+        p, n, _keep = _buffer(mask)
+        _check(lib().fh_stream_write_mask(self._h, self._e._h, p, n))
+
+    def classify(self, previous: int, slot: int) -> Optional[Classification]:
+        """The kind of the pair (previous, slot) before pushing it; None without a classifier (take it as motion)."""
+        c = _Classification()
+        return Classification(c) if _check(lib().fh_stream_classify(self._h, self._e._h, previous, slot,
+                                                                    byref(c))) == 1 else None
+
+    def push(self, slot: int, pts: float) -> Push:
+        p = _Push()
+        _check(lib().fh_stream_push(self._h, self._e._h, slot, pts, byref(p)))
+        return Push(p)
+
+    def resolve_stats(self) -> None:
+        _check(lib().fh_stream_resolve_stats(self._h, self._e._h))
+
+    def real_replaced(self) -> bool:
+        return bool(_check(lib().fh_stream_real_replaced(self._h)))
+
+    def generate(self, t: float, out: int) -> bool:
+        """True when out holds phase t of the current interval; False when the source frame is enough (t <= 0)."""
+        return _check(lib().fh_stream_generate(self._h, self._e._h, t, out)) == 1
+
+    def read(self, out: int) -> bytes:
+        n = self.width * self.height * 4
+        buf = (c_uint8 * n)()
+        _check(lib().fh_stream_read_rgba(self._h, self._e._h, out, ctypes.cast(buf, c_void_p), n))
+        return bytes(buf)
+
+    def warm_up(self) -> None:
+        _check(lib().fh_stream_warm_up(self._h, self._e._h))
+
+    def reset(self) -> None:
+        _check(lib().fh_stream_reset(self._h))
+
+    def mouse(self, t: float, dx: float, dy: float) -> None:
+        _check(lib().fh_stream_mouse(self._h, self._e._h, t, dx, dy))
+
+    def set_mouse_captured(self, captured: bool) -> None:
+        _check(lib().fh_stream_set_mouse_captured(self._h, int(bool(captured))))
+
+    def warp(self, slot: int, out: int, now: float, output: bool = False) -> bool:
+        """The camera warp of the frame about to be shown; False: present it as it is (always, in this build)."""
+        return _check(lib().fh_stream_warp(self._h, self._e._h, int(output), slot, out, now)) == 1
+
+    def report(self) -> dict:
+        return _json(lib().fh_stream_report_json, self._h)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().fh_stream_destroy(self._h)
             self._h = None
 
     def __enter__(self):

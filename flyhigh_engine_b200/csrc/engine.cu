@@ -31,6 +31,7 @@
 #include "fh_kernels.h"
 #include "json.hpp"
 #include "launch.h"
+#include "session_access.h"
 #include "stages.h"
 #include "tune.hpp"
 
@@ -297,6 +298,7 @@ struct FrameSet {
     // set is read), `released` the last compute launch that reads the set (an upload into it waits for that)
     cudaEvent_t uploaded = nullptr, released = nullptr;
     bool upload_pending = false, ever_read = false;
+    bool dev_written = false;  // the frame came by a device copy on the session stream (after the last host upload)
 };
 
 // An input slot owns one or more frame sets: a write into a set that the current pair or a queued interval reads
@@ -469,6 +471,7 @@ struct FhSession {
     int last_m = 0;       // the intervals of the last batch
     cudaStream_t fst = nullptr, sst = nullptr, rst = nullptr, nst[MAX_SETS] = {};
     cudaEvent_t st_ev = nullptr, join_evs[3 + MAX_SETS] = {};
+    cudaEvent_t access_ev = nullptr;  // fhi::input_frames: another stream after the work issued on st
     FrameSet& arena() { return rsets[rpar].arena; }
     const FrameSet& arena() const { return rsets[rpar].arena; }
     uint8_t* arena_out() const { return rsets[rpar].out; }
@@ -609,6 +612,7 @@ struct FhSession {
                 if (e) cudaEventDestroy(e);
         }
         if (st_ev) cudaEventDestroy(st_ev);
+        if (access_ev) cudaEventDestroy(access_ev);
         for (cudaEvent_t e : join_evs)
             if (e) cudaEventDestroy(e);
         for (auto& kv : mid_graphs) cudaGraphExecDestroy(kv.second);
@@ -1322,6 +1326,7 @@ struct FhSession {
     // a host upload into the set: on the upload stream after the last compute that reads the set; returns once the
     // caller's buffer has been copied
     void upload(FrameSet& fs, const uint8_t* rgba, size_t n) {
+        fs.dev_written = false;
         if (fs.ever_read) CK(cudaStreamWaitEvent(h2d, fs.released, 0));
         CK(cudaMemcpyAsync(fs.frame, rgba, n, cudaMemcpyHostToDevice, h2d));
         CK(cudaEventRecord(fs.uploaded, h2d));
@@ -1931,6 +1936,42 @@ R guard(R fallback, F f) {
 
 }  // namespace
 
+// ---------------------------------------------------------------------------------- the Stream layer's access ----
+
+namespace fhi {
+
+void set_error(const std::string& msg) { g_err = msg; }
+
+void input_frames(FhSession* s, uint32_t a, uint32_t b, cudaStream_t on, const uint8_t** fa, const uint8_t** fb) {
+    s->check_in(a);
+    s->check_in(b);
+    const FrameSet* sets[2] = {&s->cur_set(a), &s->cur_set(b)};
+    bool after_st = false;
+    for (const FrameSet* f : sets) {
+        // a host upload has landed when write_rgba returned; a device copy was issued on the session stream
+        if (f->upload_pending) CK(cudaStreamWaitEvent(on, f->uploaded, 0));
+        after_st = after_st || f->dev_written;
+    }
+    if (after_st) {
+        if (!s->access_ev) CK(cudaEventCreateWithFlags(&s->access_ev, cudaEventDisableTiming));
+        CK(cudaEventRecord(s->access_ev, s->st));
+        CK(cudaStreamWaitEvent(on, s->access_ev, 0));
+    }
+    *fa = sets[0]->frame;
+    *fb = sets[1]->frame;
+}
+
+void session_shape(const FhSession* s, int* w, int* h, int* iw, int* ih, int* k, int* repair) {
+    *w = s->w;
+    *h = s->h;
+    *iw = s->iw;
+    *ih = s->ih;
+    *k = s->k;
+    *repair = s->repair;
+}
+
+}  // namespace fhi
+
 // ------------------------------------------------------------------------------------------------- C exports ----
 
 extern "C" {
@@ -2366,6 +2407,7 @@ int fh_session_write_rgba_device(const FhSession* cs, uint32_t slot, const void*
         FrameSet& fs = s->write_target(slot);
         s->wait_upload(fs);
         CK(cudaMemcpyAsync(fs.frame, dev, n, cudaMemcpyDeviceToDevice, s->st));
+        fs.dev_written = true;
         return 0;
     });
 }

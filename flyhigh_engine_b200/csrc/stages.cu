@@ -1441,10 +1441,13 @@ __global__ void __launch_bounds__(256, 5) k_render(RenderArgs r) {
     const float2 v2r2 = bil_mix2(lo2(U00.w, R00.y), lo2(U01.w, R01.y), lo2(U10.w, R10.y), lo2(U11.w, R11.y), qfx, qfy);
     const float2 r01 = bil_mix2(h2x2(R00.x), h2x2(R01.x), h2x2(R10.x), h2x2(R11.x), qfx, qfy);
     const float f[4] = {f01.x, f01.y, f23.x, f23.y}, v[3] = {v01.x, v01.y, v2r2.x};
+    // the visibility softmax feeds the continuous blend: the fast exponential and one reciprocal, within a few ulps of
+    // expf and the two divisions (both weights share the reciprocal, so the decisive blend's wa >= wb keeps the order
+    // of their numerators)
     const float m = fmaxf(v[0], fmaxf(v[1], v[2]));
-    const float e0 = expf(v[0] - m), e1 = expf(v[1] - m), e2 = expf(v[2] - m);
-    const float s = e0 + e1 + e2;
-    const float wa_w = (e0 + 0.5f * e2) / s, wb_w = (e1 + 0.5f * e2) / s;
+    const float e0 = __expf(v[0] - m), e1 = __expf(v[1] - m), e2 = __expf(v[2] - m);
+    const float inv = __frcp_rn(e0 + e1 + e2);
+    const float wa_w = fmaf(0.5f, e2, e0) * inv, wb_w = fmaf(0.5f, e2, e1) * inv;
     const float gxa = (float)x + f[0], gya = (float)y + f[1], gxb = (float)x + f[2], gyb = (float)y + f[3];
     float3 sa3, sb3;
     if (r.cubic) {
@@ -1467,7 +1470,8 @@ __global__ void __launch_bounds__(256, 5) k_render(RenderArgs r) {
         const float es = ok.x;
         for (int c = 0; c < 3; c++) own[c] = 0.5f * (comp(pa_here, c) + comp(pb_here, c));
         const float ef = fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
-        stillw = fminf(fmaxf((ef - es) / 0.04f, 0.0f), 1.0f) * (es < 0.03f ? 1.0f : 0.0f);
+        // the ramp is continuous: x 25 for / 0.04 (within an ulp; a division costs a dozen instructions)
+        stillw = fminf(fmaxf((ef - es) * 25.0f, 0.0f), 1.0f) * (es < 0.03f ? 1.0f : 0.0f);
     }
     if (r.flags & 1u) {
         const float d = fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
@@ -2043,6 +2047,70 @@ cudaError_t set_scalar(float* dst, float v, cudaStream_t st) {
 
 cudaError_t frame_planes(const uint8_t* f, int w, int h, int hp, int wp, float* out, cudaStream_t st) {
     { const cudaError_t e_ = launch(k_frame_planes, grid2(wp, hp, 1), dim3(16, 16), 0, st, f, w, h, hp, wp, out); if (e_ != cudaSuccess) return e_; }
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------------- classify ----
+
+// One texel channel of an rgba8 frame as the texture unit reads it (unorm: k / 255), clamp to edge.
+FH_DEV float unorm_at(const uint8_t* __restrict__ f, int w, int h, int x, int y, int c) {
+    return (float)__ldg(f + ((size_t)clampi(y, 0, h - 1) * w + clampi(x, 0, w - 1)) * 4 + c) / 255.0f;
+}
+
+// classify.wgsl:13-44: a thread per grid cell, a block per 8 x 9 tile. Each cell takes one bilinear sample of both frames
+// at its centre (textureSampleLevel with a linear sampler: texel coordinates uv * size - 0.5, clamp to edge; here with
+// exact f32 weights), adds the rgb absolute difference in 1/255 steps to stats[0] and maximises stats[1]; the tile's
+// luma changes, summed signed and absolute in cell order by one thread, give stats[2] where they agree in sign
+// (|signed| >= 0.74 total: a flash, not motion).
+__global__ void __launch_bounds__(CLASSIFY_TW * CLASSIFY_TH) k_classify(const uint8_t* __restrict__ fa,
+                                                                      const uint8_t* __restrict__ fb, int w, int h,
+                                                                      int gw, int gh, uint32_t* stats) {
+    __shared__ float luma_change[CLASSIFY_TW * CLASSIFY_TH];
+    pdl_wait();
+    pdl_trigger();
+    const int gx = blockIdx.x * CLASSIFY_TW + threadIdx.x, gy = blockIdx.y * CLASSIFY_TH + threadIdx.y;
+    const int i = threadIdx.y * CLASSIFY_TW + threadIdx.x;
+    float luma = 0.0f;
+    if (gx < gw && gy < gh) {
+        const float u = ((float)gx + 0.5f) / (float)gw, v = ((float)gy + 0.5f) / (float)gh;
+        const float px = u * (float)w - 0.5f, py = v * (float)h - 0.5f;
+        const int x0 = (int)floorf(px), y0 = (int)floorf(py);
+        const float fx = px - (float)x0, fy = py - (float)y0;
+        float d[3];
+        for (int c = 0; c < 3; c++) {  // r, g, b
+            auto samp = [&](const uint8_t* f) {
+                const float top = unorm_at(f, w, h, x0, y0, c) * (1.0f - fx) + unorm_at(f, w, h, x0 + 1, y0, c) * fx;
+                const float bot = unorm_at(f, w, h, x0, y0 + 1, c) * (1.0f - fx) + unorm_at(f, w, h, x0 + 1, y0 + 1, c) * fx;
+                return top * (1.0f - fy) + bot * fy;
+            };
+            d[c] = samp(fb) - samp(fa);
+        }
+        const float s = fabsf(d[0]) * 255.0f + fabsf(d[1]) * 255.0f + fabsf(d[2]) * 255.0f;
+        const uint32_t cell = (uint32_t)s;  // u32(): toward zero
+        atomicAdd(stats, cell);
+        atomicMax(stats + 1, cell);
+        luma = d[0] * 0.2126f + d[1] * 0.7152f + d[2] * 0.0722f;
+    }
+    luma_change[i] = luma;
+    __syncthreads();
+    if (i == 0) {
+        float sgn = 0.0f, total = 0.0f;
+        for (int j = 0; j < CLASSIFY_TW * CLASSIFY_TH; j++) {
+            sgn += luma_change[j];
+            total += fabsf(luma_change[j]);
+        }
+        if (fabsf(sgn) >= 0.74f * total)
+            atomicMax(stats + 2, (uint32_t)rintf(fabsf(sgn) * 255.0f / 72.0f));  // round(): half to even
+    }
+}
+
+cudaError_t classify(const uint8_t* fa, const uint8_t* fb, int w, int h, int gw, int gh, uint32_t* stats, cudaStream_t st) {
+    if (w < 1 || h < 1 || gw < 1 || gh < 1) return cudaErrorInvalidValue;
+    cudaError_t e = cudaMemsetAsync(stats, 0, 3 * sizeof(uint32_t), st);
+    if (e != cudaSuccess) return e;
+    e = launch(k_classify, dim3((gw + CLASSIFY_TW - 1) / CLASSIFY_TW, (gh + CLASSIFY_TH - 1) / CLASSIFY_TH),
+               dim3(CLASSIFY_TW, CLASSIFY_TH), 0, st, fa, fb, w, h, gw, gh, stats);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

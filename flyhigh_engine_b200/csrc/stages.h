@@ -212,4 +212,10 @@ cudaError_t set_scalar(float* dst, float v, cudaStream_t st);
 // tex_in.wgsl: rgba8 -> padded f16 planes are never materialised; this reads one for tests: [3][hp][wp] f32 BGR
 cudaError_t frame_planes(const uint8_t* f, int w, int h, int hp, int wp, float* out, cudaStream_t st);
 
+// classify.wgsl (the Stream's pair classifier, stream/classify.rs): two rgba8 frames (w x h) sampled bilinearly at the
+// centres of a gw x gh grid; stats[0] += each cell's rgb absolute difference in 1/255 steps (0..765), stats[1] = the
+// largest, stats[2] = the strongest coherent brightness change of an 8 x 9 tile of cells. stats is zeroed here first.
+constexpr int CLASSIFY_TW = 8, CLASSIFY_TH = 9;
+cudaError_t classify(const uint8_t* fa, const uint8_t* fb, int w, int h, int gw, int gh, uint32_t* stats, cudaStream_t st);
+
 }  // namespace fhk

@@ -8,7 +8,9 @@ in for them:
   - sequence_c2(): config 2, a moving sequence whose pan velocity random-walks by +-2 px per frame, with 5 moving
     rectangles and a static 300 x 60 high-contrast HUD overlay at the bottom-left (noise-free, like a rendered HUD);
   - sequence_c3(): config 3, a camera pan of up to +-40 px per frame over a texture and a fence (a 32-px-period grid of
-    bars) covering 30 % of the frame, the periodic structure the repair stage exists for.
+    bars) covering 30 % of the frame, the periodic structure the repair stage exists for;
+  - stream_c4(): config 4's frame order for one stream: scenes of `cut_every` frames (a new seeded scene at each cut),
+    2-frame held runs every `hold_every` frames (the frame after a run's first repeats it, anime on twos).
 Every frame is (h, w, 4) uint8 with alpha 255.
 """
 from __future__ import annotations
@@ -127,6 +129,17 @@ def sequence_c3(n: int = 60, w: int = 3840, h: int = 2160, seed: int = 0):
         img[f0:f0 + fh] = fence[m + py + f0:m + py + f0 + fh, m + px:m + px + w]
         frames.append(_finish(img, rng))
     return frames
+
+
+def stream_c4(n: int = 240, cut_every: int = 48, hold_every: int = 30, scenes: int = 5, offset: int = 0):
+    """Config 4's frame order for one stream: [(scene, frame within the scene)] for its n frames. Scene changes (cuts)
+    every `cut_every` frames, starting at scene `offset`; frame i with i % hold_every == 1 repeats frame i - 1 (a 2-frame
+    held run). The frames themselves come from per-scene sequences (sequence_c2 with the scene as seed)."""
+    order = []
+    for i in range(n):
+        j = i - 1 if i % hold_every == 1 else i
+        order.append(((j // cut_every + offset) % scenes, j % cut_every))
+    return order
 
 
 def sinusoid_pair(w: int, h: int, dx: float):

@@ -92,6 +92,68 @@ int fh_session_warm_up(FhSession* session); /* builds every CUDA graph before th
 int fh_session_import_d3d11(FhSession* session, const FhEngine* engine, intptr_t handle, uint32_t width, uint32_t height);
 int fh_session_report_json(const FhSession* session, char* buf, size_t cap);
 
+/* ---- Stream: source frames with timestamps in, intervals out (flyhigh.h:101-152, capi/src/stream.rs) ----
+ * A Stream owns one session of the options given, its input ring and output slots. Realtime mode runs the pair
+ * (previous, newest) when a frame is pushed; video mode keeps one frame of lookahead (the interval that can be generated
+ * after a push starts two frames back). Pairs are classified (motion, scene cut, held frame) on the GPU. The camera
+ * warp (fh_stream_mouse / _warp) is not part of this build: fh_stream_warp always answers 0 (present the frame as it is)
+ * and cadence re-timing (video mode) is refused at creation. Single-threaded use per handle; NULL / -1 and
+ * fh_last_error on failure. */
+typedef struct FhStream FhStream;
+
+typedef struct FhStreamOptions {
+    uint32_t mode;              /* 0 realtime (default), 1 video (one frame of lookahead) */
+    uint32_t cadence;           /* must be 0 here (re-timing of elements animated on twos is not part of this build) */
+    double   scene_cut;         /* mean-difference threshold (0..1) above which a pair is a cut; 0 = never (default 0.08) */
+    uint32_t held_frames;       /* 1 = detect repeated frames (default 0) */
+    double   held_mean, held_max;   /* their thresholds; 0 = the defaults 0.0033 / 0.06 */
+    uint32_t inputs, outputs;   /* slots created up front (default 4 / 4) */
+} FhStreamOptions;
+
+typedef struct FhClassification {
+    uint32_t kind;              /* 0 motion, 1 scene cut, 2 held frame */
+    float    mean, max;         /* mean and largest per-cell difference, 0..1 */
+    uint32_t black;             /* 1 = the frames are identical */
+    double   motion;            /* the Pacer's motion units (0..765) */
+} FhClassification;
+
+typedef struct FhPush {
+    uint32_t ready;             /* 1 = an interval can be generated now */
+    int32_t  base_slot;         /* the real frame that starts it */
+    uint32_t stats_pending;     /* always 0 here (no cadence statistics) */
+    double   start_pts, end_pts;
+} FhPush;
+
+FhStreamOptions fh_stream_options_default(void);
+FhStream* fh_stream_create(const FhEngine* engine, const FhModel* model, const FhSessionOptions* session,
+                           const FhStreamOptions* options);
+void fh_stream_destroy(FhStream* stream);
+int fh_stream_add_input(FhStream* stream, const FhEngine* engine);
+int fh_stream_add_output(FhStream* stream, const FhEngine* engine);
+/* the slot to write the next frame into: never one the stream still reads nor one of the n slots in in_use; -1 = add
+ * inputs */
+int fh_stream_next_input(FhStream* stream, const uint32_t* in_use, size_t n);
+int fh_stream_write_rgba(const FhStream* stream, const FhEngine* engine, uint32_t slot, const uint8_t* rgba, size_t len);
+int fh_stream_write_mask(const FhStream* stream, const FhEngine* engine, const uint8_t* mask, size_t len);
+/* the pair (previous, slot) before pushing it, waiting for the GPU: 1 = out filled, 0 = no classifier (take it as
+ * motion), -1 = error */
+int fh_stream_classify(FhStream* stream, const FhEngine* engine, uint32_t previous, uint32_t slot, FhClassification* out);
+/* the newest frame is in slot with timestamp pts (the host's units): runs its pair; 0 / -1 */
+int fh_stream_push(FhStream* stream, const FhEngine* engine, uint32_t slot, double pts, FhPush* out);
+int fh_stream_resolve_stats(FhStream* stream, const FhEngine* engine);   /* 0: no statistics are ever pending */
+int fh_stream_real_replaced(const FhStream* stream);                      /* 0: the real frame is never re-timed */
+/* phase t of the current interval into out: 1 = written, 0 = the source frame is enough (t <= 0), -1 = error */
+int fh_stream_generate(FhStream* stream, const FhEngine* engine, float t, uint32_t out);
+int fh_stream_read_rgba(const FhStream* stream, const FhEngine* engine, uint32_t out, uint8_t* buf, size_t cap);
+int fh_stream_warm_up(FhStream* stream, const FhEngine* engine);
+int fh_stream_import_d3d11(FhStream* stream, const FhEngine* engine, intptr_t handle, uint32_t width, uint32_t height);
+int fh_stream_reset(FhStream* stream); /* seek, decoder gap */
+/* camera warp: mouse input is recorded (the report shows it) but no frame is turned: warp answers 0 */
+int fh_stream_mouse(FhStream* stream, const FhEngine* engine, double t, double dx, double dy);
+int fh_stream_set_mouse_captured(FhStream* stream, uint32_t captured);
+int fh_stream_warp(FhStream* stream, const FhEngine* engine, uint32_t output, uint32_t slot, uint32_t out, double now);
+int fh_stream_report_json(const FhStream* stream, char* buf, size_t cap);
+
 #ifdef __cplusplus
 }
 #endif

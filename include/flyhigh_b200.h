@@ -94,6 +94,11 @@ long long fh_session_kernel_launches(const FhSession* session);
 /* Kernel launches of one pair and of one mid (the nodes of their CUDA graphs). 0 on success. */
 int fh_session_launch_counts(const FhSession* session, int* pair_kernels, int* mid_kernels, int* frame_kernels);
 
+/* A frame already in device memory (a CUDA pointer, width * height * 4 bytes) into an input slot of a Stream, as
+ * fh_session_write_rgba_device does for a session: copied on the stream's session stream. 0, or -1 with
+ * fh_last_error. */
+int fh_stream_write_rgba_device(const FhStream* stream, uint32_t slot, const void* dev, size_t len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1792,6 +1792,65 @@ int or_render_diag(const uint8_t* fa, const uint8_t* fb, int w, int h, const flo
 
 int or_render_diag_size() { return RENDER_DIAG; }
 
+// classify.wgsl:13-44 (the Stream's pair classifier, stream/classify.rs:17-21 grid 48 x 27): frames a, b (w x h rgba8)
+// sampled bilinearly (texel coordinates uv * size - 0.5, clamp to edge, f32 weights) at the centre of each cell of a
+// gw x gh grid; out[0] = the sum over cells of u32(dot(|b - a|.rgb, 255)), out[1] = its largest cell, out[2] = the
+// largest round(|signed luma change| * 255 / 72) over the 8 x 9 tiles whose luma changes agree in sign (|signed| >=
+// 0.74 of their absolute sum).
+int or_classify(const uint8_t* fa, const uint8_t* fb, int w, int h, int gw, int gh, uint32_t* out) {
+    if (w < 1 || h < 1 || gw < 1 || gh < 1) {
+        g_err = "classify: empty frame or grid";
+        return -1;
+    }
+    auto texel = [&](const uint8_t* f, int x, int y, int c) {
+        x = std::max(0, std::min(x, w - 1));
+        y = std::max(0, std::min(y, h - 1));
+        return (float)f[((size_t)y * w + x) * 4 + c] / 255.0f;
+    };
+    uint32_t sum = 0, mx = 0, tile = 0;
+    const int TW = 8, TH = 9;
+    for (int ty = 0; ty < (gh + TH - 1) / TH; ty++)
+        for (int tx = 0; tx < (gw + TW - 1) / TW; tx++) {
+            float luma[72];
+            for (int ly = 0; ly < TH; ly++)
+                for (int lx = 0; lx < TW; lx++) {
+                    const int gx = tx * TW + lx, gy = ty * TH + ly;
+                    float l = 0.0f;
+                    if (gx < gw && gy < gh) {
+                        const float u = ((float)gx + 0.5f) / (float)gw, v = ((float)gy + 0.5f) / (float)gh;
+                        const float px = u * (float)w - 0.5f, py = v * (float)h - 0.5f;
+                        const int x0 = (int)floorf(px), y0 = (int)floorf(py);
+                        const float fx = px - (float)x0, fy = py - (float)y0;
+                        float d[3];
+                        for (int c = 0; c < 3; c++) {
+                            auto samp = [&](const uint8_t* f) {
+                                const float top = texel(f, x0, y0, c) * (1.0f - fx) + texel(f, x0 + 1, y0, c) * fx;
+                                const float bot = texel(f, x0, y0 + 1, c) * (1.0f - fx) + texel(f, x0 + 1, y0 + 1, c) * fx;
+                                return top * (1.0f - fy) + bot * fy;
+                            };
+                            d[c] = samp(fb) - samp(fa);
+                        }
+                        const float s = fabsf(d[0]) * 255.0f + fabsf(d[1]) * 255.0f + fabsf(d[2]) * 255.0f;
+                        const uint32_t cell = (uint32_t)s;
+                        sum += cell;
+                        mx = std::max(mx, cell);
+                        l = d[0] * 0.2126f + d[1] * 0.7152f + d[2] * 0.0722f;
+                    }
+                    luma[ly * TW + lx] = l;
+                }
+            float sg = 0.0f, total = 0.0f;
+            for (int j = 0; j < 72; j++) {
+                sg += luma[j];
+                total += fabsf(luma[j]);
+            }
+            if (fabsf(sg) >= 0.74f * total) tile = std::max(tile, (uint32_t)rintf(fabsf(sg) * 255.0f / 72.0f));
+        }
+    out[0] = sum;
+    out[1] = mx;
+    out[2] = tile;
+    return 0;
+}
+
 // The repair stage's select decisions and margins (gm_run's sel_out: 4 floats per E8 pixel) for a given pre-repair
 // flow flow_pre [4][h8][w8] (f32 values of f16) on the session's last pair (its internal-size frames A and B). Test
 // diagnostics: with another implementation's pre-repair flow it tells which cells that implementation's repair

@@ -55,6 +55,7 @@ def lib():
         L.or_render_diag.argtypes = L.or_render_planes.argtypes[:-1] + [c_int, POINTER(c_int), POINTER(c_float)]
         L.or_render_diag_size.restype = c_int
         L.or_gmhs_select.argtypes = [c_void_p, POINTER(c_float), c_int, c_int, POINTER(c_float)]
+        L.or_classify.argtypes = [POINTER(c_uint8), POINTER(c_uint8), c_int, c_int, c_int, c_int, POINTER(ctypes.c_uint32)]
         L.or_tex_down.argtypes = [POINTER(c_uint8), c_int, c_int, c_int, c_int, POINTER(c_uint16)]
         L.or_interp.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, c_int, c_int, c_int, c_float, POINTER(c_uint16)]
         L.or_warp.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, POINTER(c_uint16), c_float, POINTER(c_uint16)]
@@ -278,3 +279,66 @@ def tex_down(frame, w, h, oh, ow):
     if lib().or_tex_down(_u8(f), w, h, oh, ow, out.ctypes.data_as(POINTER(c_uint16))) != 0:
         raise RuntimeError(lib().or_error().decode())
     return out.reshape(3, oh, ow)
+
+
+# ---- the Stream's pair classifier (crates/flyhigh-engine/src/stream/classify.rs) ----
+
+CLASSIFY_GRID = (48, 27)
+
+
+def classify_stats(fa, fb, w, h, grid=CLASSIFY_GRID):
+    """classify.wgsl on two rgba8 frames: (sum of the cells' rgb differences in 1/255 steps, the largest cell, the
+    strongest coherent tile luma change)."""
+    fa = np.ascontiguousarray(fa, np.uint8)
+    fb = np.ascontiguousarray(fb, np.uint8)
+    out = (ctypes.c_uint32 * 3)()
+    if lib().or_classify(_u8(fa), _u8(fb), w, h, grid[0], grid[1], out) != 0:
+        raise RuntimeError(lib().or_error().decode())
+    return int(out[0]), int(out[1]), int(out[2])
+
+
+class Classifier:
+    """classify.rs's decisions on the kernel's sums, with their history (Classification::from_stats, with_history,
+    after, after_hold; Classifier::begin's bookkeeping of the last moving pair and the last held one), in f32 as the
+    reference computes them."""
+
+    CELL_MAX = np.float32(765.0)
+    FLASH_LUMA, FLASH_MEAN, CUT_AFTER_CALM = 32, np.float32(0.045), np.float32(0.5)
+
+    def __init__(self, scene_cut=0.08, held_frames=None, cadence=False):
+        self.cut = None if not scene_cut else np.float32(scene_cut)
+        self.hold = None
+        if held_frames:
+            h = held_frames if isinstance(held_frames, dict) else {}
+            self.hold = (np.float32(h.get("mean") or 0.0033), np.float32(h.get("max") or 0.06))
+        self.step_after_hold = self.hold is not None and not cadence
+        self.last_moving = None
+        self.last_held = False
+
+    def decide(self, stats, cells=CLASSIFY_GRID[0] * CLASSIFY_GRID[1]):
+        s, mx, tile = stats
+        mean = np.float32(np.float32(s) / np.float32(max(cells, 1))) / self.CELL_MAX
+        mean = np.float32(mean)
+        mxf = np.float32(np.float32(mx) / self.CELL_MAX)
+        kind = "motion"
+        if self.cut is not None and mean > self.cut:
+            kind = "cut"
+        elif self.hold is not None and mean < self.hold[0] and mxf < self.hold[1]:
+            kind = "hold"
+        if self.cut is not None and mean >= self.FLASH_MEAN and tile >= self.FLASH_LUMA:
+            kind = "cut"
+        elif kind == "cut" and self.cut is not None and self.last_moving is not None and \
+                self.last_moving >= self.cut * self.CUT_AFTER_CALM:
+            kind = "motion"
+        held = kind == "hold"
+        if not held:
+            self.last_moving = mean
+        if self.step_after_hold and self.last_held and kind == "motion":
+            kind = "cut"
+        self.last_held = held
+        return {"kind": kind, "mean": float(mean), "max": float(mxf), "black": bool(mxf == 0.0),
+                "motion": float(np.float64(mean) * 765.0)}
+
+    def forget(self):
+        self.last_moving = None
+        self.last_held = False

@@ -1,4 +1,4 @@
-/* Prints sizeof / offsetof of every field of the C ABI's option structs, one "name value" per line. The test suite
+/* Prints sizeof / offsetof of every field of the C ABI's structs, one "name value" per line. The test suite
  * compiles this file twice, once against this repository's include/flyhigh.h and once against the reference's own
  * header, and requires the two listings to be identical (byte-for-byte struct layout of the drop-in). */
 #include <stddef.h>
@@ -34,5 +34,26 @@ int main(void) {
     F(FhSessionOptions, keep_maps);
     F(FhSessionOptions, protection_mask);
     F(FhSessionOptions, tune);
+    printf("FhStreamOptions %zu %zu\n", sizeof(FhStreamOptions), _Alignof(FhStreamOptions));
+    F(FhStreamOptions, mode);
+    F(FhStreamOptions, cadence);
+    F(FhStreamOptions, scene_cut);
+    F(FhStreamOptions, held_frames);
+    F(FhStreamOptions, held_mean);
+    F(FhStreamOptions, held_max);
+    F(FhStreamOptions, inputs);
+    F(FhStreamOptions, outputs);
+    printf("FhClassification %zu %zu\n", sizeof(FhClassification), _Alignof(FhClassification));
+    F(FhClassification, kind);
+    F(FhClassification, mean);
+    F(FhClassification, max);
+    F(FhClassification, black);
+    F(FhClassification, motion);
+    printf("FhPush %zu %zu\n", sizeof(FhPush), _Alignof(FhPush));
+    F(FhPush, ready);
+    F(FhPush, base_slot);
+    F(FhPush, stats_pending);
+    F(FhPush, start_pts);
+    F(FhPush, end_pts);
     return 0;
 }

@@ -45,6 +45,45 @@ RENDER_GAP = 1       # levels between the GPU frame and the oracle's render of t
 KEYS_SLOPE = 2.0625  # Keys a = -0.75: max sum |w| (1.375) x max sum |w'| (3) / 2
 
 
+# layers the repair stage's flow reaches: the repaired E8 flow and everything the mid network derives from it
+POST_REPAIR = {"flow", "vis", "hm", "fh1", "fh2", "dfilm", "ft_vt", "up7", "rx", "rq1", "rq2", "rq3", "R_t"}
+
+
+def flipped_cells(gmhs):
+    """The E8 cells whose repair decision differs between the two runs' records ((oracle, gpu) gmhs_select)."""
+    if gmhs is None:
+        return np.zeros((0, 2), np.int64)
+    return np.argwhere(gmhs[0]["sel"] != gmhs[1]["sel"])
+
+
+def layer_rel_l2(name, got, ref, flipped, h8):
+    """Relative L2 of a layer, leaving out the positions that a flipped repair cell reaches (GMHS_REACH E8 cells, at
+    the layer's own resolution) when the layer comes after the repair stage: two repairs that choose differently at a
+    threshold differ there by more than dmin px of flow, as much as their choices do."""
+    from tests.parity import rel_l2
+    got, ref = np.asarray(got), np.asarray(ref)
+    if name not in POST_REPAIR or len(flipped) == 0:
+        return rel_l2(got, ref)
+    _, h, w = ref.shape
+    scale = max(1, int(round(h / h8)))  # E8 layers 1, quarter-resolution layers 2
+    keep = np.ones((h, w), bool)
+    r = GMHS_REACH * scale
+    for i, j in flipped.tolist():
+        ci, cj = i * scale, j * scale
+        keep[max(ci - r, 0):ci + r + scale, max(cj - r, 0):cj + r + scale] = False
+    return rel_l2(got[:, keep], ref[:, keep])
+
+
+def reach_mask(flipped, w, h, pp):
+    """The frame's pixels (h x w bool) within GMHS_REACH E8 cells of a flipped repair cell."""
+    yy, xx = np.mgrid[0:h, 0:w]
+    ci, cj = _e8_of(xx.reshape(-1), yy.reshape(-1), pp["fsx"], pp["fsy"], pp["w8"], pp["h8"])
+    reach = np.zeros(h * w, bool)
+    for (i, j) in np.asarray(flipped).tolist():
+        reach |= (np.abs(ci - i) <= GMHS_REACH) & (np.abs(cj - j) <= GMHS_REACH)
+    return reach.reshape(h, w)
+
+
 def _e8_of(xs, ys, fsx, fsy, w8, h8):
     """The E8 cell (i, j) under full-resolution pixels: full -> internal (/ fs) -> E8 (/ 8)."""
     j = np.clip(np.floor((xs + 0.5) / fsx / 8.0).astype(np.int64), 0, w8 - 1)
@@ -170,12 +209,8 @@ def check_frame(got, ref, fa, fb, w, h, pp, gpu_maps, ora_maps, age, gmhs=None, 
     # dmin px, so the frame there differs as much as two repairs' choices do); the whole frame's PSNR is reported too
     psnr_rest = psnr
     if len(flipped) and not gm_bad:
-        yy, xx = np.mgrid[0:H, 0:W]
-        ci, cj = _e8_of(xx.reshape(-1), yy.reshape(-1), pp["fsx"], pp["fsy"], pp["w8"], pp["h8"])
-        reach = np.zeros(H * W, bool)
-        for (i, j) in flipped.tolist():
-            reach |= (np.abs(ci - i) <= GMHS_REACH) & (np.abs(cj - j) <= GMHS_REACH)
-        keep = ~reach.reshape(H, W)
+        reach = reach_mask(flipped, W, H, pp)
+        keep = ~reach
         diff = (g - r).astype(np.float64)[keep]
         mse = float((diff ** 2).mean()) if diff.size else 0.0
         psnr_rest = float("inf") if mse == 0 else float(10 * np.log10(255.0 ** 2 / mse))

@@ -23,7 +23,7 @@ from ctypes import POINTER, Structure, c_float, c_int, c_longlong, c_void_p
 import numpy as np
 import pytest
 
-from tests.frame_parity import check_frame
+from tests.frame_parity import check_frame, flipped_cells, layer_rel_l2
 from tests.parity import FRAME_MAX_ABS, FRAME_PSNR_DB, LAYER_REL_L2, frame_stats, rel_l2
 
 pytestmark = pytest.mark.gpu
@@ -240,6 +240,7 @@ def _session_pair(model_dir, w, h, frames, t=0.5, check_age=False, mask=None, **
             assert np.array_equal(age, o.tensor("age")), f"age differs after pair {i + 1}"
         rep = check_frame(got, ref, fa, fb, w, h, pp, (s.tensor("up7"), s.tensor("R_t")),
                           (o.tensor("up7", 1), o.tensor("R_t", 1)), age, gm)
+        rep["flipped"] = flipped_cells(gm)  # the repair cells decided differently (for the layer checks)
         results.append((got, ref, rep))
     return s, o, results, (eng, model, om, s0)
 
@@ -249,13 +250,17 @@ PAIR_LAYERS = ["A", "B", "aq", "bq", "i8a", "i8b", "i16a", "i16b", "f8a", "f8b",
 MID_LAYERS = ["hm", "fh1", "fh2", "dfilm", "ft_vt", "up7", "rx", "rq1", "rq2", "rq3", "R_t"]
 
 
-def _check_layers(s, o, names, stage, tol=LAYER_REL_L2):
+def _check_layers(s, o, names, stage, tol=LAYER_REL_L2, flipped=None):
+    """Each layer within tol relative L2 of the oracle's; a layer after the repair stage leaves out what the repair
+    cells in `flipped` (decided differently by the two runs, at a threshold) reach."""
     worst = {}
+    h8 = s.tensor("flow").shape[1]
+    fl = np.zeros((0, 2), np.int64) if flipped is None else flipped
     for n in names:
         got = s.tensor(n)
         ref = o.tensor(n, stage)
         assert got.shape == ref.shape, (n, got.shape, ref.shape)
-        worst[n] = rel_l2(got, ref)
+        worst[n] = layer_rel_l2(n, got, ref, fl, h8)
     bad = {k: v for k, v in worst.items() if v > tol}
     assert not bad, f"layers above {tol}: {bad} (all: {worst})"
     return worst
@@ -266,8 +271,8 @@ def test_session_c0_layers_and_frame(synth_model_dir):
     from flyhigh_engine_b200 import synth_frames
     fa, fb, _ = synth_frames.pair_c0(640, 360, seed=0)
     s, o, res, _keep = _session_pair(synth_model_dir, 640, 360, [(fa, fb)])
-    _check_layers(s, o, PAIR_LAYERS, 0)
-    _check_layers(s, o, MID_LAYERS, 1)
+    _check_layers(s, o, PAIR_LAYERS, 0, flipped=res[0][2]["flipped"])
+    _check_layers(s, o, MID_LAYERS, 1, flipped=res[0][2]["flipped"])
     got, ref, rep = res[0]
     mx, p = frame_stats(got, ref)
     assert mx <= FRAME_MAX_ABS and p >= FRAME_PSNR_DB, (mx, p)
@@ -295,14 +300,19 @@ def test_session_1080p_frame(synth_model_dir, monkeypatch):
         assert rep["ok"], rep
 
 
-def _frame_ok(got, ref):
+def _frame_ok(got, ref, keep=None):
     """The fast render's end-to-end criterion (its own render has no decision record in the oracle): PSNR >= 50 dB and
-    at most 1e-3 of the channels beyond 2 levels; returns (ok, (PSNR, fraction beyond 2 levels, max |diff|)). The fast
-    render on identical inputs is checked to 1 level separately; the exact render's frames go through check_frame."""
+    at most 1e-3 of the channels beyond 2 levels, over the pixels `keep` (default all: the ones no repair cell flipped
+    at a threshold reaches); returns (ok, (PSNR, fraction beyond 2 levels, max |diff|)). The fast render on identical
+    inputs is checked to 1 level separately; the exact render's frames go through check_frame."""
     g = np.asarray(got, np.int32).reshape(-1, 4)[:, :3]
     r = np.asarray(ref, np.int32).reshape(-1, 4)[:, :3]
+    if keep is not None:
+        g, r = g[keep.reshape(-1)], r[keep.reshape(-1)]
     over = float((np.abs(g - r) > FRAME_MAX_ABS).mean())
-    mx, p = frame_stats(got, ref)
+    mx = int(np.abs(g - r).max())
+    mse = float(((g - r).astype(np.float64) ** 2).mean())
+    p = float("inf") if mse == 0 else 10 * np.log10(255.0 ** 2 / mse)
     return p >= FRAME_PSNR_DB and over <= 1e-3, (p, over, mx)
 
 
@@ -627,27 +637,34 @@ def test_fast_session_matches_oracle(synth_model_dir, size, opts):
     import flyhigh_engine_b200 as fh
     from flyhigh_engine_b200 import synth_frames
     from oracle.oracle import OracleModel, OracleSession
+    from tests.frame_parity import reach_mask
     w, h = size
     frames = synth_frames.sequence_c2(4, w, h, seed=7)
-    s = fh.Session(fh.Engine(), fh.Model(synth_model_dir), w, h, **opts)
-    slots = [s.add_input(), s.add_input()]
+    model = fh.Model(synth_model_dir)
+    pp = model.plan_params(w, h, **opts)
+    s = fh.Session(fh.Engine(), model, w, h, **opts)
+    s0 = fh.Session(fh.Engine(), model, w, h, repair=0, **opts)  # the GPU's pre-repair flow
+    slots, slots0 = [s.add_input(), s.add_input()], [s0.add_input(), s0.add_input()]
     out = s.add_output()
     o = OracleSession(OracleModel(synth_model_dir), w, h, **opts)
     s.write(slots[0], frames[0])
+    s0.write(slots0[0], frames[0])
     for i in range(1, len(frames)):
-        a, b = slots[(i - 1) % 2], slots[i % 2]
-        s.write(b, frames[i])
-        s.pair(a, b)
+        for ss, sl in ((s, slots), (s0, slots0)):
+            ss.write(sl[i % 2], frames[i])
+            ss.pair(sl[(i - 1) % 2], sl[i % 2])
         o.pair(frames[i - 1], frames[i])
+        fl = flipped_cells((o.gmhs_select(o.tensor("flow_pre")), o.gmhs_select(s0.tensor("flow"))))
+        keep = ~reach_mask(fl, w, h, pp) if len(fl) else None
         _check_layers(s, o, ["A", "B", "o", "fr3"], 0)
         assert np.array_equal(s.tensor("age")[:, :h, :w], o.tensor("age")[:, :h, :w]), f"age differs after pair {i}"
         for t in (0.25, 0.5, 0.75):
             s.mid(t, out)
             got = np.frombuffer(s.read(out), np.uint8)
             ref = o.mid(t)
-            ok, info = _frame_ok(got, ref)
-            assert ok, (i, t, info)
-        _check_layers(s, o, ["up7", "R_t"], 1)
+            ok, info = _frame_ok(got, ref, keep)
+            assert ok, (i, t, info, len(fl))
+        _check_layers(s, o, ["up7", "R_t"], 1, flipped=fl)
 
 
 def test_batched_fast_matches_single(synth_model_dir):
