@@ -297,47 +297,88 @@ def classify_stats(fa, fb, w, h, grid=CLASSIFY_GRID):
     return int(out[0]), int(out[1]), int(out[2])
 
 
-class Classifier:
-    """classify.rs's decisions on the kernel's sums, with their history (Classification::from_stats, with_history,
-    after, after_hold; Classifier::begin's bookkeeping of the last moving pair and the last held one), in f32 as the
-    reference computes them."""
+class Classification:
+    """classify.rs's Classification: kind, mean and max in 0..1 (f32 values), black, motion (the Pacer's units)."""
 
-    CELL_MAX = np.float32(765.0)
-    FLASH_LUMA, FLASH_MEAN, CUT_AFTER_CALM = 32, np.float32(0.045), np.float32(0.5)
+    def __init__(self, kind, mean, mx):
+        self.kind, self.mean, self.max = kind, np.float32(mean), np.float32(mx)
+        self.black = bool(self.max == 0.0)
+        self.motion = float(np.float64(self.mean) * 765.0)
+
+    def as_dict(self):
+        return {"kind": self.kind, "mean": float(self.mean), "max": float(self.max), "black": self.black,
+                "motion": self.motion}
+
+
+class Thresholds:
+    """classify.rs:38-49: cut_mean (None = never), hold_mean (None = no held frames), hold_max, step_after_hold."""
+
+    def __init__(self, cut_mean=0.08, hold_mean=None, hold_max=0.0, step_after_hold=False):
+        self.cut = None if cut_mean is None else np.float32(cut_mean)
+        self.hold = None if hold_mean is None else np.float32(hold_mean)
+        self.hold_max = np.float32(hold_max)
+        self.step_after_hold = step_after_hold
+
+
+CELL_MAX = np.float32(765.0)
+FLASH_LUMA, FLASH_MEAN, CUT_AFTER_CALM = 32, np.float32(0.045), np.float32(0.5)
+
+
+def from_stats(s, mx, cells, th):
+    """classify.rs:65-80: the kind from the kernel's sums (f32 as the reference divides)."""
+    mean = np.float32(np.float32(np.float32(s) / np.float32(max(cells, 1))) / CELL_MAX)
+    mxf = np.float32(np.float32(mx) / CELL_MAX)
+    kind = "motion"
+    if th.cut is not None and mean > th.cut:
+        kind = "cut"
+    elif th.hold is not None and mean < th.hold and mxf < th.hold_max:
+        kind = "hold"
+    return Classification(kind, mean, mxf)
+
+
+def after_hold(c, held_before, th):
+    """classify.rs:86-91: a change right after a held frame is shown as drawn (a cut)."""
+    if th.step_after_hold and held_before and c.kind == "motion":
+        return Classification("cut", c.mean, c.max)
+    return c
+
+
+def after(c, before, th):
+    """classify.rs:95-102: a cut right after a moving pair (mean >= half the threshold) is a fast camera move."""
+    if c.kind == "cut" and th.cut is not None and before is not None and np.float32(before) >= th.cut * CUT_AFTER_CALM:
+        return Classification("motion", c.mean, c.max)
+    return c
+
+
+def with_history(c, tile_luma, before, th):
+    """classify.rs:104-111: a coherent brightness step (a flash) is a cut, else after()."""
+    if th.cut is not None and c.mean >= FLASH_MEAN and tile_luma >= FLASH_LUMA:
+        return Classification("cut", c.mean, c.max)
+    return after(c, before, th)
+
+
+class Classifier:
+    """classify.rs's Classifier bookkeeping (begin's readback closure, :196-207): each pair's decision from the
+    kernel's sums with the last moving pair's mean and whether the last pair was held."""
 
     def __init__(self, scene_cut=0.08, held_frames=None, cadence=False):
-        self.cut = None if not scene_cut else np.float32(scene_cut)
-        self.hold = None
-        if held_frames:
-            h = held_frames if isinstance(held_frames, dict) else {}
-            self.hold = (np.float32(h.get("mean") or 0.0033), np.float32(h.get("max") or 0.06))
-        self.step_after_hold = self.hold is not None and not cadence
+        h = held_frames if isinstance(held_frames, dict) else {}
+        self.th = Thresholds(cut_mean=scene_cut if scene_cut else None,
+                             hold_mean=(h.get("mean") or 0.0033) if held_frames else None,
+                             hold_max=(h.get("max") or 0.06) if held_frames else 0.0,
+                             step_after_hold=bool(held_frames) and not cadence)
         self.last_moving = None
         self.last_held = False
 
     def decide(self, stats, cells=CLASSIFY_GRID[0] * CLASSIFY_GRID[1]):
         s, mx, tile = stats
-        mean = np.float32(np.float32(s) / np.float32(max(cells, 1))) / self.CELL_MAX
-        mean = np.float32(mean)
-        mxf = np.float32(np.float32(mx) / self.CELL_MAX)
-        kind = "motion"
-        if self.cut is not None and mean > self.cut:
-            kind = "cut"
-        elif self.hold is not None and mean < self.hold[0] and mxf < self.hold[1]:
-            kind = "hold"
-        if self.cut is not None and mean >= self.FLASH_MEAN and tile >= self.FLASH_LUMA:
-            kind = "cut"
-        elif kind == "cut" and self.cut is not None and self.last_moving is not None and \
-                self.last_moving >= self.cut * self.CUT_AFTER_CALM:
-            kind = "motion"
-        held = kind == "hold"
+        c = with_history(from_stats(s, mx, cells, self.th), tile, self.last_moving, self.th)
+        held = c.kind == "hold"
         if not held:
-            self.last_moving = mean
-        if self.step_after_hold and self.last_held and kind == "motion":
-            kind = "cut"
+            self.last_moving = c.mean
+        c = after_hold(c, self.last_held, self.th)
         self.last_held = held
-        return {"kind": kind, "mean": float(mean), "max": float(mxf), "black": bool(mxf == 0.0),
-                "motion": float(np.float64(mean) * 765.0)}
+        return c.as_dict()
 
     def forget(self):
         self.last_moving = None

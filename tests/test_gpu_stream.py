@@ -163,3 +163,31 @@ def test_stream_errors(synth_model_dir, cuda):
     assert st.add_input() == 2 and st.next_input([0, 1]) == 2
     st.reset()
     assert st.report()["counters"]["resets"] == 1
+
+
+def test_reference_classifier_cases(synth_model_dir, cuda):
+    """crates/flyhigh-engine/tests/stream.rs:161-203 on the GPU: motion, hold and cut told apart; a local flash and its
+    clear frame are both cuts though below the ordinary cut threshold."""
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200.synth_frames import sinusoid_pair
+    W, H = 256, 192
+    eng, model = fh.Engine(), fh.Model(synth_model_dir)
+    st = fh.Stream(eng, model, W, H, held_frames=True)
+    flat = np.full((H, W, 4), 30, np.uint8)
+    for slot, f in enumerate((sinusoid_pair(W, H, 0.0), sinusoid_pair(W, H, 2.0), sinusoid_pair(W, H, 0.0), flat)):
+        st.write(slot, f)
+    motion, hold, cut = st.classify(0, 1), st.classify(0, 2), st.classify(0, 3)
+    assert motion.kind == "motion" and 0.0033 < motion.mean < 0.08 and not motion.black
+    assert (hold.kind, hold.black) == ("hold", True)
+    assert cut.kind == "cut"
+    assert st.report()["counters"]["classified"] == 3
+    st2 = fh.Stream(eng, model, W, H)
+    original = np.zeros((H, W, 4), np.uint8)
+    original[..., :3], original[..., 3] = 48, 255
+    flash = original.copy()
+    flash[:, 3 * W // 4:, :3] = 112
+    st2.write(0, original)
+    st2.write(1, flash)
+    onset, clear = st2.classify(0, 1), st2.classify(1, 0)
+    assert onset.mean < 0.08
+    assert (onset.kind, clear.kind) == ("cut", "cut")
