@@ -53,7 +53,7 @@ def parse():
     p.add_argument("--no-strong", action="store_true", help="skip the strong-scaling arm")
     p.add_argument("--no-c4", action="store_true", help="skip config 4 (the multi-stream Stream-layer run)")
     p.add_argument("--cpu-sample", type=int, default=3, help="intervals of the CPU baseline sample")
-    p.add_argument("--batch", type=int, default=4,
+    p.add_argument("--batch", type=int, default=16,
                    help="intervals per launch (fh_session_create_batched); 1 = one interval per launch")
     return p.parse_args()
 

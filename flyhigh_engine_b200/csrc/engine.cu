@@ -1961,6 +1961,33 @@ void input_frames(FhSession* s, uint32_t a, uint32_t b, cudaStream_t on, const u
     *fb = sets[1]->frame;
 }
 
+cudaStream_t compute_stream(FhSession* s) {
+    s->join_render();
+    return s->st;
+}
+
+uint8_t* output_frame(FhSession* s, uint32_t out) {
+    s->check_out(out);
+    return s->outs[out];
+}
+
+void output_written(FhSession* s, uint32_t out) {
+    s->check_out(out);
+    CK(cudaEventRecord(s->out_ready[out], s->st));
+}
+
+void static_age(FhSession* s, const int16_t** age, int* pitch, float* min_age) {
+    *age = nullptr;
+    *pitch = s->wp;
+    *min_age = 0.0f;
+    if (!s->protects || !s->o.keep_static || !s->have_pair) return;
+    s->use_set(s->pair_set);
+    *age = s->age;
+    *min_age = s->min_age;
+}
+
+bool has_protection_mask(const FhSession* s) { return s->o.protection_mask != 0; }
+
 void session_shape(const FhSession* s, int* w, int* h, int* iw, int* ih, int* k, int* repair) {
     *w = s->w;
     *h = s->h;

@@ -16,5 +16,15 @@ void set_error(const std::string& msg);
 void input_frames(FhSession* s, uint32_t a, uint32_t b, cudaStream_t on, const uint8_t** fa, const uint8_t** fb);
 // frame width and height, network (internal) width and height, fine iterations and repair level of the session
 void session_shape(const FhSession* s, int* w, int* h, int* iw, int* ih, int* k, int* repair);
+// the stream the session's compute is ordered on (one-interval sessions: every pair and mid)
+cudaStream_t compute_stream(FhSession* s);
+// the rgba8 buffer of output slot `out`; output_written: the work issued on the compute stream so far is the last to
+// write it (a read of the slot waits for that)
+uint8_t* output_frame(FhSession* s, uint32_t out);
+void output_written(FhSession* s, uint32_t out);
+// the static age plane of the current pair (pitch in elements) and the protecting age; null / 0 without keep_static
+void static_age(FhSession* s, const int16_t** age, int* pitch, float* min_age);
+// whether the session was built with a protection mask (FhSessionOptions.protection_mask)
+bool has_protection_mask(const FhSession* s);
 
 }  // namespace fhi

@@ -2104,6 +2104,201 @@ __global__ void __launch_bounds__(CLASSIFY_TW * CLASSIFY_TH) k_classify(const ui
     }
 }
 
+// ---------------------------------------------------------------------------------------------- pan repair ----
+
+// textureSampleLevel of an rgba8 frame with a linear sampler at normalised (u, v): texel coordinates uv * size - 0.5,
+// clamp to edge, unorm values, (r, g, b); f32 weights
+FH_DEV float3 sample_unorm(const uint8_t* __restrict__ f, int w, int h, float u, float v) {
+    const float px = u * (float)w - 0.5f, py = v * (float)h - 0.5f;
+    const int x0 = (int)floorf(px), y0 = (int)floorf(py);
+    const float fx = px - (float)x0, fy = py - (float)y0;
+    float r[3];
+    for (int c = 0; c < 3; c++) {
+        const float top = unorm_at(f, w, h, x0, y0, c) * (1.0f - fx) + unorm_at(f, w, h, x0 + 1, y0, c) * fx;
+        const float bot = unorm_at(f, w, h, x0, y0 + 1, c) * (1.0f - fx) + unorm_at(f, w, h, x0 + 1, y0 + 1, c) * fx;
+        r[c] = top * (1.0f - fy) + bot * fy;
+    }
+    return make_float3(r[0], r[1], r[2]);
+}
+
+// pan.rs:44-45: the three levels (candidates per side, spacing divisor); the first searches around zero, the last may
+// trust its result
+constexpr int PAN_LEVELS = 3;
+constexpr int PAN_WIDTH[PAN_LEVELS] = {15, 9, 9};
+constexpr int PAN_DIVISOR[PAN_LEVELS] = {1, 4, 16};
+constexpr int PAN_N = 192;
+
+// pan_search.wgsl: a block of 64 threads per candidate translation; the mean over 192 jittered sparse samples of the
+// channel-mean absolute difference between frame a at uv and frame b at uv + the candidate's shift
+__global__ void __launch_bounds__(64) k_pan_search(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb,
+                                                   int w, int h, int width, int divisor, int initial,
+                                                   const float* __restrict__ fit, float* errors) {
+    __shared__ float sums[64];
+    pdl_wait();
+    pdl_trigger();
+    const int cand = blockIdx.x, lane = threadIdx.x;
+    // a negative confidence means the initial zero-shift comparison already ruled out a pan
+    if (!initial && fit[2] < 0.0f) return;  // block-uniform
+    const float sx = (float)w, sy = (float)h;
+    const float spacing = fmaxf(1.0f, sy / 144.0f) / (float)divisor;
+    const float half = (float)(width / 2);
+    const float ox = ((float)(cand % width) - half) * spacing, oy = ((float)(cand / width) - half) * spacing;
+    const float bx = initial ? 0.0f : fit[0], by = initial ? 0.0f : fit[1];
+    const float dx = (bx + ox) / sx, dy = (by + oy) / sy;
+    const float third = 1.0f / 3.0f;
+    float sum = 0.0f;
+    for (int i = lane; i < PAN_N; i += 64) {
+        // jitter the sparse grid so that a periodic edge cannot always land between sample rows
+        const float jx = (float)((i * 13) % 17) / 17.0f, jy = (float)((i * 11) % 13) / 13.0f;
+        const float u = 0.12f + 0.76f * ((float)(i % 16) + jx) / 16.0f;
+        const float v = 0.12f + 0.76f * ((float)(i / 16) + jy) / 12.0f;
+        const float3 ca = sample_unorm(fa, w, h, u, v), cb = sample_unorm(fb, w, h, u + dx, v + dy);
+        sum += fabsf(ca.x - cb.x) * third + fabsf(ca.y - cb.y) * third + fabsf(ca.z - cb.z) * third;
+    }
+    sums[lane] = sum;
+    __syncthreads();
+    for (int step = 32; step > 0; step >>= 1) {
+        if (lane < step) sums[lane] += sums[lane + step];
+        __syncthreads();
+    }
+    if (lane == 0) errors[cand] = sums[0] / (float)PAN_N;
+}
+
+// pan_select.wgsl: the best candidate becomes the next level's centre; only a close match with a large gain over the
+// zero shift is trusted (confidence 1), and a still pair rules out a pan (-1)
+__global__ void k_pan_select(const float* __restrict__ errors, float* fit, int w, int h, int width, int divisor,
+                             int initial, int finish) {
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    if (!initial && fit[2] < 0.0f) return;
+    const float sx = (float)w, sy = (float)h;
+    const int count = width * width, center = count / 2;
+    int best = center;
+    for (int j = 0; j < count; j++)
+        if (errors[j] < errors[best]) best = j;
+    const float spacing = fmaxf(1.0f, sy / 144.0f) / (float)divisor;
+    const float half = (float)(width / 2);
+    const float shx = (initial ? 0.0f : fit[0]) + ((float)(best % width) - half) * spacing;
+    const float shy = (initial ? 0.0f : fit[1]) + ((float)(best / width) - half) * spacing;
+    const float still_error = initial ? errors[center] : fit[3];
+    const bool trusted = finish && errors[best] < 0.010f && errors[best] < 0.30f * still_error && still_error > 0.016f &&
+                         sqrtf(shx * shx + shy * shy) > 1.0f && fabsf(shx) < sx * 0.10f && fabsf(shy) < sy * 0.10f;
+    const float confidence = still_error <= 0.016f ? -1.0f : (trusted ? 1.0f : 0.0f);
+    fit[0] = shx;
+    fit[1] = shy;
+    fit[2] = confidence;
+    fit[3] = still_error;
+}
+
+struct PanPatch {
+    float mean_error, max_error;
+    bool same_detail;
+};
+
+FH_DEV float rgb_peak(float3 a, float3 b) {
+    return fmaxf(fmaxf(fabsf(a.x - b.x), fabsf(a.y - b.y)), fabsf(a.z - b.z));
+}
+
+// pan_apply.wgsl compare_patch: the four samples 2 px away on either axis under both shifts; their mean and largest
+// rgb peak difference, and whether the two frames' signed local luma contrast patterns agree
+FH_DEV PanPatch compare_patch(const uint8_t* fa, const uint8_t* fb, int w, int h, float px, float py, float sax, float say,
+                              float sbx, float sby, float3 center_a, float3 center_b, bool compare_detail) {
+    const float nx[4] = {-2.0f, 2.0f, 0.0f, 0.0f}, ny[4] = {0.0f, 0.0f, -2.0f, 2.0f};
+    const float dw = (float)w, dh = (float)h;
+    float sum = 0.0f, peak = 0.0f, da[4] = {0, 0, 0, 0}, db[4] = {0, 0, 0, 0};
+    for (int i = 0; i < 4; i++) {
+        const float qx = px + nx[i], qy = py + ny[i];
+        const float3 ca = sample_unorm(fa, w, h, (qx + sax) / dw, (qy + say) / dh);
+        const float3 cb = sample_unorm(fb, w, h, (qx + sbx) / dw, (qy + sby) / dh);
+        const float e = rgb_peak(ca, cb);
+        sum += e;
+        peak = fmaxf(peak, e);
+        if (compare_detail) {
+            da[i] = (center_a.x - ca.x) * 0.2126f + (center_a.y - ca.y) * 0.7152f + (center_a.z - ca.z) * 0.0722f;
+            db[i] = (center_b.x - cb.x) * 0.2126f + (center_b.y - cb.y) * 0.7152f + (center_b.z - cb.z) * 0.0722f;
+        }
+    }
+    const float aa = da[0] * da[0] + da[1] * da[1] + da[2] * da[2] + da[3] * da[3];
+    const float bb = db[0] * db[0] + db[1] * db[1] + db[2] * db[2] + db[3] * db[3];
+    const float ab = da[0] * db[0] + da[1] * db[1] + da[2] * db[2] + da[3] * db[3];
+    const bool same = fminf(aa, bb) > 0.02f && fminf(aa, bb) > 0.42f * fmaxf(aa, bb) && ab > 0.0f &&
+                      ab * ab > 0.94f * aa * bb;
+    return PanPatch{sum * 0.25f, peak, same};
+}
+
+// pan_apply.wgsl: where the pan is trusted, each pixel takes the two frames' translated samples (mixed at phase t, or
+// the one frame that sees a revealed strip) where they agree, unless the static protection keeps it
+__global__ void k_pan_apply(const uint8_t* __restrict__ fa, const uint8_t* __restrict__ fb, int w, int h,
+                            const float* __restrict__ fit, float t, const int16_t* __restrict__ age, int age_pitch,
+                            float min_age, uint8_t* out) {
+    pdl_wait();
+    pdl_trigger();
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y;
+    if (!(fit[2] > 0.0f) || x >= w || y >= h) return;
+    const float dw = (float)w, dh = (float)h;
+    const float px = (float)x + 0.5f, py = (float)y + 0.5f;
+    const float sax = -t * fit[0], say = -t * fit[1], sbx = (1.0f - t) * fit[0], sby = (1.0f - t) * fit[1];
+    const float pax = px + sax, pay = py + say, pbx = px + sbx, pby = py + sby;
+    const float lo = 0.5f, hix = dw - lo, hiy = dh - lo;
+    const bool has_a = pax >= lo && pay >= lo && pax <= hix && pay <= hiy;
+    const bool has_b = pbx >= lo && pby >= lo && pbx <= hix && pby <= hiy;
+    const float3 ca = sample_unorm(fa, w, h, pax / dw, pay / dh), cb = sample_unorm(fb, w, h, pbx / dw, pby / dh);
+    if (has_a && has_b) {
+        // compression and subpixel sampling can leave isolated mismatches on an otherwise aligned line
+        const float peak = rgb_peak(ca, cb);
+        if (peak > 0.06f) {
+            if (peak > 0.16f) return;
+            const PanPatch local = compare_patch(fa, fb, w, h, px, py, sax, say, sbx, sby, ca, cb, true);
+            const bool colour_match = local.mean_error <= 0.045f && local.max_error <= 0.10f;
+            if (!colour_match && !(local.same_detail && local.max_error <= 0.13f)) return;
+        }
+    } else {
+        // the pan reveals or hides a strip at the frame edge: one source sees it; check the adjacent overlap first
+        if (!has_a && !has_b) return;
+        const float olx = lo - fminf(sax, sbx) + 2.0f, oly = lo - fminf(say, sby) + 2.0f;
+        const float ohx = hix - fmaxf(sax, sbx) - 2.0f, ohy = hiy - fmaxf(say, sby) - 2.0f;
+        if (olx > ohx || oly > ohy) return;
+        const float cx = fminf(fmaxf(px, olx), ohx), cy = fminf(fmaxf(py, oly), ohy);
+        if (compare_patch(fa, fb, w, h, cx, cy, sax, say, sbx, sby, ca, cb, false).max_error > 0.045f) return;
+    }
+    if (age && min_age > 0.0f) {
+        const int iax = (int)fminf(fmaxf(pax, lo), hix), iay = (int)fminf(fmaxf(pay, lo), hiy);
+        const int ibx = (int)fminf(fmaxf(pbx, lo), hix), iby = (int)fminf(fmaxf(pby, lo), hiy);
+        auto age_at = [&](int xx, int yy) { return (float)age[(size_t)yy * age_pitch + xx]; };
+        if (age_at(x, y) > min_age - 2.0f || (has_a && age_at(iax, iay) >= min_age) ||
+            (has_b && age_at(ibx, iby) >= min_age))
+            return;
+    }
+    const float wgt = has_a && has_b ? t : (has_a ? 0.0f : 1.0f);
+    const float r = ca.x * (1.0f - wgt) + cb.x * wgt, g = ca.y * (1.0f - wgt) + cb.y * wgt,
+                b = ca.z * (1.0f - wgt) + cb.z * wgt;
+    auto q = [](float v) { return (uint32_t)(fminf(fmaxf(v, 0.0f), 1.0f) * 255.0f + 0.5f); };
+    reinterpret_cast<uint32_t*>(out)[(size_t)y * w + x] = q(r) | (q(g) << 8) | (q(b) << 16) | 0xff000000u;
+}
+
+cudaError_t pan_search(const uint8_t* fa, const uint8_t* fb, int w, int h, float* fit, float* errors, cudaStream_t st) {
+    if (w < 1 || h < 1) return cudaErrorInvalidValue;
+    for (int l = 0; l < PAN_LEVELS; l++) {
+        const int width = PAN_WIDTH[l], div = PAN_DIVISOR[l], initial = div == 1 ? 1 : 0, finish = div == 16 ? 1 : 0;
+        cudaError_t e = launch(k_pan_search, dim3(width * width), dim3(64), 0, st, fa, fb, w, h, width, div, initial,
+                               (const float*)fit, errors);
+        if (e == cudaSuccess)
+            e = launch(k_pan_select, dim3(1), dim3(1), 0, st, (const float*)errors, fit, w, h, width, div, initial, finish);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t pan_apply(const uint8_t* fa, const uint8_t* fb, int w, int h, const float* fit, float t, const int16_t* age,
+                      int age_pitch, float min_age, uint8_t* out, cudaStream_t st) {
+    if (w < 1 || h < 1) return cudaErrorInvalidValue;
+    const cudaError_t e = launch(k_pan_apply, dim3((w + 7) / 8, (h + 7) / 8), dim3(8, 8), 0, st, fa, fb, w, h, fit, t,
+                                 age, age_pitch, min_age, out);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
 cudaError_t classify(const uint8_t* fa, const uint8_t* fb, int w, int h, int gw, int gh, uint32_t* stats, cudaStream_t st) {
     if (w < 1 || h < 1 || gw < 1 || gh < 1) return cudaErrorInvalidValue;
     cudaError_t e = cudaMemsetAsync(stats, 0, 3 * sizeof(uint32_t), st);

@@ -218,4 +218,14 @@ cudaError_t frame_planes(const uint8_t* f, int w, int h, int hp, int wp, float* 
 constexpr int CLASSIFY_TW = 8, CLASSIFY_TH = 9;
 cudaError_t classify(const uint8_t* fa, const uint8_t* fb, int w, int h, int gw, int gh, uint32_t* stats, cudaStream_t st);
 
+// Repair level 2's pan stage (crates/flyhigh-engine/src/pan.rs, pan_search / pan_select / pan_apply.wgsl): the single
+// translation that aligns the two source frames, searched on three levels of a candidate grid around the previous
+// level's best; where it is trusted, the generated frame takes the frames' translated pixels wherever they agree.
+// fit: 4 floats on the device (shift x, y, confidence, still error); errors: 225 floats of scratch.
+cudaError_t pan_search(const uint8_t* fa, const uint8_t* fb, int w, int h, float* fit, float* errors, cudaStream_t st);
+// out: the generated rgba8 frame (w x h), rewritten in place; age: the static age plane (pitch wp) and the protecting
+// age, or null / 0 without static protection
+cudaError_t pan_apply(const uint8_t* fa, const uint8_t* fb, int w, int h, const float* fit, float t, const int16_t* age,
+                      int age_pitch, float min_age, uint8_t* out, cudaStream_t st);
+
 }  // namespace fhk

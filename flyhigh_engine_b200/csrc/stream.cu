@@ -12,6 +12,8 @@
 // - Classification (classify.rs): the classify kernel's three sums of the pair, then the decision with its history
 //   (the last moving pair's mean, whether the last pair was held) on the host. fh_stream_classify waits for it, as the
 //   C ABI does.
+// - Repair level 2 (without a protection mask) adds the pan stage (pan.rs): its search after each pair, its apply on
+//   each generated frame.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -117,6 +119,12 @@ struct FhStream {
     cudaStream_t cst = nullptr;
     uint32_t* stats_dev = nullptr;
     uint32_t* stats_host = nullptr;  // pinned
+    // repair level 2 without a protection mask (gen_tex.rs:308-309): the pan stage's fit of the current pair and the
+    // slots of that pair; its search runs after each pair, its apply after each generated frame
+    bool pan = false;
+    float* pan_fit = nullptr;   // 4 floats
+    float* pan_err = nullptr;   // 225 floats
+    int pan_a = -1, pan_b = -1;
     // mouse input (the camera warp itself is not built: it stays off)
     bool mouse_seen = false, captured = false;
     // stream/mod.rs:134-150
@@ -126,6 +134,8 @@ struct FhStream {
     ~FhStream() {
         if (cst) cudaStreamSynchronize(cst);
         if (stats_dev) cudaFree(stats_dev);
+        if (pan_fit) cudaFree(pan_fit);
+        if (pan_err) cudaFree(pan_err);
         if (stats_host) cudaFreeHost(stats_host);
         if (cst) cudaStreamDestroy(cst);
         if (s) fh_session_destroy(s);
@@ -196,6 +206,17 @@ struct FhStream {
         return 1;
     }
 
+    // the pan stage's search on the pair just run (pan.rs:57-103), ordered after it on the session's stream
+    void pan_after_pair(int a, int b) {
+        if (!pan) return;
+        cudaStream_t st = fhi::compute_stream(s);
+        const uint8_t *fa = nullptr, *fb = nullptr;
+        fhi::input_frames(s, (uint32_t)a, (uint32_t)b, st, &fa, &fb);
+        SCK(fhk::pan_search(fa, fb, w, h, pan_fit, pan_err, st));
+        pan_a = a;
+        pan_b = b;
+    }
+
     // stream/mod.rs:366-393 with gen_tex.rs:428-468
     FhPush push(uint32_t slot, double pts) {
         check_in(slot);
@@ -211,6 +232,7 @@ struct FhStream {
             if (had) {
                 const auto prev = pushed[pushed.size() - 2];
                 if (fh_session_pair(s, (uint32_t)prev.first, slot) < 0) sfail("%s", fh_last_error());
+                pan_after_pair(prev.first, (int)slot);
                 have_interval = true;
                 base = prev.first;
                 start_pts = prev.second;
@@ -220,6 +242,7 @@ struct FhStream {
             // the interval [f(n-2), f(n-1)): its pair, in time order (see the file's note)
             const auto a = pushed[0], b = pushed[1];
             if (fh_session_pair(s, (uint32_t)a.first, (uint32_t)b.first) < 0) sfail("%s", fh_last_error());
+            pan_after_pair(a.first, b.first);
             have_interval = true;
             base = a.first;
             start_pts = a.second;
@@ -243,6 +266,17 @@ struct FhStream {
         }
         if (!have_interval) sfail(video ? "video mode: push three frames first" : "realtime mode: push two frames first");
         if (fh_session_mid(s, t, out) < 0) sfail("%s", fh_last_error());
+        if (pan) {  // gen_tex.rs:404-418: the pan apply on the generated frame, after its render
+            cudaStream_t st = fhi::compute_stream(s);
+            const uint8_t *fa = nullptr, *fb = nullptr;
+            fhi::input_frames(s, (uint32_t)pan_a, (uint32_t)pan_b, st, &fa, &fb);
+            const int16_t* age = nullptr;
+            int pitch = 0;
+            float min_age = 0.0f;
+            fhi::static_age(s, &age, &pitch, &min_age);
+            SCK(fhk::pan_apply(fa, fb, w, h, pan_fit, t, age, pitch, min_age, fhi::output_frame(s, out), st));
+            fhi::output_written(s, out);
+        }
         mids++;
         return 1;
     }
@@ -321,6 +355,12 @@ FhStream* fh_stream_create(const FhEngine* e, const FhModel* m, const FhSessionO
         SCK(cudaStreamCreateWithFlags(&st->cst, cudaStreamNonBlocking));
         SCK(cudaMalloc(&st->stats_dev, 3 * sizeof(uint32_t)));
         SCK(cudaMallocHost(&st->stats_host, 3 * sizeof(uint32_t)));
+        st->pan = st->repair == 2 && !fhi::has_protection_mask(st->s);
+        if (st->pan) {
+            SCK(cudaMalloc(&st->pan_fit, 4 * sizeof(float)));
+            SCK(cudaMemset(st->pan_fit, 0, 4 * sizeof(float)));
+            SCK(cudaMalloc(&st->pan_err, 225 * sizeof(float)));
+        }
         for (uint32_t i = 0; i < o->inputs; i++) st->add_input();
         for (uint32_t i = 0; i < o->outputs; i++) st->add_output();
         return st.release();

@@ -1792,6 +1792,172 @@ int or_render_diag(const uint8_t* fa, const uint8_t* fb, int w, int h, const flo
 
 int or_render_diag_size() { return RENDER_DIAG; }
 
+// ---- repair level 2's pan stage (pan.rs, pan_search / pan_select / pan_apply.wgsl) ----
+
+namespace pan {
+
+// textureSampleLevel with a linear sampler on an rgba8 frame at normalised (u, v): texel coordinates uv * size - 0.5,
+// clamp to edge, unorm values (r, g, b), f32 weights
+static void sample(const uint8_t* f, int w, int h, float u, float v, float out[3]) {
+    const float px = u * (float)w - 0.5f, py = v * (float)h - 0.5f;
+    const int x0 = (int)floorf(px), y0 = (int)floorf(py);
+    const float fx = px - (float)x0, fy = py - (float)y0;
+    auto t = [&](int x, int y, int c) {
+        x = std::max(0, std::min(x, w - 1));
+        y = std::max(0, std::min(y, h - 1));
+        return (float)f[((size_t)y * w + x) * 4 + c] / 255.0f;
+    };
+    for (int c = 0; c < 3; c++) {
+        const float top = t(x0, y0, c) * (1.0f - fx) + t(x0 + 1, y0, c) * fx;
+        const float bot = t(x0, y0 + 1, c) * (1.0f - fx) + t(x0 + 1, y0 + 1, c) * fx;
+        out[c] = top * (1.0f - fy) + bot * fy;
+    }
+}
+
+static float peak3(const float a[3], const float b[3]) {
+    return std::max(std::max(fabsf(a[0] - b[0]), fabsf(a[1] - b[1])), fabsf(a[2] - b[2]));
+}
+
+struct Patch {
+    float mean_error, max_error;
+    bool same_detail;
+};
+
+// pan_apply.wgsl:20-49
+static Patch compare_patch(const uint8_t* fa, const uint8_t* fb, int w, int h, float px, float py, float sax, float say,
+                           float sbx, float sby, const float ca0[3], const float cb0[3], bool detail) {
+    const float nx[4] = {-2.0f, 2.0f, 0.0f, 0.0f}, ny[4] = {0.0f, 0.0f, -2.0f, 2.0f};
+    const float dw = (float)w, dh = (float)h;
+    float sum = 0.0f, peak = 0.0f, da[4] = {0, 0, 0, 0}, db[4] = {0, 0, 0, 0};
+    for (int i = 0; i < 4; i++) {
+        const float qx = px + nx[i], qy = py + ny[i];
+        float ca[3], cb[3];
+        sample(fa, w, h, (qx + sax) / dw, (qy + say) / dh, ca);
+        sample(fb, w, h, (qx + sbx) / dw, (qy + sby) / dh, cb);
+        const float e = peak3(ca, cb);
+        sum += e;
+        peak = std::max(peak, e);
+        if (detail) {
+            da[i] = (ca0[0] - ca[0]) * 0.2126f + (ca0[1] - ca[1]) * 0.7152f + (ca0[2] - ca[2]) * 0.0722f;
+            db[i] = (cb0[0] - cb[0]) * 0.2126f + (cb0[1] - cb[1]) * 0.7152f + (cb0[2] - cb[2]) * 0.0722f;
+        }
+    }
+    const float aa = da[0] * da[0] + da[1] * da[1] + da[2] * da[2] + da[3] * da[3];
+    const float bb = db[0] * db[0] + db[1] * db[1] + db[2] * db[2] + db[3] * db[3];
+    const float ab = da[0] * db[0] + da[1] * db[1] + da[2] * db[2] + da[3] * db[3];
+    const bool same = std::min(aa, bb) > 0.02f && std::min(aa, bb) > 0.42f * std::max(aa, bb) && ab > 0.0f &&
+                      ab * ab > 0.94f * aa * bb;
+    return Patch{sum * 0.25f, peak, same};
+}
+
+}  // namespace pan
+
+// pan.rs:57-103 with pan_search.wgsl and pan_select.wgsl: three levels (15 candidates a side, then 9 and 9 at a 4x and
+// 16x finer spacing) around the previous level's best; fit = (shift x, y, confidence, still error)
+int or_pan_search(const uint8_t* fa, const uint8_t* fb, int w, int h, float* fit) {
+    const int widths[3] = {15, 9, 9}, divs[3] = {1, 4, 16};
+    const int N = 192;
+    fit[0] = fit[1] = fit[2] = fit[3] = 0.0f;
+    std::vector<float> errors(225, 0.0f);
+    const float sx = (float)w, sy = (float)h, third = 1.0f / 3.0f;
+    for (int l = 0; l < 3; l++) {
+        const int width = widths[l], div = divs[l], initial = div == 1, finish = div == 16;
+        if (!initial && fit[2] < 0.0f) continue;  // the search and the select both stand aside
+        const float spacing = std::max(1.0f, sy / 144.0f) / (float)div;
+        const float half = (float)(width / 2);
+        for (int cand = 0; cand < width * width; cand++) {
+            const float ox = ((float)(cand % width) - half) * spacing, oy = ((float)(cand / width) - half) * spacing;
+            const float bx = initial ? 0.0f : fit[0], by = initial ? 0.0f : fit[1];
+            const float dx = (bx + ox) / sx, dy = (by + oy) / sy;
+            float part[64];
+            for (int lane = 0; lane < 64; lane++) {  // the workgroup's lanes, each a strided partial sum
+                float sum = 0.0f;
+                for (int i = lane; i < N; i += 64) {
+                    const float jx = (float)((i * 13) % 17) / 17.0f, jy = (float)((i * 11) % 13) / 13.0f;
+                    const float u = 0.12f + 0.76f * ((float)(i % 16) + jx) / 16.0f;
+                    const float v = 0.12f + 0.76f * ((float)(i / 16) + jy) / 12.0f;
+                    float ca[3], cb[3];
+                    pan::sample(fa, w, h, u, v, ca);
+                    pan::sample(fb, w, h, u + dx, v + dy, cb);
+                    sum += fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
+                }
+                part[lane] = sum;
+            }
+            for (int step = 32; step > 0; step >>= 1)
+                for (int lane = 0; lane < step; lane++) part[lane] += part[lane + step];
+            errors[cand] = part[0] / (float)N;
+        }
+        const int count = width * width, center = count / 2;
+        int best = center;
+        for (int j = 0; j < count; j++)
+            if (errors[j] < errors[best]) best = j;
+        const float shx = (initial ? 0.0f : fit[0]) + ((float)(best % width) - half) * spacing;
+        const float shy = (initial ? 0.0f : fit[1]) + ((float)(best / width) - half) * spacing;
+        const float still_error = initial ? errors[center] : fit[3];
+        const bool trusted = finish && errors[best] < 0.010f && errors[best] < 0.30f * still_error &&
+                             still_error > 0.016f && sqrtf(shx * shx + shy * shy) > 1.0f && fabsf(shx) < sx * 0.10f &&
+                             fabsf(shy) < sy * 0.10f;
+        fit[0] = shx;
+        fit[1] = shy;
+        fit[2] = still_error <= 0.016f ? -1.0f : (trusted ? 1.0f : 0.0f);
+        fit[3] = still_error;
+    }
+    return 0;
+}
+
+// pan_apply.wgsl:51-103 on a generated rgba8 frame (w x h) in place; age: the static age plane (pitch in elements) and
+// the protecting age, or null / 0
+int or_pan_apply(const uint8_t* fa, const uint8_t* fb, int w, int h, const float* fit, float t, const float* age,
+                 int pitch, float min_age, uint8_t* out) {
+    if (!(fit[2] > 0.0f)) return 0;
+    const float dw = (float)w, dh = (float)h;
+#pragma omp parallel for
+    for (int y = 0; y < h; y++)
+        for (int x = 0; x < w; x++) {
+            const float px = (float)x + 0.5f, py = (float)y + 0.5f;
+            const float sax = -t * fit[0], say = -t * fit[1], sbx = (1.0f - t) * fit[0], sby = (1.0f - t) * fit[1];
+            const float pax = px + sax, pay = py + say, pbx = px + sbx, pby = py + sby;
+            const float lo = 0.5f, hix = dw - lo, hiy = dh - lo;
+            const bool has_a = pax >= lo && pay >= lo && pax <= hix && pay <= hiy;
+            const bool has_b = pbx >= lo && pby >= lo && pbx <= hix && pby <= hiy;
+            float ca[3], cb[3];
+            pan::sample(fa, w, h, pax / dw, pay / dh, ca);
+            pan::sample(fb, w, h, pbx / dw, pby / dh, cb);
+            if (has_a && has_b) {
+                const float peak = pan::peak3(ca, cb);
+                if (peak > 0.06f) {
+                    if (peak > 0.16f) continue;
+                    const pan::Patch lp = pan::compare_patch(fa, fb, w, h, px, py, sax, say, sbx, sby, ca, cb, true);
+                    const bool colour_match = lp.mean_error <= 0.045f && lp.max_error <= 0.10f;
+                    if (!colour_match && !(lp.same_detail && lp.max_error <= 0.13f)) continue;
+                }
+            } else {
+                if (!has_a && !has_b) continue;
+                const float olx = lo - std::min(sax, sbx) + 2.0f, oly = lo - std::min(say, sby) + 2.0f;
+                const float ohx = hix - std::max(sax, sbx) - 2.0f, ohy = hiy - std::max(say, sby) - 2.0f;
+                if (olx > ohx || oly > ohy) continue;
+                const float cx = std::min(std::max(px, olx), ohx), cy = std::min(std::max(py, oly), ohy);
+                if (pan::compare_patch(fa, fb, w, h, cx, cy, sax, say, sbx, sby, ca, cb, false).max_error > 0.045f)
+                    continue;
+            }
+            if (age && min_age > 0.0f) {
+                const int iax = (int)std::min(std::max(pax, lo), hix), iay = (int)std::min(std::max(pay, lo), hiy);
+                const int ibx = (int)std::min(std::max(pbx, lo), hix), iby = (int)std::min(std::max(pby, lo), hiy);
+                auto at = [&](int xx, int yy) { return age[(size_t)yy * pitch + xx]; };
+                if (at(x, y) > min_age - 2.0f || (has_a && at(iax, iay) >= min_age) || (has_b && at(ibx, iby) >= min_age))
+                    continue;
+            }
+            const float wgt = has_a && has_b ? t : (has_a ? 0.0f : 1.0f);
+            uint8_t* o = out + ((size_t)y * w + x) * 4;
+            for (int c = 0; c < 3; c++) {
+                const float v = ca[c] * (1.0f - wgt) + cb[c] * wgt;
+                o[c] = (uint8_t)(uint32_t)(std::min(std::max(v, 0.0f), 1.0f) * 255.0f + 0.5f);
+            }
+            o[3] = 255;
+        }
+    return 0;
+}
+
 // classify.wgsl:13-44 (the Stream's pair classifier, stream/classify.rs:17-21 grid 48 x 27): frames a, b (w x h rgba8)
 // sampled bilinearly (texel coordinates uv * size - 0.5, clamp to edge, f32 weights) at the centre of each cell of a
 // gw x gh grid; out[0] = the sum over cells of u32(dot(|b - a|.rgb, 255)), out[1] = its largest cell, out[2] = the

@@ -56,6 +56,9 @@ def lib():
         L.or_render_diag_size.restype = c_int
         L.or_gmhs_select.argtypes = [c_void_p, POINTER(c_float), c_int, c_int, POINTER(c_float)]
         L.or_classify.argtypes = [POINTER(c_uint8), POINTER(c_uint8), c_int, c_int, c_int, c_int, POINTER(ctypes.c_uint32)]
+        L.or_pan_search.argtypes = [POINTER(c_uint8), POINTER(c_uint8), c_int, c_int, POINTER(c_float)]
+        L.or_pan_apply.argtypes = [POINTER(c_uint8), POINTER(c_uint8), c_int, c_int, POINTER(c_float), c_float,
+                                   POINTER(c_float), c_int, c_float, POINTER(c_uint8)]
         L.or_tex_down.argtypes = [POINTER(c_uint8), c_int, c_int, c_int, c_int, POINTER(c_uint16)]
         L.or_interp.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, c_int, c_int, c_int, c_float, POINTER(c_uint16)]
         L.or_warp.argtypes = [POINTER(c_uint16), c_int, c_int, c_int, POINTER(c_uint16), c_float, POINTER(c_uint16)]
@@ -383,3 +386,28 @@ class Classifier:
     def forget(self):
         self.last_moving = None
         self.last_held = False
+
+
+# ---- repair level 2's pan stage (crates/flyhigh-engine/src/pan.rs) ----
+
+def pan_search(fa, fb, w, h):
+    """pan_search / pan_select.wgsl over the three levels: (shift x, shift y, confidence, still error)."""
+    fa = np.ascontiguousarray(fa, np.uint8)
+    fb = np.ascontiguousarray(fb, np.uint8)
+    fit = np.zeros(4, np.float32)
+    lib().or_pan_search(_u8(fa), _u8(fb), w, h, fit.ctypes.data_as(POINTER(c_float)))
+    return fit
+
+
+def pan_apply(fa, fb, w, h, fit, t, frame, age=None, min_age=0.0):
+    """pan_apply.wgsl on a generated rgba8 frame (a copy is returned); age: the static age plane [hp][wp] or None."""
+    fa = np.ascontiguousarray(fa, np.uint8)
+    fb = np.ascontiguousarray(fb, np.uint8)
+    out = np.ascontiguousarray(np.asarray(frame, np.uint8).copy())
+    fit = np.ascontiguousarray(fit, np.float32)
+    ag = None if age is None else np.ascontiguousarray(age, np.float32)
+    pitch = 0 if ag is None else ag.shape[-1]
+    f = lambda a: a.ctypes.data_as(POINTER(c_float))
+    lib().or_pan_apply(_u8(fa), _u8(fb), w, h, f(fit), c_float(t), f(ag) if ag is not None else None, pitch,
+                       c_float(min_age), _u8(out))
+    return out

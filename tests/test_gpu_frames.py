@@ -1,8 +1,8 @@
 """End-to-end parity of the configurations that bench.py times, against the oracle, frame by frame.
 
-- Config 2 as bench.py runs it: a batched session (4 intervals per launch; its stride-1 convs on the tcgen05 kernel)
-  at 1920 x 1080 with the Session defaults (k 1, repair 1, bicubic, static protection and the still test on), over 12
-  consecutive intervals of a seeded config-2 sequence, so that the HUD becomes protected.
+- Config 2 as bench.py runs it: a batched session (16 intervals per launch, and 4; each conv on the kernel the
+  autotuner chose) at 1920 x 1080 with the Session defaults (k 1, repair 1, bicubic, static protection and the still
+  test on), over 32 (12) consecutive intervals of a seeded config-2 sequence, so that the HUD becomes protected.
 - Config 3: 3840 x 2160 with three phases (0.25, 0.5, 0.75) per interval over a fence pattern, on a session run one
   interval at a time (the reference's per-call path).
 
@@ -66,11 +66,13 @@ def _check_pre_flow(flow_rep, flow_pre, sel):
     assert np.array_equal(flow_rep[:, keep], flow_pre[:, keep])
 
 
-def test_batched_1080p_defaults_match_oracle(synth_model_dir, cuda):
+@pytest.mark.parametrize("B,N", [(4, 12), (16, 32)])
+def test_batched_1080p_defaults_match_oracle(synth_model_dir, cuda, B, N):
+    """bench.py's session (batch 16 by default; batch 4 too): two or three full batches of config-2 intervals."""
     import flyhigh_engine_b200 as fh
     from flyhigh_engine_b200 import synth_frames
     from oracle.oracle import OracleModel, OracleSession
-    W, H, B, N = 1920, 1080, 4, 12
+    W, H = 1920, 1080
     frames = synth_frames.sequence_c2(N + 1, W, H, seed=7)
     model = fh.Model(synth_model_dir)
     pp = model.plan_params(W, H)
@@ -117,7 +119,7 @@ def test_batched_1080p_defaults_match_oracle(synth_model_dir, cuda):
             rep = check_frame(gots[i], ref, frames[i - 1], frames[i], W, H, pp, (up7g, rtg), (up7o, rto), age, gm)
             rep.update(i=i, flow_l1=flow_l1, protected=protected)
             rows.append(rep)
-            _report("batched_1080p", rows)
+            _report(f"batched_1080p_b{B}", rows)
             assert rep["ok"], rep
     assert protected > 2000, "the HUD should be protected after 8+ pairs"
 

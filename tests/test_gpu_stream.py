@@ -191,3 +191,80 @@ def test_reference_classifier_cases(synth_model_dir, cuda):
     onset, clear = st2.classify(0, 1), st2.classify(1, 0)
     assert onset.mean < 0.08
     assert (onset.kind, clear.kind) == ("cut", "cut")
+
+
+def _pan_pair(w, h, dx, dy, seed=21):
+    """Two noise-free frames of a texture with a fence (dark 3-px bars every 16 px over its middle third), the second
+    the first translated by (dx, dy) px: a camera pan that a single translation aligns exactly."""
+    from flyhigh_engine_b200 import synth_frames
+    m = 32
+    tex = synth_frames.texture(w, h, np.random.default_rng(seed), margin=m)
+    yy, xx = np.mgrid[0:h + 2 * m, 0:w + 2 * m]
+    band = (yy > (h + 2 * m) // 3) & (yy < 2 * (h + 2 * m) // 3)
+    bars = ((xx % 16) < 3) | ((yy % 16) < 3)
+    tex[band & bars] = 30.0
+    img = np.clip(tex, 0, 255).astype(np.uint8)
+
+    def crop(ox, oy):
+        f = np.empty((h, w, 4), np.uint8)
+        f[..., :3] = img[m + oy:m + oy + h, m + ox:m + ox + w]
+        f[..., 3] = 255
+        return f
+    return crop(0, 0), crop(dx, dy)
+
+
+@pytest.mark.parametrize("t", [0.25, 0.5])
+def test_pan_stage_matches_oracle(synth_model_dir, cuda, t):
+    """Repair level 2 in a Stream adds the pan stage (pan.rs): the search after the pair and the apply on the generated
+    frame. On an exact camera pan the pan is trusted, and the Stream's frame equals the session's frame of the same
+    options with the oracle's pan search and apply on it, byte for byte."""
+    import flyhigh_engine_b200 as fh
+    from oracle import oracle
+    w, h = 640, 360
+    fa, fb = _pan_pair(w, h, 7, -3)
+    fit = oracle.pan_search(fa, fb, w, h)
+    assert fit[2] == 1.0 and abs(fit[0] + 7.0) < 0.5 and abs(fit[1] - 3.0) < 0.5, fit  # b(x) = a(x + (7, -3))
+    model = fh.Model(synth_model_dir)
+    st = fh.Stream(fh.Engine(), model, w, h, repair=2, scene_cut=0)
+    st.write(0, fa)
+    st.push(0, 0.0)
+    st.write(1, fb)
+    assert st.push(1, 1.0).ready
+    assert st.generate(t, 0)
+    got = np.frombuffer(st.read(0), np.uint8)
+    s = fh.Session(fh.Engine(), model, w, h, repair=2)
+    a, b, out = s.add_input(), s.add_input(), s.add_output()
+    s.write(a, fa)
+    s.write(b, fb)
+    s.pair(a, b)
+    s.mid(t, out)
+    plain = np.frombuffer(s.read(out), np.uint8)
+    p = model.plan_params(w, h, repair=2)
+    ref = oracle.pan_apply(fa, fb, w, h, fit, t, plain, age=s.tensor("age")[0], min_age=p["min_age"])
+    changed = int((ref != plain).reshape(-1, 4).any(1).sum())
+    assert changed > (w * h) // 4, changed  # the pan rewrites most of the frame
+    assert np.array_equal(got, ref), int((got != ref).reshape(-1, 4).any(1).sum())
+
+
+def test_pan_stage_stays_off_without_a_pan(synth_model_dir, cuda):
+    """Independent motion (config-2 rectangles over a random-walk pan with sensor noise) is not one translation: the
+    pan is not trusted and a repair-2 Stream's frames equal the session's."""
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200 import synth_frames
+    from oracle import oracle
+    w, h = 384, 192
+    frames = synth_frames.sequence_c2(3, w, h, seed=31)
+    assert oracle.pan_search(frames[1], frames[2], w, h)[2] <= 0.0
+    model = fh.Model(synth_model_dir)
+    st = fh.Stream(fh.Engine(), model, w, h, repair=2, scene_cut=0)
+    s = fh.Session(fh.Engine(), model, w, h, repair=2)
+    a, b, out = s.add_input(), s.add_input(), s.add_output()
+    for i, f in enumerate(frames):
+        st.write(i, f)
+        st.push(i, float(i))
+        s.write(a if i % 2 == 0 else b, f)
+        if i:
+            s.pair(b if i % 2 == 0 else a, a if i % 2 == 0 else b)
+    st.generate(0.5, 0)
+    s.mid(0.5, out)
+    assert st.read(0) == s.read(out)
