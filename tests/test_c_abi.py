@@ -71,3 +71,16 @@ def test_tune_table_format(tmp_path):
     r = subprocess.run([exe], capture_output=True, text=True)
     assert r.returncode == 0, r.stdout
     assert r.stdout.count("ok ") == 11
+
+
+def test_warp_calibrator_on_synthetic_play(tmp_path):
+    """The camera warp's input calibration (csrc/warp_calib.hpp) on the reference's own synthetic play
+    (crates/flyhigh-engine/tests/warp.rs:1-138): it finds the 45 ms lag and the gain, turns off at once for a released
+    mouse and within a few frames for a menu, and the shift it applies is the gain times the counts since the input the
+    frame shows."""
+    exe = str(tmp_path / "warp_calib_test")
+    subprocess.run(["g++", "-std=c++17", "-O2", "-Wall", "-I", os.path.join(ROOT, "flyhigh_engine_b200", "csrc"), "-o",
+                    exe, os.path.join(ROOT, "tests", "c_abi", "warp_calib_test.cpp")], check=True)
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout
+    assert r.stdout.count("\nok ") + r.stdout.startswith("ok ") == 10, r.stdout
