@@ -134,6 +134,23 @@ EXPORTS = [
     ("fh_stream_set_mouse_captured", c_int, [c_void_p, c_uint32]),
     ("fh_stream_warp", c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_uint32, c_double]),
     ("fh_stream_report_json", c_int, [c_void_p, c_char_p, c_size_t]),
+    ("fh_stream_camera_warp", c_void_p, [c_void_p]),
+    ("fh_warp_create", c_void_p, [c_void_p, c_uint32, c_uint32, c_double]),
+    ("fh_warp_destroy", None, [c_void_p]),
+    ("fh_warp_mouse", c_int, [c_void_p, c_double, c_double, c_double]),
+    ("fh_warp_set_captured", c_int, [c_void_p, c_uint32]),
+    ("fh_warp_break_pair", c_int, [c_void_p]),
+    ("fh_warp_frame", c_int, [c_void_p, c_void_p, c_double]),
+    ("fh_warp_collect", c_int, [c_void_p, c_int]),
+    ("fh_warp_last_shift", c_int, [c_void_p, POINTER(c_double), POINTER(c_double)]),
+    ("fh_warp_shift", c_int, [c_void_p, c_double, c_double, POINTER(c_double), POINTER(c_double)]),
+    ("fh_warp_decide", c_int, [c_void_p, c_double, c_double, POINTER(c_double), POINTER(c_double)]),
+    ("fh_warp_render_shift", c_void_p, [c_void_p, c_void_p, c_double, c_double]),
+    ("fh_warp_render_into", c_int, [c_void_p, c_void_p, c_void_p, c_double, c_double]),
+    ("fh_warp_cuda_stream", c_int, [c_void_p, POINTER(c_void_p)]),
+    ("fh_warp_read_mask", ctypes.c_long, [c_void_p, POINTER(c_float), c_size_t]),
+    ("fh_warp_debug_tensor", ctypes.c_long, [c_void_p, c_char_p, POINTER(c_float), c_size_t]),
+    ("fh_warp_report_json", c_int, [c_void_p, c_char_p, c_size_t]),
     ("fhk_conv3x3", c_int, [c_void_p, c_int, c_void_p]),
     ("fhk_conv_pack_weights", c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
     ("fhk_conv_packed_elems", c_size_t, [c_int, c_int]),
@@ -602,8 +619,15 @@ class Stream:
         _check(lib().fh_stream_set_mouse_captured(self._h, int(bool(captured))))
 
     def warp(self, slot: int, out: int, now: float, output: bool = False) -> bool:
-        """The camera warp of the frame about to be shown; False: present it as it is (always, in this build)."""
+        """The frame about to be presented at `now` (input slot, or output slot with output=True) turned by the mouse
+        motion since the moment it shows, into output slot `out`: True = present `out`; False = the warp is off
+        (present the frame as it is)."""
         return _check(lib().fh_stream_warp(self._h, self._e._h, int(output), slot, out, now)) == 1
+
+    def camera_warp(self) -> Optional["Warp"]:
+        """The stream's camera warp (started by the first mouse call), or None; it lives as long as the stream."""
+        h = lib().fh_stream_camera_warp(self._h)
+        return Warp._borrowed(h, self) if h else None
 
     def report(self) -> dict:
         return _json(lib().fh_stream_report_json, self._h)
@@ -623,4 +647,109 @@ class Stream:
         try:
             self.close()
         except TypeError:  # interpreter shutdown: the module's globals are already gone, the process frees everything
+            pass
+
+
+class Warp:
+    """The camera warp (fh_warp_*, CameraWarp of warp/gpu.rs) over frames in device memory (rgba8, CUDA pointers).
+
+    Warp(engine, width, height, hfov_deg=106). frame(ptr, t) measures the frame's shift against the previous one on the
+    GPU; collect() hands finished measurements to the calibrator; render_shift / render_into turn a frame. Frames given
+    to frame() must be complete on the device (synchronise the stream that wrote them, or write them on
+    cuda_stream()), and stay unchanged until the next frame() call."""
+
+    def __init__(self, engine: Engine, width: int, height: int, hfov_deg: float = 0.0):
+        self.width, self.height = width, height
+        self._owner = engine
+        self._own = True
+        self._h = lib().fh_warp_create(engine._h, width, height, hfov_deg)
+        if not self._h:
+            raise _error()
+
+    @classmethod
+    def _borrowed(cls, h, owner):
+        w = cls.__new__(cls)
+        w._h, w._owner, w._own = h, owner, False
+        w.width, w.height = owner.width, owner.height
+        return w
+
+    def mouse(self, t: float, dx: float, dy: float) -> None:
+        _check(lib().fh_warp_mouse(self._h, t, dx, dy))
+
+    def set_captured(self, captured: bool) -> None:
+        _check(lib().fh_warp_set_captured(self._h, int(bool(captured))))
+
+    def break_pair(self) -> None:
+        _check(lib().fh_warp_break_pair(self._h))
+
+    def frame(self, device_ptr: int, t: float) -> None:
+        _check(lib().fh_warp_frame(self._h, c_void_p(device_ptr), t))
+
+    def collect(self, wait: bool = False) -> None:
+        _check(lib().fh_warp_collect(self._h, int(wait)))
+
+    def last_shift(self):
+        """The last collected shift (pixels at the centre), or None when it could not be measured."""
+        x, y = c_double(), c_double()
+        return (x.value, y.value) if _check(lib().fh_warp_last_shift(self._h, byref(x), byref(y))) == 1 else None
+
+    def shift(self, t_frame: float, now: float):
+        x, y = c_double(), c_double()
+        return (x.value, y.value) if _check(lib().fh_warp_shift(self._h, t_frame, now, byref(x), byref(y))) else None
+
+    def decide(self, t_frame: float, now: float):
+        x, y = c_double(), c_double()
+        return (x.value, y.value) if _check(lib().fh_warp_decide(self._h, t_frame, now, byref(x), byref(y))) else None
+
+    def render_shift(self, src_ptr: int, sx: float, sy: float) -> int:
+        """src turned by (sx, sy) into the warp's own buffer; its device pointer (valid until the render after next)."""
+        p = lib().fh_warp_render_shift(self._h, c_void_p(src_ptr), sx, sy)
+        if not p:
+            raise _error()
+        return p
+
+    def render_into(self, src_ptr: int, dst_ptr: int, sx: float, sy: float) -> None:
+        _check(lib().fh_warp_render_into(self._h, c_void_p(src_ptr), c_void_p(dst_ptr), sx, sy))
+
+    def cuda_stream(self) -> int:
+        s = c_void_p()
+        _check(lib().fh_warp_cuda_stream(self._h, byref(s)))
+        return s.value or 0
+
+    def read_mask(self):
+        """The screen-locked mask as the lock wrote it, [ceil(h/8)][ceil(w/8)] float32."""
+        import numpy as np
+        gw, gh = (self.width + 7) // 8, (self.height + 7) // 8
+        out = np.zeros((gh, gw), np.float32)
+        _check(lib().fh_warp_read_mask(self._h, out.ctypes.data_as(POINTER(c_float)), out.size))
+        return out
+
+    def tensor(self, name: str):
+        """A warp buffer as float32 (cells0..2, prev_cells0..2, best, sad, mask, grown)."""
+        import numpy as np
+        n = lib().fh_warp_debug_tensor(self._h, name.encode(), None, 0)
+        if n < 0:
+            raise _error()
+        out = np.zeros(n, np.float32)
+        _check(lib().fh_warp_debug_tensor(self._h, name.encode(), out.ctypes.data_as(POINTER(c_float)), n))
+        return out
+
+    def report(self) -> dict:
+        return _json(lib().fh_warp_report_json, self._h)
+
+    def close(self):
+        if getattr(self, "_own", False) and getattr(self, "_h", None):
+            lib().fh_warp_destroy(self._h)
+        self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except TypeError:  # interpreter shutdown
             pass

@@ -1988,6 +1988,14 @@ void static_age(FhSession* s, const int16_t** age, int* pitch, float* min_age) {
 
 bool has_protection_mask(const FhSession* s) { return s->o.protection_mask != 0; }
 
+void frames_read(FhSession* s, uint32_t a, uint32_t b) {
+    s->check_in(a);
+    s->check_in(b);
+    s->mark_read(s->cur_set(a), s->cur_set(b));
+}
+
+int engine_device(const FhEngine* e) { return e->device; }
+
 void session_shape(const FhSession* s, int* w, int* h, int* iw, int* ih, int* k, int* repair) {
     *w = s->w;
     *h = s->h;

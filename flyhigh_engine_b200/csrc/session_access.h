@@ -6,6 +6,7 @@
 #include <string>
 
 struct FhSession;
+struct FhEngine;
 
 namespace fhi {
 
@@ -26,5 +27,10 @@ void output_written(FhSession* s, uint32_t out);
 void static_age(FhSession* s, const int16_t** age, int* pitch, float* min_age);
 // whether the session was built with a protection mask (FhSessionOptions.protection_mask)
 bool has_protection_mask(const FhSession* s);
+// the work issued on the compute stream so far is the last to read input slots a and b (an upload into either waits
+// for it): for readers on other streams that the compute stream has joined
+void frames_read(FhSession* s, uint32_t a, uint32_t b);
+// the CUDA device an engine runs on
+int engine_device(const FhEngine* e);
 
 }  // namespace fhi

@@ -14,6 +14,9 @@
 //   C ABI does.
 // - Repair level 2 (without a protection mask) adds the pan stage (pan.rs): its search after each pair, its apply on
 //   each generated frame.
+// - The camera warp (warp/gpu.rs, warp.h), started by the first mouse call: each pushed frame's shift is measured on
+//   the warp's own stream, forked before the pair is issued so that the two run side by side, and joined into the
+//   session stream after it; fh_stream_warp renders on the session stream.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -21,6 +24,7 @@
 #include <cstdio>
 #include <cstring>
 #include <deque>
+#include <map>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -30,6 +34,7 @@
 #include "../../include/flyhigh_b200.h"
 #include "session_access.h"
 #include "stages.h"
+#include "warp.h"
 
 namespace {
 
@@ -125,13 +130,17 @@ struct FhStream {
     float* pan_fit = nullptr;   // 4 floats
     float* pan_err = nullptr;   // 225 floats
     int pan_a = -1, pan_b = -1;
-    // mouse input (the camera warp itself is not built: it stays off)
-    bool mouse_seen = false, captured = false;
+    // the camera warp (stream/mod.rs:199-202): started by the first mouse call; the input slot it measured last; the
+    // moment each input and output slot shows (arrival time of a pushed frame, phase time of a generated one)
+    std::unique_ptr<FhWarp> warp;
+    int warp_prev = -1;
+    std::map<int, double> in_pts, out_pts;
     // stream/mod.rs:134-150
     unsigned long long pushes = 0, pairs = 0, mids = 0, retimed = 0, source_enough = 0, classified = 0,
                        classify_busy = 0, resets = 0, warped = 0;
 
     ~FhStream() {
+        warp.reset();  // it runs on the session's stream
         if (cst) cudaStreamSynchronize(cst);
         if (stats_dev) cudaFree(stats_dev);
         if (pan_fit) cudaFree(pan_fit);
@@ -225,6 +234,12 @@ struct FhStream {
         if (had) pairs++;
         pushed.emplace_back((int)slot, pts);
         while (pushed.size() > 3) pushed.pop_front();
+        in_pts[(int)slot] = pts;
+        if (warp) {  // stream/mod.rs:393-395, issued before the pair so that the measurement runs beside it
+            const uint8_t *f = nullptr, *f2 = nullptr;
+            fhi::input_frames(s, slot, slot, warp->measure_stream(), &f, &f2);
+            warp->frame(f, pts);
+        }
         FhPush p{};
         p.base_slot = -1;
         have_interval = false;
@@ -247,6 +262,11 @@ struct FhStream {
             base = a.first;
             start_pts = a.second;
             end_pts = b.second;
+        }
+        if (warp) {  // the session stream after the measurement: what reads or rewrites its frames comes later
+            warp->join();
+            fhi::frames_read(s, (uint32_t)(warp_prev >= 0 ? warp_prev : (int)slot), slot);
+            warp_prev = (int)slot;
         }
         if (have_interval) {
             p.ready = 1;
@@ -277,7 +297,44 @@ struct FhStream {
             SCK(fhk::pan_apply(fa, fb, w, h, pan_fit, t, age, pitch, min_age, fhi::output_frame(s, out), st));
             fhi::output_written(s, out);
         }
+        out_pts[(int)out] = start_pts + (double)t * (end_pts - start_pts);
         mids++;
+        return 1;
+    }
+
+    void mouse(double t, double dx, double dy) {  // stream/mod.rs:507-514
+        if (!warp) warp.reset(new FhWarp(w, h, fhwarp::WarpOptions(), fhi::compute_stream(s)));
+        warp->mouse(t, dx, dy);
+    }
+
+    // stream/mod.rs:528-568
+    int turn(bool output, uint32_t slot, uint32_t out, double now) {
+        check_out(out);
+        if (!warp) return 0;
+        const auto& pts = output ? out_pts : in_pts;
+        const auto it = pts.find((int)slot);
+        if (it == pts.end()) return 0;
+        double sx = 0.0, sy = 0.0;
+        if (!warp->decide(it->second, now, &sx, &sy)) return 0;
+        cudaStream_t st = fhi::compute_stream(s);
+        uint8_t* dst = fhi::output_frame(s, out);
+        if (!output) {
+            check_in(slot);
+            const uint8_t *f = nullptr, *f2 = nullptr;
+            fhi::input_frames(s, slot, slot, st, &f, &f2);
+            warp->render_into(f, dst, sx, sy);
+            fhi::frames_read(s, slot, slot);
+        } else if (slot != out) {
+            check_out(slot);
+            warp->render_into(fhi::output_frame(s, slot), dst, sx, sy);
+        } else {
+            const uint8_t* turned = warp->render_shift(fhi::output_frame(s, slot), sx, sy);
+            SCK(cudaMemcpyAsync(dst, turned, (size_t)w * h * 4, cudaMemcpyDeviceToDevice, st));
+        }
+        fhi::output_written(s, out);
+        // `out` now holds a turned frame: turning it again would turn it twice
+        out_pts.erase((int)out);
+        warped++;
         return 1;
     }
 
@@ -287,20 +344,30 @@ struct FhStream {
         have_interval = false;
         last_moving_set = false;
         last_held = false;
+        if (warp) {
+            warp->break_pair();
+            warp_prev = -1;
+        }
     }
 
     std::string report() const {
-        char b[1200];
+        std::string cw = "null";
+        if (warp) {  // calib.rs:38-51, as the reference serialises it
+            const fhwarp::Calibration c = warp->report();
+            char b[320];
+            snprintf(b, sizeof b,
+                     "{\"on\":%s,\"captured\":%s,\"r\":%.17g,\"lag_ms\":%.17g,\"gain_x\":%.17g,\"gain_y\":%.17g}",
+                     c.on ? "true" : "false", c.captured ? "true" : "false", c.r, c.lag_ms, c.gain_x, c.gain_y);
+            cw = b;
+        }
+        char b[1400];
         snprintf(b, sizeof b,
                  "{\"mode\":\"%s\",\"cadence\":false,\"width\":%d,\"height\":%d,\"internal_width\":%d,"
                  "\"internal_height\":%d,\"k\":%d,\"repair\":%d,\"inputs\":%d,\"outputs\":%d,\"pushed\":%zu,"
                  "\"counters\":{\"pushes\":%llu,\"pairs\":%llu,\"mids\":%llu,\"retimed\":%llu,\"source_enough\":%llu,"
                  "\"classified\":%llu,\"classify_busy\":%llu,\"resets\":%llu,\"warped\":%llu},\"camera_warp\":%s}",
                  video ? "video" : "realtime", w, h, iw, ih, k, repair, ninputs, noutputs, pushed.size(), pushes, pairs,
-                 mids, retimed, source_enough, classified, classify_busy, resets, warped,
-                 mouse_seen ? (captured ? "{\"on\":false,\"captured\":true,\"built\":false}"
-                                        : "{\"on\":false,\"captured\":false,\"built\":false}")
-                            : "null");
+                 mids, retimed, source_enough, classified, classify_busy, resets, warped, cw.c_str());
         return b;
     }
 };
@@ -493,10 +560,11 @@ int fh_stream_reset(FhStream* s) {
     });
 }
 
-int fh_stream_mouse(FhStream* s, const FhEngine* e, double, double, double) {
+int fh_stream_mouse(FhStream* s, const FhEngine* e, double t, double dx, double dy) {
     return sguard(-1, [&] {
         if (!s || !e) sfail("null argument");
-        s->mouse_seen = true;
+        SCK(cudaSetDevice(fhi::engine_device(e)));
+        s->mouse(t, dx, dy);
         return 0;
     });
 }
@@ -504,19 +572,23 @@ int fh_stream_mouse(FhStream* s, const FhEngine* e, double, double, double) {
 int fh_stream_set_mouse_captured(FhStream* s, uint32_t captured) {
     return sguard(-1, [&] {
         if (!s) sfail("null argument");
-        s->captured = captured != 0;
+        if (s->warp) s->warp->set_captured(captured != 0);
         return 0;
     });
 }
 
-// stream/mod.rs:518-552: 0 = the warp is off, present the frame as it is (always, in this build)
-int fh_stream_warp(FhStream* s, const FhEngine* e, uint32_t output, uint32_t slot, uint32_t out, double) {
+// capi/src/stream.rs:524-553: 1 = out holds the turned frame, 0 = the warp is off, present the frame as it is
+int fh_stream_warp(FhStream* s, const FhEngine* e, uint32_t output, uint32_t slot, uint32_t out, double now) {
     return sguard(-1, [&] {
         if (!s || !e) sfail("null argument");
-        s->check_out(out);
-        if (output) s->check_out(slot);
-        else s->check_in(slot);
-        return 0;
+        return s->turn(output != 0, slot, out, now);
+    });
+}
+
+FhWarp* fh_stream_camera_warp(FhStream* s) {
+    return sguard((FhWarp*)nullptr, [&]() -> FhWarp* {
+        if (!s) sfail("null argument");
+        return s->warp.get();
     });
 }
 

@@ -96,9 +96,10 @@ int fh_session_report_json(const FhSession* session, char* buf, size_t cap);
  * A Stream owns one session of the options given, its input ring and output slots. Realtime mode runs the pair
  * (previous, newest) when a frame is pushed; video mode keeps one frame of lookahead (the interval that can be generated
  * after a push starts two frames back). Pairs are classified (motion, scene cut, held frame) on the GPU. The camera
- * warp (fh_stream_mouse / _warp) is not part of this build: fh_stream_warp always answers 0 (present the frame as it is)
- * and cadence re-timing (video mode) is refused at creation. Single-threaded use per handle; NULL / -1 and
- * fh_last_error on failure. */
+ * warp starts at the first fh_stream_mouse: every pushed frame's image shift is then measured on the GPU beside the
+ * pair, and fh_stream_warp turns a frame about to be presented by the mouse motion since the moment it shows. Cadence
+ * re-timing (video mode) is refused at creation. Single-threaded use per handle; NULL / -1 and fh_last_error on
+ * failure. */
 typedef struct FhStream FhStream;
 
 typedef struct FhStreamOptions {
@@ -148,9 +149,14 @@ int fh_stream_read_rgba(const FhStream* stream, const FhEngine* engine, uint32_t
 int fh_stream_warm_up(FhStream* stream, const FhEngine* engine);
 int fh_stream_import_d3d11(FhStream* stream, const FhEngine* engine, intptr_t handle, uint32_t width, uint32_t height);
 int fh_stream_reset(FhStream* stream); /* seek, decoder gap */
-/* camera warp: mouse input is recorded (the report shows it) but no frame is turned: warp answers 0 */
+/* mouse counts at time t (the clock of push's pts, which must then be the frames' arrival times in host ms); the
+ * first call starts the camera warp */
 int fh_stream_mouse(FhStream* stream, const FhEngine* engine, double t, double dx, double dy);
+/* captured = 0 (a cursor, a menu) holds the camera warp off at once */
 int fh_stream_set_mouse_captured(FhStream* stream, uint32_t captured);
+/* the frame about to be presented at now, input slot `slot` (output = 0) or output slot `slot` (output = 1, `out`
+ * itself allowed), turned by the mouse motion since the moment it shows into output slot out: 1 = present out; 0 = the
+ * warp is off (no mouse input, released, not following the mouse, under a quarter pixel): present the frame as it is */
 int fh_stream_warp(FhStream* stream, const FhEngine* engine, uint32_t output, uint32_t slot, uint32_t out, double now);
 int fh_stream_report_json(const FhStream* stream, char* buf, size_t cap);
 

@@ -99,6 +99,60 @@ int fh_session_launch_counts(const FhSession* session, int* pair_kernels, int* m
  * fh_last_error. */
 int fh_stream_write_rgba_device(const FhStream* stream, uint32_t slot, const void* dev, size_t len);
 
+/* ---- The camera warp (crates/flyhigh-engine/src/warp/gpu.rs CameraWarp, warp/calib.rs InputCalibrator) ----------
+ *
+ * The object a Stream starts at its first fh_stream_mouse, also usable on its own over frames in device memory
+ * (rgba8, width * height * 4 bytes, row-major). Each source frame's global image shift against the previous one is
+ * measured on the GPU; the calibrator learns from those shifts and the mouse counts how many pixels a count turns the
+ * picture and how late the picture shows it; a frame about to be presented is turned by the camera motion the mouse
+ * made since the moment it shows. Times are host milliseconds on one clock. Functions returning int give 0 (or the
+ * stated value) and -1 with fh_last_error. */
+typedef struct FhWarp FhWarp;
+
+/* CameraWarp::new with WarpOptions::default() (calibration defaults, lock margin 6/255, lock share 0.3), the
+ * horizontal field of view hfov_deg (<= 0: the default 106 degrees). */
+FhWarp* fh_warp_create(const FhEngine* engine, uint32_t width, uint32_t height, double hfov_deg);
+void fh_warp_destroy(FhWarp* warp);
+
+/* Stream::camera_warp: the stream's warp, NULL before its first fh_stream_mouse. Owned by the stream (do not destroy);
+ * its frames arrive through fh_stream_push. */
+FhWarp* fh_stream_camera_warp(FhStream* stream);
+
+/* CameraWarp::mouse / set_captured / break_pair */
+int fh_warp_mouse(FhWarp* warp, double t, double dx, double dy);
+int fh_warp_set_captured(FhWarp* warp, uint32_t captured);
+int fh_warp_break_pair(FhWarp* warp);
+
+/* CameraWarp::frame: a source frame arrived at t. Its shift against the previous frame is measured on the warp's own
+ * measurement stream, forked from the stream fh_warp_cuda_stream returns: the frame must be complete when this is
+ * called (written on that stream, or synchronised). This frame and the previous one must stay unchanged until the
+ * next fh_warp_frame. Nothing waits for the result: it reaches the calibrator at a later collect. */
+int fh_warp_frame(FhWarp* warp, const void* rgba_device, double t);
+/* CameraWarp::collect: measured shifts to the calibrator, oldest first; wait != 0 blocks until all have landed. */
+int fh_warp_collect(FhWarp* warp, int wait);
+/* CameraWarp::last_shift: 1 with the last collected shift (pixels at the centre), 0 when it was not measured. */
+int fh_warp_last_shift(const FhWarp* warp, double* sx, double* sy);
+/* CameraWarp::shift (1 = on, with the shift) and CameraWarp::decide (collects first; 0 also under a quarter pixel). */
+int fh_warp_shift(const FhWarp* warp, double t_frame, double now, double* sx, double* sy);
+int fh_warp_decide(FhWarp* warp, double t_frame, double now, double* sx, double* sy);
+/* CameraWarp::render_shift: the frame turned by a shift (pixels at the centre) into the warp's own buffer, returned
+ * (device, rgba8; valid until the render after next). CameraWarp::render_into: into dst (not src). Both on the stream
+ * fh_warp_cuda_stream returns, after the last measurement. */
+void* fh_warp_render_shift(FhWarp* warp, const void* src_device, double sx, double sy);
+int fh_warp_render_into(FhWarp* warp, const void* src_device, void* dst_device, double sx, double sy);
+/* The stream renders run on (cudaStream_t); a stream's warp: its session's compute stream. */
+int fh_warp_cuda_stream(const FhWarp* warp, void** stream);
+/* CameraWarp::read_mask: the screen-locked mask, 1.0 per locked 8 x 8 block, row-major (ceil(w/8) x ceil(h/8)), as
+ * the lock kernel wrote it (before growing). Blocks. Returns the count; out NULL asks it. */
+long fh_warp_read_mask(const FhWarp* warp, float* out, size_t cap);
+/* A buffer of the warp as f32, for parity tests: cells0..2 / prev_cells0..2 (the newest / previous frame's cell grid
+ * of each pyramid level), best (sx, sy, valid, difference per level), sad (the finest level's candidates: mean
+ * difference, overlap share), mask, grown. Blocks. Returns the count; out NULL asks it. */
+long fh_warp_debug_tensor(const FhWarp* warp, const char* name, float* out, size_t cap);
+/* The calibration (Calibration: on, captured, r, lag_ms, gain_x, gain_y) with last_shift, the size, the focal length
+ * and the warp's kernel launches, as JSON. */
+int fh_warp_report_json(const FhWarp* warp, char* buf, size_t cap);
+
 #ifdef __cplusplus
 }
 #endif

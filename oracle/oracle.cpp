@@ -2125,3 +2125,375 @@ extern "C" int or_threads(int n) {
     if (n > 0) omp_set_num_threads(n);
     return omp_get_max_threads();
 }
+
+// ------------------------------------------------------------------------------------------------ camera warp ----
+// The camera warp's measurement and render (crates/flyhigh-engine/src/warp/gpu.rs with the warp_cells / warp_shift /
+// warp_refine / warp_best / warp_lock / warp_dilate / warp_render shaders), in the arithmetic order the CUDA kernels
+// use: sums of a search in 256 strided partial sums combined pairwise, the minimum taken the same way, so that a test
+// can hold the two to the last bit where no trigonometric function of the device enters.
+namespace camwarp {
+
+constexpr int LV_GW[3] = {32, 128, 512}, LV_GH[3] = {18, 72, 288}, LV_RX[3] = {12, 6, 6}, LV_RY[3] = {6, 6, 6},
+              LV_STRIDE[3] = {1, 1, 2};
+
+// a frame's rgb at (px, py) pixels: bilinear between the nearest pixel centres, clamped to the edge, 0..1
+static void sample(const uint8_t* f, int w, int h, float px, float py, float o[3]) {
+    const float tx = px - 0.5f, ty = py - 0.5f;
+    const float fx0 = floorf(tx), fy0 = floorf(ty);
+    const float ax = tx - fx0, ay = ty - fy0;
+    const int x0 = (int)std::max(std::min(fx0, (float)(w - 1)), -1.0f);
+    const int y0 = (int)std::max(std::min(fy0, (float)(h - 1)), -1.0f);
+    const int xa = std::max(x0, 0), xb = std::min(x0 + 1, w - 1), ya = std::max(y0, 0), yb = std::min(y0 + 1, h - 1);
+    const float bx = 1.0f - ax, by = 1.0f - ay, k = 1.0f / 255.0f;
+    for (int c = 0; c < 3; c++) {
+        const float p00 = f[((size_t)ya * w + xa) * 4 + c], p01 = f[((size_t)ya * w + xb) * 4 + c];
+        const float p10 = f[((size_t)yb * w + xa) * 4 + c], p11 = f[((size_t)yb * w + xb) * 4 + c];
+        o[c] = ((p00 * bx + p01 * ax) * by + (p10 * bx + p11 * ax) * ay) * k;
+    }
+}
+
+// gpu.rs:222-226: focal length (f32), half the horizontal and vertical angle of view
+static void geometry(int w, int h, double hfov, float* f, float* ha, float* he) {
+    const double a = std::min(std::max(hfov, 10.0), 170.0) * 0.5 * 3.14159265358979323846 / 180.0;
+    *f = (float)(0.5 * (double)w / std::tan(a));
+    *ha = (float)a;
+    *he = std::atan(0.5f * (float)h / *f);
+}
+
+// warp_cells.wgsl:12-28
+static void cells(const uint8_t* src, int w, int h, int gw, int gh, float f, float ha, float he, float* out) {
+    const float W = (float)w, H = (float)h;
+    for (int i = 0; i < gw * gh; i++) {
+        const int gx = i % gw, gy = i / gw;
+        float s = 0.0f;
+        bool outside = false;
+        for (int j = 0; j < 2; j++)
+            for (int k = 0; k < 2; k++) {
+                const float ux = ((float)gx + (0.25f + 0.5f * (float)k)) / (float)gw;
+                const float uy = ((float)gy + (0.25f + 0.5f * (float)j)) / (float)gh;
+                const float az = (2.0f * ux - 1.0f) * ha;
+                const float el = (2.0f * uy - 1.0f) * he;
+                const float px = 0.5f * W + f * std::tan(az);
+                const float py = 0.5f * H + f * (std::tan(el) / std::cos(az));
+                outside = outside || px < 0.0f || py < 0.0f || px > W || py > H;
+                float c[3];
+                sample(src, w, h, px, py, c);
+                s += c[0] * 0.299f + c[1] * 0.587f + c[2] * 0.114f;
+            }
+        out[i] = outside ? -1.0f : 0.25f * s;
+    }
+}
+
+// 256 strided partial sums (thread t takes items t, t + 256, ...), combined pairwise: a block reduction's order
+template <class Item>
+static void block_sums(int n, Item item, float* sum, float* cnt) {
+    float s[256] = {}, c[256] = {};
+    for (int t = 0; t < 256; t++)
+        for (int i = t; i < n; i += 256) {
+            float d;
+            if (item(i, &d)) {
+                s[t] += d;
+                c[t] += 1.0f;
+            }
+        }
+    for (int off = 128; off > 0; off >>= 1)
+        for (int t = 0; t < off; t++) {
+            s[t] += s[t + off];
+            c[t] += c[t + off];
+        }
+    *sum = s[0];
+    *cnt = c[0];
+}
+
+// warp_shift.wgsl (level 0) and warp_refine.wgsl (levels 1, 2): sad[cand * 2] = mean difference, [+1] = overlap share
+static void search(int level, const float* A, const float* B, int w, int h, float cw, float ch, float ha, float he,
+                   const float* prior, const float* mask, int mgw, int mgh, float* sad) {
+    const int gw = LV_GW[level], gh = LV_GH[level], rx = LV_RX[level], ry = LV_RY[level], st = LV_STRIDE[level];
+    const int ncx = 2 * rx + 1, ncy = 2 * ry + 1;
+    for (int cand = 0; cand < ncx * ncy; cand++) {
+        float sum, cnt, denom;
+        if (level == 0) {
+            const int dx = cand % ncx - rx, dy = cand / ncx - ry;
+            const int x0 = std::max(0, -dx), x1 = std::min(gw, gw - dx), y0 = std::max(0, -dy), y1 = std::min(gh, gh - dy);
+            const int ow = std::max(x1 - x0, 0), n = ow * std::max(y1 - y0, 0);
+            block_sums(
+                n,
+                [&](int i, float* d) {
+                    const int ax = x0 + i % ow, ay = y0 + i / ow;
+                    const float va = A[ay * gw + ax], vb = B[(ay + dy) * gw + ax + dx];
+                    if (va < 0.0f || vb < 0.0f) return false;
+                    *d = fabsf(va - vb);
+                    return true;
+                },
+                &sum, &cnt);
+            denom = (float)(gw * gh);
+        } else {
+            const int bx0 = (int)rintf(prior[0] / cw), by0 = (int)rintf(prior[1] / ch);
+            const int dx = bx0 + cand % ncx - rx, dy = by0 + cand / ncx - ry;
+            const int hw = (gw + st - 1) / st, n = hw * ((gh + st - 1) / st);
+            const float f = cw * (float)gw / (2.0f * ha);
+            block_sums(
+                n,
+                [&](int i, float* d) {
+                    const int ax = (i % hw) * st, ay = (i / hw) * st;
+                    const float az = (((float)ax + 0.5f) / (float)gw * 2.0f - 1.0f) * ha;
+                    const int bx = ax + dx;
+                    const float byf = (float)ay + (float)dy * std::cos(az);
+                    const float fby = floorf(byf);
+                    const int by = (int)fby;
+                    const float fy = byf - fby;
+                    if (bx < 0 || by < 0 || bx >= gw || by + 1 >= gh) return false;
+                    const float va = A[ay * gw + ax], b0 = B[by * gw + bx], b1 = B[(by + 1) * gw + bx];
+                    if (va < 0.0f || b0 < 0.0f || b1 < 0.0f) return false;
+                    const float el = (((float)ay + 0.5f) / (float)gh * 2.0f - 1.0f) * he;
+                    const float px = 0.5f * (float)w + f * std::tan(az);
+                    const float py = 0.5f * (float)h + f * (std::tan(el) / std::cos(az));
+                    const int mx = std::min((int)(std::max(px, 0.0f) / 8.0f), mgw - 1);
+                    const int my = std::min((int)(std::max(py, 0.0f) / 8.0f), mgh - 1);
+                    if (mask[my * mgw + mx] > 0.5f) return false;
+                    *d = fabsf(va - (b0 * (1.0f - fy) + b1 * fy));
+                    return true;
+                },
+                &sum, &cnt);
+            denom = (float)n;
+        }
+        sad[cand * 2] = sum / std::max(cnt, 1.0f);
+        sad[cand * 2 + 1] = cnt / denom;
+    }
+}
+
+// warp_best.wgsl:20-62: [sx, sy, valid, difference] in pixels
+static void best(int level, const float* sad, float cw, float ch, const float* coarse, float* out) {
+    const int rx = LV_RX[level], ry = LV_RY[level], ncx = 2 * rx + 1, ncy = 2 * ry + 1, n = ncx * ncy;
+    float v[256], s[256] = {}, c[256] = {};
+    unsigned bi[256];
+    for (int t = 0; t < 256; t++) {
+        v[t] = 1e9f;
+        bi[t] = 0;
+        for (int i = t; i < n; i += 256) {
+            if (sad[i * 2 + 1] < 0.4f) continue;
+            const float x = sad[i * 2];
+            s[t] += x;
+            c[t] += 1.0f;
+            if (x < v[t]) {
+                v[t] = x;
+                bi[t] = (unsigned)i;
+            }
+        }
+    }
+    for (int off = 128; off > 0; off >>= 1)
+        for (int t = 0; t < off; t++) {
+            if (v[t + off] < v[t]) {
+                v[t] = v[t + off];
+                bi[t] = bi[t + off];
+            }
+            s[t] += s[t + off];
+            c[t] += c[t + off];
+        }
+    auto value = [&](int x, int y) -> float {
+        if (x < 0 || y < 0 || x >= ncx || y >= ncy) return 1e9f;
+        const int i = y * ncx + x;
+        return sad[i * 2 + 1] >= 0.4f ? sad[i * 2] : 1e9f;
+    };
+    const float v0 = v[0], mean = s[0] / std::max(c[0], 1.0f);
+    const int cx = (int)(bi[0] % (unsigned)ncx), cy = (int)(bi[0] / (unsigned)ncx);
+    float fx = 0.0f, fy = 0.0f;
+    const float l = value(cx - 1, cy), r = value(cx + 1, cy);
+    if (l < 1e8f && r < 1e8f && l + r - 2.0f * v0 > 1e-6f)
+        fx = std::min(std::max(0.5f * (l - r) / (l + r - 2.0f * v0), -0.5f), 0.5f);
+    const float u = value(cx, cy - 1), d = value(cx, cy + 1);
+    if (u < 1e8f && d < 1e8f && u + d - 2.0f * v0 > 1e-6f)
+        fy = std::min(std::max(0.5f * (u - d) / (u + d - 2.0f * v0), -0.5f), 0.5f);
+    float bx = 0.0f, by = 0.0f;
+    bool valid = v0 < 1e8f && v0 < 0.6f * mean;
+    if (level > 0) {
+        bx = rintf(coarse[0] / cw);
+        by = rintf(coarse[1] / ch);
+        valid = v0 < 1e8f && coarse[2] > 0.5f;
+    }
+    out[0] = (bx + (float)(cx - rx) + fx) * cw;
+    out[1] = (by + (float)(cy - ry) + fy) * ch;
+    out[2] = valid ? 1.0f : 0.0f;
+    out[3] = v0;
+}
+
+// warp_lock.wgsl:22-40; score (optional): e_moved - e_still - max(margin, rel * e_moved), NaN where unchanged
+static void lock(const uint8_t* a, const uint8_t* b, int w, int h, const float* bst, float margin, float rel, float f,
+                 float* mask, float* score) {
+    const int gw = (w + 7) / 8, gh = (h + 7) / 8;
+    const float sx = bst[0], sy = bst[1];
+    if (score)
+        for (int i = 0; i < gw * gh; i++) score[i] = NAN;
+    if (bst[2] < 0.5f || std::sqrt(sx * sx + sy * sy) < 4.0f) return;
+    const float W = (float)w, H = (float)h, cx = 0.5f * W, cy = 0.5f * H;
+    const float ty = sx / f, tp = sy / f;
+    const float cty = std::cos(ty), sty = std::sin(ty), ctp = std::cos(tp), stp = std::sin(tp);
+    for (int gy = 0; gy < gh; gy++)
+        for (int gx = 0; gx < gw; gx++) {
+            float es = 0.0f, em = 0.0f;
+            for (int j = 0; j < 4; j++)
+                for (int i = 0; i < 4; i++) {
+                    const float px = (float)(gx * 8 + i * 2) + 1.0f, py = (float)(gy * 8 + j * 2) + 1.0f;
+                    float cb[3], ca[3], cm[3];
+                    sample(b, w, h, px, py, cb);
+                    sample(a, w, h, px, py, ca);
+                    float dx = (px - cx) / f, dy = (py - cy) / f, dz = 1.0f;
+                    const float rx = dx * cty - dz * sty, rz = dx * sty + dz * cty;
+                    dx = rx;
+                    dz = rz;
+                    const float qy = dy * ctp - dz * stp, qz = dy * stp + dz * ctp;
+                    dy = qy;
+                    dz = qz;
+                    const float m = std::max(dz, 1e-3f);
+                    sample(a, w, h, cx + f * dx / m, cy + f * dy / m, cm);
+                    es += fabsf(ca[0] - cb[0]) * (1.0f / 3.0f) + fabsf(ca[1] - cb[1]) * (1.0f / 3.0f) +
+                          fabsf(ca[2] - cb[2]) * (1.0f / 3.0f);
+                    em += fabsf(cm[0] - cb[0]) * (1.0f / 3.0f) + fabsf(cm[1] - cb[1]) * (1.0f / 3.0f) +
+                          fabsf(cm[2] - cb[2]) * (1.0f / 3.0f);
+                }
+            es /= 16.0f;
+            em /= 16.0f;
+            const float sc = em - es - std::max(margin, rel * em);
+            mask[gy * gw + gx] = em - es > std::max(margin, rel * em) ? 1.0f : 0.0f;
+            if (score) score[gy * gw + gx] = sc;
+        }
+}
+
+// warp_dilate.wgsl
+static void dilate(const float* mask, int gw, int gh, float* grown) {
+    for (int y = 0; y < gh; y++)
+        for (int x = 0; x < gw; x++) {
+            float m = 0.0f;
+            for (int j = -1; j <= 1; j++)
+                for (int i = -1; i <= 1; i++)
+                    m = std::max(m, mask[std::min(std::max(y + j, 0), gh - 1) * gw + std::min(std::max(x + i, 0), gw - 1)]);
+            grown[y * gw + x] = m;
+        }
+}
+
+}  // namespace camwarp
+
+extern "C" {
+
+// focal length, half angles of view (gpu.rs:222-226)
+int or_warp_geometry(int w, int h, double hfov, float* out3) {
+    camwarp::geometry(w, h, hfov, &out3[0], &out3[1], &out3[2]);
+    return 0;
+}
+
+// one frame's cell grid of pyramid level `level`
+int or_warp_cells(const uint8_t* frame, int w, int h, int level, double hfov, float* out) {
+    float f, ha, he;
+    camwarp::geometry(w, h, hfov, &f, &ha, &he);
+    camwarp::cells(frame, w, h, camwarp::LV_GW[level], camwarp::LV_GH[level], f, ha, he, out);
+    return 0;
+}
+
+// one level's search and minimum from given cell grids (prev a, newest b), the level above's result (coarse, 4
+// floats; ignored at level 0) and the lock mask: sad_out [candidates][2], best_out [4]
+int or_warp_level(int level, const float* a, const float* b, int w, int h, double hfov, const float* coarse,
+                  const float* mask, float* sad_out, float* best_out) {
+    float f, ha, he;
+    camwarp::geometry(w, h, hfov, &f, &ha, &he);
+    const float cw = f * 2.0f * ha / (float)camwarp::LV_GW[level], ch = f * 2.0f * he / (float)camwarp::LV_GH[level];
+    camwarp::search(level, a, b, w, h, cw, ch, ha, he, coarse, mask, (w + 7) / 8, (h + 7) / 8, sad_out);
+    camwarp::best(level, sad_out, cw, ch, coarse, best_out);
+    return 0;
+}
+
+// a whole measurement of (prev, frame): cells, the three levels, the lock and the dilate. mask: the lock mask before
+// (read by the refine levels) and after; best_out [3][4]; grown_out [mgh][mgw]; score_out (optional, mgw * mgh)
+int or_warp_measure(const uint8_t* prev, const uint8_t* frame, int w, int h, double hfov, float lock_margin,
+                    float lock_rel, float* mask, float* best_out, float* grown_out, float* score_out) {
+    float f, ha, he;
+    camwarp::geometry(w, h, hfov, &f, &ha, &he);
+    const int mgw = (w + 7) / 8, mgh = (h + 7) / 8;
+    const float zero[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int l = 0; l < 3; l++) {
+        const int gw = camwarp::LV_GW[l], gh = camwarp::LV_GH[l];
+        std::vector<float> A((size_t)gw * gh), B((size_t)gw * gh), sad(2 * 25 * 13);
+        camwarp::cells(prev, w, h, gw, gh, f, ha, he, A.data());
+        camwarp::cells(frame, w, h, gw, gh, f, ha, he, B.data());
+        const float cw = f * 2.0f * ha / (float)gw, ch = f * 2.0f * he / (float)gh;
+        const float* coarse = l ? best_out + (l - 1) * 4 : zero;
+        camwarp::search(l, A.data(), B.data(), w, h, cw, ch, ha, he, coarse, mask, mgw, mgh, sad.data());
+        camwarp::best(l, sad.data(), cw, ch, coarse, best_out + l * 4);
+    }
+    camwarp::lock(prev, frame, w, h, best_out + 8, lock_margin, lock_rel, f, mask, score_out);
+    camwarp::dilate(mask, mgw, mgh, grown_out);
+    return 0;
+}
+
+// the lock alone on a given result (4 floats): mask updated in place, score as in or_warp_measure
+int or_warp_lock(const uint8_t* prev, const uint8_t* frame, int w, int h, double hfov, const float* bst,
+                 float lock_margin, float lock_rel, float* mask, float* score_out) {
+    float f, ha, he;
+    camwarp::geometry(w, h, hfov, &f, &ha, &he);
+    camwarp::lock(prev, frame, w, h, bst, lock_margin, lock_rel, f, mask, score_out);
+    return 0;
+}
+
+int or_warp_dilate(const float* mask, int gw, int gh, float* grown) {
+    camwarp::dilate(mask, gw, gh, grown);
+    return 0;
+}
+
+// warp_render.wgsl:18-51: src turned by (sx, sy) pixels at the centre, the grown mask's blocks kept; rgba8 out
+int or_warp_render(const uint8_t* src, int w, int h, double hfov, const float* grown, float sx, float sy, uint8_t* dst) {
+    float f, ha, he;
+    camwarp::geometry(w, h, hfov, &f, &ha, &he);
+    const int gw = (w + 7) / 8, gh = (h + 7) / 8;
+    const float ty = sx / f, tp = sy / f;
+    const float cty = std::cos(ty), sty = std::sin(ty), ctp = std::cos(tp), stp = std::sin(tp);
+    const float W = (float)w, H = (float)h, cx = 0.5f * W, cy = 0.5f * H;
+    auto locked = [&](int x, int y) {
+        return grown[std::min(std::max(y, 0), gh - 1) * gw + std::min(std::max(x, 0), gw - 1)];
+    };
+#pragma omp parallel for
+    for (int y = 0; y < h; y++)
+        for (int x = 0; x < w; x++) {
+            const float px = (float)x + 0.5f, py = (float)y + 0.5f;
+            float dx = (px - cx) / f, dy = (py - cy) / f, dz = 1.0f;
+            const float rx = dx * cty - dz * sty, rz = dx * sty + dz * cty;
+            dx = rx;
+            dz = rz;
+            const float qy = dy * ctp - dz * stp, qz = dy * stp + dz * ctp;
+            dy = qy;
+            dz = qz;
+            const float m = std::max(dz, 1e-3f);
+            const float ssx = cx + f * dx / m, ssy = cy + f * dy / m;
+            float col[3];
+            if (dz > 1e-3f && ssx >= 0.0f && ssy >= 0.0f && ssx <= W && ssy <= H) {
+                camwarp::sample(src, w, h, ssx, ssy, col);
+            } else {
+                const float ex = std::min(std::max(ssx, 0.0f), W), ey = std::min(std::max(ssy, 0.0f), H);
+                col[0] = col[1] = col[2] = 0.0f;
+                for (int j = -2; j <= 2; j++)
+                    for (int i = -2; i <= 2; i++) {
+                        float c[3];
+                        camwarp::sample(src, w, h, std::min(std::max(ex + 6.0f * (float)i, 0.0f), W),
+                                        std::min(std::max(ey + 6.0f * (float)j, 0.0f), H), c);
+                        col[0] += c[0];
+                        col[1] += c[1];
+                        col[2] += c[2];
+                    }
+                for (float& c : col) c /= 25.0f;
+            }
+            const float gxf = px / 8.0f - 0.5f, gyf = py / 8.0f - 0.5f;
+            const float g0x = floorf(gxf), g0y = floorf(gyf), frx = gxf - g0x, fry = gyf - g0y;
+            const int ix = (int)g0x, iy = (int)g0y;
+            const float top = locked(ix, iy) * (1.0f - frx) + locked(ix + 1, iy) * frx;
+            const float bot = locked(ix, iy + 1) * (1.0f - frx) + locked(ix + 1, iy + 1) * frx;
+            const float mk = top * (1.0f - fry) + bot * fry;
+            const uint8_t* own = src + ((size_t)y * w + x) * 4;
+            uint8_t* o = dst + ((size_t)y * w + x) * 4;
+            for (int c = 0; c < 3; c++) {
+                const float v = col[c] * (1.0f - mk) + (float)own[c] * (1.0f / 255.0f) * mk;
+                o[c] = (uint8_t)rintf(std::min(std::max(v, 0.0f), 1.0f) * 255.0f);
+            }
+            o[3] = 255;
+        }
+    return 0;
+}
+
+}  // extern "C"

@@ -57,6 +57,14 @@ def lib():
         L.or_gmhs_select.argtypes = [c_void_p, POINTER(c_float), c_int, c_int, POINTER(c_float)]
         L.or_classify.argtypes = [POINTER(c_uint8), POINTER(c_uint8), c_int, c_int, c_int, c_int, POINTER(ctypes.c_uint32)]
         L.or_pan_search.argtypes = [POINTER(c_uint8), POINTER(c_uint8), c_int, c_int, POINTER(c_float)]
+        F, U8 = POINTER(c_float), POINTER(c_uint8)
+        L.or_warp_geometry.argtypes = [c_int, c_int, ctypes.c_double, F]
+        L.or_warp_cells.argtypes = [U8, c_int, c_int, c_int, ctypes.c_double, F]
+        L.or_warp_level.argtypes = [c_int, F, F, c_int, c_int, ctypes.c_double, F, F, F, F]
+        L.or_warp_measure.argtypes = [U8, U8, c_int, c_int, ctypes.c_double, c_float, c_float, F, F, F, F]
+        L.or_warp_lock.argtypes = [U8, U8, c_int, c_int, ctypes.c_double, F, c_float, c_float, F, F]
+        L.or_warp_dilate.argtypes = [F, c_int, c_int, F]
+        L.or_warp_render.argtypes = [U8, c_int, c_int, ctypes.c_double, F, c_float, c_float, U8]
         L.or_pan_apply.argtypes = [POINTER(c_uint8), POINTER(c_uint8), c_int, c_int, POINTER(c_float), c_float,
                                    POINTER(c_float), c_int, c_float, POINTER(c_uint8)]
         L.or_tex_down.argtypes = [POINTER(c_uint8), c_int, c_int, c_int, c_int, POINTER(c_uint16)]
@@ -410,4 +418,83 @@ def pan_apply(fa, fb, w, h, fit, t, frame, age=None, min_age=0.0):
     f = lambda a: a.ctypes.data_as(POINTER(c_float))
     lib().or_pan_apply(_u8(fa), _u8(fb), w, h, f(fit), c_float(t), f(ag) if ag is not None else None, pitch,
                        c_float(min_age), _u8(out))
+    return out
+
+
+# ---- the camera warp (crates/flyhigh-engine/src/warp/gpu.rs and its warp_* shaders) --------------------------------
+
+WARP_LEVELS = ((32, 18, 12, 6, 1), (128, 72, 6, 6, 1), (512, 288, 6, 6, 2))  # grid w, h, range x, y, stride
+WARP_HFOV = 106.0
+WARP_LOCK_MARGIN = 6.0 / 255.0
+WARP_LOCK_REL = 0.3
+
+
+def _f32p(a):
+    return a.ctypes.data_as(POINTER(c_float))
+
+
+def warp_geometry(w, h, hfov=WARP_HFOV):
+    """(focal length, half horizontal angle, half vertical angle), f32 (gpu.rs:222-226)."""
+    out = np.zeros(3, np.float32)
+    lib().or_warp_geometry(w, h, hfov, _f32p(out))
+    return out
+
+
+def warp_cells(frame, w, h, level, hfov=WARP_HFOV):
+    """warp_cells.wgsl: the frame's cell grid at pyramid level `level`, [gh][gw] f32 (-1 outside the frame)."""
+    gw, gh = WARP_LEVELS[level][:2]
+    out = np.zeros((gh, gw), np.float32)
+    lib().or_warp_cells(_u8(np.ascontiguousarray(frame, np.uint8)), w, h, level, hfov, _f32p(out))
+    return out
+
+
+def warp_level(level, cells_a, cells_b, w, h, coarse, mask, hfov=WARP_HFOV):
+    """warp_shift / warp_refine + warp_best of one level from given grids: (sad [cand][2], best [4])."""
+    rx, ry = WARP_LEVELS[level][2:4]
+    sad = np.zeros(((2 * rx + 1) * (2 * ry + 1), 2), np.float32)
+    bst = np.zeros(4, np.float32)
+    a = np.ascontiguousarray(cells_a, np.float32)
+    b = np.ascontiguousarray(cells_b, np.float32)
+    c = np.ascontiguousarray(coarse, np.float32)
+    m = np.ascontiguousarray(mask, np.float32)
+    lib().or_warp_level(level, _f32p(a), _f32p(b), w, h, hfov, _f32p(c), _f32p(m), _f32p(sad), _f32p(bst))
+    return sad, bst
+
+
+def warp_measure(prev, frame, w, h, mask=None, hfov=WARP_HFOV):
+    """A whole measurement of (prev, frame): (best [3][4], mask after, grown, lock score). mask: the lock mask before
+    (zeros by default), [ceil(h/8)][ceil(w/8)]."""
+    mgw, mgh = (w + 7) // 8, (h + 7) // 8
+    m = np.zeros((mgh, mgw), np.float32) if mask is None else np.array(mask, np.float32, copy=True)
+    bst = np.zeros((3, 4), np.float32)
+    grown = np.zeros((mgh, mgw), np.float32)
+    score = np.zeros((mgh, mgw), np.float32)
+    lib().or_warp_measure(_u8(np.ascontiguousarray(prev, np.uint8)), _u8(np.ascontiguousarray(frame, np.uint8)), w, h,
+                          hfov, WARP_LOCK_MARGIN, WARP_LOCK_REL, _f32p(m), _f32p(bst), _f32p(grown), _f32p(score))
+    return bst, m, grown, score
+
+
+def warp_lock(prev, frame, w, h, best, mask, hfov=WARP_HFOV):
+    """warp_lock.wgsl on a given result: (mask after, score = e_moved - e_still - max(margin, rel * e_moved); NaN where
+    the lock did not run)."""
+    m = np.array(mask, np.float32, copy=True)
+    score = np.zeros_like(m)
+    b = np.ascontiguousarray(best, np.float32)
+    lib().or_warp_lock(_u8(np.ascontiguousarray(prev, np.uint8)), _u8(np.ascontiguousarray(frame, np.uint8)), w, h,
+                       hfov, _f32p(b), WARP_LOCK_MARGIN, WARP_LOCK_REL, _f32p(m), _f32p(score))
+    return m, score
+
+
+def warp_dilate(mask):
+    m = np.ascontiguousarray(mask, np.float32)
+    out = np.zeros_like(m)
+    lib().or_warp_dilate(_f32p(m), m.shape[1], m.shape[0], _f32p(out))
+    return out
+
+
+def warp_render(src, w, h, grown, sx, sy, hfov=WARP_HFOV):
+    """warp_render.wgsl: src turned by (sx, sy) px at the centre, the grown mask's blocks kept; rgba8 [h][w][4]."""
+    out = np.zeros((h, w, 4), np.uint8)
+    g = np.ascontiguousarray(grown, np.float32)
+    lib().or_warp_render(_u8(np.ascontiguousarray(src, np.uint8)), w, h, hfov, _f32p(g), sx, sy, _u8(out))
     return out

@@ -43,7 +43,8 @@ static void play(double secs, double menu0, double menu1, std::vector<double>& r
     for (size_t k = 0; k < (size_t)(secs * 1.6); k++) {
         const double t0 = 500.0 + r.f() * (secs * 1000.0 - 1000.0);
         const double d = 40.0 + 80.0 * r.f();
-        const double amp = (r.f() < 0.5 ? -1.0 : 1.0) * (2.0 + 9.0 * r.f());
+        const double sign = r.f() < 0.5 ? -1.0 : 1.0;  // drawn before the magnitude, as the reference's play draws them
+        const double amp = sign * (2.0 + 9.0 * r.f());
         for (size_t i = 0; i < n; i++) {
             const double t = (double)i;
             if (t >= t0 && t < t0 + d) rate[i] += amp * std::sin(PI * (t - t0) / d);
