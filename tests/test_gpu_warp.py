@@ -52,9 +52,9 @@ def _scaled_lock(w, h):
 
 @pytest.mark.parametrize("w,h", [(640, 360), (1920, 1080)])
 def test_kernels_match_oracle(torch_cuda, engine, w, h):
-    """One measured pair and a render: the cell grids within f32 rounding of the trigonometric functions, each level's
-    search and minimum from the GPU's own grids to 1e-4 px, the lock mask equal wherever its score is not within 1e-4 of
-    the threshold, the grown mask and the rendered bytes equal."""
+    """One measured pair and a render: the cell grids within the last-bit differences of the trigonometric functions,
+    each level's search and minimum from the GPU's own grids to 1e-4 px, the lock mask equal wherever its score is not
+    within 1e-4 of the threshold, the grown mask and the rendered bytes equal."""
     import flyhigh_engine_b200 as fh
     from oracle import oracle as orc
     torch = torch_cuda
@@ -73,7 +73,9 @@ def test_kernels_match_oracle(torch_cuda, engine, w, h):
             for got, src in ((ga, a), (gb, b)):
                 want = orc.warp_cells(src, w, h, lv)
                 assert np.array_equal(got < 0, want < 0), f"level {lv}: cells outside the frame differ"
-                assert np.abs(got - want).max() <= 1e-5, (lv, float(np.abs(got - want).max()))
+                # the device's and the host's tanf / cosf differ in the last bit: a sample point moves by up to
+                # f * 2 ulp (about 1e-4 px at 1080p), a cell's luma by that times its slope (at most 1 per px)
+                assert np.abs(got - want).max() <= 1e-4, (lv, float(np.abs(got - want).max()))
             coarse = gbest[lv - 1] if lv else np.zeros(4, np.float32)
             _, want_best = orc.warp_level(lv, ga, gb, w, h, coarse, np.zeros((mgh, mgw), np.float32))
             assert gbest[lv][2] == want_best[2], (lv, gbest[lv], want_best)
