@@ -60,6 +60,25 @@ class _Push(Structure):  # flyhigh.h FhPush
                 ("start_pts", c_double), ("end_pts", c_double)]
 
 
+class GeneratorOptions(Structure):  # flyhigh.h FhOptions, field for field
+    _fields_ = [(n, c_uint32) for n in ("width", "height", "k", "internal_w", "internal_h", "mode", "repair", "cadence",
+                                        "render_sampling", "keep_static", "static_frames", "static_tolerance",
+                                        "fast_render", "linear_t")]
+
+
+class PacerOptions(Structure):  # flyhigh.h FhPacerOptions (the Pacer is declared, not built)
+    _fields_ = [("mode", c_uint32), ("factor", c_uint32), ("target_fps", c_double), ("max_factor", c_uint32),
+                ("fps_limit", c_double), ("lookahead", c_uint32), ("limit_to_display", c_uint32),
+                ("fill_display", c_uint32), ("display_headroom", c_double), ("compute_budget", c_double),
+                ("delay_floor_ms", c_double), ("delay_max_ms", c_double), ("lateness_intervals", c_double),
+                ("queue_capacity", c_uint32), ("pressure_tau_ms", c_double), ("penalty_up", c_double),
+                ("penalty_burst", c_double), ("penalty_min_gap_ms", c_double), ("penalty_max", c_uint32),
+                ("recovery_after_ms", c_double), ("stall_window_ms", c_double), ("stall_rate_limit", c_double),
+                ("settle_ms", c_double), ("motion_adaptive", c_uint32), ("min_present_interval_ms", c_double),
+                ("playback_rate", c_double), ("mid_cost_seed_ms", c_double), ("pair_cost_seed_ms", c_double),
+                ("gpu_timestamps", c_uint32), ("low_latency", c_uint32)]
+
+
 def library_path() -> str:
     env = os.environ.get("FLYHIGH_LIB")
     if env:
@@ -135,6 +154,39 @@ EXPORTS = [
     ("fh_stream_warp", c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_uint32, c_double]),
     ("fh_stream_report_json", c_int, [c_void_p, c_char_p, c_size_t]),
     ("fh_stream_camera_warp", c_void_p, [c_void_p]),
+    ("fh_options_default", GeneratorOptions, [c_uint32, c_uint32]),
+    ("fh_generator_create", c_void_p, [c_void_p, c_void_p, POINTER(GeneratorOptions)]),
+    ("fh_generator_destroy", None, [c_void_p]),
+    ("fh_generator_warmup", c_int, [c_void_p]),
+    ("fh_generator_push", c_int, [c_void_p, c_void_p, c_size_t, c_uint32]),
+    ("fh_generator_pop", c_int, [c_void_p, c_void_p, c_size_t, POINTER(c_float), POINTER(c_int)]),
+    ("fh_pacer_options_default", PacerOptions, []),
+    ("fh_pacer_create", c_void_p, [POINTER(PacerOptions)]),
+    ("fh_pacer_destroy", None, [c_void_p]),
+    ("fh_pacer_set_options", c_int, [c_void_p, c_double, POINTER(PacerOptions)]),
+    ("fh_pacer_tick", c_int, [c_void_p, c_double, c_void_p]),
+    ("fh_pacer_source_frame", c_int, [c_void_p, c_double, c_void_p]),
+    ("fh_pacer_requests", c_int, [c_void_p, c_void_p, c_size_t]),
+    ("fh_pacer_generated", c_int, [c_void_p, c_double, ctypes.c_uint64, c_uint32]),
+    ("fh_pacer_skipped", c_int, [c_void_p, ctypes.c_uint64]),
+    ("fh_pacer_cost_sample", c_int, [c_void_p, c_double, c_uint32, c_double]),
+    ("fh_pacer_host_stall", c_int, [c_void_p, c_double, c_double]),
+    ("fh_pacer_mode_change", c_int, [c_void_p, c_double]),
+    ("fh_pacer_reset", c_int, [c_void_p, c_double]),
+    ("fh_pacer_report_json", c_int, [c_void_p, c_char_p, c_size_t]),
+    ("fh_pacer_record", c_int, [c_void_p, c_char_p]),
+    ("fh_pacer_trace_json", c_int, [c_void_p, c_char_p, c_size_t]),
+    ("fh_engine_vulkan_interop", c_int, [c_void_p, c_void_p]),
+    ("fh_vk_row_pitch", c_uint32, [c_uint32]),
+    ("fh_vk_buffer_import", c_void_p, [c_void_p, c_void_p, ctypes.c_uint64]),
+    ("fh_vk_buffer_destroy", None, [c_void_p]),
+    ("fh_vk_semaphore_import", c_void_p, [c_void_p, ctypes.c_ssize_t, c_uint32]),
+    ("fh_vk_semaphore_destroy", None, [c_void_p]),
+    ("fh_vk_signal", c_int, [c_void_p, c_void_p, ctypes.c_uint64]),
+    ("fh_stream_copy_in", c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint32, c_void_p, ctypes.c_uint64]),
+    ("fh_stream_copy_out", c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint32, c_void_p, ctypes.c_uint64]),
+    ("fh_session_copy_in", c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint32, c_void_p, ctypes.c_uint64]),
+    ("fh_session_copy_out", c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint32, c_void_p, ctypes.c_uint64]),
     ("fh_warp_create", c_void_p, [c_void_p, c_uint32, c_uint32, c_double]),
     ("fh_warp_destroy", None, [c_void_p]),
     ("fh_warp_mouse", c_int, [c_void_p, c_double, c_double, c_double]),
@@ -741,6 +793,74 @@ class Warp:
         if getattr(self, "_own", False) and getattr(self, "_h", None):
             lib().fh_warp_destroy(self._h)
         self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except TypeError:  # interpreter shutdown
+            pass
+
+
+class Generator:
+    """Source frames in, the frames to display out, in order (fh_generator_*, api.rs Generator).
+
+    Generator(engine, model, width, height, mode="realtime" | "video", k=1, internal=None, repair=1, render="model",
+    keep_static=True, static_frames=8, static_tolerance=4, fast_render=False, linear_t=False). push(rgba, factor)
+    queues the frames to display; pop() takes the next as (rgba bytes, phase, real), or None."""
+
+    def __init__(self, engine: Engine, model: Model, width: int, height: int, mode: str = "realtime", k: int = 1,
+                 internal=None, repair: int = 1, render: str = "model", keep_static: bool = True,
+                 static_frames: int = 8, static_tolerance: int = 4, fast_render: bool = False,
+                 linear_t: bool = False, cadence: bool = False):
+        L = lib()
+        o = L.fh_options_default(width, height)
+        o.k, o.mode, o.repair, o.cadence = k, _MODE[mode], repair, int(cadence)
+        if internal is not None:
+            o.internal_w, o.internal_h = internal
+        o.render_sampling = _RENDER[render]
+        o.keep_static, o.static_frames, o.static_tolerance = int(keep_static), static_frames, static_tolerance
+        o.fast_render, o.linear_t = int(fast_render), int(linear_t)
+        self.width, self.height = width, height
+        self._e, self._m = engine, model
+        self._h = L.fh_generator_create(engine._h, model._h, byref(o))
+        if not self._h:
+            raise _error()
+
+    def warmup(self) -> int:
+        return _check(lib().fh_generator_warmup(self._h))
+
+    def push(self, rgba, factor: int = 2) -> int:
+        p, n, _keep = _buffer(rgba)
+        return _check(lib().fh_generator_push(self._h, p, n, factor))
+
+    def pop(self):
+        n = self.width * self.height * 4
+        buf = (c_uint8 * n)()
+        phase, real = c_float(), c_int()
+        if _check(lib().fh_generator_pop(self._h, ctypes.cast(buf, c_void_p), n, byref(phase), byref(real))) == 0:
+            return None
+        return bytes(buf), phase.value, bool(real.value)
+
+    def frames(self, rgba, factor: int = 2) -> list:
+        """push, then every queued frame as (rgba bytes, phase, real)."""
+        self.push(rgba, factor)
+        out = []
+        while True:
+            f = self.pop()
+            if f is None:
+                return out
+            out.append(f)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().fh_generator_destroy(self._h)
+            self._h = None
 
     def __enter__(self):
         return self

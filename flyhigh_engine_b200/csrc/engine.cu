@@ -1996,6 +1996,8 @@ void frames_read(FhSession* s, uint32_t a, uint32_t b) {
 
 int engine_device(const FhEngine* e) { return e->device; }
 
+void default_internal_size(int w, int h, int* iw, int* ih) { default_internal(w, h, *iw, *ih); }
+
 void session_shape(const FhSession* s, int* w, int* h, int* iw, int* ih, int* k, int* repair) {
     *w = s->w;
     *h = s->h;

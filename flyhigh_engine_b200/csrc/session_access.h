@@ -32,5 +32,7 @@ bool has_protection_mask(const FhSession* s);
 void frames_read(FhSession* s, uint32_t a, uint32_t b);
 // the CUDA device an engine runs on
 int engine_device(const FhEngine* e);
+// the network size a session of a w x h frame takes when the host gives none (options.rs:348-356)
+void default_internal_size(int w, int h, int* iw, int* ih);
 
 }  // namespace fhi

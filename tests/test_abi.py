@@ -122,6 +122,19 @@ def test_options_defaults_match_the_reference():
     assert (o.width, o.height, o.internal_w, o.internal_h, o.k, o.repair, o.render) == (1920, 1080, 0, 0, 1, 1, 0)
     assert (o.keep_static, o.static_frames, o.static_tolerance) == (1, 8, 4)
     assert (o.fast_render, o.linear_t, o.keep_maps, o.protection_mask) == (0, 0, 0, 0)
+    g = fh.lib().fh_options_default(1920, 1080)  # capi/src/lib.rs:100-120 over Options::new (api.rs:113-148)
+    assert (g.width, g.height, g.k, g.internal_w, g.internal_h, g.mode, g.repair, g.cadence) == (1920, 1080, 1, 856, 480,
+                                                                                               0, 1, 0)
+    assert (g.render_sampling, g.keep_static, g.static_frames, g.static_tolerance, g.fast_render, g.linear_t) == \
+        (0, 1, 8, 4, 0, 0)
+    assert (fh.lib().fh_options_default(640, 360).internal_w, fh.lib().fh_options_default(640, 360).internal_h) == (0, 0)
+    p = fh.lib().fh_pacer_options_default()  # pacer/mod.rs:198-231
+    assert (p.mode, p.max_factor, p.limit_to_display, p.queue_capacity, p.penalty_max, p.motion_adaptive) == (0, 6, 1, 24,
+                                                                                                            3, 1)
+    assert (p.display_headroom, p.compute_budget, p.delay_floor_ms, p.delay_max_ms, p.settle_ms) == (0.97, 0.9, 60.0,
+                                                                                                   180.0, 1200.0)
+    assert fh.lib().fh_vk_row_pitch(1920) == 7680 and fh.lib().fh_vk_row_pitch(100) == 512
+    assert fh.lib().fh_pacer_create(None) is None and b"not part of this library" in fh.lib().fh_last_error()
     e = fh.lib().fh_engine_options_default()
     assert (e.backend, e.tensor_cores, e.autotune, e.precision, e.compact_memory) == (0, 1, 1, 0, 1)
 

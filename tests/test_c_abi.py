@@ -2,8 +2,9 @@
 
 - The reference's example host (examples/c/main.c) compiles unchanged against include/flyhigh.h and links to
   libflyhigh.so (oracle/Makefile, target _ref/c_host); without a GPU it fails cleanly through fh_last_error.
-- sizeof / offsetof of every field of FhEngineOptions, FhSessionOptions, FhStreamOptions, FhClassification and
-  FhPush (tests/c_abi/layout.c) are the same compiled against include/flyhigh.h and against the reference's
+- sizeof / offsetof of every field of every struct of the reference header (FhEngineOptions, FhSessionOptions,
+  FhStreamOptions, FhClassification, FhPush, FhOptions, FhPacerOptions, FhSourceFrame, FhRequest, FhTick, FhVkMemory;
+  tests/c_abi/layout.c) are the same compiled against include/flyhigh.h and against the reference's
   crates/flyhigh-capi/include/flyhigh.h.
 - On a GPU, the prebuilt host runs with the reference's shipped model and prints "ok": its in-between frame of an 8-px
   shift is closer to the true middle than to either source frame, with MAE < 6.
@@ -28,7 +29,7 @@ def _layout(tmp_path, include_dir, tag):
 def test_option_struct_layout_matches_reference_header(tmp_path, reference_repo):
     ours = _layout(tmp_path, os.path.join(ROOT, "include"), "ours")
     ref = _layout(tmp_path, os.path.join(reference_repo, "crates", "flyhigh-capi", "include"), "ref")
-    assert ours.count("\n") == 46
+    assert ours.count("\n") == 122
     assert ours == ref
 
 
