@@ -85,7 +85,7 @@ def test_generator_errors(synth_model_dir, cuda):
     with fh.Generator(eng, model, 256, 192) as g:
         with pytest.raises(fh.FlyHighError, match="frame size mismatch"):
             g.push(b"\0" * 100, 2)
-        assert g.push(synth_frames.sequence_c2(1, 256, 192, seed=3)[0], 2) == 1
+        assert g.push(synth_frames.sequence_c2(1, 256, 192, seed=3, hud=False)[0], 2) == 1
         import ctypes
         small = (ctypes.c_uint8 * 16)()
         assert fh.lib().fh_generator_pop(g._h, ctypes.cast(small, ctypes.c_void_p), 16, None, None) == -1
