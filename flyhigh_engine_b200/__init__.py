@@ -154,6 +154,10 @@ EXPORTS = [
     ("fh_stream_warp", c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_uint32, c_double]),
     ("fh_stream_report_json", c_int, [c_void_p, c_char_p, c_size_t]),
     ("fh_stream_camera_warp", c_void_p, [c_void_p]),
+    ("fh_session_write_rgba_async", c_int, [c_void_p, c_uint32, c_void_p, c_size_t]),
+    ("fh_session_write_wait", c_int, [c_void_p, c_uint32]),
+    ("fh_session_read_rgba_async", c_int, [c_void_p, c_uint32, c_void_p, c_size_t]),
+    ("fh_session_read_wait", c_int, [c_void_p, c_uint32]),
     ("fh_options_default", GeneratorOptions, [c_uint32, c_uint32]),
     ("fh_generator_create", c_void_p, [c_void_p, c_void_p, POINTER(GeneratorOptions)]),
     ("fh_generator_destroy", None, [c_void_p]),
@@ -273,6 +277,17 @@ def _buffer(data):
         return ctypes.cast(b, c_void_p), len(mv), b
     arr = (c_uint8 * len(mv)).from_buffer(mv)
     return ctypes.cast(arr, c_void_p), len(mv), arr
+
+
+def _async_buffer(data, n):
+    """(pointer, length) of memory an asynchronous copy may use after the call returns: a pointer (int), or a
+    C-contiguous numpy array (the caller keeps it alive); anything that would need a temporary copy is refused."""
+    if isinstance(data, int):
+        return c_void_p(data), n
+    import numpy as np
+    if isinstance(data, np.ndarray) and data.flags["C_CONTIGUOUS"]:
+        return data.ctypes.data_as(c_void_p), data.nbytes
+    raise ValueError("asynchronous copies take a pointer or a C-contiguous numpy array (pinned host memory)")
 
 
 _PRECISION = {"auto": 0, "f16": 1, "f32": 2}
@@ -454,6 +469,24 @@ class Session:
         else:
             p, n, _keep = _buffer(out)
         _check(lib().fh_session_read_rgba(self._h, slot, p, n))
+
+    def write_async(self, slot: int, rgba) -> None:
+        """fh_session_write_rgba_async: the upload is issued and the call returns; `rgba` (pinned host memory, a numpy
+        array over it or a pointer) must stay unchanged until write_wait(slot)."""
+        p, n = _async_buffer(rgba, self.width * self.height * 4)
+        _check(lib().fh_session_write_rgba_async(self._h, slot, p, n))
+
+    def write_wait(self, slot: int) -> None:
+        _check(lib().fh_session_write_wait(self._h, slot))
+
+    def read_async(self, slot: int, out) -> None:
+        """fh_session_read_rgba_async into a caller buffer (pinned host memory); its bytes are there after
+        read_wait(slot)."""
+        p, n = _async_buffer(out, self.width * self.height * 4)
+        _check(lib().fh_session_read_rgba_async(self._h, slot, p, n))
+
+    def read_wait(self, slot: int) -> None:
+        _check(lib().fh_session_read_wait(self._h, slot))
 
     def pair(self, a: int, b: int) -> None:
         _check(lib().fh_session_pair(self._h, a, b))

@@ -404,6 +404,10 @@ struct FhSession {
     std::vector<InSlot> ins;
     std::vector<uint8_t*> outs;
     std::vector<cudaEvent_t> out_ready;  // per output slot: after the last launch that writes it (read_rgba waits)
+    // per output slot: after its last asynchronous readback (fh_session_read_rgba_async), which every later write of
+    // the slot waits for while out_read_pending says one was issued
+    std::vector<cudaEvent_t> out_read;
+    std::vector<char> out_read_pending;
     // host <-> device copies on their own streams, so they overlap the compute of other intervals
     cudaStream_t h2d = nullptr, d2h = nullptr;
     // frame-stage scratch, pair and mid buffers
@@ -446,9 +450,12 @@ struct FhSession {
     // two render sets, and a batch waits for the render of the batch before the last (which used its set) before it
     // writes it. The members point into the set in use. Work on st outside a batch first waits for every batch
     // stream (join_render).
+    // the output slot of each entry of a batch, read by the batch render (written on the render stream before it)
+    uint8_t** out_tab = nullptr;
+    uint8_t* const* render_table = nullptr;  // while capturing a batch render: out_tab
     struct RenderSet {
         FrameSet arena;
-        uint8_t* out = nullptr;  // nbat rendered frames, scattered to the output slots
+        uint8_t* out = nullptr;  // nbat rendered frames (the eager profile of a batch renders here)
 #define FH_DECL(T, n) T n = nullptr;
         FH_SET_BUFFERS(FH_DECL)
 #undef FH_DECL
@@ -597,6 +604,8 @@ struct FhSession {
             if (fs->released) cudaEventDestroy(fs->released);
         }
         for (cudaEvent_t e : out_ready)
+            if (e) cudaEventDestroy(e);
+        for (cudaEvent_t e : out_read)
             if (e) cudaEventDestroy(e);
         for (int i = 0; i < 4; i++) {
             if (fork_ev[i]) cudaEventDestroy(fork_ev[i]);
@@ -1073,6 +1082,7 @@ struct FhSession {
                 ar.f8 = img(h8, w8, C8P, nf);
                 ar.f16 = img(h16, w16, C16P, nf);
                 r.out = alloc_n<uint8_t>((size_t)nb * w * h * 4);
+                if (!out_tab) out_tab = alloc_n<uint8_t*>(fhk::MAX_LIST);
                 for (cudaEvent_t* e : {&r.frame_done, &r.static_done, &r.net_done, &r.render_done})
                     CK(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
             }
@@ -1233,12 +1243,14 @@ struct FhSession {
             fhk::RenderTexArgs ra{p.a.frame, p.b.frame, p.a.frame_bs, w, h, hp, wp, up7, eup, rt, ert, qh, qw, fsx, fsy,
                                   cubic ? 1 : 0, (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, P,
                                   nearp, min_age, dsum, P, tdev, linear ? 1 : 0, out, out_bs};
+            ra.out_table = render_table;
             CK(fhk::render_tex(ra, n, st));
             mark("render_tex");
         } else {
             fhk::RenderArgs ra{p.a.half, p.b.half, p.a.half_bs, w, h, hp, wp, up7, eup, rt, ert, qh, qw, fsx, fsy,
                                cubic ? 1 : 0, (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, P, ownp,
                                nearp, P, min_age, out, out_bs};
+            ra.out_table = render_table;
             CK(fhk::render(ra, n, st));
             mark("render");
         }
@@ -1325,13 +1337,13 @@ struct FhSession {
     }
     // a host upload into the set: on the upload stream after the last compute that reads the set; returns once the
     // caller's buffer has been copied
-    void upload(FrameSet& fs, const uint8_t* rgba, size_t n) {
+    void upload(FrameSet& fs, const uint8_t* rgba, size_t n, bool wait = true) {
         fs.dev_written = false;
         if (fs.ever_read) CK(cudaStreamWaitEvent(h2d, fs.released, 0));
         CK(cudaMemcpyAsync(fs.frame, rgba, n, cudaMemcpyHostToDevice, h2d));
         CK(cudaEventRecord(fs.uploaded, h2d));
         fs.upload_pending = true;
-        CK(cudaEventSynchronize(fs.uploaded));
+        if (wait) CK(cudaEventSynchronize(fs.uploaded));
     }
 
     void ensure_features(FrameSet& fs) {
@@ -1431,6 +1443,7 @@ struct FhSession {
         use_set(pair_set);
         CK(fhk::set_scalar(tdev, t, st));
         kernels_launched++;
+        before_write(out, st);
         launch_mid(out);
         if (pair.sa) mark_read(*pair.sa, *pair.sb);
         CK(cudaEventRecord(out_ready[out], st));
@@ -1457,6 +1470,7 @@ struct FhSession {
                 if (x.mid) {
                     CK(fhk::set_scalar(tdev, x.t, st));
                     kernels_launched++;
+                    before_write(x.out, st);
                     launch_mid(x.out);
                     mark_read(*x.a, *x.b);
                     CK(cudaEventRecord(out_ready[x.out], st));
@@ -1519,10 +1533,17 @@ struct FhSession {
         }
         R.render_pending = false;
         use_set(p);
-        for (int j = 0; j <= m; j++) {
-            FrameSet* f = j == 0 ? q[m - 1].b : q[m - j].a;
-            wait_upload(*f, f_s);
-            CK(cudaMemcpyAsync(arena().frame + j * fb, f->frame, fb, cudaMemcpyDeviceToDevice, f_s));
+        {
+            const uint8_t* src[fhk::MAX_LIST];
+            uint8_t* dst[fhk::MAX_LIST];
+            for (int j = 0; j <= m; j++) {
+                FrameSet* f = j == 0 ? q[m - 1].b : q[m - j].a;
+                wait_upload(*f, f_s);
+                src[j] = f->frame;
+                dst[j] = arena().frame + j * fb;
+            }
+            CK(fhk::copy_frames(src, dst, m + 1, fb, f_s));
+            kernels_launched++;
         }
         for (int j = 0; j <= m; j++) {
             FrameSet* f = j == 0 ? q[m - 1].b : q[m - j].a;
@@ -1531,7 +1552,8 @@ struct FhSession {
         }
         std::vector<float> tv(m);
         for (int e = 0; e < m; e++) tv[e] = q[m - 1 - e].t;
-        CK(cudaMemcpyAsync(tdev, tv.data(), m * sizeof(float), cudaMemcpyHostToDevice, f_s));
+        CK(fhk::set_floats(tdev, tv.data(), m, f_s));
+        kernels_launched++;
         const bool carry = m == nbat && carried == q[0].a && q[0].a->gen == carried_gen && batches_run > 0;
         const FView fa = arena_view(1), fbv = arena_view(0);
         // graphs captured on first use (a key per set, size and carry)
@@ -1576,10 +1598,18 @@ struct FhSession {
             throw;
         }
         static_apart = false;
-        cudaGraphExec_t rg = graph(R.render_g, [&] {
-            fhk::PrioScope low(prio_on, prio_lo);
-            run_mid(PairSrc{fa, fbv}, arena_out(), (long long)fb, m, 2);
-        });
+        render_table = out_tab;
+        cudaGraphExec_t rg = nullptr;
+        try {
+            rg = graph(R.render_g, [&] {
+                fhk::PrioScope low(prio_on, prio_lo);
+                run_mid(PairSrc{fa, fbv}, arena_out(), (long long)fb, m, 2);
+            });
+        } catch (...) {
+            render_table = nullptr;
+            throw;
+        }
+        render_table = nullptr;
         launch_graph(fg, f_s);
         CK(cudaEventRecord(R.frame_done, f_s));
         if (sg) {
@@ -1592,14 +1622,25 @@ struct FhSession {
         CK(cudaEventRecord(R.net_done, n_s));
         CK(cudaStreamWaitEvent(r_s, R.net_done, 0));
         if (sg) CK(cudaStreamWaitEvent(r_s, R.static_done, 0));
+        {
+            // the render writes each entry straight into its output slot (entry e is interval m - 1 - e), after any
+            // readback of what the slot held
+            // (an interval whose slot a later interval of the batch also writes renders into the arena instead: the
+            // slot ends with the later frame, as consecutive mids into one slot leave it)
+            uint8_t* tab[fhk::MAX_LIST];
+            for (int i = 0; i < m; i++) {
+                bool later = false;
+                for (int j = i + 1; j < m; j++) later = later || q[j].out == q[i].out;
+                before_write(q[i].out, r_s);
+                tab[m - 1 - i] = later ? arena_out() + (size_t)(m - 1 - i) * fb : outs[q[i].out];
+            }
+            CK(fhk::set_pointers(out_tab, tab, m, r_s));
+            kernels_launched++;
+        }
         launch_graph(rg, r_s);
         carried = q[m - 1].b;
         carried_gen = q[m - 1].b->gen;
-        for (int i = 0; i < m; i++) {
-            const int e = m - 1 - i;
-            CK(cudaMemcpyAsync(outs[q[i].out], arena_out() + e * fb, fb, cudaMemcpyDeviceToDevice, r_s));
-            CK(cudaEventRecord(out_ready[q[i].out], r_s));
-        }
+        for (int i = 0; i < m; i++) CK(cudaEventRecord(out_ready[q[i].out], r_s));
         CK(cudaEventRecord(R.render_done, r_s));
         R.render_pending = overlap_on;
         last_batch = p;
@@ -1695,6 +1736,7 @@ struct FhSession {
             kernels_launched++;
         kernels_launched++;
             mark("set_t");
+            before_write(out, st);
             run_mid(PairSrc{view_of(A), view_of(B), &A, &B}, outs[out], 0, 1);
         } catch (...) {
             prof = nullptr;
@@ -1778,7 +1820,15 @@ struct FhSession {
         CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         CK(cudaEventRecord(e, st));  // the zeroed buffer
         out_ready.push_back(e);
+        cudaEvent_t r = nullptr;
+        CK(cudaEventCreateWithFlags(&r, cudaEventDisableTiming));
+        out_read.push_back(r);
+        out_read_pending.push_back(0);
         return (int)outs.size() - 1;
+    }
+    // the work issued on `on` next writes output slot `out`: after the slot's asynchronous readback, if one was issued
+    void before_write(uint32_t out, cudaStream_t on) {
+        if (out_read_pending[out]) CK(cudaStreamWaitEvent(on, out_read[out], 0));
     }
 };
 
@@ -1968,6 +2018,7 @@ cudaStream_t compute_stream(FhSession* s) {
 
 uint8_t* output_frame(FhSession* s, uint32_t out) {
     s->check_out(out);
+    s->before_write(out, s->st);
     return s->outs[out];
 }
 
@@ -2210,6 +2261,28 @@ int fh_session_write_rgba(const FhSession* cs, uint32_t slot, const uint8_t* rgb
     });
 }
 
+int fh_session_write_rgba_async(const FhSession* cs, uint32_t slot, const uint8_t* rgba, size_t len) {
+    return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
+        if (!s || !rgba) fail("null argument");
+        s->check_in(slot);
+        const size_t n = (size_t)s->w * s->h * 4;
+        if (len != n) fail("frame is %zu bytes, %dx%dx4 = %zu expected", len, s->w, s->h, n);
+        s->upload(s->write_target(slot), rgba, n, false);
+        return 0;
+    });
+}
+
+int fh_session_write_wait(const FhSession* cs, uint32_t slot) {
+    return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
+        if (!s) fail("null argument");
+        s->check_in(slot);
+        for (auto& fs : s->ins[slot].sets) CK(cudaEventSynchronize(fs->uploaded));
+        return 0;
+    });
+}
+
 int fh_session_write_mask(const FhSession* cs, const uint8_t* mask, size_t len) {
     return guard(-1, [&] {
         FhSession* s = const_cast<FhSession*>(cs);
@@ -2241,6 +2314,32 @@ int fh_session_read_rgba(const FhSession* cs, uint32_t slot, uint8_t* buf, size_
         CK(cudaMemcpyAsync(buf, s->outs[slot], n, cudaMemcpyDeviceToHost, s->d2h));
         CK(cudaStreamSynchronize(s->d2h));
         return (int)n;
+    });
+}
+
+int fh_session_read_rgba_async(const FhSession* cs, uint32_t slot, uint8_t* buf, size_t cap) {
+    return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
+        if (!s || !buf) fail("null argument");
+        s->check_out(slot);
+        if (s->out_pending(slot)) s->flush();
+        const size_t n = (size_t)s->w * s->h * 4;
+        if (n > cap) fail("output buffer too small (%zu needed)", n);
+        CK(cudaStreamWaitEvent(s->d2h, s->out_ready[slot], 0));
+        CK(cudaMemcpyAsync(buf, s->outs[slot], n, cudaMemcpyDeviceToHost, s->d2h));
+        CK(cudaEventRecord(s->out_read[slot], s->d2h));
+        s->out_read_pending[slot] = 1;
+        return (int)n;
+    });
+}
+
+int fh_session_read_wait(const FhSession* cs, uint32_t slot) {
+    return guard(-1, [&] {
+        FhSession* s = const_cast<FhSession*>(cs);
+        if (!s) fail("null argument");
+        s->check_out(slot);
+        if (s->out_read_pending[slot]) CK(cudaEventSynchronize(s->out_read[slot]));
+        return 0;
     });
 }
 

@@ -1545,7 +1545,8 @@ __global__ void __launch_bounds__(256, 5) k_render(RenderArgs r) {
         q[2] = (uint32_t)(clamp01(hv) * 255.0f + 0.5f);
     }
     // q[0] = B, q[1] = G, q[2] = R
-    reinterpret_cast<uint32_t*>(r.out + (long long)n * r.out_bs)[here] = q[2] | (q[1] << 8) | (q[0] << 16) | 0xff000000u;
+    uint8_t* const dst = r.out_table ? r.out_table[n] : r.out + (long long)n * r.out_bs;
+    reinterpret_cast<uint32_t*>(dst)[here] = q[2] | (q[1] << 8) | (q[0] << 16) | 0xff000000u;
 }
 
 // ---------------------------------------------------------------------------------------------- fast render ----
@@ -1776,10 +1777,51 @@ __global__ void __launch_bounds__(256) k_render_tex(RenderTexArgs r) {
         }
         q[k] = (uint32_t)(fminf(fmaxf(c[k], 0.0f), 1.0f) * 255.0f + 0.5f);
     }
-    reinterpret_cast<uint32_t*>(r.out + (long long)n * r.out_bs)[y * w + x] = q[0] | (q[1] << 8) | (q[2] << 16) | 0xff000000u;
+    uint8_t* const dst = r.out_table ? r.out_table[n] : r.out + (long long)n * r.out_bs;
+    reinterpret_cast<uint32_t*>(dst)[y * w + x] = q[0] | (q[1] << 8) | (q[2] << 16) | 0xff000000u;
 }
 
 __global__ void k_set_scalar(float* d, float v) { *d = v; }
+
+struct FloatList {
+    float v[MAX_LIST];
+};
+struct PtrList {
+    uint8_t* v[MAX_LIST];
+};
+struct CopyList {
+    const uint8_t* src[MAX_LIST];
+    uint8_t* dst[MAX_LIST];
+};
+
+__global__ void k_set_floats(float* d, FloatList l, int n) {
+    pdl_wait();
+    pdl_trigger();
+    if ((int)threadIdx.x < n) d[threadIdx.x] = l.v[threadIdx.x];
+}
+
+__global__ void k_set_pointers(uint8_t** d, PtrList l, int n) {
+    pdl_wait();
+    pdl_trigger();
+    if ((int)threadIdx.x < n) d[threadIdx.x] = l.v[threadIdx.x];
+}
+
+// blockIdx.y: the frame; 16-byte words when every address and the size allow it, else bytes
+__global__ void __launch_bounds__(256) k_copy_frames(CopyList l, size_t bytes, int words) {
+    pdl_wait();
+    pdl_trigger();
+    const uint8_t* src = l.src[blockIdx.y];
+    uint8_t* dst = l.dst[blockIdx.y];
+    const size_t step = (size_t)gridDim.x * blockDim.x;
+    if (words) {
+        const uint4* s4 = reinterpret_cast<const uint4*>(src);
+        uint4* d4 = reinterpret_cast<uint4*>(dst);
+        const size_t n4 = bytes / 16;
+        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += step) d4[i] = s4[i];
+    } else {
+        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < bytes; i += step) dst[i] = src[i];
+    }
+}
 
 // a bounded busy wait: returns after `cycles` clock cycles of its own SM
 __global__ void k_delay(long long cycles) {
@@ -2042,6 +2084,37 @@ cudaError_t delay(cudaStream_t st, long long cycles) {
 
 cudaError_t set_scalar(float* dst, float v, cudaStream_t st) {
     { const cudaError_t e_ = launch(k_set_scalar, 1, 1, 0, st, dst, v); if (e_ != cudaSuccess) return e_; }
+    return cudaGetLastError();
+}
+
+cudaError_t set_floats(float* dst, const float* v, int n, cudaStream_t st) {
+    if (n < 1 || n > MAX_LIST) return cudaErrorInvalidValue;
+    FloatList l{};
+    for (int i = 0; i < n; i++) l.v[i] = v[i];
+    { const cudaError_t e_ = launch(k_set_floats, 1, 32, 0, st, dst, l, n); if (e_ != cudaSuccess) return e_; }
+    return cudaGetLastError();
+}
+
+cudaError_t set_pointers(uint8_t** dst, uint8_t* const* v, int n, cudaStream_t st) {
+    if (n < 1 || n > MAX_LIST) return cudaErrorInvalidValue;
+    PtrList l{};
+    for (int i = 0; i < n; i++) l.v[i] = v[i];
+    { const cudaError_t e_ = launch(k_set_pointers, 1, 32, 0, st, dst, l, n); if (e_ != cudaSuccess) return e_; }
+    return cudaGetLastError();
+}
+
+cudaError_t copy_frames(const uint8_t* const* src, uint8_t* const* dst, int n, size_t bytes, cudaStream_t st) {
+    if (n < 1 || n > MAX_LIST) return cudaErrorInvalidValue;
+    CopyList l{};
+    bool words = bytes % 16 == 0;
+    for (int i = 0; i < n; i++) {
+        l.src[i] = src[i];
+        l.dst[i] = dst[i];
+        words = words && (uintptr_t)src[i] % 16 == 0 && (uintptr_t)dst[i] % 16 == 0;
+    }
+    // about two waves of 256-thread blocks over the frames
+    const unsigned bx = (unsigned)std::max(1, std::min(296 * 8 / n, (int)((bytes / (words ? 16 : 1) + 255) / 256)));
+    { const cudaError_t e_ = launch(k_copy_frames, dim3(bx, (unsigned)n), 256, 0, st, l, bytes, words ? 1 : 0); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 

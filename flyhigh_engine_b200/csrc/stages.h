@@ -169,6 +169,7 @@ struct RenderArgs {
     float min_age;
     uint8_t* out;            // w x h x 4
     long long out_bs;
+    uint8_t* const* out_table;  // when set, entry n is written to out_table[n] (device array) instead of out + n out_bs
     float qsy, qsx;          // hq / hp and wq / wp (set by render())
 };
 cudaError_t render(const RenderArgs& r, int n, cudaStream_t st);
@@ -196,6 +197,7 @@ struct RenderTexArgs {
     int linear;
     uint8_t* out;            // w x h x 4
     long long out_bs;
+    uint8_t* const* out_table;  // as RenderArgs::out_table
 };
 cudaError_t render_tex(const RenderTexArgs& r, int n, cudaStream_t st);
 
@@ -208,6 +210,16 @@ cudaError_t delay(cudaStream_t st, long long cycles);
 
 // a device scalar (the phase t of the mid stage) written on the stream
 cudaError_t set_scalar(float* dst, float v, cudaStream_t st);
+
+// up to MAX_LIST device words written on the stream by a kernel (a batch's phases, its output table): no copy engine,
+// no pageable host staging
+constexpr int MAX_LIST = 17;
+cudaError_t set_floats(float* dst, const float* v, int n, cudaStream_t st);
+cudaError_t set_pointers(uint8_t** dst, uint8_t* const* v, int n, cudaStream_t st);
+
+// whole frames copied between device buffers by the SMs: src[j] -> dst[j], `bytes` each, j < n <= MAX_LIST. The copy
+// engines stay free for the host's uploads and readbacks, which would otherwise queue these copies behind them.
+cudaError_t copy_frames(const uint8_t* const* src, uint8_t* const* dst, int n, size_t bytes, cudaStream_t st);
 
 // tex_in.wgsl: rgba8 -> padded f16 planes are never materialised; this reads one for tests: [3][hp][wp] f32 BGR
 cudaError_t frame_planes(const uint8_t* f, int w, int h, int hp, int wp, float* out, cudaStream_t st);

@@ -44,6 +44,22 @@ int fh_session_slot_device_ptr(const FhSession* session, uint32_t slot, int outp
 /* A frame already in device memory into an input slot (a device-to-device copy on the session's stream). */
 int fh_session_write_rgba_device(const FhSession* session, uint32_t slot, const void* device_rgba, size_t len);
 
+/* fh_session_write_rgba without its wait: the upload is issued on the session's upload stream and the call returns at
+ * once, so uploads, readbacks and compute run together. `rgba` should be page-locked host memory (from pageable memory
+ * the copy is synchronous) and must stay unchanged until fh_session_write_wait(slot) returns (or the session is
+ * synchronised). The pairs that read the slot wait for the upload on the device. */
+int fh_session_write_rgba_async(const FhSession* session, uint32_t slot, const uint8_t* rgba, size_t len);
+/* Returns once every upload issued into the slot has landed. */
+int fh_session_write_wait(const FhSession* session, uint32_t slot);
+
+/* fh_session_read_rgba without its wait: the readback of output slot `slot` is issued on the session's readback stream,
+ * after the last launch that writes the slot, and the call returns at once. The bytes are in `buf` (page-locked host
+ * memory, for the copy to be asynchronous) once fh_session_read_wait(slot) returns. Work that later writes the slot
+ * waits for the readback on the device. Returns width * height * 4, or -1. */
+int fh_session_read_rgba_async(const FhSession* session, uint32_t slot, uint8_t* buf, size_t cap);
+/* Returns once the slot's last asynchronous readback has landed. */
+int fh_session_read_wait(const FhSession* session, uint32_t slot);
+
 /* A named tensor of the last pair / mid, read back as f32 [c][h][w] (the reference's planar order, view applied).
  * Names follow the graph (models/graph.json): A, B, aq, bq, i8a, i8b, i16a, i16b, f8a, f8b, f16a, f16b, cv, ch1, ch2,
  * ch3r, hc, o, flow, vis, wa, wb, ia, ib, fcv, fr1, fr2, fr3, hm, fh1, fh2, dfilm, ft_vt, up7, rx, rq1, rq2, rq3, R_t,
