@@ -20,7 +20,7 @@ sharded by stream), `e2e.copy_ceiling` (the e2e loop's bytes with no compute, se
 overlapped; e2e as a fraction of the overlapped ceiling, the blocking calls' of the serial one), `roofline` (k_render against HBM: algorithmic bytes, design
 bytes, DRAM traffic from its ncu summary), `roofline_conv` (every conv of a batch against the tensor peak),
 `conv_sweep` (config 1: each isolated conv shape on both conv kernels), `config3_4k` (3840 x 2160 latency of a pair
-and three phases), `fast_render_linear_t`, `conv_kernels` (the autotuned kernel of each layer), `kernel_ms`.
+and three phases), `camera_warp` (the camera warp's measurement latency and render time at 1080p and 4K), `fast_render_linear_t`, `conv_kernels` (the autotuned kernel of each layer), `kernel_ms`.
 
 Multi-GPU (torchrun, one process per GPU): every rank runs its own seeded sequence (weak scaling, no collective on
 the data path); the step time is the max over ranks. --impl reference times the reference algorithm's CPU
@@ -485,7 +485,7 @@ def main():
             if pg is not None:
                 raise
     # config 3's latency and config 1's per-conv sweep (rank 0 of a 1-GPU run; the scaling runs skip them)
-    c3 = sweep = None
+    c3 = sweep = cwarp = None
     if rank == 0 and ws == 1 and not args.no_e2e:
         peaks = {}
         try:
@@ -501,6 +501,10 @@ def main():
             sweep = conv_sweep(f"cuda:{local}", peaks.get("bf16_tflops"))
         except Exception as e:
             sweep = {"error": str(e)}
+        try:
+            cwarp = camera_warp_timing(engine, peaks.get("hbm_gbs"))
+        except Exception as e:
+            cwarp = {"error": str(e)}
     cpu = None
     if rank == 0 and ws == 1:
         fps_cpu, dt = cpu_baseline(model_dir, frames, args.cpu_sample)
@@ -520,7 +524,7 @@ def main():
                 "gpu_launches": launches * ws,
                 "clocks": clk.summary(), "roofline": roof, "roofline_conv": roof_conv, "cpu_baseline": cpu,
                 "e2e": e2e, "strong": strong, "config4_streams": c4, "fast_render_linear_t": fast, "config3_4k": c3,
-                "conv_sweep": sweep,
+                "camera_warp": cwarp, "conv_sweep": sweep,
                 "conv_kernels": {k: v["kernel"] for k, v in s.report()["convs"].items()},
                 "kernel_ms": {k: round(v, 5) for k, v in sorted(prof.items(), key=lambda x: -x[1])[:12]}}
         print(json.dumps(line), flush=True)
@@ -599,6 +603,48 @@ def config3_latency(engine, model):
     del s
     return {"workload": "3840x2160, pair + mid(0.25 / 0.5 / 0.75), one interval per launch, fence pan frames",
             "pair_ms": pair_ms, "mid_ms": mids, "ms_per_generated_frame": (pair_ms + sum(mids)) / 3.0}
+
+
+def camera_warp_timing(engine, hbm_gbs):
+    """The camera warp (fh_warp_*) at 1080p (config-2 frames) and 4K (config 3's fence pan): the latency of one frame's
+    measurement (frame() to its shift in the host's hands: a cells launch, three search launches, lock, dilate, the
+    16-byte readback; host clock, median of 8) and the device time of one render (k_warp_render, CUDA events on the
+    warp's stream, mean of 20) with its bytes: the source frame read once and the turned frame written."""
+    import torch
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200 import synth_frames
+    res = {}
+    for w, h, frames in ((1920, 1080, synth_frames.sequence_c2(9, 1920, 1080, seed=5)),
+                         (3840, 2160, synth_frames.sequence_c3(9, 3840, 2160, seed=5))):
+        dev = torch.from_numpy(np.stack(frames)).cuda()
+        dst = torch.empty_like(dev[0])
+        torch.cuda.synchronize()
+        with fh.Warp(engine, w, h) as wp:
+            wp.frame(dev[0].data_ptr(), 0.0)
+            wp.collect(True)
+            lat = []
+            for i in range(1, 9):
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                wp.frame(dev[i].data_ptr(), 16.7 * i)
+                wp.collect(True)
+                lat.append((time.perf_counter() - t0) * 1000.0)
+            st = torch.cuda.ExternalStream(wp.cuda_stream())
+            for _ in range(3):
+                wp.render_into(dev[8].data_ptr(), dst.data_ptr(), 30.0, -5.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(20):
+                wp.render_into(dev[8].data_ptr(), dst.data_ptr(), 30.0, -5.0)
+            e1.record(st)
+            e1.synchronize()
+            rms = e0.elapsed_time(e1) / 20
+            gbs = 2 * w * h * 4 / (rms / 1000.0) / 1e9
+            res[f"{w}x{h}"] = {"measure_ms": float(np.median(lat)), "render_ms": rms, "render_gb_per_s": gbs,
+                               "render_frac_of_hbm": gbs / hbm_gbs if hbm_gbs else None,
+                               "last_shift": wp.last_shift()}
+        del dev, dst
+    return res
 
 
 def c4_pool(device, scenes=5, per_scene=48, seed=400):

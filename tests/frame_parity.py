@@ -5,9 +5,12 @@ The GPU's network outputs differ from the oracle's by the f32 summation order of
 few pixels, in four ways, each a threshold or a steep slope of the render in the oracle's own run:
 
   gmhs   the repair stage's select (gm_select.wgsl: ca + eps < cm, dv > dmin, sd > tex) decided a cell differently
-         because one of its conditions sat within GMHS_TOL of its threshold in both runs; the cell's flow differs by
-         more than dmin (several px), and so does every pixel the cell reaches through the mid network and the render
-         (within GMHS_REACH E8 cells);
+         because one of its conditions sat within GMHS_TOL of its threshold in both runs, or because the two runs'
+         pre-repair flows, within POS_ULPS f16 ulps of each other around the cell, moved a cost condition across its
+         threshold (a cost moves by the local luma gradient times the flow difference: several 1e-3 per f16 ulp at a
+         sharp edge; both decisions come from the oracle's own rule, only the flows differ); the cell's flow then
+         differs by more than dmin (several px), and so does every pixel the cell reaches through the mid network and
+         the render (within GMHS_REACH E8 cells);
   static a static rule's probe (render.wgsl's `round()` of the source position, then the 3 x 3 protected-age test)
          rounded to another pixel: the source positions of the two runs agree (to POS_ULPS f16 ulps of the flow or
          POS_ABS network px), but lie on either side of a half-pixel boundary;
@@ -91,13 +94,35 @@ def _e8_of(xs, ys, fsx, fsy, w8, h8):
     return i, j
 
 
+def _pre_flow_tol(go, gg, i, j):
+    """The largest pre-repair flow difference of the two runs over E8 cell (i, j)'s reach (GMHS_REACH cells), in units
+    of max(POS_ULPS f16 ulps of the oracle's flow, POS_ABS); None when the records carry no flows ("flow")."""
+    if "flow" not in go or "flow" not in gg:
+        return None
+    fo, fg = np.asarray(go["flow"], np.float64), np.asarray(gg["flow"], np.float64)
+    sl = (slice(None), slice(max(i - GMHS_REACH, 0), i + GMHS_REACH + 1), slice(max(j - GMHS_REACH, 0), j + GMHS_REACH + 1))
+    a, b = fo[sl], fg[sl]
+    ulp = np.spacing(np.abs(a).astype(np.float16)).astype(np.float64)
+    return float((np.abs(a - b) / np.maximum(POS_ULPS * ulp, POS_ABS)).max())
+
+
+def gmhs_records(o, gpu_pre_flow):
+    """(oracle, gpu) repair decision records on the oracle's current pair: the oracle's repair rule over its own
+    pre-repair flow and over the GPU's, each with the flow it was given ("flow")."""
+    ora = np.asarray(o.tensor("flow_pre"))
+    go, gg = o.gmhs_select(ora), o.gmhs_select(gpu_pre_flow)
+    go["flow"], gg["flow"] = ora, np.asarray(gpu_pre_flow)
+    return go, gg
+
+
 def check_frame(got, ref, fa, fb, w, h, pp, gpu_maps, ora_maps, age, gmhs=None, max_over=None):
     """Frame parity of one generated frame. got / ref: the GPU's and the oracle's rgba8 frames; fa, fb: the interval's
     source frames; pp: the session's plan parameters (Model.plan_params); gpu_maps / ora_maps: (up7, R_t) of each run;
     age: the (common, exactly checked) age plane or None; gmhs: None, or (ora, gpu), the OracleSession.gmhs_select
-    records of both runs' pre-repair flows. Returns a report dict; report["ok"] says whether the frame passes: PSNR
-    (over the pixels that no threshold-adjacent repair flip reaches), the render gap, no repair cell flipped away from a
-    threshold, and no unexplained pixel."""
+    records of both runs' pre-repair flows (gmhs_records: with the flows, so that a flip away from a threshold is
+    accepted where the two pre-repair flows agree within POS_ULPS f16 ulps around the cell). Returns a report dict;
+    report["ok"] says whether the frame passes: PSNR (over the pixels that no accepted repair flip reaches), the render
+    gap, no repair cell flipped unexplained, and no unexplained pixel."""
     H, W = h, w
     g = np.asarray(got, np.int32).reshape(H, W, 4)[..., :3]
     r = np.asarray(ref, np.int32).reshape(H, W, 4)[..., :3]
@@ -126,10 +151,16 @@ def check_frame(got, ref, fa, fb, w, h, pp, gpu_maps, ora_maps, age, gmhs=None, 
             flips = {k: max(abs(float(go[k][i, j])), abs(float(gg[k][i, j]))) for k in GMHS_TOL
                      if (float(go[k][i, j]) > 0) != (float(gg[k][i, j]) > 0)}
             near = {k: m for k, m in flips.items() if m <= GMHS_TOL[k]}
+            ft = _pre_flow_tol(go, gg, i, j)
             if near:
                 margins.append(near)
+            elif ft is not None and ft <= 1.0:
+                # both records come from the oracle's own repair rule, so the flip is the pre-repair flows' doing;
+                # those agree within POS_ULPS f16 ulps (or POS_ABS) over the cell's reach: rounding amplified by a
+                # cost that moves by the luma gradient times the flow (a few 1e-3 per f16 ulp at a sharp edge)
+                margins.append({"pre_flow_tol": ft})
             else:
-                gm_bad.append((int(i), int(j), flips))
+                gm_bad.append((int(i), int(j), dict(flips, pre_flow_tol=ft)))
         rep_out["gmhs_flipped"] = int(len(fl))
         rep_out["gmhs_margins"] = margins
         rep_out["gmhs_not_adjacent"] = gm_bad

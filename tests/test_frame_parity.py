@@ -21,7 +21,7 @@ def oracle_pair(synth_model_dir):
     pp = fh.Model(synth_model_dir).plan_params(W, H)
     gm = o.gmhs_select(o.tensor("flow_pre"))
     return dict(W=W, H=H, fa=fr[1], fb=fr[2], ref=ref, pp=pp, up7=o.tensor("up7", 1), rt=o.tensor("R_t", 1),
-                age=o.tensor("age"), gm=(gm, gm))
+                age=o.tensor("age"), gm=(gm, gm), flow_pre=o.tensor("flow_pre"))
 
 
 def _render(d, up7):
@@ -78,3 +78,32 @@ def test_planted_flow_error_is_rejected(oracle_pair):
     assert not rep["ok"]
     assert rep["cats"]["unexplained"] > 0
     assert all(u["dtol"] > 1.0 for u in rep["unexplained"])
+
+
+def _flipped_records(d, flow_shift):
+    """The oracle's repair record twice: the second with one cell's decision flipped by a cost margin of 3e-3 (beyond
+    GMHS_TOL) and its pre-repair flow moved by flow_shift px around that cell."""
+    go = {k: np.array(v, copy=True) for k, v in d["gm"][0].items()}
+    gg = {k: np.array(v, copy=True) for k, v in d["gm"][0].items()}
+    i, j = 10, 20
+    go["m_cost"][i, j], gg["m_cost"][i, j] = 0.003, -0.003
+    gg["sel"][i, j] = 1.0 - go["sel"][i, j]
+    go["flow"] = np.asarray(d["flow_pre"], np.float32)
+    gg["flow"] = go["flow"].copy()
+    gg["flow"][:, i - 2:i + 3, j - 2:j + 3] += flow_shift
+    return go, gg
+
+
+def test_repair_flip_within_flow_rounding_is_explained(oracle_pair):
+    """A repair decision flipped away from its threshold is accepted when the two pre-repair flows agree within
+    POS_ULPS f16 ulps around the cell (here 0.01 px), and rejected when they do not (0.3 px)."""
+    d = oracle_pair
+    frame = _render(d, d["up7"])
+    up7 = d["up7"]
+    ok = check_frame(frame, d["ref"], d["fa"], d["fb"], d["W"], d["H"], d["pp"], (up7, d["rt"]), (up7, d["rt"]),
+                     d["age"], _flipped_records(d, 0.01))
+    assert ok["ok"] and ok["gmhs_flipped"] == 1 and not ok["gmhs_not_adjacent"], ok
+    assert ok["gmhs_margins"][0]["pre_flow_tol"] <= 1.0
+    bad = check_frame(frame, d["ref"], d["fa"], d["fb"], d["W"], d["H"], d["pp"], (up7, d["rt"]), (up7, d["rt"]),
+                      d["age"], _flipped_records(d, 0.3))
+    assert not bad["ok"] and len(bad["gmhs_not_adjacent"]) == 1, bad

@@ -24,7 +24,7 @@ import os
 import numpy as np
 import pytest
 
-from tests.frame_parity import check_frame, flipped_cells, layer_rel_l2
+from tests.frame_parity import check_frame, flipped_cells, gmhs_records, layer_rel_l2
 from tests.parity import LAYER_REL_L2
 
 pytestmark = pytest.mark.gpu
@@ -56,8 +56,8 @@ def _report(name, rows):
 
 def _gmhs_records(o, gpu_pre_flow):
     """The repair stage's decision records of the oracle's own pre-repair flow and of the GPU's, on the oracle's
-    current pair."""
-    return o.gmhs_select(o.tensor("flow_pre")), o.gmhs_select(gpu_pre_flow)
+    current pair, with the flows."""
+    return gmhs_records(o, gpu_pre_flow)
 
 
 def _check_pre_flow(flow_rep, flow_pre, sel):

@@ -23,7 +23,7 @@ from ctypes import POINTER, Structure, c_float, c_int, c_longlong, c_void_p
 import numpy as np
 import pytest
 
-from tests.frame_parity import check_frame, flipped_cells, layer_rel_l2
+from tests.frame_parity import check_frame, flipped_cells, gmhs_records, layer_rel_l2
 from tests.parity import FRAME_MAX_ABS, FRAME_PSNR_DB, LAYER_REL_L2, frame_stats, rel_l2
 
 pytestmark = pytest.mark.gpu
@@ -234,7 +234,7 @@ def _session_pair(model_dir, w, h, frames, t=0.5, check_age=False, mask=None, **
             s0.write(a0, fa)
             s0.write(b0, fb)
             s0.pair(a0, b0)
-            gm = (o.gmhs_select(o.tensor("flow_pre")), o.gmhs_select(s0.tensor("flow")))
+            gm = gmhs_records(o, s0.tensor("flow"))
         age = s.tensor("age") if pp["protects"] else None
         if check_age:
             assert np.array_equal(age, o.tensor("age")), f"age differs after pair {i + 1}"
