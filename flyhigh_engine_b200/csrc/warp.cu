@@ -49,6 +49,14 @@ namespace {
 
 // -------------------------------------------------------------------------------------------------------- kernels --
 
+// byte k of a texel word as a float, exactly: the byte placed in the low mantissa bits of 2^23, minus 2^23 (an integer
+// permute and one add instead of an integer-to-float conversion, which issues at a quarter of the rate)
+__device__ __forceinline__ float byte_f(uint32_t v, uint32_t k) {
+    return __uint_as_float(__byte_perm(v, 0x4b000000u, 0x7650u | k)) - 8388608.0f;
+}
+// v in [0, 255]: the nearest integer, ties to even (as __float2uint_rn), by the same 2^23 offset
+__device__ __forceinline__ uint32_t round_byte(float v) { return __float_as_uint(v + 8388608.0f) & 0xffu; }
+
 // A frame's rgb at point (px, py) in pixels, 0..1: bilinear between the four nearest pixel centres, clamped to the edge.
 __device__ __forceinline__ float3 sample_rgb(const uint8_t* __restrict__ fr, int w, int h, float px, float py) {
     const float tx = px - 0.5f, ty = py - 0.5f;
@@ -56,16 +64,15 @@ __device__ __forceinline__ float3 sample_rgb(const uint8_t* __restrict__ fr, int
     const float ax = tx - fx0, ay = ty - fy0;
     const int x0 = (int)fmaxf(fminf(fx0, (float)(w - 1)), -1.0f), y0 = (int)fmaxf(fminf(fy0, (float)(h - 1)), -1.0f);
     const int xa = max(x0, 0), xb = min(x0 + 1, w - 1), ya = max(y0, 0), yb = min(y0 + 1, h - 1);
-    const uchar4 p00 = *reinterpret_cast<const uchar4*>(fr + ((size_t)ya * w + xa) * 4);
-    const uchar4 p01 = *reinterpret_cast<const uchar4*>(fr + ((size_t)ya * w + xb) * 4);
-    const uchar4 p10 = *reinterpret_cast<const uchar4*>(fr + ((size_t)yb * w + xa) * 4);
-    const uchar4 p11 = *reinterpret_cast<const uchar4*>(fr + ((size_t)yb * w + xb) * 4);
+    const uint32_t* t = reinterpret_cast<const uint32_t*>(fr);
+    const uint32_t p00 = __ldg(t + (size_t)ya * w + xa), p01 = __ldg(t + (size_t)ya * w + xb);
+    const uint32_t p10 = __ldg(t + (size_t)yb * w + xa), p11 = __ldg(t + (size_t)yb * w + xb);
     const float bx = 1.0f - ax, by = 1.0f - ay, k = 1.0f / 255.0f;
-    float3 c;
-    c.x = (((float)p00.x * bx + (float)p01.x * ax) * by + ((float)p10.x * bx + (float)p11.x * ax) * ay) * k;
-    c.y = (((float)p00.y * bx + (float)p01.y * ax) * by + ((float)p10.y * bx + (float)p11.y * ax) * ay) * k;
-    c.z = (((float)p00.z * bx + (float)p01.z * ax) * by + ((float)p10.z * bx + (float)p11.z * ax) * ay) * k;
-    return c;
+    float c[3];
+#pragma unroll
+    for (uint32_t ch = 0; ch < 3; ch++)
+        c[ch] = ((byte_f(p00, ch) * bx + byte_f(p01, ch) * ax) * by + (byte_f(p10, ch) * bx + byte_f(p11, ch) * ax) * ay) * k;
+    return make_float3(c[0], c[1], c[2]);
 }
 
 struct CellsArgs {
@@ -307,7 +314,7 @@ struct RenderArgs {
     uint8_t* dst;
     const float* grown;
     int w, h, gw, gh;
-    float f, cty, sty, ctp, stp;  // focal length; cos / sin of the yaw (sx / f) and the pitch (sy / f)
+    float f, inv_f, cty, sty, ctp, stp;  // focal length and 1 / f; cos / sin of the yaw (sx / f) and pitch (sy / f)
 };
 
 __device__ __forceinline__ float locked(const RenderArgs& p, int cx, int cy) {
@@ -323,15 +330,16 @@ __global__ void __launch_bounds__(256) k_warp_render(RenderArgs p) {
     if (x >= p.w || y >= p.h) return;
     const float W = (float)p.w, H = (float)p.h, cx = 0.5f * W, cy = 0.5f * H;
     const float px = (float)x + 0.5f, py = (float)y + 0.5f;
-    float dx = (px - cx) / p.f, dy = (py - cy) / p.f, dz = 1.0f;
+    // quotients as products with correctly rounded reciprocals (WGSL's f32 division is itself within 2.5 ulp)
+    float dx = (px - cx) * p.inv_f, dy = (py - cy) * p.inv_f, dz = 1.0f;
     const float rx = dx * p.cty - dz * p.sty, rz = dx * p.sty + dz * p.cty;
     dx = rx;
     dz = rz;
     const float qy = dy * p.ctp - dz * p.stp, qz = dy * p.stp + dz * p.ctp;
     dy = qy;
     dz = qz;
-    const float m = fmaxf(dz, 1e-3f);
-    const float sx = cx + p.f * dx / m, sy = cy + p.f * dy / m;
+    const float im = __frcp_rn(fmaxf(dz, 1e-3f));
+    const float sx = cx + (p.f * dx) * im, sy = cy + (p.f * dy) * im;
     float3 col;
     if (dz > 1e-3f && sx >= 0.0f && sy >= 0.0f && sx <= W && sy <= H) {
         col = sample_rgb(p.src, p.w, p.h, sx, sy);
@@ -358,17 +366,14 @@ __global__ void __launch_bounds__(256) k_warp_render(RenderArgs p) {
     const float top = locked(p, ix, iy) * (1.0f - frx) + locked(p, ix + 1, iy) * frx;
     const float bot = locked(p, ix, iy + 1) * (1.0f - frx) + locked(p, ix + 1, iy + 1) * frx;
     const float mk = top * (1.0f - fry) + bot * fry;
-    const uchar4 own = *reinterpret_cast<const uchar4*>(p.src + ((size_t)y * p.w + x) * 4);
+    const uint32_t own = __ldg(reinterpret_cast<const uint32_t*>(p.src) + (size_t)y * p.w + x);
     const float k = 1.0f / 255.0f;
-    const float r = col.x * (1.0f - mk) + (float)own.x * k * mk;
-    const float g = col.y * (1.0f - mk) + (float)own.y * k * mk;
-    const float b = col.z * (1.0f - mk) + (float)own.z * k * mk;
-    uchar4 o;
-    o.x = (unsigned char)__float2uint_rn(__saturatef(r) * 255.0f);
-    o.y = (unsigned char)__float2uint_rn(__saturatef(g) * 255.0f);
-    o.z = (unsigned char)__float2uint_rn(__saturatef(b) * 255.0f);
-    o.w = 255;
-    *reinterpret_cast<uchar4*>(p.dst + ((size_t)y * p.w + x) * 4) = o;
+    const float r = col.x * (1.0f - mk) + byte_f(own, 0) * k * mk;
+    const float g = col.y * (1.0f - mk) + byte_f(own, 1) * k * mk;
+    const float b = col.z * (1.0f - mk) + byte_f(own, 2) * k * mk;
+    reinterpret_cast<uint32_t*>(p.dst)[(size_t)y * p.w + x] = round_byte(__saturatef(r) * 255.0f) |
+                                                             (round_byte(__saturatef(g) * 255.0f) << 8) |
+                                                             (round_byte(__saturatef(b) * 255.0f) << 16) | 0xff000000u;
 }
 
 int div_up(int a, int b) { return (a + b - 1) / b; }
@@ -595,6 +600,7 @@ void FhWarp::draw(const uint8_t* src, uint8_t* dst, double sx, double sy) {
     r.gw = mgw_;
     r.gh = mgh_;
     r.f = f_;
+    r.inv_f = 1.0f / f_;
     // the calibrated gain is pixels at the centre per count over small steps, so the angle grows linearly with the
     // counts (warp_render.wgsl): a turn of s px is s / f radians
     const float ty = (float)sx / f_, tp = (float)sy / f_;

@@ -2443,7 +2443,7 @@ int or_warp_render(const uint8_t* src, int w, int h, double hfov, const float* g
     float f, ha, he;
     camwarp::geometry(w, h, hfov, &f, &ha, &he);
     const int gw = (w + 7) / 8, gh = (h + 7) / 8;
-    const float ty = sx / f, tp = sy / f;
+    const float ty = sx / f, tp = sy / f, inv_f = 1.0f / f;
     const float cty = std::cos(ty), sty = std::sin(ty), ctp = std::cos(tp), stp = std::sin(tp);
     const float W = (float)w, H = (float)h, cx = 0.5f * W, cy = 0.5f * H;
     auto locked = [&](int x, int y) {
@@ -2453,15 +2453,16 @@ int or_warp_render(const uint8_t* src, int w, int h, double hfov, const float* g
     for (int y = 0; y < h; y++)
         for (int x = 0; x < w; x++) {
             const float px = (float)x + 0.5f, py = (float)y + 0.5f;
-            float dx = (px - cx) / f, dy = (py - cy) / f, dz = 1.0f;
+            // the quotients as the CUDA render forms them: products with correctly rounded reciprocals
+            float dx = (px - cx) * inv_f, dy = (py - cy) * inv_f, dz = 1.0f;
             const float rx = dx * cty - dz * sty, rz = dx * sty + dz * cty;
             dx = rx;
             dz = rz;
             const float qy = dy * ctp - dz * stp, qz = dy * stp + dz * ctp;
             dy = qy;
             dz = qz;
-            const float m = std::max(dz, 1e-3f);
-            const float ssx = cx + f * dx / m, ssy = cy + f * dy / m;
+            const float im = 1.0f / std::max(dz, 1e-3f);
+            const float ssx = cx + (f * dx) * im, ssy = cy + (f * dy) * im;
             float col[3];
             if (dz > 1e-3f && ssx >= 0.0f && ssy >= 0.0f && ssx <= W && ssy <= H) {
                 camwarp::sample(src, w, h, ssx, ssy, col);
