@@ -152,6 +152,21 @@ def cpu_baseline(model_dir, frames, n_intervals):
     return n_intervals / dt, dt
 
 
+def cpu_baseline_warp(w=1920, h=1080):
+    """The camera warp's CPU restatement (oracle camwarp) on the host cores at w x h: one measurement of a panned pair
+    (cells, the three levels, lock, dilate; one thread) and one render (OpenMP over the cores), ms each."""
+    from oracle import oracle
+    from flyhigh_engine_b200 import synth_frames
+    fr = synth_frames.sequence_c2(2, w, h, seed=5)
+    t0 = time.perf_counter()
+    best, _, grown, _ = oracle.warp_measure(fr[0], fr[1], w, h)
+    t1 = time.perf_counter()
+    oracle.warp_render(fr[1], w, h, grown, 30.0, -5.0)
+    t2 = time.perf_counter()
+    return {"measure_ms": (t1 - t0) * 1000.0, "render_ms": (t2 - t1) * 1000.0, "kind": "port",
+            "cores": host_threads(), "sample": f"one config-2 pair at {w}x{h}"}
+
+
 def run_reference(args):
     ws, rank, _ = dist()
     if rank != 0:
@@ -511,6 +526,11 @@ def main():
         cpu = {"value": fps_cpu, "unit": "generated frames/s", "cores": host_threads(), "kind": "port",
                "sample": f"{args.cpu_sample} consecutive intervals of the same 1080p sequence (pair + mid(0.5)), "
                          f"{dt:.1f} s on the host cores"}
+        if not args.no_e2e:
+            try:  # beside the GPU's camera_warp numbers: the same stages restated on the host cores
+                cpu["camera_warp"] = cpu_baseline_warp()
+            except Exception as e:
+                cpu["camera_warp"] = {"error": str(e)}
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "generated frames/s", "n_gpus": ws, "steps": args.steps,
                 "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
