@@ -213,6 +213,7 @@ EXPORTS = [
     ("fhk_conv_wait_timeouts", ctypes.c_longlong, [c_int]),
     ("fhk_conv3x3_umma", c_int, [c_void_p, c_void_p]),
     ("fhk_conv_umma_fits", c_int, [c_int, c_int, c_int]),
+    ("fhk_conv_umma_persistent_fits", c_int, [c_int, c_int]),
     ("fhk_conv_pack_weights_umma", c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
     ("fhk_conv_packed_elems_umma", c_size_t, [c_int, c_int]),
     ("fhk_gmhs", c_int, [c_void_p, c_void_p]),

@@ -17,6 +17,7 @@
 // - Every wait is bounded (FhConvParams::wait_cycles); a timeout is counted (fhk_conv_wait_timeouts), no further MMA
 //   is issued, and the tensor memory is freed only after a bounded pause for work still in flight.
 #include <cuda_fp16.h>
+#include <algorithm>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -437,6 +438,289 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
     }
 }
 
+
+// ---- the persistent variant: one CTA loops over tiles, the next tile's halo gathered while the current tile's MMAs
+//      run, two accumulator sets in tensor memory so that a tile's epilogue overlaps the next tile's MMAs ----
+//
+// Per iteration i (tile t_i, halo buffer b = i & 1, accumulator set a = i & 1): gather t_i into halo[b] (halo[b] was
+// last read by the MMAs of tile t_{i-2}, whose completion the epilogue of t_{i-2} waited for in iteration i-1); every
+// thread syncs; the issuing lanes issue t_i's MMAs into set a (drained by the epilogue of t_{i-2}) and commit them to
+// mbarrier a; then every thread runs the epilogue of t_{i-1} from set a ^ 1 after waiting for mbarrier a ^ 1. The
+// MMAs of a tile, their split over the issuing warps and the epilogue's summation are those of conv3x3_umma, so each
+// output is bit for bit the same.
+//
+// Shared memory: two halo buffers | weights | bias, slopes | WCHUNKS + 2 mbarriers | TMEM base, flag.
+__host__ __device__ inline int ump_halo(int cp) { return (cp / 8) * UPLANE; }
+__host__ __device__ inline int ump_wofs(int cp) { return 2 * ump_halo(cp); }
+__host__ __device__ inline int ump_bofs(int cp, int ngw) { return ump_wofs(cp) + umma_wbytes(cp, ngw); }
+__host__ __device__ inline int ump_barofs(int cp, int ngw) { return ump_bofs(cp, ngw) + ngw * 8; }
+__host__ __device__ inline int ump_smem(int cp, int ngw) { return ump_barofs(cp, ngw) + 8 * (WCHUNKS + 2) + 16; }
+
+// the halo tile of output tile (ox0, oy0) of entry n into the planes at `plane0` (generic pointer) / `s_plane0`
+// (shared-window address): conv3x3_umma's gather, LP lanes per pixel, one chunk each; every copy issued, none waited
+__device__ __forceinline__ void ump_gather(const FhConvParams& p, uint8_t* plane0, uint32_t s_plane0, int tid, int n,
+                                           int ox0, int oy0, int nchunk) {
+    int lp = 1;
+    while (lp < nchunk) lp <<= 1;
+    const int ch = tid & (lp - 1), pstep = 128 / lp;
+    if (ch >= nchunk) return;
+    const int c8 = ch * 8;
+    int si = -1, rel = 0;
+    for (int s_ = 0; s_ < p.nsrc; s_++) {
+        const int r_ = c8 - p.src[s_].slot;
+        if (r_ >= 0 && r_ < ((p.src[s_].nc + 7) & ~7)) {
+            si = s_;
+            rel = r_;
+            break;
+        }
+    }
+    constexpr int npix = UIH * UIW;
+    uint8_t* plane = plane0 + ch * UPLANE;
+    if (si < 0) {
+        for (int pix = tid / lp; pix < npix; pix += pstep) *reinterpret_cast<uint4*>(plane + pix * 16) = make_uint4(0, 0, 0, 0);
+        return;
+    }
+    const FhConvSrc& src = p.src[si];
+    const __half* base = src.p + (long long)n * src.bs + rel;
+    const int cs = src.cs;
+    const bool narrow = src.cs < rel + 8;
+    for (int pix = tid / lp; pix < npix; pix += pstep) {
+        const int hy = pix / UIW, hx = pix - hy * UIW;
+        const int iy = oy0 - 1 + hy, ix = ox0 - 1 + hx;
+        const uint32_t d = s_plane0 + (uint32_t)(ch * UPLANE + pix * 16);
+        const bool ok = iy >= 0 && iy < p.h && ix >= 0 && ix < p.w;
+        const __half* g = ok ? base + ((long long)iy * p.w + ix) * cs : base;
+        if (!narrow) {
+            cp_async16_zfill(d, g, ok ? 16u : 0u);
+        } else {
+            cp_async8_zfill(d, g, ok ? 8u : 0u);
+            cp_async8_zfill(d + 8, base, 0u);
+        }
+    }
+}
+
+// after the gather's copies landed: partial chunks (channels past the source's count) and scaled sources, fixed by
+// the threads that copied them
+__device__ __forceinline__ void ump_fix(const FhConvParams& p, uint8_t* plane0, int tid, int nchunk) {
+    int lp = 1;
+    while (lp < nchunk) lp <<= 1;
+    const int ch = tid & (lp - 1), pstep = 128 / lp;
+    if (ch >= nchunk) return;
+    const int c8 = ch * 8;
+    for (int s_ = 0; s_ < p.nsrc; s_++) {
+        const int rel = c8 - p.src[s_].slot;
+        if (rel < 0 || rel >= ((p.src[s_].nc + 7) & ~7)) continue;
+        const int valid = p.src[s_].nc - rel;
+        const float scale = p.src[s_].scale;
+        const bool narrow = p.src[s_].cs < rel + 8;
+        if (valid >= 8 && scale == 1.0f && !narrow) return;
+        uint8_t* plane = plane0 + ch * UPLANE;
+        constexpr int npix = UIH * UIW;
+        for (int pix = tid / lp; pix < npix; pix += pstep) {
+            uint4 v = *reinterpret_cast<const uint4*>(plane + pix * 16);
+            __half* hv = reinterpret_cast<__half*>(&v);
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                if (k >= valid) hv[k] = __float2half_rn(0.0f);
+                else if (scale != 1.0f) hv[k] = __float2half_rn(__half2float(hv[k]) * scale);
+            }
+            *reinterpret_cast<uint4*>(plane + pix * 16) = v;
+        }
+        return;
+    }
+}
+
+__global__ void __launch_bounds__(128, 1) conv3x3_umma_p(const FhConvParams p, int np, int ngw, int nis) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int cslices = p.cp / 16, nchunk = p.cp / 8, nsteps = 9 * cslices;
+    const int grp = blockIdx.z, cbase = grp * ngw;
+    const int tx = (p.wo + UT_W - 1) / UT_W, ty = (p.ho + UT_H - 1) / UT_H;
+    const int ntiles = tx * ty * p.n;
+    const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(sm);
+    const int halo = ump_halo(p.cp), wofs = ump_wofs(p.cp), bofs = ump_bofs(p.cp, ngw);
+    const int barofs = ump_barofs(p.cp, ngw);
+    float* sbias = reinterpret_cast<float*>(sm + bofs);
+    float* sslope = sbias + ngw;
+    const uint32_t wbar0 = s0 + barofs, mbar0 = s0 + barofs + 8 * WCHUNKS;  // mbar0 + 8 a: accumulator set a
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + barofs + 8 * (WCHUNKS + 2));
+    volatile int& failed = *reinterpret_cast<int*>(sm + barofs + 8 * (WCHUNKS + 2) + 4);
+    const long long wait_cycles = p.wait_cycles > 0 ? p.wait_cycles : 2000000000ll;
+    const int acc_cols = ngw * nis;                            // one accumulator set: nis sets of ngw columns
+    const uint32_t ncols = (uint32_t)tmem_cols(2 * acc_cols);  // two sets
+    const bool prelu = p.slope != nullptr;
+    const int kc = (nsteps + WCHUNKS - 1) / WCHUNKS;
+
+    for (int i = tid; i < ngw; i += 128) {
+        const int c = cbase + i;
+        sbias[i] = c < p.cout ? p.bias[c] : 0.0f;
+        sslope[i] = (prelu && c < p.cout) ? p.slope[c] : 1.0f;
+    }
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int q = 0; q < WCHUNKS; q++) mbar_init(wbar0 + 8 * q, 1);
+            mbar_init(mbar0, (uint32_t)nis);
+            mbar_init(mbar0 + 8, (uint32_t)nis);
+            mbar_init_fence();
+            failed = 0;
+            for (int q = 0; q < WCHUNKS; q++) {
+                const int k0 = q * kc, k1 = min(k0 + kc, nsteps);
+                if (k0 >= k1) break;
+                mbar_expect_tx(wbar0 + 8 * q, (uint32_t)((k1 - k0) * ngw * 32 + (q == 0 ? p.test_extra_tx : 0)));
+            }
+        }
+        __syncwarp();
+        const char* wsrc = reinterpret_cast<const char*>(p.wpack) + (size_t)cbase * 32;
+        if (ngw == np) {
+            if (lane < WCHUNKS) {
+                const int k0 = lane * kc, k1 = min(k0 + kc, nsteps);
+                if (k0 < k1)
+                    bulk_g2s(s0 + wofs + k0 * ngw * 32, wsrc + (size_t)k0 * np * 32, (uint32_t)((k1 - k0) * np * 32),
+                             wbar0 + 8 * lane);
+            }
+        } else {
+            for (int k = lane; k < nsteps; k += 32)
+                bulk_g2s(s0 + wofs + k * ngw * 32, wsrc + (size_t)k * np * 32, (uint32_t)(ngw * 32), wbar0 + 8 * (k / kc));
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (warp == 0) {
+        tmem_alloc((uint32_t)__cvta_generic_to_shared(tslot), ncols);
+        tmem_relinquish();
+    }
+    // the first tile's halo: its copies land while the tensor memory is allocated (waited for in the loop)
+    int t = blockIdx.x;
+    if (t < ntiles) {
+        const int n = t / (tx * ty), r = t - n * tx * ty;
+        ump_gather(p, sm, s0, tid, n, (r % tx) * UT_W, (r / tx) * UT_H, nchunk);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+    const uint32_t idesc = (1u << 4) | ((uint32_t)(ngw >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+    const bool vec_out = (p.out_cs & 7) == 0 && (p.out_bs & 7) == 0 && ((uintptr_t)p.out & 15) == 0;
+    const bool vec_res = p.res && (p.res_cs & 7) == 0 && (p.res_bs & 7) == 0 && ((uintptr_t)p.res & 15) == 0;
+    bool weights_in = false;      // the issuing lanes have waited for every weight piece
+    uint32_t parity[2] = {0, 0};  // the next completion of each accumulator set's mbarrier
+    int prev = -1, prev_b = 0;    // the tile whose epilogue is pending, and its accumulator set
+
+    // the MMAs of the tile in accumulator set `set` have completed (bounded wait; false: they did not)
+    auto wait_set = [&](int set) {
+        const bool ok = mbar_wait_bounded(mbar0 + 8 * set, parity[set], wait_cycles) && !failed;
+        parity[set] ^= 1u;
+        tc_fence_after();
+        return ok;
+    };
+    auto epilogue = [&](int tile, int set, bool done) {
+        const int n = tile / (tx * ty), r = tile - n * tx * ty;
+        const int m = warp * 32 + lane;
+        const int oy = (r / tx) * UT_H + (m >> 3), ox = (r % tx) * UT_W + (m & 7);
+        const bool inside = oy < p.ho && ox < p.wo;
+        __half* __restrict__ out = p.out + (long long)n * p.out_bs + ((long long)oy * p.wo + ox) * p.out_cs;
+        const __half* __restrict__ res =
+            p.res ? p.res + (long long)n * p.res_bs + ((long long)oy * p.wo + ox) * p.res_cs : nullptr;
+        for (int c0 = 0; c0 < ngw; c0 += 16) {
+            float v[16];
+            {
+                uint32_t ra[16], rb[16];
+                const uint32_t ta = tbase + ((uint32_t)(warp * 32) << 16) + (uint32_t)(set * acc_cols + c0);
+                tmem_ld16_async(ta, ra);
+                if (nis == 2) tmem_ld16_async(ta + (uint32_t)ngw, rb);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; j++) v[j] = __uint_as_float(ra[j]);
+                if (nis == 2) {
+#pragma unroll
+                    for (int j = 0; j < 16; j++) v[j] += __uint_as_float(rb[j]);
+                }
+            }
+            const int cg = cbase + c0;
+            if (!inside || !done) continue;
+            if (p.res) {
+                if (p.epi == 1) umma_epilogue16<true, true>(v, sbias + c0, sslope + c0, prelu, res, vec_res, cg, p.cout, out, vec_out);
+                else umma_epilogue16<true, false>(v, sbias + c0, sslope + c0, prelu, res, vec_res, cg, p.cout, out, vec_out);
+            } else {
+                if (p.epi == 1) umma_epilogue16<false, true>(v, sbias + c0, sslope + c0, prelu, res, vec_res, cg, p.cout, out, vec_out);
+                else umma_epilogue16<false, false>(v, sbias + c0, sslope + c0, prelu, res, vec_res, cg, p.cout, out, vec_out);
+            }
+        }
+        tc_fence_before();
+    };
+
+    // iteration it: tile t in halo buffer b and accumulator set b = it & 1. Its halo (gathered during the last
+    // iteration) lands and is fixed; its MMAs are issued; the last tile's MMAs are waited for, which frees halo buffer
+    // b ^ 1 for the next tile's gather (issued, not waited); then the last tile's epilogue runs from set b ^ 1 while
+    // this tile's MMAs and the next tile's copies are in flight.
+    for (int it = 0; t < ntiles; it++, t += gridDim.x) {
+        const int b = it & 1;
+        const uint32_t sb = s0 + (uint32_t)(b * halo);
+        cp_async_wait_all();
+        ump_fix(p, sm + b * halo, tid, nchunk);
+        // written through the generic proxy, read by the tensor core through the async proxy
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (lane == 0 && warp < nis && !failed) {
+            const int kb = warp * nsteps / nis, ke = (warp + 1) * nsteps / nis;
+            const int tap = kb / cslices;
+            int sl = kb - tap * cslices, kx = tap % 3;
+            const uint32_t tap_ofs = (uint32_t)((tap / 3) * UIW + kx);
+            uint64_t ad = smem_desc(sb, UPLANE, UIW * 16) + tap_ofs + (uint32_t)(sl * (2 * UPLANE / 16));
+            uint64_t bd = smem_desc(s0 + (uint32_t)wofs, 128, 256) + (uint32_t)(kb * (ngw * 2));
+            const uint32_t dt = tbase + (uint32_t)(b * acc_cols + warp * ngw);
+            int ks = kb;
+            for (int q = kb / kc; q < WCHUNKS && ks < ke; q++) {
+                const int k1 = min(min((q + 1) * kc, nsteps), ke);
+                if (!weights_in && !mbar_wait_bounded(wbar0 + 8 * q, 0, wait_cycles)) {
+                    failed = 1;
+                    break;
+                }
+                for (; ks < k1; ks++) {
+                    umma_f16(dt, ad, bd, idesc, ks > kb ? 1u : 0u);
+                    bd += (uint32_t)(ngw * 2);
+                    if (++sl == cslices) {
+                        sl = 0;
+                        const uint32_t step = ++kx == 3 ? UIW - 2 : 1;
+                        if (kx == 3) kx = 0;
+                        ad += (uint64_t)((long long)step - (long long)((cslices - 1) * (2 * UPLANE / 16)));
+                    } else {
+                        ad += (uint32_t)(2 * UPLANE / 16);
+                    }
+                }
+            }
+            weights_in = true;
+            if (!failed) umma_commit(mbar0 + 8 * b);  // arrives once this lane's MMAs above have completed
+        }
+        __syncwarp();
+        const bool pdone = prev >= 0 ? wait_set(b ^ 1) : true;
+        const int tn = t + (int)gridDim.x;
+        if (tn < ntiles) {
+            const int n = tn / (tx * ty), r = tn - n * tx * ty;
+            ump_gather(p, sm + (b ^ 1) * halo, s0 + (uint32_t)((b ^ 1) * halo), tid, n, (r % tx) * UT_W,
+                       (r / tx) * UT_H, nchunk);
+        }
+        if (prev >= 0) epilogue(prev, b ^ 1, pdone);
+        prev = t;
+        prev_b = b;
+    }
+    if (prev >= 0) {
+        const bool done = wait_set(prev_b);
+        epilogue(prev, prev_b, done);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        if (failed) {  // MMAs may still be in flight: give them the bound before the columns are released
+            const long long t0 = clock64();
+            while (clock64() - t0 < wait_cycles) {
+            }
+        }
+        tmem_dealloc(tbase, ncols);
+    }
+}
+
 }  // namespace
 
 // the timeouts of this kernel's waits (fhk_conv_wait_timeouts adds them to conv3x3_mma's)
@@ -459,6 +743,15 @@ constexpr int UMMA_SMEM_MAX = 227 * 1024;
 extern "C" int fhk_conv_umma_fits(int cp, int cout, int stride) {
     if (stride != 1 || cp <= 0 || cp % 16 || cout < 1 || npad16(cout) > 256) return 0;
     return umma_smem(cp, npad16(cout)) <= UMMA_SMEM_MAX ? 1 : 0;
+}
+
+// 1 when the persistent variant takes this layer: the tcgen05 kernel's conditions, with two halo buffers and the whole
+// weight slice in shared memory and two accumulator sets in tensor memory
+extern "C" int fhk_conv_umma_persistent_fits(int cp, int cout) {
+    if (cp <= 0 || cp % 16 || cout < 1 || npad16(cout) > 256) return 0;
+    const int np = npad16(cout), nis = np <= 128 ? 2 : 1;
+    if (2 * np * nis > 512) return 0;
+    return ump_smem(cp, np) <= UMMA_SMEM_MAX ? 1 : 0;
 }
 
 extern "C" size_t fhk_conv_packed_elems_umma(int cout, int cp) { return (size_t)9 * (cp / 16) * npad16(cout) * 16; }
@@ -503,6 +796,30 @@ extern "C" int fhk_conv3x3_umma(const FhConvParams* pin, void* stream) {
     }
     if (p.ho != p.h || p.wo != p.w) return (int)cudaErrorInvalidValue;  // stride 1
     const int np = npad16(p.cout);
+    if (p.wm == 1) {
+        // the persistent variant: every output channel in one CTA, as many CTAs as fit on the GPU at once (shared
+        // memory, and 512 tensor-memory columns an SM), none without a tile
+        if (!fhk_conv_umma_persistent_fits(p.cp, p.cout)) return (int)cudaErrorInvalidValue;
+        const int nis = np <= 128 ? 2 : 1;
+        const size_t smem = (size_t)ump_smem(p.cp, np);
+        static bool configured_p = false;
+        if (!configured_p) {
+            cudaError_t e = cudaFuncSetAttribute(conv3x3_umma_p, cudaFuncAttributeMaxDynamicSharedMemorySize, UMMA_SMEM_MAX);
+            if (e != cudaSuccess) return (int)e;
+            configured_p = true;
+        }
+        int dev = 0, sms = 148, smem_sm = 228 * 1024;
+        if (cudaGetDevice(&dev) == cudaSuccess) {
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+        }
+        // CTAs an SM holds at once: shared memory (1 KB of it reserved per CTA) and tensor-memory columns
+        int occ = std::min(smem_sm / ((int)smem + 1024), 512 / tmem_cols(2 * np * nis));
+        const long long tiles = (long long)((p.wo + UT_W - 1) / UT_W) * ((p.ho + UT_H - 1) / UT_H) * p.n;
+        const int ctas = (int)std::max(1ll, std::min(tiles, (long long)sms * std::max(occ, 1)));
+        p.wsmem = 1;
+        return (int)fhk::launch(conv3x3_umma_p, dim3(ctas, 1, 1), dim3(128), smem, (cudaStream_t)stream, p, np, np, nis);
+    }
     // output channels split over CTAs while the grid is small (each output's sum is unchanged): the widest group (a
     // multiple of 16 dividing the padded channels) that gives 148 CTAs, else the narrowest
     const long long tiles = (long long)((p.wo + UT_W - 1) / UT_W) * ((p.ho + UT_H - 1) / UT_H) * p.n;

@@ -802,6 +802,7 @@ struct FhSession {
             CK(cudaEventCreate(&e1));
             std::vector<uint8_t> cands = {fhtune::mma(1), fhtune::mma(2), fhtune::mma(4)};
             if (umma_ok) cands.push_back(fhtune::KERNEL_UMMA);
+            if (umma_ok && fhk_conv_umma_persistent_fits(L.cp, L.cout)) cands.push_back(fhtune::UMMA_PERSISTENT);
             float best_ms = 1e30f;
             for (uint8_t c : cands) {
                 const bool um = fhtune::kernel_of(c) == fhtune::KERNEL_UMMA;
@@ -826,7 +827,7 @@ struct FhSession {
                 p.out_cs = ocs;
                 p.out_bs = out_bs;
                 p.n = L.n;
-                p.wm = um ? 0 : fhtune::wm_of(c);
+                p.wm = fhtune::wm_of(c);  // tcgen05: 1 = the persistent variant
                 auto launch = [&]() { return um ? fhk_conv3x3_umma(&p, st) : fhk_conv3x3(&p, L.stride, st); };
                 if (launch() != 0) {  // this configuration does not fit the layer: not a candidate
                     cudaGetLastError();
@@ -901,13 +902,14 @@ struct FhSession {
             // a choice the layer cannot run (a byte of another kernel set, a table from other sizes or options) falls
             // back to the fixed rule
             if (!fhtune::valid(c) ||
-                (fhtune::kernel_of(c) == fhtune::KERNEL_UMMA && !(L.stride == 1 && fhk_conv_umma_fits(L.cp, L.cout, 1)))) {
+                (fhtune::kernel_of(c) == fhtune::KERNEL_UMMA && !(L.stride == 1 && fhk_conv_umma_fits(L.cp, L.cout, 1))) ||
+                (c == fhtune::UMMA_PERSISTENT && !fhk_conv_umma_persistent_fits(L.cp, L.cout))) {
                 c = fixed_choice(L);
                 L.how = "fixed";
             }
             L.cand = c;
             L.umma = fhtune::kernel_of(c) == fhtune::KERNEL_UMMA;
-            L.wm = L.umma ? 0 : fhtune::wm_of(c);
+            L.wm = fhtune::wm_of(c);
             std::vector<uint16_t> packed = packed_for(L, L.umma);
             L.wpack = alloc_n<uint16_t>(packed.size());
             CK(cudaMemcpyAsync(L.wpack, packed.data(), packed.size() * 2, cudaMemcpyHostToDevice, st));

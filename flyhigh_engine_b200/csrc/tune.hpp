@@ -28,14 +28,16 @@ using Table = std::map<Key, uint8_t>;
 enum : uint8_t { KERNEL_MMA = 1, KERNEL_UMMA = 2 };
 
 inline uint8_t mma(int wm) { return (uint8_t)((wm << 4) | KERNEL_MMA); }
+// the tcgen05 kernel's persistent variant (fhk_conv3x3_umma with wm 1)
+constexpr uint8_t UMMA_PERSISTENT = (uint8_t)((1 << 4) | KERNEL_UMMA);
 inline int kernel_of(uint8_t c) { return c & 15; }
 inline int wm_of(uint8_t c) { return c >> 4; }
 inline bool valid(uint8_t c) {
     const int k = kernel_of(c), wm = wm_of(c);
-    return (k == KERNEL_MMA && (wm == 0 || wm == 1 || wm == 2 || wm == 4)) || (k == KERNEL_UMMA && wm == 0);
+    return (k == KERNEL_MMA && (wm == 0 || wm == 1 || wm == 2 || wm == 4)) || (k == KERNEL_UMMA && (wm == 0 || wm == 1));
 }
 inline std::string name(uint8_t c) {
-    if (kernel_of(c) == KERNEL_UMMA) return "tcgen05";
+    if (kernel_of(c) == KERNEL_UMMA) return wm_of(c) ? "tcgen05/persistent" : "tcgen05";
     return wm_of(c) ? "mma.sync/wm" + std::to_string(wm_of(c)) : "mma.sync";
 }
 

@@ -33,7 +33,7 @@ class Conv3x3:
     """One 3x3 conv layer (pad 1, bias, optional PReLU slopes, optional residual) on NHWC f16 torch tensors.
 
     kernel "mma" (fhk_conv3x3: mma.sync, stride 1 or 2; wm = rows per CTA pair, 0 = by size) or "umma"
-    (fhk_conv3x3_umma: tcgen05, stride 1 where fhk_conv_umma_fits). weight: [cout][cin][3][3] (float values, rounded
+    (fhk_conv3x3_umma: tcgen05, stride 1 where fhk_conv_umma_fits; wm 1 = its persistent variant). weight: [cout][cin][3][3] (float values, rounded
     to f16); the input tensor is [n][h][w][cs] with cs = 4 for cin <= 4 else cin rounded up to 8."""
 
     def __init__(self, weight, bias, slope=None, stride: int = 1, kernel: str = "mma", wm: int = 0, device="cuda"):
@@ -47,6 +47,8 @@ class Conv3x3:
         umma = kernel == "umma"
         if umma and not (stride == 1 and L.fhk_conv_umma_fits(self.cp, self.cout, 1)):
             raise FlyHighError(f"conv {self.cin}->{self.cout} stride {stride}: the tcgen05 kernel does not take it")
+        if umma and wm == 1 and not L.fhk_conv_umma_persistent_fits(self.cp, self.cout):
+            raise FlyHighError(f"conv {self.cin}->{self.cout}: the persistent tcgen05 variant does not take it")
         cmap = np.full(self.cp, -1, np.int32)
         cmap[:self.cin] = np.arange(self.cin)
         n_pack = (L.fhk_conv_packed_elems_umma if umma else L.fhk_conv_packed_elems)(self.cout, self.cp)

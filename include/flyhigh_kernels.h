@@ -71,10 +71,15 @@ long long fhk_conv_wait_timeouts(int reset);
 /* The same convolution (stride 1) on the 5th-generation tensor cores: tcgen05.mma into a tensor-memory f32
  * accumulator, a CTA per 8 x 16 output pixels and all output channels, the halo tile gathered into shared memory and
  * the whole weight slice staged by one bulk copy. Weights in fhk_conv_pack_weights_umma order; p->ho == p->h and
- * p->wo == p->w; wm / ngroups are ignored. fhk_conv_umma_fits tells whether a layer fits (stride 1, Cout <= 256,
- * shared memory). The f32 summation order differs from fhk_conv3x3's. */
+ * p->wo == p->w; ngroups is ignored. fhk_conv_umma_fits tells whether a layer fits (stride 1, Cout <= 256, shared
+ * memory). The f32 summation order differs from fhk_conv3x3's.
+ * p->wm == 1 selects the persistent variant (where fhk_conv_umma_persistent_fits): as many CTAs as the GPU holds at
+ * once, each staging the weights once and looping over tiles, the next tile's halo gathered and the last tile's
+ * epilogue run while the current tile's MMAs execute (two halo buffers, two accumulator sets). Its outputs are bit for
+ * bit those of wm == 0. */
 int fhk_conv3x3_umma(const FhConvParams* p, void* stream);
 int fhk_conv_umma_fits(int cp, int cout, int stride);
+int fhk_conv_umma_persistent_fits(int cp, int cout);
 int fhk_conv_pack_weights_umma(const uint16_t* w, int cin, int cout, const int* map, int cp, uint16_t* out);
 size_t fhk_conv_packed_elems_umma(int cout, int cp);
 /* Replaces buildb / buildb_tap (ops/conv/kernels.rs:66-78, :194-207): torch [cout][cin][3][3] f16 bits -> the

@@ -23,10 +23,13 @@ int main() {
     check(fhtune::parse(" 48 , 48 , 60 , 108 , 1 = 33 \r\n").at(fhtune::Key{48, 48, 60, 108, 1}) == 33, "spaces");
     // this library's candidate bytes
     check(fhtune::valid(fhtune::mma(1)) && fhtune::valid(fhtune::mma(2)) && fhtune::valid(fhtune::mma(4)) &&
-              fhtune::valid(fhtune::mma(0)) && fhtune::valid(fhtune::KERNEL_UMMA),
+              fhtune::valid(fhtune::mma(0)) && fhtune::valid(fhtune::KERNEL_UMMA) &&
+              fhtune::valid(fhtune::UMMA_PERSISTENT) && fhtune::UMMA_PERSISTENT == 18,
           "candidates valid");
-    check(!fhtune::valid(18) && !fhtune::valid(0) && !fhtune::valid(0x31) && !fhtune::valid(3), "others refused");
-    check(fhtune::name(fhtune::mma(2)) == "mma.sync/wm2" && fhtune::name(fhtune::KERNEL_UMMA) == "tcgen05", "names");
+    check(!fhtune::valid(0x22) && !fhtune::valid(0) && !fhtune::valid(0x31) && !fhtune::valid(3), "others refused");
+    check(fhtune::name(fhtune::mma(2)) == "mma.sync/wm2" && fhtune::name(fhtune::KERNEL_UMMA) == "tcgen05" &&
+              fhtune::name(fhtune::UMMA_PERSISTENT) == "tcgen05/persistent",
+          "names");
     const std::string f = fhtune::file_name("/tmp/x", "NVIDIA B200", 12090);
     check(f.rfind("/tmp/x/tune-10de-", 0) == 0 && f.size() > 30 && f.substr(f.size() - 16) == "-f16-tc-b200.txt",
           "file name");

@@ -147,14 +147,17 @@ UMMA_CASES = [c for c in CONV_CASES if c[4] == 1] + [(30, 54, 96, 96, 1, True), 
 
 
 @pytest.mark.parametrize("h,w,cin,cout,stride,res", UMMA_CASES)
-def test_conv_umma_matches_oracle(torch_cuda, h, w, cin, cout, stride, res):
-    """The tcgen05 kernel on the stride-1 shapes that fit it, against the oracle (f32 accumulation in another order:
-    a few f16 ulps at most)."""
+@pytest.mark.parametrize("wm", [0, 1])
+def test_conv_umma_matches_oracle(torch_cuda, h, w, cin, cout, stride, res, wm):
+    """The tcgen05 kernel (wm 1: its persistent variant) on the stride-1 shapes that fit it, against the oracle (f32
+    accumulation in another order: a few f16 ulps at most)."""
     import flyhigh_engine_b200 as fh
     from oracle import oracle
     cp = (_up8(cin) + 15) // 16 * 16
     if not fh.lib().fhk_conv_umma_fits(cp, cout, 1):
         pytest.skip("weights and halo tile exceed shared memory: conv3x3_mma takes this layer")
+    if wm == 1 and not fh.lib().fhk_conv_umma_persistent_fits(cp, cout):
+        pytest.skip("two halo buffers and the weights exceed shared memory: no persistent variant")
     rng = np.random.default_rng(h * 1000 + cin * 10 + cout + 7)
     x = rng.standard_normal((cin, h, w)).astype(np.float16)
     wt = (rng.standard_normal((cout, cin, 3, 3)) / np.sqrt(9 * cin)).astype(np.float16).astype(np.float32)
@@ -162,15 +165,46 @@ def test_conv_umma_matches_oracle(torch_cuda, h, w, cin, cout, stride, res):
     slope = np.full(cout, 0.1, np.float32)
     resid = rng.standard_normal((cout, h, w)).astype(np.float16) if res else None
     ref = oracle.conv(x, wt, bias, slope, 1, resid).astype(np.float32)
-    got = run_conv(torch_cuda, x, wt, bias, slope, 1, resid, umma=True).astype(np.float32)
+    got = run_conv(torch_cuda, x, wt, bias, slope, 1, resid, wm=wm, umma=True).astype(np.float32)
     assert rel_l2(got, ref) < 2e-3
     assert np.abs(got - ref).max() <= 4e-3 * max(1.0, np.abs(ref).max())
     assert fh.lib().fhk_conv_wait_timeouts(0) == 0
 
 
-@pytest.mark.parametrize("h,w,cin,cout,umma", [(60, 108, 48, 48, False), (30, 54, 279, 96, False),
-                                               (60, 108, 48, 48, True)])
-def test_conv_weight_wait_runs_out(torch_cuda, h, w, cin, cout, umma):
+@pytest.mark.parametrize("h,w,cin,cout,res", [(60, 108, 48, 48, False), (60, 108, 48, 7, True), (37, 29, 24, 24, True),
+                                              (30, 54, 96, 96, True), (120, 216, 14, 24, False), (17, 9, 3, 36, False)])
+def test_conv_umma_persistent_is_bit_exact(torch_cuda, h, w, cin, cout, res):
+    """The persistent variant (a CTA looping over tiles, halo and accumulators double-buffered) gives the bytes of the
+    one-tile-per-CTA kernel, over a batch of 5 entries (tiles of several entries per CTA)."""
+    import flyhigh_engine_b200 as fh
+    from flyhigh_engine_b200.kernels import Conv3x3
+    torch = torch_cuda
+    cp = (_up8(cin) + 15) // 16 * 16
+    if not fh.lib().fhk_conv_umma_persistent_fits(cp, cout):
+        pytest.skip("no persistent variant for this shape")
+    rng = np.random.default_rng(cin * 31 + cout)
+    cs = 4 if cin <= 4 else _up8(cin)
+    x = torch.zeros((5, h, w, cs), dtype=torch.float16)
+    x[..., :cin] = torch.from_numpy(rng.standard_normal((5, h, w, cin)).astype(np.float16))
+    x = x.cuda()
+    wt = (rng.standard_normal((cout, cin, 3, 3)) / np.sqrt(9 * cin)).astype(np.float32)
+    bias = (0.1 * rng.standard_normal(cout)).astype(np.float32)
+    slope = np.full(cout, 0.1, np.float32)
+    outs = []
+    for wm in (0, 1):
+        conv = Conv3x3(wt, bias, slope, kernel="umma", wm=wm)
+        r = None
+        if res:
+            torch.manual_seed(3)
+            r = torch.randn(conv.out_shape(5, h, w), dtype=torch.float16, device="cuda")
+        outs.append(conv(x, r).cpu().numpy())
+    assert np.array_equal(outs[0].view(np.uint16), outs[1].view(np.uint16))
+    assert fh.lib().fhk_conv_wait_timeouts(0) == 0
+
+
+@pytest.mark.parametrize("h,w,cin,cout,umma,wm", [(60, 108, 48, 48, False, 0), (30, 54, 279, 96, False, 0),
+                                                  (60, 108, 48, 48, True, 0), (60, 108, 48, 48, True, 1)])
+def test_conv_weight_wait_runs_out(torch_cuda, h, w, cin, cout, umma, wm):
     """Failure detection without a fault: the weight staging's mbarrier is made to expect 16 bytes that no copy brings
     (whole slice: 48 -> 48; streamed ring: 279 -> 96), so every wait runs out after its bound; the kernel counts the
     timeouts, finishes and leaves the context usable, and the next normal launch is exact again."""
@@ -183,9 +217,9 @@ def test_conv_weight_wait_runs_out(torch_cuda, h, w, cin, cout, umma):
     bias = np.zeros(cout, np.float32)
     slope = np.full(cout, 0.1, np.float32)
     assert L.fhk_conv_wait_timeouts(1) >= 0
-    run_conv(torch_cuda, x, wt, bias, slope, 1, wait_cycles=200000, extra_tx=16, umma=umma)
+    run_conv(torch_cuda, x, wt, bias, slope, 1, wm=wm, wait_cycles=200000, extra_tx=16, umma=umma)
     assert L.fhk_conv_wait_timeouts(1) > 0
-    got = run_conv(torch_cuda, x, wt, bias, slope, 1, umma=umma).astype(np.float32)
+    got = run_conv(torch_cuda, x, wt, bias, slope, 1, wm=wm, umma=umma).astype(np.float32)
     assert L.fhk_conv_wait_timeouts(0) == 0
     ref = oracle.conv(x, wt, bias, slope, 1).astype(np.float32)
     assert rel_l2(got, ref) < 2e-3
