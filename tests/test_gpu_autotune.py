@@ -1,6 +1,6 @@
 """The conv autotuner (ops/conv/autotune.rs:74-150 conv_pick, ops/conv/tune_cache.rs): when a session is built, each
 conv shape (cin, cout, h, w, stride) not chosen before on the device is timed over its candidate kernels (mma.sync at
-1, 2 and 4 rows per CTA pair, tcgen05 where it fits) and the fastest kept; FhEngineOptions.tune_cache persists the
+1, 2 and 4 rows per CTA pair, tcgen05 and its persistent variant where they fit) and the fastest kept; FhEngineOptions.tune_cache persists the
 choices per GPU and driver, FhSessionOptions.tune imposes a table, autotune = 0 keeps the fixed rule. Every other GPU
 test runs on autotuned sessions (the default) against the oracle."""
 import os
@@ -69,7 +69,7 @@ def test_tune_cache_persists_and_reloads(synth_model_dir, cuda, tmp_path):
     assert len(lines) == first["engine"]["autotune_entries"] and lines == sorted(lines)
     for ln in lines:
         key, val = ln.split("=")
-        assert len(key.split(",")) == 5 and int(val) in (0x11, 0x21, 0x41, 0x02), ln
+        assert len(key.split(",")) == 5 and int(val) in (0x11, 0x21, 0x41, 0x02, 0x12), ln
     second = _child(synth_model_dir, cache, tmp_path / "b.npy")
     assert second["session"]["autotuned"] == 0
     assert all(c["choice"] == "table" for c in second["session"]["convs"].values())

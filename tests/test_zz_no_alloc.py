@@ -2,7 +2,8 @@
 reserve their GPU memory up front, plugins whose memory belongs to the host application's allocator). Its scratch is
 a device array inside the library, so it is checked here against the allocating entry point fhk_gmhs, which takes
 the caller's scratch: the same inputs must give the same repaired flow, on two calls in a row with different inputs
-(the shared array keeps the previous call's contents, which must not leak into the next result).
+(the shared array keeps the previous call's contents, which must not leak into the next result), and the second
+call must leave the device's free memory as it found it.
 
 This file sorts last so that a run stopping at the first failure has run every other test before it.
 """
@@ -38,10 +39,13 @@ def _repair(torch, lib, entry, a, b, flow, full_w, with_scratch):
         scratch = torch.full((lib.fhk_gmhs_scratch_floats(h, w),), float("nan"), dtype=torch.float32, device="cuda")
     p = GmhsParams(F.data_ptr(), 0, h8, w8, A.data_ptr(), B.data_ptr(), 0, h, w, full_w, 1,
                    scratch.data_ptr() if scratch is not None else None, 1)
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
     rc = entry(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == 0, rc
     torch.cuda.synchronize()
-    return F[:, :, :4].permute(2, 0, 1).float().cpu().numpy()
+    free_after = torch.cuda.mem_get_info()[0]
+    return F[:, :, :4].permute(2, 0, 1).float().cpu().numpy(), free_before - free_after
 
 
 def test_gmhs_without_allocation_matches_gmhs(synth_model_dir):
@@ -60,8 +64,10 @@ def test_gmhs_without_allocation_matches_gmhs(synth_model_dir):
         o.pair(fa, fb)
         a, b, pre, post = o.tensor("A"), o.tensor("B"), o.tensor("flow_pre"), o.tensor("flow")
         full_w = o.dims()["wp"]
-        ref = _repair(torch, lib, lib.fhk_gmhs, a, b, pre, full_w, with_scratch=True)
-        got = _repair(torch, lib, lib.fhk_gmhs_noalloc, a, b, pre, full_w, with_scratch=False)
+        ref, _ = _repair(torch, lib, lib.fhk_gmhs, a, b, pre, full_w, with_scratch=True)
+        got, taken = _repair(torch, lib, lib.fhk_gmhs_noalloc, a, b, pre, full_w, with_scratch=False)
+        if seed == 11:  # past the first call (which may load the library's device code), a call takes no memory
+            assert taken == 0, taken
         # the repair stage is bit-exact against the oracle, so the two entry points must agree exactly
         assert np.array_equal(got, ref), int((got != ref).any(axis=0).sum())
         assert np.array_equal(got, post)
