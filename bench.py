@@ -806,9 +806,9 @@ def render_bytes(p) -> float:
 
 
 def render_design_bytes(p) -> float:
-    """Bytes this design's render reads beyond the algorithmic ones: the static planes of the padded plane that
-    k_static_planes writes (the own-pixel (es, kk) pair as two f32 and near as u8, 9 B/px)."""
-    return float(p["hp"] * p["wp"] * 9)
+    """Bytes this design's render reads beyond the algorithmic ones: the own-pixel word of the padded plane that
+    k_static_planes writes (near, the keep_static ramp and the still test's mean in 32 bits, 4 B/px)."""
+    return float(p["hp"] * p["wp"] * 4)
 
 
 RENDER_PROFILE = os.path.join(ROOT, "profiles", "k_render_1080p.md")

@@ -349,7 +349,7 @@ struct Pending {
 
 // The per-interval buffers of a session (nbat entries each), held once per render set (FhSession::RenderSet)
 #define FH_SET_BUFFERS(X)                                                                                          \
-    X(int16_t*, age) X(uint8_t*, nearp) X(float*, dsum) X(float2*, ownp) X(__half*, cv) X(__half*, ch1)            \
+    X(int16_t*, age) X(uint8_t*, nearp) X(float*, dsum) X(uint32_t*, ownp) X(__half*, cv) X(__half*, ch1)            \
     X(__half*, ch2) X(__half*, ch3r) X(__half*, hcb) X(__half*, ob) X(__half*, fv) X(__half*, wbuf) X(__half*, fcv) \
     X(__half*, fr1) X(__half*, fr2) X(__half*, fr3) X(__half*, wt36) X(float*, coef) X(float*, maps) X(float*, tmp) \
     X(float*, tdev) X(__half*, hm) X(__half*, fh1) X(__half*, fh2) X(__half*, dfilm) X(__half*, ftvt)              \
@@ -423,9 +423,9 @@ struct FhSession {
     uint32_t* spread = nullptr;  // the static age pass's byte thresholds
     uint8_t* mask = nullptr;
     uchar4* state = nullptr;
-    // the per-interval buffers of the render set in use: age (static age), nearp (near a protected pixel), dsum (the
-    // still test's per-pixel |A - B| sums), ownp (the exact render's own-pixel (es, kk) plane), the network's
-    // activations and maps, tdev (the entries' phases)
+    // the per-interval buffers of the render set in use: age (static age), nearp (the fast render's near a protected
+    // pixel), dsum (the still test's per-pixel |A - B| sums), ownp (the exact render's own-pixel words: near, kk, es),
+    // the network's activations and maps, tdev (the entries' phases)
 #define FH_DECL(T, n) T n = nullptr;
     FH_SET_BUFFERS(FH_DECL)
 #undef FH_DECL
@@ -1020,10 +1020,10 @@ struct FhSession {
         for (int p = 0; p < (nbat > 1 ? nsets : 1); p++) {
             if (protects) {
                 age = alloc_n<int16_t>((size_t)nb * hp * wp);
-                nearp = alloc_n<uint8_t>((size_t)nb * hp * wp);
+                if (fast) nearp = alloc_n<uint8_t>((size_t)nb * hp * wp);
             }
             if (still) dsum = alloc_n<float>((size_t)nb * hp * wp);
-            if (!fast && (still || protects)) ownp = alloc_n<float2>((size_t)nb * hp * wp);
+            if (!fast && (still || protects)) ownp = alloc_n<uint32_t>((size_t)nb * hp * wp);
             cv = img(h16, w16, 56, nb);
             ch1 = img(h16, w16, CCP, nb);
             ch2 = img(h16, w16, CCP, nb);
@@ -1164,14 +1164,14 @@ struct FhSession {
                                sp_out));
             mark("static_age");
         }
-        // the fast render's probes clamp to the frame, the exact render's to the padded plane; the exact
-        // render also takes its own-pixel (es, kk) plane
+        // the fast render's probes clamp to the frame (its near plane), the exact render's to the padded plane (near
+        // inside its own-pixel words, beside es and kk)
         if (fast && protects) {
             CK(fhk::static_planes(age, nullptr, P, wp, hp, min_age, nearp, nullptr, n, st, w, h));
             mark("static_planes");
         } else if (!fast) {
-            CK(fhk::static_planes(protects ? age : nullptr, still ? dsum : nullptr, P, wp, hp, min_age,
-                                  protects ? nearp : nullptr, ownp, n, st));
+            CK(fhk::static_planes(protects ? age : nullptr, still ? dsum : nullptr, P, wp, hp, min_age, nullptr, ownp,
+                                  n, st));
             mark("static_planes");
         }
     }
@@ -1251,7 +1251,7 @@ struct FhSession {
         } else {
             fhk::RenderArgs ra{p.a.half, p.b.half, p.a.half_bs, w, h, hp, wp, up7, eup, rt, ert, qh, qw, fsx, fsy,
                                cubic ? 1 : 0, (decisive ? 1u : 0u) | (still ? 2u : 0u), protects ? age : nullptr, P, ownp,
-                               nearp, P, min_age, out, out_bs};
+                               P, min_age, out, out_bs};
             ra.out_table = render_table;
             CK(fhk::render(ra, n, st));
             mark("render");

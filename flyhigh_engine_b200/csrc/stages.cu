@@ -335,12 +335,14 @@ __global__ void __launch_bounds__(256) k_pair_planes(const uint8_t* __restrict__
 // The static planes the render reads, per pixel of the region, in one pass:
 //  - near (AGE): render_static's on_static (gpu/pipeline.rs:10-34), an age >= min_age in the clamped 3 x 3
 //    neighbourhood;
-//  - own (OWN): the render's terms at its own pixel, (es, kk). es = the still test's 27-term mean of |A - B| over the
-//    clamped 3 x 3 neighbourhood (render.wgsl:136-143): the sum of the 9 per-pixel channel sums (ES, from
-//    pair_planes; every partial sum is exact in f32, so the order does not matter) / 27; where the pixel's age is
-//    below 3 in magnitude (AGE: the static rules zero the still weight there) es is 1, which the still test's
-//    es < 0.03 turns into the same zero weight. kk = the keep_static apply ramp of the pixel's age
-//    (keep_static.wgsl:25-26), 0 without static protection. The render reads both in one 8-byte load.
+//  - own (OWN): the render's terms at its own pixel in one 32-bit word, near included (bit 31). es = the still test's
+//    27-term mean of |A - B| over the clamped 3 x 3 neighbourhood (render.wgsl:136-143): the sum of the 9 per-pixel
+//    channel sums (ES, from pair_planes; every partial sum is exact in f32, so the order does not matter) / 27; where
+//    the pixel's age is below 3 in magnitude (AGE: the static rules zero the still weight there) es is 1, which the
+//    still test's es < 0.03 turns into the same zero weight. kk = the keep_static apply ramp of the pixel's age
+//    (keep_static.wgsl:25-26), 0 without static protection: min_age is a whole number of frames, so kk is 0, 0.5 or
+//    1, two bits (29-30). es is 0 or in [2^-23, 1], where f32 bit 30 is 0 and bit 29 is 1: bits 0-28 carry it
+//    (own_es). The render reads all three in one 4-byte load, 4 bytes a pixel instead of 9.
 // A warp is one 32-pixel row segment (blocks of 32 x 8): each lane reduces its column over rows y - 1 .. y + 1, and the
 // columns either side come from the neighbouring lanes (a ballot shifted one column each way for near, shuffles for
 // es) or, for lanes 0 and 31, from the columns either side of the segment.
@@ -348,9 +350,9 @@ constexpr int NEAR_ROWS = 4;
 // W x H: the region covered and clamped to (the padded plane, or the frame for the fast render); pitch: the planes' row
 // pitch in elements
 template <bool AGE, bool ES, bool OWN>
-__global__ void __launch_bounds__(256) k_static_planes(const int16_t* __restrict__ age, const float* __restrict__ dsum,
+__global__ void __launch_bounds__(256, 4) k_static_planes(const int16_t* __restrict__ age, const float* __restrict__ dsum,
                                                        long long bs, int pitch, int W, int H, float min_age,
-                                                       uint8_t* near, float2* own_plane) {
+                                                       uint8_t* near, uint32_t* own_plane) {
     pdl_wait();
     pdl_trigger();
     // a thread takes NEAR_ROWS consecutive rows: rows y0 - 1 .. y0 + NEAR_ROWS of its column (and of its outer column)
@@ -383,12 +385,14 @@ __global__ void __launch_bounds__(256) k_static_planes(const int16_t* __restrict
         const int y = y0 + k;
         if (y >= H) break;  // warp-uniform
         const long long o = blockIdx.z * bs + (long long)y * pitch + x;
+        uint32_t near_bit = 0;
         if (AGE) {
             auto on = [&](int16_t v) { return (float)v >= min_age; };
             const uint32_t col = __ballot_sync(0xffffffffu, on(ac[k]) | on(ac[k + 1]) | on(ac[k + 2]));
             const uint32_t eb = __ballot_sync(0xffffffffu, on(ae[k]) | on(ae[k + 1]) | on(ae[k + 2]));
             const uint32_t nb = col | (col << 1) | (eb & 1u) | (col >> 1) | (eb & 0x80000000u);
-            if (x < W) near[o] = (uint8_t)((nb >> lane) & 1u);
+            near_bit = (nb >> lane) & 1u;
+            if (!OWN && x < W) near[o] = (uint8_t)near_bit;
         }
         if (OWN) {
             float es = 0.0f, kk = 0.0f;
@@ -404,7 +408,9 @@ __global__ void __launch_bounds__(256) k_static_planes(const int16_t* __restrict
                 if (!(fabsf(age_o) >= 3.0f)) es = 1.0f;
                 kk = fminf(fmaxf((age_o - min_age + 2.0f) / 2.0f, 0.0f), 1.0f);
             }
-            if (x < W) own_plane[o] = make_float2(es, kk);
+            // kk in halves (exact: a whole age and min_age), es without its bit 29 (own_es puts it back)
+            const uint32_t word = (__float_as_uint(es) & 0x1fffffffu) | ((uint32_t)(kk * 2.0f) << 29) | (near_bit << 31);
+            if (x < W) own_plane[o] = word;
         }
     }
 }
@@ -1335,27 +1341,23 @@ FH_DEV float3 sample_frame(const uint2* __restrict__ f, int w, int h, float gx, 
                        bil_mix(p00.z, p01.z, p10.z, p11.z, ax, ay));
 }
 
-// The Keys weights of sample_frame on float2 lanes (lane x: frame A, lane y: frame B), operation for operation, so each
-// lane rounds as cub1 / cub2 do.
+// The Keys weights of sample_frame on float2 lanes (lane x: frame A, lane y: frame B) as fused Horner steps: 3 packed
+// instructions a weight instead of 5 or 6. A weight differs from cub1 / cub2's by an f32 rounding or two; the weights
+// feed only continuous sums (the samples, and through them the still and decisive ramps), never a decision.
 FH_DEV float2 cub1x2(float2 x) {  // ((a + 2) x - (a + 3)) x x + 1, a = -0.75
-    float2 t = __fmul2_rn(make_float2(1.25f, 1.25f), x);
-    t = __fadd2_rn(t, make_float2(-2.25f, -2.25f));
-    t = __fmul2_rn(t, x);
-    t = __fmul2_rn(t, x);
-    return __fadd2_rn(t, make_float2(1.0f, 1.0f));
+    const float2 t = __ffma2_rn(make_float2(1.25f, 1.25f), x, make_float2(-2.25f, -2.25f));
+    return __ffma2_rn(t, __fmul2_rn(x, x), make_float2(1.0f, 1.0f));
 }
 FH_DEV float2 cub2x2(float2 x) {  // ((a x - 5 a) x + 8 a) x - 4 a
-    float2 t = __fmul2_rn(make_float2(-0.75f, -0.75f), x);
-    t = __fadd2_rn(t, make_float2(3.75f, 3.75f));
-    t = __fmul2_rn(t, x);
-    t = __fadd2_rn(t, make_float2(-6.0f, -6.0f));
-    t = __fmul2_rn(t, x);
-    return __fadd2_rn(t, make_float2(3.0f, 3.0f));
+    float2 t = __ffma2_rn(make_float2(-0.75f, -0.75f), x, make_float2(3.75f, 3.75f));
+    t = __ffma2_rn(t, x, make_float2(-6.0f, -6.0f));
+    return __ffma2_rn(t, x, make_float2(3.0f, 3.0f));
 }
 
 // Bicubic samples of both frames (A at (gxa, gya), B at (gxb, gyb)) with the two frames on the lanes of float2
-// arithmetic: the weights, the row sums and the column sum each take one packed instruction for both frames, with the
-// roundings of sample_frame per lane. Where either sample's taps reach the border, each frame is sampled alone.
+// arithmetic: the weights (cub1x2 / cub2x2), the row sums and the column sum each take packed instructions for both
+// frames, the sums with the roundings of sample_frame per lane. Where either sample's taps reach the border, each frame
+// is sampled alone.
 FH_DEV void sample_pair(const uint2* __restrict__ A, const uint2* __restrict__ B, int w, int h, float gxa, float gya,
                         float gxb, float gyb, float3& sa, float3& sb) {
     const int pxa = (int)floorf(gxa), pya = (int)floorf(gya), pxb = (int)floorf(gxb), pyb = (int)floorf(gyb);
@@ -1403,150 +1405,209 @@ FH_DEV void sample_pair(const uint2* __restrict__ A, const uint2* __restrict__ B
     sb = make_float3(acc_b.y, acc_g.y, acc_r.y);
 }
 
-// render.wgsl:82-161 + gpu/pipeline.rs:10-34 (static rules) + keep_static.wgsl:21-32 + rgba_out.wgsl:9-17.
-// Plane offsets are 32-bit (a padded plane holds < 2^31 pixels; checked by render()).
-__global__ void __launch_bounds__(256, 5) k_render(RenderArgs r) {
-    pdl_wait();
-    pdl_trigger();
-    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y * blockDim.y + threadIdx.y, n = blockIdx.z;
-    if (x >= r.w || y >= r.h) return;
-    const int H = r.hp, W = r.wp, hq = r.hq, wq = r.wq;
-    const uint2* __restrict__ A = reinterpret_cast<const uint2*>(r.ha + (long long)n * r.h_bs);
-    const uint2* __restrict__ B = reinterpret_cast<const uint2*>(r.hb + (long long)n * r.h_bs);
-    const __half* up = r.up7 + (long long)n * r.up_bs;
-    const __half* rt = r.rt + (long long)n * r.rt_bs;
-    const int16_t* age = r.age ? r.age + (long long)n * r.age_bs : nullptr;
-    // the Q-res sample corners (render.wgsl:87-92)
-    const float iy = ((float)y + 0.5f) * r.qsy - 0.5f, ix = ((float)x + 0.5f) * r.qsx - 0.5f;
-    const int qy0 = (int)floorf(iy), qx0 = (int)floorf(ix);
-    const float qfy = iy - (float)qy0, qfx = ix - (float)qx0;
-    const int qr0 = clampi(qy0, 0, hq - 1) * wq, qr1 = clampi(qy0 + 1, 0, hq - 1) * wq;
-    const int qc0 = clampi(qx0, 0, wq - 1), qc1 = clampi(qx0 + 1, 0, wq - 1);
-    // the four Q corners: flow_tq (0-3) and vis_tq (4-6) in one 16-byte load each, R_t in one 8-byte load each
-    const uint4* U = reinterpret_cast<const uint4*>(up);
-    const uint4 U00 = __ldg(U + qr0 + qc0), U01 = __ldg(U + qr0 + qc1), U10 = __ldg(U + qr1 + qc0),
-                U11 = __ldg(U + qr1 + qc1);
-    const uint2* RT = reinterpret_cast<const uint2*>(rt);
-    const uint2 R00 = __ldg(RT + qr0 + qc0), R01 = __ldg(RT + qr0 + qc1), R10 = __ldg(RT + qr1 + qc0),
-                R11 = __ldg(RT + qr1 + qc1);
-    // channel pairs on float2 lanes: (flow 0, 1), (flow 2, 3), (vis 0, 1), (vis 2, R_t 2), (R_t 0, 1)
-    const float2 fs = make_float2(r.fsx, r.fsy);
-    const float2 f01 = __fmul2_rn(bil_mix2(h2x2(U00.x), h2x2(U01.x), h2x2(U10.x), h2x2(U11.x), qfx, qfy), fs);
-    const float2 f23 = __fmul2_rn(bil_mix2(h2x2(U00.y), h2x2(U01.y), h2x2(U10.y), h2x2(U11.y), qfx, qfy), fs);
-    const float2 v01 = bil_mix2(h2x2(U00.z), h2x2(U01.z), h2x2(U10.z), h2x2(U11.z), qfx, qfy);
+// The own-pixel word of static_planes: es (bits 0-28, its f32 bit 29 restored unless es is 0), kk (bits 29-30, in
+// halves), near (bit 31)
+FH_DEV float own_es(uint32_t w) {
+    const uint32_t low = w & 0x1fffffffu;
+    return low ? __uint_as_float(low | 0x20000000u) : 0.0f;
+}
+FH_DEV float own_kk(uint32_t w) { return (float)((w >> 29) & 3u) * 0.5f; }
+
+// A render block covers 32 columns x 8 * RENDER_ROWS rows: a thread takes rows ty, ty + 8, ... of its column. The
+// quarter-resolution maps are bilinear in two steps (bil_mix2: the two corners of a Q row mixed by the column's
+// fraction, then the two rows by the row's fraction). The first step depends only on the Q row and the column, so the
+// block forms it once per Q row it touches and column, into shared memory (RENDER_QSTRIDE floats per entry: the five
+// channel pairs flow 0-1, flow 2-3, vis 0-1, (vis 2, R_t 2), R_t 0-1, and two floats of padding, which keeps a warp's
+// 16-byte reads of one Q row free of bank conflicts), and each pixel does the second step from two entries.
+constexpr int RENDER_ROWS = 8;
+constexpr int RENDER_QSTRIDE = 12;
+// Q rows a block can touch: its rows y .. y + 8 RENDER_ROWS - 1 map to Q rows floor(fy) .. floor(fy + (8 RENDER_ROWS - 1)
+// qsy) + 1, with qsy <= 1
+static inline int render_q_rows(float qsy) { return (int)((float)(8 * RENDER_ROWS - 1) * qsy) + 4; }
+
+// The first step of the Q-res bilinear for Q row `row` (its offset in the maps) at one column: corners qc0 / qc1,
+// fraction ax; bil_mix2's top (or bot) for each channel pair, with its roundings.
+FH_DEV void q_row_mix(const uint4* __restrict__ U, const uint2* __restrict__ RT, int row, int qc0, int qc1, float ax,
+                      float4* dst) {
+    const uint4 u0 = __ldg(U + row + qc0), u1 = __ldg(U + row + qc1);
+    const uint2 r0 = __ldg(RT + row + qc0), r1 = __ldg(RT + row + qc1);
+    const float2 bx = make_float2(1.0f - ax, 1.0f - ax), fx = make_float2(ax, ax);
+    auto mix = [&](float2 v0, float2 v1) { return __fadd2_rn(__fmul2_rn(v0, bx), __fmul2_rn(v1, fx)); };
     auto lo2 = [](uint32_t a, uint32_t b) {  // the low halves of two words
         return make_float2(__half2float(__ushort_as_half((unsigned short)(a & 0xffffu))),
                            __half2float(__ushort_as_half((unsigned short)(b & 0xffffu))));
     };
-    const float2 v2r2 = bil_mix2(lo2(U00.w, R00.y), lo2(U01.w, R01.y), lo2(U10.w, R10.y), lo2(U11.w, R11.y), qfx, qfy);
-    const float2 r01 = bil_mix2(h2x2(R00.x), h2x2(R01.x), h2x2(R10.x), h2x2(R11.x), qfx, qfy);
-    const float f[4] = {f01.x, f01.y, f23.x, f23.y}, v[3] = {v01.x, v01.y, v2r2.x};
-    // the visibility softmax feeds the continuous blend: the fast exponential and one reciprocal, within a few ulps of
-    // expf and the two divisions (both weights share the reciprocal, so the decisive blend's wa >= wb keeps the order
-    // of their numerators)
-    const float m = fmaxf(v[0], fmaxf(v[1], v[2]));
-    const float e0 = __expf(v[0] - m), e1 = __expf(v[1] - m), e2 = __expf(v[2] - m);
-    const float inv = __frcp_rn(e0 + e1 + e2);
-    const float wa_w = fmaf(0.5f, e2, e0) * inv, wb_w = fmaf(0.5f, e2, e1) * inv;
-    const float gxa = (float)x + f[0], gya = (float)y + f[1], gxb = (float)x + f[2], gyb = (float)y + f[3];
-    float3 sa3, sb3;
-    if (r.cubic) {
-        sample_pair(A, B, r.w, r.h, gxa, gya, gxb, gyb, sa3, sb3);
-    } else {
-        sa3 = sample_frame(A, r.w, r.h, gxa, gya, false);
-        sb3 = sample_frame(B, r.w, r.h, gxb, gyb, false);
-    }
-    const float ca[3] = {sa3.x, sa3.y, sa3.z}, cb[3] = {sb3.x, sb3.y, sb3.z};
-    const float cr[3] = {r01.x, r01.y, v2r2.y};
-    float bwa = wa_w, bwb = wb_w, rk = 1.0f, stillw = 0.0f, own[3] = {0.0f, 0.0f, 0.0f};
-    const float third = 1.0f / 3.0f;
-    const int here = y * r.w + x;  // x < w, y < h: no clamp
-    const float3 pa_here = px3(A + here), pb_here = px3(B + here);
-    const int o = y * W + x;
-    // the pixel's (es, kk) (static_planes): the still test's 27-term mean (1 where the static rules zero the still
-    // weight) and the keep_static ramp
-    const float2 ok = r.own ? __ldg(r.own + (long long)n * r.plane_bs + o) : make_float2(0.0f, 0.0f);
-    if (r.flags & 2u) {
-        const float es = ok.x;
-        for (int c = 0; c < 3; c++) own[c] = 0.5f * (comp(pa_here, c) + comp(pb_here, c));
-        const float ef = fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
-        // the ramp is continuous: x 25 for / 0.04 (within an ulp; a division costs a dozen instructions)
-        stillw = fminf(fmaxf((ef - es) * 25.0f, 0.0f), 1.0f) * (es < 0.03f ? 1.0f : 0.0f);
-    }
-    if (r.flags & 1u) {
-        const float d = fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
-        const float k = fminf(fmaxf((d - 0.04f) / 0.08f, 0.0f), 1.0f);
-        const float pa = wa_w >= wb_w ? 1.0f : 0.0f;
-        bwa = wa_w * (1.0f - k) + pa * k;
-        bwb = wb_w * (1.0f - k) + (1.0f - pa) * k;
-        rk = 1.0f - k;
-    }
-    float raw = 0.0f, kk = 0.0f;
-    if (age) {
-        const uint8_t* near = r.near + (long long)n * r.plane_bs;
-        auto on_static = [&](float gx, float gy) {
-            const int cx = (int)rintf(gx), cy = (int)rintf(gy);  // WGSL round(): half to even
-            if (cx >= 0 && cx < W && cy >= 0 && cy < H) return __ldg(near + cy * W + cx) != 0;
-            for (int dy = -1; dy <= 1; dy++)
-                for (int dx = -1; dx <= 1; dx++)
-                    if ((float)age[clampi(cy + dy, 0, H - 1) * W + clampi(cx + dx, 0, W - 1)] >= r.min_age) return true;
-            return false;
-        };
-        const bool sa = on_static(gxa, gya), sb = on_static(gxb, gyb);
-        if (sa && sb) {
-            rk = 0.0f;
-            raw = 1.0f;
-        } else if (sa) {
-            rk = 0.0f;
-            bwa = 0.0f;
-            bwb = 1.0f;
-        } else if (sb) {
-            rk = 0.0f;
-            bwa = 1.0f;
-            bwb = 0.0f;
-        }
-        kk = ok.y;  // keep_static apply ramp (keep_static.wgsl:25-26)
-    }
-    // per channel: the blend, the still mix, the static mix, the f16 render plane, the keep_static ramp, rgba8. B and G
-    // on the lanes of packed f32x2 arithmetic (each lane rounding as the scalar code of R), R alone.
-    auto clamp01 = [](float v) { return fminf(fmaxf(v, 0.0f), 1.0f); };
-    auto dup = [](float v) { return make_float2(v, v); };
-    const float2 sw = dup(stillw), sw1 = dup(1.0f - stillw), rw = dup(raw), rw1 = dup(1.0f - raw), k2 = dup(kk),
-                 k1 = dup(1.0f - kk);
-    uint32_t q[3];
-    {
-        const float2 mixv = __fadd2_rn(__fadd2_rn(__fmul2_rn(make_float2(ca[0], ca[1]), dup(bwa)),
-                                                  __fmul2_rn(make_float2(cb[0], cb[1]), dup(bwb))),
-                                       __fmul2_rn(make_float2(cr[0], cr[1]), dup(rk)));
-        float2 ov = __fadd2_rn(__fmul2_rn(mixv, sw1), __fmul2_rn(make_float2(own[0], own[1]), sw));
-        ov = make_float2(clamp01(ov.x), clamp01(ov.y));
-        const float2 src = __fmul2_rn(dup(0.5f), __fadd2_rn(make_float2(pa_here.x, pa_here.y),
-                                                             make_float2(pb_here.x, pb_here.y)));
-        if (age) {
-            ov = __fadd2_rn(__fmul2_rn(ov, rw1), __fmul2_rn(src, rw));
-            ov = make_float2(clamp01(ov.x), clamp01(ov.y));
-        }
-        float2 hv = __half22float2(__floats2half2_rn(ov.x, ov.y));  // the render plane is f16
-        if (kk > 0.0f) {
-            const float2 m = __fadd2_rn(__fmul2_rn(hv, k1), __fmul2_rn(src, k2));
-            hv = __half22float2(__floats2half2_rn(m.x, m.y));
-        }
-        const float2 qv = __fadd2_rn(__fmul2_rn(make_float2(clamp01(hv.x), clamp01(hv.y)), dup(255.0f)), dup(0.5f));
-        q[0] = (uint32_t)qv.x;
-        q[1] = (uint32_t)qv.y;
-    }
-    {
-        const float mixv = ca[2] * bwa + cb[2] * bwb + cr[2] * rk;
-        float ov = clamp01(mixv * (1.0f - stillw) + own[2] * stillw);
-        const float src = 0.5f * (pa_here.z + pb_here.z);
-        if (age) ov = clamp01(ov * (1.0f - raw) + src * raw);
-        float hv = rh(ov);
-        if (kk > 0.0f) hv = rh(hv * (1.0f - kk) + src * kk);
-        q[2] = (uint32_t)(clamp01(hv) * 255.0f + 0.5f);
-    }
-    // q[0] = B, q[1] = G, q[2] = R
+    const float2 f01 = mix(h2x2(u0.x), h2x2(u1.x)), f23 = mix(h2x2(u0.y), h2x2(u1.y));
+    const float2 v01 = mix(h2x2(u0.z), h2x2(u1.z)), v2r2 = mix(lo2(u0.w, r0.y), lo2(u1.w, r1.y));
+    const float2 r01 = mix(h2x2(r0.x), h2x2(r1.x));
+    dst[0] = make_float4(f01.x, f01.y, f23.x, f23.y);
+    dst[1] = make_float4(v01.x, v01.y, v2r2.x, v2r2.y);
+    dst[2] = make_float4(r01.x, r01.y, 0.0f, 0.0f);
+}
+
+// bil_mix2's second step: the two rows' mixes by the row fraction
+FH_DEV float2 q_col_mix(float2 top, float2 bot, float ay) {
+    return __fadd2_rn(__fmul2_rn(top, make_float2(1.0f - ay, 1.0f - ay)), __fmul2_rn(bot, make_float2(ay, ay)));
+}
+
+// render.wgsl:82-161 + gpu/pipeline.rs:10-34 (static rules) + keep_static.wgsl:21-32 + rgba_out.wgsl:9-17.
+// Plane offsets are 32-bit (a padded plane holds < 2^31 pixels; checked by render()). Dynamic shared memory:
+// r.q_rows x 32 x RENDER_QSTRIDE floats.
+__global__ void __launch_bounds__(256, 4) k_render(RenderArgs r) {
+    extern __shared__ float4 qtab[];  // [q row of the block][column][RENDER_QSTRIDE / 4]
+    pdl_wait();
+    pdl_trigger();
+    const int lane = threadIdx.x, x = blockIdx.x * 32 + lane, n = blockIdx.z;
+    const int yb = blockIdx.y * (8 * RENDER_ROWS);
+    if (yb >= r.h) return;  // block-uniform
+    const int H = r.hp, W = r.wp, hq = r.hq, wq = r.wq;
+    const uint4* U = reinterpret_cast<const uint4*>(r.up7 + (long long)n * r.up_bs);
+    const uint2* RT = reinterpret_cast<const uint2*>(r.rt + (long long)n * r.rt_bs);
+    // the Q-res sample corners (render.wgsl:87-92): the column's, and the Q rows the block's rows reach (the row
+    // corner is monotonic in y, so they are qlo .. qhi)
+    const int ylast = min(yb + 8 * RENDER_ROWS, r.h) - 1;
+    const int qlo = clampi((int)floorf(((float)yb + 0.5f) * r.qsy - 0.5f), 0, hq - 1);
+    const int qhi = clampi((int)floorf(((float)ylast + 0.5f) * r.qsy - 0.5f) + 1, 0, hq - 1);
+    const int nq = min(qhi - qlo + 1, r.q_rows);
+    const int xs = min(x, r.w - 1);  // columns past the frame form a valid entry and store nothing
+    const float ix = ((float)xs + 0.5f) * r.qsx - 0.5f;
+    const int qx0 = (int)floorf(ix);
+    const float qfx = ix - (float)qx0;
+    const int qc0 = clampi(qx0, 0, wq - 1), qc1 = clampi(qx0 + 1, 0, wq - 1);
+    for (int q = threadIdx.y; q < nq; q += 8)
+        q_row_mix(U, RT, (qlo + q) * wq, qc0, qc1, qfx, qtab + (q * 32 + lane) * (RENDER_QSTRIDE / 4));
+    __syncthreads();
+    if (x >= r.w) return;
+    const uint2* __restrict__ A = reinterpret_cast<const uint2*>(r.ha + (long long)n * r.h_bs);
+    const uint2* __restrict__ B = reinterpret_cast<const uint2*>(r.hb + (long long)n * r.h_bs);
+    const int16_t* age = r.age ? r.age + (long long)n * r.age_bs : nullptr;
+    const uint32_t* own = r.own ? r.own + (long long)n * r.plane_bs : nullptr;
     uint8_t* const dst = r.out_table ? r.out_table[n] : r.out + (long long)n * r.out_bs;
-    reinterpret_cast<uint32_t*>(dst)[here] = q[2] | (q[1] << 8) | (q[0] << 16) | 0xff000000u;
+    const float2 fs = make_float2(r.fsx, r.fsy);
+#pragma unroll 1
+    for (int i = 0; i < RENDER_ROWS; i++) {
+        const int y = yb + threadIdx.y + 8 * i;
+        if (y >= r.h) break;
+        const float iy = ((float)y + 0.5f) * r.qsy - 0.5f;
+        const int qy0 = (int)floorf(iy);
+        const float qfy = iy - (float)qy0;
+        const int q0 = min(clampi(qy0, 0, hq - 1) - qlo, nq - 1), q1 = min(clampi(qy0 + 1, 0, hq - 1) - qlo, nq - 1);
+        const float4* t0 = qtab + (q0 * 32 + lane) * (RENDER_QSTRIDE / 4);
+        const float4* t1 = qtab + (q1 * 32 + lane) * (RENDER_QSTRIDE / 4);
+        const float4 a0 = t0[0], a1 = t0[1], a2 = t0[2], b0 = t1[0], b1 = t1[1], b2 = t1[2];
+        // channel pairs on float2 lanes: (flow 0, 1), (flow 2, 3), (vis 0, 1), (vis 2, R_t 2), (R_t 0, 1)
+        const float2 f01 = __fmul2_rn(q_col_mix(make_float2(a0.x, a0.y), make_float2(b0.x, b0.y), qfy), fs);
+        const float2 f23 = __fmul2_rn(q_col_mix(make_float2(a0.z, a0.w), make_float2(b0.z, b0.w), qfy), fs);
+        const float2 v01 = q_col_mix(make_float2(a1.x, a1.y), make_float2(b1.x, b1.y), qfy);
+        const float2 v2r2 = q_col_mix(make_float2(a1.z, a1.w), make_float2(b1.z, b1.w), qfy);
+        const float2 r01 = q_col_mix(make_float2(a2.x, a2.y), make_float2(b2.x, b2.y), qfy);
+        const float f[4] = {f01.x, f01.y, f23.x, f23.y}, v[3] = {v01.x, v01.y, v2r2.x};
+        // the visibility softmax feeds the continuous blend: the fast exponential and one reciprocal, within a few ulps
+        // of expf and the two divisions (both weights share the reciprocal, so the decisive blend's wa >= wb keeps the
+        // order of their numerators)
+        const float m = fmaxf(v[0], fmaxf(v[1], v[2]));
+        const float e0 = __expf(v[0] - m), e1 = __expf(v[1] - m), e2 = __expf(v[2] - m);
+        const float inv = __frcp_rn(e0 + e1 + e2);
+        const float wa_w = fmaf(0.5f, e2, e0) * inv, wb_w = fmaf(0.5f, e2, e1) * inv;
+        const float gxa = (float)x + f[0], gya = (float)y + f[1], gxb = (float)x + f[2], gyb = (float)y + f[3];
+        float3 sa3, sb3;
+        if (r.cubic) {
+            sample_pair(A, B, r.w, r.h, gxa, gya, gxb, gyb, sa3, sb3);
+        } else {
+            sa3 = sample_frame(A, r.w, r.h, gxa, gya, false);
+            sb3 = sample_frame(B, r.w, r.h, gxb, gyb, false);
+        }
+        const float ca[3] = {sa3.x, sa3.y, sa3.z}, cb[3] = {sb3.x, sb3.y, sb3.z};
+        const float cr[3] = {r01.x, r01.y, v2r2.y};
+        float bwa = wa_w, bwb = wb_w, rk = 1.0f, stillw = 0.0f, mean[3] = {0.0f, 0.0f, 0.0f};
+        const float third = 1.0f / 3.0f;
+        const int here = y * r.w + x;  // x < w, y < h: no clamp
+        const float3 pa_here = px3(A + here), pb_here = px3(B + here);
+        const int o = y * W + x;
+        // the pixel's word (static_planes): the still test's 27-term mean es (1 where the static rules zero the still
+        // weight) and the keep_static ramp kk
+        const uint32_t ow = own ? __ldg(own + o) : 0u;
+        if (r.flags & 2u) {
+            const float es = own_es(ow);
+            for (int c = 0; c < 3; c++) mean[c] = 0.5f * (comp(pa_here, c) + comp(pb_here, c));
+            const float ef = fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
+            // the ramp is continuous: x 25 for / 0.04 (within an ulp; a division costs a dozen instructions)
+            stillw = fminf(fmaxf((ef - es) * 25.0f, 0.0f), 1.0f) * (es < 0.03f ? 1.0f : 0.0f);
+        }
+        if (r.flags & 1u) {
+            const float d = fabsf(ca[0] - cb[0]) * third + fabsf(ca[1] - cb[1]) * third + fabsf(ca[2] - cb[2]) * third;
+            const float k = fminf(fmaxf((d - 0.04f) / 0.08f, 0.0f), 1.0f);
+            const float pa = wa_w >= wb_w ? 1.0f : 0.0f;
+            bwa = wa_w * (1.0f - k) + pa * k;
+            bwb = wb_w * (1.0f - k) + (1.0f - pa) * k;
+            rk = 1.0f - k;
+        }
+        float raw = 0.0f, kk = 0.0f;
+        if (age) {
+            // near is bit 31 of the probed pixel's word
+            auto on_static = [&](float gx, float gy) {
+                const int cx = (int)rintf(gx), cy = (int)rintf(gy);  // WGSL round(): half to even
+                if (cx >= 0 && cx < W && cy >= 0 && cy < H) return (int)__ldg(own + cy * W + cx) < 0;
+                for (int dy = -1; dy <= 1; dy++)
+                    for (int dx = -1; dx <= 1; dx++)
+                        if ((float)age[clampi(cy + dy, 0, H - 1) * W + clampi(cx + dx, 0, W - 1)] >= r.min_age) return true;
+                return false;
+            };
+            const bool sa = on_static(gxa, gya), sb = on_static(gxb, gyb);
+            if (sa && sb) {
+                rk = 0.0f;
+                raw = 1.0f;
+            } else if (sa) {
+                rk = 0.0f;
+                bwa = 0.0f;
+                bwb = 1.0f;
+            } else if (sb) {
+                rk = 0.0f;
+                bwa = 1.0f;
+                bwb = 0.0f;
+            }
+            kk = own_kk(ow);  // keep_static apply ramp (keep_static.wgsl:25-26)
+        }
+        // per channel: the blend, the still mix, the static mix, the f16 render plane, the keep_static ramp, rgba8. B
+        // and G on the lanes of packed f32x2 arithmetic (each lane rounding as the scalar code of R), R alone.
+        auto clamp01 = [](float v) { return fminf(fmaxf(v, 0.0f), 1.0f); };
+        auto dup = [](float v) { return make_float2(v, v); };
+        const float2 sw = dup(stillw), sw1 = dup(1.0f - stillw), rw = dup(raw), rw1 = dup(1.0f - raw), k2 = dup(kk),
+                     k1 = dup(1.0f - kk);
+        uint32_t q[3];
+        {
+            const float2 mixv = __fadd2_rn(__fadd2_rn(__fmul2_rn(make_float2(ca[0], ca[1]), dup(bwa)),
+                                                      __fmul2_rn(make_float2(cb[0], cb[1]), dup(bwb))),
+                                           __fmul2_rn(make_float2(cr[0], cr[1]), dup(rk)));
+            float2 ov = __fadd2_rn(__fmul2_rn(mixv, sw1), __fmul2_rn(make_float2(mean[0], mean[1]), sw));
+            ov = make_float2(clamp01(ov.x), clamp01(ov.y));
+            const float2 src = __fmul2_rn(dup(0.5f), __fadd2_rn(make_float2(pa_here.x, pa_here.y),
+                                                                 make_float2(pb_here.x, pb_here.y)));
+            if (age) {
+                ov = __fadd2_rn(__fmul2_rn(ov, rw1), __fmul2_rn(src, rw));
+                ov = make_float2(clamp01(ov.x), clamp01(ov.y));
+            }
+            float2 hv = __half22float2(__floats2half2_rn(ov.x, ov.y));  // the render plane is f16
+            if (kk > 0.0f) {
+                const float2 mk = __fadd2_rn(__fmul2_rn(hv, k1), __fmul2_rn(src, k2));
+                hv = __half22float2(__floats2half2_rn(mk.x, mk.y));
+            }
+            const float2 qv = __fadd2_rn(__fmul2_rn(make_float2(clamp01(hv.x), clamp01(hv.y)), dup(255.0f)), dup(0.5f));
+            q[0] = (uint32_t)qv.x;
+            q[1] = (uint32_t)qv.y;
+        }
+        {
+            const float mixv = ca[2] * bwa + cb[2] * bwb + cr[2] * rk;
+            float ov = clamp01(mixv * (1.0f - stillw) + mean[2] * stillw);
+            const float src = 0.5f * (pa_here.z + pb_here.z);
+            if (age) ov = clamp01(ov * (1.0f - raw) + src * raw);
+            float hv = rh(ov);
+            if (kk > 0.0f) hv = rh(hv * (1.0f - kk) + src * kk);
+            q[2] = (uint32_t)(clamp01(hv) * 255.0f + 0.5f);
+        }
+        // q[0] = B, q[1] = G, q[2] = R
+        reinterpret_cast<uint32_t*>(dst)[here] = q[2] | (q[1] << 8) | (q[0] << 16) | 0xff000000u;
+    }
 }
 
 // ---------------------------------------------------------------------------------------------- fast render ----
@@ -1947,9 +2008,11 @@ cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, long long frame_bs
 }
 
 cudaError_t static_planes(const int16_t* age, const float* dsum, long long bs, int wp, int hp, float min_age,
-                          uint8_t* near, float2* own, int n, cudaStream_t st, int cw_, int ch_) {
+                          uint8_t* near, uint32_t* own, int n, cudaStream_t st, int cw_, int ch_) {
     const int cw = cw_ > 0 ? cw_ : wp, ch = ch_ > 0 ? ch_ : hp;
-    if (!age != !near || (dsum && !own) || (!age && !own) || (!age && !dsum)) return cudaErrorInvalidValue;
+    // near alone (the fast render: age, no dsum) or own (the exact render: age or dsum, near in its words)
+    if (!own ? (!age || !near || dsum) : (near || (!age && !dsum))) return cudaErrorInvalidValue;
+    if (min_age != floorf(min_age)) return cudaErrorInvalidValue;  // kk in halves
     const dim3 g = grid2(cw, ch, n, 32, 8 * NEAR_ROWS), b(32, 8);
     const cudaError_t e =
         !own    ? launch(k_static_planes<true, false, false>, g, b, 0, st, age, dsum, bs, wp, cw, ch, min_age, near, own)
@@ -2055,11 +2118,16 @@ cudaError_t refine_input(const __half* up7, long long up_bs, Img4 aq, Img4 bq, i
 cudaError_t render(const RenderArgs& r0, int n, cudaStream_t st) {
     if ((long long)r0.hp * r0.wp >= (1ll << 31) || r0.w > r0.wp || r0.h > r0.hp) return cudaErrorInvalidValue;
     if (((r0.flags & 2u) || r0.age) && !r0.own) return cudaErrorInvalidValue;
-    if (r0.age && !r0.near) return cudaErrorInvalidValue;
+    if (r0.hq < 1 || r0.wq < 1 || r0.hq > r0.hp || r0.wq > r0.wp) return cudaErrorInvalidValue;
+    if ((uintptr_t)r0.up7 % 16 || (uintptr_t)r0.rt % 8 || (uintptr_t)r0.ha % 8 || (uintptr_t)r0.hb % 8 ||
+        (uintptr_t)r0.own % 4)
+        return cudaErrorMisalignedAddress;
     RenderArgs r = r0;
     r.qsy = (float)r.hq / (float)r.hp;  // the same IEEE quotients render.wgsl:87-88 forms per pixel
     r.qsx = (float)r.wq / (float)r.wp;
-    { const cudaError_t e_ = launch(k_render, grid2(r.w, r.h, n, 32, 8), dim3(32, 8), 0, st, r); if (e_ != cudaSuccess) return e_; }
+    r.q_rows = render_q_rows(r.qsy);
+    const size_t smem = (size_t)r.q_rows * 32 * RENDER_QSTRIDE * sizeof(float);
+    { const cudaError_t e_ = launch(k_render, grid2(r.w, r.h, n, 32, 8 * RENDER_ROWS), dim3(32, 8), smem, st, r); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
 

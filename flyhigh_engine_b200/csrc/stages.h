@@ -54,13 +54,16 @@ inline int changed_words(int wp) { return (wp + 31) >> 5; }
 cudaError_t pair_planes(const uint8_t* fa, const uint8_t* fb, long long frame_bs, const StaticArgs& s, uint32_t* changed,
                         long long changed_bs, float* dsum, long long dsum_bs, int n, cudaStream_t st);
 // per pair after the age pass, the planes the render reads (n planes bs elements apart, row pitch wp):
-//  - near (with age): an age >= min_age in the clamped 3 x 3 neighbourhood (render_static on_static);
-//  - own (the exact render): per pixel (es, kk): es the still test's 3 x 3 mean of dsum (dsum may be null when the
-//    still test is off), set to 1 where the age is below 3 in magnitude, and kk the keep_static ramp of the age (0
-//    without age).
+//  - near (the fast render, with age): an age >= min_age in the clamped 3 x 3 neighbourhood (render_static
+//    on_static), one byte per pixel;
+//  - own (the exact render): one 32-bit word per pixel holding near (bit 31), the keep_static ramp kk of the age
+//    (bits 29-30: 0, 0.5 or 1 in halves; 0 without age) and es in bits 0-28, es being the still test's 3 x 3 mean of
+//    dsum (0 when the still test is off), set to 1 where the age is below 3 in magnitude. Every es is 0 or in
+//    [2^-23, 1] (dsum is a multiple of 2^-18), so its f32 bit 30 is 0 and bit 29 is 1 unless es is 0: bits 0-28 keep
+//    it exactly. near and own are not written together.
 // (cw, ch: the region, clamped to itself; 0 = the padded plane. The fast render's on_static clamps to the frame.)
 cudaError_t static_planes(const int16_t* age, const float* dsum, long long bs, int wp, int hp, float min_age,
-                          uint8_t* near, float2* own, int n, cudaStream_t st, int cw = 0, int ch = 0);
+                          uint8_t* near, uint32_t* own, int n, cudaStream_t st, int cw = 0, int ch = 0);
 // per pair after pair_planes: moved = the changed plane dilated by the 41 probes of keep_static_age.wgsl:59-70 (the
 // clamped 3 x 3 neighbourhood and the far ring), same layout; n planes bs words apart
 cudaError_t moved_plane(const uint32_t* changed, long long bs, int wp, int hp, uint32_t* moved, int n, cudaStream_t st);
@@ -163,14 +166,14 @@ struct RenderArgs {
     unsigned flags;          // bit 0 decisive, bit 1 still test
     const int16_t* age;      // static age plane (padded), or null
     long long age_bs;
-    const float2* own;       // static_planes' (es, kk) plane (when flags bit 1 or age is set)
-    const uint8_t* near;     // static_planes' near plane (when age is set)
+    const uint32_t* own;     // static_planes' own-pixel word (near, kk, es; when flags bit 1 or age is set)
     long long plane_bs;
     float min_age;
     uint8_t* out;            // w x h x 4
     long long out_bs;
     uint8_t* const* out_table;  // when set, entry n is written to out_table[n] (device array) instead of out + n out_bs
     float qsy, qsx;          // hq / hp and wq / wp (set by render())
+    int q_rows;              // Q rows a block's shared table holds (set by render())
 };
 cudaError_t render(const RenderArgs& r, int n, cudaStream_t st);
 
