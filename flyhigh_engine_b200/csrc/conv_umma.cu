@@ -347,31 +347,38 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tslot;
+    // the warp index and the accumulator base as values the compiler sees as uniform across the warp
+    const int warp_u = __shfl_sync(0xffffffffu, warp, 0);
+    const uint32_t tbase_u = __shfl_sync(0xffffffffu, tbase, 0);
 
-    // ---- the MMAs: lane 0 of each of the first nis warps issues a contiguous half (or all) of the k-steps into its
-    //      own accumulator, each weight piece as soon as it has landed. A single issuing thread spends several times
-    //      a small-N MMA's tensor-pipe time on each issue; two issuers keep the pipe busy. ----
-    if (lane == 0 && warp < nis) {
+    // ---- the MMAs: each of the first nis warps issues a contiguous half (or all) of the k-steps into its own
+    //      accumulator, each weight piece as soon as it has landed. The whole warp runs the issue loop (every lane
+    //      forms the same descriptors, from values the compiler sees as warp-uniform, so they stay in uniform
+    //      registers) and lane 0 issues each MMA and the commit. Two issuers keep the pipe busy at small N. ----
+    if (warp_u < nis) {
         // k-step ks = tap * cslices + sl: A starts at the tap's shift within the halo planes plus two planes per
         // slice, B at ks * NG * 32 bytes. Both advance by adding to the descriptors' start-address field (address
         // >> 4; every address here is 16-byte aligned and below 2^18, so the field never carries).
         const uint32_t idesc = (1u << 4) | ((uint32_t)(ngw >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-        const int kb = warp * nsteps / nis, ke = (warp + 1) * nsteps / nis;
+        const int kb = warp_u * nsteps / nis, ke = (warp_u + 1) * nsteps / nis;
         const int tap = kb / cslices;
         int sl = kb - tap * cslices, kx = tap % 3;
         uint32_t tap_ofs = (uint32_t)((tap / 3) * UIW + kx);  // (ky * UIW + kx) * 16 bytes, in 16-byte units
         uint64_t ad = smem_desc(s0, UPLANE, UIW * 16) + tap_ofs + (uint32_t)(sl * (2 * UPLANE / 16));
         uint64_t bd = smem_desc(s0 + (uint32_t)wofs, 128, 256) + (uint32_t)(kb * (ngw * 2));
-        const uint32_t dt = tbase + (uint32_t)(warp * ngw);
+        const uint32_t dt = tbase_u + (uint32_t)(warp_u * ngw);
         int ks = kb;
-        for (int q = kb / kc; q < WCHUNKS && ks < ke && !failed; q++) {
+        for (int q = kb / kc; q < WCHUNKS && ks < ke; q++) {
+            if (__any_sync(0xffffffffu, failed != 0)) break;
             const int k1 = min(min((q + 1) * kc, nsteps), ke);
-            if (!mbar_wait_bounded(wbar0 + 8 * q, 0, wait_cycles)) {
-                failed = 1;
+            bool landed = false;
+            if (lane == 0) landed = mbar_wait_bounded(wbar0 + 8 * q, 0, wait_cycles);
+            if (!__shfl_sync(0xffffffffu, landed, 0)) {
+                if (lane == 0) failed = 1;
                 break;
             }
             for (; ks < k1; ks++) {
-                umma_f16(dt, ad, bd, idesc, ks > kb ? 1u : 0u);
+                if (lane == 0) umma_f16(dt, ad, bd, idesc, ks > kb ? 1u : 0u);
                 bd += (uint32_t)(ngw * 2);
                 if (++sl == cslices) {
                     sl = 0;
@@ -383,7 +390,7 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
                 }
             }
         }
-        umma_commit(mbar);  // arrives once every MMA above has completed (at once when none was issued)
+        if (lane == 0) umma_commit(mbar);  // arrives once every MMA above has completed (at once when none was issued)
     }
     __syncwarp();
     const bool mma_done = mbar_wait_bounded(mbar, 0, wait_cycles) && !failed;
@@ -599,6 +606,8 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma_p(const FhConvParams p, i
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tslot;
+    const int warp_u = __shfl_sync(0xffffffffu, warp, 0);  // warp-uniform to the compiler
+    const uint32_t tbase_u = __shfl_sync(0xffffffffu, tbase, 0);
     const uint32_t idesc = (1u << 4) | ((uint32_t)(ngw >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
     const bool vec_out = (p.out_cs & 7) == 0 && (p.out_bs & 7) == 0 && ((uintptr_t)p.out & 15) == 0;
     const bool vec_res = p.res && (p.res_cs & 7) == 0 && (p.res_bs & 7) == 0 && ((uintptr_t)p.res & 15) == 0;
@@ -663,23 +672,29 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma_p(const FhConvParams p, i
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
-        if (lane == 0 && warp < nis && !failed) {
-            const int kb = warp * nsteps / nis, ke = (warp + 1) * nsteps / nis;
+        // the whole issuing warp runs the loop on warp-uniform values (descriptors in uniform registers); lane 0
+        // issues each MMA and the commit
+        if (warp_u < nis && !__any_sync(0xffffffffu, failed != 0)) {
+            const int kb = warp_u * nsteps / nis, ke = (warp_u + 1) * nsteps / nis;
             const int tap = kb / cslices;
             int sl = kb - tap * cslices, kx = tap % 3;
             const uint32_t tap_ofs = (uint32_t)((tap / 3) * UIW + kx);
             uint64_t ad = smem_desc(sb, UPLANE, UIW * 16) + tap_ofs + (uint32_t)(sl * (2 * UPLANE / 16));
             uint64_t bd = smem_desc(s0 + (uint32_t)wofs, 128, 256) + (uint32_t)(kb * (ngw * 2));
-            const uint32_t dt = tbase + (uint32_t)(b * acc_cols + warp * ngw);
+            const uint32_t dt = tbase_u + (uint32_t)(b * acc_cols + warp_u * ngw);
             int ks = kb;
             for (int q = kb / kc; q < WCHUNKS && ks < ke; q++) {
                 const int k1 = min(min((q + 1) * kc, nsteps), ke);
-                if (!weights_in && !mbar_wait_bounded(wbar0 + 8 * q, 0, wait_cycles)) {
-                    failed = 1;
-                    break;
+                if (!weights_in) {
+                    bool landed = false;
+                    if (lane == 0) landed = mbar_wait_bounded(wbar0 + 8 * q, 0, wait_cycles);
+                    if (!__shfl_sync(0xffffffffu, landed, 0)) {
+                        if (lane == 0) failed = 1;
+                        break;
+                    }
                 }
                 for (; ks < k1; ks++) {
-                    umma_f16(dt, ad, bd, idesc, ks > kb ? 1u : 0u);
+                    if (lane == 0) umma_f16(dt, ad, bd, idesc, ks > kb ? 1u : 0u);
                     bd += (uint32_t)(ngw * 2);
                     if (++sl == cslices) {
                         sl = 0;
@@ -692,7 +707,7 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma_p(const FhConvParams p, i
                 }
             }
             weights_in = true;
-            if (!failed) umma_commit(mbar0 + 8 * b);  // arrives once this lane's MMAs above have completed
+            if (lane == 0 && !failed) umma_commit(mbar0 + 8 * b);  // arrives once lane 0's MMAs above have completed
         }
         __syncwarp();
         const bool pdone = prev >= 0 ? wait_set(b ^ 1) : true;

@@ -1377,13 +1377,37 @@ FH_DEV void sample_pair(const uint2* __restrict__ A, const uint2* __restrict__ B
     const uint2* a0 = A + (pya - 1) * w + (pxa - 1);
     const uint2* b0 = B + (pyb - 1) * w + (pxb - 1);
     float2 acc_b = make_float2(0.0f, 0.0f), acc_g = acc_b, acc_r = acc_b;
+    // the taps' raw words a row ahead: row j + 1's eight loads are issued before row j's conversions and sums
+    uint2 ua[4], ub[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        ua[k] = __ldg(a0 + k);
+        ub[k] = __ldg(b0 + k);
+    }
 #pragma unroll
     for (int j = 0; j < 4; j++) {
+        uint2 na[4], nb[4];
+        if (j < 3) {
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                na[k] = __ldg(a0 + (j + 1) * w + k);
+                nb[k] = __ldg(b0 + (j + 1) * w + k);
+            }
+        }
         float3 pa[4], pb[4];
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-            pa[k] = px3(a0 + j * w + k);
-            pb[k] = px3(b0 + j * w + k);
+            const float2 bga = __half22float2(*reinterpret_cast<const __half2*>(&ua[k].x));
+            const float2 bgb = __half22float2(*reinterpret_cast<const __half2*>(&ub[k].x));
+            pa[k] = make_float3(bga.x, bga.y, __low2float(*reinterpret_cast<const __half2*>(&ua[k].y)));
+            pb[k] = make_float3(bgb.x, bgb.y, __low2float(*reinterpret_cast<const __half2*>(&ub[k].y)));
+        }
+        if (j < 3) {
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                ua[k] = na[k];
+                ub[k] = nb[k];
+            }
         }
         float2 rb = __fmul2_rn(make_float2(pa[0].x, pb[0].x), cx0);
         float2 rg = __fmul2_rn(make_float2(pa[0].y, pb[0].y), cx0);
