@@ -1285,6 +1285,11 @@ FH_DEV float cub2(float x) {
     return ((a * x - 5.0f * a) * x + 8.0f * a) * x - 4.0f * a;
 }
 
+// the B, G, R halves of one f16-plane pixel as floats
+FH_DEV float3 h3(uint2 u) {
+    const float2 bg = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    return make_float3(bg.x, bg.y, __low2float(*reinterpret_cast<const __half2*>(&u.y)));
+}
 FH_DEV float3 px3(const uint2* p) {
     const uint2 u = __ldg(p);
     const float2 bg = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
@@ -1512,6 +1517,13 @@ __global__ void __launch_bounds__(256, 4) k_render(RenderArgs r) {
     for (int i = 0; i < RENDER_ROWS; i++) {
         const int y = yb + threadIdx.y + 8 * i;
         if (y >= r.h) break;
+        // the pixel's own values in both frames and its word (static_planes: the still test's 27-term mean es, 1
+        // where the static rules zero the still weight; the keep_static ramp kk; near), loaded first: they do not
+        // depend on the flow
+        const int here = y * r.w + x;  // x < w, y < h: no clamp
+        const int o = y * W + x;
+        const uint2 uha = __ldg(A + here), uhb = __ldg(B + here);
+        const uint32_t ow = own ? __ldg(own + o) : 0u;
         const float iy = ((float)y + 0.5f) * r.qsy - 0.5f;
         const int qy0 = (int)floorf(iy);
         const float qfy = iy - (float)qy0;
@@ -1545,12 +1557,7 @@ __global__ void __launch_bounds__(256, 4) k_render(RenderArgs r) {
         const float cr[3] = {r01.x, r01.y, v2r2.y};
         float bwa = wa_w, bwb = wb_w, rk = 1.0f, stillw = 0.0f, mean[3] = {0.0f, 0.0f, 0.0f};
         const float third = 1.0f / 3.0f;
-        const int here = y * r.w + x;  // x < w, y < h: no clamp
-        const float3 pa_here = px3(A + here), pb_here = px3(B + here);
-        const int o = y * W + x;
-        // the pixel's word (static_planes): the still test's 27-term mean es (1 where the static rules zero the still
-        // weight) and the keep_static ramp kk
-        const uint32_t ow = own ? __ldg(own + o) : 0u;
+        const float3 pa_here = h3(uha), pb_here = h3(uhb);
         if (r.flags & 2u) {
             const float es = own_es(ow);
             for (int c = 0; c < 3; c++) mean[c] = 0.5f * (comp(pa_here, c) + comp(pb_here, c));
