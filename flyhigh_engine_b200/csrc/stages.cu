@@ -1546,6 +1546,13 @@ __global__ void __launch_bounds__(256, 4) k_render(RenderArgs r) {
         const float inv = __frcp_rn(e0 + e1 + e2);
         const float wa_w = fmaf(0.5f, e2, e0) * inv, wb_w = fmaf(0.5f, e2, e1) * inv;
         const float gxa = (float)x + f[0], gya = (float)y + f[1], gxb = (float)x + f[2], gyb = (float)y + f[3];
+        // the static rules' probes (render_static's on_static): each sample rounded to its pixel (WGSL round(), half
+        // to even) and, inside the padded plane, that pixel's word loaded now, before the taps; near is its bit 31
+        const int pcxa = (int)rintf(gxa), pcya = (int)rintf(gya), pcxb = (int)rintf(gxb), pcyb = (int)rintf(gyb);
+        const bool ina = pcxa >= 0 && pcxa < W && pcya >= 0 && pcya < H;
+        const bool inb = pcxb >= 0 && pcxb < W && pcyb >= 0 && pcyb < H;
+        const uint32_t pwa = (age && ina) ? __ldg(own + pcya * W + pcxa) : 0u;
+        const uint32_t pwb = (age && inb) ? __ldg(own + pcyb * W + pcxb) : 0u;
         float3 sa3, sb3;
         if (r.cubic) {
             sample_pair(A, B, r.w, r.h, gxa, gya, gxb, gyb, sa3, sb3);
@@ -1575,16 +1582,15 @@ __global__ void __launch_bounds__(256, 4) k_render(RenderArgs r) {
         }
         float raw = 0.0f, kk = 0.0f;
         if (age) {
-            // near is bit 31 of the probed pixel's word
-            auto on_static = [&](float gx, float gy) {
-                const int cx = (int)rintf(gx), cy = (int)rintf(gy);  // WGSL round(): half to even
-                if (cx >= 0 && cx < W && cy >= 0 && cy < H) return (int)__ldg(own + cy * W + cx) < 0;
+            // outside the padded plane: an age >= min_age in the clamped 3 x 3 neighbourhood of the rounded sample
+            auto on_static = [&](int cx, int cy, bool in, uint32_t wd) {
+                if (in) return (int)wd < 0;
                 for (int dy = -1; dy <= 1; dy++)
                     for (int dx = -1; dx <= 1; dx++)
                         if ((float)age[clampi(cy + dy, 0, H - 1) * W + clampi(cx + dx, 0, W - 1)] >= r.min_age) return true;
                 return false;
             };
-            const bool sa = on_static(gxa, gya), sb = on_static(gxb, gyb);
+            const bool sa = on_static(pcxa, pcya, ina, pwa), sb = on_static(pcxb, pcyb, inb, pwb);
             if (sa && sb) {
                 rk = 0.0f;
                 raw = 1.0f;
