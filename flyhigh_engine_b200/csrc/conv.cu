@@ -58,7 +58,8 @@ __host__ __device__ inline int halo_w(int s) { return (TW - 1) * s + 3; }
 // the halo tile's bytes, rounded to 16
 __host__ __device__ inline int tile_bytes(int wm, int s, int cp) { return halo_h(wm, s) * halo_w(s) * (cp + 8) * 2; }
 
-// 16 bytes global -> shared, asynchronously; src_bytes 0 writes zeros (the source is not read)
+// 16 bytes global -> shared, asynchronously: src_bytes bytes are read and the rest of the 16 zero-filled (0: zeros,
+// the source is not read)
 __device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
@@ -217,7 +218,10 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
             scale = src.scale;
             narrow = src.cs < rel + 8;
         }
-        const bool plain = valid >= 8 && scale == 1.0f && !narrow;
+        // a partial chunk (channels past the source's count) copies its valid channels and the copy zero-fills the
+        // rest; only a scaled source's chunks are fixed after the copies land
+        const uint32_t cpy = 2u * (uint32_t)min(valid, narrow ? 4 : 8);
+        const bool plain = scale == 1.0f;
         const int npix = IH * IW;
         // every pixel of every chunk an asynchronous copy, all of them in flight at once: 16 bytes (8 for a 4-channel
         // pixel of a 3-channel image, the other 8 zero-filled), zero-filled outside the image. A chunk past every
@@ -235,15 +239,15 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
                 const __half* g = ok ? base + ((long long)iy * p.w + ix) * cs : base;
                 const uint32_t d = t0 + (uint32_t)(pix * P + c8) * 2;
                 if (!narrow) {
-                    cp_async16_zfill(d, g, ok ? 16u : 0u);
+                    cp_async16_zfill(d, g, ok ? cpy : 0u);
                 } else {
-                    cp_async8_zfill(d, g, ok ? 8u : 0u);
+                    cp_async8_zfill(d, g, ok ? cpy : 0u);
                     cp_async8_zfill(d + 8, base, 0u);
                 }
             }
         }
         cp_async_wait_all();
-        // partial chunks (channels past the source's count) and scaled sources: each thread fixes the pixels it copied
+        // scaled sources: each thread fixes the pixels it copied
         if (ch < nchunk && si >= 0 && !plain) {
             for (int pix = tid / lp; pix < npix; pix += pstep) {
                 uint4 v = *reinterpret_cast<const uint4*>(tile + pix * P + c8);

@@ -84,7 +84,8 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     return true;
 }
 
-// 16 bytes global -> shared, asynchronously; src_bytes 0 writes zeros (the source is not read)
+// 16 bytes global -> shared, asynchronously: src_bytes bytes are read and the rest of the 16 zero-filled (0: zeros,
+// the source is not read)
 __device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
@@ -299,7 +300,10 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
             scale = src.scale;
             narrow = src.cs < rel + 8;
         }
-        const bool plain = valid >= 8 && scale == 1.0f && !narrow;
+        // a partial chunk (channels past the source's count) copies its valid channels and the copy zero-fills the
+        // rest; only a scaled source's chunks are fixed after the copies land
+        const uint32_t cpy = 2u * (uint32_t)min(valid, narrow ? 4 : 8);
+        const bool plain = scale == 1.0f;
         constexpr int npix = UIH * UIW;
         // every pixel of every chunk an asynchronous copy, all of them in flight at once: 16 bytes (8 for a 4-channel
         // pixel of a 3-channel image, the other 8 zero-filled), zero-filled outside the image. A chunk past every
@@ -317,15 +321,15 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
                 const bool ok = iy >= 0 && iy < p.h && ix >= 0 && ix < p.w;
                 const __half* g = ok ? base + ((long long)iy * p.w + ix) * cs : base;
                 if (!narrow) {
-                    cp_async16_zfill(d, g, ok ? 16u : 0u);
+                    cp_async16_zfill(d, g, ok ? cpy : 0u);
                 } else {
-                    cp_async8_zfill(d, g, ok ? 8u : 0u);
+                    cp_async8_zfill(d, g, ok ? cpy : 0u);
                     cp_async8_zfill(d + 8, base, 0u);
                 }
             }
         }
         cp_async_wait_all();
-        // partial chunks (channels past the source's count) and scaled sources: each thread fixes the pixels it copied
+        // scaled sources: each thread fixes the pixels it copied
         if (ch < nchunk && si >= 0 && !plain) {
             uint8_t* plane = sm + ch * UPLANE;
             for (int pix = tid / lp; pix < npix; pix += pstep) {
@@ -491,6 +495,8 @@ __device__ __forceinline__ void ump_gather(const FhConvParams& p, uint8_t* plane
     const __half* base = src.p + (long long)n * src.bs + rel;
     const int cs = src.cs;
     const bool narrow = src.cs < rel + 8;
+    // a partial chunk copies its valid channels, the copy zero-filling the rest
+    const uint32_t cpy = 2u * (uint32_t)min(src.nc - rel, narrow ? 4 : 8);
     for (int pix = tid / lp; pix < npix; pix += pstep) {
         const int hy = pix / UIW, hx = pix - hy * UIW;
         const int iy = oy0 - 1 + hy, ix = ox0 - 1 + hx;
@@ -498,16 +504,16 @@ __device__ __forceinline__ void ump_gather(const FhConvParams& p, uint8_t* plane
         const bool ok = iy >= 0 && iy < p.h && ix >= 0 && ix < p.w;
         const __half* g = ok ? base + ((long long)iy * p.w + ix) * cs : base;
         if (!narrow) {
-            cp_async16_zfill(d, g, ok ? 16u : 0u);
+            cp_async16_zfill(d, g, ok ? cpy : 0u);
         } else {
-            cp_async8_zfill(d, g, ok ? 8u : 0u);
+            cp_async8_zfill(d, g, ok ? cpy : 0u);
             cp_async8_zfill(d + 8, base, 0u);
         }
     }
 }
 
-// after the gather's copies landed: partial chunks (channels past the source's count) and scaled sources, fixed by
-// the threads that copied them
+// after the gather's copies landed: scaled sources, fixed by the threads that copied them (a partial chunk's channels
+// past the source's count were zero-filled by the copies)
 __device__ __forceinline__ void ump_fix(const FhConvParams& p, uint8_t* plane0, int tid, int nchunk) {
     int lp = 1;
     while (lp < nchunk) lp <<= 1;
@@ -519,8 +525,7 @@ __device__ __forceinline__ void ump_fix(const FhConvParams& p, uint8_t* plane0, 
         if (rel < 0 || rel >= ((p.src[s_].nc + 7) & ~7)) continue;
         const int valid = p.src[s_].nc - rel;
         const float scale = p.src[s_].scale;
-        const bool narrow = p.src[s_].cs < rel + 8;
-        if (valid >= 8 && scale == 1.0f && !narrow) return;
+        if (scale == 1.0f) return;  // partial chunks were zero-filled by their copies
         uint8_t* plane = plane0 + ch * UPLANE;
         constexpr int npix = UIH * UIW;
         for (int pix = tid / lp; pix < npix; pix += pstep) {

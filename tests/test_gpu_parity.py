@@ -54,15 +54,16 @@ def _up8(c):
 
 
 def run_conv(torch, x_chw, w, bias, slope, stride, resid_chw=None, wm=0, ngroups=0, wait_cycles=0, extra_tx=0,
-             umma=False):
-    """One conv through fhk_conv3x3 on NHWC device buffers; returns CHW f16."""
+             umma=False, pad_fill=0.0):
+    """One conv through fhk_conv3x3 on NHWC device buffers; returns CHW f16. pad_fill: the value of the input's
+    channels past cin (the pixel pitch rounds cin up to 8, or 4)."""
     import flyhigh_engine_b200 as fh
     L = fh.lib()
     cin, h, wd = x_chw.shape
     cout = w.shape[0]
     cs = 4 if cin <= 4 else _up8(cin)
     ho, wo = (h - 1) // stride + 1, (wd - 1) // stride + 1
-    x = torch.zeros((h, wd, cs), dtype=torch.float16)
+    x = torch.full((h, wd, cs), pad_fill, dtype=torch.float16)
     x[:, :, :cin] = torch.from_numpy(np.ascontiguousarray(x_chw.transpose(1, 2, 0)))
     x = x.cuda()
     cp = (_up8(cin) + 15) // 16 * 16
@@ -141,6 +142,32 @@ def test_conv_matches_oracle(torch_cuda, h, w, cin, cout, stride, res, split):
     assert rel_l2(got, ref) < 2e-3
     # f32 accumulation order differs from the oracle's: a few f16 ulps at most
     assert np.abs(got - ref).max() <= 4e-3 * max(1.0, np.abs(ref).max())
+
+
+@pytest.mark.parametrize("cin,stride", [(155, 1), (14, 1), (3, 2), (36, 2)])
+@pytest.mark.parametrize("kernel", ["mma", "umma", "umma_persistent"])
+def test_conv_never_reads_padding_channels(torch_cuda, cin, stride, kernel):
+    """The channels past cin in an input pixel (its pitch rounds cin up to 8, or 4) hold NaN here: the halo copies read
+    only the valid channels of a partial 8-channel chunk and zero-fill the rest, so the output equals the one with
+    zeros there, bit for bit (a NaN read would reach every output through its zero weight)."""
+    import flyhigh_engine_b200 as fh
+    umma = kernel != "mma"
+    wm = 1 if kernel == "umma_persistent" else 0
+    cp = (_up8(cin) + 15) // 16 * 16
+    if umma and (stride != 1 or not fh.lib().fhk_conv_umma_fits(cp, 48, 1)):
+        pytest.skip("the tcgen05 kernel takes stride 1 only")
+    if wm == 1 and not fh.lib().fhk_conv_umma_persistent_fits(cp, 48):
+        pytest.skip("no persistent variant for this shape")
+    rng = np.random.default_rng(cin * 7 + stride)
+    h, w, cout = 60, 108, 48
+    x = rng.standard_normal((cin, h, w)).astype(np.float16)
+    wt = (rng.standard_normal((cout, cin, 3, 3)) / np.sqrt(9 * cin)).astype(np.float16).astype(np.float32)
+    bias = rng.standard_normal(cout).astype(np.float16).astype(np.float32) * 0.1
+    slope = np.full(cout, 0.1, np.float32)
+    ref = run_conv(torch_cuda, x, wt, bias, slope, stride, wm=wm, umma=umma, pad_fill=0.0)
+    got = run_conv(torch_cuda, x, wt, bias, slope, stride, wm=wm, umma=umma, pad_fill=float("nan"))
+    assert np.isfinite(got).all()
+    assert np.array_equal(got.view(np.uint16), ref.view(np.uint16))
 
 
 UMMA_CASES = [c for c in CONV_CASES if c[4] == 1] + [(30, 54, 96, 96, 1, True), (120, 216, 24, 24, 1, True)]
