@@ -188,16 +188,18 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
     pdl_wait();
     pdl_trigger();
 
-    // ---- halo tile: IH x IW pixels x cp channels, zero outside the image and beyond every source. The 128 threads
-    //      form groups of LP (a power of two >= the chunk count) lanes per pixel: a thread owns one 8-channel chunk
-    //      (its source, offset and view scale resolved once) and walks every (128 / LP)-th pixel ----
+    // ---- halo tile: IH x IW pixels x cp channels, zero outside the image and beyond every source. The threads form
+    //      groups of nchunk lanes per pixel: a thread owns one 8-channel chunk (its source, offset and view scale
+    //      resolved once) and walks every (threads / nchunk)-th pixel ----
     {
-        int lp = 1;
-        while (lp < nchunk) lp <<= 1;  // nchunk <= 128 (checked on the host)
-        const int ch = tid & (lp - 1), pstep = (WARPS * 32) / lp;
+        // one lane per 8-channel chunk of a pixel, WARPS * 32 / nchunk pixels at a time (nchunk <= 128); the last
+        // threads past a whole number of pixels idle
+        const int lp = nchunk;
+        const int ch = tid % lp, pstep = (WARPS * 32) / lp;
+        const bool lane_on = tid < lp * pstep;
         const int c8 = ch * 8;
         int si = -1, rel = 0;
-        if (ch < nchunk)
+        if (lane_on)
             for (int s_ = 0; s_ < p.nsrc; s_++) {
                 const int r_ = c8 - p.src[s_].slot;
                 if (r_ >= 0 && r_ < ((p.src[s_].nc + 7) & ~7)) {
@@ -227,7 +229,8 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
         // pixel of a 3-channel image, the other 8 zero-filled), zero-filled outside the image. A chunk past every
         // source is zeroed by plain stores.
         const uint32_t t0 = (uint32_t)__cvta_generic_to_shared(tile);
-        if (ch < nchunk) {
+        if (lane_on) {
+#pragma unroll 4
             for (int pix = tid / lp; pix < npix; pix += pstep) {
                 const int hy = pix / IW, hx = pix - hy * IW;
                 const int iy = iy0 + hy, ix = ix0 + hx;
@@ -248,7 +251,7 @@ __global__ void __launch_bounds__(WARPS * 32) conv3x3_mma(const FhConvParams p) 
         }
         cp_async_wait_all();
         // scaled sources: each thread fixes the pixels it copied
-        if (ch < nchunk && si >= 0 && !plain) {
+        if (lane_on && si >= 0 && !plain) {
             for (int pix = tid / lp; pix < npix; pix += pstep) {
                 uint4 v = *reinterpret_cast<const uint4*>(tile + pix * P + c8);
                 __half* hv = reinterpret_cast<__half*>(&v);

@@ -272,14 +272,16 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
     }
 
     // ---- halo tile: planes [chunk][UIH x UIW] of 16-byte pixels, zero outside the image and beyond every source.
-    //      LP lanes (a power of two >= the chunk count) per pixel, each owning one chunk ----
+    //      nchunk lanes per pixel, each owning one chunk ----
     {
-        int lp = 1;
-        while (lp < nchunk) lp <<= 1;
-        const int ch = tid & (lp - 1), pstep = 128 / lp;
+        // one lane per 8-channel chunk of a pixel, 128 / nchunk pixels at a time (nchunk <= 128); the last
+        // threads past a whole number of pixels idle
+        const int lp = nchunk;
+        const int ch = tid % lp, pstep = 128 / lp;
+        const bool lane_on = tid < lp * pstep;
         const int c8 = ch * 8;
         int si = -1, rel = 0;
-        if (ch < nchunk)
+        if (lane_on)
             for (int s_ = 0; s_ < p.nsrc; s_++) {
                 const int r_ = c8 - p.src[s_].slot;
                 if (r_ >= 0 && r_ < ((p.src[s_].nc + 7) & ~7)) {
@@ -308,8 +310,9 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
         // every pixel of every chunk an asynchronous copy, all of them in flight at once: 16 bytes (8 for a 4-channel
         // pixel of a 3-channel image, the other 8 zero-filled), zero-filled outside the image. A chunk past every
         // source is zeroed by plain stores.
-        if (ch < nchunk) {
+        if (lane_on) {
             uint8_t* plane = sm + ch * UPLANE;
+#pragma unroll 4
             for (int pix = tid / lp; pix < npix; pix += pstep) {
                 const int hy = pix / UIW, hx = pix - hy * UIW;
                 const int iy = oy0 - 1 + hy, ix = ox0 - 1 + hx;
@@ -330,7 +333,7 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
         }
         cp_async_wait_all();
         // scaled sources: each thread fixes the pixels it copied
-        if (ch < nchunk && si >= 0 && !plain) {
+        if (lane_on && si >= 0 && !plain) {
             uint8_t* plane = sm + ch * UPLANE;
             for (int pix = tid / lp; pix < npix; pix += pstep) {
                 uint4 v = *reinterpret_cast<const uint4*>(plane + pix * 16);
@@ -471,10 +474,12 @@ __host__ __device__ inline int ump_smem(int cp, int ngw) { return ump_barofs(cp,
 // (shared-window address): conv3x3_umma's gather, LP lanes per pixel, one chunk each; every copy issued, none waited
 __device__ __forceinline__ void ump_gather(const FhConvParams& p, uint8_t* plane0, uint32_t s_plane0, int tid, int n,
                                            int ox0, int oy0, int nchunk) {
-    int lp = 1;
-    while (lp < nchunk) lp <<= 1;
-    const int ch = tid & (lp - 1), pstep = 128 / lp;
-    if (ch >= nchunk) return;
+    // one lane per 8-channel chunk of a pixel, 128 / nchunk pixels at a time (nchunk <= 128); the last
+    // threads past a whole number of pixels idle
+    const int lp = nchunk;
+    const int ch = tid % lp, pstep = 128 / lp;
+    const bool lane_on = tid < lp * pstep;
+    if (!lane_on) return;
     const int c8 = ch * 8;
     int si = -1, rel = 0;
     for (int s_ = 0; s_ < p.nsrc; s_++) {
@@ -497,6 +502,7 @@ __device__ __forceinline__ void ump_gather(const FhConvParams& p, uint8_t* plane
     const bool narrow = src.cs < rel + 8;
     // a partial chunk copies its valid channels, the copy zero-filling the rest
     const uint32_t cpy = 2u * (uint32_t)min(src.nc - rel, narrow ? 4 : 8);
+#pragma unroll 4
     for (int pix = tid / lp; pix < npix; pix += pstep) {
         const int hy = pix / UIW, hx = pix - hy * UIW;
         const int iy = oy0 - 1 + hy, ix = ox0 - 1 + hx;
@@ -515,10 +521,12 @@ __device__ __forceinline__ void ump_gather(const FhConvParams& p, uint8_t* plane
 // after the gather's copies landed: scaled sources, fixed by the threads that copied them (a partial chunk's channels
 // past the source's count were zero-filled by the copies)
 __device__ __forceinline__ void ump_fix(const FhConvParams& p, uint8_t* plane0, int tid, int nchunk) {
-    int lp = 1;
-    while (lp < nchunk) lp <<= 1;
-    const int ch = tid & (lp - 1), pstep = 128 / lp;
-    if (ch >= nchunk) return;
+    // one lane per 8-channel chunk of a pixel, 128 / nchunk pixels at a time (nchunk <= 128); the last
+    // threads past a whole number of pixels idle
+    const int lp = nchunk;
+    const int ch = tid % lp, pstep = 128 / lp;
+    const bool lane_on = tid < lp * pstep;
+    if (!lane_on) return;
     const int c8 = ch * 8;
     for (int s_ = 0; s_ < p.nsrc; s_++) {
         const int rel = c8 - p.src[s_].slot;
