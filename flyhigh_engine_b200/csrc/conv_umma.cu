@@ -464,11 +464,14 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma(const FhConvParams p, int
 // output is bit for bit the same.
 //
 // Shared memory: two halo buffers | weights | bias, slopes | WCHUNKS + 2 mbarriers | TMEM base, flag.
+// nhb: halo buffers (2; 1 where the weights leave room for one halo tile only)
 __host__ __device__ inline int ump_halo(int cp) { return (cp / 8) * UPLANE; }
-__host__ __device__ inline int ump_wofs(int cp) { return 2 * ump_halo(cp); }
-__host__ __device__ inline int ump_bofs(int cp, int ngw) { return ump_wofs(cp) + umma_wbytes(cp, ngw); }
-__host__ __device__ inline int ump_barofs(int cp, int ngw) { return ump_bofs(cp, ngw) + ngw * 8; }
-__host__ __device__ inline int ump_smem(int cp, int ngw) { return ump_barofs(cp, ngw) + 8 * (WCHUNKS + 2) + 16; }
+__host__ __device__ inline int ump_wofs(int cp, int nhb) { return nhb * ump_halo(cp); }
+__host__ __device__ inline int ump_bofs(int cp, int ngw, int nhb) { return ump_wofs(cp, nhb) + umma_wbytes(cp, ngw); }
+__host__ __device__ inline int ump_barofs(int cp, int ngw, int nhb) { return ump_bofs(cp, ngw, nhb) + ngw * 8; }
+__host__ __device__ inline int ump_smem(int cp, int ngw, int nhb) {
+    return ump_barofs(cp, ngw, nhb) + 8 * (WCHUNKS + 2) + 16;
+}
 
 // the halo tile of output tile (ox0, oy0) of entry n into the planes at `plane0` (generic pointer) / `s_plane0`
 // (shared-window address): conv3x3_umma's gather, LP lanes per pixel, one chunk each; every copy issued, none waited
@@ -550,7 +553,7 @@ __device__ __forceinline__ void ump_fix(const FhConvParams& p, uint8_t* plane0, 
     }
 }
 
-__global__ void __launch_bounds__(128, 1) conv3x3_umma_p(const FhConvParams p, int np, int ngw, int nis) {
+__global__ void __launch_bounds__(128, 1) conv3x3_umma_p(const FhConvParams p, int np, int ngw, int nis, int nhb) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int cslices = p.cp / 16, nchunk = p.cp / 8, nsteps = 9 * cslices;
@@ -558,8 +561,8 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma_p(const FhConvParams p, i
     const int tx = (p.wo + UT_W - 1) / UT_W, ty = (p.ho + UT_H - 1) / UT_H;
     const int ntiles = tx * ty * p.n;
     const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(sm);
-    const int halo = ump_halo(p.cp), wofs = ump_wofs(p.cp), bofs = ump_bofs(p.cp, ngw);
-    const int barofs = ump_barofs(p.cp, ngw);
+    const int halo = ump_halo(p.cp), wofs = ump_wofs(p.cp, nhb), bofs = ump_bofs(p.cp, ngw, nhb);
+    const int barofs = ump_barofs(p.cp, ngw, nhb);
     float* sbias = reinterpret_cast<float*>(sm + bofs);
     float* sslope = sbias + ngw;
     const uint32_t wbar0 = s0 + barofs, mbar0 = s0 + barofs + 8 * WCHUNKS;  // mbar0 + 8 a: accumulator set a
@@ -675,11 +678,14 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma_p(const FhConvParams p, i
     // iteration) lands and is fixed; its MMAs are issued; the last tile's MMAs are waited for, which frees halo buffer
     // b ^ 1 for the next tile's gather (issued, not waited); then the last tile's epilogue runs from set b ^ 1 while
     // this tile's MMAs and the next tile's copies are in flight.
+    // With one halo buffer (nhb 1): the last tile's epilogue runs from set b ^ 1 while this tile's MMAs are in flight,
+    // then this tile's MMAs are waited for, which frees the buffer for the next tile's gather.
+    bool pdone_prev = true;  // nhb 1: the last tile's MMAs completed (waited for in its own iteration)
     for (int it = 0; t < ntiles; it++, t += gridDim.x) {
-        const int b = it & 1;
-        const uint32_t sb = s0 + (uint32_t)(b * halo);
+        const int b = it & 1, hb = nhb == 2 ? b : 0;
+        const uint32_t sb = s0 + (uint32_t)(hb * halo);
         cp_async_wait_all();
-        ump_fix(p, sm + b * halo, tid, nchunk);
+        ump_fix(p, sm + hb * halo, tid, nchunk);
         // written through the generic proxy, read by the tensor core through the async proxy
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         tc_fence_before();
@@ -723,19 +729,28 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma_p(const FhConvParams p, i
             if (lane == 0 && !failed) umma_commit(mbar0 + 8 * b);  // arrives once lane 0's MMAs above have completed
         }
         __syncwarp();
-        const bool pdone = prev >= 0 ? wait_set(b ^ 1) : true;
         const int tn = t + (int)gridDim.x;
-        if (tn < ntiles) {
-            const int n = tn / (tx * ty), r = tn - n * tx * ty;
-            ump_gather(p, sm + (b ^ 1) * halo, s0 + (uint32_t)((b ^ 1) * halo), tid, n, (r % tx) * UT_W,
-                       (r / tx) * UT_H, nchunk);
+        if (nhb == 2) {
+            const bool pdone = prev >= 0 ? wait_set(b ^ 1) : true;
+            if (tn < ntiles) {
+                const int n = tn / (tx * ty), r = tn - n * tx * ty;
+                ump_gather(p, sm + (b ^ 1) * halo, s0 + (uint32_t)((b ^ 1) * halo), tid, n, (r % tx) * UT_W,
+                           (r / tx) * UT_H, nchunk);
+            }
+            if (prev >= 0) epilogue(prev, b ^ 1, pdone);
+        } else {
+            if (prev >= 0) epilogue(prev, b ^ 1, pdone_prev);
+            pdone_prev = wait_set(b);
+            if (tn < ntiles) {
+                const int n = tn / (tx * ty), r = tn - n * tx * ty;
+                ump_gather(p, sm, s0, tid, n, (r % tx) * UT_W, (r / tx) * UT_H, nchunk);
+            }
         }
-        if (prev >= 0) epilogue(prev, b ^ 1, pdone);
         prev = t;
         prev_b = b;
     }
     if (prev >= 0) {
-        const bool done = wait_set(prev_b);
+        const bool done = nhb == 2 ? wait_set(prev_b) : pdone_prev;
         epilogue(prev, prev_b, done);
     }
     __syncthreads();
@@ -773,13 +788,13 @@ extern "C" int fhk_conv_umma_fits(int cp, int cout, int stride) {
     return umma_smem(cp, npad16(cout)) <= UMMA_SMEM_MAX ? 1 : 0;
 }
 
-// 1 when the persistent variant takes this layer: the tcgen05 kernel's conditions, with two halo buffers and the whole
-// weight slice in shared memory and two accumulator sets in tensor memory
+// 1 when the persistent variant takes this layer: the tcgen05 kernel's conditions, with a halo buffer (two where they
+// fit) and the whole weight slice in shared memory and two accumulator sets in tensor memory
 extern "C" int fhk_conv_umma_persistent_fits(int cp, int cout) {
     if (cp <= 0 || cp % 16 || cout < 1 || npad16(cout) > 256) return 0;
     const int np = npad16(cout), nis = np <= 128 ? 2 : 1;
     if (2 * np * nis > 512) return 0;
-    return ump_smem(cp, np) <= UMMA_SMEM_MAX ? 1 : 0;
+    return ump_smem(cp, np, 1) <= UMMA_SMEM_MAX ? 1 : 0;
 }
 
 extern "C" size_t fhk_conv_packed_elems_umma(int cout, int cp) { return (size_t)9 * (cp / 16) * npad16(cout) * 16; }
@@ -829,7 +844,9 @@ extern "C" int fhk_conv3x3_umma(const FhConvParams* pin, void* stream) {
         // memory, and 512 tensor-memory columns an SM), none without a tile
         if (!fhk_conv_umma_persistent_fits(p.cp, p.cout)) return (int)cudaErrorInvalidValue;
         const int nis = np <= 128 ? 2 : 1;
-        const size_t smem = (size_t)ump_smem(p.cp, np);
+        // two halo buffers where they fit beside the weights, else one
+        const int nhb = ump_smem(p.cp, np, 2) <= UMMA_SMEM_MAX ? 2 : 1;
+        const size_t smem = (size_t)ump_smem(p.cp, np, nhb);
         static bool configured_p = false;
         if (!configured_p) {
             cudaError_t e = cudaFuncSetAttribute(conv3x3_umma_p, cudaFuncAttributeMaxDynamicSharedMemorySize, UMMA_SMEM_MAX);
@@ -846,7 +863,8 @@ extern "C" int fhk_conv3x3_umma(const FhConvParams* pin, void* stream) {
         const long long tiles = (long long)((p.wo + UT_W - 1) / UT_W) * ((p.ho + UT_H - 1) / UT_H) * p.n;
         const int ctas = (int)std::max(1ll, std::min(tiles, (long long)sms * std::max(occ, 1)));
         p.wsmem = 1;
-        return (int)fhk::launch(conv3x3_umma_p, dim3(ctas, 1, 1), dim3(128), smem, (cudaStream_t)stream, p, np, np, nis);
+        return (int)fhk::launch(conv3x3_umma_p, dim3(ctas, 1, 1), dim3(128), smem, (cudaStream_t)stream, p, np, np, nis,
+                                nhb);
     }
     // output channels split over CTAs while the grid is small (each output's sum is unchanged): the widest group (a
     // multiple of 16 dividing the padded channels) that gives 148 CTAs, else the narrowest

@@ -199,10 +199,12 @@ def test_conv_umma_matches_oracle(torch_cuda, h, w, cin, cout, stride, res, wm):
 
 
 @pytest.mark.parametrize("h,w,cin,cout,res", [(60, 108, 48, 48, False), (60, 108, 48, 7, True), (37, 29, 24, 24, True),
-                                              (30, 54, 96, 96, True), (120, 216, 14, 24, False), (17, 9, 3, 36, False)])
+                                              (30, 54, 96, 96, True), (120, 216, 14, 24, False), (17, 9, 3, 36, False),
+                                              (60, 108, 155, 48, False)])
 def test_conv_umma_persistent_is_bit_exact(torch_cuda, h, w, cin, cout, res):
-    """The persistent variant (a CTA looping over tiles, halo and accumulators double-buffered) gives the bytes of the
-    one-tile-per-CTA kernel, over a batch of 5 entries (tiles of several entries per CTA)."""
+    """The persistent variant (a CTA looping over tiles, accumulators double-buffered, the halo too where two buffers
+    fit beside the weights: 155 -> 48 has one) gives the bytes of the one-tile-per-CTA kernel, over a batch of 5
+    entries (tiles of several entries per CTA)."""
     import flyhigh_engine_b200 as fh
     from flyhigh_engine_b200.kernels import Conv3x3
     torch = torch_cuda
