@@ -764,6 +764,170 @@ __global__ void __launch_bounds__(128, 1) conv3x3_umma_p(const FhConvParams p, i
     }
 }
 
+// ---- the streamed-weights variant: the layers whose whole weight slice does not fit beside the halo tile (coarse.c1,
+//      279 -> 96: 498 KB) ----
+//
+// One CTA per output tile, every output channel (N = np). The weights pass through a ring of R shared-memory slots of
+// S k-steps each: the producer (warp 3, lane 0) copies piece q (k-steps [q S, (q + 1) S)) into slot q % R once the
+// MMAs of piece q - R have drained from it (a tcgen05.commit per piece onto the slot's `empty` mbarrier); the issuer
+// (warp 0, lane 0, the warp running the loop on uniform values) waits for each piece's `full` mbarrier, issues its
+// MMAs into one accumulator and commits. The first R pieces are requested before the wait for the preceding kernel
+// (the weights are written only when the session is planned). Every wait is bounded.
+//
+// Shared memory: halo planes | R slots | bias, slopes | 2 R + 1 mbarriers (full, empty, accumulator) | TMEM base, flag.
+__host__ __device__ inline int umr_slot(int np, int S) { return S * np * 32; }
+__host__ __device__ inline int umr_bofs(int cp, int np, int S, int R) { return ump_halo(cp) + R * umr_slot(np, S); }
+__host__ __device__ inline int umr_barofs(int cp, int np, int S, int R) { return umr_bofs(cp, np, S, R) + np * 8; }
+__host__ __device__ inline int umr_smem(int cp, int np, int S, int R) {
+    return umr_barofs(cp, np, S, R) + 8 * (2 * R + 1) + 16;
+}
+constexpr int UMR_SLOTS = 3;
+
+__global__ void __launch_bounds__(128, 1) conv3x3_umma_ring(const FhConvParams p, int np, int S, int R) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int cslices = p.cp / 16, nchunk = p.cp / 8, nsteps = 9 * cslices;
+    const int npieces = (nsteps + S - 1) / S;
+    const int n = blockIdx.z, ox0 = blockIdx.x * UT_W, oy0 = blockIdx.y * UT_H;
+    const uint32_t s0 = (uint32_t)__cvta_generic_to_shared(sm);
+    const int rofs = ump_halo(p.cp), slot_bytes = umr_slot(np, S), bofs = umr_bofs(p.cp, np, S, R);
+    const int barofs = umr_barofs(p.cp, np, S, R);
+    float* sbias = reinterpret_cast<float*>(sm + bofs);
+    float* sslope = sbias + np;
+    const uint32_t full0 = s0 + barofs, empty0 = full0 + 8 * R, mbar = full0 + 16 * R;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + barofs + 8 * (2 * R + 1));
+    volatile int& failed = *reinterpret_cast<int*>(sm + barofs + 8 * (2 * R + 1) + 4);
+    const long long wait_cycles = p.wait_cycles > 0 ? p.wait_cycles : 2000000000ll;
+    const uint32_t ncols = (uint32_t)tmem_cols(np);
+    const bool prelu = p.slope != nullptr;
+    const char* wsrc = reinterpret_cast<const char*>(p.wpack);
+    // piece q: its k-steps' bytes, from k-step q S of the packed rows (np * 32 bytes a k-step)
+    auto piece_bytes = [&](int q) { return (uint32_t)((min((q + 1) * S, nsteps) - q * S) * np * 32); };
+    auto request = [&](int q) {  // producer lane: piece q into slot q % R
+        const uint32_t full = full0 + 8 * (q % R);
+        mbar_expect_tx(full, piece_bytes(q) + (q == 0 ? (uint32_t)p.test_extra_tx : 0u));
+        bulk_g2s(s0 + (uint32_t)(rofs + (q % R) * slot_bytes), wsrc + (size_t)q * S * np * 32, piece_bytes(q), full);
+    };
+
+    for (int i = tid; i < np; i += 128) {
+        sbias[i] = i < p.cout ? p.bias[i] : 0.0f;
+        sslope[i] = (prelu && i < p.cout) ? p.slope[i] : 1.0f;
+    }
+    if (tid == 0) {
+        for (int r = 0; r < R; r++) {
+            mbar_init(full0 + 8 * r, 1);
+            mbar_init(empty0 + 8 * r, 1);
+        }
+        mbar_init(mbar, 1);
+        mbar_init_fence();
+        failed = 0;
+    }
+    __syncthreads();
+    if (warp == 3 && lane == 0)
+        for (int q = 0; q < min(R, npieces); q++) request(q);
+    pdl_wait();
+    pdl_trigger();
+    if (warp == 0) {
+        tmem_alloc((uint32_t)__cvta_generic_to_shared(tslot), ncols);
+        tmem_relinquish();
+    }
+    ump_gather(p, sm, s0, tid, n, ox0, oy0, nchunk);
+    cp_async_wait_all();
+    ump_fix(p, sm, tid, nchunk);
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+    const int warp_u = __shfl_sync(0xffffffffu, warp, 0);
+    const uint32_t tbase_u = __shfl_sync(0xffffffffu, tbase, 0);
+
+    if (warp_u == 0) {
+        // the issuer: k-step ks = tap * cslices + sl; A advances as in conv3x3_umma, B restarts at each piece's slot
+        const uint32_t idesc = (1u << 4) | ((uint32_t)(np >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+        uint64_t ad = smem_desc(s0, UPLANE, UIW * 16);
+        int sl = 0, kx = 0, ks = 0;
+        for (int q = 0; q < npieces; q++) {
+            bool landed = false;
+            if (lane == 0) landed = mbar_wait_bounded(full0 + 8 * (q % R), (uint32_t)((q / R) & 1), wait_cycles);
+            if (!__shfl_sync(0xffffffffu, landed, 0)) {
+                if (lane == 0) failed = 1;
+                break;
+            }
+            tc_fence_after();
+            uint64_t bd = smem_desc(s0 + (uint32_t)(rofs + (q % R) * slot_bytes), 128, 256);
+            const int k1 = min((q + 1) * S, nsteps);
+            for (; ks < k1; ks++) {
+                if (lane == 0) umma_f16(tbase_u, ad, bd, idesc, ks > 0 ? 1u : 0u);
+                bd += (uint32_t)(np * 2);
+                if (++sl == cslices) {
+                    sl = 0;
+                    const uint32_t step = ++kx == 3 ? UIW - 2 : 1;
+                    if (kx == 3) kx = 0;
+                    ad += (uint64_t)((long long)step - (long long)((cslices - 1) * (2 * UPLANE / 16)));
+                } else {
+                    ad += (uint32_t)(2 * UPLANE / 16);
+                }
+            }
+            if (lane == 0) umma_commit(empty0 + 8 * (q % R));  // the slot is free once these MMAs have read it
+        }
+        if (lane == 0) umma_commit(mbar);  // the accumulator: every MMA above
+        __syncwarp();
+    } else if (warp_u == 3) {
+        // the producer: piece q once piece q - R has drained from its slot
+        for (int q = R; q < npieces; q++) {
+            bool drained = false;
+            if (lane == 0)
+                drained = !failed && mbar_wait_bounded(empty0 + 8 * (q % R), (uint32_t)((q / R - 1) & 1), wait_cycles);
+            if (!__shfl_sync(0xffffffffu, drained, 0)) {
+                if (lane == 0) failed = 1;
+                break;
+            }
+            if (lane == 0) request(q);
+        }
+        __syncwarp();
+    }
+    const bool mma_done = mbar_wait_bounded(mbar, 0, wait_cycles) && !failed;
+    tc_fence_after();
+
+    // the epilogue: warp w holds accumulator lanes 32 w .. 32 w + 31 = tile pixels m (row m / 8, column m % 8)
+    const int m = warp * 32 + lane;
+    const int oy = oy0 + (m >> 3), ox = ox0 + (m & 7);
+    const bool inside = oy < p.ho && ox < p.wo;
+    __half* __restrict__ out = p.out + (long long)n * p.out_bs + ((long long)oy * p.wo + ox) * p.out_cs;
+    const __half* __restrict__ res =
+        p.res ? p.res + (long long)n * p.res_bs + ((long long)oy * p.wo + ox) * p.res_cs : nullptr;
+    const bool vec_out = (p.out_cs & 7) == 0 && (p.out_bs & 7) == 0 && ((uintptr_t)p.out & 15) == 0;
+    const bool vec_res = p.res && (p.res_cs & 7) == 0 && (p.res_bs & 7) == 0 && ((uintptr_t)p.res & 15) == 0;
+    for (int c0 = 0; c0 < np; c0 += 16) {
+        float v[16];
+        {
+            uint32_t r[16];
+            tmem_ld16_async(tbase + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[j] = __uint_as_float(r[j]);
+        }
+        if (!inside || !mma_done) continue;
+        if (p.res) {
+            if (p.epi == 1) umma_epilogue16<true, true>(v, sbias + c0, sslope + c0, prelu, res, vec_res, c0, p.cout, out, vec_out);
+            else umma_epilogue16<true, false>(v, sbias + c0, sslope + c0, prelu, res, vec_res, c0, p.cout, out, vec_out);
+        } else {
+            if (p.epi == 1) umma_epilogue16<false, true>(v, sbias + c0, sslope + c0, prelu, res, vec_res, c0, p.cout, out, vec_out);
+            else umma_epilogue16<false, false>(v, sbias + c0, sslope + c0, prelu, res, vec_res, c0, p.cout, out, vec_out);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (failed) {
+        // MMAs or weight copies may still be in flight: every thread gives them the bound before the CTA ends
+        const long long t0 = clock64();
+        while (clock64() - t0 < wait_cycles) {
+        }
+    }
+    if (warp == 0) tmem_dealloc(tbase, ncols);
+}
+
 }  // namespace
 
 // the timeouts of this kernel's waits (fhk_conv_wait_timeouts adds them to conv3x3_mma's)
@@ -780,12 +944,14 @@ long long umma_wait_timeouts(int reset) {
 }  // namespace fhk
 
 constexpr int UMMA_SMEM_MAX = 227 * 1024;
-// 1 when the tcgen05 kernel takes this layer: stride 1, N <= 256, and its halo tile plus the whole weight slice fit
-// in shared memory. (A layer whose weights fit only split over channel groups, such as coarse.c1's 279 -> 96, runs
-// longer here than on conv3x3_mma: every CTA then issues 126 small-N MMAs, and the MMA issue rate bounds it.)
+// 1 when the tcgen05 kernel takes this layer: stride 1, N <= 256, and its halo tile with the whole weight slice, or
+// with a ring of weight pieces (the streamed-weights variant, for a slice such as coarse.c1's 279 -> 96 at 498 KB),
+// fits in shared memory.
 extern "C" int fhk_conv_umma_fits(int cp, int cout, int stride) {
     if (stride != 1 || cp <= 0 || cp % 16 || cout < 1 || npad16(cout) > 256) return 0;
-    return umma_smem(cp, npad16(cout)) <= UMMA_SMEM_MAX ? 1 : 0;
+    if (umma_smem(cp, npad16(cout)) <= UMMA_SMEM_MAX) return 1;
+    // else the streamed-weights variant: the halo tile and a ring of UMMA_SLOTS slots of one k-step at least
+    return umr_smem(cp, npad16(cout), 1, UMR_SLOTS) <= UMMA_SMEM_MAX ? 1 : 0;
 }
 
 // 1 when the persistent variant takes this layer: the tcgen05 kernel's conditions, with a halo buffer (two where they
@@ -865,6 +1031,24 @@ extern "C" int fhk_conv3x3_umma(const FhConvParams* pin, void* stream) {
         p.wsmem = 1;
         return (int)fhk::launch(conv3x3_umma_p, dim3(ctas, 1, 1), dim3(128), smem, (cudaStream_t)stream, p, np, np, nis,
                                 nhb);
+    }
+    if (umma_smem(p.cp, np) > UMMA_SMEM_MAX) {
+        // the streamed-weights variant: every output channel in one CTA, pieces of as many k-steps as the ring's
+        // slots leave room for
+        const int per_step = np * 32, nsteps = 9 * (p.cp / 16);
+        int S = (UMMA_SMEM_MAX - umr_smem(p.cp, np, 0, UMR_SLOTS)) / (UMR_SLOTS * per_step);
+        S = std::min(S, (nsteps + UMR_SLOTS - 1) / UMR_SLOTS);
+        if (S < 1) return (int)cudaErrorInvalidValue;
+        const size_t smem = (size_t)umr_smem(p.cp, np, S, UMR_SLOTS);
+        static bool configured_r = false;
+        if (!configured_r) {
+            cudaError_t e = cudaFuncSetAttribute(conv3x3_umma_ring, cudaFuncAttributeMaxDynamicSharedMemorySize, UMMA_SMEM_MAX);
+            if (e != cudaSuccess) return (int)e;
+            configured_r = true;
+        }
+        p.wsmem = 2;
+        const dim3 grid((p.wo + UT_W - 1) / UT_W, (p.ho + UT_H - 1) / UT_H, p.n);
+        return (int)fhk::launch(conv3x3_umma_ring, grid, dim3(128), smem, (cudaStream_t)stream, p, np, S, UMR_SLOTS);
     }
     // output channels split over CTAs while the grid is small (each output's sum is unchanged): the widest group (a
     // multiple of 16 dividing the padded channels) that gives 148 CTAs, else the narrowest

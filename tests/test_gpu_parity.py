@@ -144,7 +144,7 @@ def test_conv_matches_oracle(torch_cuda, h, w, cin, cout, stride, res, split):
     assert np.abs(got - ref).max() <= 4e-3 * max(1.0, np.abs(ref).max())
 
 
-@pytest.mark.parametrize("cin,stride", [(155, 1), (14, 1), (3, 2), (36, 2)])
+@pytest.mark.parametrize("cin,stride", [(155, 1), (14, 1), (3, 2), (36, 2), (279, 1)])
 @pytest.mark.parametrize("kernel", ["mma", "umma", "umma_persistent"])
 def test_conv_never_reads_padding_channels(torch_cuda, cin, stride, kernel):
     """The channels past cin in an input pixel (its pitch rounds cin up to 8, or 4) hold NaN here: the halo copies read
@@ -232,11 +232,12 @@ def test_conv_umma_persistent_is_bit_exact(torch_cuda, h, w, cin, cout, res):
 
 
 @pytest.mark.parametrize("h,w,cin,cout,umma,wm", [(60, 108, 48, 48, False, 0), (30, 54, 279, 96, False, 0),
-                                                  (60, 108, 48, 48, True, 0), (60, 108, 48, 48, True, 1)])
+                                                  (60, 108, 48, 48, True, 0), (60, 108, 48, 48, True, 1),
+                                                  (30, 54, 279, 96, True, 0)])
 def test_conv_weight_wait_runs_out(torch_cuda, h, w, cin, cout, umma, wm):
     """Failure detection without a fault: the weight staging's mbarrier is made to expect 16 bytes that no copy brings
-    (whole slice: 48 -> 48; streamed ring: 279 -> 96), so every wait runs out after its bound; the kernel counts the
-    timeouts, finishes and leaves the context usable, and the next normal launch is exact again."""
+    (whole slice: 48 -> 48; streamed ring: 279 -> 96, on both kernels), so every wait runs out after its bound; the
+    kernel counts the timeouts, finishes and leaves the context usable, and the next normal launch is exact again."""
     import flyhigh_engine_b200 as fh
     from oracle import oracle
     L = fh.lib()
