@@ -58,6 +58,9 @@ def parse():
     p.add_argument("--cpu-sample", type=int, default=3, help="intervals of the CPU baseline sample")
     p.add_argument("--batch", type=int, default=16,
                    help="intervals per launch (fh_session_create_batched); 1 = one interval per launch")
+    p.add_argument("--e2e-ring", type=int, default=32, help="pinned host buffers the e2e loop reads generated frames into")
+    p.add_argument("--e2e-lag", type=int, default=2,
+                   help="the e2e loop reads each interval's frame this many batches after submitting it")
     return p.parse_args()
 
 
@@ -337,10 +340,10 @@ def main():
         outbuf = torch.empty((H, W, 4), dtype=torch.uint8).pin_memory()
         out_np = outbuf.numpy()
 
-        lag = 1 if args.batch <= 1 else 2 * args.batch
+        lag = 1 if args.batch <= 1 else args.e2e_lag * args.batch
         outs = [out] + [s.add_output() for _ in range(2 * lag - 1)]
 
-        RING = 32  # host buffers of generated frames (a second of output at 30 fps: what a host queues for display)
+        RING = args.e2e_ring  # host buffers of generated frames (32: a second of output at 30 fps, what a host queues)
         ring = torch.empty((RING, H, W, 4), dtype=torch.uint8).pin_memory()
         ring_np = [ring[k].numpy() for k in range(RING)]
 
