@@ -59,8 +59,9 @@ def parse():
     p.add_argument("--batch", type=int, default=16,
                    help="intervals per launch (fh_session_create_batched); 1 = one interval per launch")
     p.add_argument("--e2e-ring", type=int, default=32, help="pinned host buffers the e2e loop reads generated frames into")
-    p.add_argument("--e2e-lag", type=int, default=2,
-                   help="the e2e loop reads each interval's frame this many batches after submitting it")
+    p.add_argument("--e2e-lag", type=int, default=3,
+                   help="the e2e loop reads each interval's frame this many batches after submitting it (3 measured "
+                        "about 5 %% above 2: a third batch in flight covers the copy of the last one)")
     return p.parse_args()
 
 
