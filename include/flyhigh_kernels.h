@@ -69,14 +69,17 @@ int fhk_conv3x3(const FhConvParams* p, int stride, void* stream);
  * last reset, on the current device; reset != 0 zeroes the count. Returns -1 when the count cannot be read. */
 long long fhk_conv_wait_timeouts(int reset);
 /* The same convolution (stride 1) on the 5th-generation tensor cores: tcgen05.mma into a tensor-memory f32
- * accumulator, a CTA per 8 x 16 output pixels and all output channels, the halo tile gathered into shared memory and
- * the whole weight slice staged by one bulk copy. Weights in fhk_conv_pack_weights_umma order; p->ho == p->h and
- * p->wo == p->w; ngroups is ignored. fhk_conv_umma_fits tells whether a layer fits (stride 1, Cout <= 256, shared
- * memory). The f32 summation order differs from fhk_conv3x3's.
- * p->wm == 1 selects the persistent variant (where fhk_conv_umma_persistent_fits): as many CTAs as the GPU holds at
- * once, each staging the weights once and looping over tiles, the next tile's halo gathered and the last tile's
- * epilogue run while the current tile's MMAs execute (two halo buffers, two accumulator sets). Its outputs are bit for
- * bit those of wm == 0. */
+ * accumulator, a CTA per 8 x 16 output pixels and all output channels (or a slice of them while the grid is small),
+ * the halo tile gathered into shared memory and the whole weight slice staged by bulk copies. Where the whole slice
+ * does not fit beside the halo tile, the weights stream through a ring of three shared-memory slots refilled as the
+ * MMAs drain them (one accumulator; its f32 order differs from the whole-slice kernel's). Weights in
+ * fhk_conv_pack_weights_umma order; p->ho == p->h and p->wo == p->w; ngroups is ignored. fhk_conv_umma_fits tells
+ * whether a layer fits either way (stride 1, Cout <= 256, shared memory). The f32 summation order differs from
+ * fhk_conv3x3's.
+ * p->wm == 1 selects the persistent variant (where fhk_conv_umma_persistent_fits: the whole weight slice and one halo
+ * tile fit): as many CTAs as the GPU holds at once, each staging the weights once and looping over tiles, the next
+ * tile's halo gathered and the last tile's epilogue run while the current tile's MMAs execute (two halo buffers where
+ * they fit, two accumulator sets). Its outputs are bit for bit those of wm == 0 with the whole slice. */
 int fhk_conv3x3_umma(const FhConvParams* p, void* stream);
 int fhk_conv_umma_fits(int cp, int cout, int stride);
 int fhk_conv_umma_persistent_fits(int cp, int cout);
