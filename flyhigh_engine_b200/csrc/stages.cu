@@ -974,15 +974,27 @@ __global__ void k_gm_cost(GmArgs g) {
         const float bot = lum(s, y1c, x0c) * (1.0f - ax) + lum(s, y1c, x1c) * ax;
         return top * (1.0f - ay) + bot * ay;
     };
-    auto flow8 = [&](int c, float rx, float ry) {
+    // the flow's four channels at (rx, ry): the four corners' channels 0-3 in one 8-byte load each (the pixel pitch is
+    // 8 halves), then each channel's bilinear with the same weights and order as one channel alone
+    auto flow8x4 = [&](float rx, float ry, float (&f)[4]) {
         const float ix = (rx + 0.5f) * (float)w8 / (float)w - 0.5f, iy = (ry + 0.5f) * (float)h8 / (float)h - 0.5f;
         const int x0 = (int)floorf(ix), y0 = (int)floorf(iy);
         const float fx = ix - (float)x0, fy = iy - (float)y0;
         const int x0c = clampi(x0, 0, w8 - 1), x1c = clampi(x0 + 1, 0, w8 - 1);
         const int y0c = clampi(y0, 0, h8 - 1), y1c = clampi(y0 + 1, 0, h8 - 1);
-        const float top = h2f(fl[((long long)y0c * w8 + x0c) * 8 + c]) * (1.0f - fx) + h2f(fl[((long long)y0c * w8 + x1c) * 8 + c]) * fx;
-        const float bot = h2f(fl[((long long)y1c * w8 + x0c) * 8 + c]) * (1.0f - fx) + h2f(fl[((long long)y1c * w8 + x1c) * 8 + c]) * fx;
-        return top * (1.0f - fy) + bot * fy;
+        const uint2* F = reinterpret_cast<const uint2*>(fl);
+        const uint2 c00 = __ldg(F + ((long long)y0c * w8 + x0c) * 2), c01 = __ldg(F + ((long long)y0c * w8 + x1c) * 2);
+        const uint2 c10 = __ldg(F + ((long long)y1c * w8 + x0c) * 2), c11 = __ldg(F + ((long long)y1c * w8 + x1c) * 2);
+        auto ch = [](uint2 u, int c) {
+            const uint32_t wd = c < 2 ? u.x : u.y;
+            return __half2float(__ushort_as_half((unsigned short)((c & 1) ? wd >> 16 : wd & 0xffffu)));
+        };
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const float top = ch(c00, c) * (1.0f - fx) + ch(c01, c) * fx;
+            const float bot = ch(c10, c) * (1.0f - fx) + ch(c11, c) * fx;
+            f[c] = top * (1.0f - fy) + bot * fy;
+        }
     };
     auto aff = [&](int c, float rx, float ry) {
         const float ix = (rx + 0.5f) * (float)w8 / (float)w - 0.5f, iy = (ry + 0.5f) * (float)h8 / (float)h - 0.5f;
@@ -991,7 +1003,9 @@ __global__ void k_gm_cost(GmArgs g) {
     };
     const float ds = 2.0f;
     const float rx = ((float)x + 0.5f) * ds - 0.5f, ry = ((float)y + 0.5f) * ds - 0.5f;
-    const float f0x = flow8(0, rx, ry), f0y = flow8(1, rx, ry), f1x = flow8(2, rx, ry), f1y = flow8(3, rx, ry);
+    float fq[4];
+    flow8x4(rx, ry, fq);
+    const float f0x = fq[0], f0y = fq[1], f1x = fq[2], f1y = fq[3];
     const float cm = fabsf(samp(A, rx + f0x, ry + f0y) - samp(B, rx + f1x, ry + f1y));
     const float g0x = aff(0, rx, ry), g0y = aff(1, rx, ry), g1x = aff(2, rx, ry), g1y = aff(3, rx, ry);
     const float wm = (float)w - 1.0f, hm = (float)h - 1.0f;
@@ -1049,6 +1063,52 @@ __global__ void k_box_v(const float* src, long long src_bs, float* dst, long lon
     }
     dst[n * dst_bs + (long long)ch * h * w + (long long)y * w + x] = acc / (float)(2 * r + 1);
 }
+// k_box_v with the radius a template parameter (RR <= 16): a thread forms BOXV_ROWS consecutive outputs of its column
+// from one register window of BOXV_ROWS + 2 RR loaded values; each output sums its 2 RR + 1 taps in the same order as
+// k_box_v (top to bottom, clamped rows), then / (2 RR + 1)
+constexpr int BOXV_ROWS = 8;
+template <int RR>
+__global__ void __launch_bounds__(256) k_box_v_w(const float* src, long long src_bs, float* dst, long long dst_bs, int c,
+                                                 int h, int w) {
+    pdl_wait();
+    pdl_trigger();
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y0 = (blockIdx.y * blockDim.y + threadIdx.y) * BOXV_ROWS;
+    const int n = blockIdx.z / c, ch = blockIdx.z - n * c;
+    if (x >= w || y0 >= h) return;
+    const float* plane = src + n * src_bs + (long long)ch * h * w;
+    float v[BOXV_ROWS + 2 * RR];
+#pragma unroll
+    for (int k = 0; k < BOXV_ROWS + 2 * RR; k++) v[k] = __ldg(plane + (long long)clampi(y0 - RR + k, 0, h - 1) * w + x);
+    float* out = dst + n * dst_bs + (long long)ch * h * w + x;
+#pragma unroll
+    for (int k = 0; k < BOXV_ROWS; k++) {
+        if (y0 + k >= h) break;
+        float acc = 0.0f;
+#pragma unroll
+        for (int d = 0; d <= 2 * RR; d++) acc = acc + v[k + d];
+        out[(long long)(y0 + k) * w] = acc / (float)(2 * RR + 1);
+    }
+}
+template <int RR>
+cudaError_t box_v_w(const float* src, long long src_bs, float* dst, long long dst_bs, int c, int h, int w, int nz,
+                    cudaStream_t st) {
+    return launch(k_box_v_w<RR>, grid2(w, (h + BOXV_ROWS - 1) / BOXV_ROWS, nz, 32, 8), dim3(32, 8), 0, st, src, src_bs,
+                  dst, dst_bs, c, h, w);
+}
+// the vertical box pass: the register-window kernel for radii up to 16, else k_box_v
+cudaError_t box_v(const float* src, long long src_bs, float* dst, long long dst_bs, int c, int h, int w, int r, int nz,
+                  cudaStream_t st) {
+    switch (r) {
+#define FH_BOXV(R) \
+    case R: return box_v_w<R>(src, src_bs, dst, dst_bs, c, h, w, nz, st);
+        FH_BOXV(1) FH_BOXV(2) FH_BOXV(3) FH_BOXV(4) FH_BOXV(5) FH_BOXV(6) FH_BOXV(7) FH_BOXV(8)
+        FH_BOXV(9) FH_BOXV(10) FH_BOXV(11) FH_BOXV(12) FH_BOXV(13) FH_BOXV(14) FH_BOXV(15) FH_BOXV(16)
+#undef FH_BOXV
+        default:
+            return launch(k_box_v, grid2(w, h, nz, 32, 8), dim3(32, 8), 0, st, src, src_bs, dst, dst_bs, c, h, w, r);
+    }
+}
+
 // gm_select.wgsl:12-15: the cost cell that select sample j (of w8) reads, along one axis of hc or wc cells
 FH_DEV int gm_cell(int j, int cells, int n8) { return clampi((int)floorf(((float)j + 0.5f) * (float)cells / (float)n8), 0, cells - 1); }
 
@@ -2110,10 +2170,11 @@ cudaError_t gmhs_fit(const GmArgs& g, int n, cudaStream_t st) {
 }
 cudaError_t gmhs_maps(const GmArgs& g, int n, cudaStream_t st) {
     if (g.w8 > g.wc) return cudaErrorInvalidValue;  // the column planes live in tmp's [5][hc][wc] per entry
+    if ((uintptr_t)g.fv % 8 || g.fv_bs % 4) return cudaErrorMisalignedAddress;  // k_gm_cost's 8-byte flow loads
     { const cudaError_t e_ = launch(k_gm_cost, grid2(g.wc, g.hc, n, 32, 8), dim3(32, 8), 0, st, g); if (e_ != cudaSuccess) return e_; }
     const long long bs5 = 5LL * g.hc * g.wc, bs6 = 6LL * g.hc * g.wc;
     { const cudaError_t e_ = launch(k_box_h, grid2(g.wc, g.hc, 3 * n, 32, 8), dim3(32, 8), 0, st, (const float*)g.maps, bs6, g.tmp, bs5, 3, g.hc, g.wc, g.r_blk); if (e_ != cudaSuccess) return e_; }
-    { const cudaError_t e_ = launch(k_box_v, grid2(g.wc, g.hc, 3 * n, 32, 8), dim3(32, 8), 0, st, (const float*)g.tmp, bs5, g.maps, bs6, 3, g.hc, g.wc, g.r_blk); if (e_ != cudaSuccess) return e_; }
+    { const cudaError_t e_ = box_v((const float*)g.tmp, bs5, g.maps, bs6, 3, g.hc, g.wc, g.r_blk, 3 * n, st); if (e_ != cudaSuccess) return e_; }
     { const cudaError_t e_ = launch(k_box_h_cols, grid2(g.w8, g.hc, 5 * n, 32, 8), dim3(32, 8), 0, st, g, bs5); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
 }
