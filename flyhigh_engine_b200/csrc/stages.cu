@@ -1109,6 +1109,57 @@ cudaError_t box_v(const float* src, long long src_bs, float* dst, long long dst_
     }
 }
 
+// k_box_h with the radius a template parameter (RR <= 16): a thread forms BOXH_COLS consecutive outputs of its row
+// from one register window of BOXH_COLS + 2 RR loaded values; each output sums its taps left to right (clamped columns),
+// then / (2 RR + 1), as k_box_h does
+constexpr int BOXH_COLS = 4;
+template <int RR>
+__global__ void __launch_bounds__(256) k_box_h_w(const float* src, long long src_bs, float* dst, long long dst_bs, int c,
+                                                 int h, int w) {
+    pdl_wait();
+    pdl_trigger();
+    const int x0 = (blockIdx.x * blockDim.x + threadIdx.x) * BOXH_COLS, y = blockIdx.y * blockDim.y + threadIdx.y;
+    const int n = blockIdx.z / c, ch = blockIdx.z - n * c;
+    if (x0 >= w || y >= h) return;
+    const float* row = src + n * src_bs + ((long long)ch * h + y) * w;
+    float v[BOXH_COLS + 2 * RR];
+    if (x0 - RR >= 0 && x0 + BOXH_COLS - 1 + RR <= w - 1) {  // no tap clamped
+#pragma unroll
+        for (int k = 0; k < BOXH_COLS + 2 * RR; k++) v[k] = __ldg(row + x0 - RR + k);
+    } else {
+#pragma unroll
+        for (int k = 0; k < BOXH_COLS + 2 * RR; k++) v[k] = __ldg(row + clampi(x0 - RR + k, 0, w - 1));
+    }
+    float* out = dst + n * dst_bs + ((long long)ch * h + y) * w;
+#pragma unroll
+    for (int k = 0; k < BOXH_COLS; k++) {
+        if (x0 + k >= w) break;
+        float acc = 0.0f;
+#pragma unroll
+        for (int d = 0; d <= 2 * RR; d++) acc = acc + v[k + d];
+        out[x0 + k] = acc / (float)(2 * RR + 1);
+    }
+}
+template <int RR>
+cudaError_t box_h_w(const float* src, long long src_bs, float* dst, long long dst_bs, int c, int h, int w, int nz,
+                    cudaStream_t st) {
+    return launch(k_box_h_w<RR>, grid2((w + BOXH_COLS - 1) / BOXH_COLS, h, nz, 32, 8), dim3(32, 8), 0, st, src, src_bs,
+                  dst, dst_bs, c, h, w);
+}
+// the horizontal box pass: the register-window kernel for radii up to 16, else k_box_h
+cudaError_t box_h(const float* src, long long src_bs, float* dst, long long dst_bs, int c, int h, int w, int r, int nz,
+                  cudaStream_t st) {
+    switch (r) {
+#define FH_BOXH(R) \
+    case R: return box_h_w<R>(src, src_bs, dst, dst_bs, c, h, w, nz, st);
+        FH_BOXH(1) FH_BOXH(2) FH_BOXH(3) FH_BOXH(4) FH_BOXH(5) FH_BOXH(6) FH_BOXH(7) FH_BOXH(8)
+        FH_BOXH(9) FH_BOXH(10) FH_BOXH(11) FH_BOXH(12) FH_BOXH(13) FH_BOXH(14) FH_BOXH(15) FH_BOXH(16)
+#undef FH_BOXH
+        default:
+            return launch(k_box_h, grid2(w, h, nz, 32, 8), dim3(32, 8), 0, st, src, src_bs, dst, dst_bs, c, h, w, r);
+    }
+}
+
 // gm_select.wgsl:12-15: the cost cell that select sample j (of w8) reads, along one axis of hc or wc cells
 FH_DEV int gm_cell(int j, int cells, int n8) { return clampi((int)floorf(((float)j + 0.5f) * (float)cells / (float)n8), 0, cells - 1); }
 
@@ -2173,7 +2224,7 @@ cudaError_t gmhs_maps(const GmArgs& g, int n, cudaStream_t st) {
     if ((uintptr_t)g.fv % 8 || g.fv_bs % 4) return cudaErrorMisalignedAddress;  // k_gm_cost's 8-byte flow loads
     { const cudaError_t e_ = launch(k_gm_cost, grid2(g.wc, g.hc, n, 32, 8), dim3(32, 8), 0, st, g); if (e_ != cudaSuccess) return e_; }
     const long long bs5 = 5LL * g.hc * g.wc, bs6 = 6LL * g.hc * g.wc;
-    { const cudaError_t e_ = launch(k_box_h, grid2(g.wc, g.hc, 3 * n, 32, 8), dim3(32, 8), 0, st, (const float*)g.maps, bs6, g.tmp, bs5, 3, g.hc, g.wc, g.r_blk); if (e_ != cudaSuccess) return e_; }
+    { const cudaError_t e_ = box_h((const float*)g.maps, bs6, g.tmp, bs5, 3, g.hc, g.wc, g.r_blk, 3 * n, st); if (e_ != cudaSuccess) return e_; }
     { const cudaError_t e_ = box_v((const float*)g.tmp, bs5, g.maps, bs6, 3, g.hc, g.wc, g.r_blk, 3 * n, st); if (e_ != cudaSuccess) return e_; }
     { const cudaError_t e_ = launch(k_box_h_cols, grid2(g.w8, g.hc, 5 * n, 32, 8), dim3(32, 8), 0, st, g, bs5); if (e_ != cudaSuccess) return e_; }
     return cudaGetLastError();
